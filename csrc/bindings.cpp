@@ -1,0 +1,289 @@
+// Python bindings of the sm_100a kernels (module hrm_flashrenderer_b200._C).
+//
+// Every entry point validates devices, dtypes, shapes, contiguity and alignment and launches on the current
+// torch CUDA stream (so the calls are capturable in CUDA graphs).  Scratch memory (split-K partials, tickets,
+// attention split partials) is passed in by the caller; nothing here allocates except the returned outputs of the
+// convenience wrappers.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "gemm_w8a16.h"
+#include "kernels.h"
+#include "comm.h"
+
+namespace {
+
+#define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
+#define CHECK_CONTIG(t) TORCH_CHECK((t).is_contiguous(), #t " must be contiguous")
+#define CHECK_DTYPE(t, d) TORCH_CHECK((t).scalar_type() == (d), #t " has dtype ", (t).scalar_type(), ", expected ", (d))
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_ws(const hrm::GemmPlan& p, const at::Tensor& ws, const at::Tensor& counters) {
+  if (p.splits > 1) {
+    CHECK_CUDA(ws);
+    CHECK_CUDA(counters);
+    CHECK_DTYPE(ws, at::kFloat);
+    CHECK_DTYPE(counters, at::kInt);
+    TORCH_CHECK((size_t)ws.numel() >= p.ws_floats, "split-K workspace too small: need ", p.ws_floats, " floats");
+    TORCH_CHECK(counters.numel() >= p.counters, "split-K counters too small: need ", p.counters);
+  }
+}
+
+hrm::GemmArgs base_args(const at::Tensor& x, const at::Tensor& w, const at::Tensor& scale,
+                        const c10::optional<at::Tensor>& bias, const at::Tensor& ws, const at::Tensor& counters) {
+  CHECK_CUDA(x); CHECK_CUDA(w); CHECK_CUDA(scale);
+  CHECK_DTYPE(x, at::kHalf); CHECK_DTYPE(w, at::kChar); CHECK_DTYPE(scale, at::kFloat);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2, "x [M,K] and w [N,K] must be 2-D");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "inner dims must be contiguous");
+  TORCH_CHECK(x.size(1) == w.size(1), "K mismatch: x ", x.size(1), " vs w ", w.size(1));
+  TORCH_CHECK(w.stride(0) == w.size(1), "w must be row-major contiguous");
+  TORCH_CHECK(scale.numel() == w.size(0), "scale must have N entries");
+  hrm::GemmArgs a{};
+  a.M = (int)x.size(0);
+  a.N = (int)w.size(0);
+  a.K = (int)x.size(1);
+  a.scale = scale.data_ptr<float>();
+  if (bias.has_value() && bias->defined()) {
+    CHECK_DTYPE((*bias), at::kFloat);
+    TORCH_CHECK(bias->numel() == a.N, "bias must have N entries");
+    a.bias = bias->data_ptr<float>();
+  }
+  a.ws = ws.defined() && ws.numel() ? ws.data_ptr<float>() : nullptr;
+  a.counters = counters.defined() && counters.numel() ? counters.data_ptr<int>() : nullptr;
+  return a;
+}
+
+std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K, int64_t force_splits) {
+  auto p = hrm::gemm_plan((int)M, (int)N, (int)K, (int)force_splits);
+  return {p.bn, p.n_tiles, p.m_tiles, p.k_tiles, p.splits, (int64_t)p.ws_floats, p.counters};
+}
+
+// out = x @ (w * scale)^T (+ bias): out dtype f16 or f32 (preallocated [M, >=N] row-major).
+void w8a16_gemm(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<at::Tensor> bias, at::Tensor out,
+                at::Tensor ws, at::Tensor counters, int64_t force_splits) {
+  c10::cuda::CUDAGuard g(x.device());
+  auto a = base_args(x, w, scale, bias, ws, counters);
+  if (a.M == 0) return;
+  CHECK_CUDA(out);
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == a.M && out.size(1) >= a.N && out.stride(1) == 1, "bad out shape");
+  int epi;
+  if (out.scalar_type() == at::kHalf) epi = hrm::EPI_F16;
+  else if (out.scalar_type() == at::kFloat) epi = hrm::EPI_F32;
+  else TORCH_CHECK(false, "out must be f16 or f32");
+  a.out = out.data_ptr();
+  a.ldo = (int)out.stride(0);
+  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_splits);
+  check_ws(p, ws, counters);
+  hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), epi, a, p, cur_stream());
+}
+
+// resid += x @ (w * scale)^T  (fp32 residual stream)
+void w8a16_gemm_residual(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor resid, at::Tensor ws,
+                         at::Tensor counters, int64_t force_splits) {
+  c10::cuda::CUDAGuard g(x.device());
+  auto a = base_args(x, w, scale, c10::nullopt, ws, counters);
+  if (a.M == 0) return;
+  CHECK_CUDA(resid); CHECK_DTYPE(resid, at::kFloat);
+  TORCH_CHECK(resid.dim() == 2 && resid.size(0) == a.M && resid.size(1) == a.N && resid.stride(1) == 1,
+              "bad resid shape");
+  a.resid = resid.data_ptr<float>();
+  a.ldr = (int)resid.stride(0);
+  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_splits);
+  check_ws(p, ws, counters);
+  hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_RESID, a, p, cur_stream());
+}
+
+// out [M, N/2] f16 = silu(gate) * up, where w rows are interleaved per 128-row tile: 64 gate rows then the 64
+// matching up rows.
+void w8a16_gemm_swiglu(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor out, at::Tensor ws,
+                       at::Tensor counters, int64_t force_splits) {
+  c10::cuda::CUDAGuard g(x.device());
+  auto a = base_args(x, w, scale, c10::nullopt, ws, counters);
+  if (a.M == 0) return;
+  CHECK_CUDA(out); CHECK_DTYPE(out, at::kHalf);
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == a.M && out.size(1) == a.N / 2 && out.stride(1) == 1, "bad out");
+  a.out = out.data_ptr();
+  a.ldo = (int)out.stride(0);
+  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_splits);
+  check_ws(p, ws, counters);
+  hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_SWIGLU, a, p, cur_stream());
+}
+
+// Fused QKV projection + bias + RoPE + paged-KV append.  w rows: [q (q_rows) | k (kv_rows) | v (kv_rows)].
+void w8a16_gemm_qkv(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<at::Tensor> bias, int64_t q_rows,
+                    int64_t kv_rows, int64_t head_dim, at::Tensor positions, at::Tensor slots, at::Tensor cos_t,
+                    at::Tensor sin_t, at::Tensor q_out, at::Tensor k_cache, at::Tensor v_cache, at::Tensor ws,
+                    at::Tensor counters, int64_t force_splits) {
+  c10::cuda::CUDAGuard g(x.device());
+  auto a = base_args(x, w, scale, bias, ws, counters);
+  if (a.M == 0) return;
+  TORCH_CHECK(a.N == q_rows + 2 * kv_rows, "w rows must be q_rows + 2*kv_rows");
+  CHECK_DTYPE(positions, at::kInt); CHECK_DTYPE(slots, at::kInt);
+  CHECK_DTYPE(cos_t, at::kFloat); CHECK_DTYPE(sin_t, at::kFloat);
+  CHECK_DTYPE(q_out, at::kBFloat16); CHECK_DTYPE(k_cache, at::kBFloat16); CHECK_DTYPE(v_cache, at::kBFloat16);
+  CHECK_CONTIG(q_out); CHECK_CONTIG(k_cache); CHECK_CONTIG(v_cache); CHECK_CONTIG(cos_t); CHECK_CONTIG(sin_t);
+  TORCH_CHECK(positions.numel() >= a.M && slots.numel() >= a.M, "positions/slots too short");
+  TORCH_CHECK(q_out.numel() >= (int64_t)a.M * q_rows, "q_out too small");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(3) == head_dim, "k_cache must be [blocks, Hk, bs, D]");
+  TORCH_CHECK(k_cache.sizes() == v_cache.sizes(), "k/v cache shape mismatch");
+  TORCH_CHECK(cos_t.size(1) == head_dim / 2, "rope table width must be head_dim/2");
+  a.q_rows = (int)q_rows;
+  a.kv_rows = (int)kv_rows;
+  a.head_dim = (int)head_dim;
+  a.kv_heads = (int)k_cache.size(1);
+  a.block_size = (int)k_cache.size(2);
+  TORCH_CHECK(a.kv_heads * head_dim == kv_rows, "kv_rows must equal cache kv_heads * head_dim");
+  a.positions = positions.data_ptr<int>();
+  a.slots = slots.data_ptr<int>();
+  a.cos_t = cos_t.data_ptr<float>();
+  a.sin_t = sin_t.data_ptr<float>();
+  a.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+  a.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr());
+  a.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
+  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_splits);
+  check_ws(p, ws, counters);
+  hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_QKV, a, p, cur_stream());
+}
+
+void rmsnorm(at::Tensor x, c10::optional<at::Tensor> delta, at::Tensor w, double eps, at::Tensor out) {
+  c10::cuda::CUDAGuard g(x.device());
+  CHECK_CUDA(x); CHECK_DTYPE(x, at::kFloat); CHECK_CONTIG(x);
+  CHECK_DTYPE(w, at::kFloat); CHECK_DTYPE(out, at::kHalf); CHECK_CONTIG(out);
+  const int H = (int)x.size(-1);
+  const int M = (int)(x.numel() / H);
+  TORCH_CHECK(H % 4 == 0, "hidden must be a multiple of 4");
+  TORCH_CHECK(out.numel() == x.numel() && w.numel() == H, "shape mismatch");
+  const float* d = nullptr;
+  if (delta.has_value() && delta->defined()) {
+    CHECK_DTYPE((*delta), at::kFloat); CHECK_CONTIG((*delta));
+    TORCH_CHECK(delta->numel() == x.numel(), "delta shape mismatch");
+    d = delta->data_ptr<float>();
+  }
+  hrm::rmsnorm_launch(x.data_ptr<float>(), d, w.data_ptr<float>(), reinterpret_cast<__half*>(out.data_ptr()), M, H,
+                      (float)eps, cur_stream());
+}
+
+void embed_q8(at::Tensor ids, at::Tensor q, at::Tensor scale, int64_t vocab_start, at::Tensor out) {
+  c10::cuda::CUDAGuard g(ids.device());
+  CHECK_DTYPE(ids, at::kLong); CHECK_DTYPE(q, at::kChar); CHECK_DTYPE(scale, at::kFloat); CHECK_DTYPE(out, at::kFloat);
+  CHECK_CONTIG(ids); CHECK_CONTIG(q); CHECK_CONTIG(out);
+  const int H = (int)q.size(1);
+  TORCH_CHECK(H % 4 == 0 && out.numel() == ids.numel() * H, "shape mismatch");
+  hrm::embed_q8_launch(ids.data_ptr<int64_t>(), q.data_ptr<int8_t>(), scale.data_ptr<float>(), out.data_ptr<float>(),
+                       (int)ids.numel(), H, (int)vocab_start, (int)q.size(0), cur_stream());
+}
+
+void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_tables,
+                      at::Tensor context_lens, at::Tensor out, at::Tensor ws, int64_t splits, int64_t keys_per_split,
+                      double scale) {
+  c10::cuda::CUDAGuard g(q.device());
+  CHECK_DTYPE(q, at::kBFloat16); CHECK_DTYPE(k_cache, at::kBFloat16); CHECK_DTYPE(v_cache, at::kBFloat16);
+  CHECK_DTYPE(block_tables, at::kInt); CHECK_DTYPE(context_lens, at::kInt); CHECK_DTYPE(out, at::kHalf);
+  CHECK_CONTIG(q); CHECK_CONTIG(k_cache); CHECK_CONTIG(v_cache); CHECK_CONTIG(block_tables); CHECK_CONTIG(out);
+  TORCH_CHECK(q.dim() == 3, "q must be [B, Hq, D]");
+  hrm::DecodeAttnArgs a{};
+  a.B = (int)q.size(0); a.Hq = (int)q.size(1); a.D = (int)q.size(2);
+  a.Hk = (int)k_cache.size(1); a.block_size = (int)k_cache.size(2);
+  a.max_blocks = (int)block_tables.size(1);
+  a.splits = (int)splits; a.keys_per_split = (int)keys_per_split;
+  a.scale = (float)scale;
+  TORCH_CHECK(a.Hq % a.Hk == 0, "Hq must be a multiple of Hk");
+  TORCH_CHECK(out.numel() == q.numel(), "out shape mismatch");
+  if (a.splits > 1) {
+    CHECK_DTYPE(ws, at::kFloat);
+    TORCH_CHECK((size_t)ws.numel() >= hrm::decode_attn_ws_floats(a.B, a.Hq, a.D, a.splits), "attention ws too small");
+    a.ws = ws.data_ptr<float>();
+  }
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  a.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  a.block_tables = block_tables.data_ptr<int>();
+  a.context_lens = context_lens.data_ptr<int>();
+  a.out = reinterpret_cast<__half*>(out.data_ptr());
+  if (a.B == 0) return;
+  hrm::decode_attn_launch(a, cur_stream());
+}
+
+void prefill_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_tables,
+                       at::Tensor cu_q, at::Tensor q_start, at::Tensor context_lens, at::Tensor out, int64_t max_q,
+                       double scale) {
+  c10::cuda::CUDAGuard g(q.device());
+  CHECK_DTYPE(q, at::kBFloat16); CHECK_DTYPE(k_cache, at::kBFloat16); CHECK_DTYPE(v_cache, at::kBFloat16);
+  CHECK_DTYPE(block_tables, at::kInt); CHECK_DTYPE(cu_q, at::kInt); CHECK_DTYPE(q_start, at::kInt);
+  CHECK_DTYPE(context_lens, at::kInt); CHECK_DTYPE(out, at::kHalf);
+  CHECK_CONTIG(q); CHECK_CONTIG(k_cache); CHECK_CONTIG(v_cache); CHECK_CONTIG(block_tables); CHECK_CONTIG(out);
+  TORCH_CHECK(q.dim() == 3, "q must be [Tq, Hq, D]");
+  hrm::PrefillAttnArgs a{};
+  a.Hq = (int)q.size(1); a.D = (int)q.size(2);
+  a.Hk = (int)k_cache.size(1); a.block_size = (int)k_cache.size(2);
+  a.S = (int)q_start.numel(); a.max_blocks = (int)block_tables.size(1); a.max_q = (int)max_q;
+  a.scale = (float)scale;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  a.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  a.block_tables = block_tables.data_ptr<int>();
+  a.cu_q = cu_q.data_ptr<int>();
+  a.q_start = q_start.data_ptr<int>();
+  a.context_lens = context_lens.data_ptr<int>();
+  a.out = reinterpret_cast<__half*>(out.data_ptr());
+  hrm::prefill_attn_launch(a, cur_stream());
+}
+
+void argmax_rows(at::Tensor logits, int64_t vocab_start, c10::optional<at::Tensor> keys, at::Tensor tokens) {
+  c10::cuda::CUDAGuard g(logits.device());
+  CHECK_DTYPE(logits, at::kFloat); CHECK_DTYPE(tokens, at::kLong);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be [M, V] row-major");
+  unsigned long long* kp = nullptr;
+  if (keys.has_value() && keys->defined()) {
+    CHECK_DTYPE((*keys), at::kLong);
+    kp = reinterpret_cast<unsigned long long*>(keys->data_ptr<int64_t>());
+  }
+  hrm::argmax_launch(logits.data_ptr<float>(), (int)logits.size(0), (int)logits.size(1), (int)logits.stride(0),
+                     (int)vocab_start, kp, tokens.data_ptr<int64_t>(), cur_stream());
+}
+
+void decode_prepare_bs(at::Tensor positions, at::Tensor tables, int64_t block_size, c10::optional<at::Tensor> active,
+                       at::Tensor slots, at::Tensor context_lens) {
+  c10::cuda::CUDAGuard g(positions.device());
+  CHECK_DTYPE(positions, at::kInt); CHECK_DTYPE(tables, at::kInt); CHECK_DTYPE(slots, at::kInt);
+  CHECK_DTYPE(context_lens, at::kInt); CHECK_CONTIG(tables);
+  const int* ap = nullptr;
+  if (active.has_value() && active->defined()) { CHECK_DTYPE((*active), at::kInt); ap = active->data_ptr<int>(); }
+  hrm::decode_prepare_launch(positions.data_ptr<int>(), tables.data_ptr<int>(), (int)tables.size(1),
+                             (int)block_size, ap, slots.data_ptr<int>(), context_lens.data_ptr<int>(),
+                             (int)positions.numel(), cur_stream());
+}
+
+void decode_advance(at::Tensor tokens, at::Tensor ids, at::Tensor positions, c10::optional<at::Tensor> active) {
+  c10::cuda::CUDAGuard g(tokens.device());
+  CHECK_DTYPE(tokens, at::kLong); CHECK_DTYPE(ids, at::kLong); CHECK_DTYPE(positions, at::kInt);
+  const int* ap = nullptr;
+  if (active.has_value() && active->defined()) { CHECK_DTYPE((*active), at::kInt); ap = active->data_ptr<int>(); }
+  hrm::decode_advance_launch(tokens.data_ptr<int64_t>(), ids.data_ptr<int64_t>(), positions.data_ptr<int>(), ap,
+                             (int)positions.numel(), cur_stream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of hrm_flashrenderer_b200";
+  m.def("gemm_plan", &gemm_plan_py, "split-K plan: (bn, n_tiles, m_tiles, k_tiles, splits, ws_floats, counters)");
+  m.def("w8a16_gemm", &w8a16_gemm);
+  m.def("w8a16_gemm_residual", &w8a16_gemm_residual);
+  m.def("w8a16_gemm_swiglu", &w8a16_gemm_swiglu);
+  m.def("w8a16_gemm_qkv", &w8a16_gemm_qkv);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("embed_q8", &embed_q8);
+  m.def("decode_attention", &decode_attention);
+  m.def("decode_attn_ws_floats", [](int64_t B, int64_t Hq, int64_t D, int64_t s) {
+    return (int64_t)hrm::decode_attn_ws_floats((int)B, (int)Hq, (int)D, (int)s);
+  });
+  m.def("prefill_attention", &prefill_attention);
+  m.def("argmax_rows", &argmax_rows);
+  m.def("decode_prepare", &decode_prepare_bs);
+  m.def("decode_advance", &decode_advance);
+  m.def("sm_count", []() { return hrm::gemm_sm_count(); });
+  hrm::register_comm_bindings(m);
+}

@@ -1,0 +1,208 @@
+// Shared device helpers for the sm_100a kernels: mbarriers with bounded waits, TMA tile loads, tcgen05 (UMMA)
+// descriptors / MMA / TMEM access, and small numeric helpers.  Written against the public PTX ISA for sm_100a.
+//
+// Rules enforced here for every kernel of this library:
+//  * every spin-wait is bounded; on timeout it records an error code in a global status word and returns
+//    (no __trap, no device assert);
+//  * TMA loads never use cluster multicast (loads are CTA-local);
+//  * tcgen05.mma operands are f16 x f16 (kind::f16) - A and B always share one type.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#define HRM_DEVINL __device__ __forceinline__
+
+namespace hrm {
+
+// Error codes written to the kernel status word (0 = ok).
+enum : int {
+  kErrNone = 0,
+  kErrTimeoutFull = 1,
+  kErrTimeoutEmpty = 2,
+  kErrTimeoutDequant = 3,
+  kErrTimeoutAccum = 4,
+  kErrTimeoutPeer = 5,
+  kErrBadShape = 6,
+};
+
+// ~2^24 polls of try_wait (each poll itself blocks for a hardware-defined interval) is seconds, far above any
+// legitimate wait in these kernels.
+constexpr uint32_t kSpinLimit = 1u << 24;
+
+HRM_DEVINL uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+HRM_DEVINL void record_error(int* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+// ---------------------------------------------------------------- mbarrier
+HRM_DEVINL void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+HRM_DEVINL void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+HRM_DEVINL void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
+}
+HRM_DEVINL void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
+               ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+HRM_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait.  Returns false (and records `code`) when the limit is hit.
+HRM_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  record_error(status, code);
+  return false;
+}
+
+// ---------------------------------------------------------------- TMA (no multicast)
+HRM_DEVINL void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+HRM_DEVINL void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+HRM_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ---------------------------------------------------------------- tcgen05 / TMEM
+HRM_DEVINL void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {  // whole warp
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+               ::"r"(smem_u32(smem_slot)), "r"(ncols) : "memory");
+}
+HRM_DEVINL void tmem_relinquish() {  // whole warp
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+HRM_DEVINL void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // whole warp
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+HRM_DEVINL void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+HRM_DEVINL void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16, fp32 accumulate; single issuing thread.
+HRM_DEVINL void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// Arrive on an mbarrier once all previously issued tcgen05.mma of this thread have completed.
+HRM_DEVINL void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Instruction descriptor, kind::f16: D = f32, A = B = f16, both K-major, shape M x N.
+HRM_DEVINL constexpr uint32_t idesc_f16_f32(int M, int N) {
+  return (1u << 4)                      // D format: f32
+       | (0u << 7) | (0u << 10)         // A, B format: f16
+       | (0u << 15) | (0u << 16)        // K-major A and B
+       | ((uint32_t)(N >> 3) << 17)
+       | ((uint32_t)(M >> 4) << 24);
+}
+// Same with bf16 operands (used by attention where Q/K/V are bf16).
+HRM_DEVINL constexpr uint32_t idesc_bf16_f32(int M, int N, bool b_mn_major = false) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (0u << 15) | ((b_mn_major ? 1u : 0u) << 16)
+       | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor for a K-major operand stored in the 128-byte-swizzled canonical layout:
+// rows of 128 bytes, 8-row groups 1024 bytes apart (SBO = 1024), atom base 1024-byte aligned.  Advancing along
+// K inside the 128-byte row is done by adding the byte offset to the start address.
+HRM_DEVINL uint64_t sdesc_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);      // start address
+  d |= (uint64_t)(16u >> 4) << 16;                  // LBO (ignored for swizzled K-major; canonical value 1)
+  d |= (uint64_t)(1024u >> 4) << 32;                // SBO
+  d |= (uint64_t)1 << 46;                           // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                           // SWIZZLE_128B
+  return d;
+}
+// MN-major operand in the 128-byte-swizzled canonical layout: 64 MN-elements (128 bytes) per row, rows along K,
+// 8-row (8 K) groups 1024 bytes apart; consecutive 64-element MN blocks are LBO bytes apart.
+HRM_DEVINL uint64_t sdesc_sw128_mn(uint32_t smem_addr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// 32 lanes x 32 bit, 16 consecutive columns per thread.
+HRM_DEVINL void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+// 32 lanes x 32 bit, 16 consecutive columns per thread (store into TMEM).
+HRM_DEVINL void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- numerics
+// Four signed int8 (one 32-bit word) -> two f16x2, exact.  Each byte is biased to unsigned (xor 0x80), placed
+// in the mantissa of the f16 1024.0 (0x6400 | u gives 1024 + u, exact for u < 1024), then 1024 + 128 is
+// subtracted.
+HRM_DEVINL void i8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  asm("prmt.b32 %0, %1, %2, 0x4140;" : "=r"(lo) : "r"(u), "r"(0x64646464u));
+  asm("prmt.b32 %0, %1, %2, 0x4342;" : "=r"(hi) : "r"(u), "r"(0x64646464u));
+  const uint32_t bias = 0x64806480u;  // f16x2 (1152, 1152)
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(lo), "r"(bias));
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(hi), "r"(bias));
+}
+
+HRM_DEVINL float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+HRM_DEVINL float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+HRM_DEVINL float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+// Monotone float -> uint32 map (total order) and the packed 64-bit argmax key: larger value wins, then the
+// lower index (the low word stores ~idx).
+HRM_DEVINL uint32_t float_order(float f) {
+  uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+HRM_DEVINL unsigned long long argmax_key(float v, uint32_t idx) {
+  return ((unsigned long long)float_order(v) << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
+}
+
+}  // namespace hrm

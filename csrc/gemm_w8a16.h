@@ -1,0 +1,56 @@
+// Host-visible declarations of the W8A16 tcgen05 GEMM (see gemm_w8a16.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace hrm {
+
+enum GemmEpilogue : int {
+  EPI_F16 = 0,     // out f16 [M, ldo]            = acc * scale (+ bias)
+  EPI_F32 = 1,     // out f32 [M, ldo]            = acc * scale (+ bias)
+  EPI_RESID = 2,   // resid f32 [M, ldr]         += acc * scale (+ bias)
+  EPI_SWIGLU = 3,  // out f16 [M, N/2]            = silu(gate) * up, rows interleaved 64 gate / 64 up per tile
+  EPI_QKV = 4,     // q_out bf16 [M, q_rows]; K/V rows -> paged cache (bias + rotate-half RoPE on q and k)
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int k_tiles, tiles_per_split, splits;     // filled by the launcher from the plan
+  const float* scale;                       // [N]
+  const float* bias;                        // [N] or nullptr
+  void* out;                                // EPI_F16 / EPI_F32 / EPI_SWIGLU
+  int ldo;
+  float* resid;                             // EPI_RESID
+  int ldr;
+  float* ws;                                // split-K workspace: plan.ws_floats floats
+  int* counters;                            // split-K tickets: plan.counters ints, zero before first use
+  // EPI_QKV
+  int q_rows, kv_rows, head_dim, kv_heads, block_size;
+  const int* positions;                     // [M] absolute positions
+  const int* slots;                         // [M] block * block_size + offset, or -1 to skip the KV write
+  const float* cos_t;                       // [max_pos, head_dim / 2]
+  const float* sin_t;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_cache;                   // [num_blocks, kv_heads, block_size, head_dim]
+  __nv_bfloat16* v_cache;
+  int* status;                              // bounded-wait error word (may be nullptr)
+};
+
+struct GemmPlan {
+  int bn, n_tiles, m_tiles, k_tiles, tiles_per_split, splits;
+  size_t ws_floats;
+  int counters;
+};
+
+GemmPlan gemm_plan(int M, int N, int K, int force_splits = 0);
+void gemm_w8a16_launch(const void* x, int ldx, const int8_t* w, int epi, GemmArgs a, const GemmPlan& p,
+                       cudaStream_t stream);
+void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                  uint64_t outer, uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                  CUtensorMapSwizzle swz);
+int gemm_sm_count();
+
+}  // namespace hrm

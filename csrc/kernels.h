@@ -1,0 +1,54 @@
+// Host-visible launchers of the non-GEMM kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace hrm {
+
+void rmsnorm_launch(float* x, const float* delta, const float* w, __half* out, int M, int H, float eps,
+                    cudaStream_t s);
+void embed_q8_launch(const int64_t* ids, const int8_t* q, const float* scale, float* out, int M, int H,
+                     int vocab_start, int vocab_local, cudaStream_t s);
+
+// Paged decode attention (one query token per sequence), split-K over the context + combine.
+struct DecodeAttnArgs {
+  const __nv_bfloat16* q;      // [B, Hq, D]
+  const __nv_bfloat16* k_cache;  // [num_blocks, Hk, bs, D]
+  const __nv_bfloat16* v_cache;
+  const int* block_tables;     // [B, max_blocks]
+  const int* context_lens;     // [B]
+  __half* out;                 // [B, Hq, D]
+  float* ws;                   // split partials: [B, Hq, splits, D + 2]
+  int B, Hq, Hk, D, block_size, max_blocks, splits, keys_per_split;
+  float scale;
+};
+void decode_attn_launch(const DecodeAttnArgs& a, cudaStream_t s);
+size_t decode_attn_ws_floats(int B, int Hq, int D, int splits);
+
+// Paged prefill attention over varlen query chunks (causal with absolute positions).
+struct PrefillAttnArgs {
+  const __nv_bfloat16* q;      // [Tq, Hq, D] (all sequences' chunk tokens, concatenated)
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  const int* block_tables;     // [S, max_blocks]
+  const int* cu_q;             // [S + 1] query offsets
+  const int* q_start;          // [S] absolute position of each sequence's first chunk token
+  const int* context_lens;     // [S] keys visible to the chunk's last token (q_start + chunk len)
+  __half* out;                 // [Tq, Hq, D]
+  int S, Hq, Hk, D, block_size, max_blocks, max_q;
+  float scale;
+};
+void prefill_attn_launch(const PrefillAttnArgs& a, cudaStream_t s);
+
+// Row argmax of fp32 logits [M, V] -> packed (order(value) << 32 | ~global_idx) keys, and token ids.
+void argmax_launch(const float* logits, int M, int V, int ld, int vocab_start, unsigned long long* keys,
+                   int64_t* tokens, cudaStream_t s);
+
+void decode_prepare_launch(const int* positions, const int* tables, int maxb, int bs, const int* active, int* slots,
+                           int* context_lens, int B, cudaStream_t s);
+void decode_advance_launch(const int64_t* tokens, int64_t* ids, int* positions, const int* active, int B,
+                           cudaStream_t s);
+
+}  // namespace hrm

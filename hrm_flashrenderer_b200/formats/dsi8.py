@@ -1,0 +1,237 @@
+"""DSI8 model file: reader, writer and HF-safetensors exporter.
+
+The byte layout is kept bit-compatible with the reference exporter (``hrm_flash/deepseek_export.py:179-220``)
+and the engine loader (``scripts/deepseek_native_engine.sh:315-357``) so files move between the two:
+
+* header: ``b"DSI8"``, u32 version (4), 8 x u32 ``D, H, KVH, Dh, F, V, L, Tmax``, f64 rope_theta, f32 rms_eps,
+  u32 bos, u32 eos;
+* records until EOF: u32 name_len, name, u32 ttype (0 = Q8, 1 = F32), u32 ndim, ndim x u32 dims, payload;
+* Q8 payload: ``rows`` f32 scales followed by ``rows*cols`` int8 row-major;  F32 payload: ``prod(dims)`` f32.
+
+Differences from the reference (documented, forward compatible): ``Tmax`` is the config's
+``max_position_embeddings`` (the reference hard-codes 4096), and the header ``eos`` is the first id of an EOS list.
+Llama-3 rope-scaling parameters and the full EOS list are carried in an optional trailing F32 record named
+``__hrm_b200_meta__`` (a JSON blob stored as bytes padded to 4), which the reference loader stores as an unused
+F32 tensor and ignores.
+"""
+from __future__ import annotations
+
+import json
+import mmap
+import os
+import struct
+from dataclasses import replace
+from pathlib import Path
+from typing import Dict, Iterable, Optional, Tuple
+
+import numpy as np
+import torch
+
+from ..config import ModelConfig, RopeScaling
+from ..models.weights import (QTensor, Tensorish, matrix_shapes, vector_shapes, quantize_rows, EMBED, LM_HEAD)
+
+MAGIC = b"DSI8"
+VERSION = 4
+TTYPE_Q8 = 0
+TTYPE_F32 = 1
+TTYPE_Q4 = 2
+META_NAME = "__hrm_b200_meta__"
+
+
+def _write_record(f, name: str, ttype: int, dims: Tuple[int, ...], payloads: Iterable[bytes]) -> None:
+    nb = name.encode()
+    f.write(struct.pack("<I", len(nb)))
+    f.write(nb)
+    f.write(struct.pack("<II", ttype, len(dims)))
+    for d in dims:
+        f.write(struct.pack("<I", int(d)))
+    for p in payloads:
+        f.write(p)
+
+
+def write_dsi8(path: str | Path, cfg: ModelConfig, weights: Dict[str, Tensorish]) -> Path:
+    """Write ``weights`` (QTensor matrices + fp32 vectors) in DSI8 record order."""
+    path = Path(path)
+    path.parent.mkdir(parents=True, exist_ok=True)
+    tmp = path.with_suffix(path.suffix + ".tmp")
+    with tmp.open("wb") as f:
+        f.write(MAGIC)
+        f.write(struct.pack("<I", VERSION))
+        f.write(struct.pack("<IIIIIIII", cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.intermediate,
+                            cfg.vocab, cfg.layers, cfg.max_position_embeddings))
+        f.write(struct.pack("<d", float(cfg.rope_theta)))
+        f.write(struct.pack("<f", float(cfg.rms_eps)))
+        f.write(struct.pack("<II", int(cfg.bos_token_id), int(cfg.eos_token_ids[0])))
+        for name, (rows, cols) in matrix_shapes(cfg):
+            if name not in weights:
+                continue
+            t = weights[name]
+            assert isinstance(t, QTensor) and t.shape == (rows, cols), name
+            _write_record(f, name, TTYPE_Q8, (rows, cols), [
+                t.scale.detach().cpu().to(torch.float32).contiguous().numpy().tobytes(),
+                t.q.detach().cpu().contiguous().numpy().tobytes()])
+        for name, n in vector_shapes(cfg):
+            if name not in weights:
+                continue
+            v = weights[name].detach().cpu().to(torch.float32).contiguous()
+            assert v.numel() == n, name
+            _write_record(f, name, TTYPE_F32, (n,), [v.numpy().tobytes()])
+        meta = {
+            "name": cfg.name,
+            "eos_token_ids": list(cfg.eos_token_ids),
+            "qkv_bias": cfg.qkv_bias,
+            "tie_embeddings": cfg.tie_embeddings,
+            "rope_scaling": None if cfg.rope_scaling is None else cfg.rope_scaling.__dict__,
+        }
+        blob = json.dumps(meta, sort_keys=True).encode()
+        blob += b" " * ((-len(blob)) % 4)
+        _write_record(f, META_NAME, TTYPE_F32, (len(blob) // 4,), [blob])
+    os.replace(tmp, path)
+    return path
+
+
+class DSI8File:
+    """Memory-mapped DSI8 reader.  Tensors are zero-copy numpy views into the mapping."""
+
+    def __init__(self, path: str | Path):
+        self.path = Path(path)
+        self._f = self.path.open("rb")
+        self._mm = mmap.mmap(self._f.fileno(), 0, access=mmap.ACCESS_READ)
+        buf = self._mm
+        if buf[:4] != MAGIC:
+            raise ValueError(f"{path}: bad magic {bytes(buf[:4])!r}")
+        (self.version,) = struct.unpack_from("<I", buf, 4)
+        if self.version < 3:
+            raise ValueError(f"{path}: need version >= 3, got {self.version}")
+        D, H, KVH, Dh, F, V, L, Tmax = struct.unpack_from("<IIIIIIII", buf, 8)
+        (theta,) = struct.unpack_from("<d", buf, 40)
+        (eps,) = struct.unpack_from("<f", buf, 48)
+        bos, eos = struct.unpack_from("<II", buf, 52)
+        o = 60
+        self.records: Dict[str, Tuple[int, Tuple[int, ...], int]] = {}
+        n = len(buf)
+        while o + 4 <= n:
+            (nl,) = struct.unpack_from("<I", buf, o)
+            o += 4
+            if o + nl > n:
+                break
+            name = bytes(buf[o:o + nl]).decode()
+            o += nl
+            ttype, ndim = struct.unpack_from("<II", buf, o)
+            o += 8
+            dims = struct.unpack_from("<" + "I" * ndim, buf, o)
+            o += 4 * ndim
+            self.records[name] = (ttype, tuple(dims), o)
+            if ttype == TTYPE_Q8:
+                rows = dims[0]
+                cols = dims[1] if ndim > 1 else 1
+                o += rows * 4 + rows * cols
+            elif ttype == TTYPE_Q4:
+                rows = dims[0]
+                cols = dims[1] if ndim > 1 else 1
+                o += rows * 4 + rows * ((cols + 1) // 2)
+            else:
+                o += int(np.prod(dims)) * 4
+        meta = {}
+        if META_NAME in self.records:
+            _, dims, off = self.records[META_NAME]
+            meta = json.loads(bytes(buf[off:off + dims[0] * 4]).decode().strip())
+        rs = meta.get("rope_scaling")
+        qkv_bias = bool(meta.get("qkv_bias", any(k.endswith("q_proj.bias") for k in self.records)))
+        tie = bool(meta.get("tie_embeddings", LM_HEAD not in self.records))
+        self.config = ModelConfig(
+            name=str(meta.get("name", self.path.stem)), hidden=D, layers=L, heads=H, kv_heads=KVH, head_dim=Dh,
+            intermediate=F, vocab=V, rms_eps=float(eps), rope_theta=float(theta),
+            rope_scaling=RopeScaling(**rs) if rs else None, qkv_bias=qkv_bias, tie_embeddings=tie,
+            max_position_embeddings=Tmax, bos_token_id=bos,
+            eos_token_ids=tuple(meta.get("eos_token_ids", [eos])),
+        )
+
+    def close(self) -> None:
+        self._mm.close()
+        self._f.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def names(self):
+        return [k for k in self.records if k != META_NAME]
+
+    def get(self, name: str) -> Tensorish:
+        ttype, dims, off = self.records[name]
+        if ttype == TTYPE_Q8:
+            rows = dims[0]
+            cols = dims[1] if len(dims) > 1 else 1
+            scale = np.frombuffer(self._mm, dtype=np.float32, count=rows, offset=off)
+            q = np.frombuffer(self._mm, dtype=np.int8, count=rows * cols, offset=off + rows * 4).reshape(rows, cols)
+            return QTensor(torch.from_numpy(q.copy()), torch.from_numpy(scale.copy()))
+        if ttype == TTYPE_F32:
+            cnt = int(np.prod(dims))
+            return torch.from_numpy(np.frombuffer(self._mm, dtype=np.float32, count=cnt, offset=off).copy())
+        raise ValueError(f"{name}: unsupported tensor type {ttype} (only q8 is supported; q4 is rejected)")
+
+    def load_all(self) -> Dict[str, Tensorish]:
+        return {k: self.get(k) for k in self.names()}
+
+
+def read_dsi8(path: str | Path) -> Tuple[ModelConfig, Dict[str, Tensorish]]:
+    with DSI8File(path) as f:
+        return f.config, f.load_all()
+
+
+# ------------------------------------------------------------------------------------------------
+# safetensors -> DSI8 exporter (reference: ``export_dsi_v4``, ``hrm_flash/deepseek_export.py:110-222``)
+# ------------------------------------------------------------------------------------------------
+_ST_DTYPES = {"F32": np.float32, "F16": np.float16, "BF16": np.uint16, "I8": np.int8}
+
+
+def _iter_safetensors(path: Path):
+    with path.open("rb") as f:
+        (hs,) = struct.unpack("<Q", f.read(8))
+        hdr = json.loads(f.read(hs))
+    base = 8 + hs
+    mm = np.memmap(path, dtype=np.uint8, mode="r")
+    for k, m in hdr.items():
+        if k == "__metadata__":
+            continue
+        s, e = m["data_offsets"]
+        dt = m["dtype"]
+        raw = mm[base + s: base + e]
+        if dt == "BF16":
+            arr = (raw.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+        elif dt in _ST_DTYPES:
+            arr = raw.view(_ST_DTYPES[dt]).astype(np.float32)
+        else:
+            raise ValueError(f"{path}:{k}: unsupported safetensors dtype {dt}")
+        yield k, arr.reshape(m["shape"])
+
+
+def export_dsi8(model_dir: str | Path, out_path: str | Path, quant: str = "q8") -> Path:
+    """Export a local HF checkpoint directory (config.json + *.safetensors) to DSI8 (q8 only).
+
+    q4 is rejected: the reference engine parses tensor type 2 as F32 and the production scripts lock it out
+    (``deepseek_export.py:53-79,196-198``; ``deepseek_native_engine.sh:342-355``).
+    """
+    if str(quant).lower() != "q8":
+        raise ValueError(f"unsupported quant={quant!r}: only q8 is supported")
+    model_dir = Path(model_dir)
+    cfg = ModelConfig.from_hf_dir(model_dir)
+    want_2d = dict(matrix_shapes(cfg))
+    want_1d = dict(vector_shapes(cfg))
+    weights: Dict[str, Tensorish] = {}
+    for fn in sorted(model_dir.glob("*.safetensors")):
+        for k, arr in _iter_safetensors(fn):
+            if k in want_2d:
+                weights[k] = quantize_rows(torch.from_numpy(np.ascontiguousarray(arr, dtype=np.float32)))
+            elif k in want_1d:
+                weights[k] = torch.from_numpy(np.ascontiguousarray(arr, dtype=np.float32)).reshape(-1)
+    if not weights:
+        raise RuntimeError(f"no safetensors tensors found under {model_dir}")
+    if cfg.qkv_bias and not any(k.endswith("q_proj.bias") for k in weights):
+        cfg = replace(cfg, qkv_bias=False)
+    if LM_HEAD not in weights and EMBED in weights:
+        cfg = replace(cfg, tie_embeddings=True)
+    return write_dsi8(out_path, cfg, weights)

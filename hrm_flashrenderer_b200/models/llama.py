@@ -1,0 +1,246 @@
+"""Llama / Qwen2 decoder on the sm_100a kernels, tensor-parallel over one process per GPU.
+
+Per layer and token batch (rows = tokens of all scheduled sequences, decode or chunked prefill):
+
+    h   = rmsnorm(x)                         (fp32 residual x -> f16 GEMM operand)
+    q   = QKV GEMM + bias + RoPE, K/V -> paged cache          (one kernel)
+    o   = paged attention(q)                 (decode split-K or varlen causal prefill)
+    x  += all_reduce(o @ Wo^T) ; h = rmsnorm(x)               (fused GEMM+AR+residual+norm when TP > 1)
+    a   = silu(h @ Wg^T) * (h @ Wu^T)        (one kernel, gate/up interleaved per tile)
+    x  += all_reduce(a @ Wd^T) ; h = rmsnorm(x)
+
+Reference counterparts: ``TPLlamaAttention`` / ``TPLlamaMLP`` / ``TPLlamaBlock`` / ``TPLlamaForCausalLM``
+(``engine/llama_tp.py:110-311``) and the native engine's per-layer loop (``scripts/deepseek_native_engine.sh:1041-1099``).
+Semantics follow HF (rotate-half RoPE with llama3 scaling, ``kv_head = head // group``, Qwen2 QKV bias), not the
+reference's quirks.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional
+
+import torch
+
+from .. import ops
+from ..config import ModelConfig
+from ..models.oracle import rope_tables
+from ..models.weights import (QTensor, Tensorish, ShardPlan, layer_names, shard_plan, synth_matrix, matrix_shapes,
+                              vector_shapes, quantize_rows, EMBED, FINAL_NORM, LM_HEAD, get_lm_head)
+from ..runtime.kv_cache import PagedKVPool
+
+
+@dataclass
+class LayerWeights:
+    w_qkv: torch.Tensor
+    s_qkv: torch.Tensor
+    b_qkv: Optional[torch.Tensor]
+    w_o: torch.Tensor
+    s_o: torch.Tensor
+    w_gu: torch.Tensor
+    s_gu: torch.Tensor
+    w_d: torch.Tensor
+    s_d: torch.Tensor
+    ln1: torch.Tensor
+    ln2: torch.Tensor
+
+
+@dataclass
+class BatchMeta:
+    """Device-side description of one forward step (all int32 unless noted).
+
+    ``ids`` int64 [T]; ``positions`` [T]; ``slots`` [T] (block*bs + offset, -1 = no KV write);
+    decode: ``block_tables`` [B, maxb], ``context_lens`` [B]; prefill: additionally ``cu_q`` [S+1], ``q_start`` [S],
+    ``max_q``; ``last_rows`` int64 [S] rows whose hidden state feeds the lm_head.
+    """
+
+    ids: torch.Tensor
+    positions: torch.Tensor
+    slots: torch.Tensor
+    block_tables: torch.Tensor
+    context_lens: torch.Tensor
+    last_rows: torch.Tensor
+    is_decode: bool
+    cu_q: Optional[torch.Tensor] = None
+    q_start: Optional[torch.Tensor] = None
+    max_q: int = 1
+    attn_splits: int = 0
+    attn_keys_per_split: int = 0
+
+
+def pack_layer(cfg: ModelConfig, w: Dict[str, Tensorish], l: int, device) -> LayerWeights:
+    """Pack one (already sharded) layer into the kernel layouts: fused QKV rows, interleaved gate/up tiles."""
+    n = layer_names(l)
+    q, k, v = w[n["q"]], w[n["k"]], w[n["v"]]
+    w_qkv = torch.cat([q.q, k.q, v.q], 0).to(device).contiguous()
+    s_qkv = torch.cat([q.scale, k.scale, v.scale], 0).to(device, torch.float32).contiguous()
+    b_qkv = None
+    if cfg.qkv_bias:
+        b_qkv = torch.cat([w[n["bq"]], w[n["bk"]], w[n["bv"]]], 0).to(device, torch.float32).contiguous()
+    g, u = w[n["gate"]], w[n["up"]]
+    w_gu, s_gu = ops.interleave_gate_up(g.q.to(device), u.q.to(device), g.scale.to(device), u.scale.to(device))
+    o, d = w[n["o"]], w[n["down"]]
+    return LayerWeights(
+        w_qkv=w_qkv, s_qkv=s_qkv, b_qkv=b_qkv,
+        w_o=o.q.to(device).contiguous(), s_o=o.scale.to(device, torch.float32).contiguous(),
+        w_gu=w_gu, s_gu=s_gu.to(torch.float32),
+        w_d=d.q.to(device).contiguous(), s_d=d.scale.to(device, torch.float32).contiguous(),
+        ln1=w[n["ln1"]].to(device, torch.float32).contiguous(), ln2=w[n["ln2"]].to(device, torch.float32).contiguous())
+
+
+class LlamaW8:
+    """Int8-weight decoder shard for TP rank ``plan.rank`` of ``plan.world`` on one CUDA device."""
+
+    def __init__(self, cfg: ModelConfig, plan: ShardPlan, layers: List[LayerWeights], embed: QTensor,
+                 lm_head: QTensor, final_norm: torch.Tensor, device, comm=None, max_pos: int = 8192):
+        self.cfg, self.plan, self.layers, self.device = cfg, plan, layers, torch.device(device)
+        self.embed_q, self.embed_s = embed.q.contiguous(), embed.scale.contiguous()
+        self.head_q, self.head_s = lm_head.q.contiguous(), lm_head.scale.contiguous()
+        self.final_norm = final_norm
+        self.comm = comm
+        self.q_rows = plan.local_heads * cfg.head_dim
+        self.kv_rows = plan.local_kv_heads * cfg.head_dim
+        cos, sin = rope_tables(cfg, max_pos)
+        self.cos, self.sin = cos.to(self.device).contiguous(), sin.to(self.device).contiguous()
+        self.max_pos = max_pos
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        self.kv: Optional[PagedKVPool] = None
+
+    # ------------------------------------------------------------------ construction
+    @classmethod
+    def from_weights(cls, cfg: ModelConfig, weights: Dict[str, Tensorish], rank: int = 0, world: int = 1,
+                     device="cuda", comm=None, max_pos: int = 8192) -> "LlamaW8":
+        from .weights import shard_weights
+        plan = shard_plan(cfg, rank, world)
+        w = shard_weights(cfg, weights, rank, world) if world > 1 else dict(weights)
+        if world == 1:
+            w[LM_HEAD] = get_lm_head(cfg, weights)
+        layers = [pack_layer(cfg, w, l, device) for l in range(cfg.layers)]
+        return cls(cfg, plan, layers, w[EMBED].to(device), w[LM_HEAD].to(device),
+                   w[FINAL_NORM].to(device, torch.float32), device, comm, max_pos)
+
+    @classmethod
+    def synthesize(cls, cfg: ModelConfig, rank: int = 0, world: int = 1, device="cuda", seed: int = 0,
+                   comm=None, max_pos: int = 8192, norm_jitter: float = 0.0) -> "LlamaW8":
+        """Random-init int8 weights generated directly on the device, layer by layer (70B never exists in fp32).
+
+        Matrix ``i`` (DSI8 record order) draws from a generator seeded ``seed*1000003 + i`` exactly like
+        :func:`~hrm_flashrenderer_b200.models.weights.synth_weights`, so a shard equals the slice of the full model.
+        """
+        from .weights import synth_weights, shard_weights
+        dev = torch.device(device)
+        plan = shard_plan(cfg, rank, world)
+        shapes = list(matrix_shapes(cfg))
+        idx_of = {name: i for i, (name, _) in enumerate(shapes)}
+        vec = {}
+        base = 10_000_000
+        for i, (name, n) in enumerate(vector_shapes(cfg)):
+            g = torch.Generator(device="cpu").manual_seed(seed * 1_000_003 + base + i)
+            if name.endswith("layernorm.weight") or name == FINAL_NORM:
+                v = torch.ones(n) + (torch.randn(n, generator=g) * norm_jitter if norm_jitter else 0.0)
+            else:
+                v = torch.randn(n, generator=g) * 0.02
+            vec[name] = v.to(torch.float32)
+
+        def mat(name):
+            rows, cols = dict(shapes)[name]
+            return synth_matrix(rows, cols, seed=seed * 1_000_003 + idx_of[name], device=dev)
+
+        layers = []
+        for l in range(cfg.layers):
+            n = layer_names(l)
+            full = {k: mat(n[k]) for k in ("q", "k", "v", "o", "gate", "up", "down")}
+            lw = {n[k]: t for k, t in full.items()}
+            for k in ("ln1", "ln2", "bq", "bk", "bv"):
+                if n[k] in vec:
+                    lw[n[k]] = vec[n[k]]
+            sub_cfg = cfg.with_layers(1)
+            # re-key layer l as layer 0 for sharding/packing helpers
+            re = {name.replace(f"model.layers.{l}.", "model.layers.0."): t for name, t in lw.items()}
+            if world > 1:
+                re.update({EMBED: QTensor(torch.zeros(cfg.vocab, 1, dtype=torch.int8), torch.ones(cfg.vocab)),
+                           LM_HEAD: QTensor(torch.zeros(cfg.vocab, 1, dtype=torch.int8), torch.ones(cfg.vocab)),
+                           FINAL_NORM: vec[FINAL_NORM]})
+                re = shard_weights(sub_cfg, re, rank, world)
+            layers.append(pack_layer(sub_cfg, re, 0, dev))
+            del full, lw, re
+        emb = mat(EMBED)
+        head = emb if cfg.tie_embeddings else mat(LM_HEAD)
+        v0, v1 = plan.vocab_start, plan.vocab_start + plan.vocab_per_rank
+        emb, head = emb.rows(v0, v1).contiguous(), head.rows(v0, v1).contiguous()
+        return cls(cfg, plan, layers, emb, head, vec[FINAL_NORM].to(dev), dev, comm, max_pos)
+
+    def weight_bytes(self) -> int:
+        tot = 0
+        for L in self.layers:
+            for t in (L.w_qkv, L.w_o, L.w_gu, L.w_d):
+                tot += t.numel()
+        return tot + self.embed_q.numel() + self.head_q.numel()
+
+    # ------------------------------------------------------------------ KV cache
+    def alloc_kv(self, num_blocks: int, block_size: int = 16) -> PagedKVPool:
+        self.kv = PagedKVPool(self.cfg.layers, num_blocks, self.plan.local_kv_heads, self.cfg.head_dim, block_size,
+                              torch.bfloat16, self.device)
+        return self.kv
+
+    # ------------------------------------------------------------------ forward
+    def _all_reduce_add_norm(self, x: torch.Tensor, partial: torch.Tensor, gamma: torch.Tensor, h_out: torch.Tensor):
+        """TP reduction of a row-parallel partial + residual add + RMSNorm (baseline: NCCL then one norm kernel)."""
+        self.comm.all_reduce_(partial)
+        return ops.add_rmsnorm_(x, partial, gamma, self.cfg.rms_eps, out=h_out)
+
+    @torch.no_grad()
+    def forward(self, b: BatchMeta) -> torch.Tensor:
+        """Runs all layers for the batch and returns greedy next tokens ``[len(last_rows)]`` (int64, global ids)."""
+        cfg, p = self.cfg, self.plan
+        T = b.ids.shape[0]
+        H = cfg.hidden
+        tp = p.world > 1
+        x = ops.embedding_q8(b.ids, self.embed_q, self.embed_s, p.vocab_start)
+        if tp:
+            self.comm.all_reduce_(x)
+        h = torch.empty(T, H, dtype=torch.float16, device=self.device)
+        ops.rmsnorm(x, self.layers[0].ln1, cfg.rms_eps, out=h)
+        D = cfg.head_dim
+        q_out = torch.empty(T, self.q_rows, dtype=torch.bfloat16, device=self.device)
+        attn = torch.empty(T, p.local_heads, D, dtype=torch.float16, device=self.device)
+        act = torch.empty(T, p.local_inter, dtype=torch.float16, device=self.device)
+        partial = torch.empty(T, H, dtype=torch.float32, device=self.device) if tp else None
+        for l, L in enumerate(self.layers):
+            kc, vc = self.kv.k[l], self.kv.v[l]
+            ops.w8a16_qkv_rope_append(h, L.w_qkv, L.s_qkv, L.b_qkv, self.q_rows, self.kv_rows, D, b.positions,
+                                      b.slots, self.cos, self.sin, kc, vc, q_out=q_out)
+            q3 = q_out.view(T, p.local_heads, D)
+            if b.is_decode:
+                ops.paged_decode_attention(q3, kc, vc, b.block_tables, b.context_lens, self.scale,
+                                           b.attn_splits, b.attn_keys_per_split, out=attn)
+            else:
+                ops.paged_prefill_attention(q3, kc, vc, b.block_tables, b.cu_q, b.q_start, b.context_lens, b.max_q,
+                                            self.scale, out=attn)
+            a2 = attn.view(T, self.q_rows)
+            if tp:
+                self._mm_f32(a2, L.w_o, L.s_o, partial)
+                self._all_reduce_add_norm(x, partial, L.ln2, h)
+            else:
+                ops.w8a16_residual_(a2, L.w_o, L.s_o, x)
+                ops.rmsnorm(x, L.ln2, cfg.rms_eps, out=h)
+            act = ops.w8a16_swiglu(h, L.w_gu, L.s_gu)
+            g_next = self.layers[l + 1].ln1 if l + 1 < len(self.layers) else self.final_norm
+            if tp:
+                self._mm_f32(act, L.w_d, L.s_d, partial)
+                self._all_reduce_add_norm(x, partial, g_next, h)
+            else:
+                ops.w8a16_residual_(act, L.w_d, L.s_d, x)
+                ops.rmsnorm(x, g_next, cfg.rms_eps, out=h)
+        hl = h.index_select(0, b.last_rows)
+        logits = ops.w8a16_linear(hl, self.head_q, self.head_s, out_dtype=torch.float32)
+        if tp:
+            keys = torch.empty(hl.shape[0], dtype=torch.int64, device=self.device)
+            ops.argmax_rows(logits, p.vocab_start, keys=keys)
+            self.comm.all_reduce_max_(keys)
+            from ..parallel.dist import unpack_argmax
+            return unpack_argmax(keys)
+        return ops.argmax_rows(logits, 0)
+
+    def _mm_f32(self, x, w, s, out):
+        return ops.w8a16_linear_out(x, w, s, out)

@@ -1,0 +1,405 @@
+"""Operator layer: sm_100a kernels for CUDA tensors, fp32 reference math for CPU tensors.
+
+The CPU branch is the numerics oracle used by the CPU/gloo tests; it is not a fallback for CUDA tensors.  A CUDA
+tensor always goes to the compiled extension and raises if the extension is missing (there is no silent eager path
+on the GPU).
+
+Scratch memory (split-K partials and tickets, attention split partials) comes from :class:`Workspace`, which the
+engine sizes once before CUDA-graph capture so captured kernels always see the same addresses.
+"""
+from __future__ import annotations
+
+import math
+import threading
+from typing import Optional, Tuple
+
+import torch
+
+_C = None
+_C_ERR: Optional[BaseException] = None
+try:  # the in-tree build: python setup.py build_ext --inplace
+    from .. import _C as _C  # type: ignore[attr-defined]
+except Exception as e:  # pragma: no cover - depends on the build
+    _C_ERR = e
+
+
+def ext():
+    """The compiled extension; raises with the import error if it is unavailable."""
+    if _C is None:
+        raise RuntimeError(
+            "hrm_flashrenderer_b200._C is not built or failed to load "
+            f"({_C_ERR!r}); run `python setup.py build_ext --inplace`")
+    return _C
+
+
+def has_ext() -> bool:
+    return _C is not None
+
+
+class _LaunchCounter:
+    """Counts kernels launched through this module (used by the benchmark to report its own launches)."""
+
+    def __init__(self):
+        self.enabled = False
+        self.count = 0
+
+    def reset(self):
+        self.count = 0
+
+    def add(self, n: int = 1):
+        if self.enabled:
+            self.count += n
+
+
+LAUNCH_COUNTER = _LaunchCounter()
+
+
+# ------------------------------------------------------------------------------------------------ workspace
+class Workspace:
+    """Per-device scratch: fp32 split-K partials + int32 tickets (zeroed once; kernels re-arm them)."""
+
+    _lock = threading.Lock()
+    _per_device: dict = {}
+
+    def __init__(self, device: torch.device, floats: int = 1 << 20, counters: int = 1 << 14):
+        self.device = device
+        self.ws = torch.empty(floats, dtype=torch.float32, device=device)
+        self.counters = torch.zeros(counters, dtype=torch.int32, device=device)
+        self.frozen = False
+
+    def ensure(self, floats: int, counters: int = 0) -> None:
+        if floats > self.ws.numel():
+            if self.frozen:
+                raise RuntimeError(f"workspace frozen (graph capture) but {floats} floats requested")
+            self.ws = torch.empty(int(floats * 1.25) + 1024, dtype=torch.float32, device=self.device)
+        if counters > self.counters.numel():
+            if self.frozen:
+                raise RuntimeError("workspace frozen (graph capture) but more split-K counters requested")
+            self.counters = torch.zeros(int(counters * 1.25) + 64, dtype=torch.int32, device=self.device)
+
+    @classmethod
+    def get(cls, device) -> "Workspace":
+        device = torch.device(device)
+        key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+        with cls._lock:
+            w = cls._per_device.get(key)
+            if w is None:
+                w = cls._per_device[key] = Workspace(torch.device("cuda", key[1]))
+            return w
+
+
+def gemm_plan(M: int, N: int, K: int, force_splits: int = 0) -> dict:
+    bn, nt, mt, kt, splits, wsf, cnt = ext().gemm_plan(int(M), int(N), int(K), int(force_splits))
+    return dict(bn=bn, n_tiles=nt, m_tiles=mt, k_tiles=kt, splits=splits, ws_floats=wsf, counters=cnt)
+
+
+def _ws_for(M, N, K, device, force_splits=0):
+    p = gemm_plan(M, N, K, force_splits)
+    w = Workspace.get(device)
+    w.ensure(p["ws_floats"], p["counters"])
+    return w
+
+
+def _as_f16_2d(x: torch.Tensor) -> torch.Tensor:
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.dtype != torch.float16:
+        x2 = x2.to(torch.float16)
+    if x2.stride(-1) != 1 or (x2.data_ptr() % 16) or (x2.stride(0) * 2) % 16:
+        x2 = x2.contiguous()
+    return x2
+
+
+# ------------------------------------------------------------------------------------------------ GEMMs
+def w8a16_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                 out_dtype: Optional[torch.dtype] = None, force_splits: int = 0) -> torch.Tensor:
+    """``y = x @ (qweight * scale[:, None])^T (+ bias)``; int8 weights ``[N, K]`` with per-row fp32 scales."""
+    N, K = qweight.shape
+    if not x.is_cuda:
+        y = x.to(torch.float32) @ (qweight.to(torch.float32) * scale.to(torch.float32)[:, None]).t()
+        if bias is not None:
+            y = y + bias.to(torch.float32)
+        return y.to(out_dtype) if out_dtype is not None else y
+    C = ext()
+    lead = x.shape[:-1]
+    x2 = _as_f16_2d(x)
+    M = x2.shape[0]
+    od = out_dtype or torch.float16
+    out = torch.empty(M, N, dtype=torch.float32 if od == torch.float32 else torch.float16, device=x.device)
+    w = _ws_for(M, N, K, x.device, force_splits)
+    C.w8a16_gemm(x2, qweight, scale, bias, out, w.ws, w.counters, force_splits)
+    LAUNCH_COUNTER.add()
+    out = out if out.dtype == od else out.to(od)
+    return out.reshape(*lead, N)
+
+
+def w8a16_linear_out(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, out: torch.Tensor,
+                     force_splits: int = 0) -> torch.Tensor:
+    """``out[:] = x @ W^T`` into a preallocated f16/f32 ``[M, N]`` buffer."""
+    if not x.is_cuda:
+        out.copy_(x.to(torch.float32) @ (qweight.to(torch.float32) * scale[:, None]).t())
+        return out
+    x2 = _as_f16_2d(x)
+    w = _ws_for(x2.shape[0], qweight.shape[0], qweight.shape[1], x.device, force_splits)
+    ext().w8a16_gemm(x2, qweight, scale, None, out, w.ws, w.counters, force_splits)
+    LAUNCH_COUNTER.add()
+    return out
+
+
+def w8a16_residual_(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, resid: torch.Tensor,
+                    force_splits: int = 0) -> torch.Tensor:
+    """``resid += x @ W^T`` in place (fp32 residual stream)."""
+    if not x.is_cuda:
+        resid += x.to(torch.float32) @ (qweight.to(torch.float32) * scale[:, None]).t()
+        return resid
+    x2 = _as_f16_2d(x)
+    w = _ws_for(x2.shape[0], qweight.shape[0], qweight.shape[1], x.device, force_splits)
+    ext().w8a16_gemm_residual(x2, qweight, scale, resid, w.ws, w.counters, force_splits)
+    LAUNCH_COUNTER.add()
+    return resid
+
+
+def swiglu_half(F: int) -> int:
+    """Gate (= up) rows per packed tile: 64 (the kernel's 128-row tile) when possible, else the whole F (CPU only)."""
+    return 64 if F % 64 == 0 else F
+
+
+def interleave_gate_up(gate_q: torch.Tensor, up_q: torch.Tensor, gate_s: torch.Tensor, up_s: torch.Tensor,
+                       half: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Pack gate/up rows as [64 gate rows, the matching 64 up rows] per 128-row tile (the SwiGLU epilogue layout)."""
+    F, K = gate_q.shape
+    h = half or swiglu_half(F)
+    assert F % h == 0
+    q = torch.stack([gate_q.view(F // h, h, K), up_q.view(F // h, h, K)], dim=1).reshape(2 * F, K)
+    s = torch.stack([gate_s.view(F // h, h), up_s.view(F // h, h)], dim=1).reshape(2 * F)
+    return q.contiguous(), s.contiguous()
+
+
+def w8a16_swiglu(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, force_splits: int = 0) -> torch.Tensor:
+    """``silu(x @ Wg^T) * (x @ Wu^T)`` with ``w_gu`` packed by :func:`interleave_gate_up`; f16 output."""
+    N2, K = w_gu.shape
+    F = N2 // 2
+    if not x.is_cuda:
+        h = swiglu_half(F)
+        y = x.to(torch.float32) @ (w_gu.to(torch.float32) * s_gu[:, None]).t()
+        y = y.view(*y.shape[:-1], F // h, 2, h)
+        return (torch.nn.functional.silu(y[..., 0, :]) * y[..., 1, :]).reshape(*x.shape[:-1], F)
+    x2 = _as_f16_2d(x)
+    out = torch.empty(x2.shape[0], F, dtype=torch.float16, device=x.device)
+    w = _ws_for(x2.shape[0], N2, K, x.device, force_splits)
+    ext().w8a16_gemm_swiglu(x2, w_gu, s_gu, out, w.ws, w.counters, force_splits)
+    LAUNCH_COUNTER.add()
+    return out.reshape(*x.shape[:-1], F)
+
+
+def w8a16_qkv_rope_append(x: torch.Tensor, w_qkv: torch.Tensor, s_qkv: torch.Tensor, bias: Optional[torch.Tensor],
+                          q_rows: int, kv_rows: int, head_dim: int, positions: torch.Tensor, slots: torch.Tensor,
+                          cos_t: torch.Tensor, sin_t: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                          q_out: Optional[torch.Tensor] = None, force_splits: int = 0) -> torch.Tensor:
+    """Fused QKV projection + bias + rotate-half RoPE + paged KV append.  Returns q ``[M, q_rows]`` bf16."""
+    M = x.reshape(-1, x.shape[-1]).shape[0]
+    if not x.is_cuda:
+        y = w8a16_linear(x.reshape(M, -1), w_qkv, s_qkv, bias)
+        D = head_dim
+        q = y[:, :q_rows].view(M, -1, D)
+        k = y[:, q_rows:q_rows + kv_rows].view(M, -1, D)
+        v = y[:, q_rows + kv_rows:].view(M, -1, D)
+        from ..models.oracle import apply_rope
+        q = apply_rope(q, cos_t, sin_t, positions.long())
+        k = apply_rope(k, cos_t, sin_t, positions.long())
+        bs = k_cache.shape[2]
+        for m in range(M):
+            s = int(slots[m])
+            if s >= 0:
+                k_cache[s // bs, :, s % bs] = k[m].to(k_cache.dtype)
+                v_cache[s // bs, :, s % bs] = v[m].to(v_cache.dtype)
+        qb = q.reshape(M, q_rows).to(torch.bfloat16)
+        if q_out is not None:
+            q_out.copy_(qb)
+            return q_out
+        return qb
+    x2 = _as_f16_2d(x)
+    if q_out is None:
+        q_out = torch.empty(M, q_rows, dtype=torch.bfloat16, device=x.device)
+    w = _ws_for(M, w_qkv.shape[0], w_qkv.shape[1], x.device, force_splits)
+    ext().w8a16_gemm_qkv(x2, w_qkv, s_qkv, bias, q_rows, kv_rows, head_dim, positions, slots, cos_t, sin_t, q_out,
+                         k_cache, v_cache, w.ws, w.counters, force_splits)
+    LAUNCH_COUNTER.add()
+    return q_out
+
+
+# ------------------------------------------------------------------------------------------------ norms / embed
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out_dtype: Optional[torch.dtype] = None,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not x.is_cuda:
+        xf = x.to(torch.float32)
+        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.to(torch.float32)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y.to(out_dtype) if out_dtype is not None else y
+    xf = x if x.dtype == torch.float32 and x.is_contiguous() else x.to(torch.float32).contiguous()
+    if out is None:
+        out = torch.empty(xf.shape, dtype=torch.float16, device=x.device)
+    ext().rmsnorm(xf, None, w, float(eps), out)
+    LAUNCH_COUNTER.add()
+    return out if out_dtype in (None, torch.float16) else out.to(out_dtype)
+
+
+def add_rmsnorm_(x: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: float,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``x += delta`` (in place, fp32) then return ``rmsnorm(x)`` (f16 on CUDA, fp32 on CPU)."""
+    if not x.is_cuda:
+        x += delta.to(x.dtype)
+        return rmsnorm(x, w, eps, out=out)
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.float16, device=x.device)
+    ext().rmsnorm(x, delta.contiguous(), w, float(eps), out)
+    LAUNCH_COUNTER.add()
+    return out
+
+
+def embedding_q8(ids: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, vocab_start: int = 0,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Masked int8 row lookup: rows outside ``[vocab_start, vocab_start + V_local)`` are zero (vocab parallel)."""
+    V, H = qweight.shape
+    if not ids.is_cuda:
+        local = ids.long() - vocab_start
+        mask = (local >= 0) & (local < V)
+        lc = local.clamp(0, V - 1)
+        emb = qweight[lc].to(torch.float32) * scale[lc].unsqueeze(-1)
+        return emb * mask.unsqueeze(-1).to(emb.dtype)
+    ids64 = ids.to(torch.int64).contiguous()
+    if out is None:
+        out = torch.empty(*ids.shape, H, dtype=torch.float32, device=ids.device)
+    ext().embed_q8(ids64, qweight, scale, int(vocab_start), out)
+    LAUNCH_COUNTER.add()
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ attention
+def decode_splits(max_ctx: int, batch_heads: int, block_size: int = 16, sms: int = 148) -> Tuple[int, int]:
+    """Split-K plan for decode attention: enough CTAs to cover ~2 waves, at least 4 blocks per split."""
+    blocks = max(1, (max_ctx + block_size - 1) // block_size)
+    want = max(1, (2 * sms + batch_heads - 1) // max(1, batch_heads))
+    splits = max(1, min(want, blocks // 4 if blocks >= 8 else 1))
+    per = (blocks + splits - 1) // splits
+    splits = (blocks + per - 1) // per
+    return splits, per * block_size
+
+
+def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                           context_lens: torch.Tensor, scale: Optional[float] = None, splits: int = 0,
+                           keys_per_split: int = 0, out: Optional[torch.Tensor] = None,
+                           max_ctx: Optional[int] = None) -> torch.Tensor:
+    """One query token per sequence.  ``q [B, Hq, D]`` bf16 -> ``[B, Hq, D]`` f16."""
+    B, Hq, D = q.shape
+    scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    if not q.is_cuda:
+        from ..runtime.kv_cache import gather_kv_reference
+        Hk = k_cache.shape[1]
+        outs = []
+        for b in range(B):
+            L = int(context_lens[b])
+            tab = block_tables[b].tolist()
+            k = gather_kv_reference(k_cache, tab, L).float()
+            v = gather_kv_reference(v_cache, tab, L).float()
+            kk = k.repeat_interleave(Hq // Hk, dim=1)
+            vv = v.repeat_interleave(Hq // Hk, dim=1)
+            s = torch.einsum("hd,shd->hs", q[b].float(), kk) * scale
+            outs.append(torch.einsum("hs,shd->hd", torch.softmax(s, -1), vv))
+        res = torch.stack(outs).to(torch.float16)
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
+    bs = k_cache.shape[2]
+    if splits <= 0:
+        mc = int(max_ctx) if max_ctx is not None else int(block_tables.shape[1] * bs)
+        splits, keys_per_split = decode_splits(mc, B * k_cache.shape[1], bs, ext().sm_count())
+    if out is None:
+        out = torch.empty(B, Hq, D, dtype=torch.float16, device=q.device)
+    ws = Workspace.get(q.device)
+    need = ext().decode_attn_ws_floats(B, Hq, D, splits) if splits > 1 else 0
+    ws.ensure(need)
+    ext().decode_attention(q.contiguous(), k_cache, v_cache, block_tables, context_lens, out, ws.ws, splits,
+                           keys_per_split, float(scale))
+    LAUNCH_COUNTER.add(2 if splits > 1 else 1)
+    return out
+
+
+def paged_prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                            block_tables: torch.Tensor, cu_q: torch.Tensor, q_start: torch.Tensor,
+                            context_lens: torch.Tensor, max_q: int, scale: Optional[float] = None,
+                            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal attention of varlen query chunks ``q [Tq, Hq, D]`` against the paged cache (chunk already appended)."""
+    Tq, Hq, D = q.shape
+    scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    if not q.is_cuda:
+        from ..runtime.kv_cache import gather_kv_reference
+        from ..models.oracle import attention
+        Hk = k_cache.shape[1]
+        res = torch.zeros(Tq, Hq, D)
+        for s in range(q_start.numel()):
+            a, b = int(cu_q[s]), int(cu_q[s + 1])
+            L = int(context_lens[s])
+            tab = block_tables[s].tolist()
+            k = gather_kv_reference(k_cache, tab, L).float()
+            v = gather_kv_reference(v_cache, tab, L).float()
+            pos = torch.arange(int(q_start[s]), int(q_start[s]) + (b - a))
+            res[a:b] = attention(q[a:b].float() * (scale * math.sqrt(D)), k, v, pos, Hq // Hk)
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res.to(torch.float16)
+    if out is None:
+        out = torch.empty(Tq, Hq, D, dtype=torch.float16, device=q.device)
+    ext().prefill_attention(q.contiguous(), k_cache, v_cache, block_tables, cu_q, q_start, context_lens, out,
+                            int(max_q), float(scale))
+    LAUNCH_COUNTER.add()
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ sampling
+def argmax_rows(logits: torch.Tensor, vocab_start: int = 0, keys: Optional[torch.Tensor] = None,
+                tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Greedy token per row (global id = local + vocab_start); ties -> lowest id.  Optionally packed keys."""
+    if not logits.is_cuda:
+        from ..parallel.dist import pack_argmax
+        val, idx = torch.max(logits.float(), dim=-1)
+        if keys is not None:
+            keys.copy_(pack_argmax(val, idx + vocab_start))
+        return idx.to(torch.int64) + vocab_start
+    if tokens is None:
+        tokens = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
+    ext().argmax_rows(logits, int(vocab_start), keys, tokens)
+    LAUNCH_COUNTER.add()
+    return tokens
+
+
+# ------------------------------------------------------------------------------------------------ decode bookkeeping
+def decode_prepare(positions: torch.Tensor, tables: torch.Tensor, block_size: int, active: Optional[torch.Tensor],
+                   slots: torch.Tensor, context_lens: torch.Tensor) -> None:
+    """``slots[b] = table[b][pos // bs] * bs + pos % bs`` (``-1`` when inactive); ``context_lens = pos + 1``."""
+    if positions.is_cuda:
+        ext().decode_prepare(positions, tables, int(block_size), active, slots, context_lens)
+        LAUNCH_COUNTER.add()
+        return
+    pos = positions.long()
+    blk = (pos // block_size).clamp(max=tables.shape[1] - 1)
+    s = tables.gather(1, blk.view(-1, 1)).view(-1).long() * block_size + pos % block_size
+    if active is not None:
+        s = torch.where(active != 0, s, torch.full_like(s, -1))
+    slots.copy_(s.to(slots.dtype))
+    context_lens.copy_((pos + 1).to(context_lens.dtype))
+
+
+def decode_advance(tokens: torch.Tensor, ids: torch.Tensor, positions: torch.Tensor,
+                   active: Optional[torch.Tensor]) -> None:
+    """``ids = tokens``, ``positions += 1`` for active rows."""
+    if tokens.is_cuda:
+        ext().decode_advance(tokens, ids, positions, active)
+        LAUNCH_COUNTER.add()
+        return
+    on = torch.ones_like(positions, dtype=torch.bool) if active is None else active != 0
+    ids.copy_(torch.where(on, tokens, ids))
+    positions.copy_(torch.where(on, positions + 1, positions))

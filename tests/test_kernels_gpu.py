@@ -1,0 +1,202 @@
+"""sm_100a kernels vs plain PyTorch fp32 references of the same op (run on a B200 with -m gpu)."""
+import math
+
+import pytest
+import torch
+
+from hrm_flashrenderer_b200 import ops
+from hrm_flashrenderer_b200.models.weights import quantize_rows
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _qw(N, K, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    qt = quantize_rows(torch.randn(N, K, generator=g) * 0.02)
+    return qt.q.to(DEV), qt.scale.to(DEV)
+
+
+def _x(M, K, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return torch.randn(M, K, generator=g).to(DEV, torch.float16)
+
+
+def _ref(x, q, s):
+    return x.float() @ (q.float() * s[:, None]).t()
+
+
+def test_extension_loaded():
+    assert ops.has_ext(), "the CUDA extension must be built and loaded on a GPU box"
+
+
+@pytest.mark.parametrize("M", [1, 5, 16, 33, 64, 100, 257])
+@pytest.mark.parametrize("N,K", [(128, 128), (384, 512), (1000, 1024), (256, 4096)])
+def test_w8a16_gemm(M, N, K):
+    q, s = _qw(N, K, 1)
+    x = _x(M, K, 2)
+    y = ops.w8a16_linear(x, q, s, out_dtype=torch.float32)
+    ref = _ref(x, q, s)
+    err = (y - ref).abs().max().item()
+    assert err <= 1e-3 * max(1.0, ref.abs().max().item()), err
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7])
+def test_w8a16_split_k_deterministic(splits):
+    q, s = _qw(512, 2048, 3)
+    x = _x(16, 2048, 4)
+    a = ops.w8a16_linear(x, q, s, out_dtype=torch.float32, force_splits=splits)
+    b = ops.w8a16_linear(x, q, s, out_dtype=torch.float32, force_splits=splits)
+    assert torch.equal(a, b)
+    ref = _ref(x, q, s)
+    assert (a - ref).abs().max().item() < 1e-3
+
+
+def test_w8a16_f16_out_and_bias():
+    q, s = _qw(256, 512, 5)
+    x = _x(9, 512, 6)
+    bias = torch.randn(256, device=DEV)
+    y = ops.w8a16_linear(x, q, s, bias=bias)
+    assert y.dtype == torch.float16
+    ref = _ref(x, q, s) + bias
+    assert (y.float() - ref).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("M", [1, 16, 130])
+def test_w8a16_residual(M):
+    q, s = _qw(1024, 768, 7)
+    x = _x(M, 768, 8)
+    r0 = torch.randn(M, 1024, device=DEV)
+    r = r0.clone()
+    ops.w8a16_residual_(x, q, s, r)
+    assert (r - (r0 + _ref(x, q, s))).abs().max().item() < 1e-3
+
+
+@pytest.mark.parametrize("M", [1, 16, 70])
+def test_w8a16_swiglu(M):
+    F, K = 384, 512
+    gq, gs = _qw(F, K, 9)
+    uq, us = _qw(F, K, 10)
+    wq, ws = ops.interleave_gate_up(gq, uq, gs, us)
+    x = _x(M, K, 11)
+    y = ops.w8a16_swiglu(x, wq, ws)
+    ref = torch.nn.functional.silu(_ref(x, gq, gs)) * _ref(x, uq, us)
+    assert (y.float() - ref).abs().max().item() < 1e-2
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("M", [1, 7, 40])
+def test_w8a16_qkv_rope_append(D, M):
+    from hrm_flashrenderer_b200.models.oracle import apply_rope, rope_tables
+    from hrm_flashrenderer_b200.config import TINY
+    from dataclasses import replace
+    Hq, Hk, K = 4, 2, 256
+    cfg = replace(TINY, head_dim=D, rope_theta=10000.0)
+    cos, sin = rope_tables(cfg, 512)
+    q_rows, kv_rows = Hq * D, Hk * D
+    wq, ws = _qw(q_rows + 2 * kv_rows, K, 12)
+    bias = torch.randn(q_rows + 2 * kv_rows, device=DEV) * 0.1
+    x = _x(M, K, 13)
+    pos = torch.randint(0, 500, (M,), dtype=torch.int32)
+    nb, bs = 64, 16
+    perm = torch.randperm(nb * bs)[:M]
+    slots = perm.to(torch.int32)
+    slots[0] = -1 if M > 1 else slots[0]
+    kc = torch.zeros(nb, Hk, bs, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    q = ops.w8a16_qkv_rope_append(x, wq, ws, bias, q_rows, kv_rows, D, pos.to(DEV), slots.to(DEV), cos.to(DEV),
+                                  sin.to(DEV), kc, vc)
+    y = (_ref(x, wq, ws) + bias).cpu()
+    qr = apply_rope(y[:, :q_rows].view(M, Hq, D), cos, sin, pos.long()).reshape(M, q_rows)
+    kr = apply_rope(y[:, q_rows:q_rows + kv_rows].view(M, Hk, D), cos, sin, pos.long())
+    vr = y[:, q_rows + kv_rows:].view(M, Hk, D)
+    assert (q.float().cpu() - qr).abs().max().item() < 2e-2
+    kcc, vcc = kc.float().cpu(), vc.float().cpu()
+    for m in range(M):
+        sl = int(slots[m])
+        if sl < 0:
+            continue
+        assert (kcc[sl // bs, :, sl % bs] - kr[m]).abs().max().item() < 2e-2
+        assert (vcc[sl // bs, :, sl % bs] - vr[m]).abs().max().item() < 2e-2
+
+
+def _paged(B, lens, Hk, D, bs=16, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    nb = sum((L + bs - 1) // bs for L in lens) + 4
+    perm = torch.randperm(nb, generator=g)
+    kc = torch.randn(nb, Hk, bs, D, generator=g).to(torch.bfloat16)
+    vc = torch.randn(nb, Hk, bs, D, generator=g).to(torch.bfloat16)
+    maxb = max((L + bs - 1) // bs for L in lens)
+    tab = torch.zeros(B, maxb, dtype=torch.int32)
+    i = 0
+    for b, L in enumerate(lens):
+        n = (L + bs - 1) // bs
+        tab[b, :n] = perm[i:i + n].to(torch.int32)
+        i += n
+    return kc, vc, tab
+
+
+@pytest.mark.parametrize("D,Hq,Hk", [(128, 8, 1), (128, 40, 8), (64, 8, 2)])
+@pytest.mark.parametrize("lens", [[1, 17, 300], [4096], [33, 2000]])
+@pytest.mark.parametrize("splits", [0, 1])
+def test_paged_decode_attention(D, Hq, Hk, lens, splits):
+    B = len(lens)
+    kc, vc, tab = _paged(B, lens, Hk, D)
+    q = torch.randn(B, Hq, D).to(torch.bfloat16)
+    cl = torch.tensor(lens, dtype=torch.int32)
+    ref = ops.paged_decode_attention(q, kc, vc, tab, cl)
+    kw = {} if splits == 0 else dict(splits=1, keys_per_split=tab.shape[1] * 16)
+    out = ops.paged_decode_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), tab.to(DEV), cl.to(DEV), **kw)
+    assert (out.float().cpu() - ref.float()).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("D,Hq,Hk", [(128, 8, 2), (64, 4, 4)])
+@pytest.mark.parametrize("chunks", [[(0, 100)], [(0, 37), (50, 64), (7, 1)]])
+def test_paged_prefill_attention(D, Hq, Hk, chunks):
+    """chunks: (q_start, q_len) per sequence; context = q_start + q_len."""
+    lens = [a + b for a, b in chunks]
+    kc, vc, tab = _paged(len(chunks), lens, Hk, D, seed=3)
+    Tq = sum(b for _, b in chunks)
+    q = torch.randn(Tq, Hq, D).to(torch.bfloat16)
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor([b for _, b in chunks]), 0)), dtype=torch.int32)
+    qs = torch.tensor([a for a, _ in chunks], dtype=torch.int32)
+    cl = torch.tensor(lens, dtype=torch.int32)
+    mq = max(b for _, b in chunks)
+    ref = ops.paged_prefill_attention(q, kc, vc, tab, cu, qs, cl, mq)
+    out = ops.paged_prefill_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), tab.to(DEV), cu.to(DEV), qs.to(DEV),
+                                      cl.to(DEV), mq)
+    assert (out.float().cpu() - ref.float()).abs().max().item() < 2e-2
+
+
+def test_rmsnorm_and_add():
+    x = torch.randn(5, 1024, device=DEV)
+    d = torch.randn(5, 1024, device=DEV)
+    w = torch.randn(1024, device=DEV)
+    ref_x = x + d
+    ref = ref_x * torch.rsqrt(ref_x.pow(2).mean(-1, keepdim=True) + 1e-5) * w
+    xx = x.clone()
+    h = ops.add_rmsnorm_(xx, d, w, 1e-5)
+    assert torch.allclose(xx, ref_x)
+    assert (h.float() - ref).abs().max().item() < 1e-2
+
+
+def test_embedding_vocab_parallel():
+    q, s = _qw(100, 64, 14)
+    ids = torch.tensor([0, 99, 150, 250, 120], device=DEV)
+    out = ops.embedding_q8(ids, q, s, vocab_start=100)
+    ref = ops.embedding_q8(ids.cpu(), q.cpu(), s.cpu(), vocab_start=100)
+    assert torch.allclose(out.cpu(), ref)
+
+
+def test_argmax_ties_lowest_index():
+    logits = torch.randn(4, 5000, device=DEV)
+    logits[1, 17] = 100.0
+    logits[1, 4000] = 100.0
+    keys = torch.empty(4, dtype=torch.int64, device=DEV)
+    t = ops.argmax_rows(logits, vocab_start=10, keys=keys)
+    assert t[1].item() == 27
+    ref = torch.argmax(logits, -1) + 10
+    assert torch.equal(t, ref)
+    from hrm_flashrenderer_b200.parallel.dist import pack_argmax
+    val, idx = torch.max(logits, -1)
+    assert torch.equal(keys.cpu(), pack_argmax(val.cpu(), idx.cpu() + 10))

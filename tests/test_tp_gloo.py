@@ -1,0 +1,77 @@
+"""Config 1: tiny Llama on CPU/gloo, TP world_size=2 must match the unsharded TP=1 run token-for-token.
+
+Architecture: 4 layers, hidden 256, 8 q heads / 2 kv heads (head_dim 32), SwiGLU 688, vocab 1024, eps 1e-5,
+theta 1e4, no bias; weights N(0, 0.02) from seed 0 quantised per row; paged KV block 16; 2 prompts x 16 ids from
+seed 1; 32 greedy tokens.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from hrm_flashrenderer_b200.config import TINY, EngineConfig
+from hrm_flashrenderer_b200.models.weights import synth_weights
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _prompts():
+    g = torch.Generator().manual_seed(1)
+    return [torch.randint(0, 1024, (16,), generator=g).tolist() for _ in range(2)]
+
+
+def _run(rank, world, port, q):
+    from hrm_flashrenderer_b200.parallel.dist import init_dist, destroy
+    from hrm_flashrenderer_b200.parallel.comm import TPComm
+    from hrm_flashrenderer_b200.models.llama import LlamaW8
+    from hrm_flashrenderer_b200.runtime.engine import InferenceEngine
+    torch.set_num_threads(2)
+    init_dist(rank, world, "127.0.0.1", port, backend="gloo", timeout_s=60)
+    try:
+        w = synth_weights(TINY, seed=0)
+        model = LlamaW8.from_weights(TINY, w, rank=rank, world=world, device="cpu", comm=TPComm(), max_pos=256)
+        eng = InferenceEngine(model, EngineConfig(max_seq_len=64, max_batch=2, use_cuda_graphs=False), num_blocks=16)
+        out = eng.generate(_prompts(), 32, stop_on_eos=False)
+        q.put((rank, out))
+    finally:
+        destroy()
+
+
+def _spawn(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_run, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, out = q.get(timeout=300)
+        res[r] = out
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return res
+
+
+def test_tp2_matches_tp1_token_for_token():
+    tp1 = _spawn(1)[0]
+    tp2 = _spawn(2)
+    assert tp2[0] == tp2[1], "ranks disagree"
+    assert tp2[0] == tp1
+    assert all(len(o) == 32 for o in tp1)
+
+
+def test_tp1_matches_oracle():
+    from hrm_flashrenderer_b200.models.oracle import OracleLlama
+    w = synth_weights(TINY, seed=0)
+    ref = OracleLlama(TINY, w, max_pos=256).generate(_prompts(), 32)
+    assert _spawn(1)[0] == ref
