@@ -178,6 +178,11 @@ __global__ void decode_combine_kernel(const DecodeAttnArgs a) {
   a.out[(size_t)bh * D + d] = __float2half_rn(L > 0.f ? A / L : 0.f);
 }
 
+void decode_combine_launch(const DecodeAttnArgs& a, cudaStream_t s) {
+  if (a.D == 128) decode_combine_kernel<128><<<a.B * a.Hq, 128, 0, s>>>(a);
+  else decode_combine_kernel<64><<<a.B * a.Hq, 64, 0, s>>>(a);
+}
+
 size_t decode_attn_ws_floats(int B, int Hq, int D, int splits) { return (size_t)B * Hq * splits * (D + 2); }
 
 void decode_attn_launch(const DecodeAttnArgs& a, cudaStream_t s) {

@@ -1,0 +1,342 @@
+// Paged decode attention on tcgen05 tensor cores (one query token per sequence, GQA).
+//
+// One CTA = (context split, kv head, sequence).  Keys go on the MMA M side ("swap-AB"), the group's query heads
+// (padded to 16) on N:
+//     S^T[128 keys x 16]  = K_tile[128 x D] . Q^T            (A = K tile, K-major; B = Q, K-major)
+//     O^T[D x 16]        += V_tile^T[D x 128] . P^T          (A = V tile, MN-major; B = P^T, K-major)
+// so no tensor-core work is wasted on padding rows and every K/V byte is read once per kv head.
+//
+// K/V tiles of 128 keys (8 paged blocks of 16 tokens) are fetched by TMA from the paged cache viewed as a 4-D tensor
+// [num_blocks][Hk][16][D]: one box = 16 tokens x 64 dims (2 KB, 128-byte swizzle), so the smem tile lands directly in
+// the canonical UMMA layout (two 64-dim regions of [128 keys][128 B]).  The same layout serves as the K-major
+// A operand of S and as the MN-major A operand of O.  A 3-slot ring of 32 KB (K0, V0, K1, V1, ...) keeps loads in
+// flight; S is double-buffered in TMEM so the next S MMA overlaps the softmax of the current tile.
+//
+// Warp roles: warp 0 TMA producer, warp 1 MMA issuer (one thread), warps 2-5 softmax / O rescale / epilogue
+// (thread = TMEM lane = key within the tile, or = output dim for O).  Softmax uses exp2 with the scale folded in;
+// the running max is exchanged across the 4 warps each tile, row sums stay per thread until the end.  Splits are
+// merged by the existing combine kernel (partials stored in natural-log units).
+#include "common.cuh"
+#include "kernels.h"
+#include "gemm_w8a16.h"
+
+#include <stdexcept>
+
+namespace hrm {
+
+namespace {
+constexpr int kKeys = 128;              // keys per tile
+constexpr int kD = 128;                 // head dim supported by this kernel
+constexpr int kN = 16;                  // padded heads per group
+constexpr int kSlotBytes = kKeys * kD * 2;   // 32 KB: one K or V tile
+constexpr int kSlots = 3;
+constexpr int kThreads = 6 * 32;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct Smem {
+  static constexpr int kRing = 0;                                  // kSlots x 32 KB
+  static constexpr int kQ = kRing + kSlots * kSlotBytes;           // 2 regions x 16 rows x 128 B = 4 KB
+  static constexpr int kP = kQ + 2 * kN * 128;                     // 4 KB
+  static constexpr int kRed = kP + 2 * kN * 128;                   // [4 warps][16] floats
+  static constexpr int kBar = kRed + 4 * kN * 4 + 64 * 4;
+  static constexpr int kBytes = kBar + 16 * 8 + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+};
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 2)
+attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                      const DecodeAttnArgs a, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = base + Smem::kRing;
+  uint8_t* qs = base + Smem::kQ;
+  uint8_t* ps = base + Smem::kP;
+  float* red = reinterpret_cast<float*>(base + Smem::kRed);     // [4][16] tile maxima, reused for final sums
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + Smem::kBar);
+  uint64_t* empty = full + kSlots;
+  uint64_t* sfull = empty + kSlots;     // [2]
+  uint64_t* pfull = sfull + 2;
+  uint64_t* pvdone = pfull + 1;
+  uint64_t* qready = pvdone + 1;
+  uint64_t* mdone = qready + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int G = a.Hq / a.Hk;
+  const int ctx = a.context_lens[b];
+  const int k0 = split * a.keys_per_split;
+  const int k1 = min(ctx, k0 + a.keys_per_split);
+  const int nt = k1 > k0 ? (k1 - k0 + kKeys - 1) / kKeys : 0;
+  const float scale2 = a.scale * kLog2e;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&sfull[0], 1);
+    mbar_init(&sfull[1], 1);
+    mbar_init(pfull, 128);
+    mbar_init(pvdone, 1);
+    mbar_init(qready, 128);
+    mbar_init(mdone, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 64);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tO = tmem + 32;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0 && nt > 0) {
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const int* btab = a.block_tables + (size_t)b * a.max_blocks;
+      int issued = 0;
+      for (int t = 0; t < nt; ++t) {
+        const int key0 = k0 + t * kKeys;
+        for (int kv = 0; kv < 2; ++kv) {
+          const int u = 2 * t + kv, s = u % kSlots;
+          const uint32_t ph = (uint32_t)(u / kSlots) & 1u;
+          if (!mbar_wait_ab(&empty[s], ph ^ 1u, status, kErrTimeoutEmpty, abort_flag)) goto prod_done;
+          mbar_arrive_expect_tx(&full[s], kSlotBytes);
+          uint8_t* dst = ring + s * kSlotBytes;
+          for (int j = 0; j < kKeys / 16; ++j) {
+            int bi = key0 / 16 + j;
+            bi = bi < a.max_blocks ? bi : a.max_blocks - 1;
+            const int blk = btab[bi];
+            const CUtensorMap* m = kv ? &tmV : &tmK;
+            // 4-D coordinates: (dim, slot, head, block)
+            asm volatile(
+                "cp.async.bulk.tensor.4d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
+                ::"r"(smem_u32(dst + j * 2048)), "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(&full[s])),
+                  "r"(0), "r"(0), "r"(hk), "r"(blk) : "memory");
+            asm volatile(
+                "cp.async.bulk.tensor.4d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
+                ::"r"(smem_u32(dst + 16384 + j * 2048)), "l"(reinterpret_cast<uint64_t>(m)),
+                  "r"(smem_u32(&full[s])), "r"(64), "r"(0), "r"(hk), "r"(blk) : "memory");
+          }
+          ++issued;
+        }
+      }
+  prod_done:
+      // drain: every issued TMA must have landed before the CTA may exit
+      for (int u = max(0, issued - kSlots); u < issued; ++u)
+        mbar_wait(&full[u % kSlots], (uint32_t)(u / kSlots) & 1u, status, kErrTimeoutFull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nt > 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(kKeys, kN, false);   // A K-major (K tile), B K-major (Q)
+      // O^T: A = V tile MN-major (bit 15), B = P^T K-major
+      constexpr uint32_t idO = idesc_bf16_f32(kD, kN, false) | (1u << 15);
+      bool ok = mbar_wait_ab(qready, 0, status, kErrTimeoutFull, abort_flag);
+      const uint32_t qa = smem_u32(qs), pa = smem_u32(ps);
+      auto issue_s = [&](int t) -> bool {
+        const int u = 2 * t, s = u % kSlots;
+        if (!mbar_wait_ab(&full[s], (uint32_t)(u / kSlots) & 1u, status, kErrTimeoutFull, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(ring + s * kSlotBytes);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint32_t qoff = (kk >> 2) * (kN * 128) + (kk & 3) * 32;
+          umma_f16_ss(tmem + (uint32_t)(t & 1) * 16u, sdesc_sw128(ka + off), sdesc_sw128(qa + qoff), idS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+        umma_commit(&sfull[t & 1]);
+        return true;
+      };
+      ok = ok && issue_s(0);
+      for (int t = 0; ok && t < nt; ++t) {
+        if (t + 1 < nt && !issue_s(t + 1)) break;
+        if (!mbar_wait_ab(pfull, (uint32_t)t & 1u, status, kErrTimeoutDequant, abort_flag)) break;
+        const int u = 2 * t + 1, s = u % kSlots;
+        if (!mbar_wait_ab(&full[s], (uint32_t)(u / kSlots) & 1u, status, kErrTimeoutFull, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t va = smem_u32(ring + s * kSlotBytes);
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; ++kk) {
+          const uint32_t poff = (kk >> 2) * (kN * 128) + (kk & 3) * 32;
+          umma_f16_ss(tO, sdesc_sw128_mn(va + kk * 2048, 16384), sdesc_sw128(pa + poff), idO,
+                      (t > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+        umma_commit(pvdone);
+      }
+      // drain: all issued MMAs complete before TMEM is read for the last time / freed
+      umma_commit(mdone);
+      mbar_wait(mdone, 0, status, kErrTimeoutAccum);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax / correction / epilogue
+    const int t = threadIdx.x - 64;            // 0..127
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;          // TMEM lane owned by this thread
+    const int w4 = warp - 2;                   // 0..3 index for the cross-warp exchange
+    // Q^T operand: row h, dim d -> region d/64, row h, chunk ((d%64)/8) ^ (h%8)
+    {
+      const int h = t >> 3, c = t & 7;
+      for (int reg = 0; reg < 2; ++reg) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (h < G) v = *reinterpret_cast<const uint4*>(a.q + ((size_t)b * a.Hq + hk * G + h) * kD + reg * 64 + c * 8);
+        *reinterpret_cast<uint4*>(qs + reg * (kN * 128) + h * 128 + ((c ^ (h & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(qready);
+    }
+    float lsum[kN];
+    float mrun[kN];
+#pragma unroll
+    for (int h = 0; h < kN; ++h) { lsum[h] = 0.f; mrun[h] = -INFINITY; }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+
+    for (int it = 0; it < nt; ++it) {
+      mbar_wait_ab(&sfull[it & 1], (uint32_t)(it >> 1) & 1u, status, kErrTimeoutAccum, abort_flag);
+      tc_fence_after();
+      float s[kN];
+      tmem_ld16(tmem + (uint32_t)(it & 1) * 16u + ((uint32_t)(quad * 32) << 16), s);
+      const int key = k0 + it * kKeys + row;
+      const bool valid = key < k1;
+      float tmax[kN];
+#pragma unroll
+      for (int h = 0; h < kN; ++h) {
+        s[h] = valid ? s[h] * scale2 : -INFINITY;
+        tmax[h] = warp_max(s[h]);
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int h = 0; h < kN; ++h) red[w4 * kN + h] = tmax[h];
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      float corr[kN];
+      bool any_corr = false;
+#pragma unroll
+      for (int h = 0; h < kN; ++h) {
+        const float tm = fmaxf(fmaxf(red[h], red[kN + h]), fmaxf(red[2 * kN + h], red[3 * kN + h]));
+        const float mn = fmaxf(mrun[h], tm);
+        corr[h] = (mn == -INFINITY || mrun[h] == mn) ? 1.f : exp2f(mrun[h] - mn);
+        any_corr |= corr[h] != 1.f;
+        const float p = (mn == -INFINITY) ? 0.f : exp2f(s[h] - mn);
+        s[h] = p;
+        lsum[h] = lsum[h] * corr[h] + p;
+        mrun[h] = mn;
+      }
+      // previous P.V must be done before P is overwritten and O rescaled
+      if (it > 0) mbar_wait_ab(pvdone, (uint32_t)(it - 1) & 1u, status, kErrTimeoutAccum, abort_flag);
+      tc_fence_after();
+      // P^T operand: row h, key k=row -> region k/64, chunk ((k%64)/8) ^ (h%8), byte (k%8)*2
+      {
+        const int reg = row >> 6, kk = row & 63;
+        uint8_t* pb = ps + reg * (kN * 128) + ((kk & 7) << 1);
+#pragma unroll
+        for (int h = 0; h < kN; ++h) {
+          __nv_bfloat16 v = __float2bfloat16_rn(s[h]);
+          *reinterpret_cast<__nv_bfloat16*>(pb + h * 128 + ((((kk >> 3) ^ (h & 7))) << 4)) = v;
+        }
+      }
+      if (it > 0 && any_corr) {   // any_corr is uniform: every thread saw the same maxima
+        float o[kN];
+        tmem_ld16(tO + ((uint32_t)(quad * 32) << 16), o);
+        uint32_t ob[kN];
+#pragma unroll
+        for (int h = 0; h < kN; ++h) ob[h] = __float_as_uint(o[h] * corr[h]);
+        tmem_st16(tO + ((uint32_t)(quad * 32) << 16), ob);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(pfull);
+      asm volatile("bar.sync 1, 128;" ::: "memory");   // red[] reused next tile
+    }
+
+    // ---------------------------------------------------------------- epilogue
+    // global row sums: reduce per-thread partial sums over the 128 threads
+#pragma unroll
+    for (int h = 0; h < kN; ++h) lsum[h] = warp_sum(lsum[h]);
+    if (lane == 0) {
+#pragma unroll
+      for (int h = 0; h < kN; ++h) red[w4 * kN + h] = lsum[h];
+    }
+    if (nt > 0) mbar_wait_ab(pvdone, (uint32_t)(nt - 1) & 1u, status, kErrTimeoutAccum, abort_flag);
+    tc_fence_after();
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    float o[kN];
+    if (nt > 0) tmem_ld16(tO + ((uint32_t)(quad * 32) << 16), o);
+    const int d = row;
+#pragma unroll
+    for (int h = 0; h < kN; ++h) {
+      if (h >= G) break;
+      const float L = red[h] + red[kN + h] + red[2 * kN + h] + red[3 * kN + h];
+      const float A = nt > 0 ? o[h] : 0.f;
+      const int hq = hk * G + h;
+      if (a.splits == 1) {
+        a.out[((size_t)b * a.Hq + hq) * kD + d] = __float2half_rn(L > 0.f ? A / L : 0.f);
+      } else {
+        float* p = a.ws + (((size_t)b * a.Hq + hq) * a.splits + split) * (kD + 2);
+        p[2 + d] = A;
+        if (d == 0) {
+          p[0] = nt > 0 ? mrun[h] * kLn2 : -INFINITY;
+          p[1] = L;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ host
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn tmap_encode_fn();
+
+static void make_kv_map(CUtensorMap* m, const void* cache, int num_blocks, int Hk, int bs) {
+  if ((reinterpret_cast<uintptr_t>(cache) & 15) != 0) throw std::runtime_error("KV cache must be 16-byte aligned");
+  cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)bs, (cuuint64_t)Hk, (cuuint64_t)num_blocks};
+  cuuint64_t strides[3] = {(cuuint64_t)kD * 2, (cuuint64_t)bs * kD * 2, (cuuint64_t)Hk * bs * kD * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)bs, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = tmap_encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(cache), dims, strides, box,
+                                es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("KV tensor map encode failed: " + std::to_string((int)r));
+}
+
+bool decode_attn_tc_supported(const DecodeAttnArgs& a) {
+  return a.D == kD && a.block_size == 16 && a.Hq / a.Hk <= kN && a.keys_per_split % kKeys == 0;
+}
+
+void decode_attn_tc_launch(const DecodeAttnArgs& a, int num_blocks, int* status, cudaStream_t s) {
+  if (!decode_attn_tc_supported(a)) throw std::runtime_error("tcgen05 decode attention: unsupported shape");
+  CUtensorMap tk, tv;
+  make_kv_map(&tk, a.k_cache, num_blocks, a.Hk, a.block_size);
+  make_kv_map(&tv, a.v_cache, num_blocks, a.Hk, a.block_size);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(attn_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::kAlloc);
+    attr = true;
+  }
+  dim3 grid(a.splits, a.Hk, a.B);
+  if (status == nullptr) status = status_word();
+  attn_decode_tc_kernel<<<grid, kThreads, Smem::kAlloc, s>>>(tk, tv, a, status);
+  if (a.splits > 1) decode_combine_launch(a, s);
+}
+
+}  // namespace hrm

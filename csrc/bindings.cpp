@@ -12,6 +12,8 @@
 #include "kernels.h"
 #include "comm.h"
 
+namespace py = pybind11;
+
 namespace {
 
 #define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
@@ -21,7 +23,7 @@ namespace {
 cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
 void check_ws(const hrm::GemmPlan& p, const at::Tensor& ws, const at::Tensor& counters) {
-  if (p.splits > 1) {
+  if (p.ws_floats > 0) {
     CHECK_CUDA(ws);
     CHECK_CUDA(counters);
     CHECK_DTYPE(ws, at::kFloat);
@@ -32,7 +34,8 @@ void check_ws(const hrm::GemmPlan& p, const at::Tensor& ws, const at::Tensor& co
 }
 
 hrm::GemmArgs base_args(const at::Tensor& x, const at::Tensor& w, const at::Tensor& scale,
-                        const c10::optional<at::Tensor>& bias, const at::Tensor& ws, const at::Tensor& counters) {
+                        const c10::optional<at::Tensor>& bias, const at::Tensor& ws, const at::Tensor& counters,
+                        const c10::optional<at::Tensor>& status = c10::nullopt) {
   CHECK_CUDA(x); CHECK_CUDA(w); CHECK_CUDA(scale);
   CHECK_DTYPE(x, at::kHalf); CHECK_DTYPE(w, at::kChar); CHECK_DTYPE(scale, at::kFloat);
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2, "x [M,K] and w [N,K] must be 2-D");
@@ -52,17 +55,21 @@ hrm::GemmArgs base_args(const at::Tensor& x, const at::Tensor& w, const at::Tens
   }
   a.ws = ws.defined() && ws.numel() ? ws.data_ptr<float>() : nullptr;
   a.counters = counters.defined() && counters.numel() ? counters.data_ptr<int>() : nullptr;
+  if (status.has_value() && status->defined()) {
+    CHECK_DTYPE((*status), at::kInt);
+    a.status = status->data_ptr<int>();
+  }
   return a;
 }
 
-std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K, int64_t force_splits) {
-  auto p = hrm::gemm_plan((int)M, (int)N, (int)K, (int)force_splits);
+std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K, int64_t force_ctas) {
+  auto p = hrm::gemm_plan((int)M, (int)N, (int)K, (int)force_ctas);
   return {p.bn, p.n_tiles, p.m_tiles, p.k_tiles, p.splits, (int64_t)p.ws_floats, p.counters};
 }
 
 // out = x @ (w * scale)^T (+ bias): out dtype f16 or f32 (preallocated [M, >=N] row-major).
 void w8a16_gemm(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<at::Tensor> bias, at::Tensor out,
-                at::Tensor ws, at::Tensor counters, int64_t force_splits) {
+                at::Tensor ws, at::Tensor counters, int64_t force_ctas) {
   c10::cuda::CUDAGuard g(x.device());
   auto a = base_args(x, w, scale, bias, ws, counters);
   if (a.M == 0) return;
@@ -74,14 +81,14 @@ void w8a16_gemm(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<at::
   else TORCH_CHECK(false, "out must be f16 or f32");
   a.out = out.data_ptr();
   a.ldo = (int)out.stride(0);
-  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_splits);
+  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_ctas);
   check_ws(p, ws, counters);
   hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), epi, a, p, cur_stream());
 }
 
 // resid += x @ (w * scale)^T  (fp32 residual stream)
 void w8a16_gemm_residual(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor resid, at::Tensor ws,
-                         at::Tensor counters, int64_t force_splits) {
+                         at::Tensor counters, int64_t force_ctas) {
   c10::cuda::CUDAGuard g(x.device());
   auto a = base_args(x, w, scale, c10::nullopt, ws, counters);
   if (a.M == 0) return;
@@ -90,7 +97,7 @@ void w8a16_gemm_residual(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tenso
               "bad resid shape");
   a.resid = resid.data_ptr<float>();
   a.ldr = (int)resid.stride(0);
-  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_splits);
+  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_ctas);
   check_ws(p, ws, counters);
   hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_RESID, a, p, cur_stream());
 }
@@ -98,7 +105,7 @@ void w8a16_gemm_residual(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tenso
 // out [M, N/2] f16 = silu(gate) * up, where w rows are interleaved per 128-row tile: 64 gate rows then the 64
 // matching up rows.
 void w8a16_gemm_swiglu(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor out, at::Tensor ws,
-                       at::Tensor counters, int64_t force_splits) {
+                       at::Tensor counters, int64_t force_ctas) {
   c10::cuda::CUDAGuard g(x.device());
   auto a = base_args(x, w, scale, c10::nullopt, ws, counters);
   if (a.M == 0) return;
@@ -106,7 +113,7 @@ void w8a16_gemm_swiglu(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor 
   TORCH_CHECK(out.dim() == 2 && out.size(0) == a.M && out.size(1) == a.N / 2 && out.stride(1) == 1, "bad out");
   a.out = out.data_ptr();
   a.ldo = (int)out.stride(0);
-  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_splits);
+  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_ctas);
   check_ws(p, ws, counters);
   hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_SWIGLU, a, p, cur_stream());
 }
@@ -115,7 +122,7 @@ void w8a16_gemm_swiglu(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor 
 void w8a16_gemm_qkv(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<at::Tensor> bias, int64_t q_rows,
                     int64_t kv_rows, int64_t head_dim, at::Tensor positions, at::Tensor slots, at::Tensor cos_t,
                     at::Tensor sin_t, at::Tensor q_out, at::Tensor k_cache, at::Tensor v_cache, at::Tensor ws,
-                    at::Tensor counters, int64_t force_splits) {
+                    at::Tensor counters, int64_t force_ctas) {
   c10::cuda::CUDAGuard g(x.device());
   auto a = base_args(x, w, scale, bias, ws, counters);
   if (a.M == 0) return;
@@ -142,7 +149,7 @@ void w8a16_gemm_qkv(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<
   a.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
   a.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr());
   a.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
-  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_splits);
+  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_ctas);
   check_ws(p, ws, counters);
   hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_QKV, a, p, cur_stream());
 }
@@ -177,7 +184,7 @@ void embed_q8(at::Tensor ids, at::Tensor q, at::Tensor scale, int64_t vocab_star
 
 void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_tables,
                       at::Tensor context_lens, at::Tensor out, at::Tensor ws, int64_t splits, int64_t keys_per_split,
-                      double scale) {
+                      double scale, c10::optional<at::Tensor> status, bool allow_tc) {
   c10::cuda::CUDAGuard g(q.device());
   CHECK_DTYPE(q, at::kBFloat16); CHECK_DTYPE(k_cache, at::kBFloat16); CHECK_DTYPE(v_cache, at::kBFloat16);
   CHECK_DTYPE(block_tables, at::kInt); CHECK_DTYPE(context_lens, at::kInt); CHECK_DTYPE(out, at::kHalf);
@@ -203,7 +210,13 @@ void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::
   a.context_lens = context_lens.data_ptr<int>();
   a.out = reinterpret_cast<__half*>(out.data_ptr());
   if (a.B == 0) return;
-  hrm::decode_attn_launch(a, cur_stream());
+  int* st = nullptr;
+  if (status.has_value() && status->defined()) { CHECK_DTYPE((*status), at::kInt); st = status->data_ptr<int>(); }
+  if (allow_tc && hrm::decode_attn_tc_supported(a)) {
+    hrm::decode_attn_tc_launch(a, (int)k_cache.size(0), st, cur_stream());
+  } else {
+    hrm::decode_attn_launch(a, cur_stream());
+  }
 }
 
 void prefill_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_tables,
@@ -276,7 +289,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("w8a16_gemm_qkv", &w8a16_gemm_qkv);
   m.def("rmsnorm", &rmsnorm);
   m.def("embed_q8", &embed_q8);
-  m.def("decode_attention", &decode_attention);
+  m.def("decode_attention", &decode_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("block_tables"), py::arg("context_lens"), py::arg("out"), py::arg("ws"), py::arg("splits"),
+        py::arg("keys_per_split"), py::arg("scale"), py::arg("status") = py::none(), py::arg("allow_tc") = true);
   m.def("decode_attn_ws_floats", [](int64_t B, int64_t Hq, int64_t D, int64_t s) {
     return (int64_t)hrm::decode_attn_ws_floats((int)B, (int)Hq, (int)D, (int)s);
   });
@@ -285,5 +300,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_prepare", &decode_prepare_bs);
   m.def("decode_advance", &decode_advance);
   m.def("sm_count", []() { return hrm::gemm_sm_count(); });
+  m.def("set_status_word", [](at::Tensor t) {
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kInt, "status word must be a CUDA int32 tensor");
+    hrm::set_status_word(t.device().index(), t.data_ptr<int>());
+  });
   hrm::register_comm_bindings(m);
 }

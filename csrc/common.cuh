@@ -68,6 +68,17 @@ HRM_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code)
   record_error(status, code);
   return false;
 }
+// Bounded wait with a CTA-wide abort flag in shared memory: once any thread of the CTA timed out, every other wait
+// returns false at once, so the CTA drains quickly (callers keep uniform control flow and skip issuing new work).
+HRM_DEVINL bool mbar_wait_ab(uint64_t* bar, uint32_t parity, int* status, int code, volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  record_error(status, code);
+  return false;
+}
 
 // ---------------------------------------------------------------- TMA (no multicast)
 HRM_DEVINL void tma_prefetch_desc(const CUtensorMap* map) {

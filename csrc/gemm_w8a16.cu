@@ -1,23 +1,28 @@
-// W8A16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM, TMA-fed), with fused epilogues.
+// W8A16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM, TMA-fed), persistent stream-K, fused epilogues.
 //
 //   Y[m, n] = sum_k X[m, k] * (Wq[n, k] * scale[n])        X: f16 [M, K], Wq: int8 [N, K] (DSI8 row layout)
 //
-// This replaces the reference's DP4A GEMVs (`gemv_w8_prequant` / `gemv_w8`,
-// scripts/deepseek_native_engine.sh:446-529) and the fp16 cuBLAS matmuls of the torch TP path
-// (tp/parallel_linear.py:31-35,59-66).
+// Replaces the reference's DP4A GEMVs (`gemv_w8_prequant` / `gemv_w8`, scripts/deepseek_native_engine.sh:446-529)
+// and the fp16 library matmuls of the torch TP path (tp/parallel_linear.py:31-35,59-66).
 //
-// Design ("swap-AB", weight rows on the MMA M side):
-//  * one CTA owns 128 weight rows (MMA M = 128) x BN tokens (MMA N = BN in {16..256}) x a K range (split-K);
-//  * warp 0 issues TMA loads: the raw int8 weight tile [128 x 64] (64-byte swizzle) and the f16 activation tile
-//    [BN x 64] (128-byte swizzle, the UMMA canonical K-major layout);
-//  * 8 dequant warps convert int8 -> f16 exactly (prmt + f16x2 subtract) straight into the 128-byte-swizzled
-//    canonical layout of the A operand; the per-row scale is applied once in the epilogue;
-//  * one thread of warp 1 issues tcgen05.mma (kind::f16, fp32 accumulator in TMEM) and tcgen05.commit frees
-//    each stage;
-//  * the same 8 warps run the epilogue out of TMEM (tcgen05.ld): plain f16/f32 stores, residual add, SwiGLU over
-//    gate/up rows interleaved per tile, or QKV bias + rotate-half RoPE + paged-KV append.
-//  * split-K partials go to a caller-provided fp32 workspace; the last CTA of a tile (atomic ticket) sums the
-//    partials in split order, so results are bitwise deterministic whatever the CTA scheduling.
+// Design ("swap-AB": weight rows on the MMA M side, tokens on N):
+//  * persistent grid, one CTA per SM.  The work is the list of (tile, k-tile) units, tile = 128 weight rows x BN
+//    tokens (BN in {16..256}); CTA c takes the contiguous unit range [c*U/G, (c+1)*U/G) ("stream-K"), so every SM
+//    streams the same number of weight bytes whatever the tile count.  A tile cut between CTAs is a set of k-segments
+//    whose fp32 partials go to a caller-provided workspace; the last segment to finish (atomic ticket) sums them in
+//    k order, so results are bitwise deterministic whatever the scheduling.
+//  * warp 0: TMA producer.  Raw int8 weight tiles [128 x 64] (64-byte swizzle) and the f16 activation tile [BN x 64]
+//    (128-byte swizzle, canonical K-major UMMA layout) stream through a deep ring (R slots), across segment and
+//    tile boundaries, so HBM sees a continuous stream.
+//  * warps 2-9: dequant int8 -> f16 exactly (prmt + f16x2 subtract) into a shorter ring of 128-byte-swizzled A tiles;
+//    the per-row scale is applied once in the epilogue.
+//  * warp 1: one thread issues tcgen05.mma (kind::f16, fp32 accumulate) into one of two TMEM accumulators and
+//    tcgen05.commit releases ring slots / publishes a finished accumulator.
+//  * warps 10-13: epilogue (thread = TMEM lane = weight row), overlapped with the next segment's mainloop: plain
+//    f16/f32 stores, residual add, SwiGLU over gate/up rows interleaved per tile, or QKV bias + rotate-half RoPE +
+//    paged-KV append (cross-row pairs exchanged through a 16-column smem chunk).
+//  * every wait is bounded; a timeout sets the CTA abort flag, records an error code, drains in-flight TMA/MMA and
+//    exits without hanging.
 #include "common.cuh"
 #include "gemm_w8a16.h"
 
@@ -32,66 +37,163 @@ namespace hrm {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kDqWarps = 8;
+constexpr int kEpiWarps = 4;
 constexpr int kFirstDqWarp = 2;
-constexpr int kThreads = (kFirstDqWarp + kDqWarps) * 32;
-constexpr int kEpiThreads = kDqWarps * 32;
-constexpr int kWrawBytes = kBM * kBK;          // int8 tile
-constexpr int kW16Bytes = kBM * kBK * 2;       // f16 tile
+constexpr int kFirstEpiWarp = kFirstDqWarp + kDqWarps;
+constexpr int kThreads = (kFirstEpiWarp + kEpiWarps) * 32;   // 448
+constexpr int kDqThreads = kDqWarps * 32;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kWrawBytes = kBM * kBK;          // int8 tile, 8 KB
+constexpr int kW16Bytes = kBM * kBK * 2;       // f16 tile, 16 KB
+constexpr int kChunk = 16;                     // epilogue columns per TMEM load
 
-template <int BN> struct GemmCfg;
-template <> struct GemmCfg<16>  { static constexpr int kStages = 4; };
-template <> struct GemmCfg<32>  { static constexpr int kStages = 4; };
-template <> struct GemmCfg<64>  { static constexpr int kStages = 4; };
-template <> struct GemmCfg<128> { static constexpr int kStages = 4; };
-template <> struct GemmCfg<256> { static constexpr int kStages = 3; };
+template <int BN> struct GemmCfg;   // raw ring depth R, f16 ring depth F
+template <> struct GemmCfg<16>  { static constexpr int R = 12, F = 4; };
+template <> struct GemmCfg<32>  { static constexpr int R = 10, F = 4; };
+template <> struct GemmCfg<64>  { static constexpr int R = 8, F = 4; };
+template <> struct GemmCfg<128> { static constexpr int R = 5, F = 3; };
+template <> struct GemmCfg<256> { static constexpr int R = 3, F = 3; };
 
 template <int BN>
 struct GemmSmem {
-  static constexpr int kStages = GemmCfg<BN>::kStages;
+  static constexpr int R = GemmCfg<BN>::R, F = GemmCfg<BN>::F;
   static constexpr int kXBytes = BN * kBK * 2;
   static constexpr int kW16Off = 0;
-  static constexpr int kXOff = kW16Off + kStages * kW16Bytes;
-  static constexpr int kWrawOff = kXOff + kStages * kXBytes;
-  static constexpr int kBarOff = kWrawOff + kStages * kWrawBytes;
-  static constexpr int kBytes = kBarOff + (3 * kStages + 1) * 8 + 16;
-  static constexpr int kAlloc = kBytes + 1024;   // slack for manual 1024-byte alignment
-  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  static_assert(kStages * (kW16Bytes + kXBytes + kWrawBytes) >= BN * kBM * 4, "staging area too small");
+  static constexpr int kXOff = kW16Off + F * kW16Bytes;
+  static constexpr int kWrawOff = kXOff + R * kXBytes;
+  static constexpr int kStageOff = kWrawOff + R * kWrawBytes;          // [16 cols][128 rows] fp32 = 8 KB
+  static constexpr int kBarOff = kStageOff + kChunk * kBM * 4;
+  static constexpr int kNumBars = 2 * R + 2 * F + 5;
+  static constexpr int kBytes = kBarOff + kNumBars * 8 + 32;
+  static constexpr int kAlloc = kBytes + 1024;
+  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  static_assert(kAlloc <= 227 * 1024, "shared memory budget exceeded");
 };
+
+// ------------------------------------------------------------------ stream-K partition helpers (device + host)
+HRM_DEVINL int64_t unit_start(int64_t c, int64_t U, int64_t G) { return (c * U) / G; }
+HRM_DEVINL int owner_of(int64_t x, int64_t U, int64_t G) { return (int)(((x + 1) * G - 1) / U); }
+
+template <int BN, int EPI>
+HRM_DEVINL void epilogue_store(const GemmArgs& a, int n_tile, int m_tile, int row, int c0, const float (&v)[kChunk],
+                               float* stage, int et) {
+  const int n = n_tile * kBM + row;
+  const float sc = (n < a.N) ? a.scale[n] : 0.f;
+  const float bi = (a.bias != nullptr && n < a.N) ? a.bias[n] : 0.f;
+  if constexpr (EPI == EPI_SWIGLU || EPI == EPI_QKV) {
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) stage[j * kBM + row] = v[j] * sc + bi;
+    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+    if constexpr (EPI == EPI_SWIGLU) {
+      // rows [0,64) are gate rows, [64,128) the matching up rows; output column n_tile*64 + i
+      for (int idx = et; idx < kChunk * 64; idx += kEpiThreads) {
+        const int j = idx >> 6, i = idx & 63;
+        const int m = m_tile * BN + c0 + j;
+        const int oc = n_tile * 64 + i;
+        if (m < a.M && oc * 2 < a.N) {
+          const float g = stage[j * kBM + i];
+          const float u = stage[j * kBM + 64 + i];
+          reinterpret_cast<__half*>(a.out)[(size_t)m * a.ldo + oc] = __float2half_rn(silu(g) * u);
+        }
+      }
+    } else {
+      const int D = a.head_dim, halfD = D >> 1;
+      for (int idx = et; idx < kChunk * kBM; idx += kEpiThreads) {
+        const int j = idx >> 7, rr = idx & (kBM - 1);
+        const int m = m_tile * BN + c0 + j;
+        const int gn = n_tile * kBM + rr;
+        if (m >= a.M || gn >= a.N) continue;
+        const int d = gn % D;
+        const float* srow = stage + j * kBM;
+        float y;
+        if (gn < a.q_rows + a.kv_rows) {
+          const int pos = a.positions[m];
+          const int dd = d < halfD ? d : d - halfD;
+          const float c = a.cos_t[(size_t)pos * halfD + dd];
+          const float s = a.sin_t[(size_t)pos * halfD + dd];
+          y = d < halfD ? srow[rr] * c - srow[rr + halfD] * s : srow[rr - halfD] * s + srow[rr] * c;
+        } else {
+          y = srow[rr];
+        }
+        if (gn < a.q_rows) {
+          a.q_out[(size_t)m * a.q_rows + gn] = __float2bfloat16_rn(y);
+        } else {
+          const int slot = a.slots[m];
+          if (slot < 0) continue;
+          const bool is_k = gn < a.q_rows + a.kv_rows;
+          const int kvh = (gn - a.q_rows - (is_k ? 0 : a.kv_rows)) / D;
+          const int blk = slot / a.block_size, off = slot - blk * a.block_size;
+          __nv_bfloat16* cache = is_k ? a.k_cache : a.v_cache;
+          cache[(((size_t)blk * a.kv_heads + kvh) * a.block_size + off) * D + d] = __float2bfloat16_rn(y);
+        }
+      }
+    }
+    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+  } else {
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      const int m = m_tile * BN + c0 + j;
+      if (m < a.M && n < a.N) {
+        const float y = v[j] * sc + bi;
+        if constexpr (EPI == EPI_F16) {
+          reinterpret_cast<__half*>(a.out)[(size_t)m * a.ldo + n] = __float2half_rn(y);
+        } else if constexpr (EPI == EPI_F32) {
+          reinterpret_cast<float*>(a.out)[(size_t)m * a.ldo + n] = y;
+        } else {
+          float* rp = &a.resid[(size_t)m * a.ldr + n];
+          *rp = *rp + y;
+        }
+      }
+    }
+  }
+}
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
 w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                   const GemmArgs a) {
   using S = GemmSmem<BN>;
-  constexpr int ST = S::kStages;
+  constexpr int R = S::R, F = S::F;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* w16 = base + S::kW16Off;
   uint8_t* xs = base + S::kXOff;
   uint8_t* wraw = base + S::kWrawOff;
-  uint64_t* full = reinterpret_cast<uint64_t*>(base + S::kBarOff);
-  uint64_t* dqf = full + ST;
-  uint64_t* empty = dqf + ST;
-  uint64_t* accf = empty + ST;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
-  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  float* stage = reinterpret_cast<float*>(base + S::kStageOff);
+  uint64_t* rfull = reinterpret_cast<uint64_t*>(base + S::kBarOff);
+  uint64_t* rempty = rfull + R;
+  uint64_t* ffull = rempty + R;
+  uint64_t* fempty = ffull + F;
+  uint64_t* afull = fempty + F;      // [2] accumulator ready (MMA -> epilogue)
+  uint64_t* aempty = afull + 2;      // [2] accumulator drained (epilogue -> MMA)
+  uint64_t* mdone = aempty + 2;      // all MMAs of this CTA complete (drain before TMEM is freed)
+  int* misc = reinterpret_cast<int*>(mdone + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc);
+  int* last_flag = misc + 1;
+  volatile int* abort_flag = misc + 2;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x, m_tile = blockIdx.y, split = blockIdx.z;
-  const int kt0 = split * a.tiles_per_split;
-  const int kt1 = min(a.k_tiles, kt0 + a.tiles_per_split);
-  const int nkt = kt1 - kt0;
+  const int64_t G = gridDim.x;
+  const int64_t U = (int64_t)a.tiles * a.k_tiles;
+  const int64_t u0 = unit_start(blockIdx.x, U, G), u1 = unit_start(blockIdx.x + 1, U, G);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < ST; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&dqf[s], kEpiThreads);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < R; ++s) {
+      mbar_init(&rfull[s], 1);
+      mbar_init(&rempty[s], 1);
     }
-    mbar_init(accf, 1);
+    for (int s = 0; s < F; ++s) {
+      mbar_init(&ffull[s], kDqThreads);
+      mbar_init(&fempty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&afull[s], 1);
+      mbar_init(&aempty[s], kEpiThreads);
+    }
+    mbar_init(mdone, 1);
     *last_flag = 0;
+    *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -108,52 +210,72 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
     if (lane == 0) {
       tma_prefetch_desc(&tmW);
       tma_prefetch_desc(&tmX);
-      for (int i = 0; i < nkt; ++i) {
-        const int s = i % ST;
-        const uint32_t ph = (uint32_t)(i / ST) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, a.status, kErrTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&full[s], kWrawBytes + S::kXBytes);
-        const int kx = (kt0 + i) * kBK;
-        tma_load_2d(wraw + s * kWrawBytes, &tmW, &full[s], kx, n_tile * kBM);
-        tma_load_2d(xs + s * S::kXBytes, &tmX, &full[s], kx, m_tile * BN);
+      int64_t i = 0;
+      for (int64_t u = u0; u < u1; ++u, ++i) {
+        const int tile = (int)(u / a.k_tiles), kt = (int)(u % a.k_tiles);
+        const int n_tile = tile % a.n_tiles, m_tile = tile / a.n_tiles;
+        const int s = (int)(i % R);
+        const uint32_t ph = (uint32_t)(i / R) & 1u;
+        if (!mbar_wait_ab(&rempty[s], ph ^ 1u, a.status, kErrTimeoutEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(&rfull[s], kWrawBytes + S::kXBytes);
+        tma_load_2d(wraw + s * kWrawBytes, &tmW, &rfull[s], kt * kBK, n_tile * kBM);
+        tma_load_2d(xs + s * S::kXBytes, &tmX, &rfull[s], kt * kBK, m_tile * BN);
       }
+      // drain: the last R issued loads must have landed before exit
+      for (int64_t j = (i > R ? i - R : 0); j < i; ++j)
+        mbar_wait(&rfull[j % R], (uint32_t)(j / R) & 1u, a.status, kErrTimeoutFull);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
-      for (int i = 0; i < nkt; ++i) {
-        const int s = i % ST;
-        const uint32_t ph = (uint32_t)(i / ST) & 1u;
-        if (!mbar_wait(&full[s], ph, a.status, kErrTimeoutFull)) break;
-        if (!mbar_wait(&dqf[s], ph, a.status, kErrTimeoutDequant)) break;
+      int64_t i = 0;
+      int seg = 0;
+      bool ok = true;
+      for (int64_t u = u0; ok && u < u1; ++seg) {
+        const int tile = (int)(u / a.k_tiles);
+        const int64_t tile_end = (int64_t)(tile + 1) * a.k_tiles;
+        const int64_t ue = tile_end < u1 ? tile_end : u1;
+        const int acc = seg & 1;
+        const uint32_t acc_addr = tmem + (uint32_t)(acc * BN);
+        ok = mbar_wait_ab(&aempty[acc], ((uint32_t)(seg >> 1) & 1u) ^ 1u, a.status, kErrTimeoutAccum, abort_flag);
         tc_fence_after();
-        const uint32_t a0 = smem_u32(w16 + s * kW16Bytes);
-        const uint32_t b0 = smem_u32(xs + s * S::kXBytes);
+        for (int64_t k = u; ok && k < ue; ++k, ++i) {
+          const int r = (int)(i % R), f = (int)(i % F);
+          ok = mbar_wait_ab(&rfull[r], (uint32_t)(i / R) & 1u, a.status, kErrTimeoutFull, abort_flag) &&
+               mbar_wait_ab(&ffull[f], (uint32_t)(i / F) & 1u, a.status, kErrTimeoutDequant, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(w16 + f * kW16Bytes);
+          const uint32_t b0 = smem_u32(xs + r * S::kXBytes);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-          umma_f16_ss(tmem, sdesc_sw128(a0 + kk * 32), sdesc_sw128(b0 + kk * 32), idesc,
-                      (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16_ss(acc_addr, sdesc_sw128(a0 + kk * 32), sdesc_sw128(b0 + kk * 32), idesc,
+                        (k > u || kk > 0) ? 1u : 0u);
+          umma_commit(&rempty[r]);
+          umma_commit(&fempty[f]);
         }
-        umma_commit(&empty[s]);
+        umma_commit(&afull[acc]);
+        u = ue;
       }
-      umma_commit(accf);
+      umma_commit(mdone);
+      mbar_wait(mdone, 0, a.status, kErrTimeoutAccum);
     }
-  } else {
+  } else if (warp < kFirstEpiWarp) {
     // ------------------------------------------------------------------ dequant
-    const int t = threadIdx.x - kFirstDqWarp * 32;  // 0..255
+    const int t = threadIdx.x - kFirstDqWarp * 32;   // 0..255
     const int r = t & (kBM - 1);
-    const int h = t >> 7;                           // which 32-element half of the 64-wide K stage
-    for (int i = 0; i < nkt; ++i) {
-      const int s = i % ST;
-      const uint32_t ph = (uint32_t)(i / ST) & 1u;
-      if (!mbar_wait(&full[s], ph, a.status, kErrTimeoutFull)) break;
-      const uint8_t* src = wraw + s * kWrawBytes + r * 64;
-      const int sw64 = (r >> 1) & 3;
+    const int h = t >> 7;
+    const int sw64 = (r >> 1) & 3, sw128 = r & 7;
+    int64_t i = 0;
+    for (int64_t u = u0; u < u1; ++u, ++i) {
+      const int rs = (int)(i % R), fs = (int)(i % F);
+      if (!mbar_wait_ab(&rfull[rs], (uint32_t)(i / R) & 1u, a.status, kErrTimeoutFull, abort_flag)) break;
+      if (!mbar_wait_ab(&fempty[fs], ((uint32_t)(i / F) & 1u) ^ 1u, a.status, kErrTimeoutEmpty, abort_flag)) break;
+      const uint8_t* src = wraw + rs * kWrawBytes + r * 64;
       const uint4 v0 = *reinterpret_cast<const uint4*>(src + (((2 * h) ^ sw64) << 4));
       const uint4 v1 = *reinterpret_cast<const uint4*>(src + (((2 * h + 1) ^ sw64) << 4));
-      uint8_t* dst = w16 + s * kW16Bytes + r * 128;
-      const int sw128 = r & 7;
+      uint8_t* dst = w16 + fs * kW16Bytes + r * 128;
       uint4 o;
       i8x4_to_f16x4(v0.x, o.x, o.y); i8x4_to_f16x4(v0.y, o.z, o.w);
       *reinterpret_cast<uint4*>(dst + (((4 * h + 0) ^ sw128) << 4)) = o;
@@ -164,131 +286,78 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       i8x4_to_f16x4(v1.z, o.x, o.y); i8x4_to_f16x4(v1.w, o.z, o.w);
       *reinterpret_cast<uint4*>(dst + (((4 * h + 3) ^ sw128) << 4)) = o;
       fence_proxy_async_smem();
-      mbar_arrive(&dqf[s]);
+      mbar_arrive(&ffull[fs]);
     }
-
-    // ------------------------------------------------------------------ epilogue
-    mbar_wait(accf, 0, a.status, kErrTimeoutAccum);
-    tc_fence_after();
-    const int quad = warp & 3;                       // TMEM lanes this warp may access
-    const int row = quad * 32 + lane;                // tile row == TMEM lane
-    const int colgrp = (warp - kFirstDqWarp) >> 2;   // 0 or 1
-    constexpr int kColsPerWarp = BN / 2 < 16 ? 16 : BN / 2;
-    const int c_begin = colgrp * kColsPerWarp;
-    const int c_end = min(BN, c_begin + kColsPerWarp);
-    const int n = n_tile * kBM + row;
-    const int tile_id = m_tile * gridDim.x + n_tile;
-    const bool split_k = a.splits > 1;
-
-    if (split_k) {
-      float* my = a.ws + ((size_t)tile_id * a.splits + split) * (size_t)(BN * kBM);
-      for (int c0 = c_begin; c0 < c_end; c0 += 16) {
-        float v[16];
-        tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) __stcg(&my[(c0 + j) * kBM + row], v[j]);
-      }
-      __threadfence();
-      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
-      if (t == 0) {
-        const int prev = atomicAdd(&a.counters[tile_id], 1);
-        const int is_last = (prev == a.splits - 1);
-        if (is_last) a.counters[tile_id] = 0;      // re-arm for the next launch
-        *last_flag = is_last;
-      }
-      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
-      if (!*last_flag) goto done;
-      __threadfence();
-    }
-
-    {
-      const float sc = (n < a.N) ? a.scale[n] : 0.f;
-      const float bi = (a.bias != nullptr && n < a.N) ? a.bias[n] : 0.f;
-      float* stage = reinterpret_cast<float*>(base);   // [BN][128] fp32, reuses the pipeline buffers
-      for (int c0 = c_begin; c0 < c_end; c0 += 16) {
-        float v[16];
-        if (split_k) {
-          const float* wsb = a.ws + (size_t)tile_id * a.splits * (size_t)(BN * kBM);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = __ldcg(&wsb[(c0 + j) * kBM + row]);
-          for (int sp = 1; sp < a.splits; ++sp) {
-            const float* p = wsb + (size_t)sp * (BN * kBM);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] += __ldcg(&p[(c0 + j) * kBM + row]);
+  } else {
+    // ------------------------------------------------------------------ epilogue (overlapped)
+    const int et = threadIdx.x - kFirstEpiWarp * 32;   // 0..127
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    int seg = 0;
+    for (int64_t u = u0; u < u1; ++seg) {
+      const int tile = (int)(u / a.k_tiles);
+      const int ka = (int)(u % a.k_tiles);
+      const int64_t tile_end = (int64_t)(tile + 1) * a.k_tiles;
+      const int64_t ue = tile_end < u1 ? tile_end : u1;
+      const bool whole = ka == 0 && ue == tile_end;
+      const int n_tile = tile % a.n_tiles, m_tile = tile / a.n_tiles;
+      const int acc = seg & 1;
+      const uint32_t acc_addr = tmem + (uint32_t)(acc * BN) + ((uint32_t)(quad * 32) << 16);
+      mbar_wait_ab(&afull[acc], (uint32_t)(seg >> 1) & 1u, a.status, kErrTimeoutAccum, abort_flag);
+      tc_fence_after();
+      if (whole) {
+        for (int c0 = 0; c0 < BN; c0 += kChunk) {
+          float v[kChunk];
+          tmem_ld16(acc_addr + (uint32_t)c0, v);
+          if (c0 + kChunk >= BN) {   // accumulator fully read: hand it back to the MMA warp early
+            tc_fence_before();
+            mbar_arrive(&aempty[acc]);
           }
-        } else {
-          tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
+          epilogue_store<BN, EPI>(a, n_tile, m_tile, row, c0, v, stage, et);
         }
+      } else {
+        // partial segment: write fp32 partial, take a ticket; the last segment of the tile reduces in k order
+        const int first = owner_of((int64_t)tile * a.k_tiles, U, G);
+        const int nseg = owner_of(tile_end - 1, U, G) - first + 1;
+        const int segidx = (int)blockIdx.x - first;
+        float* ws_tile = a.ws + (size_t)tile * a.max_seg * (BN * kBM);
+        float* mine = ws_tile + (size_t)segidx * (BN * kBM);
+        for (int c0 = 0; c0 < BN; c0 += kChunk) {
+          float v[kChunk];
+          tmem_ld16(acc_addr + (uint32_t)c0, v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m_tile * BN + c0 + j;
-          const float y = v[j] * sc + bi;
-          if constexpr (EPI == EPI_SWIGLU || EPI == EPI_QKV) {
-            stage[(c0 + j) * kBM + row] = y;
-          } else {
-            if (m < a.M && n < a.N) {
-              if constexpr (EPI == EPI_F16) {
-                reinterpret_cast<__half*>(a.out)[(size_t)m * a.ldo + n] = __float2half_rn(y);
-              } else if constexpr (EPI == EPI_F32) {
-                reinterpret_cast<float*>(a.out)[(size_t)m * a.ldo + n] = y;
-              } else if constexpr (EPI == EPI_RESID) {
-                float* rp = &a.resid[(size_t)m * a.ldr + n];
-                *rp = *rp + y;
-              }
-            }
-          }
+          for (int j = 0; j < kChunk; ++j) __stcg(&mine[(c0 + j) * kBM + row], v[j]);
         }
-      }
-      if constexpr (EPI == EPI_SWIGLU || EPI == EPI_QKV) {
+        tc_fence_before();
+        mbar_arrive(&aempty[acc]);
+        __threadfence();
         asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
-        if constexpr (EPI == EPI_SWIGLU) {
-          // Tile rows [0,64) are gate rows, [64,128) the matching up rows; output column n_tile*64 + i.
-          for (int idx = t; idx < BN * 64; idx += kEpiThreads) {
-            const int j = idx >> 6, i = idx & 63;
-            const int m = m_tile * BN + j;
-            const int oc = n_tile * 64 + i;
-            if (m < a.M && oc * 2 < a.N) {
-              const float g = stage[j * kBM + i];
-              const float u = stage[j * kBM + 64 + i];
-              reinterpret_cast<__half*>(a.out)[(size_t)m * a.ldo + oc] = __float2half_rn(silu(g) * u);
+        if (et == 0) {
+          const int prev = atomicAdd(&a.counters[tile], 1);
+          const int is_last = prev == nseg - 1;
+          if (is_last) a.counters[tile] = 0;   // re-arm for the next launch
+          *last_flag = is_last;
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+        const bool is_last = *last_flag != 0;
+        asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+        if (is_last) {
+          __threadfence();
+          for (int c0 = 0; c0 < BN; c0 += kChunk) {
+            float v[kChunk];
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) v[j] = __ldcg(&ws_tile[(c0 + j) * kBM + row]);
+            for (int sg = 1; sg < nseg; ++sg) {
+              const float* p = ws_tile + (size_t)sg * (BN * kBM);
+#pragma unroll
+              for (int j = 0; j < kChunk; ++j) v[j] += __ldcg(&p[(c0 + j) * kBM + row]);
             }
-          }
-        } else {
-          const int D = a.head_dim, halfD = D >> 1;
-          for (int idx = t; idx < BN * kBM; idx += kEpiThreads) {
-            const int j = idx >> 7, rr = idx & (kBM - 1);
-            const int m = m_tile * BN + j;
-            const int gn = n_tile * kBM + rr;
-            if (m >= a.M || gn >= a.N) continue;
-            const int d = gn % D;
-            const float* srow = stage + j * kBM;
-            float y;
-            if (gn < a.q_rows + a.kv_rows) {
-              const int pos = a.positions[m];
-              const int dd = d < halfD ? d : d - halfD;
-              const float c = a.cos_t[(size_t)pos * halfD + dd];
-              const float s = a.sin_t[(size_t)pos * halfD + dd];
-              if (d < halfD) y = srow[rr] * c - srow[rr + halfD] * s;
-              else y = srow[rr - halfD] * s + srow[rr] * c;
-            } else {
-              y = srow[rr];
-            }
-            if (gn < a.q_rows) {
-              a.q_out[(size_t)m * a.q_rows + gn] = __float2bfloat16_rn(y);
-            } else {
-              const int slot = a.slots[m];
-              if (slot < 0) continue;
-              const bool is_k = gn < a.q_rows + a.kv_rows;
-              const int kvh = (gn - a.q_rows - (is_k ? 0 : a.kv_rows)) / D;
-              const int blk = slot / a.block_size, off = slot - blk * a.block_size;
-              __nv_bfloat16* cache = is_k ? a.k_cache : a.v_cache;
-              cache[(((size_t)blk * a.kv_heads + kvh) * a.block_size + off) * D + d] = __float2bfloat16_rn(y);
-            }
+            epilogue_store<BN, EPI>(a, n_tile, m_tile, row, c0, v, stage, et);
           }
         }
       }
+      u = ue;
     }
-  done:;
   }
 
   tc_fence_before();
@@ -304,7 +373,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-static EncodeTiledFn encode_fn() {
+EncodeTiledFn tmap_encode_fn() {
   static EncodeTiledFn fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -327,10 +396,21 @@ void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int
   cuuint64_t strides[1] = {row_stride_elems * (uint64_t)elem_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode_fn()(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = tmap_encode_fn()(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+}
+
+// Per-device bounded-wait status word (device int32), registered once by the Python layer.
+static int* g_status[64] = {nullptr};
+void set_status_word(int device, int* p) {
+  if (device >= 0 && device < 64) g_status[device] = p;
+}
+int* status_word() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return (d >= 0 && d < 64) ? g_status[d] : nullptr;
 }
 
 int gemm_pick_bn(int M) {
@@ -352,27 +432,33 @@ int gemm_sm_count() {
   return sms;
 }
 
-GemmPlan gemm_plan(int M, int N, int K, int force_splits) {
+static int owner_host(int64_t x, int64_t U, int64_t G) { return (int)(((x + 1) * G - 1) / U); }
+
+GemmPlan gemm_plan(int M, int N, int K, int force_ctas) {
   GemmPlan p{};
   p.bn = gemm_pick_bn(M);
   p.n_tiles = (N + kBM - 1) / kBM;
   p.m_tiles = (M + p.bn - 1) / p.bn;
   p.k_tiles = K / kBK;
-  const int tiles = p.n_tiles * p.m_tiles;
-  int splits = 1;
-  if (force_splits > 0) {
-    splits = force_splits;
-  } else {
-    // Up to two 1-CTA-per-SM residents fit per SM for BN <= 64 (<= ~110 KB smem); fill those slots, keep at
-    // least 4 K stages per split.
-    const int slots = gemm_sm_count() * (p.bn <= 64 ? 2 : 1);
-    if (tiles < slots) splits = std::max(1, std::min(slots / tiles, p.k_tiles / 4));
+  p.tiles = p.n_tiles * p.m_tiles;
+  const int64_t U = (int64_t)p.tiles * p.k_tiles;
+  int64_t G = force_ctas > 0 ? force_ctas : gemm_sm_count();
+  if (G > U) G = U;
+  if (G < 1) G = 1;
+  p.ctas = (int)G;
+  // largest number of k-segments any tile is cut into
+  int max_seg = 1;
+  bool any_split = false;
+  for (int t = 0; t < p.tiles; ++t) {
+    const int64_t f = (int64_t)t * p.k_tiles, l = f + p.k_tiles - 1;
+    const int n = owner_host(l, U, G) - owner_host(f, U, G) + 1;
+    max_seg = std::max(max_seg, n);
+    any_split |= n > 1;
   }
-  splits = std::max(1, std::min(splits, p.k_tiles));
-  p.tiles_per_split = (p.k_tiles + splits - 1) / splits;
-  p.splits = (p.k_tiles + p.tiles_per_split - 1) / p.tiles_per_split;
-  p.ws_floats = p.splits > 1 ? (size_t)tiles * p.splits * p.bn * kBM : 0;
-  p.counters = p.splits > 1 ? tiles : 0;
+  p.max_seg = max_seg;
+  p.splits = max_seg;
+  p.ws_floats = any_split ? (size_t)p.tiles * max_seg * p.bn * kBM : 0;
+  p.counters = any_split ? p.tiles : 0;
   return p;
 }
 
@@ -385,8 +471,7 @@ static void launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, const GemmAr
     cudaFuncSetAttribute(w8a16_gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
     attr_set = true;
   }
-  dim3 grid(p.n_tiles, p.m_tiles, p.splits);
-  w8a16_gemm_kernel<BN, EPI><<<grid, kThreads, S::kAlloc, stream>>>(tw, tx, a);
+  w8a16_gemm_kernel<BN, EPI><<<p.ctas, kThreads, S::kAlloc, stream>>>(tw, tx, a);
 }
 
 template <int EPI>
@@ -406,12 +491,16 @@ void gemm_w8a16_launch(const void* x, int ldx, const int8_t* w, int epi, GemmArg
   if (a.K % kBK != 0) throw std::runtime_error("w8a16 gemm: K must be a multiple of 64");
   if (epi == EPI_QKV && (kBM % a.head_dim != 0)) throw std::runtime_error("w8a16 gemm: head_dim must divide 128");
   if (epi == EPI_SWIGLU && a.N % kBM != 0) throw std::runtime_error("w8a16 gemm: swiglu N must be a multiple of 128");
+  if (p.ws_floats && (a.ws == nullptr || a.counters == nullptr))
+    throw std::runtime_error("w8a16 gemm: this shape needs the split-K workspace");
   CUtensorMap tw, tx;
   make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.N, a.K, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_64B);
   make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.K, a.M, ldx, kBK, p.bn, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (a.status == nullptr) a.status = status_word();
   a.k_tiles = p.k_tiles;
-  a.tiles_per_split = p.tiles_per_split;
-  a.splits = p.splits;
+  a.n_tiles = p.n_tiles;
+  a.tiles = p.tiles;
+  a.max_seg = p.max_seg;
   switch (epi) {
     case EPI_F16: launch_epi<EPI_F16>(tw, tx, a, p, stream); break;
     case EPI_F32: launch_epi<EPI_F32>(tw, tx, a, p, stream); break;

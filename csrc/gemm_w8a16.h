@@ -18,15 +18,15 @@ enum GemmEpilogue : int {
 
 struct GemmArgs {
   int M, N, K;
-  int k_tiles, tiles_per_split, splits;     // filled by the launcher from the plan
+  int k_tiles, n_tiles, tiles, max_seg;     // filled by the launcher from the plan
   const float* scale;                       // [N]
   const float* bias;                        // [N] or nullptr
   void* out;                                // EPI_F16 / EPI_F32 / EPI_SWIGLU
   int ldo;
   float* resid;                             // EPI_RESID
   int ldr;
-  float* ws;                                // split-K workspace: plan.ws_floats floats
-  int* counters;                            // split-K tickets: plan.counters ints, zero before first use
+  float* ws;                                // stream-K partials: plan.ws_floats floats
+  int* counters;                            // stream-K tickets: plan.counters ints, zero before first use
   // EPI_QKV
   int q_rows, kv_rows, head_dim, kv_heads, block_size;
   const int* positions;                     // [M] absolute positions
@@ -39,18 +39,22 @@ struct GemmArgs {
   int* status;                              // bounded-wait error word (may be nullptr)
 };
 
+// Persistent stream-K plan: `ctas` CTAs share tiles*k_tiles (tile, k) units evenly; a tile is cut into at most
+// `max_seg` k-segments (== `splits`), whose partials need `ws_floats` floats of workspace and `counters` tickets.
 struct GemmPlan {
-  int bn, n_tiles, m_tiles, k_tiles, tiles_per_split, splits;
+  int bn, n_tiles, m_tiles, k_tiles, tiles, ctas, max_seg, splits;
   size_t ws_floats;
   int counters;
 };
 
-GemmPlan gemm_plan(int M, int N, int K, int force_splits = 0);
+GemmPlan gemm_plan(int M, int N, int K, int force_ctas = 0);
 void gemm_w8a16_launch(const void* x, int ldx, const int8_t* w, int epi, GemmArgs a, const GemmPlan& p,
                        cudaStream_t stream);
 void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
                   uint64_t outer, uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
                   CUtensorMapSwizzle swz);
 int gemm_sm_count();
+void set_status_word(int device, int* p);
+int* status_word();
 
 }  // namespace hrm

@@ -25,6 +25,10 @@ struct DecodeAttnArgs {
   float scale;
 };
 void decode_attn_launch(const DecodeAttnArgs& a, cudaStream_t s);
+void decode_combine_launch(const DecodeAttnArgs& a, cudaStream_t s);
+// tcgen05 variant (head_dim 128, block size 16, group <= 16, keys_per_split a multiple of 128)
+bool decode_attn_tc_supported(const DecodeAttnArgs& a);
+void decode_attn_tc_launch(const DecodeAttnArgs& a, int num_blocks, int* status, cudaStream_t s);
 size_t decode_attn_ws_floats(int B, int Hq, int D, int splits);
 
 // Paged prefill attention over varlen query chunks (causal with absolute positions).

@@ -65,6 +65,7 @@ class Workspace:
         self.device = device
         self.ws = torch.empty(floats, dtype=torch.float32, device=device)
         self.counters = torch.zeros(counters, dtype=torch.int32, device=device)
+        self.status = torch.zeros(4, dtype=torch.int32, device=device)   # bounded-wait error word of the kernels
         self.frozen = False
 
     def ensure(self, floats: int, counters: int = 0) -> None:
@@ -85,16 +86,18 @@ class Workspace:
             w = cls._per_device.get(key)
             if w is None:
                 w = cls._per_device[key] = Workspace(torch.device("cuda", key[1]))
+                if _C is not None:
+                    _C.set_status_word(w.status)
             return w
 
 
-def gemm_plan(M: int, N: int, K: int, force_splits: int = 0) -> dict:
-    bn, nt, mt, kt, splits, wsf, cnt = ext().gemm_plan(int(M), int(N), int(K), int(force_splits))
+def gemm_plan(M: int, N: int, K: int, force_ctas: int = 0) -> dict:
+    bn, nt, mt, kt, splits, wsf, cnt = ext().gemm_plan(int(M), int(N), int(K), int(force_ctas))
     return dict(bn=bn, n_tiles=nt, m_tiles=mt, k_tiles=kt, splits=splits, ws_floats=wsf, counters=cnt)
 
 
-def _ws_for(M, N, K, device, force_splits=0):
-    p = gemm_plan(M, N, K, force_splits)
+def _ws_for(M, N, K, device, force_ctas=0):
+    p = gemm_plan(M, N, K, force_ctas)
     w = Workspace.get(device)
     w.ensure(p["ws_floats"], p["counters"])
     return w
@@ -111,7 +114,7 @@ def _as_f16_2d(x: torch.Tensor) -> torch.Tensor:
 
 # ------------------------------------------------------------------------------------------------ GEMMs
 def w8a16_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, bias: Optional[torch.Tensor] = None,
-                 out_dtype: Optional[torch.dtype] = None, force_splits: int = 0) -> torch.Tensor:
+                 out_dtype: Optional[torch.dtype] = None, force_ctas: int = 0) -> torch.Tensor:
     """``y = x @ (qweight * scale[:, None])^T (+ bias)``; int8 weights ``[N, K]`` with per-row fp32 scales."""
     N, K = qweight.shape
     if not x.is_cuda:
@@ -125,35 +128,35 @@ def w8a16_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, bi
     M = x2.shape[0]
     od = out_dtype or torch.float16
     out = torch.empty(M, N, dtype=torch.float32 if od == torch.float32 else torch.float16, device=x.device)
-    w = _ws_for(M, N, K, x.device, force_splits)
-    C.w8a16_gemm(x2, qweight, scale, bias, out, w.ws, w.counters, force_splits)
+    w = _ws_for(M, N, K, x.device, force_ctas)
+    C.w8a16_gemm(x2, qweight, scale, bias, out, w.ws, w.counters, force_ctas)
     LAUNCH_COUNTER.add()
     out = out if out.dtype == od else out.to(od)
     return out.reshape(*lead, N)
 
 
 def w8a16_linear_out(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, out: torch.Tensor,
-                     force_splits: int = 0) -> torch.Tensor:
+                     force_ctas: int = 0) -> torch.Tensor:
     """``out[:] = x @ W^T`` into a preallocated f16/f32 ``[M, N]`` buffer."""
     if not x.is_cuda:
         out.copy_(x.to(torch.float32) @ (qweight.to(torch.float32) * scale[:, None]).t())
         return out
     x2 = _as_f16_2d(x)
-    w = _ws_for(x2.shape[0], qweight.shape[0], qweight.shape[1], x.device, force_splits)
-    ext().w8a16_gemm(x2, qweight, scale, None, out, w.ws, w.counters, force_splits)
+    w = _ws_for(x2.shape[0], qweight.shape[0], qweight.shape[1], x.device, force_ctas)
+    ext().w8a16_gemm(x2, qweight, scale, None, out, w.ws, w.counters, force_ctas)
     LAUNCH_COUNTER.add()
     return out
 
 
 def w8a16_residual_(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, resid: torch.Tensor,
-                    force_splits: int = 0) -> torch.Tensor:
+                    force_ctas: int = 0) -> torch.Tensor:
     """``resid += x @ W^T`` in place (fp32 residual stream)."""
     if not x.is_cuda:
         resid += x.to(torch.float32) @ (qweight.to(torch.float32) * scale[:, None]).t()
         return resid
     x2 = _as_f16_2d(x)
-    w = _ws_for(x2.shape[0], qweight.shape[0], qweight.shape[1], x.device, force_splits)
-    ext().w8a16_gemm_residual(x2, qweight, scale, resid, w.ws, w.counters, force_splits)
+    w = _ws_for(x2.shape[0], qweight.shape[0], qweight.shape[1], x.device, force_ctas)
+    ext().w8a16_gemm_residual(x2, qweight, scale, resid, w.ws, w.counters, force_ctas)
     LAUNCH_COUNTER.add()
     return resid
 
@@ -174,7 +177,7 @@ def interleave_gate_up(gate_q: torch.Tensor, up_q: torch.Tensor, gate_s: torch.T
     return q.contiguous(), s.contiguous()
 
 
-def w8a16_swiglu(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, force_splits: int = 0) -> torch.Tensor:
+def w8a16_swiglu(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, force_ctas: int = 0) -> torch.Tensor:
     """``silu(x @ Wg^T) * (x @ Wu^T)`` with ``w_gu`` packed by :func:`interleave_gate_up`; f16 output."""
     N2, K = w_gu.shape
     F = N2 // 2
@@ -185,8 +188,8 @@ def w8a16_swiglu(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, force_
         return (torch.nn.functional.silu(y[..., 0, :]) * y[..., 1, :]).reshape(*x.shape[:-1], F)
     x2 = _as_f16_2d(x)
     out = torch.empty(x2.shape[0], F, dtype=torch.float16, device=x.device)
-    w = _ws_for(x2.shape[0], N2, K, x.device, force_splits)
-    ext().w8a16_gemm_swiglu(x2, w_gu, s_gu, out, w.ws, w.counters, force_splits)
+    w = _ws_for(x2.shape[0], N2, K, x.device, force_ctas)
+    ext().w8a16_gemm_swiglu(x2, w_gu, s_gu, out, w.ws, w.counters, force_ctas)
     LAUNCH_COUNTER.add()
     return out.reshape(*x.shape[:-1], F)
 
@@ -194,7 +197,7 @@ def w8a16_swiglu(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, force_
 def w8a16_qkv_rope_append(x: torch.Tensor, w_qkv: torch.Tensor, s_qkv: torch.Tensor, bias: Optional[torch.Tensor],
                           q_rows: int, kv_rows: int, head_dim: int, positions: torch.Tensor, slots: torch.Tensor,
                           cos_t: torch.Tensor, sin_t: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
-                          q_out: Optional[torch.Tensor] = None, force_splits: int = 0) -> torch.Tensor:
+                          q_out: Optional[torch.Tensor] = None, force_ctas: int = 0) -> torch.Tensor:
     """Fused QKV projection + bias + rotate-half RoPE + paged KV append.  Returns q ``[M, q_rows]`` bf16."""
     M = x.reshape(-1, x.shape[-1]).shape[0]
     if not x.is_cuda:
@@ -220,9 +223,9 @@ def w8a16_qkv_rope_append(x: torch.Tensor, w_qkv: torch.Tensor, s_qkv: torch.Ten
     x2 = _as_f16_2d(x)
     if q_out is None:
         q_out = torch.empty(M, q_rows, dtype=torch.bfloat16, device=x.device)
-    w = _ws_for(M, w_qkv.shape[0], w_qkv.shape[1], x.device, force_splits)
+    w = _ws_for(M, w_qkv.shape[0], w_qkv.shape[1], x.device, force_ctas)
     ext().w8a16_gemm_qkv(x2, w_qkv, s_qkv, bias, q_rows, kv_rows, head_dim, positions, slots, cos_t, sin_t, q_out,
-                         k_cache, v_cache, w.ws, w.counters, force_splits)
+                         k_cache, v_cache, w.ws, w.counters, force_ctas)
     LAUNCH_COUNTER.add()
     return q_out
 
@@ -277,20 +280,33 @@ def embedding_q8(ids: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, 
 
 
 # ------------------------------------------------------------------------------------------------ attention
+KEYS_PER_TILE = 128   # the tensor-core decode kernel consumes 128-key tiles
+
+
 def decode_splits(max_ctx: int, batch_heads: int, block_size: int = 16, sms: int = 148) -> Tuple[int, int]:
-    """Split-K plan for decode attention: enough CTAs to cover ~2 waves, at least 4 blocks per split."""
-    blocks = max(1, (max_ctx + block_size - 1) // block_size)
-    want = max(1, (2 * sms + batch_heads - 1) // max(1, batch_heads))
-    splits = max(1, min(want, blocks // 4 if blocks >= 8 else 1))
-    per = (blocks + splits - 1) // splits
-    splits = (blocks + per - 1) // per
-    return splits, per * block_size
+    """Split-K plan for decode attention: about two resident CTAs per SM, whole 128-key tiles per split."""
+    tiles = max(1, (max_ctx + KEYS_PER_TILE - 1) // KEYS_PER_TILE)
+    want = max(1, (2 * sms) // max(1, batch_heads))
+    splits = max(1, min(want, tiles))
+    per = (tiles + splits - 1) // splits
+    splits = (tiles + per - 1) // per
+    return splits, per * KEYS_PER_TILE
+
+
+def check_status(device=None) -> None:
+    """Raise if any kernel on ``device`` hit a bounded-wait timeout (reads the status word; synchronizes)."""
+    w = Workspace.get(device if device is not None else torch.device("cuda"))
+    v = int(w.status[0].item())
+    if v:
+        w.status.zero_()
+        w.counters.zero_()   # stream-K tickets may be left mid-count by an aborted launch
+        raise RuntimeError(f"a kernel reported a bounded-wait timeout (code {v})")
 
 
 def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                            context_lens: torch.Tensor, scale: Optional[float] = None, splits: int = 0,
                            keys_per_split: int = 0, out: Optional[torch.Tensor] = None,
-                           max_ctx: Optional[int] = None) -> torch.Tensor:
+                           max_ctx: Optional[int] = None, allow_tc: bool = True) -> torch.Tensor:
     """One query token per sequence.  ``q [B, Hq, D]`` bf16 -> ``[B, Hq, D]`` f16."""
     B, Hq, D = q.shape
     scale = scale if scale is not None else 1.0 / math.sqrt(D)
@@ -322,7 +338,7 @@ def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torc
     need = ext().decode_attn_ws_floats(B, Hq, D, splits) if splits > 1 else 0
     ws.ensure(need)
     ext().decode_attention(q.contiguous(), k_cache, v_cache, block_tables, context_lens, out, ws.ws, splits,
-                           keys_per_split, float(scale))
+                           keys_per_split, float(scale), ws.status, bool(allow_tc))
     LAUNCH_COUNTER.add(2 if splits > 1 else 1)
     return out
 

@@ -41,12 +41,12 @@ def test_w8a16_gemm(M, N, K):
     assert err <= 1e-3 * max(1.0, ref.abs().max().item()), err
 
 
-@pytest.mark.parametrize("splits", [1, 2, 3, 7])
-def test_w8a16_split_k_deterministic(splits):
+@pytest.mark.parametrize("splits", [1, 2, 3, 7, 37, 148])
+def test_w8a16_stream_k_deterministic(splits):
     q, s = _qw(512, 2048, 3)
     x = _x(16, 2048, 4)
-    a = ops.w8a16_linear(x, q, s, out_dtype=torch.float32, force_splits=splits)
-    b = ops.w8a16_linear(x, q, s, out_dtype=torch.float32, force_splits=splits)
+    a = ops.w8a16_linear(x, q, s, out_dtype=torch.float32, force_ctas=splits)
+    b = ops.w8a16_linear(x, q, s, out_dtype=torch.float32, force_ctas=splits)
     assert torch.equal(a, b)
     ref = _ref(x, q, s)
     assert (a - ref).abs().max().item() < 1e-3
@@ -136,18 +136,34 @@ def _paged(B, lens, Hk, D, bs=16, seed=0):
     return kc, vc, tab
 
 
-@pytest.mark.parametrize("D,Hq,Hk", [(128, 8, 1), (128, 40, 8), (64, 8, 2)])
-@pytest.mark.parametrize("lens", [[1, 17, 300], [4096], [33, 2000]])
-@pytest.mark.parametrize("splits", [0, 1])
-def test_paged_decode_attention(D, Hq, Hk, lens, splits):
+@pytest.mark.parametrize("D,Hq,Hk", [(128, 8, 1), (128, 40, 8), (128, 64, 8), (64, 8, 2)])
+@pytest.mark.parametrize("lens", [[1, 17, 300], [4096], [33, 2000, 129, 128]])
+@pytest.mark.parametrize("splits", [0, 1, 3])
+@pytest.mark.parametrize("tc", [True, False])
+def test_paged_decode_attention(D, Hq, Hk, lens, splits, tc):
     B = len(lens)
     kc, vc, tab = _paged(B, lens, Hk, D)
     q = torch.randn(B, Hq, D).to(torch.bfloat16)
     cl = torch.tensor(lens, dtype=torch.int32)
     ref = ops.paged_decode_attention(q, kc, vc, tab, cl)
-    kw = {} if splits == 0 else dict(splits=1, keys_per_split=tab.shape[1] * 16)
-    out = ops.paged_decode_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), tab.to(DEV), cl.to(DEV), **kw)
+    kw = {}
+    if splits:
+        tiles = (tab.shape[1] * 16 + 127) // 128
+        per = (tiles + splits - 1) // splits
+        kw = dict(splits=(tiles + per - 1) // per, keys_per_split=per * 128)
+    out = ops.paged_decode_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), tab.to(DEV), cl.to(DEV), allow_tc=tc, **kw)
+    ops.check_status()
     assert (out.float().cpu() - ref.float()).abs().max().item() < 2e-2
+
+
+def test_decode_attention_tc_deterministic():
+    lens = [4000, 1500]
+    kc, vc, tab = _paged(2, lens, 8, 128, seed=9)
+    q = torch.randn(2, 64, 128).to(torch.bfloat16).to(DEV)
+    args = (kc.to(DEV), vc.to(DEV), tab.to(DEV), torch.tensor(lens, dtype=torch.int32, device=DEV))
+    a = ops.paged_decode_attention(q, *args)
+    b = ops.paged_decode_attention(q, *args)
+    assert torch.equal(a, b)
 
 
 @pytest.mark.parametrize("D,Hq,Hk", [(128, 8, 2), (64, 4, 4)])
