@@ -339,4 +339,299 @@ void decode_attn_tc_launch(const DecodeAttnArgs& a, int num_blocks, int* status,
   if (a.splits > 1) decode_combine_launch(a, s);
 }
 
+
+// ================================================================================================================
+// Paged prefill (varlen, causal) flash attention on tcgen05.
+//
+// One CTA = (query tile, kv head, sequence).  A query tile is 128 MMA rows packing the GQA group: row r is token
+// t0 + r / G, head hk*G + r % G, so one K/V tile feeds all heads sharing the kv head (tokens per tile = 128 / G).
+//     S[128 rows x 128 keys] = Q_tile . K_tile^T          (A = Q, K-major; B = K tile, K-major)
+//     O[128 rows x D]       += P . V_tile                 (A = P, K-major; B = V tile, MN-major)
+// Q arrives by one 3-D TMA box per 64 dims (view [T][Hq][D]); K/V tiles come from the paged cache exactly as in
+// decode.  Softmax: thread = row (TMEM lane), two TMEM passes per tile (max, then exp2 + P store), lazy rescaling:
+// O and the row sum are rescaled only when the row max grows by more than 2^8, so most tiles skip the O round trip.
+// S is double-buffered in TMEM (2 x 128 columns) so the next QK^T overlaps the softmax; O uses 128 more columns.
+// CTAs are launched heaviest-first (last query tiles see the most keys).
+// ================================================================================================================
+namespace {
+constexpr int kPfRows = 128;
+constexpr int kPfThreads = 6 * 32;
+constexpr float kRescaleThresh = 8.0f;   // log2 units
+struct PfSmem {
+  static constexpr int kQ = 0;                                 // 2 regions x [128 rows][128 B] = 32 KB
+  static constexpr int kRing = kQ + 2 * kPfRows * 128;         // kSlots x 32 KB
+  static constexpr int kP = kRing + kSlots * kSlotBytes;       // 2 regions x 16 KB
+  static constexpr int kBar = kP + 2 * kPfRows * 128;
+  static constexpr int kBytes = kBar + 16 * 8 + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+};
+}  // namespace
+
+__global__ void __launch_bounds__(kPfThreads, 1)
+attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const PrefillAttnArgs a, int tpt, int* status) {
+  const int G = a.Hq / a.Hk;
+  const int tile = gridDim.x - 1 - blockIdx.x;   // heaviest (latest) tiles first
+  const int hk = blockIdx.y, seq = blockIdx.z;
+  const int qo = a.cu_q[seq];
+  const int qlen = a.cu_q[seq + 1] - qo;
+  const int t0 = tile * tpt;
+  if (t0 >= qlen) return;   // uniform exit before any barrier / TMEM allocation
+  const int qstart = a.q_start[seq];
+  const int ctx = a.context_lens[seq];
+  const int tl = min(qlen, t0 + tpt) - 1;
+  const int kend = min(ctx, qstart + tl + 1);
+  const int nt = (kend + kKeys - 1) / kKeys;
+  const float scale2 = a.scale * kLog2e;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* qs = base + PfSmem::kQ;
+  uint8_t* ring = base + PfSmem::kRing;
+  uint8_t* ps = base + PfSmem::kP;
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + PfSmem::kBar);
+  uint64_t* empty = full + kSlots;
+  uint64_t* sfull = empty + kSlots;   // [2]
+  uint64_t* pfull = sfull + 2;
+  uint64_t* pvdone = pfull + 1;
+  uint64_t* qfull = pvdone + 1;
+  uint64_t* mdone = qfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&sfull[0], 1);
+    mbar_init(&sfull[1], 1);
+    mbar_init(pfull, 128);
+    mbar_init(pvdone, 1);
+    mbar_init(qfull, 1);
+    mbar_init(mdone, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(qfull, 2 * 128 * G * tpt);
+      tma_load_3d(qs, &tmQ, qfull, 0, hk * G, qo + t0);
+      tma_load_3d(qs + kPfRows * 128, &tmQ, qfull, 64, hk * G, qo + t0);
+      const int* btab = a.block_tables + (size_t)seq * a.max_blocks;
+      int issued = 0;
+      for (int t = 0; t < nt; ++t) {
+        for (int kv = 0; kv < 2; ++kv) {
+          const int u = 2 * t + kv, s = u % kSlots;
+          if (!mbar_wait_ab(&empty[s], ((uint32_t)(u / kSlots) & 1u) ^ 1u, status, kErrTimeoutEmpty, abort_flag))
+            goto pf_prod_done;
+          mbar_arrive_expect_tx(&full[s], kSlotBytes);
+          uint8_t* dst = ring + s * kSlotBytes;
+          const CUtensorMap* m = kv ? &tmV : &tmK;
+          for (int j = 0; j < kKeys / 16; ++j) {
+            int bi = t * (kKeys / 16) + j;
+            bi = bi < a.max_blocks ? bi : a.max_blocks - 1;
+            const int blk = btab[bi];
+            tma_load_4d(dst + j * 2048, m, &full[s], 0, 0, hk, blk);
+            tma_load_4d(dst + 16384 + j * 2048, m, &full[s], 64, 0, hk, blk);
+          }
+          ++issued;
+        }
+      }
+    pf_prod_done:
+      mbar_wait(qfull, 0, status, kErrTimeoutFull);
+      for (int u = max(0, issued - kSlots); u < issued; ++u)
+        mbar_wait(&full[u % kSlots], (uint32_t)(u / kSlots) & 1u, status, kErrTimeoutFull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(kPfRows, kKeys, false);
+      constexpr uint32_t idO = idesc_bf16_f32(kPfRows, kD, true);   // B = V tile, MN-major
+      const uint32_t qa = smem_u32(qs), pa = smem_u32(ps);
+      bool ok = mbar_wait_ab(qfull, 0, status, kErrTimeoutFull, abort_flag);
+      auto issue_s = [&](int t) -> bool {
+        const int u = 2 * t, s = u % kSlots;
+        if (!mbar_wait_ab(&full[s], (uint32_t)(u / kSlots) & 1u, status, kErrTimeoutFull, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(ring + s * kSlotBytes);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_f16_ss(tmem + (uint32_t)(t & 1) * 128u, sdesc_sw128(qa + off), sdesc_sw128(ka + off), idS,
+                      kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+        umma_commit(&sfull[t & 1]);
+        return true;
+      };
+      ok = ok && issue_s(0);
+      for (int t = 0; ok && t < nt; ++t) {
+        if (t + 1 < nt && !issue_s(t + 1)) break;
+        if (!mbar_wait_ab(pfull, (uint32_t)t & 1u, status, kErrTimeoutDequant, abort_flag)) break;
+        const int u = 2 * t + 1, s = u % kSlots;
+        if (!mbar_wait_ab(&full[s], (uint32_t)(u / kSlots) & 1u, status, kErrTimeoutFull, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t va = smem_u32(ring + s * kSlotBytes);
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; ++kk) {
+          const uint32_t poff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_f16_ss(tO, sdesc_sw128(pa + poff), sdesc_sw128_mn(va + kk * 2048, 16384), idO,
+                      (t > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+        umma_commit(pvdone);
+      }
+      umma_commit(mdone);
+      mbar_wait(mdone, 0, status, kErrTimeoutAccum);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax (thread = row)
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const bool row_ok = r < G * tpt && t0 + r / G < qlen;
+    const int pos = qstart + t0 + r / G;
+    const int kmax = row_ok ? min(ctx, pos + 1) : 0;   // keys [0, kmax) visible to this row
+    float m_used = -INFINITY, l = 0.f;
+    for (int it = 0; it < nt; ++it) {
+      mbar_wait_ab(&sfull[it & 1], (uint32_t)(it >> 1) & 1u, status, kErrTimeoutAccum, abort_flag);
+      tc_fence_after();
+      const uint32_t sa = tmem + (uint32_t)(it & 1) * 128u + lane_off;
+      const int key0 = it * kKeys;
+      float tmax = -INFINITY;
+      for (int c = 0; c < kKeys; c += 32) {
+        float v[32];
+        tmem_ld32(sa + (uint32_t)c, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (key0 + c + i < kmax) tmax = fmaxf(tmax, v[i]);
+      }
+      tmax *= scale2;
+      float corr = 1.f;
+      bool rescale = false;
+      if (tmax > m_used + kRescaleThresh || (m_used == -INFINITY && tmax != -INFINITY)) {
+        corr = m_used == -INFINITY ? 0.f : exp2f(m_used - tmax);
+        rescale = m_used != -INFINITY;
+        m_used = tmax;
+        l *= corr;
+      }
+      if (it > 0) mbar_wait_ab(pvdone, (uint32_t)(it - 1) & 1u, status, kErrTimeoutAccum, abort_flag);
+      tc_fence_after();
+      if (rescale && it > 0) {
+        for (int c = 0; c < kD; c += 32) {
+          float o[32];
+          tmem_ld32(tO + lane_off + (uint32_t)c, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= corr;
+          tmem_st32(tO + lane_off + (uint32_t)c, o);
+        }
+      }
+      // P row: keys [c, c+32) -> region c/64, 16-byte chunks ((c%64)/8 + q) ^ (r%8)
+      for (int c = 0; c < kKeys; c += 32) {
+        float v[32];
+        tmem_ld32(sa + (uint32_t)c, v);
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = (key0 + c + i < kmax && m_used != -INFINITY) ? exp2f(v[i] * scale2 - m_used) : 0.f;
+          const float p1 = (key0 + c + i + 1 < kmax && m_used != -INFINITY) ? exp2f(v[i + 1] * scale2 - m_used) : 0.f;
+          l += p0 + p1;
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+          pk[i >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        uint8_t* prow = ps + (c >> 6) * 16384 + r * 128;
+        const int cb = (c & 63) >> 3;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(prow + (((cb + q) ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(pfull);
+    }
+    if (nt > 0) mbar_wait_ab(pvdone, (uint32_t)(nt - 1) & 1u, status, kErrTimeoutAccum, abort_flag);
+    tc_fence_after();
+    {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __half* orow = a.out + ((size_t)(qo + t0 + r / G) * a.Hq + hk * G + r % G) * kD;
+      for (int c = 0; c < kD; c += 32) {
+        float o[32];
+        if (nt > 0) {
+          tmem_ld32(tO + lane_off + (uint32_t)c, o);   // warp-collective: every lane loads
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (!row_ok) continue;
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          __half2 h0 = __floats2half2_rn(o[i] * inv, o[i + 1] * inv), h1 = __floats2half2_rn(o[i + 2] * inv, o[i + 3] * inv);
+          __half2 h2 = __floats2half2_rn(o[i + 4] * inv, o[i + 5] * inv), h3 = __floats2half2_rn(o[i + 6] * inv, o[i + 7] * inv);
+          *reinterpret_cast<uint4*>(orow + c + i) =
+              make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                         *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+bool prefill_attn_tc_supported(const PrefillAttnArgs& a) {
+  const int G = a.Hk > 0 ? a.Hq / a.Hk : 0;
+  return a.D == kD && a.block_size == 16 && G >= 1 && G <= 128 && a.Hq % a.Hk == 0;
+}
+
+void prefill_attn_tc_launch(const PrefillAttnArgs& a, int num_blocks, int total_q, int* status, cudaStream_t s) {
+  if (!prefill_attn_tc_supported(a)) throw std::runtime_error("tcgen05 prefill attention: unsupported shape");
+  if (a.S == 0 || a.max_q == 0) return;
+  const int G = a.Hq / a.Hk;
+  const int tpt = kPfRows / G;
+  CUtensorMap tq, tk, tv;
+  {
+    if ((reinterpret_cast<uintptr_t>(a.q) & 15) != 0) throw std::runtime_error("q must be 16-byte aligned");
+    cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)a.Hq, (cuuint64_t)total_q};
+    cuuint64_t strides[2] = {(cuuint64_t)kD * 2, (cuuint64_t)a.Hq * kD * 2};
+    cuuint32_t box[3] = {64, (cuuint32_t)G, (cuuint32_t)tpt};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = tmap_encode_fn()(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<__nv_bfloat16*>(a.q), dims,
+                                  strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("Q tensor map encode failed: " + std::to_string((int)r));
+  }
+  make_kv_map(&tk, a.k_cache, num_blocks, a.Hk, a.block_size);
+  make_kv_map(&tv, a.v_cache, num_blocks, a.Hk, a.block_size);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PfSmem::kAlloc);
+    attr = true;
+  }
+  if (status == nullptr) status = status_word();
+  dim3 grid((a.max_q + tpt - 1) / tpt, a.Hk, a.S);
+  attn_prefill_tc_kernel<<<grid, kPfThreads, PfSmem::kAlloc, s>>>(tq, tk, tv, a, tpt, status);
+}
+
 }  // namespace hrm

@@ -221,7 +221,7 @@ void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::
 
 void prefill_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_tables,
                        at::Tensor cu_q, at::Tensor q_start, at::Tensor context_lens, at::Tensor out, int64_t max_q,
-                       double scale) {
+                       double scale, bool allow_tc) {
   c10::cuda::CUDAGuard g(q.device());
   CHECK_DTYPE(q, at::kBFloat16); CHECK_DTYPE(k_cache, at::kBFloat16); CHECK_DTYPE(v_cache, at::kBFloat16);
   CHECK_DTYPE(block_tables, at::kInt); CHECK_DTYPE(cu_q, at::kInt); CHECK_DTYPE(q_start, at::kInt);
@@ -241,7 +241,10 @@ void prefill_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at:
   a.q_start = q_start.data_ptr<int>();
   a.context_lens = context_lens.data_ptr<int>();
   a.out = reinterpret_cast<__half*>(out.data_ptr());
-  hrm::prefill_attn_launch(a, cur_stream());
+  if (allow_tc && hrm::prefill_attn_tc_supported(a))
+    hrm::prefill_attn_tc_launch(a, (int)k_cache.size(0), (int)q.size(0), nullptr, cur_stream());
+  else
+    hrm::prefill_attn_launch(a, cur_stream());
 }
 
 void argmax_rows(at::Tensor logits, int64_t vocab_start, c10::optional<at::Tensor> keys, at::Tensor tokens) {
@@ -295,7 +298,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attn_ws_floats", [](int64_t B, int64_t Hq, int64_t D, int64_t s) {
     return (int64_t)hrm::decode_attn_ws_floats((int)B, (int)Hq, (int)D, (int)s);
   });
-  m.def("prefill_attention", &prefill_attention);
+  m.def("prefill_attention", &prefill_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("block_tables"), py::arg("cu_q"), py::arg("q_start"), py::arg("context_lens"), py::arg("out"),
+        py::arg("max_q"), py::arg("scale"), py::arg("allow_tc") = true);
   m.def("argmax_rows", &argmax_rows);
   m.def("decode_prepare", &decode_prepare_bs);
   m.def("decode_advance", &decode_advance);

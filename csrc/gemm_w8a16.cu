@@ -14,8 +14,8 @@
 //  * warp 0: TMA producer.  Raw int8 weight tiles [128 x 64] (64-byte swizzle) and the f16 activation tile [BN x 64]
 //    (128-byte swizzle, canonical K-major UMMA layout) stream through a deep ring (R slots), across segment and
 //    tile boundaries, so HBM sees a continuous stream.
-//  * warps 2-9: dequant int8 -> f16 exactly (prmt + f16x2 subtract) into a shorter ring of 128-byte-swizzled A tiles;
-//    the per-row scale is applied once in the epilogue.
+//  * warps 2-9: dequant int8 -> f16 exactly (prmt + f16x2 subtract) into a shorter ring of 128-byte-swizzled A tiles,
+//    as 4 independent 2-warp groups taking alternate k-tiles; the per-row scale is applied once in the epilogue.
 //  * warp 1: one thread issues tcgen05.mma (kind::f16, fp32 accumulate) into one of two TMEM accumulators and
 //    tcgen05.commit releases ring slots / publishes a finished accumulator.
 //  * warps 10-13: epilogue (thread = TMEM lane = weight row), overlapped with the next segment's mainloop: plain
@@ -42,6 +42,8 @@ constexpr int kFirstDqWarp = 2;
 constexpr int kFirstEpiWarp = kFirstDqWarp + kDqWarps;
 constexpr int kThreads = (kFirstEpiWarp + kEpiWarps) * 32;   // 448
 constexpr int kDqThreads = kDqWarps * 32;
+constexpr int kDqGroups = 4;                   // independent dequant groups (2 warps each)
+constexpr int kDqGroupThreads = kDqThreads / kDqGroups;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kWrawBytes = kBM * kBK;          // int8 tile, 8 KB
 constexpr int kW16Bytes = kBM * kBK * 2;       // f16 tile, 16 KB
@@ -51,8 +53,8 @@ template <int BN> struct GemmCfg;   // raw ring depth R, f16 ring depth F
 template <> struct GemmCfg<16>  { static constexpr int R = 12, F = 4; };
 template <> struct GemmCfg<32>  { static constexpr int R = 10, F = 4; };
 template <> struct GemmCfg<64>  { static constexpr int R = 8, F = 4; };
-template <> struct GemmCfg<128> { static constexpr int R = 5, F = 3; };
-template <> struct GemmCfg<256> { static constexpr int R = 3, F = 3; };
+template <> struct GemmCfg<128> { static constexpr int R = 5, F = 4; };
+template <> struct GemmCfg<256> { static constexpr int R = 3, F = 4; };
 
 template <int BN>
 struct GemmSmem {
@@ -184,7 +186,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       mbar_init(&rempty[s], 1);
     }
     for (int s = 0; s < F; ++s) {
-      mbar_init(&ffull[s], kDqThreads);
+      mbar_init(&ffull[s], kDqGroupThreads);
       mbar_init(&fempty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
@@ -263,28 +265,32 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
     }
   } else if (warp < kFirstEpiWarp) {
     // ------------------------------------------------------------------ dequant
+    // 4 independent groups of 2 warps; group g converts k-tiles i = g, g+4, ... so four tiles are in conversion
+    // at once and one tile's latency (smem round trip, proxy fence, barrier) never stalls the stream.
     const int t = threadIdx.x - kFirstDqWarp * 32;   // 0..255
-    const int r = t & (kBM - 1);
-    const int h = t >> 7;
-    const int sw64 = (r >> 1) & 3, sw128 = r & 7;
-    int64_t i = 0;
-    for (int64_t u = u0; u < u1; ++u, ++i) {
+    const int g = t >> 6;                             // group 0..3
+    const int gt = t & 63;                            // thread within group: rows gt and gt + 64
+    const int64_t n_units = u1 - u0;
+    for (int64_t i = g; i < n_units; i += kDqGroups) {
       const int rs = (int)(i % R), fs = (int)(i % F);
       if (!mbar_wait_ab(&rfull[rs], (uint32_t)(i / R) & 1u, a.status, kErrTimeoutFull, abort_flag)) break;
       if (!mbar_wait_ab(&fempty[fs], ((uint32_t)(i / F) & 1u) ^ 1u, a.status, kErrTimeoutEmpty, abort_flag)) break;
-      const uint8_t* src = wraw + rs * kWrawBytes + r * 64;
-      const uint4 v0 = *reinterpret_cast<const uint4*>(src + (((2 * h) ^ sw64) << 4));
-      const uint4 v1 = *reinterpret_cast<const uint4*>(src + (((2 * h + 1) ^ sw64) << 4));
-      uint8_t* dst = w16 + fs * kW16Bytes + r * 128;
-      uint4 o;
-      i8x4_to_f16x4(v0.x, o.x, o.y); i8x4_to_f16x4(v0.y, o.z, o.w);
-      *reinterpret_cast<uint4*>(dst + (((4 * h + 0) ^ sw128) << 4)) = o;
-      i8x4_to_f16x4(v0.z, o.x, o.y); i8x4_to_f16x4(v0.w, o.z, o.w);
-      *reinterpret_cast<uint4*>(dst + (((4 * h + 1) ^ sw128) << 4)) = o;
-      i8x4_to_f16x4(v1.x, o.x, o.y); i8x4_to_f16x4(v1.y, o.z, o.w);
-      *reinterpret_cast<uint4*>(dst + (((4 * h + 2) ^ sw128) << 4)) = o;
-      i8x4_to_f16x4(v1.z, o.x, o.y); i8x4_to_f16x4(v1.w, o.z, o.w);
-      *reinterpret_cast<uint4*>(dst + (((4 * h + 3) ^ sw128) << 4)) = o;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int r = gt + half * 64;
+        const int sw64 = (r >> 1) & 3, sw128 = r & 7;
+        const uint8_t* src = wraw + rs * kWrawBytes + r * 64;
+        uint8_t* dst = w16 + fs * kW16Bytes + r * 128;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 v = *reinterpret_cast<const uint4*>(src + ((c ^ sw64) << 4));
+          uint4 o;
+          i8x4_to_f16x4(v.x, o.x, o.y); i8x4_to_f16x4(v.y, o.z, o.w);
+          *reinterpret_cast<uint4*>(dst + (((2 * c) ^ sw128) << 4)) = o;
+          i8x4_to_f16x4(v.z, o.x, o.y); i8x4_to_f16x4(v.w, o.z, o.w);
+          *reinterpret_cast<uint4*>(dst + (((2 * c + 1) ^ sw128) << 4)) = o;
+        }
+      }
       fence_proxy_async_smem();
       mbar_arrive(&ffull[fs]);
     }

@@ -45,6 +45,9 @@ struct PrefillAttnArgs {
   float scale;
 };
 void prefill_attn_launch(const PrefillAttnArgs& a, cudaStream_t s);
+// tcgen05 variant (head_dim 128, block size 16); total_q = rows of q
+bool prefill_attn_tc_supported(const PrefillAttnArgs& a);
+void prefill_attn_tc_launch(const PrefillAttnArgs& a, int num_blocks, int total_q, int* status, cudaStream_t s);
 
 // Row argmax of fp32 logits [M, V] -> packed (order(value) << 32 | ~global_idx) keys, and token ids.
 void argmax_launch(const float* logits, int M, int V, int ld, int vocab_start, unsigned long long* keys,

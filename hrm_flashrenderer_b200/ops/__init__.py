@@ -346,7 +346,7 @@ def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torc
 def paged_prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                             block_tables: torch.Tensor, cu_q: torch.Tensor, q_start: torch.Tensor,
                             context_lens: torch.Tensor, max_q: int, scale: Optional[float] = None,
-                            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                            out: Optional[torch.Tensor] = None, allow_tc: bool = True) -> torch.Tensor:
     """Causal attention of varlen query chunks ``q [Tq, Hq, D]`` against the paged cache (chunk already appended)."""
     Tq, Hq, D = q.shape
     scale = scale if scale is not None else 1.0 / math.sqrt(D)
@@ -369,8 +369,9 @@ def paged_prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
         return res.to(torch.float16)
     if out is None:
         out = torch.empty(Tq, Hq, D, dtype=torch.float16, device=q.device)
+    Workspace.get(q.device)   # registers the kernels' status word
     ext().prefill_attention(q.contiguous(), k_cache, v_cache, block_tables, cu_q, q_start, context_lens, out,
-                            int(max_q), float(scale))
+                            int(max_q), float(scale), bool(allow_tc))
     LAUNCH_COUNTER.add()
     return out
 

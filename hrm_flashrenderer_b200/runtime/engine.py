@@ -179,8 +179,11 @@ class InferenceEngine:
             ws.frozen = False
         g.ids.copy_(saved[0]); g.positions.copy_(saved[1]); g.active.copy_(saved[2])
 
-    def load_decode_batch(self, seq_ids: Sequence[int], last_tokens: Sequence[int], reserve: int) -> _DecodeGraph:
-        """Stage a decode batch: block tables grown for ``reserve`` more tokens, current tokens and positions."""
+    def load_decode_batch(self, seq_ids: Sequence[int], last_tokens: Sequence[int], reserve: int,
+                          positions: Optional[Sequence[int]] = None) -> _DecodeGraph:
+        """Stage a decode batch: block tables grown for ``reserve`` more tokens, current tokens and positions.
+
+        ``positions[i]`` is the absolute position of ``last_tokens[i]`` (default: the prefilled length)."""
         n = len(seq_ids)
         bucket = self._bucket(n)
         g = self._decode_state(bucket)
@@ -189,7 +192,7 @@ class InferenceEngine:
         ids = torch.zeros(bucket, dtype=torch.int64)
         act = torch.zeros(bucket, dtype=torch.int32)
         for i, (sid, t) in enumerate(zip(seq_ids, last_tokens)):
-            L = self.bm.lengths.get(sid, 0)
+            L = int(positions[i]) if positions is not None else self.bm.lengths.get(sid, 0)
             tab = self.bm.grow(sid, min(L + reserve, self.max_blocks * self.block_size))
             tabs[i, :len(tab)] = torch.tensor(tab, dtype=torch.int32)
             pos[i] = L

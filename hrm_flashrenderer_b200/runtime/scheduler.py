@@ -1,0 +1,218 @@
+"""Continuous-batching scheduler over :class:`~hrm_flashrenderer_b200.runtime.engine.InferenceEngine`.
+
+One background thread owns the engine (and its CUDA graphs).  Each iteration it
+
+1. admits waiting requests while the decode batch has room and the KV pool has blocks (chunked prefill of up to
+   ``prefill_chunk`` prompt tokens per forward, several requests per chunk), which yields their first token;
+2. runs one graph-replayed decode step for every running request (the batch is re-staged on the device only when
+   its membership changed; otherwise the sampled tokens are fed back on the device);
+3. streams tokens to the requests, retires finished ones (EOS or ``max_new_tokens``) and frees their blocks.
+
+The reference serves one request at a time per engine process (``hrm_flash/serve.py:147,235-301`` with the
+``max_concurrent=1`` semaphore and file IPC into ``deepseek_native_engine``); this scheduler is what lets one lane
+serve many concurrent requests with one weight stream per step.  Metrics (TTFT, inter-token latency, queue depth,
+batch size, tok/s) are kept for ``/v1/health``.
+"""
+from __future__ import annotations
+
+import collections
+import queue
+import threading
+import time
+from concurrent.futures import Future
+from dataclasses import dataclass, field
+from typing import Callable, Deque, Dict, List, Optional, Sequence
+
+import torch
+
+
+@dataclass
+class GenRequest:
+    prompt_ids: List[int]
+    max_new_tokens: int
+    stop_on_eos: bool = True
+    on_token: Optional[Callable[[int], None]] = None
+    rid: int = 0
+    arrival: float = field(default_factory=time.perf_counter)
+    first_token_at: Optional[float] = None
+    finished_at: Optional[float] = None
+    tokens: List[int] = field(default_factory=list)
+    future: Future = field(default_factory=Future)
+    seq_id: int = -1
+    error: Optional[BaseException] = None
+
+    @property
+    def ttft_s(self) -> Optional[float]:
+        return None if self.first_token_at is None else self.first_token_at - self.arrival
+
+
+class Scheduler:
+    def __init__(self, engine, max_batch: Optional[int] = None, prefill_chunk: Optional[int] = None,
+                 idle_sleep_s: float = 0.0005):
+        self.engine = engine
+        self.max_batch = int(max_batch or engine.ecfg.max_batch)
+        self.prefill_chunk = int(prefill_chunk or engine.ecfg.prefill_chunk)
+        self.idle_sleep_s = idle_sleep_s
+        self._inbox: "queue.Queue[GenRequest]" = queue.Queue()
+        self._waiting: Deque[GenRequest] = collections.deque()
+        self._running: List[GenRequest] = []
+        self._stop = threading.Event()
+        self._thread: Optional[threading.Thread] = None
+        self._next_rid = 0
+        self._lock = threading.Lock()
+        self.eos = set(engine.cfg.eos_token_ids)
+        # metrics
+        self.completed = 0
+        self.generated_tokens = 0
+        self.ttfts: Deque[float] = collections.deque(maxlen=4096)
+        self.itls: Deque[float] = collections.deque(maxlen=4096)
+        self.started_at = time.perf_counter()
+        self.last_error: Optional[str] = None
+
+    # ------------------------------------------------------------------ lifecycle
+    def start(self) -> "Scheduler":
+        if self._thread is None:
+            self._thread = threading.Thread(target=self._loop, name="hrm-b200-scheduler", daemon=True)
+            self._thread.start()
+        return self
+
+    def stop(self, timeout: float = 10.0) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout)
+            self._thread = None
+
+    def alive(self) -> bool:
+        return self._thread is not None and self._thread.is_alive()
+
+    # ------------------------------------------------------------------ API
+    def submit(self, prompt_ids: Sequence[int], max_new_tokens: int, stop_on_eos: bool = True,
+               on_token: Optional[Callable[[int], None]] = None) -> GenRequest:
+        if not prompt_ids:
+            raise ValueError("empty prompt")
+        limit = self.engine.max_blocks * self.engine.block_size
+        if len(prompt_ids) + max_new_tokens > limit:
+            raise ValueError(f"prompt ({len(prompt_ids)}) + max_new_tokens ({max_new_tokens}) exceeds the "
+                             f"engine's max sequence length {limit}")
+        with self._lock:
+            rid = self._next_rid
+            self._next_rid += 1
+        r = GenRequest(list(map(int, prompt_ids)), int(max_new_tokens), stop_on_eos, on_token, rid)
+        self._inbox.put(r)
+        return r
+
+    def generate(self, prompt_ids: Sequence[int], max_new_tokens: int, timeout: Optional[float] = None,
+                 stop_on_eos: bool = True) -> List[int]:
+        return self.submit(prompt_ids, max_new_tokens, stop_on_eos).future.result(timeout)
+
+    def metrics(self) -> Dict:
+        el = max(1e-9, time.perf_counter() - self.started_at)
+        tt = sorted(self.ttfts)
+        it = sorted(self.itls)
+        pct = lambda a, q: (a[min(len(a) - 1, int(q * len(a)))] * 1e3) if a else None
+        return {"queue_depth": len(self._waiting) + self._inbox.qsize(), "batch_size": len(self._running),
+                "completed": self.completed, "generated_tokens": self.generated_tokens,
+                "tok_per_s": self.generated_tokens / el, "ttft_p50_ms": pct(tt, 0.5), "ttft_p99_ms": pct(tt, 0.99),
+                "itl_p50_ms": pct(it, 0.5), "last_error": self.last_error}
+
+    # ------------------------------------------------------------------ loop
+    def _finish(self, r: GenRequest) -> None:
+        r.finished_at = time.perf_counter()
+        self.engine.release(r.seq_id)
+        self.completed += 1
+        if not r.future.done():
+            r.future.set_result(list(r.tokens))
+
+    def _emit(self, r: GenRequest, tok: int) -> bool:
+        """Append a token; returns True when the request is finished."""
+        r.tokens.append(tok)
+        self.generated_tokens += 1
+        if r.on_token is not None:
+            try:
+                r.on_token(tok)
+            except Exception:
+                pass
+        return len(r.tokens) >= r.max_new_tokens or (r.stop_on_eos and tok in self.eos)
+
+    def _admit(self) -> bool:
+        while True:
+            try:
+                self._waiting.append(self._inbox.get_nowait())
+            except queue.Empty:
+                break
+        if not self._waiting or len(self._running) >= self.max_batch:
+            return False
+        batch, used = [], 0
+        eng = self.engine
+        while self._waiting and len(self._running) + len(batch) < self.max_batch and used < self.prefill_chunk:
+            r = self._waiting[0]
+            need = eng.bm.blocks_needed(-1, len(r.prompt_ids) + r.max_new_tokens)
+            if need > eng.bm.free_blocks - sum(eng.bm.blocks_needed(-1, len(b.prompt_ids) + b.max_new_tokens)
+                                               for b in batch):
+                break
+            self._waiting.popleft()
+            r.seq_id = eng.new_seq()
+            batch.append(r)
+            used += len(r.prompt_ids)
+        if not batch:
+            return False
+        firsts = eng.prefill([(r.seq_id, r.prompt_ids) for r in batch])
+        now = time.perf_counter()
+        for r, t in zip(batch, firsts):
+            r.first_token_at = now
+            self.ttfts.append(now - r.arrival)
+            r._last_tok_at = now
+            r._pos = len(r.prompt_ids)
+            if self._emit(r, int(t)):
+                self._finish(r)
+            else:
+                self._running.append(r)
+        return True
+
+    def _decode(self, staged: bool, g) -> tuple:
+        eng = self.engine
+        if not staged:
+            g = eng.load_decode_batch([r.seq_id for r in self._running], [r.tokens[-1] for r in self._running],
+                                      reserve=max(r.max_new_tokens - len(r.tokens) for r in self._running) + 1,
+                                      positions=[r._pos for r in self._running])
+        tok = eng.decode_step(g)
+        host = tok[:len(self._running)].tolist()
+        now = time.perf_counter()
+        still, changed = [], False
+        for r, t in zip(self._running, host):
+            r._pos += 1
+            self.itls.append(now - r._last_tok_at)
+            r._last_tok_at = now
+            if self._emit(r, int(t)):
+                self._finish(r)
+                changed = True
+            else:
+                still.append(r)
+        self._running = still
+        return (not changed), g
+
+    def _loop(self) -> None:
+        staged, g = False, None
+        dev = self.engine.device
+        if dev.type == "cuda":
+            torch.cuda.set_device(dev)
+        while not self._stop.is_set():
+            try:
+                admitted = self._admit()
+                if admitted:
+                    staged = False
+                if self._running:
+                    staged, g = self._decode(staged, g)
+                elif not admitted:
+                    time.sleep(self.idle_sleep_s)
+            except BaseException as e:   # fail the in-flight requests, keep serving new ones
+                self.last_error = repr(e)
+                for r in self._running + list(self._waiting):
+                    if not r.future.done():
+                        r.future.set_exception(e)
+                    try:
+                        self.engine.release(r.seq_id)
+                    except Exception:
+                        pass
+                self._running, staged = [], False
+                self._waiting.clear()

@@ -1,0 +1,127 @@
+"""Generation backends behind the HTTP service.
+
+* :class:`EngineBackend` -- the in-process B200 engine + continuous-batching scheduler (replaces the reference's
+  ``DeepSeekNativeEngine``: a child process driven through prompt/tokens/done files polled every 50-200 ms,
+  ``hrm_flash/deepseek_native.py:182-369``).  Weights come from a DSI8 file or from random-init synthesis of a preset
+  architecture; the tokenizer is a local HF tokenizer or the byte tokenizer.
+* :class:`EchoBackend` -- deterministic stand-in used by tests and the mock lanes.
+
+All backends expose ``tokenizer``, ``generate(prompt_text, max_new_tokens, timeout_s) -> str``, ``is_running()``,
+``stop()`` and ``metrics()``.
+"""
+from __future__ import annotations
+
+import hashlib
+import threading
+from pathlib import Path
+from typing import Dict, List, Optional
+
+
+class ByteTokenizer:
+    """UTF-8 byte tokenizer (ids 3..258 = bytes; 0 pad, 1 bos, 2 eos).  Used when no HF tokenizer is configured
+    (synthetic random-init models); HF-compatible call signature for the prompt budget fitter."""
+
+    pad_id, bos_id, eos_id, offset = 0, 1, 2, 3
+
+    def __call__(self, text: str, add_special_tokens: bool = True, **_):
+        ids = [b + self.offset for b in text.encode("utf-8")]
+        if add_special_tokens:
+            ids = [self.bos_id] + ids
+        return {"input_ids": ids}
+
+    def encode(self, text: str, add_special_tokens: bool = True) -> List[int]:
+        return self(text, add_special_tokens)["input_ids"]
+
+    def decode(self, ids, skip_special_tokens: bool = True) -> str:
+        bs = bytes((int(i) - self.offset) % 256 for i in ids
+                   if not (skip_special_tokens and int(i) < self.offset))
+        return bs.decode("utf-8", errors="replace")
+
+
+def load_tokenizer(source: Optional[str], local_files_only: bool = True):
+    if not source or source == "bytes":
+        return ByteTokenizer()
+    from transformers import AutoTokenizer
+    return AutoTokenizer.from_pretrained(str(source), local_files_only=bool(local_files_only))
+
+
+class EchoBackend:
+    """Deterministic fake LLM: a short text derived from a hash of the prompt (tests, mock lanes)."""
+
+    def __init__(self, tokenizer=None, fail: bool = False):
+        self.tokenizer = tokenizer or ByteTokenizer()
+        self.fail = fail
+        self.calls: List[Dict] = []
+
+    def generate(self, prompt_text: str, max_new_tokens: int = 64, timeout_s: float = 180.0) -> str:
+        self.calls.append({"prompt": prompt_text, "max_new_tokens": max_new_tokens})
+        if self.fail:
+            raise RuntimeError("echo backend configured to fail")
+        h = hashlib.sha256(prompt_text.encode()).hexdigest()[:16]
+        return f"answer-{h}"[: max(1, max_new_tokens * 4)]
+
+    def is_running(self) -> bool:
+        return True
+
+    def stop(self) -> None:
+        pass
+
+    def metrics(self) -> Dict:
+        return {"calls": len(self.calls)}
+
+
+class EngineBackend:
+    """The B200 engine with a continuous-batching scheduler, on one GPU (TP=1) or as rank 0 of a TP group."""
+
+    def __init__(self, model_source: str, tokenizer_source: Optional[str] = None, device: str = "cuda:0",
+                 max_seq_len: int = 8192, max_batch: int = 64, prefill_chunk: int = 4096,
+                 kv_fraction: float = 0.85, max_prompt_tokens: int = 2048, local_files_only: bool = True,
+                 seed: int = 0, comm=None, rank: int = 0, world: int = 1, engine=None):
+        import torch
+        from ..config import EngineConfig, get_preset
+        from ..models.llama import LlamaW8
+        from ..runtime.engine import InferenceEngine
+        from ..runtime.kv_cache import PagedKVPool
+        from ..runtime.scheduler import Scheduler
+        self.tokenizer = load_tokenizer(tokenizer_source, local_files_only)
+        self.max_prompt_tokens = int(max_prompt_tokens)
+        if engine is None:
+            dev = torch.device(device)
+            if str(model_source).startswith("synthetic:"):
+                cfg = get_preset(model_source.split(":", 1)[1])
+                model = LlamaW8.synthesize(cfg, rank=rank, world=world, device=dev, seed=seed, comm=comm,
+                                           max_pos=max_seq_len + 16)
+            else:
+                from ..formats.dsi8 import read_dsi8
+                cfg, w = read_dsi8(model_source)
+                model = LlamaW8.from_weights(cfg, w, rank=rank, world=world, device=dev, comm=comm,
+                                             max_pos=max_seq_len + 16)
+            free, _ = torch.cuda.mem_get_info(dev)
+            nb = PagedKVPool.blocks_for_budget(int(free * kv_fraction), cfg.layers, model.plan.local_kv_heads,
+                                               cfg.head_dim)
+            ecfg = EngineConfig(tp=world, max_seq_len=max_seq_len, max_batch=max_batch, prefill_chunk=prefill_chunk)
+            engine = InferenceEngine(model, ecfg, num_blocks=nb)
+        self.engine = engine
+        self.scheduler = Scheduler(engine).start()
+
+    def encode_prompt(self, text: str) -> List[int]:
+        ids = self.tokenizer(text, add_special_tokens=True)["input_ids"]
+        if len(ids) > self.max_prompt_tokens:          # left-truncate (reference: deepseek_native.py:345-346)
+            ids = ids[-self.max_prompt_tokens:]
+        return ids
+
+    def generate_ids(self, ids: List[int], max_new_tokens: int, timeout_s: float = 180.0) -> List[int]:
+        return self.scheduler.generate(ids, max_new_tokens, timeout=timeout_s)
+
+    def generate(self, prompt_text: str, max_new_tokens: int = 256, timeout_s: float = 180.0) -> str:
+        out = self.generate_ids(self.encode_prompt(prompt_text), max_new_tokens, timeout_s)
+        return self.tokenizer.decode(out, skip_special_tokens=True)
+
+    def is_running(self) -> bool:
+        return self.scheduler.alive()
+
+    def stop(self) -> None:
+        self.scheduler.stop()
+
+    def metrics(self) -> Dict:
+        return self.scheduler.metrics()

@@ -1,0 +1,421 @@
+"""Multi-lane router: lane selection, failover, OpenAI-compatible endpoints with SSE keep-alive.
+
+Semantics of the reference router (``hrm_flash/router.py:154-575``), retargeted to an 8xB200 box:
+
+* logical lanes keep their public names: ``solo_22gb`` (the max-model lane, e.g. TP=8), ``nvlink_pair`` (the
+  balanced lane, e.g. TP=4) and ``solo_3080`` (the fast lane, e.g. TP=2/1); aliases: quality/best -> solo_22gb,
+  balanced/default/pair -> nvlink_pair, fast/latency -> solo_3080;
+* primary lane: ``prefer_backend`` > ``route_hint`` > collapsed max-model mode (solo_22gb and nvlink_pair share an
+  endpoint -> nvlink_pair) > size classes (prompt <= 256 tokens and max_new <= 192 -> fast; <= 1200 / <= 384 ->
+  balanced; else max-model);
+* per-lane max_new caps (192 / 384 / 768), failover order per primary, 503 ``{error, primary, attempted,
+  backend_errors}`` when every candidate fails; prompts truncated to the last ``max_prompt_chars`` (3000) chars;
+* OpenAI endpoints default to ``mode = deepseek_only``; streaming sends ``: keepalive`` every 5 s until the result,
+  then one chunk, a stop chunk with usage, and ``[DONE]``.
+"""
+import argparse
+import asyncio
+import json
+import os
+import sys
+import time
+import urllib.error
+import urllib.request
+from dataclasses import dataclass
+from typing import Any, Dict, List, Optional, Tuple
+
+from .prompt_builder import SUPPORTED_MODES, normalize_mode
+
+LANES = ("solo_22gb", "nvlink_pair", "solo_3080")
+ALIASES = {
+    "22gb": "solo_22gb", "solo22": "solo_22gb", "solo_22": "solo_22gb", "solo_22gb": "solo_22gb",
+    "quality": "solo_22gb", "best": "solo_22gb", "max": "solo_22gb", "tp8": "solo_22gb",
+    "pair": "nvlink_pair", "nvlink": "nvlink_pair", "nvlink_pair": "nvlink_pair", "balanced": "nvlink_pair",
+    "default": "nvlink_pair", "tp4": "nvlink_pair",
+    "3080": "solo_3080", "solo_3080": "solo_3080", "fast": "solo_3080", "low_latency": "solo_3080",
+    "latency": "solo_3080", "tp2": "solo_3080",
+}
+FAILOVER = {
+    "solo_3080": ["solo_3080", "nvlink_pair", "solo_22gb"],
+    "nvlink_pair": ["nvlink_pair", "solo_22gb", "solo_3080"],
+    "solo_22gb": ["solo_22gb", "nvlink_pair", "solo_3080"],
+}
+USER_MARKERS = ["\nuser:", "\nUser:", "\nUSER:", "<｜User｜>", "<|User|>", "### User:", "\nHuman:"]
+DEFAULT_MODEL_ID = "deepseek-r1-distill-llama-70b-b200"
+
+
+@dataclass(frozen=True)
+class Backend:
+    name: str
+    base_url: str
+
+
+class RouterState:
+    def __init__(self):
+        self.backends: Dict[str, Backend] = {}
+        self.short_prompt_tokens = 256
+        self.medium_prompt_tokens = 1200
+        self.short_max_new_tokens = 192
+        self.medium_max_new_tokens = 384
+        self.long_max_new_tokens = 768
+        self.request_timeout_s = 180.0
+        self.health_timeout_s = 1.5
+        self.chars_per_token = 4.0
+        self.max_concurrent = 8
+        self.sem: Optional[asyncio.Semaphore] = None
+        self.tokenizer: Any = None
+        self.tokenizer_name: Optional[str] = None
+        self.default_mode = "mixed"
+        self.max_prompt_chars = 3000
+        self.keepalive_s = 5.0
+        self.model_id = DEFAULT_MODEL_ID
+        self.post = http_json_post    # injectable transport (tests)
+        self.get = http_json_get
+
+
+def http_json_get(url: str, timeout_s: float) -> Tuple[Dict[str, Any], int]:
+    t0 = time.perf_counter()
+    with urllib.request.urlopen(urllib.request.Request(url, method="GET"), timeout=timeout_s) as r:
+        raw = r.read()
+    ms = int((time.perf_counter() - t0) * 1000)
+    obj = json.loads(raw.decode("utf-8"))
+    if not isinstance(obj, dict):
+        raise RuntimeError(f"invalid JSON shape from {url}")
+    return obj, ms
+
+
+def http_json_post(url: str, payload: Dict[str, Any], timeout_s: float) -> Tuple[Dict[str, Any], int]:
+    req = urllib.request.Request(url, data=json.dumps(payload).encode("utf-8"), method="POST",
+                                 headers={"Content-Type": "application/json"})
+    t0 = time.perf_counter()
+    try:
+        with urllib.request.urlopen(req, timeout=timeout_s) as r:
+            raw = r.read()
+    except urllib.error.HTTPError as e:
+        try:
+            detail = e.read().decode("utf-8", errors="replace")
+        except Exception:
+            detail = str(e)
+        raise RuntimeError(f"HTTP {e.code} from backend {url}: {detail}") from e
+    except Exception as e:
+        raise RuntimeError(f"request to backend failed ({url}): {e}") from e
+    ms = int((time.perf_counter() - t0) * 1000)
+    obj = json.loads(raw.decode("utf-8"))
+    if not isinstance(obj, dict):
+        raise RuntimeError(f"invalid JSON shape from backend {url}")
+    return obj, ms
+
+
+def normalize_backend_name(v: Optional[str]) -> Optional[str]:
+    if not v:
+        return None
+    s = v.strip().lower()
+    return ALIASES.get(s, s)
+
+
+def estimate_prompt_tokens(st: RouterState, prompt: str) -> Tuple[int, str]:
+    if st.tokenizer is not None:
+        try:
+            ids = st.tokenizer(prompt, add_special_tokens=True).get("input_ids", [])
+            return max(1, len(ids)), "tokenizer"
+        except Exception:
+            pass
+    return max(1, int(len(prompt) / max(1e-6, st.chars_per_token) + 0.999)), "chars"
+
+
+def collapsed_max_model_mode(st: RouterState) -> bool:
+    s, p, f = (st.backends.get(n) for n in LANES)
+    return s is not None and p is not None and f is not None and s.base_url == p.base_url
+
+
+def primary_backend(st: RouterState, prompt_tokens: int, max_new: int, route_hint: Optional[str],
+                    prefer_backend: Optional[str]) -> str:
+    pref = normalize_backend_name(prefer_backend)
+    if pref in st.backends:
+        return pref
+    hint = normalize_backend_name(route_hint)
+    if hint in st.backends:
+        return hint
+    if collapsed_max_model_mode(st):
+        return "nvlink_pair"
+    if prompt_tokens <= st.short_prompt_tokens and max_new <= st.short_max_new_tokens:
+        return "solo_3080"
+    if prompt_tokens <= st.medium_prompt_tokens and max_new <= st.medium_max_new_tokens:
+        return "nvlink_pair"
+    return "solo_22gb"
+
+
+def max_new_limit(st: RouterState, lane: str) -> int:
+    return {"solo_3080": st.short_max_new_tokens, "nvlink_pair": st.medium_max_new_tokens}.get(
+        lane, st.long_max_new_tokens)
+
+
+def candidate_order(st: RouterState, primary: str, allow_failover: bool) -> List[str]:
+    if not allow_failover:
+        return [primary]
+    order = ["nvlink_pair", "solo_22gb"] if collapsed_max_model_mode(st) else \
+        FAILOVER.get(primary, [primary, "nvlink_pair", "solo_22gb", "solo_3080"])
+    out: List[str] = []
+    for n in order:
+        if n in st.backends and n not in out:
+            out.append(n)
+    return out
+
+
+def resolve_show_sources(show: Optional[bool], mode: str) -> bool:
+    if mode == "deepseek_only":
+        return False
+    return mode == "retrieval" if show is None else bool(show)
+
+
+def last_user_prompt(prompt: str) -> str:
+    text = str(prompt or "").strip()
+    best_at, best = -1, ""
+    for m in USER_MARKERS:
+        at = text.rfind(m)
+        if at > best_at:
+            best_at, best = at, m
+    return text[best_at + len(best):].strip() if best_at >= 0 else text
+
+
+def chat_messages_to_prompt(messages: Any) -> str:
+    if not isinstance(messages, list):
+        return ""
+    parts = []
+    for msg in messages:
+        if not isinstance(msg, dict):
+            continue
+        c = msg.get("content")
+        text = " ".join(str(p.get("text") or "") for p in c if isinstance(p, dict)) if isinstance(c, list) \
+            else str(c or "")
+        if text.strip() and str(msg.get("role") or "user").lower() == "user":
+            parts.append(text.strip())
+    return "\n".join(parts).strip()
+
+
+def create_app(st: RouterState):
+    from fastapi import FastAPI, HTTPException, Request
+    from fastapi.responses import JSONResponse, StreamingResponse
+    from pydantic import BaseModel
+
+    app = FastAPI(title="hrm-flash-b200-router", version="0.1.0")
+
+    class GenerateReq(BaseModel):
+        prompt: str
+        max_new_tokens: Optional[int] = None
+        mode: Optional[str] = None
+        show_sources: Optional[bool] = None
+        route_hint: Optional[str] = None
+        prefer_backend: Optional[str] = None
+        allow_failover: bool = True
+
+    def truncate(prompt: str) -> str:
+        t = str(prompt or "").strip()
+        return t if len(t) <= st.max_prompt_chars else t[-st.max_prompt_chars:]
+
+    async def run_generate(req: GenerateReq) -> Dict[str, Any]:
+        if not req.prompt or not req.prompt.strip():
+            raise HTTPException(status_code=400, detail="prompt required")
+        prompt = truncate(req.prompt)
+        try:
+            mode = normalize_mode(req.mode if req.mode is not None else st.default_mode)
+        except ValueError as e:
+            raise HTTPException(status_code=400, detail=str(e))
+        if st.sem is None:
+            st.sem = asyncio.Semaphore(st.max_concurrent)
+        async with st.sem:
+            req_new = max(1, min(4096, int(req.max_new_tokens) if req.max_new_tokens is not None else 256))
+            ptoks, estimator = estimate_prompt_tokens(st, prompt)
+            if mode == "deepseek_only":
+                print("[router] mode=deepseek_only HRM disabled (no retrieval)", file=sys.stderr, flush=True)
+            primary = primary_backend(st, ptoks, req_new, req.route_hint, req.prefer_backend)
+            attempted, errors = [], []
+            show = resolve_show_sources(req.show_sources, mode)
+            for lane in candidate_order(st, primary, bool(req.allow_failover)):
+                be = st.backends[lane]
+                lane_new = min(req_new, max_new_limit(st, lane))
+                attempted.append(lane)
+                try:
+                    body, ms = await asyncio.to_thread(st.post, be.base_url + "/v1/generate",
+                                                       {"prompt": prompt, "max_new_tokens": lane_new, "mode": mode,
+                                                        "show_sources": show}, st.request_timeout_s)
+                    if not bool(body.get("ok", True)):
+                        raise RuntimeError(str(body.get("detail") or body.get("error") or "backend returned ok=false"))
+                    out = dict(body)
+                    out["route"] = {"primary": primary, "selected": lane, "attempted": attempted,
+                                    "estimator": estimator, "prompt_tokens": ptoks,
+                                    "requested_max_new_tokens": req_new, "backend_max_new_tokens": lane_new,
+                                    "latency_ms": ms}
+                    return out
+                except Exception as e:
+                    errors.append(f"{lane}: {e}")
+            raise HTTPException(status_code=503, detail={"error": "all backends failed", "primary": primary,
+                                                         "attempted": attempted, "backend_errors": errors})
+
+    def usage(prompt: str, text: str) -> Dict[str, int]:
+        p, _ = estimate_prompt_tokens(st, prompt)
+        c, _ = estimate_prompt_tokens(st, text)
+        return {"prompt_tokens": p, "completion_tokens": c, "total_tokens": p + c}
+
+    async def stream(task: "asyncio.Task", model: str, prompt: str, chat: bool):
+        while not task.done():
+            yield ": keepalive\n\n"
+            try:
+                await asyncio.wait_for(asyncio.shield(task), timeout=st.keepalive_s)
+            except asyncio.TimeoutError:
+                pass
+            except Exception:
+                break
+        try:
+            result = await task
+        except HTTPException as e:
+            yield f"data: {json.dumps({'error': e.detail})}\n\n"
+            yield "data: [DONE]\n\n"
+            return
+        text = str(result.get("text") or "")
+        now = int(time.time())
+        if chat:
+            cid = f"chatcmpl-{int(time.time() * 1000)}"
+            first = {"id": cid, "object": "chat.completion.chunk", "created": now, "model": model,
+                     "choices": [{"index": 0, "delta": {"content": text}, "finish_reason": None}]}
+            done = {"id": cid, "object": "chat.completion.chunk", "created": now, "model": model,
+                    "choices": [{"index": 0, "delta": {}, "finish_reason": "stop"}], "usage": usage(prompt, text)}
+        else:
+            cid = f"cmpl-{int(time.time() * 1000)}"
+            first = {"id": cid, "object": "text_completion", "created": now, "model": model,
+                     "choices": [{"index": 0, "text": text, "finish_reason": None}]}
+            done = {"id": cid, "object": "text_completion", "created": now, "model": model,
+                    "choices": [{"index": 0, "text": "", "finish_reason": "stop"}], "usage": usage(prompt, text)}
+        yield f"data: {json.dumps(first)}\n\n"
+        yield f"data: {json.dumps(done)}\n\n"
+        yield "data: [DONE]\n\n"
+
+    def check(lane: str) -> Dict[str, Any]:
+        be = st.backends[lane]
+        try:
+            payload, ms = st.get(be.base_url + "/v1/health", st.health_timeout_s)
+            return {"ok": bool(payload.get("ok", False)), "latency_ms": ms, "url": be.base_url}
+        except Exception as e:
+            return {"ok": False, "error": str(e), "url": be.base_url}
+
+    @app.get("/v1/health")
+    async def health():
+        names = [n for n in LANES if n in st.backends]
+        checks = await asyncio.gather(*[asyncio.to_thread(check, n) for n in names])
+        bh = dict(zip(names, checks))
+        return {"ok": any(c["ok"] for c in checks),
+                "router": {"tokenizer": st.tokenizer_name, "collapsed_max_model_mode": collapsed_max_model_mode(st),
+                           "request_timeout_s": st.request_timeout_s, "max_concurrent": st.max_concurrent,
+                           "max_prompt_chars": st.max_prompt_chars, "default_mode": st.default_mode,
+                           "supported_modes": sorted(SUPPORTED_MODES),
+                           "thresholds": {"short_prompt_tokens": st.short_prompt_tokens,
+                                          "medium_prompt_tokens": st.medium_prompt_tokens,
+                                          "short_max_new_tokens": st.short_max_new_tokens,
+                                          "medium_max_new_tokens": st.medium_max_new_tokens,
+                                          "long_max_new_tokens": st.long_max_new_tokens}},
+                "backends": bh}
+
+    @app.post("/v1/generate")
+    async def generate(request: Request):
+        return JSONResponse(await run_generate(GenerateReq(**(await request.json()))))
+
+    @app.get("/v1/models")
+    async def models():
+        return {"object": "list", "data": [{"id": st.model_id, "object": "model", "created": 0,
+                                            "owned_by": "hrm-flashrenderer-b200"}]}
+
+    async def openai(body: Dict[str, Any], prompt: str, chat: bool):
+        prompt = truncate(last_user_prompt(prompt))
+        model = str(body.get("model") or st.model_id)
+        req = GenerateReq(prompt=prompt, mode=str(body.get("mode") or "deepseek_only"),
+                          max_new_tokens=body.get("max_tokens") or body.get("max_completion_tokens")
+                          or body.get("max_new_tokens"),
+                          route_hint=body.get("route_hint"), prefer_backend=body.get("prefer_backend"))
+        if bool(body.get("stream")):
+            task = asyncio.create_task(run_generate(req))
+            return StreamingResponse(stream(task, model, prompt, chat), media_type="text/event-stream")
+        result = await run_generate(req)
+        text = str(result.get("text") or "")
+        if chat:
+            return JSONResponse({"id": f"chatcmpl-{int(time.time() * 1000)}", "object": "chat.completion",
+                                 "created": int(time.time()), "model": model,
+                                 "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
+                                              "finish_reason": "stop"}], "usage": usage(prompt, text)})
+        return JSONResponse({"id": f"cmpl-{int(time.time() * 1000)}", "object": "text_completion",
+                             "created": int(time.time()), "model": model,
+                             "choices": [{"index": 0, "text": text, "finish_reason": "stop"}],
+                             "usage": usage(prompt, text)})
+
+    @app.post("/v1/completions")
+    async def completions(request: Request):
+        body = await request.json()
+        prompt = body.get("prompt", "")
+        if isinstance(prompt, list):
+            prompt = "\n".join(str(x) for x in prompt)
+        return await openai(body, str(prompt), chat=False)
+
+    @app.post("/v1/chat/completions")
+    async def chat_completions(request: Request):
+        body = await request.json()
+        return await openai(body, chat_messages_to_prompt(body.get("messages")), chat=True)
+
+    return app
+
+
+def build_arg_parser() -> argparse.ArgumentParser:
+    ap = argparse.ArgumentParser(prog="hrm-flash-router", description="Lane router for hrm-flash B200 services")
+    ap.add_argument("--host", default="0.0.0.0")
+    ap.add_argument("--port", type=int, default=8090)
+    ap.add_argument("--endpoint_solo_22gb", default="http://127.0.0.1:8081")
+    ap.add_argument("--endpoint_nvlink_pair", default="http://127.0.0.1:8082")
+    ap.add_argument("--endpoint_solo_3080", default="http://127.0.0.1:8083")
+    ap.add_argument("--short_prompt_tokens", type=int, default=256)
+    ap.add_argument("--medium_prompt_tokens", type=int, default=1200)
+    ap.add_argument("--short_max_new_tokens", type=int, default=192)
+    ap.add_argument("--medium_max_new_tokens", type=int, default=384)
+    ap.add_argument("--long_max_new_tokens", type=int, default=768)
+    ap.add_argument("--request_timeout_s", type=float, default=180.0)
+    ap.add_argument("--health_timeout_s", type=float, default=1.5)
+    ap.add_argument("--max_concurrent", type=int, default=8)
+    ap.add_argument("--tokenizer_model", default=None)
+    ap.add_argument("--chars_per_token", type=float, default=4.0)
+    ap.add_argument("--local_files_only", action="store_true")
+    ap.add_argument("--disable_tokenizer", action="store_true")
+    ap.add_argument("--default_mode", choices=["retrieval", "mixed", "deepseek_only"], default="mixed")
+    ap.add_argument("--max_prompt_chars", type=int, default=int(os.environ.get("ROUTER_MAX_PROMPT_CHARS", "3000")))
+    return ap
+
+
+def state_from_args(args) -> RouterState:
+    st = RouterState()
+    st.backends = {n: Backend(n, str(getattr(args, f"endpoint_{n}")).strip().rstrip("/")) for n in LANES}
+    st.short_prompt_tokens = max(16, int(args.short_prompt_tokens))
+    st.medium_prompt_tokens = max(st.short_prompt_tokens + 1, int(args.medium_prompt_tokens))
+    st.short_max_new_tokens = max(16, int(args.short_max_new_tokens))
+    st.medium_max_new_tokens = max(st.short_max_new_tokens, int(args.medium_max_new_tokens))
+    st.long_max_new_tokens = max(st.medium_max_new_tokens, int(args.long_max_new_tokens))
+    st.request_timeout_s = max(1.0, float(args.request_timeout_s))
+    st.health_timeout_s = max(0.2, float(args.health_timeout_s))
+    st.chars_per_token = max(1.0, float(args.chars_per_token))
+    st.max_concurrent = max(1, int(args.max_concurrent))
+    st.default_mode = normalize_mode(args.default_mode)
+    st.max_prompt_chars = max(1024, int(args.max_prompt_chars))
+    if not args.disable_tokenizer and args.tokenizer_model:
+        try:
+            from transformers import AutoTokenizer
+            st.tokenizer = AutoTokenizer.from_pretrained(args.tokenizer_model, local_files_only=args.local_files_only)
+            st.tokenizer_name = str(args.tokenizer_model)
+        except Exception as e:
+            print(f"[router] tokenizer unavailable, using char-estimate: {e}", file=sys.stderr, flush=True)
+    return st
+
+
+def main(argv=None):
+    args = build_arg_parser().parse_args(argv)
+    st = state_from_args(args)
+    import uvicorn
+    uvicorn.run(create_app(st), host=args.host, port=args.port, log_level="info")
+
+
+if __name__ == "__main__":
+    main()

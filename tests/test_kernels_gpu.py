@@ -166,9 +166,10 @@ def test_decode_attention_tc_deterministic():
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("D,Hq,Hk", [(128, 8, 2), (64, 4, 4)])
-@pytest.mark.parametrize("chunks", [[(0, 100)], [(0, 37), (50, 64), (7, 1)]])
-def test_paged_prefill_attention(D, Hq, Hk, chunks):
+@pytest.mark.parametrize("D,Hq,Hk", [(128, 8, 2), (64, 4, 4), (128, 16, 2), (128, 10, 2), (128, 4, 4)])
+@pytest.mark.parametrize("chunks", [[(0, 100)], [(0, 37), (50, 64), (7, 1)], [(0, 300)], [(200, 129), (0, 17)]])
+@pytest.mark.parametrize("tc", [True, False])
+def test_paged_prefill_attention(D, Hq, Hk, chunks, tc):
     """chunks: (q_start, q_len) per sequence; context = q_start + q_len."""
     lens = [a + b for a, b in chunks]
     kc, vc, tab = _paged(len(chunks), lens, Hk, D, seed=3)
@@ -180,7 +181,8 @@ def test_paged_prefill_attention(D, Hq, Hk, chunks):
     mq = max(b for _, b in chunks)
     ref = ops.paged_prefill_attention(q, kc, vc, tab, cu, qs, cl, mq)
     out = ops.paged_prefill_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), tab.to(DEV), cu.to(DEV), qs.to(DEV),
-                                      cl.to(DEV), mq)
+                                      cl.to(DEV), mq, allow_tc=tc)
+    ops.check_status()
     assert (out.float().cpu() - ref.float()).abs().max().item() < 2e-2
 
 

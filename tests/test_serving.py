@@ -1,0 +1,186 @@
+"""Prompt modes, the lane service and the router (CPU; echo backend, real HRM core for retrieval)."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+from hrm_flashrenderer_b200.serving import prompt_builder as pb
+from hrm_flashrenderer_b200.serving.backend import EchoBackend, ByteTokenizer
+from hrm_flashrenderer_b200.serving.serve import ServiceState, create_app, build_prompt
+from hrm_flashrenderer_b200.serving import router as rt
+
+sys.path.insert(0, os.path.dirname(__file__))
+from _http import LiveServer, post, get  # noqa: E402
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HRM = os.path.join(ROOT, "hrm_core", "build", "hrm")
+
+
+# ---------------------------------------------------------------------------------------------- prompt modes
+def test_mode_aliases_and_default():
+    assert pb.normalize_mode(None) == "mixed"
+    for a, m in [("silent", "mixed"), ("default", "mixed"), ("deepseek", "deepseek_only"), ("full", "deepseek_only"),
+                 ("llm_only", "deepseek_only"), (" Retrieval ", "retrieval")]:
+        assert pb.normalize_mode(a) == m
+    with pytest.raises(ValueError):
+        pb.normalize_mode("nonsense")
+
+
+def test_templates():
+    srcs = [pb.Source("0001#s0002", "alpha"), pb.Source("0003#s0004", "beta")]
+    mixed = pb.build_prompt_for_mode("Q?", srcs, "mixed")
+    assert mixed.startswith("[SYSTEM]\n" + pb.MIXED_SYSTEM_PROMPT + "\n\n[BACKGROUND_KNOWLEDGE]\n<kb_01> alpha\n<kb_02> beta")
+    assert mixed.endswith("[USER]\nQ?\n\n[ASSISTANT]\n")
+    assert "0001#s0002" not in mixed                       # ids hidden in mixed mode
+    ret = pb.build_prompt_for_mode("Q?", srcs, "retrieval")
+    assert "[SOURCES]\n[0001#s0002] alpha\n[0003#s0004] beta" in ret
+    assert pb.build_prompt_for_mode("Q?", srcs, "deepseek_only") == "Q?"
+    assert pb.SILENT_SYSTEM_PROMPT == pb.MIXED_SYSTEM_PROMPT
+    assert "Never mention \"sources\"" in pb.MIXED_SYSTEM_PROMPT
+
+
+def test_build_sources_caps():
+    raw = {"chosen": [{"sid": f"s{i}", "txt": "x" * 1300} for i in range(20)] + [{"sid": "", "txt": "y"}]}
+    s = pb.build_sources(raw)
+    assert len(s) == 16 and s[0].txt.endswith(" …") and len(s[0].txt) == 1202
+
+
+def test_token_budget_fit():
+    tok = ByteTokenizer()
+    srcs = [pb.Source(f"s{i}", "w" * 200) for i in range(5)]
+    q, s = pb.fit_prompt_to_token_budget("question?", srcs, tok, 900, mode="mixed")
+    assert len(tok(pb.build_prompt_for_mode(q, s, "mixed"), add_special_tokens=False)["input_ids"]) <= 900
+    assert 1 <= len(s) < 5
+    q2, s2 = pb.fit_prompt_to_token_budget("question?", srcs, tok, 5, mode="mixed")
+    assert (q2, s2) == ("", [])
+
+
+# ---------------------------------------------------------------------------------------------- lane service
+@pytest.fixture(scope="module")
+def hrm_model(tmp_path_factory):
+    subprocess.run(["make", "-C", os.path.join(ROOT, "hrm_core"), "-j4", "all"], check=True, capture_output=True)
+    d = tmp_path_factory.mktemp("kb")
+    lines = ["The silver bridge is guarded by the night watch.", "Merchants promised the king bread and wine.",
+             "Winter makes the tower dark and cold.", "The river stone shines under the golden light."] * 3
+    (d / "kb.txt").write_text("\n".join(lines) + "\n")
+    subprocess.run([HRM, "prep", "--input", str(d / "kb.txt"), "--out", str(d / "p.jsonl"), "--cluster-size", "4"],
+                   check=True, capture_output=True)
+    subprocess.run([HRM, "build", "--payloads", str(d / "p.jsonl"), "--outdir", str(d / "m")], check=True,
+                   capture_output=True)
+    return d / "m"
+
+
+def _state(hrm_model, backend=None, **kw):
+    return ServiceState(backend=backend or EchoBackend(), hrm_model=hrm_model, max_seq_len=4096, max_new_tokens=64,
+                        max_concurrent=4, **kw)
+
+
+def test_deepseek_only_never_calls_hrm(hrm_model, monkeypatch):
+    import hrm_flashrenderer_b200.serving.serve as serve
+    monkeypatch.setattr(serve, "run_hrm_query", lambda **k: (_ for _ in ()).throw(AssertionError("HRM called")))
+    st = _state(hrm_model)
+    text, srcs, mode, active = build_prompt(st, "who guards the bridge", "deepseek")
+    assert (text, srcs, mode, active) == ("who guards the bridge", [], "deepseek_only", False)
+    assert st.hrm_query_calls_total == 0
+
+
+def test_generate_modes_over_http(hrm_model):
+    be = EchoBackend()
+    st = _state(hrm_model, be)
+    with LiveServer(create_app(st)) as srv:
+        code, body = post(srv.url + "/v1/generate", {"prompt": "who guards the silver bridge", "mode": "retrieval"})
+        r = json.loads(body)
+        assert code == 200 and r["ok"] and r["mode"] == "retrieval" and r["hrm_active"] is True
+        assert r["source_count"] > 0 and "sources" in r and r["audit"]["prompt_template"] == "retrieval_explicit"
+        assert "[SOURCES]" in be.calls[-1]["prompt"]
+        code, body = post(srv.url + "/v1/generate", {"prompt": "who guards the silver bridge"})
+        r = json.loads(body)
+        assert r["mode"] == "mixed" and "sources" not in r and r["audit"]["prompt_template"] == "mixed_silent"
+        assert "<kb_01>" in be.calls[-1]["prompt"] and "#s" not in be.calls[-1]["prompt"]
+        code, body = post(srv.url + "/v1/generate", {"prompt": "hello", "mode": "deepseek_only", "show_sources": True})
+        r = json.loads(body)
+        assert r["hrm_active"] is False and r["source_count"] == 0 and "sources" not in r
+        assert be.calls[-1]["prompt"] == "hello"
+        code, body = post(srv.url + "/v1/generate", {"prompt": "zzqx", "mode": "mixed"})
+        r = json.loads(body)
+        if r["source_count"] == 0:
+            assert r["text"] == "I don't know."
+        code, _ = post(srv.url + "/v1/generate", {"prompt": "x", "mode": "bogus"})
+        assert code == 400
+        code, h = get(srv.url + "/v1/health")
+        assert h["ok"] and h["audit"]["requests_total"] >= 4
+        assert h["audit"]["mode_counts"]["retrieval"] == 1 and h["audit"]["hrm_query_calls_by_mode"]["deepseek_only"] == 0
+
+
+def test_deterministic_repeat(hrm_model):
+    st = _state(hrm_model)
+    with LiveServer(create_app(st)) as srv:
+        outs = [post(srv.url + "/v1/generate", {"prompt": "what did the merchants promise", "mode": "mixed"})[1]
+                for _ in range(3)]
+    assert len(set(outs)) == 1
+
+
+def test_missing_tokenizer_means_no_prompt(hrm_model):
+    be = EchoBackend()
+    be.tokenizer = None
+    st = _state(hrm_model, be)
+    text, srcs, mode, active = build_prompt(st, "who guards the silver bridge", "mixed")
+    assert text == "" and srcs == [] and active is True
+
+
+# ---------------------------------------------------------------------------------------------- router
+def _router(post_fn, endpoints=None):
+    st = rt.RouterState()
+    endpoints = endpoints or {"solo_22gb": "http://a", "nvlink_pair": "http://b", "solo_3080": "http://c"}
+    st.backends = {n: rt.Backend(n, u) for n, u in endpoints.items()}
+    st.post = post_fn
+    st.get = lambda url, t: ({"ok": not url.startswith("http://c")}, 1)
+    st.keepalive_s = 0.05
+    return st
+
+
+def test_router_primary_selection():
+    st = _router(None)
+    assert rt.primary_backend(st, 100, 100, None, None) == "solo_3080"
+    assert rt.primary_backend(st, 1000, 300, None, None) == "nvlink_pair"
+    assert rt.primary_backend(st, 5000, 100, None, None) == "solo_22gb"
+    assert rt.primary_backend(st, 100, 100, "quality", None) == "solo_22gb"
+    assert rt.primary_backend(st, 100, 100, "quality", "fast") == "solo_3080"
+    collapsed = _router(None, {"solo_22gb": "http://a", "nvlink_pair": "http://a", "solo_3080": "http://c"})
+    assert rt.primary_backend(collapsed, 10, 10, None, None) == "nvlink_pair"
+    assert rt.candidate_order(collapsed, "nvlink_pair", True) == ["nvlink_pair", "solo_22gb"]
+    assert rt.candidate_order(st, "solo_3080", True) == ["solo_3080", "nvlink_pair", "solo_22gb"]
+    assert rt.resolve_show_sources(True, "deepseek_only") is False
+    assert rt.resolve_show_sources(None, "retrieval") is True
+
+
+def test_router_failover_and_503():
+    calls = []
+
+    def fake_post(url, payload, timeout):
+        calls.append((url, payload))
+        if url.startswith("http://c"):
+            raise RuntimeError("lane down")
+        return {"ok": True, "text": "t", "mode": payload["mode"]}, 3
+
+    st = _router(fake_post)
+    with LiveServer(rt.create_app(st)) as srv:
+        code, body = post(srv.url + "/v1/generate", {"prompt": "short", "max_new_tokens": 50})
+        r = json.loads(body)
+        assert code == 200 and r["route"]["primary"] == "solo_3080" and r["route"]["selected"] == "nvlink_pair"
+        assert r["route"]["attempted"] == ["solo_3080", "nvlink_pair"] and r["route"]["backend_max_new_tokens"] == 50
+        code, body = post(srv.url + "/v1/generate", {"prompt": "short", "max_new_tokens": 50, "allow_failover": False})
+        assert code == 503 and json.loads(body)["detail"]["error"] == "all backends failed"
+        code, h = get(srv.url + "/v1/health")
+        assert h["ok"] and h["backends"]["solo_3080"]["ok"] is False
+        code, m = get(srv.url + "/v1/models")
+        assert m["object"] == "list"
+        code, body = post(srv.url + "/v1/chat/completions",
+                          {"messages": [{"role": "system", "content": "s"}, {"role": "user", "content": "hi"}]})
+        r = json.loads(body)
+        assert r["object"] == "chat.completion" and r["choices"][0]["message"]["content"] == "t"
+        assert calls[-1][1]["mode"] == "deepseek_only" and calls[-1][1]["prompt"] == "hi"
+        code, body = post(srv.url + "/v1/completions", {"prompt": "x", "stream": True})
+        assert code == 200 and body.rstrip().endswith("data: [DONE]") and '"text_completion"' in body
