@@ -76,6 +76,11 @@ def _prompts(batch, ctx, vocab, seed=1):
     return [torch.randint(0, vocab, (ctx,), generator=g).tolist() for _ in range(batch)]
 
 
+def _log(rank, msg):
+    if rank == 0:
+        print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def _emit(rank, rec):
     if rank == 0:
         print(json.dumps(rec), flush=True)
@@ -101,6 +106,7 @@ def run_ours(a):
                                max_pos=a.ctx + a.steps + a.warmup + 256)
     torch.cuda.synchronize()
     t_synth = time.time() - t0
+    _log(rank, f"synthesized {cfg.name} shard in {t_synth:.1f}s ({model.weight_bytes() / 1e9:.1f} GB int8)")
     total_len = a.ctx + a.steps + a.warmup + 2 * 16 + (a.steps + 8 if not a.no_e2e else 0)
     ecfg = EngineConfig(tp=world, max_seq_len=total_len + 16, max_batch=a.batch, prefill_chunk=4096,
                         graph_batch_buckets=(a.batch,))
@@ -119,13 +125,19 @@ def run_ours(a):
         e.record()
         e.synchronize()
         ttft_ms.append(ev0.elapsed_time(e))
+        _log(rank, f"prefilled seq {sid}: first token at {ttft_ms[-1]:.0f} ms")
+    ops.check_status(dev)
     ttft_p50 = _max_over_ranks(statistics.median(ttft_ms), world)
 
     # ---- decode (device-timed; one CUDA graph replay per step)
     g = eng.load_decode_batch(sids, first, reserve=a.warmup + a.steps + 8)
     eng.capture(g.bucket)
+    _log(rank, "decode graph captured")
     for _ in range(a.warmup):
         eng.decode_step(g)
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    _log(rank, "warm-up done")
     _barrier(world)
     sampler = ClockSampler(visible_gpu_indices(world)).start() if rank == 0 else None
     s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -68,10 +68,23 @@ std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K, int64_t force
 }
 
 // out = x @ (w * scale)^T (+ bias): out dtype f16 or f32 (preallocated [M, >=N] row-major).
+void set_in_norm(hrm::GemmArgs& a, const c10::optional<at::Tensor>& in_ssq, double inv_h, double eps) {
+  if (in_ssq.has_value() && in_ssq->defined()) {
+    CHECK_DTYPE((*in_ssq), at::kFloat); CHECK_CONTIG((*in_ssq));
+    TORCH_CHECK(in_ssq->numel() % a.M == 0, "in_ssq must be [tiles, M]");
+    a.in_ssq = in_ssq->data_ptr<float>();
+    a.in_ssq_tiles = (int)(in_ssq->numel() / a.M);
+    a.in_inv_h = (float)inv_h;
+    a.in_eps = (float)eps;
+  }
+}
+
 void w8a16_gemm(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<at::Tensor> bias, at::Tensor out,
-                at::Tensor ws, at::Tensor counters, int64_t force_ctas) {
+                at::Tensor ws, at::Tensor counters, int64_t force_ctas, c10::optional<at::Tensor> in_ssq,
+                double inv_h, double eps) {
   c10::cuda::CUDAGuard g(x.device());
   auto a = base_args(x, w, scale, bias, ws, counters);
+  set_in_norm(a, in_ssq, inv_h, eps);
   if (a.M == 0) return;
   CHECK_CUDA(out);
   TORCH_CHECK(out.dim() == 2 && out.size(0) == a.M && out.size(1) >= a.N && out.stride(1) == 1, "bad out shape");
@@ -88,9 +101,23 @@ void w8a16_gemm(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<at::
 
 // resid += x @ (w * scale)^T  (fp32 residual stream)
 void w8a16_gemm_residual(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor resid, at::Tensor ws,
-                         at::Tensor counters, int64_t force_ctas) {
+                         at::Tensor counters, int64_t force_ctas, c10::optional<at::Tensor> gamma_next,
+                         c10::optional<at::Tensor> xg_out, c10::optional<at::Tensor> ssq_out) {
   c10::cuda::CUDAGuard g(x.device());
   auto a = base_args(x, w, scale, c10::nullopt, ws, counters);
+  if (xg_out.has_value() && xg_out->defined()) {
+    TORCH_CHECK(gamma_next.has_value() && gamma_next->defined(), "xg_out needs gamma_next");
+    CHECK_DTYPE((*xg_out), at::kHalf); CHECK_DTYPE((*gamma_next), at::kFloat);
+    TORCH_CHECK(xg_out->stride(1) == 1 && gamma_next->numel() == w.size(0), "bad xg_out / gamma_next");
+    a.xg_out = reinterpret_cast<__half*>(xg_out->data_ptr());
+    a.ldxg = (int)xg_out->stride(0);
+    a.gamma_next = gamma_next->data_ptr<float>();
+  }
+  if (ssq_out.has_value() && ssq_out->defined()) {
+    CHECK_DTYPE((*ssq_out), at::kFloat);
+    TORCH_CHECK(ssq_out->numel() >= (int64_t)((w.size(0) + 127) / 128) * x.size(0), "ssq_out too small");
+    a.ssq_out = ssq_out->data_ptr<float>();
+  }
   if (a.M == 0) return;
   CHECK_CUDA(resid); CHECK_DTYPE(resid, at::kFloat);
   TORCH_CHECK(resid.dim() == 2 && resid.size(0) == a.M && resid.size(1) == a.N && resid.stride(1) == 1,
@@ -102,12 +129,52 @@ void w8a16_gemm_residual(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tenso
   hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_RESID, a, p, cur_stream());
 }
 
+// Tensor-parallel residual GEMM fused with the all-reduce over peer memory (decode, M <= 64):
+//   resid = resid + sum_ranks(x_r @ W_r^T);  xg = resid * gamma_next;  ssq = per-tile sums of squares.
+void w8a16_gemm_residual_ar(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor resid, at::Tensor ws,
+                            at::Tensor counters, at::Tensor gamma_next, at::Tensor xg_out, at::Tensor ssq_out,
+                            at::Tensor peers, int64_t rank, int64_t world, int64_t off_partials, int64_t off_final,
+                            int64_t off_flags, int64_t tile_floats, int64_t max_tiles, int64_t epoch_ptr,
+                            at::Tensor launch_ticket) {
+  c10::cuda::CUDAGuard g(x.device());
+  auto a = base_args(x, w, scale, c10::nullopt, ws, counters);
+  if (a.M == 0) return;
+  CHECK_DTYPE(resid, at::kFloat); CHECK_DTYPE(gamma_next, at::kFloat); CHECK_DTYPE(xg_out, at::kHalf);
+  CHECK_DTYPE(ssq_out, at::kFloat); CHECK_DTYPE(peers, at::kLong); CHECK_DTYPE(launch_ticket, at::kInt);
+  TORCH_CHECK(resid.size(0) == a.M && resid.size(1) == a.N && resid.stride(1) == 1, "bad resid");
+  TORCH_CHECK(peers.numel() == world && rank < world, "bad peer table");
+  TORCH_CHECK(a.N % 128 == 0 && a.M <= 64, "fused all-reduce needs N % 128 == 0 and M <= 64");
+  TORCH_CHECK((int64_t)a.M * 128 <= tile_floats, "symmetric tile slot too small for M");
+  a.resid = resid.data_ptr<float>();
+  a.ldr = (int)resid.stride(0);
+  a.gamma_next = gamma_next.data_ptr<float>();
+  a.xg_out = reinterpret_cast<__half*>(xg_out.data_ptr());
+  a.ldxg = (int)xg_out.stride(0);
+  a.ssq_out = ssq_out.data_ptr<float>();
+  a.peers = reinterpret_cast<const long long*>(peers.data_ptr<int64_t>());
+  a.tp_rank = (int)rank;
+  a.tp_world = (int)world;
+  a.off_partials = off_partials;
+  a.off_final = off_final;
+  a.off_flags = off_flags;
+  a.ar_tile_floats = (int)tile_floats;
+  a.ar_max_tiles = (int)max_tiles;
+  a.epoch = reinterpret_cast<int*>((uintptr_t)epoch_ptr);
+  a.launch_ticket = launch_ticket.data_ptr<int>();
+  auto p = hrm::gemm_plan(a.M, a.N, a.K, 0);
+  check_ws(p, ws, counters);
+  hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_RESID_AR, a, p,
+                         cur_stream());
+}
+
 // out [M, N/2] f16 = silu(gate) * up, where w rows are interleaved per 128-row tile: 64 gate rows then the 64
 // matching up rows.
 void w8a16_gemm_swiglu(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor out, at::Tensor ws,
-                       at::Tensor counters, int64_t force_ctas) {
+                       at::Tensor counters, int64_t force_ctas, c10::optional<at::Tensor> in_ssq, double inv_h,
+                       double eps) {
   c10::cuda::CUDAGuard g(x.device());
   auto a = base_args(x, w, scale, c10::nullopt, ws, counters);
+  set_in_norm(a, in_ssq, inv_h, eps);
   if (a.M == 0) return;
   CHECK_CUDA(out); CHECK_DTYPE(out, at::kHalf);
   TORCH_CHECK(out.dim() == 2 && out.size(0) == a.M && out.size(1) == a.N / 2 && out.stride(1) == 1, "bad out");
@@ -122,9 +189,11 @@ void w8a16_gemm_swiglu(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor 
 void w8a16_gemm_qkv(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<at::Tensor> bias, int64_t q_rows,
                     int64_t kv_rows, int64_t head_dim, at::Tensor positions, at::Tensor slots, at::Tensor cos_t,
                     at::Tensor sin_t, at::Tensor q_out, at::Tensor k_cache, at::Tensor v_cache, at::Tensor ws,
-                    at::Tensor counters, int64_t force_ctas) {
+                    at::Tensor counters, int64_t force_ctas, c10::optional<at::Tensor> in_ssq, double inv_h,
+                    double eps) {
   c10::cuda::CUDAGuard g(x.device());
   auto a = base_args(x, w, scale, bias, ws, counters);
+  set_in_norm(a, in_ssq, inv_h, eps);
   if (a.M == 0) return;
   TORCH_CHECK(a.N == q_rows + 2 * kv_rows, "w rows must be q_rows + 2*kv_rows");
   CHECK_DTYPE(positions, at::kInt); CHECK_DTYPE(slots, at::kInt);
@@ -170,6 +239,23 @@ void rmsnorm(at::Tensor x, c10::optional<at::Tensor> delta, at::Tensor w, double
   }
   hrm::rmsnorm_launch(x.data_ptr<float>(), d, w.data_ptr<float>(), reinterpret_cast<__half*>(out.data_ptr()), M, H,
                       (float)eps, cur_stream());
+}
+
+void norm_prep(at::Tensor x, c10::optional<at::Tensor> delta, at::Tensor gamma, at::Tensor xg, at::Tensor ssq) {
+  c10::cuda::CUDAGuard g(x.device());
+  CHECK_DTYPE(x, at::kFloat); CHECK_CONTIG(x); CHECK_DTYPE(gamma, at::kFloat); CHECK_DTYPE(xg, at::kHalf);
+  CHECK_CONTIG(xg); CHECK_DTYPE(ssq, at::kFloat); CHECK_CONTIG(ssq);
+  const int H = (int)x.size(-1);
+  const int M = (int)(x.numel() / H);
+  TORCH_CHECK(H % 128 == 0, "hidden must be a multiple of 128");
+  TORCH_CHECK(xg.numel() == x.numel() && ssq.numel() >= (int64_t)(H / 128) * M, "shape mismatch");
+  const float* d = nullptr;
+  if (delta.has_value() && delta->defined()) {
+    CHECK_DTYPE((*delta), at::kFloat); CHECK_CONTIG((*delta));
+    d = delta->data_ptr<float>();
+  }
+  hrm::norm_prep_launch(x.data_ptr<float>(), d, gamma.data_ptr<float>(), reinterpret_cast<__half*>(xg.data_ptr()),
+                        ssq.data_ptr<float>(), M, H, cur_stream());
 }
 
 void embed_q8(at::Tensor ids, at::Tensor q, at::Tensor scale, int64_t vocab_start, at::Tensor out) {
@@ -286,12 +372,24 @@ void decode_advance(at::Tensor tokens, at::Tensor ids, at::Tensor positions, c10
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of hrm_flashrenderer_b200";
   m.def("gemm_plan", &gemm_plan_py, "split-K plan: (bn, n_tiles, m_tiles, k_tiles, splits, ws_floats, counters)");
-  m.def("w8a16_gemm", &w8a16_gemm);
-  m.def("w8a16_gemm_residual", &w8a16_gemm_residual);
-  m.def("w8a16_gemm_swiglu", &w8a16_gemm_swiglu);
-  m.def("w8a16_gemm_qkv", &w8a16_gemm_qkv);
+  m.def("w8a16_gemm", &w8a16_gemm, py::arg("x"), py::arg("w"), py::arg("scale"), py::arg("bias"), py::arg("out"),
+        py::arg("ws"), py::arg("counters"), py::arg("force_ctas") = 0, py::arg("in_ssq") = py::none(),
+        py::arg("inv_h") = 0.0, py::arg("eps") = 0.0);
+  m.def("w8a16_gemm_residual", &w8a16_gemm_residual, py::arg("x"), py::arg("w"), py::arg("scale"), py::arg("resid"),
+        py::arg("ws"), py::arg("counters"), py::arg("force_ctas") = 0, py::arg("gamma_next") = py::none(),
+        py::arg("xg_out") = py::none(), py::arg("ssq_out") = py::none());
+  m.def("w8a16_gemm_residual_ar", &w8a16_gemm_residual_ar);
+  m.def("w8a16_gemm_swiglu", &w8a16_gemm_swiglu, py::arg("x"), py::arg("w"), py::arg("scale"), py::arg("out"),
+        py::arg("ws"), py::arg("counters"), py::arg("force_ctas") = 0, py::arg("in_ssq") = py::none(),
+        py::arg("inv_h") = 0.0, py::arg("eps") = 0.0);
+  m.def("w8a16_gemm_qkv", &w8a16_gemm_qkv, py::arg("x"), py::arg("w"), py::arg("scale"), py::arg("bias"),
+        py::arg("q_rows"), py::arg("kv_rows"), py::arg("head_dim"), py::arg("positions"), py::arg("slots"),
+        py::arg("cos_t"), py::arg("sin_t"), py::arg("q_out"), py::arg("k_cache"), py::arg("v_cache"), py::arg("ws"),
+        py::arg("counters"), py::arg("force_ctas") = 0, py::arg("in_ssq") = py::none(), py::arg("inv_h") = 0.0,
+        py::arg("eps") = 0.0);
   m.def("rmsnorm", &rmsnorm);
   m.def("embed_q8", &embed_q8);
+  m.def("norm_prep", &norm_prep);
   m.def("decode_attention", &decode_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("block_tables"), py::arg("context_lens"), py::arg("out"), py::arg("ws"), py::arg("splits"),
         py::arg("keys_per_split"), py::arg("scale"), py::arg("status") = py::none(), py::arg("allow_tc") = true);

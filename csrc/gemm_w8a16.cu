@@ -64,7 +64,9 @@ struct GemmSmem {
   static constexpr int kXOff = kW16Off + F * kW16Bytes;
   static constexpr int kWrawOff = kXOff + R * kXBytes;
   static constexpr int kStageOff = kWrawOff + R * kWrawBytes;          // [16 cols][128 rows] fp32 = 8 KB
-  static constexpr int kBarOff = kStageOff + kChunk * kBM * 4;
+  static constexpr int kInvOff = kStageOff + kChunk * kBM * 4;         // [BN] per-token input row scale
+  static constexpr int kSsqOff = kInvOff + BN * 4;                     // [4 warps][16] partial sums of squares
+  static constexpr int kBarOff = kSsqOff + kEpiWarps * kChunk * 4;
   static constexpr int kNumBars = 2 * R + 2 * F + 5;
   static constexpr int kBytes = kBarOff + kNumBars * 8 + 32;
   static constexpr int kAlloc = kBytes + 1024;
@@ -76,12 +78,139 @@ struct GemmSmem {
 HRM_DEVINL int64_t unit_start(int64_t c, int64_t U, int64_t G) { return (c * U) / G; }
 HRM_DEVINL int owner_of(int64_t x, int64_t U, int64_t G) { return (int)(((x + 1) * G - 1) / U); }
 
+// Per-token input row scale (RMSNorm folded into the consumer GEMM): inv[j] for the tile's BN tokens.
+template <int BN>
+HRM_DEVINL void compute_row_scale(const GemmArgs& a, int m_tile, float* inv, int et) {
+  asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");   // previous tile's readers are done with inv
+  for (int j = et; j < BN; j += kEpiThreads) {
+    const int m = m_tile * BN + j;
+    float s = 0.f;
+    if (m < a.M)
+      for (int t = 0; t < a.in_ssq_tiles; ++t) s += a.in_ssq[(size_t)t * a.M + m];
+    inv[j] = rsqrtf(s * a.in_inv_h + a.in_eps);
+  }
+  asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+}
+
+// ------------------------------------------------------------------ peer-memory (NVLink) flags for EPI_RESID_AR
+HRM_DEVINL void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+HRM_DEVINL int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait for a peer flag to reach `want` (epochs only grow).  Records kErrTimeoutPeer on timeout.
+HRM_DEVINL bool wait_peer_flag(const int* p, int want, int* status) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (ld_acquire_sys(p) - want >= 0) return true;
+    if ((i & 63u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+      record_error(status, kErrTimeoutPeer);
+      return false;
+    }
+  }
+}
+
+// x_new of 16 tokens for this thread's row -> residual, xg = x * gamma_next, per-tile sums of squares.
+template <int BN>
+HRM_DEVINL void store_residual_outputs(const GemmArgs& a, int n_tile, int m_tile, int row, int c0,
+                                       const float (&xn)[kChunk], int et, float* ssq_red) {
+  const int n = n_tile * kBM + row;
+  const float gn = (a.gamma_next != nullptr && n < a.N) ? a.gamma_next[n] : 0.f;
+  float sq[kChunk];
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) {
+    const int m = m_tile * BN + c0 + j;
+    const bool ok = m < a.M && n < a.N;
+    if (ok) {
+      a.resid[(size_t)m * a.ldr + n] = xn[j];
+      if (a.xg_out != nullptr) a.xg_out[(size_t)m * a.ldxg + n] = __float2half_rn(xn[j] * gn);
+    }
+    sq[j] = ok ? xn[j] * xn[j] : 0.f;
+  }
+  if (a.ssq_out != nullptr) {
+    const int w = et >> 5, lane = et & 31;
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      const float s = warp_sum(sq[j]);
+      if (lane == 0) ssq_red[w * kChunk + j] = s;
+    }
+    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+    if (et < kChunk) {
+      const int m = m_tile * BN + c0 + et;
+      const float s = ssq_red[et] + ssq_red[kChunk + et] + ssq_red[2 * kChunk + et] + ssq_red[3 * kChunk + et];
+      if (m < a.M) a.ssq_out[(size_t)n_tile * a.M + m] = s;
+    }
+    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+  }
+}
+
+// Tensor-parallel residual epilogue, after this rank's partial tile was written to its symmetric buffer:
+// publish it, then the owner rank (tile % world) sums all ranks' partials in rank order + the residual, publishes
+// the reduced tile, and every other rank copies it.  All ranks end with identical x / xg / ssq.
+template <int BN>
+HRM_DEVINL void ar_reduce_tile(const GemmArgs& a, int n_tile, int m_tile, int row, int et, int ep, float* ssq_red) {
+  const int tile = n_tile;   // decode: one m tile
+  char* local = reinterpret_cast<char*>(a.peers[a.tp_rank]);
+  int* ready = reinterpret_cast<int*>(local + a.off_flags) + tile;
+  int* done = reinterpret_cast<int*>(local + a.off_flags) + a.ar_max_tiles + tile;
+  __threadfence_system();
+  asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+  if (et == 0) st_release_sys(ready, ep);
+  const int owner = tile % a.tp_world;
+  const int n = n_tile * kBM + row;
+  if (owner == a.tp_rank) {
+    if (et < a.tp_world) {
+      const char* pb = reinterpret_cast<const char*>(a.peers[et]);
+      wait_peer_flag(reinterpret_cast<const int*>(pb + a.off_flags) + tile, ep, a.status);
+    }
+    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+    float* fin = reinterpret_cast<float*>(local + a.off_final) + (size_t)tile * a.ar_tile_floats;
+    for (int c0 = 0; c0 < BN; c0 += kChunk) {
+      float xn[kChunk];
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        const int m = m_tile * BN + c0 + j;
+        float acc = (m < a.M && n < a.N) ? a.resid[(size_t)m * a.ldr + n] : 0.f;
+        float sum = 0.f;
+        for (int r = 0; r < a.tp_world; ++r) {
+          const float* pp = reinterpret_cast<const float*>(reinterpret_cast<const char*>(a.peers[r]) + a.off_partials) +
+                            (size_t)tile * a.ar_tile_floats + (c0 + j) * kBM + row;
+          sum += __ldcv(pp);
+        }
+        xn[j] = acc + sum;
+        fin[(c0 + j) * kBM + row] = xn[j];
+      }
+      store_residual_outputs<BN>(a, n_tile, m_tile, row, c0, xn, et, ssq_red);
+    }
+    __threadfence_system();
+    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+    if (et == 0) st_release_sys(done, ep);
+  } else {
+    const char* ob = reinterpret_cast<const char*>(a.peers[owner]);
+    if (et == 0) wait_peer_flag(reinterpret_cast<const int*>(ob + a.off_flags) + a.ar_max_tiles + tile, ep, a.status);
+    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+    const float* fin = reinterpret_cast<const float*>(ob + a.off_final) + (size_t)tile * a.ar_tile_floats;
+    for (int c0 = 0; c0 < BN; c0 += kChunk) {
+      float xn[kChunk];
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) xn[j] = __ldcv(&fin[(c0 + j) * kBM + row]);
+      store_residual_outputs<BN>(a, n_tile, m_tile, row, c0, xn, et, ssq_red);
+    }
+  }
+}
+
 template <int BN, int EPI>
-HRM_DEVINL void epilogue_store(const GemmArgs& a, int n_tile, int m_tile, int row, int c0, const float (&v)[kChunk],
-                               float* stage, int et) {
+HRM_DEVINL void epilogue_store(const GemmArgs& a, int n_tile, int m_tile, int row, int c0, const float (&v0)[kChunk],
+                               float* stage, int et, const float* inv, float* ssq_red) {
   const int n = n_tile * kBM + row;
   const float sc = (n < a.N) ? a.scale[n] : 0.f;
   const float bi = (a.bias != nullptr && n < a.N) ? a.bias[n] : 0.f;
+  float v[kChunk];
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) v[j] = a.in_ssq != nullptr ? v0[j] * inv[c0 + j] : v0[j];
   if constexpr (EPI == EPI_SWIGLU || EPI == EPI_QKV) {
 #pragma unroll
     for (int j = 0; j < kChunk; ++j) stage[j * kBM + row] = v[j] * sc + bi;
@@ -131,6 +260,20 @@ HRM_DEVINL void epilogue_store(const GemmArgs& a, int n_tile, int m_tile, int ro
       }
     }
     asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+  } else if constexpr (EPI == EPI_RESID) {
+    float xn[kChunk];
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      const int m = m_tile * BN + c0 + j;
+      xn[j] = (m < a.M && n < a.N) ? a.resid[(size_t)m * a.ldr + n] + (v[j] * sc + bi) : 0.f;
+    }
+    store_residual_outputs<BN>(a, n_tile, m_tile, row, c0, xn, et, ssq_red);
+  } else if constexpr (EPI == EPI_RESID_AR) {
+    // this rank's partial tile -> its symmetric buffer ([token][128 rows], one slot per n tile)
+    float* part = reinterpret_cast<float*>(reinterpret_cast<char*>(a.peers[a.tp_rank]) + a.off_partials) +
+                  (size_t)n_tile * a.ar_tile_floats;
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) __stcg(&part[(c0 + j) * kBM + row], v[j] * sc);
   } else {
 #pragma unroll
     for (int j = 0; j < kChunk; ++j) {
@@ -139,11 +282,8 @@ HRM_DEVINL void epilogue_store(const GemmArgs& a, int n_tile, int m_tile, int ro
         const float y = v[j] * sc + bi;
         if constexpr (EPI == EPI_F16) {
           reinterpret_cast<__half*>(a.out)[(size_t)m * a.ldo + n] = __float2half_rn(y);
-        } else if constexpr (EPI == EPI_F32) {
-          reinterpret_cast<float*>(a.out)[(size_t)m * a.ldo + n] = y;
         } else {
-          float* rp = &a.resid[(size_t)m * a.ldr + n];
-          *rp = *rp + y;
+          reinterpret_cast<float*>(a.out)[(size_t)m * a.ldo + n] = y;
         }
       }
     }
@@ -162,6 +302,8 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
   uint8_t* xs = base + S::kXOff;
   uint8_t* wraw = base + S::kWrawOff;
   float* stage = reinterpret_cast<float*>(base + S::kStageOff);
+  float* inv = reinterpret_cast<float*>(base + S::kInvOff);
+  float* ssq_red = reinterpret_cast<float*>(base + S::kSsqOff);
   uint64_t* rfull = reinterpret_cast<uint64_t*>(base + S::kBarOff);
   uint64_t* rempty = rfull + R;
   uint64_t* ffull = rempty + R;
@@ -299,6 +441,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
     const int et = threadIdx.x - kFirstEpiWarp * 32;   // 0..127
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
+    const int ep = (EPI == EPI_RESID_AR) ? *reinterpret_cast<volatile int*>(a.epoch) + 1 : 0;
     int seg = 0;
     for (int64_t u = u0; u < u1; ++seg) {
       const int tile = (int)(u / a.k_tiles);
@@ -312,6 +455,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       mbar_wait_ab(&afull[acc], (uint32_t)(seg >> 1) & 1u, a.status, kErrTimeoutAccum, abort_flag);
       tc_fence_after();
       if (whole) {
+        if (a.in_ssq != nullptr) compute_row_scale<BN>(a, m_tile, inv, et);
         for (int c0 = 0; c0 < BN; c0 += kChunk) {
           float v[kChunk];
           tmem_ld16(acc_addr + (uint32_t)c0, v);
@@ -319,8 +463,9 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
             tc_fence_before();
             mbar_arrive(&aempty[acc]);
           }
-          epilogue_store<BN, EPI>(a, n_tile, m_tile, row, c0, v, stage, et);
+          epilogue_store<BN, EPI>(a, n_tile, m_tile, row, c0, v, stage, et, inv, ssq_red);
         }
+        if constexpr (EPI == EPI_RESID_AR) ar_reduce_tile<BN>(a, n_tile, m_tile, row, et, ep, ssq_red);
       } else {
         // partial segment: write fp32 partial, take a ticket; the last segment of the tile reduces in k order
         const int first = owner_of((int64_t)tile * a.k_tiles, U, G);
@@ -349,6 +494,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
         asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
         if (is_last) {
           __threadfence();
+          if (a.in_ssq != nullptr) compute_row_scale<BN>(a, m_tile, inv, et);
           for (int c0 = 0; c0 < BN; c0 += kChunk) {
             float v[kChunk];
 #pragma unroll
@@ -358,8 +504,9 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
 #pragma unroll
               for (int j = 0; j < kChunk; ++j) v[j] += __ldcg(&p[(c0 + j) * kBM + row]);
             }
-            epilogue_store<BN, EPI>(a, n_tile, m_tile, row, c0, v, stage, et);
+            epilogue_store<BN, EPI>(a, n_tile, m_tile, row, c0, v, stage, et, inv, ssq_red);
           }
+          if constexpr (EPI == EPI_RESID_AR) ar_reduce_tile<BN>(a, n_tile, m_tile, row, et, ep, ssq_red);
         }
       }
       u = ue;
@@ -371,6 +518,16 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, S::kTmemCols);
+  }
+  if constexpr (EPI == EPI_RESID_AR) {
+    if (threadIdx.x == 0) {   // the last CTA to finish advances this rank's epoch for the next launch
+      __threadfence();
+      if (atomicAdd(a.launch_ticket, 1) == (int)gridDim.x - 1) {
+        *reinterpret_cast<volatile int*>(a.epoch) = *reinterpret_cast<volatile int*>(a.epoch) + 1;
+        *a.launch_ticket = 0;
+        __threadfence();
+      }
+    }
   }
 }
 
@@ -513,6 +670,11 @@ void gemm_w8a16_launch(const void* x, int ldx, const int8_t* w, int epi, GemmArg
     case EPI_RESID: launch_epi<EPI_RESID>(tw, tx, a, p, stream); break;
     case EPI_SWIGLU: launch_epi<EPI_SWIGLU>(tw, tx, a, p, stream); break;
     case EPI_QKV: launch_epi<EPI_QKV>(tw, tx, a, p, stream); break;
+    case EPI_RESID_AR:
+      if (p.m_tiles != 1 || p.bn > 64) throw std::runtime_error("w8a16 gemm: fused all-reduce supports M <= 64");
+      if (a.N / 128 > a.ar_max_tiles) throw std::runtime_error("w8a16 gemm: too many tiles for the symmetric buffer");
+      launch_epi<EPI_RESID_AR>(tw, tx, a, p, stream);
+      break;
     default: throw std::runtime_error("w8a16 gemm: bad epilogue");
   }
 }

@@ -14,6 +14,7 @@ enum GemmEpilogue : int {
   EPI_RESID = 2,   // resid f32 [M, ldr]         += acc * scale (+ bias)
   EPI_SWIGLU = 3,  // out f16 [M, N/2]            = silu(gate) * up, rows interleaved 64 gate / 64 up per tile
   EPI_QKV = 4,     // q_out bf16 [M, q_rows]; K/V rows -> paged cache (bias + rotate-half RoPE on q and k)
+  EPI_RESID_AR = 5,  // tensor-parallel residual GEMM: partial tiles all-reduced over peer memory, then as EPI_RESID
 };
 
 struct GemmArgs {
@@ -25,6 +26,25 @@ struct GemmArgs {
   int ldo;
   float* resid;                             // EPI_RESID
   int ldr;
+  // EPI_RESID optional outputs feeding the next RMSNorm without a norm kernel:
+  //   xg_out[m, n] = f16(x_new[m, n] * gamma_next[n]);  ssq_out[n_tile * M + m] = sum over the tile's rows of x_new^2
+  __half* xg_out;
+  int ldxg;
+  const float* gamma_next;
+  float* ssq_out;
+  // consumer side: every output of token m is multiplied by rsqrt(sum_t in_ssq[t * M + m] * in_inv_h + in_eps)
+  // (the RMSNorm of the un-normalised GEMM input, whose gamma is already folded into X)
+  const float* in_ssq;
+  int in_ssq_tiles;
+  float in_inv_h, in_eps;
+  // EPI_RESID_AR: symmetric buffers of all ranks (peers[r] = base address of rank r's buffer, mapped locally)
+  const long long* peers;
+  int tp_rank, tp_world;
+  long long off_partials, off_final, off_flags;   // byte offsets inside every rank's buffer
+  int ar_tile_floats;                             // floats per tile slot (max_bn * 128)
+  int ar_max_tiles;
+  int* epoch;                                     // this rank's launch epoch counter (in its symmetric buffer)
+  int* launch_ticket;                             // CTA-completion ticket (device memory, zero between launches)
   float* ws;                                // stream-K partials: plan.ws_floats floats
   int* counters;                            // stream-K tickets: plan.counters ints, zero before first use
   // EPI_QKV

@@ -9,6 +9,8 @@ namespace hrm {
 
 void rmsnorm_launch(float* x, const float* delta, const float* w, __half* out, int M, int H, float eps,
                     cudaStream_t s);
+void norm_prep_launch(float* x, const float* delta, const float* gamma, __half* xg, float* ssq, int M, int H,
+                      cudaStream_t s);
 void embed_q8_launch(const int64_t* ids, const int8_t* q, const float* scale, float* out, int M, int H,
                      int vocab_start, int vocab_local, cudaStream_t s);
 

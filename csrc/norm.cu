@@ -132,3 +132,48 @@ void decode_advance_launch(const int64_t* tokens, int64_t* ids, int* positions, 
 }
 
 }  // namespace hrm
+
+namespace hrm {
+
+// RMSNorm preparation without normalising: optionally x += delta, then
+//   xg[m, n] = f16(x[m, n] * gamma[n])          (the next GEMM's operand, gamma folded in)
+//   ssq[t * M + m] = sum_{n in [128t, 128t+128)} x[m, n]^2
+// The consuming GEMM multiplies token m's outputs by rsqrt(sum_t ssq[t*M+m] / H + eps).  One CTA per row; each
+// thread owns 32 consecutive columns, 4 threads per 128-column tile.
+__global__ void __launch_bounds__(256) norm_prep_kernel(float* __restrict__ x, const float* __restrict__ delta,
+                                                        const float* __restrict__ gamma, __half* __restrict__ xg,
+                                                        float* __restrict__ ssq, int M, int H) {
+  const int m = blockIdx.x;
+  float* xr = x + (size_t)m * H;
+  for (int c0 = threadIdx.x * 32; c0 < H; c0 += blockDim.x * 32) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      float4 v = *reinterpret_cast<float4*>(xr + c0 + i);
+      if (delta) {
+        const float4 d = *reinterpret_cast<const float4*>(delta + (size_t)m * H + c0 + i);
+        v.x += d.x; v.y += d.y; v.z += d.z; v.w += d.w;
+        *reinterpret_cast<float4*>(xr + c0 + i) = v;
+      }
+      s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      const float4 g = *reinterpret_cast<const float4*>(gamma + c0 + i);
+      __half2 a = __floats2half2_rn(v.x * g.x, v.y * g.y), b = __floats2half2_rn(v.z * g.z, v.w * g.w);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&a);
+      pk.y = *reinterpret_cast<uint32_t*>(&b);
+      *reinterpret_cast<uint2*>(xg + (size_t)m * H + c0 + i) = pk;
+    }
+    // 4 consecutive threads cover one 128-column tile
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if ((threadIdx.x & 3) == 0) ssq[(size_t)(c0 / 128) * M + m] = s;
+  }
+}
+
+void norm_prep_launch(float* x, const float* delta, const float* gamma, __half* xg, float* ssq, int M, int H,
+                      cudaStream_t s) {
+  if (M == 0) return;
+  norm_prep_kernel<<<M, 256, 0, s>>>(x, delta, gamma, xg, ssq, M, H);
+}
+
+}  // namespace hrm

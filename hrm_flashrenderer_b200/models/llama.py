@@ -105,6 +105,14 @@ class LlamaW8:
         self.max_pos = max_pos
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self.kv: Optional[PagedKVPool] = None
+        self.symm = None   # SymmetricWorkspace: enables the fused GEMM + all-reduce kernels when TP > 1
+
+    def enable_fused_collectives(self, group=None) -> None:
+        """Allocate / exchange the NVLink symmetric buffers (collective over the TP group)."""
+        if self.plan.world > 1 and self.device.type == "cuda" and self.symm is None:
+            from ..parallel.symm import SymmetricWorkspace
+            self.symm = SymmetricWorkspace(self.plan.rank, self.plan.world, self.device,
+                                           max_tiles=max(64, self.cfg.hidden // 128), max_bn=64, group=group)
 
     # ------------------------------------------------------------------ construction
     @classmethod
@@ -191,25 +199,34 @@ class LlamaW8:
 
     @torch.no_grad()
     def forward(self, b: BatchMeta) -> torch.Tensor:
-        """Runs all layers for the batch and returns greedy next tokens ``[len(last_rows)]`` (int64, global ids)."""
+        """Runs all layers for the batch and returns greedy next tokens ``[len(last_rows)]`` (int64, global ids).
+
+        RMSNorm is folded into the GEMMs: the residual stream ``x`` (fp32) is accompanied by ``xg = x * gamma``
+        (the next GEMM's operand) and per-128-column sums of squares ``ssq``; the consuming GEMM scales each
+        token's outputs by ``rsqrt(sum(ssq) / H + eps)``.  With TP=1 the residual GEMMs produce ``xg``/``ssq`` in
+        their epilogue; with TP > 1 the row-parallel partial is all-reduced first.
+        """
         cfg, p = self.cfg, self.plan
         T = b.ids.shape[0]
         H = cfg.hidden
         tp = p.world > 1
+        dev = self.device
+        cuda = dev.type == "cuda"
         x = ops.embedding_q8(b.ids, self.embed_q, self.embed_s, p.vocab_start)
         if tp:
             self.comm.all_reduce_(x)
-        h = torch.empty(T, H, dtype=torch.float16, device=self.device)
-        ops.rmsnorm(x, self.layers[0].ln1, cfg.rms_eps, out=h)
+        xg = torch.empty(T, H, dtype=torch.float16 if cuda else torch.float32, device=dev)
+        ssq = torch.empty(H // 128, T, dtype=torch.float32, device=dev)
+        ops.norm_prep(x, None, self.layers[0].ln1, xg, ssq)
+        norm = (ssq, H, cfg.rms_eps)
         D = cfg.head_dim
-        q_out = torch.empty(T, self.q_rows, dtype=torch.bfloat16, device=self.device)
-        attn = torch.empty(T, p.local_heads, D, dtype=torch.float16, device=self.device)
-        act = torch.empty(T, p.local_inter, dtype=torch.float16, device=self.device)
-        partial = torch.empty(T, H, dtype=torch.float32, device=self.device) if tp else None
+        q_out = torch.empty(T, self.q_rows, dtype=torch.bfloat16, device=dev)
+        attn = torch.empty(T, p.local_heads, D, dtype=torch.float16 if cuda else torch.float32, device=dev)
+        partial = torch.empty(T, H, dtype=torch.float32, device=dev) if tp else None
         for l, L in enumerate(self.layers):
             kc, vc = self.kv.k[l], self.kv.v[l]
-            ops.w8a16_qkv_rope_append(h, L.w_qkv, L.s_qkv, L.b_qkv, self.q_rows, self.kv_rows, D, b.positions,
-                                      b.slots, self.cos, self.sin, kc, vc, q_out=q_out)
+            ops.w8a16_qkv_rope_append(xg, L.w_qkv, L.s_qkv, L.b_qkv, self.q_rows, self.kv_rows, D, b.positions,
+                                      b.slots, self.cos, self.sin, kc, vc, q_out=q_out, in_norm=norm)
             q3 = q_out.view(T, p.local_heads, D)
             if b.is_decode:
                 ops.paged_decode_attention(q3, kc, vc, b.block_tables, b.context_lens, self.scale,
@@ -218,24 +235,33 @@ class LlamaW8:
                 ops.paged_prefill_attention(q3, kc, vc, b.block_tables, b.cu_q, b.q_start, b.context_lens, b.max_q,
                                             self.scale, out=attn)
             a2 = attn.view(T, self.q_rows)
-            if tp:
-                self._mm_f32(a2, L.w_o, L.s_o, partial)
-                self._all_reduce_add_norm(x, partial, L.ln2, h)
+            fused = tp and self.symm is not None and T <= 64
+            if fused:
+                ops.w8a16_residual_ar_(a2, L.w_o, L.s_o, x, self.symm, L.ln2, xg, ssq)
+            elif tp:
+                ops.w8a16_linear_out(a2, L.w_o, L.s_o, partial)
+                self.comm.all_reduce_(partial)
+                ops.norm_prep(x, partial, L.ln2, xg, ssq)
             else:
-                ops.w8a16_residual_(a2, L.w_o, L.s_o, x)
-                ops.rmsnorm(x, L.ln2, cfg.rms_eps, out=h)
-            act = ops.w8a16_swiglu(h, L.w_gu, L.s_gu)
+                ops.w8a16_residual_(a2, L.w_o, L.s_o, x, gamma_next=L.ln2, xg_out=xg, ssq_out=ssq)
+            act = ops.w8a16_swiglu(xg, L.w_gu, L.s_gu, in_norm=norm)
             g_next = self.layers[l + 1].ln1 if l + 1 < len(self.layers) else self.final_norm
-            if tp:
-                self._mm_f32(act, L.w_d, L.s_d, partial)
-                self._all_reduce_add_norm(x, partial, g_next, h)
+            if fused:
+                ops.w8a16_residual_ar_(act, L.w_d, L.s_d, x, self.symm, g_next, xg, ssq)
+            elif tp:
+                ops.w8a16_linear_out(act, L.w_d, L.s_d, partial)
+                self.comm.all_reduce_(partial)
+                ops.norm_prep(x, partial, g_next, xg, ssq)
             else:
-                ops.w8a16_residual_(act, L.w_d, L.s_d, x)
-                ops.rmsnorm(x, g_next, cfg.rms_eps, out=h)
-        hl = h.index_select(0, b.last_rows)
-        logits = ops.w8a16_linear(hl, self.head_q, self.head_s, out_dtype=torch.float32)
+                ops.w8a16_residual_(act, L.w_d, L.s_d, x, gamma_next=g_next, xg_out=xg, ssq_out=ssq)
+        if b.is_decode:
+            xl, nl = xg, norm
+        else:
+            xl = xg.index_select(0, b.last_rows)
+            nl = (ssq.index_select(1, b.last_rows).contiguous(), H, cfg.rms_eps)
+        logits = ops.w8a16_linear(xl, self.head_q, self.head_s, out_dtype=torch.float32, in_norm=nl)
         if tp:
-            keys = torch.empty(hl.shape[0], dtype=torch.int64, device=self.device)
+            keys = torch.empty(xl.shape[0], dtype=torch.int64, device=dev)
             ops.argmax_rows(logits, p.vocab_start, keys=keys)
             self.comm.all_reduce_max_(keys)
             from ..parallel.dist import unpack_argmax

@@ -113,12 +113,26 @@ def _as_f16_2d(x: torch.Tensor) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------------------------------------ GEMMs
+# ``in_norm = (ssq, H, eps)`` folds an RMSNorm into a GEMM: X is the un-normalised input times gamma (see
+# :func:`norm_prep`) and token m's outputs are scaled by rsqrt(sum_t ssq[t, m] / H + eps).
+def _inv_rms(in_norm):
+    ssq, H, eps = in_norm
+    return torch.rsqrt(ssq.reshape(-1, ssq.shape[-1]).sum(0) / float(H) + float(eps))
+
+
+def _norm_kw(in_norm):
+    if in_norm is None:
+        return {}
+    ssq, H, eps = in_norm
+    return dict(in_ssq=ssq, inv_h=1.0 / float(H), eps=float(eps))
 def w8a16_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, bias: Optional[torch.Tensor] = None,
-                 out_dtype: Optional[torch.dtype] = None, force_ctas: int = 0) -> torch.Tensor:
+                 out_dtype: Optional[torch.dtype] = None, force_ctas: int = 0, in_norm=None) -> torch.Tensor:
     """``y = x @ (qweight * scale[:, None])^T (+ bias)``; int8 weights ``[N, K]`` with per-row fp32 scales."""
     N, K = qweight.shape
     if not x.is_cuda:
         y = x.to(torch.float32) @ (qweight.to(torch.float32) * scale.to(torch.float32)[:, None]).t()
+        if in_norm is not None:
+            y = y * _inv_rms(in_norm).view(*([1] * (y.dim() - 2)), -1, 1)
         if bias is not None:
             y = y + bias.to(torch.float32)
         return y.to(out_dtype) if out_dtype is not None else y
@@ -129,34 +143,55 @@ def w8a16_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, bi
     od = out_dtype or torch.float16
     out = torch.empty(M, N, dtype=torch.float32 if od == torch.float32 else torch.float16, device=x.device)
     w = _ws_for(M, N, K, x.device, force_ctas)
-    C.w8a16_gemm(x2, qweight, scale, bias, out, w.ws, w.counters, force_ctas)
+    C.w8a16_gemm(x2, qweight, scale, bias, out, w.ws, w.counters, force_ctas, **_norm_kw(in_norm))
     LAUNCH_COUNTER.add()
     out = out if out.dtype == od else out.to(od)
     return out.reshape(*lead, N)
 
 
 def w8a16_linear_out(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, out: torch.Tensor,
-                     force_ctas: int = 0) -> torch.Tensor:
+                     force_ctas: int = 0, in_norm=None) -> torch.Tensor:
     """``out[:] = x @ W^T`` into a preallocated f16/f32 ``[M, N]`` buffer."""
     if not x.is_cuda:
-        out.copy_(x.to(torch.float32) @ (qweight.to(torch.float32) * scale[:, None]).t())
+        y = x.to(torch.float32) @ (qweight.to(torch.float32) * scale[:, None]).t()
+        if in_norm is not None:
+            y = y * _inv_rms(in_norm)[:, None]
+        out.copy_(y)
         return out
     x2 = _as_f16_2d(x)
     w = _ws_for(x2.shape[0], qweight.shape[0], qweight.shape[1], x.device, force_ctas)
-    ext().w8a16_gemm(x2, qweight, scale, None, out, w.ws, w.counters, force_ctas)
+    ext().w8a16_gemm(x2, qweight, scale, None, out, w.ws, w.counters, force_ctas, **_norm_kw(in_norm))
     LAUNCH_COUNTER.add()
     return out
 
 
 def w8a16_residual_(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, resid: torch.Tensor,
-                    force_ctas: int = 0) -> torch.Tensor:
-    """``resid += x @ W^T`` in place (fp32 residual stream)."""
+                    force_ctas: int = 0, gamma_next: Optional[torch.Tensor] = None,
+                    xg_out: Optional[torch.Tensor] = None, ssq_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``resid += x @ W^T`` in place (fp32 residual stream); optionally also ``xg_out = resid * gamma_next`` and the
+    per-128-column sums of squares ``ssq_out [N/128, M]`` for the next (folded) RMSNorm."""
     if not x.is_cuda:
         resid += x.to(torch.float32) @ (qweight.to(torch.float32) * scale[:, None]).t()
+        if xg_out is not None:
+            norm_prep(resid, None, gamma_next, xg_out, ssq_out)
         return resid
     x2 = _as_f16_2d(x)
     w = _ws_for(x2.shape[0], qweight.shape[0], qweight.shape[1], x.device, force_ctas)
-    ext().w8a16_gemm_residual(x2, qweight, scale, resid, w.ws, w.counters, force_ctas)
+    ext().w8a16_gemm_residual(x2, qweight, scale, resid, w.ws, w.counters, force_ctas, gamma_next, xg_out, ssq_out)
+    LAUNCH_COUNTER.add()
+    return resid
+
+
+def w8a16_residual_ar_(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, resid: torch.Tensor, symm,
+                       gamma_next: torch.Tensor, xg_out: torch.Tensor, ssq_out: torch.Tensor) -> torch.Tensor:
+    """Tensor-parallel row-parallel GEMM fused with its all-reduce over NVLink peer memory (decode, M <= 64):
+    ``resid += sum over ranks of x_r @ W_r^T``; also writes ``xg_out = resid * gamma_next`` and ``ssq_out``.
+    Every rank ends with bitwise-identical outputs (rank-ordered reduction by the tile's owner rank)."""
+    x2 = _as_f16_2d(x)
+    w = _ws_for(x2.shape[0], qweight.shape[0], qweight.shape[1], x.device)
+    ext().w8a16_gemm_residual_ar(x2, qweight, scale, resid, w.ws, w.counters, gamma_next, xg_out, ssq_out, symm.peers,
+                                 symm.rank, symm.world, symm.off_partials, symm.off_final, symm.off_flags,
+                                 symm.max_bn * 128, symm.max_tiles, symm.epoch_ptr, symm.ticket)
     LAUNCH_COUNTER.add()
     return resid
 
@@ -177,19 +212,22 @@ def interleave_gate_up(gate_q: torch.Tensor, up_q: torch.Tensor, gate_s: torch.T
     return q.contiguous(), s.contiguous()
 
 
-def w8a16_swiglu(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, force_ctas: int = 0) -> torch.Tensor:
+def w8a16_swiglu(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, force_ctas: int = 0,
+                 in_norm=None) -> torch.Tensor:
     """``silu(x @ Wg^T) * (x @ Wu^T)`` with ``w_gu`` packed by :func:`interleave_gate_up`; f16 output."""
     N2, K = w_gu.shape
     F = N2 // 2
     if not x.is_cuda:
         h = swiglu_half(F)
         y = x.to(torch.float32) @ (w_gu.to(torch.float32) * s_gu[:, None]).t()
+        if in_norm is not None:
+            y = y * _inv_rms(in_norm)[:, None]
         y = y.view(*y.shape[:-1], F // h, 2, h)
         return (torch.nn.functional.silu(y[..., 0, :]) * y[..., 1, :]).reshape(*x.shape[:-1], F)
     x2 = _as_f16_2d(x)
     out = torch.empty(x2.shape[0], F, dtype=torch.float16, device=x.device)
     w = _ws_for(x2.shape[0], N2, K, x.device, force_ctas)
-    ext().w8a16_gemm_swiglu(x2, w_gu, s_gu, out, w.ws, w.counters, force_ctas)
+    ext().w8a16_gemm_swiglu(x2, w_gu, s_gu, out, w.ws, w.counters, force_ctas, **_norm_kw(in_norm))
     LAUNCH_COUNTER.add()
     return out.reshape(*x.shape[:-1], F)
 
@@ -197,11 +235,11 @@ def w8a16_swiglu(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, force_
 def w8a16_qkv_rope_append(x: torch.Tensor, w_qkv: torch.Tensor, s_qkv: torch.Tensor, bias: Optional[torch.Tensor],
                           q_rows: int, kv_rows: int, head_dim: int, positions: torch.Tensor, slots: torch.Tensor,
                           cos_t: torch.Tensor, sin_t: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
-                          q_out: Optional[torch.Tensor] = None, force_ctas: int = 0) -> torch.Tensor:
+                          q_out: Optional[torch.Tensor] = None, force_ctas: int = 0, in_norm=None) -> torch.Tensor:
     """Fused QKV projection + bias + rotate-half RoPE + paged KV append.  Returns q ``[M, q_rows]`` bf16."""
     M = x.reshape(-1, x.shape[-1]).shape[0]
     if not x.is_cuda:
-        y = w8a16_linear(x.reshape(M, -1), w_qkv, s_qkv, bias)
+        y = w8a16_linear(x.reshape(M, -1), w_qkv, s_qkv, bias, in_norm=in_norm)
         D = head_dim
         q = y[:, :q_rows].view(M, -1, D)
         k = y[:, q_rows:q_rows + kv_rows].view(M, -1, D)
@@ -225,7 +263,7 @@ def w8a16_qkv_rope_append(x: torch.Tensor, w_qkv: torch.Tensor, s_qkv: torch.Ten
         q_out = torch.empty(M, q_rows, dtype=torch.bfloat16, device=x.device)
     w = _ws_for(M, w_qkv.shape[0], w_qkv.shape[1], x.device, force_ctas)
     ext().w8a16_gemm_qkv(x2, w_qkv, s_qkv, bias, q_rows, kv_rows, head_dim, positions, slots, cos_t, sin_t, q_out,
-                         k_cache, v_cache, w.ws, w.counters, force_ctas)
+                         k_cache, v_cache, w.ws, w.counters, force_ctas, **_norm_kw(in_norm))
     LAUNCH_COUNTER.add()
     return q_out
 
@@ -259,6 +297,20 @@ def add_rmsnorm_(x: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: flo
     ext().rmsnorm(x, delta.contiguous(), w, float(eps), out)
     LAUNCH_COUNTER.add()
     return out
+
+
+def norm_prep(x: torch.Tensor, delta: Optional[torch.Tensor], gamma: torch.Tensor, xg: torch.Tensor,
+              ssq: torch.Tensor) -> None:
+    """``x += delta`` (optional), ``xg = x * gamma`` (f16 on CUDA), ``ssq[t, m] = sum of x[m, 128t:128t+128]^2``."""
+    if not x.is_cuda:
+        if delta is not None:
+            x += delta.to(x.dtype)
+        xg.copy_(x * gamma)
+        M, H = x.reshape(-1, x.shape[-1]).shape
+        ssq.view(-1)[: (H // 128) * M].copy_(x.reshape(M, H // 128, 128).pow(2).sum(-1).t().reshape(-1))
+        return
+    ext().norm_prep(x, delta, gamma, xg, ssq)
+    LAUNCH_COUNTER.add()
 
 
 def embedding_q8(ids: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, vocab_start: int = 0,

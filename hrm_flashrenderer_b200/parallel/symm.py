@@ -1,0 +1,79 @@
+"""Symmetric peer memory over NVLink/NVSwitch for the fused compute+collective kernels.
+
+Every rank ``cudaMalloc``s one equally sized buffer, exports a CUDA IPC handle, exchanges handles over the
+``torch.distributed`` control group and maps every peer's buffer (``cudaIpcOpenMemHandle``).  Kernels then read and
+write peers directly through a device table of base pointers ``peers[r]`` (``peers[rank]`` is the local buffer).
+
+Layout of the buffer (all offsets 256-byte aligned):
+
+* ``partials``  fp32 [max_tiles][max_bn][128]  -- this rank's row-parallel partial tiles;
+* ``final``     fp32 [max_tiles][max_bn][128]  -- reduced tiles owned by this rank (tile % world == rank);
+* ``flags``     int32 [2][max_tiles] (ready, done), plus scalars (the per-launch epoch counter, argmax keys).
+
+Flags carry an epoch number that every fused launch increments once, so a flag written by a previous launch is never
+mistaken for a current one and no reset pass is needed between launches.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+
+ALIGN = 256
+
+
+def _al(x: int) -> int:
+    return (x + ALIGN - 1) // ALIGN * ALIGN
+
+
+class SymmetricWorkspace:
+    def __init__(self, rank: int, world: int, device: torch.device, max_tiles: int = 1024, max_bn: int = 64,
+                 group=None, extra_bytes: int = 1 << 20):
+        self.rank, self.world, self.device = rank, world, torch.device(device)
+        self.max_tiles, self.max_bn = max_tiles, max_bn
+        tile_bytes = max_bn * 128 * 4
+        self.off_partials = 0
+        self.off_final = _al(self.off_partials + max_tiles * tile_bytes)
+        self.off_flags = _al(self.off_final + max_tiles * tile_bytes)
+        self.off_scalars = _al(self.off_flags + 2 * max_tiles * 4)
+        self.off_extra = _al(self.off_scalars + 4096)
+        self.bytes = _al(self.off_extra + extra_bytes)
+        C = ops.ext()
+        with torch.cuda.device(self.device):
+            self.local_ptr, handle = C.symm_alloc(self.bytes)
+        handles = [None] * world
+        if world > 1:
+            dist.all_gather_object(handles, handle, group=group)
+        else:
+            handles = [handle]
+        self.ptrs = []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                self.ptrs.append(self.local_ptr if r == rank else C.symm_open(h))
+        self.peers = torch.tensor(self.ptrs, dtype=torch.int64, device=self.device)
+        # epoch counter lives in this rank's scalars (local memory); the CTA-completion ticket next to it
+        self.epoch = C.tensor_from_ptr(self.local_ptr + self.off_scalars, [1], torch.int32, self.device.index or 0)
+        self.ticket = C.tensor_from_ptr(self.local_ptr + self.off_scalars + 128, [1], torch.int32,
+                                        self.device.index or 0)
+        self.group = group
+
+    @property
+    def epoch_ptr(self) -> int:
+        return self.local_ptr + self.off_scalars
+
+    def view(self, offset: int, shape, dtype=torch.float32) -> torch.Tensor:
+        return ops.ext().tensor_from_ptr(self.local_ptr + offset, list(shape), dtype, self.device.index or 0)
+
+    def close(self) -> None:
+        C = ops.ext()
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                try:
+                    C.symm_close(p)
+                except Exception:
+                    pass
+        if self.world > 1:
+            dist.barrier(group=self.group)   # peers unmapped before the owner frees
+        C.symm_free(self.local_ptr)
+        self.ptrs = []

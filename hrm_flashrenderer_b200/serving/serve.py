@@ -33,8 +33,9 @@ class ServiceState:
                  max_seq_len: int = 8192, max_new_tokens: int = 256, max_sources: int = 16,
                  max_chars_per_source: int = 1200, reserve_prompt_tokens: int = 16, disable_token_budget: bool = False,
                  expose_sources: bool = False, max_concurrent: int = 1, request_timeout_s: float = 180.0,
-                 hrm_timeout_s: float = 1.8, world: int = 1, backend_name: str = "b200_int8"):
+                 hrm_timeout_s: float = 1.8, world: int = 1, backend_name: str = "b200_int8", query_fn=None):
         self.backend = backend
+        self.query_fn = query_fn      # retrieval function (default: run_hrm_query); injectable for mock lanes
         self.hrm_model = Path(hrm_model) if hrm_model else None
         self.hrm_bin = hrm_bin
         self.max_seq_len = max_seq_len
@@ -68,8 +69,9 @@ def build_prompt(state: ServiceState, prompt: str, mode: str) -> Tuple[str, List
         return build_prompt_for_mode(prompt, [], resolved), [], resolved, False
     state.hrm_query_calls_total += 1
     state.hrm_query_calls_by_mode[resolved] = state.hrm_query_calls_by_mode.get(resolved, 0) + 1
-    r = run_hrm_query(hrm_bin=state.hrm_bin, model_dir=state.hrm_model, prompt=prompt, top_k=16, top_m=400, k=16,
-                      prefer_api=True, repo_root=REPO_ROOT, timeout_s=state.hrm_timeout_s)
+    q = state.query_fn or run_hrm_query
+    r = q(hrm_bin=state.hrm_bin, model_dir=state.hrm_model, prompt=prompt, top_k=16, top_m=400, k=16,
+          prefer_api=True, repo_root=REPO_ROOT, timeout_s=state.hrm_timeout_s)
     sources = build_sources(r.raw, max_sources=state.max_sources, max_chars_per_source=state.max_chars_per_source)
     if not sources:
         return "", [], resolved, True
@@ -234,13 +236,18 @@ def main(argv=None):
     hrm_model = Path(args.hrm_model).resolve()
     if not (hrm_model / "router_index.bin").is_file() or not (hrm_model / "index.sqlite").is_file():
         raise SystemExit(f"ERR: HRM model directory must contain router_index.bin and index.sqlite: {hrm_model}")
+    if args.backend != "echo" and args.world > 1:
+        # TP lane: one process per GPU; rank 0 hosts HTTP + scheduler, the other ranks mirror its engine calls
+        from .daemon import LaneArgs, spawn_lane
+        src, tok = resolve_model(args.llm_model, REPO_ROOT / "llm_models")
+        lane = LaneArgs(src, args.world, args.max_seq_len, args.prefill_chunk_size, args.max_batch, "cuda",
+                        master_port=int(os.environ.get("HRM_LANE_MASTER_PORT", str(29600 + args.port % 1000))))
+        spawn_lane(lane, _HttpEntry(args, str(hrm_model), args.tokenizer_model or tok))
+        return
     if args.backend == "echo":
         from .backend import EchoBackend
         backend = EchoBackend()
     else:
-        if args.world > 1:
-            raise SystemExit("ERR: --world > 1 lanes are launched with `hrm-flash daemon --world N` "
-                             "(one process per GPU); serve runs on one GPU")
         from .backend import EngineBackend
         src, tok = resolve_model(args.llm_model, REPO_ROOT / "llm_models")
         backend = EngineBackend(src, tokenizer_source=args.tokenizer_model or tok, device=args.device,
@@ -258,6 +265,31 @@ def main(argv=None):
     app = create_app(state)
     import uvicorn
     uvicorn.run(app, host=args.host, port=args.port, log_level="info")
+
+
+class _HttpEntry:
+    """Rank-0 body of a TP lane (picklable for mp.spawn): HTTP service over the mirrored engine."""
+
+    def __init__(self, args, hrm_model: str, tokenizer_source):
+        self.args, self.hrm_model, self.tok = args, hrm_model, tokenizer_source
+
+    def __call__(self, engine):
+        from .backend import EngineBackend
+        a = self.args
+        backend = EngineBackend("", tokenizer_source=self.tok, max_prompt_tokens=a.max_prompt_tokens,
+                                local_files_only=a.local_files_only, engine=engine)
+        state = ServiceState(backend=backend, hrm_model=Path(self.hrm_model),
+                             hrm_bin=find_hrm_binary(repo_root=REPO_ROOT, explicit=a.hrm_bin),
+                             max_seq_len=a.max_seq_len, max_new_tokens=a.max_new_tokens, max_sources=a.max_sources,
+                             max_chars_per_source=a.max_chars_per_source,
+                             reserve_prompt_tokens=a.reserve_prompt_tokens, disable_token_budget=a.disable_token_budget,
+                             expose_sources=a.expose_sources, max_concurrent=a.max_concurrent,
+                             request_timeout_s=a.native_request_timeout_s, world=a.world, backend_name=a.backend)
+        import uvicorn
+        try:
+            uvicorn.run(create_app(state), host=a.host, port=a.port, log_level="info")
+        finally:
+            backend.stop()
 
 
 if __name__ == "__main__":

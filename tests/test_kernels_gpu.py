@@ -62,7 +62,7 @@ def test_w8a16_f16_out_and_bias():
     assert (y.float() - ref).abs().max().item() < 2e-2
 
 
-@pytest.mark.parametrize("M", [1, 16, 130])
+@pytest.mark.parametrize("M", [1, 16, 130, 300])
 def test_w8a16_residual(M):
     q, s = _qw(1024, 768, 7)
     x = _x(M, 768, 8)
@@ -72,7 +72,45 @@ def test_w8a16_residual(M):
     assert (r - (r0 + _ref(x, q, s))).abs().max().item() < 1e-3
 
 
-@pytest.mark.parametrize("M", [1, 16, 70])
+@pytest.mark.parametrize("M", [1, 16, 130, 300])
+def test_w8a16_residual_norm_outputs_and_folded_norm(M):
+    """Residual epilogue writes xg = x*gamma and per-tile sums of squares; a consumer GEMM with in_norm equals
+    rmsnorm(x)*gamma @ W^T."""
+    H, N2 = 1024, 512
+    q, s = _qw(H, 768, 17)
+    x = _x(M, 768, 18)
+    r = torch.randn(M, H, device=DEV)
+    gamma = torch.rand(H, device=DEV) + 0.5
+    xg = torch.empty(M, H, dtype=torch.float16, device=DEV)
+    ssq = torch.empty(H // 128, M, device=DEV)
+    r_ref = r + _ref(x, q, s)
+    ops.w8a16_residual_(x, q, s, r, gamma_next=gamma, xg_out=xg, ssq_out=ssq)
+    assert (r - r_ref).abs().max().item() < 1e-3
+    assert (xg.float() - r_ref * gamma).abs().max().item() < 1e-2 * max(1.0, (r_ref * gamma).abs().max().item())
+    assert torch.allclose(ssq.sum(0), r_ref.pow(2).sum(-1), rtol=1e-4)
+    w2, s2 = _qw(N2, H, 19)
+    y = ops.w8a16_linear(xg, w2, s2, out_dtype=torch.float32, in_norm=(ssq, H, 1e-5))
+    h = r_ref * torch.rsqrt(r_ref.pow(2).mean(-1, keepdim=True) + 1e-5) * gamma
+    ref = _ref(h.half(), w2, s2)
+    assert (y - ref).abs().max().item() < 2e-2 * max(1.0, ref.abs().max().item())
+
+
+def test_norm_prep_matches_reference():
+    M, H = 7, 2048
+    x = torch.randn(M, H, device=DEV)
+    d = torch.randn(M, H, device=DEV)
+    g = torch.rand(H, device=DEV)
+    xg = torch.empty(M, H, dtype=torch.float16, device=DEV)
+    ssq = torch.empty(H // 128, M, device=DEV)
+    x2 = x.clone()
+    ops.norm_prep(x2, d, g, xg, ssq)
+    xr = x + d
+    assert torch.allclose(x2, xr)
+    assert (xg.float() - xr * g).abs().max().item() < 1e-2
+    assert torch.allclose(ssq, xr.view(M, H // 128, 128).pow(2).sum(-1).t(), rtol=1e-4)
+
+
+@pytest.mark.parametrize("M", [1, 16, 70, 165, 300])
 def test_w8a16_swiglu(M):
     F, K = 384, 512
     gq, gs = _qw(F, K, 9)
@@ -85,7 +123,7 @@ def test_w8a16_swiglu(M):
 
 
 @pytest.mark.parametrize("D", [64, 128])
-@pytest.mark.parametrize("M", [1, 7, 40])
+@pytest.mark.parametrize("M", [1, 7, 40, 165, 300])
 def test_w8a16_qkv_rope_append(D, M):
     from hrm_flashrenderer_b200.models.oracle import apply_rope, rope_tables
     from hrm_flashrenderer_b200.config import TINY

@@ -53,6 +53,23 @@ def test_gpu_engine_deterministic_and_graph_equals_eager():
     assert outs[0] == outs[1] == outs[2]
 
 
+def test_prefill_logits_identical_across_engine_instances():
+    """Two engines built one after the other in one process produce bitwise-identical prefill tokens and decode."""
+    cfg = SMALL
+    w = synth_weights(cfg, seed=1)
+    prompts = _prompts(5, 33, cfg.vocab, seed=2)
+    firsts = []
+    for _ in range(3):
+        model = LlamaW8.from_weights(cfg, w, device="cuda", max_pos=512)
+        eng = InferenceEngine(model, EngineConfig(max_seq_len=256, max_batch=8, use_cuda_graphs=False),
+                              num_blocks=128)
+        sids = [eng.new_seq() for _ in prompts]
+        firsts.append(eng.prefill(list(zip(sids, prompts))))
+        from hrm_flashrenderer_b200 import ops
+        ops.check_status()
+    assert firsts[0] == firsts[1] == firsts[2]
+
+
 def test_synthesize_on_device_shapes():
     cfg = replace(SMALL, layers=1)
     m = LlamaW8.synthesize(cfg, device="cuda")
