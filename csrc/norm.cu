@@ -145,28 +145,33 @@ __global__ void __launch_bounds__(256) norm_prep_kernel(float* __restrict__ x, c
                                                         float* __restrict__ ssq, int M, int H) {
   const int m = blockIdx.x;
   float* xr = x + (size_t)m * H;
-  for (int c0 = threadIdx.x * 32; c0 < H; c0 += blockDim.x * 32) {
+  // every thread runs the same number of iterations so the 4-lane shuffles below always see full warps
+  for (int base = 0; base < H; base += blockDim.x * 32) {
+    const int c0 = base + threadIdx.x * 32;
+    const bool act = c0 < H;   // H % 128 == 0: the 4 threads of one tile are all active or all idle
     float s = 0.f;
+    if (act) {
 #pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      float4 v = *reinterpret_cast<float4*>(xr + c0 + i);
-      if (delta) {
-        const float4 d = *reinterpret_cast<const float4*>(delta + (size_t)m * H + c0 + i);
-        v.x += d.x; v.y += d.y; v.z += d.z; v.w += d.w;
-        *reinterpret_cast<float4*>(xr + c0 + i) = v;
+      for (int i = 0; i < 32; i += 4) {
+        float4 v = *reinterpret_cast<float4*>(xr + c0 + i);
+        if (delta) {
+          const float4 d = *reinterpret_cast<const float4*>(delta + (size_t)m * H + c0 + i);
+          v.x += d.x; v.y += d.y; v.z += d.z; v.w += d.w;
+          *reinterpret_cast<float4*>(xr + c0 + i) = v;
+        }
+        s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        const float4 g = *reinterpret_cast<const float4*>(gamma + c0 + i);
+        __half2 a = __floats2half2_rn(v.x * g.x, v.y * g.y), b = __floats2half2_rn(v.z * g.z, v.w * g.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&a);
+        pk.y = *reinterpret_cast<uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(xg + (size_t)m * H + c0 + i) = pk;
       }
-      s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-      const float4 g = *reinterpret_cast<const float4*>(gamma + c0 + i);
-      __half2 a = __floats2half2_rn(v.x * g.x, v.y * g.y), b = __floats2half2_rn(v.z * g.z, v.w * g.w);
-      uint2 pk;
-      pk.x = *reinterpret_cast<uint32_t*>(&a);
-      pk.y = *reinterpret_cast<uint32_t*>(&b);
-      *reinterpret_cast<uint2*>(xg + (size_t)m * H + c0 + i) = pk;
     }
     // 4 consecutive threads cover one 128-column tile
     s += __shfl_xor_sync(0xffffffffu, s, 1);
     s += __shfl_xor_sync(0xffffffffu, s, 2);
-    if ((threadIdx.x & 3) == 0) ssq[(size_t)(c0 / 128) * M + m] = s;
+    if (act && (threadIdx.x & 3) == 0) ssq[(size_t)(c0 / 128) * M + m] = s;
   }
 }
 
