@@ -1,0 +1,231 @@
+"""HRM front layer + grounded renderer: retrieval picks the sources, a language model only renders a JSON answer
+from them, and every citation / quote is validated against the sources (extractive fallback otherwise).
+
+Reference: ``renderer/hrm_render.py:39-266`` (system prompt, SOURCES block with 1200-char snippets, strict JSON
+``{answer, citations, quotes:[{id, quote}]}``, exact-substring quote check, extractive fallback of 6 snippets with
+240-char quotes, ``hrm`` echo of cids/top_k/top_m/k, REPL).  The reference renders with a small GGUF model through
+llama-cpp-python; that package is optional here (``--llm model.gguf`` uses it when importable).  The B200 path is
+``--engine <model>``: the same greedy render on this library's GPU engine (``EngineBackend``, e.g.
+``synthetic:tiny`` or a DSI8 file).  Any renderer failure degrades to the extractive answer with an ``error`` field,
+as in the reference.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import subprocess
+from pathlib import Path
+from typing import Any, Callable, Dict, List, Optional, Tuple
+
+from .utils import find_hrm_binary
+
+SYSTEM_PROMPT = (
+    "You are a grounded renderer.\n"
+    "Use ONLY the provided SOURCES.\n"
+    "Return STRICT JSON with keys:\n"
+    "  answer (string), citations (list of snippet ids), quotes (list of {id,quote}).\n"
+    "Rules:\n"
+    "- Each quote MUST be an exact substring from the cited source.\n"
+    "- If you cannot answer from sources, say so in answer and keep citations/quotes minimal.\n"
+)
+MAX_SNIPPET_CHARS = 1200
+FALLBACK_SNIPPETS = 6
+FALLBACK_QUOTE_CHARS = 240
+
+
+def hrm_query(hrm_bin: str, model_dir: str, prompt: str, top_k: int = 5, top_m: int = 400, k: int = 8,
+              lam_num: int = 7, lam_den: int = 10, timeout_s: Optional[float] = 30.0) -> Dict[str, Any]:
+    cmd = [hrm_bin, "query", "--model", model_dir, "--format", "json", "--top-k", str(top_k), "--top-m", str(top_m),
+           "--k", str(k), "--lam-num", str(lam_num), "--lam-den", str(lam_den), "--prompt", prompt]
+    p = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout_s)
+    if p.returncode != 0:
+        raise RuntimeError(f"HRM query failed (code={p.returncode}): {p.stderr.strip()}")
+    try:
+        return json.loads(p.stdout)
+    except json.JSONDecodeError as e:
+        raise RuntimeError(f"HRM returned non-JSON: {p.stdout[:1000]}") from e
+
+
+def sources_block(chosen: List[Dict[str, Any]]) -> Tuple[str, Dict[str, str]]:
+    lines, src = ["[SOURCES]"], {}
+    for c in chosen:
+        sid, txt = str(c["sid"]), str(c.get("txt", ""))
+        if len(txt) > MAX_SNIPPET_CHARS:
+            txt = txt[:MAX_SNIPPET_CHARS].rstrip() + "…"
+        src[sid] = txt
+        lines.append(f"{sid}: {txt}")
+    lines.append("[/SOURCES]")
+    return "\n".join(lines), src
+
+
+def first_json_object(text: str) -> Dict[str, Any]:
+    """The first balanced ``{...}`` in ``text`` that parses (strings and escapes respected)."""
+    start = text.find("{")
+    while start >= 0:
+        depth, in_str, esc = 0, False, False
+        for i in range(start, len(text)):
+            ch = text[i]
+            if in_str:
+                if esc:
+                    esc = False
+                elif ch == "\\":
+                    esc = True
+                elif ch == '"':
+                    in_str = False
+            elif ch == '"':
+                in_str = True
+            elif ch == "{":
+                depth += 1
+            elif ch == "}":
+                depth -= 1
+                if depth == 0:
+                    try:
+                        obj = json.loads(text[start:i + 1])
+                        if isinstance(obj, dict):
+                            return obj
+                    except json.JSONDecodeError:
+                        pass
+                    break
+        start = text.find("{", start + 1)
+    raise ValueError("no json object found")
+
+
+def validate(obj: Any, sources: Dict[str, str]) -> Tuple[bool, str]:
+    if not isinstance(obj, dict):
+        return False, "not a dict"
+    if not isinstance(obj.get("answer"), str):
+        return False, "missing answer"
+    cits = obj.get("citations", [])
+    if not isinstance(cits, list):
+        return False, "citations not list"
+    for sid in cits:
+        if sid not in sources:
+            return False, f"unknown citation {sid}"
+    quotes = obj.get("quotes", [])
+    if not isinstance(quotes, list):
+        return False, "quotes not list"
+    for q in quotes:
+        if not isinstance(q, dict):
+            return False, "quote item not dict"
+        sid, qt = q.get("id"), q.get("quote")
+        if sid not in sources:
+            return False, f"quote id unknown {sid}"
+        if not isinstance(qt, str) or not qt.strip():
+            return False, f"empty quote for {sid}"
+        if qt not in sources[sid]:
+            return False, f"quote not substring for {sid}"
+    return True, "ok"
+
+
+def extractive_answer(chosen: List[Dict[str, Any]]) -> Dict[str, Any]:
+    take = chosen[:FALLBACK_SNIPPETS]
+    return {"answer": "\n".join(f"[{c['sid']}] {c.get('txt_c', c.get('txt', ''))}" for c in take),
+            "citations": [c["sid"] for c in take],
+            "quotes": [{"id": c["sid"], "quote": str(c.get("txt", ""))[:FALLBACK_QUOTE_CHARS]} for c in take],
+            "mode": "fallback_extractive"}
+
+
+def chat_prompt(system: str, user: str) -> str:
+    return f"<|system|>\n{system}\n<|user|>\n{user}\n<|assistant|>\n"
+
+
+def gguf_renderer(path: str, n_ctx: int = 4096, n_threads: int = 1, n_gpu_layers: int = 0) -> Callable[[str, int], str]:
+    from llama_cpp import Llama   # optional dependency
+    llm = Llama(model_path=path, n_ctx=n_ctx, n_threads=n_threads, n_gpu_layers=n_gpu_layers, seed=0,
+                logits_all=False, verbose=False)
+
+    def render(prompt: str, max_tokens: int) -> str:
+        out = llm(prompt, max_tokens=max_tokens, temperature=0.0, top_k=1, top_p=1.0, repeat_penalty=1.0,
+                  stop=["</s>", "<|user|>", "<|system|>"])
+        return out["choices"][0]["text"]
+    return render
+
+
+def engine_renderer(model_source: str, tokenizer: Optional[str] = None, device: str = "cuda:0"):
+    from .backend import EngineBackend
+    be = EngineBackend(model_source, tokenizer_source=tokenizer, device=device)
+
+    def render(prompt: str, max_tokens: int) -> str:
+        return be.generate(prompt, max_new_tokens=max_tokens)
+    return render
+
+
+def render_answer(prompt: str, hrm: Dict[str, Any], render: Optional[Callable[[str, int], str]], max_tokens: int = 256,
+                  top_k: int = 5, top_m: int = 400, k: int = 8) -> Dict[str, Any]:
+    chosen = hrm.get("chosen", [])
+    ctx, sources = sources_block(chosen)
+    user = f"{ctx}\n\nQUESTION:\n{prompt}\n\nReturn JSON now."
+    try:
+        if render is None:
+            raise RuntimeError("no renderer configured")
+        obj = first_json_object(render(chat_prompt(SYSTEM_PROMPT, user), max_tokens))
+        ok, why = validate(obj, sources)
+        if not ok:
+            obj = extractive_answer(chosen)
+            obj["error"] = f"validation_failed: {why}"
+    except Exception as e:
+        obj = extractive_answer(chosen)
+        obj["error"] = f"renderer_failed: {type(e).__name__}: {e}"
+    obj["hrm"] = {"cids": hrm.get("cids", []), "top_k": top_k, "top_m": top_m, "k": k}
+    return obj
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(prog="hrm-flash-render", description="HRM retrieval + grounded JSON renderer")
+    ap.add_argument("--hrm_bin", default=None)
+    ap.add_argument("--model", required=True, help="HRM model directory (router_index.bin + index.sqlite)")
+    ap.add_argument("--prompt", help="single prompt; without it a REPL starts")
+    g = ap.add_mutually_exclusive_group()
+    g.add_argument("--llm", help="local GGUF renderer model (needs llama-cpp-python)")
+    g.add_argument("--engine", help="render on this library's GPU engine (synthetic:<preset> or a DSI8 file)")
+    ap.add_argument("--tokenizer", default=None)
+    ap.add_argument("--device", default="cuda:0")
+    ap.add_argument("--top_k", type=int, default=5)
+    ap.add_argument("--top_m", type=int, default=400)
+    ap.add_argument("--k", type=int, default=8)
+    ap.add_argument("--lam_num", type=int, default=7)
+    ap.add_argument("--lam_den", type=int, default=10)
+    ap.add_argument("--max_tokens", type=int, default=256)
+    ap.add_argument("--n_ctx", type=int, default=4096)
+    ap.add_argument("--n_threads", type=int, default=1)
+    ap.add_argument("--n_gpu_layers", type=int, default=0)
+    ap.add_argument("--json", action="store_true", help="print the JSON object only")
+    a = ap.parse_args(argv)
+    hrm_bin = str(find_hrm_binary(explicit=a.hrm_bin))
+    if not Path(hrm_bin).is_file():
+        raise SystemExit(f"hrm binary not found: {hrm_bin} (build it with: make -C hrm_core)")
+    render = None
+    try:
+        if a.llm:
+            render = gguf_renderer(a.llm, a.n_ctx, a.n_threads, a.n_gpu_layers)
+        elif a.engine:
+            render = engine_renderer(a.engine, a.tokenizer, a.device)
+    except Exception as e:   # renderer unavailable -> every answer is extractive, with the reason
+        err = f"{type(e).__name__}: {e}"
+
+        def render(_p, _n, _err=err):
+            raise RuntimeError(_err)
+
+    def one(prompt: str) -> None:
+        hrm = hrm_query(hrm_bin, str(Path(a.model).resolve()), prompt, a.top_k, a.top_m, a.k, a.lam_num, a.lam_den)
+        obj = render_answer(prompt, hrm, render, a.max_tokens, a.top_k, a.top_m, a.k)
+        if not a.json:
+            print("\n[cids]", hrm.get("cids", []))
+        print(json.dumps(obj, ensure_ascii=False, sort_keys=True, indent=2), flush=True)
+
+    if a.prompt:
+        one(a.prompt)
+        return 0
+    print("HRM front REPL (deterministic retrieval + greedy renderer). Ctrl+C to exit.")
+    while True:
+        try:
+            p = input("\n> ").strip()
+        except (KeyboardInterrupt, EOFError):
+            print("\nbye")
+            return 0
+        if p:
+            one(p)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
