@@ -533,12 +533,15 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_con
       }
       if (it > 0) mbar_wait_ab(pvdone, (uint32_t)(it - 1) & 1u, status, kErrTimeoutAccum, abort_flag);
       tc_fence_after();
-      if (rescale && it > 0) {
+      // tcgen05.ld/st are warp-collective: the rescale runs for the whole warp whenever any of its rows needs it
+      // (rows that do not rescale multiply by 1).
+      if (__any_sync(0xffffffffu, rescale && it > 0)) {
+        const float cf = (rescale && it > 0) ? corr : 1.f;
         for (int c = 0; c < kD; c += 32) {
           float o[32];
           tmem_ld32(tO + lane_off + (uint32_t)c, o);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= corr;
+          for (int i = 0; i < 32; ++i) o[i] *= cf;
           tmem_st32(tO + lane_off + (uint32_t)c, o);
         }
       }

@@ -38,14 +38,23 @@ hrm::GemmArgs base_args(const at::Tensor& x, const at::Tensor& w, const at::Tens
                         const c10::optional<at::Tensor>& status = c10::nullopt) {
   CHECK_CUDA(x); CHECK_CUDA(w); CHECK_CUDA(scale);
   CHECK_DTYPE(x, at::kHalf); CHECK_DTYPE(w, at::kChar); CHECK_DTYPE(scale, at::kFloat);
-  TORCH_CHECK(x.dim() == 2 && w.dim() == 2, "x [M,K] and w [N,K] must be 2-D");
-  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "inner dims must be contiguous");
-  TORCH_CHECK(x.size(1) == w.size(1), "K mismatch: x ", x.size(1), " vs w ", w.size(1));
-  TORCH_CHECK(w.stride(0) == w.size(1), "w must be row-major contiguous");
-  TORCH_CHECK(scale.numel() == w.size(0), "scale must have N entries");
+  TORCH_CHECK(x.dim() == 2, "x [M,K] must be 2-D");
+  TORCH_CHECK(x.stride(1) == 1, "x inner dim must be contiguous");
   hrm::GemmArgs a{};
+  if (w.dim() == 3) {   // pre-tiled [ceil(N/128)][K/64][8192]
+    TORCH_CHECK(w.is_contiguous() && w.size(2) == 8192, "tiled w must be contiguous [N/128, K/64, 8192]");
+    TORCH_CHECK(w.size(1) * 64 == x.size(1), "K mismatch: x ", x.size(1), " vs tiled w ", w.size(1) * 64);
+    TORCH_CHECK(w.size(0) == (scale.numel() + 127) / 128, "tiled w row tiles do not match scale (N entries)");
+    a.N = (int)scale.numel();
+    a.w_tiles = w.data_ptr<int8_t>();
+  } else {
+    TORCH_CHECK(w.dim() == 2 && w.stride(1) == 1, "w must be [N,K] with contiguous rows (or pre-tiled 3-D)");
+    TORCH_CHECK(x.size(1) == w.size(1), "K mismatch: x ", x.size(1), " vs w ", w.size(1));
+    TORCH_CHECK(w.stride(0) == w.size(1), "w must be row-major contiguous");
+    TORCH_CHECK(scale.numel() == w.size(0), "scale must have N entries");
+    a.N = (int)w.size(0);
+  }
   a.M = (int)x.size(0);
-  a.N = (int)w.size(0);
   a.K = (int)x.size(1);
   a.scale = scale.data_ptr<float>();
   if (bias.has_value() && bias->defined()) {
@@ -64,7 +73,7 @@ hrm::GemmArgs base_args(const at::Tensor& x, const at::Tensor& w, const at::Tens
 
 std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K, int64_t force_ctas) {
   auto p = hrm::gemm_plan((int)M, (int)N, (int)K, (int)force_ctas);
-  return {p.bn, p.n_tiles, p.m_tiles, p.k_tiles, p.splits, (int64_t)p.ws_floats, p.counters};
+  return {p.bn, p.n_tiles, p.m_tiles, p.k_tiles, p.splits, (int64_t)p.ws_floats, p.counters, p.ku};
 }
 
 // out = x @ (w * scale)^T (+ bias): out dtype f16 or f32 (preallocated [M, >=N] row-major).
@@ -108,14 +117,14 @@ void w8a16_gemm_residual(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tenso
   if (xg_out.has_value() && xg_out->defined()) {
     TORCH_CHECK(gamma_next.has_value() && gamma_next->defined(), "xg_out needs gamma_next");
     CHECK_DTYPE((*xg_out), at::kHalf); CHECK_DTYPE((*gamma_next), at::kFloat);
-    TORCH_CHECK(xg_out->stride(1) == 1 && gamma_next->numel() == w.size(0), "bad xg_out / gamma_next");
+    TORCH_CHECK(xg_out->stride(1) == 1 && gamma_next->numel() == a.N, "bad xg_out / gamma_next");
     a.xg_out = reinterpret_cast<__half*>(xg_out->data_ptr());
     a.ldxg = (int)xg_out->stride(0);
     a.gamma_next = gamma_next->data_ptr<float>();
   }
   if (ssq_out.has_value() && ssq_out->defined()) {
     CHECK_DTYPE((*ssq_out), at::kFloat);
-    TORCH_CHECK(ssq_out->numel() >= (int64_t)((w.size(0) + 127) / 128) * x.size(0), "ssq_out too small");
+    TORCH_CHECK(ssq_out->numel() >= (int64_t)((a.N + 127) / 128) * x.size(0), "ssq_out too small");
     a.ssq_out = ssq_out->data_ptr<float>();
   }
   if (a.M == 0) return;
@@ -371,7 +380,7 @@ void decode_advance(at::Tensor tokens, at::Tensor ids, at::Tensor positions, c10
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of hrm_flashrenderer_b200";
-  m.def("gemm_plan", &gemm_plan_py, "split-K plan: (bn, n_tiles, m_tiles, k_tiles, splits, ws_floats, counters)");
+  m.def("gemm_plan", &gemm_plan_py, "stream-K plan: (bn, n_tiles, m_tiles, units per tile, splits, ws_floats, counters, k-tiles per unit)");
   m.def("w8a16_gemm", &w8a16_gemm, py::arg("x"), py::arg("w"), py::arg("scale"), py::arg("bias"), py::arg("out"),
         py::arg("ws"), py::arg("counters"), py::arg("force_ctas") = 0, py::arg("in_ssq") = py::none(),
         py::arg("inv_h") = 0.0, py::arg("eps") = 0.0);
@@ -403,6 +412,27 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_prepare", &decode_prepare_bs);
   m.def("decode_advance", &decode_advance);
   m.def("sm_count", []() { return hrm::gemm_sm_count(); });
+  m.def("pho_score", [](at::Tensor rec_ids, at::Tensor rec_len, at::Tensor q, at::Tensor scores) {
+    c10::cuda::CUDAGuard g(rec_ids.device());
+    TORCH_CHECK(rec_ids.is_cuda() && rec_ids.scalar_type() == at::kInt && rec_ids.dim() == 2 && rec_ids.size(1) == 8 &&
+                    rec_ids.is_contiguous(), "rec_ids: int32 [n, 8] contiguous on the GPU");
+    TORCH_CHECK(rec_len.scalar_type() == at::kInt && rec_len.numel() == rec_ids.size(0), "rec_len: int32 [n]");
+    TORCH_CHECK(q.scalar_type() == at::kInt && q.is_cuda() && q.numel() <= 32, "q: int32 [<= 32] on the GPU");
+    TORCH_CHECK(scores.scalar_type() == at::kFloat && scores.numel() == rec_ids.size(0), "scores: f32 [n]");
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(rec_ids.data_ptr()) & 15) == 0, "rec_ids must be 16-byte aligned");
+    hrm::pho_score_launch(reinterpret_cast<const uint32_t*>(rec_ids.data_ptr<int>()),
+                          reinterpret_cast<const uint32_t*>(rec_len.data_ptr<int>()),
+                          reinterpret_cast<const uint32_t*>(q.data_ptr<int>()), (int)q.numel(),
+                          scores.data_ptr<float>(), rec_ids.size(0), hrm::gemm_sm_count(), cur_stream());
+  });
+  m.def("set_gemm_trace", [](c10::optional<at::Tensor> t) {
+    if (t.has_value() && t->defined()) {
+      TORCH_CHECK(t->scalar_type() == at::kLong && t->numel() >= 12 * hrm::kGemmTraceLen, "trace: int64[12*1024]");
+      hrm::set_gemm_trace(reinterpret_cast<long long*>(t->data_ptr<int64_t>()));
+    } else {
+      hrm::set_gemm_trace(nullptr);
+    }
+  });
   m.def("set_status_word", [](at::Tensor t) {
     TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kInt, "status word must be a CUDA int32 tensor");
     hrm::set_status_word(t.device().index(), t.data_ptr<int>());

@@ -11,11 +11,15 @@
 //    streams the same number of weight bytes whatever the tile count.  A tile cut between CTAs is a set of k-segments
 //    whose fp32 partials go to a caller-provided workspace; the last segment to finish (atomic ticket) sums them in
 //    k order, so results are bitwise deterministic whatever the scheduling.
-//  * warp 0: TMA producer.  Raw int8 weight tiles [128 x 64] (64-byte swizzle) and the f16 activation tile [BN x 64]
-//    (128-byte swizzle, canonical K-major UMMA layout) stream through a deep ring (R slots), across segment and
-//    tile boundaries, so HBM sees a continuous stream.
-//  * warps 2-9: dequant int8 -> f16 exactly (prmt + f16x2 subtract) into a shorter ring of 128-byte-swizzled A tiles,
-//    as 4 independent 2-warp groups taking alternate k-tiles; the per-row scale is applied once in the epilogue.
+//  * warp 0: TMA producer.  Raw int8 weight tiles [128 x 64] (64-byte swizzle) stream through a deep ring that the
+//    dequant warps release as soon as a tile is in registers; the f16 activation tile [BN x 64] (128-byte swizzle,
+//    canonical K-major UMMA layout) has its own ring released by the MMA.  Both rings run across segment and tile
+//    boundaries, so HBM sees a continuous stream.
+//  * warps 2-9: dequant int8 -> f16 exactly (prmt + f16x2 subtract); the per-row scale is applied once in the
+//    epilogue.  Decode widths (BN <= 128) write the f16 A tile straight into tensor memory (tcgen05.st, thread =
+//    row = TMEM lane) and the MMA reads A from TMEM: shared memory then carries 2 bytes per weight byte instead of 6,
+//    which is what bounds a weight-streaming GEMM.  The prefill width (BN = 256) keeps A in 128-byte-swizzled
+//    shared memory.
 //  * warp 1: one thread issues tcgen05.mma (kind::f16, fp32 accumulate) into one of two TMEM accumulators and
 //    tcgen05.commit releases ring slots / publishes a finished accumulator.
 //  * warps 10-13: epilogue (thread = TMEM lane = weight row), overlapped with the next segment's mainloop: plain
@@ -28,6 +32,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -42,37 +47,96 @@ constexpr int kFirstDqWarp = 2;
 constexpr int kFirstEpiWarp = kFirstDqWarp + kDqWarps;
 constexpr int kThreads = (kFirstEpiWarp + kEpiWarps) * 32;   // 448
 constexpr int kDqThreads = kDqWarps * 32;
-constexpr int kDqGroups = 4;                   // independent dequant groups (2 warps each)
-constexpr int kDqGroupThreads = kDqThreads / kDqGroups;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kWrawBytes = kBM * kBK;          // int8 tile, 8 KB
 constexpr int kW16Bytes = kBM * kBK * 2;       // f16 tile, 16 KB
 constexpr int kChunk = 16;                     // epilogue columns per TMEM load
 
-template <int BN> struct GemmCfg;   // raw ring depth R, f16 ring depth F
-template <> struct GemmCfg<16>  { static constexpr int R = 12, F = 4; };
-template <> struct GemmCfg<32>  { static constexpr int R = 10, F = 4; };
-template <> struct GemmCfg<64>  { static constexpr int R = 8, F = 4; };
-template <> struct GemmCfg<128> { static constexpr int R = 5, F = 4; };
-template <> struct GemmCfg<256> { static constexpr int R = 3, F = 4; };
+// Pipeline shape per token-tile width BN.
+//  TS (BN <= 128, decode): dequantised A tiles go to tensor memory and the MMA reads A from TMEM; 2 dequant groups of
+//    4 warps, thread = weight row (= TMEM lane).  With pre-tiled weights the dequant threads stream W straight from
+//    HBM into registers; with plain row-major weights W goes through a TMA ring in shared memory.
+//  SS (BN = 256, prefill): A tiles in shared memory (F stages of 16 KB, 128-byte swizzle); 4 dequant groups of
+//    2 warps.  Here the MMA time per tile hides the extra shared-memory traffic.
+// KU: 64-wide k-tiles per pipeline unit.  At decode widths every per-unit step (barrier waits, commits, TMA issue)
+// costs hundreds of cycles, so units of KU k-tiles (KU x 8 KB of weights, KU x 4 MMAs) amortise them; the launcher
+// picks ku = KU, or 2 / 1 when K/64 is not a multiple of KU.
+// RW: raw weight ring (units), released by its dequant group once the unit is in registers.  RX: activation ring
+// (units), released by the MMA.  F: A stages (units).  RW and F are multiples of the group count, so every slot of
+// those rings is always consumed by the same group, in order: no waiter can ever mistake a phase two generations
+// old for the one it waits for.
+// NACC: independent partial accumulators per output tile, summed in the epilogue.
+template <int BN> struct GemmCfg;
+template <> struct GemmCfg<16>  { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 2, RX = 8, F = 2, NACC = 4; };
+template <> struct GemmCfg<32>  { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 2, RX = 5, F = 2, NACC = 4; };
+template <> struct GemmCfg<64>  { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 2, RX = 3, F = 2, NACC = 2; };
+template <> struct GemmCfg<128> { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 2, RX = 2, F = 2, NACC = 1; };
+template <> struct GemmCfg<256> { static constexpr bool TS = false; static constexpr int KU = 1, RW = 4, RX = 3, F = 4, NACC = 1; };
 
 template <int BN>
 struct GemmSmem {
-  static constexpr int R = GemmCfg<BN>::R, F = GemmCfg<BN>::F;
-  static constexpr int kXBytes = BN * kBK * 2;
-  static constexpr int kW16Off = 0;
-  static constexpr int kXOff = kW16Off + F * kW16Bytes;
-  static constexpr int kWrawOff = kXOff + R * kXBytes;
-  static constexpr int kStageOff = kWrawOff + R * kWrawBytes;          // [16 cols][128 rows] fp32 = 8 KB
+  static constexpr bool TS = GemmCfg<BN>::TS;
+  static constexpr int KU = GemmCfg<BN>::KU;
+  static constexpr int RW = GemmCfg<BN>::RW, RX = GemmCfg<BN>::RX, F = GemmCfg<BN>::F;
+  static constexpr int NACC = GemmCfg<BN>::NACC;
+  static constexpr int kAccCols = NACC * BN;                            // one accumulator buffer (NACC partials)
+  static constexpr int NG = TS ? 2 : 4;                                // dequant groups
+  static constexpr int kGroupThreads = kDqThreads / NG;
+  static constexpr int kXSub = BN * kBK * 2;                           // one k-tile of activations
+  static constexpr int kXSlot = KU * kXSub;
+  static constexpr int kWSlot = KU * kWrawBytes;
+  static constexpr int kW16Off = 0;                                    // SS only: F x 16 KB
+  static constexpr int kXOff = kW16Off + (TS ? 0 : F * kW16Bytes);
+  static constexpr int kWrawOff = kXOff + RX * kXSlot;
+  static constexpr int kStageOff = kWrawOff + RW * kWSlot;             // [16 cols][128 rows] fp32 = 8 KB
   static constexpr int kInvOff = kStageOff + kChunk * kBM * 4;         // [BN] per-token input row scale
   static constexpr int kSsqOff = kInvOff + BN * 4;                     // [4 warps][16] partial sums of squares
   static constexpr int kBarOff = kSsqOff + kEpiWarps * kChunk * 4;
-  static constexpr int kNumBars = 2 * R + 2 * F + 5;
+  static constexpr int kNumBars = 2 * RW + 2 * RX + 2 * F + 5;
   static constexpr int kBytes = kBarOff + kNumBars * 8 + 32;
   static constexpr int kAlloc = kBytes + 1024;
-  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int kAcol = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;  // first TMEM column of the A stages (TS)
+  static constexpr int kAStageCols = KU * 32;
+  static constexpr int kTmemCols = 512;
   static_assert(kAlloc <= 227 * 1024, "shared memory budget exceeded");
+  static_assert(RW % NG == 0 && F % NG == 0, "ring depths must be multiples of the dequant group count");
+  static_assert(!TS || kAcol + F * kAStageCols <= kTmemCols, "TMEM budget exceeded");
+  static_assert(TS || (2 * kAccCols <= kTmemCols && KU == 1), "SS path: TMEM budget / unit size");
+  static_assert(NACC == 1 || NACC == 2 || NACC == 4, "NACC must divide the 4 MMAs of a k-tile");
 };
+
+// Pipeline trace for performance analysis: clock64 of CTA 0 at each stage of unit i (points listed at the call
+// sites: 0 load issued, 1 raw tile landed, 2 A stage free, 3 dequant done, 4 MMA operands ready, 5/6 epilogue
+// start/end of segment i, 7 kernel start/end).  Off (a.trace == nullptr) in normal launches.
+HRM_DEVINL void trace_mark(const GemmArgs& a, int point, int64_t i) {
+  if (a.trace != nullptr && blockIdx.x == 0 && i < kGemmTraceLen) a.trace[point * kGemmTraceLen + i] = clock64();
+}
+
+// 16 accumulator columns summed over the NACC partial accumulators (NACC loads in flight, one wait).
+template <int BN, int NACC>
+HRM_DEVINL void tmem_ld_acc(uint32_t taddr, float (&v)[16]) {
+  if constexpr (NACC == 1) {
+    tmem_ld16(taddr, v);
+  } else {
+    uint32_t r[NACC][16];
+#pragma unroll
+    for (int j = 0; j < NACC; ++j)
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+          : "=r"(r[j][0]), "=r"(r[j][1]), "=r"(r[j][2]), "=r"(r[j][3]), "=r"(r[j][4]), "=r"(r[j][5]),
+            "=r"(r[j][6]), "=r"(r[j][7]), "=r"(r[j][8]), "=r"(r[j][9]), "=r"(r[j][10]), "=r"(r[j][11]),
+            "=r"(r[j][12]), "=r"(r[j][13]), "=r"(r[j][14]), "=r"(r[j][15])
+          : "r"(taddr + (uint32_t)(j * BN)));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float acc = __uint_as_float(r[0][i]);
+#pragma unroll
+      for (int j = 1; j < NACC; ++j) acc += __uint_as_float(r[j][i]);
+      v[i] = acc;
+    }
+  }
+}
 
 // ------------------------------------------------------------------ stream-K partition helpers (device + host)
 HRM_DEVINL int64_t unit_start(int64_t c, int64_t U, int64_t G) { return (c * U) / G; }
@@ -295,7 +359,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                   const GemmArgs a) {
   using S = GemmSmem<BN>;
-  constexpr int R = S::R, F = S::F;
+  constexpr int RW = S::RW, RX = S::RX, F = S::F, NG = S::NG;
+  constexpr bool TS = S::TS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* w16 = base + S::kW16Off;
@@ -304,10 +369,12 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
   float* stage = reinterpret_cast<float*>(base + S::kStageOff);
   float* inv = reinterpret_cast<float*>(base + S::kInvOff);
   float* ssq_red = reinterpret_cast<float*>(base + S::kSsqOff);
-  uint64_t* rfull = reinterpret_cast<uint64_t*>(base + S::kBarOff);
-  uint64_t* rempty = rfull + R;
-  uint64_t* ffull = rempty + R;
-  uint64_t* fempty = ffull + F;
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(base + S::kBarOff);   // [RW] raw weight tile landed (TMA)
+  uint64_t* wempty = wfull + RW;                                      // [RW] raw tile read by its dequant group
+  uint64_t* xfull = wempty + RW;                                      // [RX] activation tile landed (TMA)
+  uint64_t* xempty = xfull + RX;                                      // [RX] activation tile consumed (MMA)
+  uint64_t* ffull = xempty + RX;                                      // [F] A stage written (dequant)
+  uint64_t* fempty = ffull + F;                                       // [F] A stage consumed (MMA)
   uint64_t* afull = fempty + F;      // [2] accumulator ready (MMA -> epilogue)
   uint64_t* aempty = afull + 2;      // [2] accumulator drained (epilogue -> MMA)
   uint64_t* mdone = aempty + 2;      // all MMAs of this CTA complete (drain before TMEM is freed)
@@ -321,14 +388,19 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
   const int64_t G = gridDim.x;
   const int64_t U = (int64_t)a.tiles * a.k_tiles;
   const int64_t u0 = unit_start(blockIdx.x, U, G), u1 = unit_start(blockIdx.x + 1, U, G);
+  if (threadIdx.x == 0) trace_mark(a, 7, 0);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < R; ++s) {
-      mbar_init(&rfull[s], 1);
-      mbar_init(&rempty[s], 1);
+    for (int s = 0; s < RW; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], S::kGroupThreads);
+    }
+    for (int s = 0; s < RX; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);
     }
     for (int s = 0; s < F; ++s) {
-      mbar_init(&ffull[s], kDqGroupThreads);
+      mbar_init(&ffull[s], S::kGroupThreads);
       mbar_init(&fempty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
@@ -348,26 +420,55 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int ku = a.ku;                       // k-tiles per unit (<= KU)
+  const int kt_total = a.k_tiles * ku;       // 64-wide k-tiles per output tile
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      tma_prefetch_desc(&tmW);
+      if (a.w_tiles == nullptr) tma_prefetch_desc(&tmW);
       tma_prefetch_desc(&tmX);
-      int64_t i = 0;
-      for (int64_t u = u0; u < u1; ++u, ++i) {
-        const int tile = (int)(u / a.k_tiles), kt = (int)(u % a.k_tiles);
-        const int n_tile = tile % a.n_tiles, m_tile = tile / a.n_tiles;
-        const int s = (int)(i % R);
-        const uint32_t ph = (uint32_t)(i / R) & 1u;
-        if (!mbar_wait_ab(&rempty[s], ph ^ 1u, a.status, kErrTimeoutEmpty, abort_flag)) break;
-        mbar_arrive_expect_tx(&rfull[s], kWrawBytes + S::kXBytes);
-        tma_load_2d(wraw + s * kWrawBytes, &tmW, &rfull[s], kt * kBK, n_tile * kBM);
-        tma_load_2d(xs + s * S::kXBytes, &tmX, &rfull[s], kt * kBK, m_tile * BN);
+      int64_t nw = 0, nx = 0;   // units issued into each ring
+      // (n-tile, m-tile, unit-within-tile) of the current unit, advanced incrementally (no divisions in the loop)
+      const int tile0 = (int)(u0 / a.k_tiles);
+      int kt = (int)(u0 % a.k_tiles);
+      int n_tile = tile0 % a.n_tiles, m_tile = tile0 / a.n_tiles;
+      int sw = 0, sx = 0;
+      uint32_t pw = 1u, px = 1u;   // producer-side parities of the empty barriers (first pass: free)
+      // decode widths with pre-tiled weights stream W straight into the dequant warps' registers: no W ring
+      const bool w_ring = !(TS && a.w_tiles != nullptr);
+      for (int64_t u = u0; u < u1; ++u) {
+        const int64_t i = u - u0;
+        trace_mark(a, 0, i);
+        if (w_ring) {
+          if (!mbar_wait_ab(&wempty[sw], pw, a.status, kErrTimeoutEmpty, abort_flag)) break;
+          mbar_arrive_expect_tx(&wfull[sw], (uint32_t)(ku * kWrawBytes));
+          uint8_t* dst = wraw + sw * S::kWSlot;
+          if (a.w_tiles != nullptr) {
+            bulk_load(dst, a.w_tiles + ((size_t)n_tile * kt_total + (size_t)kt * ku) * kWrawBytes,
+                      (uint32_t)(ku * kWrawBytes), &wfull[sw]);
+          } else {
+            for (int j = 0; j < ku; ++j)
+              tma_load_2d(dst + j * kWrawBytes, &tmW, &wfull[sw], (kt * ku + j) * kBK, n_tile * kBM);
+          }
+          nw = i + 1;
+        }
+        if (!mbar_wait_ab(&xempty[sx], px, a.status, kErrTimeoutEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(&xfull[sx], (uint32_t)(ku * S::kXSub));
+        tma_load_3d(xs + sx * S::kXSlot, &tmX, &xfull[sx], 0, m_tile * BN, kt * ku);
+        nx = i + 1;
+        if (++sw == RW) { sw = 0; pw ^= 1u; }
+        if (++sx == RX) { sx = 0; px ^= 1u; }
+        if (++kt == a.k_tiles) {
+          kt = 0;
+          if (++n_tile == a.n_tiles) { n_tile = 0; ++m_tile; }
+        }
       }
-      // drain: the last R issued loads must have landed before exit
-      for (int64_t j = (i > R ? i - R : 0); j < i; ++j)
-        mbar_wait(&rfull[j % R], (uint32_t)(j / R) & 1u, a.status, kErrTimeoutFull);
+      // drain: every issued load must have landed before exit (earlier ones were consumed, hence landed)
+      for (int64_t j = (nw > RW ? nw - RW : 0); j < nw; ++j)
+        mbar_wait(&wfull[j % RW], (uint32_t)(j / RW) & 1u, a.status, kErrTimeoutFull);
+      for (int64_t j = (nx > RX ? nx - RX : 0); j < nx; ++j)
+        mbar_wait(&xfull[j % RX], (uint32_t)(j / RX) & 1u, a.status, kErrTimeoutFull);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -381,22 +482,32 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
         const int64_t tile_end = (int64_t)(tile + 1) * a.k_tiles;
         const int64_t ue = tile_end < u1 ? tile_end : u1;
         const int acc = seg & 1;
-        const uint32_t acc_addr = tmem + (uint32_t)(acc * BN);
+        const uint32_t acc_addr = tmem + (uint32_t)(acc * S::kAccCols);
         ok = mbar_wait_ab(&aempty[acc], ((uint32_t)(seg >> 1) & 1u) ^ 1u, a.status, kErrTimeoutAccum, abort_flag);
         tc_fence_after();
         for (int64_t k = u; ok && k < ue; ++k, ++i) {
-          const int r = (int)(i % R), f = (int)(i % F);
-          ok = mbar_wait_ab(&rfull[r], (uint32_t)(i / R) & 1u, a.status, kErrTimeoutFull, abort_flag) &&
+          const int sx = (int)(i % RX), f = (int)(i % F);
+          ok = mbar_wait_ab(&xfull[sx], (uint32_t)(i / RX) & 1u, a.status, kErrTimeoutFull, abort_flag) &&
                mbar_wait_ab(&ffull[f], (uint32_t)(i / F) & 1u, a.status, kErrTimeoutDequant, abort_flag);
           if (!ok) break;
+          trace_mark(a, 4, i);
           tc_fence_after();
-          const uint32_t a0 = smem_u32(w16 + f * kW16Bytes);
-          const uint32_t b0 = smem_u32(xs + r * S::kXBytes);
+          const uint32_t b0 = smem_u32(xs + sx * S::kXSlot);
+          for (int j = 0; j < ku; ++j) {
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_f16_ss(acc_addr, sdesc_sw128(a0 + kk * 32), sdesc_sw128(b0 + kk * 32), idesc,
-                        (k > u || kk > 0) ? 1u : 0u);
-          umma_commit(&rempty[r]);
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const int q = j * (kBK / 16) + kk;   // 16-wide K step within the unit
+              const uint32_t d = acc_addr + (uint32_t)((q % S::NACC) * BN);
+              const uint32_t en = (k > u || q >= S::NACC) ? 1u : 0u;
+              const uint64_t bd = sdesc_sw128(b0 + (uint32_t)(j * S::kXSub + kk * 32));
+              if constexpr (TS) {
+                umma_f16_ts(d, tmem + (uint32_t)(S::kAcol + f * S::kAStageCols + j * 32 + kk * 8), bd, idesc, en);
+              } else {
+                umma_f16_ss(d, sdesc_sw128(smem_u32(w16 + f * kW16Bytes) + kk * 32), bd, idesc, en);
+              }
+            }
+          }
+          umma_commit(&xempty[sx]);
           umma_commit(&fempty[f]);
         }
         umma_commit(&afull[acc]);
@@ -407,34 +518,143 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
     }
   } else if (warp < kFirstEpiWarp) {
     // ------------------------------------------------------------------ dequant
-    // 4 independent groups of 2 warps; group g converts k-tiles i = g, g+4, ... so four tiles are in conversion
-    // at once and one tile's latency (smem round trip, proxy fence, barrier) never stalls the stream.
-    const int t = threadIdx.x - kFirstDqWarp * 32;   // 0..255
-    const int g = t >> 6;                             // group 0..3
-    const int gt = t & 63;                            // thread within group: rows gt and gt + 64
+    // NG independent groups take alternate units (group g: units i = g, g + NG, ...); int8 -> f16 is exact
+    // (prmt + f16x2 subtract); the per-row scale is applied once in the epilogue.
     const int64_t n_units = u1 - u0;
-    for (int64_t i = g; i < n_units; i += kDqGroups) {
-      const int rs = (int)(i % R), fs = (int)(i % F);
-      if (!mbar_wait_ab(&rfull[rs], (uint32_t)(i / R) & 1u, a.status, kErrTimeoutFull, abort_flag)) break;
-      if (!mbar_wait_ab(&fempty[fs], ((uint32_t)(i / F) & 1u) ^ 1u, a.status, kErrTimeoutEmpty, abort_flag)) break;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int r = gt + half * 64;
-        const int sw64 = (r >> 1) & 3, sw128 = r & 7;
-        const uint8_t* src = wraw + rs * kWrawBytes + r * 64;
-        uint8_t* dst = w16 + fs * kW16Bytes + r * 128;
+    if constexpr (TS) {
+      const int dw = warp - kFirstDqWarp;   // 0..7
+      const int g = dw >> 2;                // group 0..1 (4 consecutive warps cover the 4 TMEM lane quarters)
+      const int quad = warp & 3;
+      const int r = quad * 32 + lane;       // weight row = TMEM lane
+      const bool tracer = lane == 0 && (dw & 3) == 0;
+      const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)S::kAcol;
+      auto to_f16 = [](const uint4 (&v)[4], uint32_t (&o)[32]) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const uint4 v = *reinterpret_cast<const uint4*>(src + ((c ^ sw64) << 4));
-          uint4 o;
-          i8x4_to_f16x4(v.x, o.x, o.y); i8x4_to_f16x4(v.y, o.z, o.w);
-          *reinterpret_cast<uint4*>(dst + (((2 * c) ^ sw128) << 4)) = o;
-          i8x4_to_f16x4(v.z, o.x, o.y); i8x4_to_f16x4(v.w, o.z, o.w);
-          *reinterpret_cast<uint4*>(dst + (((2 * c + 1) ^ sw128) << 4)) = o;
+          i8x4_to_f16x4(v[c].x, o[8 * c + 0], o[8 * c + 1]);
+          i8x4_to_f16x4(v[c].y, o[8 * c + 2], o[8 * c + 3]);
+          i8x4_to_f16x4(v[c].z, o[8 * c + 4], o[8 * c + 5]);
+          i8x4_to_f16x4(v[c].w, o[8 * c + 6], o[8 * c + 7]);
+        }
+      };
+      if (a.w_tiles != nullptr) {
+        // Streaming: each thread loads its row's 64 bytes of every k-tile straight from HBM (chunk-major tiles: a
+        // warp's 16-byte loads cover 512 contiguous bytes), one unit (ku k-tiles) ahead of the conversion, so every
+        // SM keeps 256 threads x ku x 64 B of weights in flight without a shared-memory stage.
+        const uint8_t* wt = reinterpret_cast<const uint8_t*>(a.w_tiles) + r * 16;
+        int64_t nl = g;                                  // next unit to load
+        int lk = 0, ln = 0;                              // its (unit within tile, n-tile)
+        if (u0 + g < u1) {
+          const int64_t uu = u0 + g;
+          lk = (int)(uu % a.k_tiles);
+          ln = (int)((uu / a.k_tiles) % a.n_tiles);
+        }
+        uint4 buf[S::KU][4];
+        auto load_sub = [&](uint4 (&v)[4], int j) {      // k-tile j of unit nl
+          const uint8_t* p = wt + ((size_t)ln * kt_total + (size_t)lk * ku + j) * kWrawBytes;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) v[c] = ldg_stream(p + c * 2048);
+        };
+        auto advance = [&]() {
+          nl += NG;
+          lk += NG;
+          while (lk >= a.k_tiles) {
+            lk -= a.k_tiles;
+            if (++ln == a.n_tiles) ln = 0;
+          }
+        };
+        if (nl < n_units) {
+#pragma unroll
+          for (int j = 0; j < S::KU; ++j)
+            if (j < ku) load_sub(buf[j], j);
+        }
+        advance();
+        for (int64_t i = g; i < n_units; i += NG) {
+          const int f = (int)(i % F);
+          if (!mbar_wait_ab(&fempty[f], ((uint32_t)(i / F) & 1u) ^ 1u, a.status, kErrTimeoutEmpty, abort_flag)) break;
+          if (tracer) trace_mark(a, 2, i);
+          tc_fence_after();
+          const bool more = nl < n_units;
+#pragma unroll
+          for (int j = 0; j < S::KU; ++j) {
+            if (j < ku) {
+              uint32_t o[32];
+              to_f16(buf[j], o);
+              if (more) load_sub(buf[j], j);              // next unit of this group, same k-tile slot
+              tmem_st32u(tl + (uint32_t)(f * S::kAStageCols + j * 32), o);
+            }
+          }
+          advance();
+          tc_fence_before();
+          mbar_arrive_relaxed(&ffull[f]);                 // keeps this thread's prefetch loads in flight
+          if (tracer) trace_mark(a, 3, i);
+        }
+      } else {
+        const int sw64 = (r >> 1) & 3;
+        for (int64_t i = g; i < n_units; i += NG) {
+          const int sw = (int)(i % RW), f = (int)(i % F);
+          if (!mbar_wait_ab(&wfull[sw], (uint32_t)(i / RW) & 1u, a.status, kErrTimeoutFull, abort_flag)) break;
+          if (tracer) trace_mark(a, 1, i);
+          if (!mbar_wait_ab(&fempty[f], ((uint32_t)(i / F) & 1u) ^ 1u, a.status, kErrTimeoutEmpty, abort_flag)) break;
+          if (tracer) trace_mark(a, 2, i);
+          tc_fence_after();
+          for (int j = 0; j < ku; ++j) {
+            const uint8_t* src = wraw + sw * S::kWSlot + j * kWrawBytes + r * 64;
+            uint4 v[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) v[c] = *reinterpret_cast<const uint4*>(src + ((c ^ sw64) << 4));
+            uint32_t o[32];
+            to_f16(v, o);
+            tmem_st32u(tl + (uint32_t)(f * S::kAStageCols + j * 32), o);
+          }
+          mbar_arrive(&wempty[sw]);
+          tc_fence_before();
+          mbar_arrive(&ffull[f]);
+          if (tracer) trace_mark(a, 3, i);
         }
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&ffull[fs]);
+    } else {
+      const int t = threadIdx.x - kFirstDqWarp * 32;   // 0..255
+      const int g = t >> 6;                             // group 0..3
+      const int gt = t & 63;                            // thread within group: rows gt and gt + 64
+      const bool tiled = a.w_tiles != nullptr;
+      for (int64_t i = g; i < n_units; i += NG) {
+        const int sw = (int)(i % RW), f = (int)(i % F);
+        if (!mbar_wait_ab(&wfull[sw], (uint32_t)(i / RW) & 1u, a.status, kErrTimeoutFull, abort_flag)) break;
+        if (gt == 0) trace_mark(a, 1, i);
+        uint4 v[2][4];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int r = gt + half * 64;
+          const uint8_t* slot = wraw + sw * S::kWSlot;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            // tiled weights land chunk-major ([c][r][16 B]); plain weights as TMA's 64-byte-swizzled rows
+            const int off = tiled ? c * 2048 + r * 16 : r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
+            v[half][c] = *reinterpret_cast<const uint4*>(slot + off);
+          }
+        }
+        mbar_arrive(&wempty[sw]);
+        if (!mbar_wait_ab(&fempty[f], ((uint32_t)(i / F) & 1u) ^ 1u, a.status, kErrTimeoutEmpty, abort_flag)) break;
+        if (gt == 0) trace_mark(a, 2, i);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int r = gt + half * 64;
+          const int sw128 = r & 7;
+          uint8_t* dst = w16 + f * kW16Bytes + r * 128;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint4 o;
+            i8x4_to_f16x4(v[half][c].x, o.x, o.y); i8x4_to_f16x4(v[half][c].y, o.z, o.w);
+            *reinterpret_cast<uint4*>(dst + (((2 * c) ^ sw128) << 4)) = o;
+            i8x4_to_f16x4(v[half][c].z, o.x, o.y); i8x4_to_f16x4(v[half][c].w, o.z, o.w);
+            *reinterpret_cast<uint4*>(dst + (((2 * c + 1) ^ sw128) << 4)) = o;
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&ffull[f]);
+        if (gt == 0) trace_mark(a, 3, i);
+      }
     }
   } else {
     // ------------------------------------------------------------------ epilogue (overlapped)
@@ -451,14 +671,15 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       const bool whole = ka == 0 && ue == tile_end;
       const int n_tile = tile % a.n_tiles, m_tile = tile / a.n_tiles;
       const int acc = seg & 1;
-      const uint32_t acc_addr = tmem + (uint32_t)(acc * BN) + ((uint32_t)(quad * 32) << 16);
+      const uint32_t acc_addr = tmem + (uint32_t)(acc * S::kAccCols) + ((uint32_t)(quad * 32) << 16);
       mbar_wait_ab(&afull[acc], (uint32_t)(seg >> 1) & 1u, a.status, kErrTimeoutAccum, abort_flag);
+      if (et == 0) trace_mark(a, 5, seg);
       tc_fence_after();
       if (whole) {
         if (a.in_ssq != nullptr) compute_row_scale<BN>(a, m_tile, inv, et);
         for (int c0 = 0; c0 < BN; c0 += kChunk) {
           float v[kChunk];
-          tmem_ld16(acc_addr + (uint32_t)c0, v);
+          tmem_ld_acc<BN, S::NACC>(acc_addr + (uint32_t)c0, v);
           if (c0 + kChunk >= BN) {   // accumulator fully read: hand it back to the MMA warp early
             tc_fence_before();
             mbar_arrive(&aempty[acc]);
@@ -475,7 +696,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
         float* mine = ws_tile + (size_t)segidx * (BN * kBM);
         for (int c0 = 0; c0 < BN; c0 += kChunk) {
           float v[kChunk];
-          tmem_ld16(acc_addr + (uint32_t)c0, v);
+          tmem_ld_acc<BN, S::NACC>(acc_addr + (uint32_t)c0, v);
 #pragma unroll
           for (int j = 0; j < kChunk; ++j) __stcg(&mine[(c0 + j) * kBM + row], v[j]);
         }
@@ -509,12 +730,14 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
           if constexpr (EPI == EPI_RESID_AR) ar_reduce_tile<BN>(a, n_tile, m_tile, row, et, ep, ssq_red);
         }
       }
+      if (et == 0) trace_mark(a, 6, seg);
       u = ue;
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) trace_mark(a, 7, 1);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, S::kTmemCols);
@@ -570,6 +793,9 @@ static int* g_status[64] = {nullptr};
 void set_status_word(int device, int* p) {
   if (device >= 0 && device < 64) g_status[device] = p;
 }
+static long long* g_trace = nullptr;
+void set_gemm_trace(long long* p) { g_trace = p; }
+
 int* status_word() {
   int d = 0;
   cudaGetDevice(&d);
@@ -602,7 +828,10 @@ GemmPlan gemm_plan(int M, int N, int K, int force_ctas) {
   p.bn = gemm_pick_bn(M);
   p.n_tiles = (N + kBM - 1) / kBM;
   p.m_tiles = (M + p.bn - 1) / p.bn;
-  p.k_tiles = K / kBK;
+  const int kt = K / kBK;
+  const int ku_max = p.bn <= 128 ? 4 : 1;   // GemmCfg<BN>::KU
+  p.ku = (ku_max >= 4 && kt % 4 == 0) ? 4 : (ku_max >= 2 && kt % 2 == 0) ? 2 : 1;
+  p.k_tiles = kt / p.ku;
   p.tiles = p.n_tiles * p.m_tiles;
   const int64_t U = (int64_t)p.tiles * p.k_tiles;
   int64_t G = force_ctas > 0 ? force_ctas : gemm_sm_count();
@@ -657,10 +886,30 @@ void gemm_w8a16_launch(const void* x, int ldx, const int8_t* w, int epi, GemmArg
   if (p.ws_floats && (a.ws == nullptr || a.counters == nullptr))
     throw std::runtime_error("w8a16 gemm: this shape needs the split-K workspace");
   CUtensorMap tw, tx;
-  make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.N, a.K, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_64B);
-  make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.K, a.M, ldx, kBK, p.bn, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (p.ku < 1 || (a.K / kBK) % p.ku != 0) throw std::runtime_error("w8a16 gemm: bad plan (ku)");
+  if (a.w_tiles == nullptr) {
+    make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.N, a.K, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_64B);
+  } else {
+    std::memset(&tw, 0, sizeof(tw));   // unused: the tiled weights are fetched with bulk copies
+    if ((reinterpret_cast<uintptr_t>(a.w_tiles) & 15) != 0) throw std::runtime_error("tiled weights not 16B aligned");
+  }
+  // activations as a 3-D view (64 k, M rows, K/64 k-tiles) so one TMA box brings a whole unit: [ku][BN][64]
+  {
+    if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) throw std::runtime_error("TMA base must be 16-byte aligned");
+    if (((uint64_t)ldx * 2) % 16 != 0) throw std::runtime_error("x row stride must be a multiple of 16 bytes");
+    cuuint64_t dims[3] = {(cuuint64_t)kBK, (cuuint64_t)a.M, (cuuint64_t)(a.K / kBK)};
+    cuuint64_t strides[2] = {(cuuint64_t)ldx * 2, (cuuint64_t)kBK * 2};
+    cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)p.bn, (cuuint32_t)p.ku};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = tmap_encode_fn()(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(x), dims, strides, box, es,
+                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("x tensor map encode failed: " + std::to_string((int)r));
+  }
   if (a.status == nullptr) a.status = status_word();
+  if (a.trace == nullptr) a.trace = g_trace;
   a.k_tiles = p.k_tiles;
+  a.ku = p.ku;
   a.n_tiles = p.n_tiles;
   a.tiles = p.tiles;
   a.max_seg = p.max_seg;

@@ -19,8 +19,12 @@ enum GemmEpilogue : int {
 
 struct GemmArgs {
   int M, N, K;
-  int k_tiles, n_tiles, tiles, max_seg;     // filled by the launcher from the plan
+  int k_tiles, n_tiles, tiles, max_seg;     // filled by the launcher from the plan (k_tiles = units per tile)
+  int ku;                                   // 64-wide k-tiles per pipeline unit (1, 2 or 4)
   const float* scale;                       // [N]
+  // Pre-tiled weights (preferred): [ceil(N/128)][K/64][8192] int8, each 8 KB block the 64-byte-swizzled image of
+  // one 128-row x 64-k tile, fetched with one contiguous bulk copy.  nullptr: plain row-major [N, K] via 2-D TMA.
+  const int8_t* w_tiles;
   const float* bias;                        // [N] or nullptr
   void* out;                                // EPI_F16 / EPI_F32 / EPI_SWIGLU
   int ldo;
@@ -57,12 +61,16 @@ struct GemmArgs {
   __nv_bfloat16* k_cache;                   // [num_blocks, kv_heads, block_size, head_dim]
   __nv_bfloat16* v_cache;
   int* status;                              // bounded-wait error word (may be nullptr)
+  long long* trace;                         // optional per-stage clock64 stamps of CTA 0 ([12][kGemmTraceLen])
 };
+
+constexpr int kGemmTraceLen = 1024;
 
 // Persistent stream-K plan: `ctas` CTAs share tiles*k_tiles (tile, k) units evenly; a tile is cut into at most
 // `max_seg` k-segments (== `splits`), whose partials need `ws_floats` floats of workspace and `counters` tickets.
 struct GemmPlan {
-  int bn, n_tiles, m_tiles, k_tiles, tiles, ctas, max_seg, splits;
+  int bn, n_tiles, m_tiles, k_tiles, tiles, ctas, max_seg, splits;   // k_tiles: pipeline units per output tile
+  int ku;                                                            // 64-wide k-tiles per unit
   size_t ws_floats;
   int counters;
 };
@@ -75,6 +83,8 @@ void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int
                   CUtensorMapSwizzle swz);
 int gemm_sm_count();
 void set_status_word(int device, int* p);
+// Per-stage timestamps of CTA 0 for every following launch (nullptr switches tracing off).
+void set_gemm_trace(long long* p);
 int* status_word();
 
 }  // namespace hrm

@@ -11,6 +11,9 @@ void rmsnorm_launch(float* x, const float* delta, const float* w, __half* out, i
                     cudaStream_t s);
 void norm_prep_launch(float* x, const float* delta, const float* gamma, __half* xg, float* ssq, int M, int H,
                       cudaStream_t s);
+// PHO index prototype: scores[i] = #(record id == query id pairs) - 0.05 * |len_i - q_len|; rec_ids [n][8] u32.
+void pho_score_launch(const uint32_t* rec_ids, const uint32_t* rec_len, const uint32_t* q, int q_len, float* scores,
+                      long long n, int sm_count, cudaStream_t s);
 void embed_q8_launch(const int64_t* ids, const int8_t* q, const float* scale, float* out, int M, int H,
                      int vocab_start, int vocab_local, cudaStream_t s);
 

@@ -80,11 +80,14 @@ def pack_layer(cfg: ModelConfig, w: Dict[str, Tensorish], l: int, device) -> Lay
     g, u = w[n["gate"]], w[n["up"]]
     w_gu, s_gu = ops.interleave_gate_up(g.q.to(device), u.q.to(device), g.scale.to(device), u.scale.to(device))
     o, d = w[n["o"]], w[n["down"]]
+    w_o, w_d = o.q.to(device).contiguous(), d.q.to(device).contiguous()
+    if torch.device(device).type == "cuda":   # GPU layout: pre-tiled blocks streamed by contiguous bulk copies
+        w_qkv, w_o, w_gu, w_d = (ops.tile_w8(t) for t in (w_qkv, w_o, w_gu, w_d))
     return LayerWeights(
         w_qkv=w_qkv, s_qkv=s_qkv, b_qkv=b_qkv,
-        w_o=o.q.to(device).contiguous(), s_o=o.scale.to(device, torch.float32).contiguous(),
+        w_o=w_o, s_o=o.scale.to(device, torch.float32).contiguous(),
         w_gu=w_gu, s_gu=s_gu.to(torch.float32),
-        w_d=d.q.to(device).contiguous(), s_d=d.scale.to(device, torch.float32).contiguous(),
+        w_d=w_d, s_d=d.scale.to(device, torch.float32).contiguous(),
         ln1=w[n["ln1"]].to(device, torch.float32).contiguous(), ln2=w[n["ln2"]].to(device, torch.float32).contiguous())
 
 
@@ -96,6 +99,8 @@ class LlamaW8:
         self.cfg, self.plan, self.layers, self.device = cfg, plan, layers, torch.device(device)
         self.embed_q, self.embed_s = embed.q.contiguous(), embed.scale.contiguous()
         self.head_q, self.head_s = lm_head.q.contiguous(), lm_head.scale.contiguous()
+        if self.head_q.is_cuda:
+            self.head_q = ops.tile_w8(self.head_q)
         self.final_norm = final_norm
         self.comm = comm
         self.q_rows = plan.local_heads * cfg.head_dim

@@ -92,8 +92,8 @@ class Workspace:
 
 
 def gemm_plan(M: int, N: int, K: int, force_ctas: int = 0) -> dict:
-    bn, nt, mt, kt, splits, wsf, cnt = ext().gemm_plan(int(M), int(N), int(K), int(force_ctas))
-    return dict(bn=bn, n_tiles=nt, m_tiles=mt, k_tiles=kt, splits=splits, ws_floats=wsf, counters=cnt)
+    bn, nt, mt, kt, splits, wsf, cnt, ku = ext().gemm_plan(int(M), int(N), int(K), int(force_ctas))
+    return dict(bn=bn, n_tiles=nt, m_tiles=mt, k_units=kt, splits=splits, ws_floats=wsf, counters=cnt, ku=ku)
 
 
 def _ws_for(M, N, K, device, force_ctas=0):
@@ -120,6 +120,34 @@ def _inv_rms(in_norm):
     return torch.rsqrt(ssq.reshape(-1, ssq.shape[-1]).sum(0) / float(H) + float(eps))
 
 
+def tile_w8(q: torch.Tensor) -> torch.Tensor:
+    """Pre-tile an int8 weight ``[N, K]`` for the GEMM's streaming paths: ``[ceil(N/128), K/64, 8192]``; block
+    ``(n, k)`` covers rows ``128n..128n+127`` x columns ``64k..64k+63`` stored chunk-major: byte
+    ``c*2048 + r*16 + b`` = ``W[128n + r, 64k + 16c + b]``.  A warp reading 16-byte chunk c of 32 consecutive rows
+    then touches 512 contiguous bytes (global loads fully coalesced, shared-memory reads conflict-free).  Rows past N
+    are zero."""
+    N, K = q.shape
+    if K % 64:
+        raise ValueError(f"K={K} must be a multiple of 64")
+    NT = (N + 127) // 128
+    if NT * 128 != N:
+        q = torch.nn.functional.pad(q, (0, 0, 0, NT * 128 - N))
+    return q.reshape(NT, 128, K // 64, 4, 16).permute(0, 2, 3, 1, 4).reshape(NT, K // 64, 8192).contiguous()
+
+
+def untile_w8(t: torch.Tensor, N: int) -> torch.Tensor:
+    """Inverse of :func:`tile_w8` (for checks and CPU math)."""
+    NT, KT, _ = t.shape
+    return t.view(NT, KT, 4, 128, 16).permute(0, 3, 1, 2, 4).reshape(NT * 128, KT * 64)[:N].contiguous()
+
+
+def weight_nk(qweight: torch.Tensor, scale: torch.Tensor) -> Tuple[int, int]:
+    """(N, K) of a plain ``[N, K]`` or pre-tiled int8 weight."""
+    if qweight.dim() == 3:
+        return int(scale.numel()), int(qweight.shape[1]) * 64
+    return int(qweight.shape[0]), int(qweight.shape[1])
+
+
 def _norm_kw(in_norm):
     if in_norm is None:
         return {}
@@ -127,8 +155,9 @@ def _norm_kw(in_norm):
     return dict(in_ssq=ssq, inv_h=1.0 / float(H), eps=float(eps))
 def w8a16_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, bias: Optional[torch.Tensor] = None,
                  out_dtype: Optional[torch.dtype] = None, force_ctas: int = 0, in_norm=None) -> torch.Tensor:
-    """``y = x @ (qweight * scale[:, None])^T (+ bias)``; int8 weights ``[N, K]`` with per-row fp32 scales."""
-    N, K = qweight.shape
+    """``y = x @ (qweight * scale[:, None])^T (+ bias)``; int8 weights ``[N, K]`` (or pre-tiled by :func:`tile_w8`)
+    with per-row fp32 scales."""
+    N, K = weight_nk(qweight, scale)
     if not x.is_cuda:
         y = x.to(torch.float32) @ (qweight.to(torch.float32) * scale.to(torch.float32)[:, None]).t()
         if in_norm is not None:
@@ -159,7 +188,7 @@ def w8a16_linear_out(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor
         out.copy_(y)
         return out
     x2 = _as_f16_2d(x)
-    w = _ws_for(x2.shape[0], qweight.shape[0], qweight.shape[1], x.device, force_ctas)
+    w = _ws_for(x2.shape[0], *weight_nk(qweight, scale), x.device, force_ctas)
     ext().w8a16_gemm(x2, qweight, scale, None, out, w.ws, w.counters, force_ctas, **_norm_kw(in_norm))
     LAUNCH_COUNTER.add()
     return out
@@ -176,7 +205,7 @@ def w8a16_residual_(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor,
             norm_prep(resid, None, gamma_next, xg_out, ssq_out)
         return resid
     x2 = _as_f16_2d(x)
-    w = _ws_for(x2.shape[0], qweight.shape[0], qweight.shape[1], x.device, force_ctas)
+    w = _ws_for(x2.shape[0], *weight_nk(qweight, scale), x.device, force_ctas)
     ext().w8a16_gemm_residual(x2, qweight, scale, resid, w.ws, w.counters, force_ctas, gamma_next, xg_out, ssq_out)
     LAUNCH_COUNTER.add()
     return resid
@@ -188,7 +217,7 @@ def w8a16_residual_ar_(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tens
     ``resid += sum over ranks of x_r @ W_r^T``; also writes ``xg_out = resid * gamma_next`` and ``ssq_out``.
     Every rank ends with bitwise-identical outputs (rank-ordered reduction by the tile's owner rank)."""
     x2 = _as_f16_2d(x)
-    w = _ws_for(x2.shape[0], qweight.shape[0], qweight.shape[1], x.device)
+    w = _ws_for(x2.shape[0], *weight_nk(qweight, scale), x.device)
     ext().w8a16_gemm_residual_ar(x2, qweight, scale, resid, w.ws, w.counters, gamma_next, xg_out, ssq_out, symm.peers,
                                  symm.rank, symm.world, symm.off_partials, symm.off_final, symm.off_flags,
                                  symm.max_bn * 128, symm.max_tiles, symm.epoch_ptr, symm.ticket)
@@ -215,7 +244,7 @@ def interleave_gate_up(gate_q: torch.Tensor, up_q: torch.Tensor, gate_s: torch.T
 def w8a16_swiglu(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, force_ctas: int = 0,
                  in_norm=None) -> torch.Tensor:
     """``silu(x @ Wg^T) * (x @ Wu^T)`` with ``w_gu`` packed by :func:`interleave_gate_up`; f16 output."""
-    N2, K = w_gu.shape
+    N2, K = weight_nk(w_gu, s_gu)
     F = N2 // 2
     if not x.is_cuda:
         h = swiglu_half(F)
@@ -261,7 +290,7 @@ def w8a16_qkv_rope_append(x: torch.Tensor, w_qkv: torch.Tensor, s_qkv: torch.Ten
     x2 = _as_f16_2d(x)
     if q_out is None:
         q_out = torch.empty(M, q_rows, dtype=torch.bfloat16, device=x.device)
-    w = _ws_for(M, w_qkv.shape[0], w_qkv.shape[1], x.device, force_ctas)
+    w = _ws_for(M, *weight_nk(w_qkv, s_qkv), x.device, force_ctas)
     ext().w8a16_gemm_qkv(x2, w_qkv, s_qkv, bias, q_rows, kv_rows, head_dim, positions, slots, cos_t, sin_t, q_out,
                          k_cache, v_cache, w.ws, w.counters, force_ctas, **_norm_kw(in_norm))
     LAUNCH_COUNTER.add()

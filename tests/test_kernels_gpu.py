@@ -41,6 +41,19 @@ def test_w8a16_gemm(M, N, K):
     assert err <= 1e-3 * max(1.0, ref.abs().max().item()), err
 
 
+@pytest.mark.parametrize("M", [1, 16, 64, 130, 300])
+@pytest.mark.parametrize("N,K", [(1000, 1024), (1536, 4096)])
+def test_w8a16_tiled_weights_bitwise_equal_plain(M, N, K):
+    """Pre-tiled weights (bulk-copy path) give bit-identical results to the plain row-major TMA path."""
+    q, s = _qw(N, K, 11)
+    x = _x(M, K, 12)
+    t = ops.tile_w8(q)
+    assert torch.equal(ops.untile_w8(t, N), q)
+    a = ops.w8a16_linear(x, q, s, out_dtype=torch.float32)
+    b = ops.w8a16_linear(x, t, s, out_dtype=torch.float32)
+    assert torch.equal(a, b)
+
+
 @pytest.mark.parametrize("splits", [1, 2, 3, 7, 37, 148])
 def test_w8a16_stream_k_deterministic(splits):
     q, s = _qw(512, 2048, 3)

@@ -81,3 +81,17 @@ def test_eos_stops_generation():
     free = eng.generate([[5, 6, 7]], 6, stop_on_eos=False)[0]
     stop = eng.generate([[5, 6, 7]], 6, stop_on_eos=True, eos_ids=[free[2]])[0]
     assert stop == free[:3]
+
+
+def test_tile_w8_roundtrip_and_layout():
+    from hrm_flashrenderer_b200 import ops
+    g = torch.Generator().manual_seed(0)
+    q = torch.randint(-128, 128, (300, 192), dtype=torch.int8, generator=g)
+    t = ops.tile_w8(q)
+    assert t.shape == (3, 3, 8192)
+    assert torch.equal(ops.untile_w8(t, 300), q)
+    # block (n=1, k=2) is chunk-major: [chunk c][row r][16 bytes]
+    blk = t[1, 2].view(4, 128, 16)
+    for c in range(4):
+        assert torch.equal(blk[c, 5], q[128 + 5, 128 + 16 * c:128 + 16 * c + 16])
+    assert int(t[2, 0].view(4, 128, 16)[:, 300 - 256:].abs().sum()) == 0   # padded rows are zero

@@ -9,6 +9,7 @@ from hrm_flashrenderer_b200.models.oracle import OracleLlama
 from hrm_flashrenderer_b200.models.weights import synth_weights
 from hrm_flashrenderer_b200.models.llama import LlamaW8
 from hrm_flashrenderer_b200.runtime.engine import InferenceEngine
+from hrm_flashrenderer_b200 import ops
 
 pytestmark = pytest.mark.gpu
 
@@ -74,6 +75,8 @@ def test_synthesize_on_device_shapes():
     cfg = replace(SMALL, layers=1)
     m = LlamaW8.synthesize(cfg, device="cuda")
     L = m.layers[0]
-    assert L.w_qkv.shape == (cfg.q_dim + 2 * cfg.kv_dim, cfg.hidden)
-    assert L.w_gu.shape == (2 * cfg.intermediate, cfg.hidden)
+    # GPU weights are pre-tiled: [N/128, K/64, 8192]
+    assert ops.weight_nk(L.w_qkv, L.s_qkv) == (cfg.q_dim + 2 * cfg.kv_dim, cfg.hidden)
+    assert ops.weight_nk(L.w_gu, L.s_gu) == (2 * cfg.intermediate, cfg.hidden)
+    assert L.w_qkv.shape == ((cfg.q_dim + 2 * cfg.kv_dim) // 128, cfg.hidden // 64, 8192)
     assert m.weight_bytes() > 0
