@@ -45,7 +45,8 @@ constexpr int kDqWarps = 8;
 constexpr int kEpiWarps = 4;
 constexpr int kFirstDqWarp = 2;
 constexpr int kFirstEpiWarp = kFirstDqWarp + kDqWarps;
-constexpr int kThreads = (kFirstEpiWarp + kEpiWarps) * 32;   // 448
+constexpr int kMma2Warp = kFirstEpiWarp + kEpiWarps;         // second MMA issuer (warp 14)
+constexpr int kThreads = (kMma2Warp + 1) * 32;               // 480
 constexpr int kDqThreads = kDqWarps * 32;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kWrawBytes = kBM * kBK;          // int8 tile, 8 KB
@@ -53,9 +54,10 @@ constexpr int kW16Bytes = kBM * kBK * 2;       // f16 tile, 16 KB
 constexpr int kChunk = 16;                     // epilogue columns per TMEM load
 
 // Pipeline shape per token-tile width BN.
-//  TS (BN <= 128, decode): dequantised A tiles go to tensor memory and the MMA reads A from TMEM; 2 dequant groups of
-//    4 warps, thread = weight row (= TMEM lane).  With pre-tiled weights the dequant threads stream W straight from
-//    HBM into registers; with plain row-major weights W goes through a TMA ring in shared memory.
+//  TS (BN <= 128, decode): dequantised A tiles go to tensor memory and the MMA reads A from TMEM; one dequant group
+//    of 8 warps converts each unit (thread = weight row = TMEM lane; the two warps of a lane quarter take alternate
+//    k-tiles of the unit).  Shared memory then carries 2 bytes per weight byte (bulk-copy
+//    write + one conflict-free read) instead of 6.
 //  SS (BN = 256, prefill): A tiles in shared memory (F stages of 16 KB, 128-byte swizzle); 4 dequant groups of
 //    2 warps.  Here the MMA time per tile hides the extra shared-memory traffic.
 // KU: 64-wide k-tiles per pipeline unit.  At decode widths every per-unit step (barrier waits, commits, TMA issue)
@@ -65,11 +67,14 @@ constexpr int kChunk = 16;                     // epilogue columns per TMEM load
 // (units), released by the MMA.  F: A stages (units).  RW and F are multiples of the group count, so every slot of
 // those rings is always consumed by the same group, in order: no waiter can ever mistake a phase two generations
 // old for the one it waits for.
-// NACC: independent partial accumulators per output tile, summed in the epilogue.
+// NACC: MMA-issuing warps.  A single thread issuing one unit's small-N MMAs and then its commits and barrier waits
+// leaves the tensor core idle during the bookkeeping; with two issuers (warps 1 and 14) taking alternate units, one
+// issues while the other does its bookkeeping.  Each issuer accumulates into its own partial accumulator; the
+// epilogue sums the partials that the segment wrote.
 template <int BN> struct GemmCfg;
-template <> struct GemmCfg<16>  { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 2, RX = 8, F = 2, NACC = 4; };
-template <> struct GemmCfg<32>  { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 2, RX = 5, F = 2, NACC = 4; };
-template <> struct GemmCfg<64>  { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 2, RX = 3, F = 2, NACC = 2; };
+template <> struct GemmCfg<16>  { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 4, RX = 8, F = 3, NACC = 2; };
+template <> struct GemmCfg<32>  { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 4, RX = 4, F = 3, NACC = 2; };
+template <> struct GemmCfg<64>  { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 4, RX = 2, F = 2, NACC = 2; };
 template <> struct GemmCfg<128> { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 2, RX = 2, F = 2, NACC = 1; };
 template <> struct GemmCfg<256> { static constexpr bool TS = false; static constexpr int KU = 1, RW = 4, RX = 3, F = 4, NACC = 1; };
 
@@ -80,7 +85,7 @@ struct GemmSmem {
   static constexpr int RW = GemmCfg<BN>::RW, RX = GemmCfg<BN>::RX, F = GemmCfg<BN>::F;
   static constexpr int NACC = GemmCfg<BN>::NACC;
   static constexpr int kAccCols = NACC * BN;                            // one accumulator buffer (NACC partials)
-  static constexpr int NG = TS ? 2 : 4;                                // dequant groups
+  static constexpr int NG = TS ? 1 : 4;                                // dequant groups
   static constexpr int kGroupThreads = kDqThreads / NG;
   static constexpr int kXSub = BN * kBK * 2;                           // one k-tile of activations
   static constexpr int kXSlot = KU * kXSub;
@@ -102,7 +107,7 @@ struct GemmSmem {
   static_assert(RW % NG == 0 && F % NG == 0, "ring depths must be multiples of the dequant group count");
   static_assert(!TS || kAcol + F * kAStageCols <= kTmemCols, "TMEM budget exceeded");
   static_assert(TS || (2 * kAccCols <= kTmemCols && KU == 1), "SS path: TMEM budget / unit size");
-  static_assert(NACC == 1 || NACC == 2 || NACC == 4, "NACC must divide the 4 MMAs of a k-tile");
+  static_assert(NACC == 1 || NACC == 2, "one or two MMA issuers");
 };
 
 // Pipeline trace for performance analysis: clock64 of CTA 0 at each stage of unit i (points listed at the call
@@ -112,9 +117,10 @@ HRM_DEVINL void trace_mark(const GemmArgs& a, int point, int64_t i) {
   if (a.trace != nullptr && blockIdx.x == 0 && i < kGemmTraceLen) a.trace[point * kGemmTraceLen + i] = clock64();
 }
 
-// 16 accumulator columns summed over the NACC partial accumulators (NACC loads in flight, one wait).
+// 16 accumulator columns summed over the partial accumulators whose bit is set in `valid` (all are loaded, so the
+// warp-collective loads stay uniform; one wait).
 template <int BN, int NACC>
-HRM_DEVINL void tmem_ld_acc(uint32_t taddr, float (&v)[16]) {
+HRM_DEVINL void tmem_ld_acc(uint32_t taddr, float (&v)[16], uint32_t valid) {
   if constexpr (NACC == 1) {
     tmem_ld16(taddr, v);
   } else {
@@ -130,9 +136,10 @@ HRM_DEVINL void tmem_ld_acc(uint32_t taddr, float (&v)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      float acc = __uint_as_float(r[0][i]);
+      float acc = 0.f;
 #pragma unroll
-      for (int j = 1; j < NACC; ++j) acc += __uint_as_float(r[j][i]);
+      for (int j = 0; j < NACC; ++j)
+        if (valid & (1u << j)) acc += __uint_as_float(r[j][i]);
       v[i] = acc;
     }
   }
@@ -361,6 +368,9 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
   using S = GemmSmem<BN>;
   constexpr int RW = S::RW, RX = S::RX, F = S::F, NG = S::NG;
   constexpr bool TS = S::TS;
+  // TS with a single dequant group and an activation ring deeper than the A-stage ring: the dequant warps wait for
+  // the unit's activation tile (they run ahead of the MMA anyway), so the MMA thread waits on one barrier per unit.
+  constexpr bool kFoldX = TS && NG == 1 && RX > F;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* w16 = base + S::kW16Off;
@@ -404,10 +414,10 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       mbar_init(&fempty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&afull[s], 1);
+      mbar_init(&afull[s], S::NACC);
       mbar_init(&aempty[s], kEpiThreads);
     }
-    mbar_init(mdone, 1);
+    mbar_init(mdone, S::NACC);   // every MMA issuer commits once at the end
     *last_flag = 0;
     *abort_flag = 0;
     fence_barrier_init();
@@ -435,8 +445,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       int n_tile = tile0 % a.n_tiles, m_tile = tile0 / a.n_tiles;
       int sw = 0, sx = 0;
       uint32_t pw = 1u, px = 1u;   // producer-side parities of the empty barriers (first pass: free)
-      // decode widths with pre-tiled weights stream W straight into the dequant warps' registers: no W ring
-      const bool w_ring = !(TS && a.w_tiles != nullptr);
+      const bool w_ring = true;
       for (int64_t u = u0; u < u1; ++u) {
         const int64_t i = u - u0;
         trace_mark(a, 0, i);
@@ -470,47 +479,69 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       for (int64_t j = (nx > RX ? nx - RX : 0); j < nx; ++j)
         mbar_wait(&xfull[j % RX], (uint32_t)(j / RX) & 1u, a.status, kErrTimeoutFull);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+  } else if (warp == 1 || warp == kMma2Warp) {
+    // ------------------------------------------------------------------ MMA issuers (NACC of them)
+    const int mw = warp == 1 ? 0 : 1;   // issuer index = its partial accumulator
+    if (lane == 0 && mw < S::NACC) {
       constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
-      int64_t i = 0;
+      const uint64_t xdesc0 = sdesc_sw128(smem_u32(xs));
+      const uint64_t wdesc0 = sdesc_sw128(smem_u32(w16));
       int seg = 0;
       bool ok = true;
+      int sx = 0, f = 0;                  // ring slots of the current unit
+      uint32_t phx = 0u, phf = 0u;        // their full-barrier parities
+      // issuer mw takes the units whose CTA-local index is congruent to mw (mod NACC); the slot counters still step
+      // over every unit so they stay in lock-step with the rings
       for (int64_t u = u0; ok && u < u1; ++seg) {
         const int tile = (int)(u / a.k_tiles);
         const int64_t tile_end = (int64_t)(tile + 1) * a.k_tiles;
         const int64_t ue = tile_end < u1 ? tile_end : u1;
         const int acc = seg & 1;
-        const uint32_t acc_addr = tmem + (uint32_t)(acc * S::kAccCols);
+        const uint32_t acc_addr = tmem + (uint32_t)(acc * S::kAccCols + mw * BN);
         ok = mbar_wait_ab(&aempty[acc], ((uint32_t)(seg >> 1) & 1u) ^ 1u, a.status, kErrTimeoutAccum, abort_flag);
         tc_fence_after();
-        for (int64_t k = u; ok && k < ue; ++k, ++i) {
-          const int sx = (int)(i % RX), f = (int)(i % F);
-          ok = mbar_wait_ab(&xfull[sx], (uint32_t)(i / RX) & 1u, a.status, kErrTimeoutFull, abort_flag) &&
-               mbar_wait_ab(&ffull[f], (uint32_t)(i / F) & 1u, a.status, kErrTimeoutDequant, abort_flag);
+        bool first = true;                  // this issuer's first unit of the segment overwrites its partial
+        for (int64_t k = u; ok && k < ue; ++k) {
+          if (((k - u0) % S::NACC) != mw) {
+            if (++sx == RX) { sx = 0; phx ^= 1u; }
+            if (++f == F) { f = 0; phf ^= 1u; }
+            continue;
+          }
+          // with kFoldX the dequant warps already waited for this unit's activation tile before publishing ffull
+          if constexpr (!kFoldX)
+            ok = mbar_wait_ab(&xfull[sx], phx, a.status, kErrTimeoutFull, abort_flag);
+          ok = ok && mbar_wait_ab(&ffull[f], phf, a.status, kErrTimeoutDequant, abort_flag);
           if (!ok) break;
-          trace_mark(a, 4, i);
+          trace_mark(a, 4, k - u0);
           tc_fence_after();
-          const uint32_t b0 = smem_u32(xs + sx * S::kXSlot);
-          for (int j = 0; j < ku; ++j) {
+          // descriptors: start-address fields advance by (byte offset >> 4); no carry leaves the 14-bit field
+          const uint64_t bdesc = xdesc0 + (uint64_t)((sx * S::kXSlot) >> 4);
+          const uint32_t a_t = tmem + (uint32_t)(S::kAcol + f * S::kAStageCols);
+          const uint64_t adesc = wdesc0 + (uint64_t)((f * kW16Bytes) >> 4);
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk) {
-              const int q = j * (kBK / 16) + kk;   // 16-wide K step within the unit
-              const uint32_t d = acc_addr + (uint32_t)((q % S::NACC) * BN);
-              const uint32_t en = (k > u || q >= S::NACC) ? 1u : 0u;
-              const uint64_t bd = sdesc_sw128(b0 + (uint32_t)(j * S::kXSub + kk * 32));
-              if constexpr (TS) {
-                umma_f16_ts(d, tmem + (uint32_t)(S::kAcol + f * S::kAStageCols + j * 32 + kk * 8), bd, idesc, en);
-              } else {
-                umma_f16_ss(d, sdesc_sw128(smem_u32(w16 + f * kW16Bytes) + kk * 32), bd, idesc, en);
+          for (int j = 0; j < S::KU; ++j) {
+            if (j < ku) {
+#pragma unroll
+              for (int kk = 0; kk < kBK / 16; ++kk) {
+                const int q = j * (kBK / 16) + kk;   // 16-wide K step within the unit
+                const uint32_t d = acc_addr;
+                const uint32_t en = (!first || q > 0) ? 1u : 0u;
+                const uint64_t bd = bdesc + (uint64_t)((j * S::kXSub + kk * 32) >> 4);
+                if constexpr (TS) {
+                  umma_f16_ts(d, a_t + (uint32_t)(j * 32 + kk * 8), bd, idesc, en);
+                } else {
+                  umma_f16_ss(d, adesc + (uint64_t)((kk * 32) >> 4), bd, idesc, en);
+                }
               }
             }
           }
           umma_commit(&xempty[sx]);
           umma_commit(&fempty[f]);
+          first = false;
+          if (++sx == RX) { sx = 0; phx ^= 1u; }
+          if (++f == F) { f = 0; phf ^= 1u; }
         }
-        umma_commit(&afull[acc]);
+        umma_commit(&afull[acc]);   // every issuer arrives once per segment (count NACC), even with no unit in it
         u = ue;
       }
       umma_commit(mdone);
@@ -523,10 +554,11 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
     const int64_t n_units = u1 - u0;
     if constexpr (TS) {
       const int dw = warp - kFirstDqWarp;   // 0..7
-      const int g = dw >> 2;                // group 0..1 (4 consecutive warps cover the 4 TMEM lane quarters)
+      const int g = 0;                      // single group: all 8 warps convert every unit
+      const int half = dw >> 2;             // warps 2-5 take k-tiles 0, 2 of a unit; warps 6-9 take 1, 3
       const int quad = warp & 3;
       const int r = quad * 32 + lane;       // weight row = TMEM lane
-      const bool tracer = lane == 0 && (dw & 3) == 0;
+      const bool tracer = lane == 0 && dw == 0;
       const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)S::kAcol;
       auto to_f16 = [](const uint4 (&v)[4], uint32_t (&o)[32]) {
 #pragma unroll
@@ -537,72 +569,28 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
           i8x4_to_f16x4(v[c].w, o[8 * c + 6], o[8 * c + 7]);
         }
       };
-      if (a.w_tiles != nullptr) {
-        // Streaming: each thread loads its row's 64 bytes of every k-tile straight from HBM (chunk-major tiles: a
-        // warp's 16-byte loads cover 512 contiguous bytes), one unit (ku k-tiles) ahead of the conversion, so every
-        // SM keeps 256 threads x ku x 64 B of weights in flight without a shared-memory stage.
-        const uint8_t* wt = reinterpret_cast<const uint8_t*>(a.w_tiles) + r * 16;
-        int64_t nl = g;                                  // next unit to load
-        int lk = 0, ln = 0;                              // its (unit within tile, n-tile)
-        if (u0 + g < u1) {
-          const int64_t uu = u0 + g;
-          lk = (int)(uu % a.k_tiles);
-          ln = (int)((uu / a.k_tiles) % a.n_tiles);
-        }
-        uint4 buf[S::KU][4];
-        auto load_sub = [&](uint4 (&v)[4], int j) {      // k-tile j of unit nl
-          const uint8_t* p = wt + ((size_t)ln * kt_total + (size_t)lk * ku + j) * kWrawBytes;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) v[c] = ldg_stream(p + c * 2048);
-        };
-        auto advance = [&]() {
-          nl += NG;
-          lk += NG;
-          while (lk >= a.k_tiles) {
-            lk -= a.k_tiles;
-            if (++ln == a.n_tiles) ln = 0;
-          }
-        };
-        if (nl < n_units) {
-#pragma unroll
-          for (int j = 0; j < S::KU; ++j)
-            if (j < ku) load_sub(buf[j], j);
-        }
-        advance();
-        for (int64_t i = g; i < n_units; i += NG) {
-          const int f = (int)(i % F);
-          if (!mbar_wait_ab(&fempty[f], ((uint32_t)(i / F) & 1u) ^ 1u, a.status, kErrTimeoutEmpty, abort_flag)) break;
-          if (tracer) trace_mark(a, 2, i);
-          tc_fence_after();
-          const bool more = nl < n_units;
-#pragma unroll
-          for (int j = 0; j < S::KU; ++j) {
-            if (j < ku) {
-              uint32_t o[32];
-              to_f16(buf[j], o);
-              if (more) load_sub(buf[j], j);              // next unit of this group, same k-tile slot
-              tmem_st32u(tl + (uint32_t)(f * S::kAStageCols + j * 32), o);
-            }
-          }
-          advance();
-          tc_fence_before();
-          mbar_arrive_relaxed(&ffull[f]);                 // keeps this thread's prefetch loads in flight
-          if (tracer) trace_mark(a, 3, i);
-        }
-      } else {
+      {
+        // smem image of one k-tile: pre-tiled weights chunk-major ([c][r][16 B], a warp reads 512 contiguous bytes);
+        // plain weights as TMA's 64-byte-swizzled rows
+        const bool tiled = a.w_tiles != nullptr;
         const int sw64 = (r >> 1) & 3;
+        int sw = 0, f = 0, sx = 0;
+        uint32_t pw = 0u, pf = 1u, px = 0u;   // wfull parity, fempty parity (first pass free), xfull parity
         for (int64_t i = g; i < n_units; i += NG) {
-          const int sw = (int)(i % RW), f = (int)(i % F);
-          if (!mbar_wait_ab(&wfull[sw], (uint32_t)(i / RW) & 1u, a.status, kErrTimeoutFull, abort_flag)) break;
+          if (!mbar_wait_ab(&wfull[sw], pw, a.status, kErrTimeoutFull, abort_flag)) break;
           if (tracer) trace_mark(a, 1, i);
-          if (!mbar_wait_ab(&fempty[f], ((uint32_t)(i / F) & 1u) ^ 1u, a.status, kErrTimeoutEmpty, abort_flag)) break;
+          if (!mbar_wait_ab(&fempty[f], pf, a.status, kErrTimeoutEmpty, abort_flag)) break;
+          if constexpr (kFoldX) {
+            if (!mbar_wait_ab(&xfull[sx], px, a.status, kErrTimeoutFull, abort_flag)) break;
+          }
           if (tracer) trace_mark(a, 2, i);
           tc_fence_after();
-          for (int j = 0; j < ku; ++j) {
-            const uint8_t* src = wraw + sw * S::kWSlot + j * kWrawBytes + r * 64;
+          for (int j = half; j < ku; j += 2) {
+            const uint8_t* sub = wraw + sw * S::kWSlot + j * kWrawBytes;
             uint4 v[4];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) v[c] = *reinterpret_cast<const uint4*>(src + ((c ^ sw64) << 4));
+            for (int c = 0; c < 4; ++c)
+              v[c] = *reinterpret_cast<const uint4*>(sub + (tiled ? c * 2048 + r * 16 : r * 64 + ((c ^ sw64) << 4)));
             uint32_t o[32];
             to_f16(v, o);
             tmem_st32u(tl + (uint32_t)(f * S::kAStageCols + j * 32), o);
@@ -611,6 +599,9 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
           tc_fence_before();
           mbar_arrive(&ffull[f]);
           if (tracer) trace_mark(a, 3, i);
+          if (++sw == RW) { sw = 0; pw ^= 1u; }
+          if (++f == F) { f = 0; pf ^= 1u; }
+          if (++sx == RX) { sx = 0; px ^= 1u; }
         }
       }
     } else {
@@ -672,6 +663,8 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       const int n_tile = tile % a.n_tiles, m_tile = tile / a.n_tiles;
       const int acc = seg & 1;
       const uint32_t acc_addr = tmem + (uint32_t)(acc * S::kAccCols) + ((uint32_t)(quad * 32) << 16);
+      // partials written in this segment: both issuers when it has >= 2 units, else only the owner of its unit
+      const uint32_t valid = (S::NACC == 1 || ue - u >= 2) ? ((1u << S::NACC) - 1u) : (1u << ((u - u0) % S::NACC));
       mbar_wait_ab(&afull[acc], (uint32_t)(seg >> 1) & 1u, a.status, kErrTimeoutAccum, abort_flag);
       if (et == 0) trace_mark(a, 5, seg);
       tc_fence_after();
@@ -679,7 +672,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
         if (a.in_ssq != nullptr) compute_row_scale<BN>(a, m_tile, inv, et);
         for (int c0 = 0; c0 < BN; c0 += kChunk) {
           float v[kChunk];
-          tmem_ld_acc<BN, S::NACC>(acc_addr + (uint32_t)c0, v);
+          tmem_ld_acc<BN, S::NACC>(acc_addr + (uint32_t)c0, v, valid);
           if (c0 + kChunk >= BN) {   // accumulator fully read: hand it back to the MMA warp early
             tc_fence_before();
             mbar_arrive(&aempty[acc]);
@@ -696,7 +689,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
         float* mine = ws_tile + (size_t)segidx * (BN * kBM);
         for (int c0 = 0; c0 < BN; c0 += kChunk) {
           float v[kChunk];
-          tmem_ld_acc<BN, S::NACC>(acc_addr + (uint32_t)c0, v);
+          tmem_ld_acc<BN, S::NACC>(acc_addr + (uint32_t)c0, v, valid);
 #pragma unroll
           for (int j = 0; j < kChunk; ++j) __stcg(&mine[(c0 + j) * kBM + row], v[j]);
         }
