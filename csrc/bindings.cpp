@@ -412,6 +412,24 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_prepare", &decode_prepare_bs);
   m.def("decode_advance", &decode_advance);
   m.def("sm_count", []() { return hrm::gemm_sm_count(); });
+  m.def("grad_clip_factor", [](at::Tensor g, double clip, at::Tensor partial, at::Tensor scalars) {
+    c10::cuda::CUDAGuard gd(g.device());
+    TORCH_CHECK(g.is_cuda() && g.scalar_type() == at::kFloat && g.is_contiguous(), "g: contiguous f32 CUDA");
+    TORCH_CHECK(partial.numel() >= 1024 && scalars.numel() >= 2, "partial[1024], scalars[2]");
+    hrm::grad_clip_factor_launch(g.data_ptr<float>(), g.numel(), (float)clip, partial.data_ptr<float>(),
+                                 scalars.data_ptr<float>(), cur_stream());
+  });
+  m.def("adamw_flat", [](at::Tensor w, at::Tensor m_, at::Tensor v, at::Tensor g, double lr, double wd, double b1,
+                         double b2, double eps, at::Tensor step, at::Tensor scalars) {
+    c10::cuda::CUDAGuard gd(w.device());
+    for (auto* t : {&w, &m_, &v, &g})
+      TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == w.numel(),
+                  "w, m, v, g: contiguous f32 CUDA of one size");
+    TORCH_CHECK(step.scalar_type() == at::kInt && scalars.scalar_type() == at::kFloat, "step int32, scalars f32");
+    hrm::adamw_flat_launch(w.data_ptr<float>(), m_.data_ptr<float>(), v.data_ptr<float>(), g.data_ptr<float>(),
+                           w.numel(), (float)lr, (float)wd, (float)b1, (float)b2, (float)eps, step.data_ptr<int>(),
+                           scalars.data_ptr<float>(), hrm::gemm_sm_count(), cur_stream());
+  });
   m.def("pho_score", [](at::Tensor rec_ids, at::Tensor rec_len, at::Tensor q, at::Tensor scores) {
     c10::cuda::CUDAGuard g(rec_ids.device());
     TORCH_CHECK(rec_ids.is_cuda() && rec_ids.scalar_type() == at::kInt && rec_ids.dim() == 2 && rec_ids.size(1) == 8 &&

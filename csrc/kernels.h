@@ -14,6 +14,10 @@ void norm_prep_launch(float* x, const float* delta, const float* gamma, __half* 
 // PHO index prototype: scores[i] = #(record id == query id pairs) - 0.05 * |len_i - q_len|; rec_ids [n][8] u32.
 void pho_score_launch(const uint32_t* rec_ids, const uint32_t* rec_len, const uint32_t* q, int q_len, float* scores,
                       long long n, int sm_count, cudaStream_t s);
+// Trainer optimizer step over one flat fp32 buffer: device-side global-norm clip factor, then AdamW.
+void grad_clip_factor_launch(const float* g, long long n, float clip, float* partial, float* scalars, cudaStream_t s);
+void adamw_flat_launch(float* w, float* m, float* v, const float* g, long long n, float lr, float wd, float b1,
+                       float b2, float eps, int* step, const float* scalars, int sm_count, cudaStream_t s);
 void embed_q8_launch(const int64_t* ids, const int8_t* q, const float* scale, float* out, int M, int H,
                      int vocab_start, int vocab_local, cudaStream_t s);
 
