@@ -39,7 +39,9 @@ def _args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid as a bench)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--baseline-comm", action="store_true", help="NCCL all-reduce instead of the fused kernels")
+    ap.add_argument("--baseline-comm", action="store_true", help="NCCL all-reduce (the default)")
+    ap.add_argument("--fused-comm", action="store_true",
+                    help="row-parallel GEMMs with the in-kernel peer-memory all-reduce instead of NCCL")
     return ap.parse_args()
 
 
@@ -86,6 +88,28 @@ def _emit(rank, rec):
         print(json.dumps(rec), flush=True)
 
 
+def _teardown(world, eng, state, model):
+    """Release the decode graphs (they hold NCCL calls) before the process group goes away.  The result line is
+    already printed, so a teardown that still stalls is cut short by a watchdog instead of holding the GPUs."""
+    import gc
+    import threading
+    sys.stdout.flush()
+    sys.stderr.flush()
+    wd = threading.Timer(60.0, lambda: os._exit(0))
+    wd.daemon = True
+    wd.start()
+    eng.release_graphs()
+    del state, eng
+    if getattr(model, "symm", None) is not None:
+        model.symm = None          # IPC mappings are closed by process exit
+    gc.collect()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    wd.cancel()
+
+
 # ====================================================================================================== ours
 def run_ours(a):
     from hrm_flashrenderer_b200.config import get_preset, EngineConfig
@@ -104,6 +128,9 @@ def run_ours(a):
     t0 = time.time()
     model = LlamaW8.synthesize(cfg, rank=rank, world=world, device=dev, seed=0, comm=comm,
                                max_pos=a.ctx + a.steps + a.warmup + 256)
+    fused = world > 1 and a.fused_comm and not a.baseline_comm
+    if fused:
+        model.enable_fused_collectives()   # row-parallel GEMMs reduce over NVLink peer memory inside the kernel
     torch.cuda.synchronize()
     t_synth = time.time() - t0
     _log(rank, f"synthesized {cfg.name} shard in {t_synth:.1f}s ({model.weight_bytes() / 1e9:.1f} GB int8)")
@@ -187,16 +214,14 @@ def run_ours(a):
         "data": "synthetic random-token prompts, random-init N(0,0.02) int8 weights",
         "config": {"model": cfg.name, "global_batch": a.batch, "seq_len": a.ctx, "parallelism": f"tp{world}",
                    "decode_context": f"{a.ctx}..{a.ctx + a.warmup + a.steps}", "l2": "inputs larger than L2",
-                   "comm": "nccl" if world > 1 else "none"},
+                   "comm": ("fused GEMM+all-reduce over peer memory" if fused else "nccl") if world > 1 else "none"},
         "p50_ttft_ms": round(ttft_p50, 2), "impl": "ours", "gpu_launches": launches,
         "clocks": clocks, "e2e": e2e, "synth_s": round(t_synth, 1),
     }
     if a.layers:
         rec["invalid"] = f"layers overridden to {a.layers} (debug run)"
     _emit(rank, rec)
-    del eng
-    if world > 1:
-        dist.destroy_process_group()
+    _teardown(world, eng, g, model)
 
 
 # ====================================================================================================== reference

@@ -155,6 +155,15 @@ class InferenceEngine:
         g.tokens.copy_(tok)
         ops.decode_advance(g.tokens, g.ids, g.positions, g.active)
 
+    def release_graphs(self) -> None:
+        """Drop every captured decode graph.  Graphs that captured NCCL calls must be released before the process
+        group is destroyed, or the communicator teardown waits on them forever."""
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        for g in self._graphs.values():
+            g.graph = None
+        self._graphs.clear()
+
     def capture(self, bucket: int) -> None:
         """Warm up (sizes the workspace) and capture the decode step of ``bucket`` sequences."""
         g = self._decode_state(bucket)

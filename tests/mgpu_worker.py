@@ -1,0 +1,104 @@
+"""Worker for the multi-GPU tests (run by tests/test_tp_multi_gpu.py under torchrun, one process per GPU).
+
+1. The fused tensor-parallel residual GEMM + peer-memory all-reduce (EPI_RESID_AR) against NCCL all-reduce of the
+   same partials: equal within fp32 summation-order tolerance, bitwise identical on every rank, over repeated
+   launches (epoch flags).
+2. The engine at TP = world (fused collectives and plain NCCL) against TP = 1: same greedy tokens.
+"""
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+from hrm_flashrenderer_b200 import ops
+from hrm_flashrenderer_b200.config import EngineConfig, ModelConfig
+from hrm_flashrenderer_b200.models.llama import LlamaW8
+from hrm_flashrenderer_b200.models.weights import synth_weights
+from hrm_flashrenderer_b200.parallel.comm import TPComm
+from hrm_flashrenderer_b200.parallel.dist import init_dist_env
+from hrm_flashrenderer_b200.parallel.symm import SymmetricWorkspace
+from hrm_flashrenderer_b200.runtime.engine import InferenceEngine
+
+
+def check_fused_ar(rank, world, dev):
+    N, Kl = 2048, 1024
+    symm = SymmetricWorkspace(rank, world, dev, max_tiles=64, max_bn=64)
+    g = torch.Generator(device="cpu").manual_seed(100 + rank)
+    w = torch.randint(-127, 128, (N, Kl), generator=g, dtype=torch.int8).to(dev)
+    s = (torch.rand(N, generator=g) * 1e-3 + 1e-4).to(dev)
+    wt = ops.tile_w8(w)
+    gamma = (torch.rand(N, generator=torch.Generator().manual_seed(7)) + 0.5).to(dev)
+    worst = 0.0
+    for M in (1, 5, 16, 64):
+        for rep in range(3):
+            x = torch.randn(M, Kl, generator=g).half().to(dev)
+            resid = torch.randn(M, N, generator=torch.Generator().manual_seed(M * 10 + rep)).to(dev)
+            part = torch.empty(M, N, dtype=torch.float32, device=dev)
+            ops.w8a16_linear_out(x, wt, s, part)
+            dist.all_reduce(part)
+            ref = resid + part
+            got = resid.clone()
+            xg = torch.empty(M, N, dtype=torch.float16, device=dev)
+            ssq = torch.empty(N // 128, M, dtype=torch.float32, device=dev)
+            ops.w8a16_residual_ar_(x, wt, s, got, symm, gamma, xg, ssq)
+            torch.cuda.synchronize()
+            ops.check_status(dev)
+            err = float((got - ref).abs().max())
+            worst = max(worst, err)
+            assert err < 1e-3 * max(1.0, float(ref.abs().max())), (M, rep, err)
+            torch.testing.assert_close(xg.float(), (got * gamma).half().float(), rtol=0, atol=0)
+            ref_ssq = got.view(M, N // 128, 128).pow(2).sum(-1).t()
+            torch.testing.assert_close(ssq, ref_ssq, rtol=1e-5, atol=1e-4)
+            gathered = [torch.empty_like(got) for _ in range(world)]
+            dist.all_gather(gathered, got)
+            assert all(torch.equal(gathered[0], t) for t in gathered), "ranks disagree"
+    symm.close()
+    return worst
+
+
+def check_engine(rank, world, dev):
+    cfg = ModelConfig(name="tp-small", hidden=1024, layers=2, heads=8, kv_heads=8, head_dim=128, intermediate=2816,
+                      vocab=4096, rms_eps=1e-5, rope_theta=500000.0)
+    w = synth_weights(cfg, seed=1)
+    prompts = [torch.randint(0, cfg.vocab, (40,), generator=torch.Generator().manual_seed(i)).tolist() for i in range(3)]
+    outs = {}
+    for fused in (False, True):
+        model = LlamaW8.from_weights(cfg, w, rank=rank, world=world, device=dev, comm=TPComm(), max_pos=512)
+        if fused:
+            model.enable_fused_collectives()
+        eng = InferenceEngine(model, EngineConfig(tp=world, max_seq_len=256, max_batch=4, use_cuda_graphs=True),
+                              num_blocks=64)
+        outs[fused] = eng.generate(prompts, 12, stop_on_eos=False)
+        del eng
+        if model.symm is not None:
+            model.symm.close()
+    single = None
+    if rank == 0:
+        m1 = LlamaW8.from_weights(cfg, w, device=dev, max_pos=512)
+        e1 = InferenceEngine(m1, EngineConfig(max_seq_len=256, max_batch=4, use_cuda_graphs=False), num_blocks=64)
+        single = e1.generate(prompts, 12, stop_on_eos=False)
+    return outs[False], outs[True], single
+
+
+def main():
+    rank, local, world = init_dist_env("nccl")
+    dev = torch.device("cuda", local)
+    worst = check_fused_ar(rank, world, dev)
+    nccl_out, fused_out, single = check_engine(rank, world, dev)
+    ok = True
+    if rank == 0:
+        first_div = lambda a, b: next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), len(a))
+        agree_fused = fused_out == nccl_out
+        agree_single = min(first_div(a, b) for a, b in zip(nccl_out, single))
+        ok = agree_single >= 8
+        print(json.dumps({"ok": ok, "world": world, "fused_ar_max_err": worst, "fused_equals_nccl": agree_fused,
+                          "tp_vs_tp1_first_divergence": agree_single}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(0 if ok else 1)
+
+
+if __name__ == "__main__":
+    main()
