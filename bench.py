@@ -39,9 +39,8 @@ def _args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid as a bench)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--baseline-comm", action="store_true", help="NCCL all-reduce (the default)")
-    ap.add_argument("--fused-comm", action="store_true",
-                    help="row-parallel GEMMs with the in-kernel peer-memory all-reduce instead of NCCL")
+    ap.add_argument("--baseline-comm", action="store_true",
+                    help="NCCL all-reduce after the row-parallel GEMMs instead of the fused in-kernel all-reduce")
     return ap.parse_args()
 
 
@@ -128,7 +127,7 @@ def run_ours(a):
     t0 = time.time()
     model = LlamaW8.synthesize(cfg, rank=rank, world=world, device=dev, seed=0, comm=comm,
                                max_pos=a.ctx + a.steps + a.warmup + 256)
-    fused = world > 1 and a.fused_comm and not a.baseline_comm
+    fused = world > 1 and not a.baseline_comm
     if fused:
         model.enable_fused_collectives()   # row-parallel GEMMs reduce over NVLink peer memory inside the kernel
     torch.cuda.synchronize()

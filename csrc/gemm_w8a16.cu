@@ -218,57 +218,58 @@ HRM_DEVINL void store_residual_outputs(const GemmArgs& a, int n_tile, int m_tile
   }
 }
 
-// Tensor-parallel residual epilogue, after this rank's partial tile was written to its symmetric buffer:
-// publish it, then the owner rank (tile % world) sums all ranks' partials in rank order + the residual, publishes
-// the reduced tile, and every other rank copies it.  All ranks end with identical x / xg / ssq.
+// Tensor-parallel residual epilogue: one-shot all-reduce by peer-memory PUSH over NVLink (decode, one m tile).
+// Receive area of every rank: [launch parity][source rank][tile][128 rows][max_bn tokens] fp32 (double-buffered by
+// launch parity: a slow peer may still be reading the previous launch's data).
+// Phase 1 (per finished tile, in the overlapped epilogue): the tile's partial is stored into the source-rank slot of
+// EVERY rank's receive area (posted NVLink writes: no round trip on the critical path).
+// Phase 2 (once per CTA, after the mainloop): the CTAs of this rank meet at a grid-wide ticket; the last one fences
+// and writes this rank's epoch into every rank's flag array.  Each CTA waits on its LOCAL flags, then reduces its
+// share of the tiles from local memory: x = resid + sum over source ranks in rank order, so every rank computes
+// bit-identical x / xg / ssq.  One flag hop per launch; every load is local.
+HRM_DEVINL float* ar_slot(const GemmArgs& a, int dst, int src, int par, int tile) {
+  float* base = reinterpret_cast<float*>(reinterpret_cast<char*>(a.peers[dst]) + a.off_partials);
+  return base + (((size_t)par * a.tp_world + src) * a.ar_max_tiles + tile) * a.ar_tile_floats;
+}
+
 template <int BN>
-HRM_DEVINL void ar_reduce_tile(const GemmArgs& a, int n_tile, int m_tile, int row, int et, int ep, float* ssq_red) {
-  const int tile = n_tile;   // decode: one m tile
-  char* local = reinterpret_cast<char*>(a.peers[a.tp_rank]);
-  int* ready = reinterpret_cast<int*>(local + a.off_flags) + tile;
-  int* done = reinterpret_cast<int*>(local + a.off_flags) + a.ar_max_tiles + tile;
-  __threadfence_system();
+HRM_DEVINL void ar_oneshot(const GemmArgs& a, int row, int et, int ep, float* ssq_red) {
+  int* my_flags = reinterpret_cast<int*>(reinterpret_cast<char*>(a.peers[a.tp_rank]) + a.off_flags);
+  __threadfence_system();   // this thread's pushed partials are visible system-wide before the ticket
   asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
-  if (et == 0) st_release_sys(ready, ep);
-  const int owner = tile % a.tp_world;
-  const int n = n_tile * kBM + row;
-  if (owner == a.tp_rank) {
-    if (et < a.tp_world) {
-      const char* pb = reinterpret_cast<const char*>(a.peers[et]);
-      wait_peer_flag(reinterpret_cast<const int*>(pb + a.off_flags) + tile, ep, a.status);
+  if (et == 0) {
+    if (atomicAdd(&a.launch_ticket[0], 1) == (int)gridDim.x - 1) {
+      a.launch_ticket[0] = 0;   // re-arm for the next launch (every CTA has arrived)
+      __threadfence_system();
+      for (int r = 0; r < a.tp_world; ++r)
+        st_release_sys(reinterpret_cast<int*>(reinterpret_cast<char*>(a.peers[r]) + a.off_flags) + a.tp_rank, ep);
     }
-    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
-    float* fin = reinterpret_cast<float*>(local + a.off_final) + (size_t)tile * a.ar_tile_floats;
-    for (int c0 = 0; c0 < BN; c0 += kChunk) {
+  }
+  if (et < a.tp_world) wait_peer_flag(my_flags + et, ep, a.status);
+  asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+  const int par = ep & 1;
+  const int stride = a.ar_tile_floats / kBM;   // tokens per row slot (max_bn)
+  for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+    const int n = t * kBM + row;
+    for (int c0 = 0; c0 < BN && c0 < a.M; c0 += kChunk) {
+      float sum[kChunk];
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) sum[j] = 0.f;
+      for (int src = 0; src < a.tp_world; ++src) {
+        const float4* p = reinterpret_cast<const float4*>(ar_slot(a, a.tp_rank, src, par, t) + (size_t)row * stride + c0);
+#pragma unroll
+        for (int q = 0; q < kChunk / 4; ++q) {
+          const float4 v = __ldcg(p + q);
+          sum[4 * q] += v.x; sum[4 * q + 1] += v.y; sum[4 * q + 2] += v.z; sum[4 * q + 3] += v.w;
+        }
+      }
       float xn[kChunk];
 #pragma unroll
       for (int j = 0; j < kChunk; ++j) {
-        const int m = m_tile * BN + c0 + j;
-        float acc = (m < a.M && n < a.N) ? a.resid[(size_t)m * a.ldr + n] : 0.f;
-        float sum = 0.f;
-        for (int r = 0; r < a.tp_world; ++r) {
-          const float* pp = reinterpret_cast<const float*>(reinterpret_cast<const char*>(a.peers[r]) + a.off_partials) +
-                            (size_t)tile * a.ar_tile_floats + (c0 + j) * kBM + row;
-          sum += __ldcv(pp);
-        }
-        xn[j] = acc + sum;
-        fin[(c0 + j) * kBM + row] = xn[j];
+        const int m = c0 + j;
+        xn[j] = (m < a.M && n < a.N) ? a.resid[(size_t)m * a.ldr + n] + sum[j] : 0.f;
       }
-      store_residual_outputs<BN>(a, n_tile, m_tile, row, c0, xn, et, ssq_red);
-    }
-    __threadfence_system();
-    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
-    if (et == 0) st_release_sys(done, ep);
-  } else {
-    const char* ob = reinterpret_cast<const char*>(a.peers[owner]);
-    if (et == 0) wait_peer_flag(reinterpret_cast<const int*>(ob + a.off_flags) + a.ar_max_tiles + tile, ep, a.status);
-    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
-    const float* fin = reinterpret_cast<const float*>(ob + a.off_final) + (size_t)tile * a.ar_tile_floats;
-    for (int c0 = 0; c0 < BN; c0 += kChunk) {
-      float xn[kChunk];
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) xn[j] = __ldcv(&fin[(c0 + j) * kBM + row]);
-      store_residual_outputs<BN>(a, n_tile, m_tile, row, c0, xn, et, ssq_red);
+      store_residual_outputs<BN>(a, t, 0, row, c0, xn, et, ssq_red);
     }
   }
 }
@@ -341,10 +342,17 @@ HRM_DEVINL void epilogue_store(const GemmArgs& a, int n_tile, int m_tile, int ro
     store_residual_outputs<BN>(a, n_tile, m_tile, row, c0, xn, et, ssq_red);
   } else if constexpr (EPI == EPI_RESID_AR) {
     // this rank's partial tile -> its symmetric buffer ([token][128 rows], one slot per n tile)
-    float* part = reinterpret_cast<float*>(reinterpret_cast<char*>(a.peers[a.tp_rank]) + a.off_partials) +
-                  (size_t)n_tile * a.ar_tile_floats;
+    // push this rank's partial (16 tokens of this thread's row) into every rank's receive slot for this rank
+    const int ep = *reinterpret_cast<const volatile int*>(a.epoch) + 1;
+    const int stride = a.ar_tile_floats / kBM;
+    float4 q[kChunk / 4];
 #pragma unroll
-    for (int j = 0; j < kChunk; ++j) __stcg(&part[(c0 + j) * kBM + row], v[j] * sc);
+    for (int i = 0; i < kChunk / 4; ++i) q[i] = make_float4(v[4 * i] * sc, v[4 * i + 1] * sc, v[4 * i + 2] * sc, v[4 * i + 3] * sc);
+    for (int dst = 0; dst < a.tp_world; ++dst) {
+      float4* p = reinterpret_cast<float4*>(ar_slot(a, dst, a.tp_rank, ep & 1, n_tile) + (size_t)row * stride + c0);
+#pragma unroll
+      for (int i = 0; i < kChunk / 4; ++i) p[i] = q[i];
+    }
   } else {
 #pragma unroll
     for (int j = 0; j < kChunk; ++j) {
@@ -679,7 +687,6 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
           }
           epilogue_store<BN, EPI>(a, n_tile, m_tile, row, c0, v, stage, et, inv, ssq_red);
         }
-        if constexpr (EPI == EPI_RESID_AR) ar_reduce_tile<BN>(a, n_tile, m_tile, row, et, ep, ssq_red);
       } else {
         // partial segment: write fp32 partial, take a ticket; the last segment of the tile reduces in k order
         const int first = owner_of((int64_t)tile * a.k_tiles, U, G);
@@ -720,12 +727,12 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
             }
             epilogue_store<BN, EPI>(a, n_tile, m_tile, row, c0, v, stage, et, inv, ssq_red);
           }
-          if constexpr (EPI == EPI_RESID_AR) ar_reduce_tile<BN>(a, n_tile, m_tile, row, et, ep, ssq_red);
         }
       }
       if (et == 0) trace_mark(a, 6, seg);
       u = ue;
     }
+    if constexpr (EPI == EPI_RESID_AR) ar_oneshot<BN>(a, row, et, ep, ssq_red);
   }
 
   tc_fence_before();
@@ -738,9 +745,9 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
   if constexpr (EPI == EPI_RESID_AR) {
     if (threadIdx.x == 0) {   // the last CTA to finish advances this rank's epoch for the next launch
       __threadfence();
-      if (atomicAdd(a.launch_ticket, 1) == (int)gridDim.x - 1) {
+      if (atomicAdd(&a.launch_ticket[1], 1) == (int)gridDim.x - 1) {
         *reinterpret_cast<volatile int*>(a.epoch) = *reinterpret_cast<volatile int*>(a.epoch) + 1;
-        *a.launch_ticket = 0;
+        a.launch_ticket[1] = 0;
         __threadfence();
       }
     }

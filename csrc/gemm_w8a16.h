@@ -48,7 +48,7 @@ struct GemmArgs {
   int ar_tile_floats;                             // floats per tile slot (max_bn * 128)
   int ar_max_tiles;
   int* epoch;                                     // this rank's launch epoch counter (in its symmetric buffer)
-  int* launch_ticket;                             // CTA-completion ticket (device memory, zero between launches)
+  int* launch_ticket;                             // [2] CTA tickets: phase-1 barrier, kernel end (zero between launches)
   float* ws;                                // stream-K partials: plan.ws_floats floats
   int* counters;                            // stream-K tickets: plan.counters ints, zero before first use
   // EPI_QKV

@@ -6,9 +6,12 @@ write peers directly through a device table of base pointers ``peers[r]`` (``pee
 
 Layout of the buffer (all offsets 256-byte aligned):
 
-* ``partials``  fp32 [max_tiles][max_bn][128]  -- this rank's row-parallel partial tiles;
-* ``final``     fp32 [max_tiles][max_bn][128]  -- reduced tiles owned by this rank (tile % world == rank);
-* ``flags``     int32 [2][max_tiles] (ready, done), plus scalars (the per-launch epoch counter, argmax keys).
+* ``partials``  fp32 [2][world][max_tiles][128][max_bn] -- receive area: every rank pushes its row-parallel partial
+  tiles into slot [launch parity][its rank] of every rank (double-buffered by launch parity: a slow peer may still be
+  reading the previous launch's data when this rank starts the next one);
+* ``final``     fp32 [max_tiles][max_bn][128]  -- spare reduction space;
+* ``flags``     int32 [world]: the epoch up to which each source rank's partials are complete, plus scalars (the
+  per-launch epoch counter and two CTA tickets).
 
 Flags carry an epoch number that every fused launch increments once, so a flag written by a previous launch is never
 mistaken for a current one and no reset pass is needed between launches.
@@ -34,7 +37,7 @@ class SymmetricWorkspace:
         self.max_tiles, self.max_bn = max_tiles, max_bn
         tile_bytes = max_bn * 128 * 4
         self.off_partials = 0
-        self.off_final = _al(self.off_partials + max_tiles * tile_bytes)
+        self.off_final = _al(self.off_partials + 2 * world * max_tiles * tile_bytes)
         self.off_flags = _al(self.off_final + max_tiles * tile_bytes)
         self.off_scalars = _al(self.off_flags + 2 * max_tiles * 4)
         self.off_extra = _al(self.off_scalars + 4096)
@@ -54,7 +57,7 @@ class SymmetricWorkspace:
         self.peers = torch.tensor(self.ptrs, dtype=torch.int64, device=self.device)
         # epoch counter lives in this rank's scalars (local memory); the CTA-completion ticket next to it
         self.epoch = C.tensor_from_ptr(self.local_ptr + self.off_scalars, [1], torch.int32, self.device.index or 0)
-        self.ticket = C.tensor_from_ptr(self.local_ptr + self.off_scalars + 128, [1], torch.int32,
+        self.ticket = C.tensor_from_ptr(self.local_ptr + self.off_scalars + 128, [2], torch.int32,
                                         self.device.index or 0)
         self.group = group
 
