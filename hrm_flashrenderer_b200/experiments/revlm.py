@@ -261,15 +261,25 @@ class RevLM(torch.nn.Module):
 
 # ------------------------------------------------------------------------------------------------ incremental decode
 class ChatState:
-    """Incremental greedy decoding with a per-layer KV cache (batch 1), the reference's chat path (:1856-2165)."""
+    """Incremental greedy decoding with a per-layer KV cache (batch 1), the reference's chat path (:1856-2165).
 
-    def __init__(self, model: RevLM):
+    Every step has static shapes (attention runs over the whole Tmax cache under a position mask, the cache row is
+    written at a device-side index), so on a GPU the step is captured once as a CUDA graph and each token costs one
+    graph replay plus one 8-byte device-to-host read of the next token."""
+
+    def __init__(self, model: RevLM, use_graph: Optional[bool] = None):
         self.m = model
         cfg = model.cfg
         dev = model.device
         self.k = torch.zeros(cfg.layers, cfg.tmax, cfg.heads, cfg.dh, device=dev)
         self.v = torch.zeros_like(self.k)
         self.t = 0
+        self.tok_in = torch.zeros((), dtype=torch.long, device=dev)
+        self.pos_in = torch.zeros((), dtype=torch.long, device=dev)
+        self.tok_out = torch.zeros((), dtype=torch.long, device=dev)
+        self.ar = torch.arange(cfg.tmax, device=dev)
+        self.graph = None
+        self.use_graph = (dev.type == "cuda") if use_graph is None else use_graph
 
     def reset(self) -> None:
         self.k.zero_()
@@ -277,30 +287,57 @@ class ChatState:
         self.t = 0
 
     @torch.no_grad()
-    def step(self, token: int) -> int:
+    def _step_static(self) -> None:
         m, cfg = self.m, self.m.cfg
-        if self.t >= cfg.tmax:
-            raise RuntimeError("context full")
         p = m.p()
-        t = self.t
-        x = p["wte"][token] + p["wpe"][t]
-        y1, y2 = x[:cfg.dhf].clone(), x[cfg.dhf:].clone()
-        cos, sin = m.cos[t:t + 1], m.sin[t:t + 1]
+        t = self.pos_in
+        x = p["wte"][self.tok_in] + p["wpe"][t]
+        y1, y2 = x[:cfg.dhf], x[cfg.dhf:]
+        cos, sin = m.cos[t].unsqueeze(0), m.sin[t].unsqueeze(0)
+        visible = self.ar <= t
         for l in range(cfg.layers):
             n = rms(y2, p[f"gf.{l}"], cfg.eps)
             q = apply_rope((n @ p[f"Wq.{l}"]).view(1, cfg.heads, cfg.dh), cos, sin)[0]
             k = apply_rope((n @ p[f"Wk.{l}"]).view(1, cfg.heads, cfg.dh), cos, sin)[0]
-            self.k[l, t] = k
-            self.v[l, t] = (n @ p[f"Wv.{l}"]).view(cfg.heads, cfg.dh)
-            sc = torch.einsum("hd,thd->ht", q, self.k[l, :t + 1]) / math.sqrt(cfg.dh)
-            o = torch.einsum("ht,thd->hd", torch.softmax(sc, -1), self.v[l, :t + 1]).reshape(cfg.dhf)
+            self.k[l].index_copy_(0, t.view(1), k.unsqueeze(0))
+            self.v[l].index_copy_(0, t.view(1), (n @ p[f"Wv.{l}"]).view(1, cfg.heads, cfg.dh))
+            sc = torch.einsum("hd,thd->ht", q, self.k[l]) / math.sqrt(cfg.dh)
+            sc = sc.masked_fill(~visible[None, :], -float("inf"))
+            o = torch.einsum("ht,thd->hd", torch.softmax(sc, -1), self.v[l]).reshape(cfg.dhf)
             y1 = y1 + o @ p[f"Wo.{l}"]
             n = rms(y1, p[f"gg.{l}"], cfg.eps)
             y2 = y2 + gelu_tanh(n @ p[f"W1.{l}"]) @ p[f"W2.{l}"]
         h = rms(torch.cat([y1, y2]), p["gout"], cfg.eps)
-        logits = h @ p["Wout"][:, :cfg.vocab]
+        self.tok_out.copy_(torch.argmax(h @ p["Wout"][:, :cfg.vocab]))
+
+    def _capture(self) -> None:
+        s = torch.cuda.Stream(device=self.m.device)
+        s.wait_stream(torch.cuda.current_stream(self.m.device))
+        with torch.cuda.stream(s):
+            self._step_static()
+        torch.cuda.current_stream(self.m.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._step_static()
+        self.graph = g
+
+    @torch.no_grad()
+    def step(self, token: int) -> int:
+        if self.t >= self.m.cfg.tmax:
+            raise RuntimeError("context full")
+        self.tok_in.fill_(int(token))
+        self.pos_in.fill_(self.t)
+        if self.use_graph:
+            if self.graph is None:
+                k0, v0 = self.k.clone(), self.v.clone()
+                self._capture()                  # the warm-up and capture ran the step twice: restore the cache
+                self.k.copy_(k0)
+                self.v.copy_(v0)
+            self.graph.replay()
+        else:
+            self._step_static()
         self.t += 1
-        return int(torch.argmax(logits))
+        return int(self.tok_out)
 
 
 # ------------------------------------------------------------------------------------------------ checkpoint v11
