@@ -45,9 +45,37 @@ struct Smem {
 };
 }  // namespace
 
+// One 128-key x 128-dim K or V tile (8 paged blocks of 16 tokens) into the canonical SW128 K-major image
+// [2 dim halves][128 keys][128 B].  When the tile's 8 blocks are consecutive in the pool (the usual case: blocks are
+// handed out lowest id first) two TMA boxes of 8 blocks each bring it; otherwise 16 one-block boxes.  TMA issue cost
+// per instruction, not bytes, bounds this loop, so the 8-block path moves the same 32 KB with 8x fewer instructions.
+HRM_DEVINL void load_kv_tile(uint8_t* dst, const CUtensorMap* m1, const CUtensorMap* m8, uint64_t* bar, const int* btab,
+                             int bi0, int max_blocks, int hk, int num_blocks) {
+  int blk[kKeys / 16];
+  bool run = true;
+#pragma unroll
+  for (int j = 0; j < kKeys / 16; ++j) {
+    const int bi = bi0 + j < max_blocks ? bi0 + j : max_blocks - 1;
+    blk[j] = btab[bi];
+    run = run && blk[j] == blk[0] + j;
+  }
+  run = run && blk[0] >= 0 && blk[0] + kKeys / 16 <= num_blocks;
+  if (run) {
+    tma_load_4d(dst, m8, bar, 0, 0, hk, blk[0]);
+    tma_load_4d(dst + 16384, m8, bar, 64, 0, hk, blk[0]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < kKeys / 16; ++j) {
+      tma_load_4d(dst + j * 2048, m1, bar, 0, 0, hk, blk[j]);
+      tma_load_4d(dst + 16384 + j * 2048, m1, bar, 64, 0, hk, blk[j]);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 2)
 attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                      const DecodeAttnArgs a, int* status) {
+                      const __grid_constant__ CUtensorMap tmK8, const __grid_constant__ CUtensorMap tmV8,
+                      const DecodeAttnArgs a, int num_blocks, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = base + Smem::kRing;
@@ -102,6 +130,8 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
     if (lane == 0 && nt > 0) {
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmK8);
+      tma_prefetch_desc(&tmV8);
       const int* btab = a.block_tables + (size_t)b * a.max_blocks;
       int issued = 0;
       for (int t = 0; t < nt; ++t) {
@@ -112,21 +142,8 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
           if (!mbar_wait_ab(&empty[s], ph ^ 1u, status, kErrTimeoutEmpty, abort_flag)) goto prod_done;
           mbar_arrive_expect_tx(&full[s], kSlotBytes);
           uint8_t* dst = ring + s * kSlotBytes;
-          for (int j = 0; j < kKeys / 16; ++j) {
-            int bi = key0 / 16 + j;
-            bi = bi < a.max_blocks ? bi : a.max_blocks - 1;
-            const int blk = btab[bi];
-            const CUtensorMap* m = kv ? &tmV : &tmK;
-            // 4-D coordinates: (dim, slot, head, block)
-            asm volatile(
-                "cp.async.bulk.tensor.4d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
-                ::"r"(smem_u32(dst + j * 2048)), "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(&full[s])),
-                  "r"(0), "r"(0), "r"(hk), "r"(blk) : "memory");
-            asm volatile(
-                "cp.async.bulk.tensor.4d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
-                ::"r"(smem_u32(dst + 16384 + j * 2048)), "l"(reinterpret_cast<uint64_t>(m)),
-                  "r"(smem_u32(&full[s])), "r"(64), "r"(0), "r"(hk), "r"(blk) : "memory");
-          }
+          load_kv_tile(dst, kv ? &tmV : &tmK, kv ? &tmV8 : &tmK8, &full[s], btab, key0 / 16, a.max_blocks, hk,
+                       num_blocks);
           ++issued;
         }
       }
@@ -307,11 +324,11 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn tmap_encode_fn();
 
-static void make_kv_map(CUtensorMap* m, const void* cache, int num_blocks, int Hk, int bs) {
+static void make_kv_map(CUtensorMap* m, const void* cache, int num_blocks, int Hk, int bs, int blocks_per_box = 1) {
   if ((reinterpret_cast<uintptr_t>(cache) & 15) != 0) throw std::runtime_error("KV cache must be 16-byte aligned");
   cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)bs, (cuuint64_t)Hk, (cuuint64_t)num_blocks};
   cuuint64_t strides[3] = {(cuuint64_t)kD * 2, (cuuint64_t)bs * kD * 2, (cuuint64_t)Hk * bs * kD * 2};
-  cuuint32_t box[4] = {64, (cuuint32_t)bs, 1, 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)bs, 1, (cuuint32_t)blocks_per_box};
   cuuint32_t es[4] = {1, 1, 1, 1};
   CUresult r = tmap_encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(cache), dims, strides, box,
                                 es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -325,9 +342,11 @@ bool decode_attn_tc_supported(const DecodeAttnArgs& a) {
 
 void decode_attn_tc_launch(const DecodeAttnArgs& a, int num_blocks, int* status, cudaStream_t s) {
   if (!decode_attn_tc_supported(a)) throw std::runtime_error("tcgen05 decode attention: unsupported shape");
-  CUtensorMap tk, tv;
+  CUtensorMap tk, tv, tk8, tv8;
   make_kv_map(&tk, a.k_cache, num_blocks, a.Hk, a.block_size);
   make_kv_map(&tv, a.v_cache, num_blocks, a.Hk, a.block_size);
+  make_kv_map(&tk8, a.k_cache, num_blocks, a.Hk, a.block_size, kKeys / 16);
+  make_kv_map(&tv8, a.v_cache, num_blocks, a.Hk, a.block_size, kKeys / 16);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(attn_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::kAlloc);
@@ -335,7 +354,7 @@ void decode_attn_tc_launch(const DecodeAttnArgs& a, int num_blocks, int* status,
   }
   dim3 grid(a.splits, a.Hk, a.B);
   if (status == nullptr) status = status_word();
-  attn_decode_tc_kernel<<<grid, kThreads, Smem::kAlloc, s>>>(tk, tv, a, status);
+  attn_decode_tc_kernel<<<grid, kThreads, Smem::kAlloc, s>>>(tk, tv, tk8, tv8, a, num_blocks, status);
   if (a.splits > 1) decode_combine_launch(a, s);
 }
 
@@ -369,7 +388,9 @@ struct PfSmem {
 
 __global__ void __launch_bounds__(kPfThreads, 1)
 attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, const PrefillAttnArgs a, int tpt, int* status) {
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmK8,
+                       const __grid_constant__ CUtensorMap tmV8, const PrefillAttnArgs a, int tpt, int num_blocks,
+                       int* status) {
   const int G = a.Hq / a.Hk;
   const int tile = gridDim.x - 1 - blockIdx.x;   // heaviest (latest) tiles first
   const int hk = blockIdx.y, seq = blockIdx.z;
@@ -430,6 +451,8 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_con
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmK8);
+      tma_prefetch_desc(&tmV8);
       mbar_arrive_expect_tx(qfull, 2 * 128 * G * tpt);
       tma_load_3d(qs, &tmQ, qfull, 0, hk * G, qo + t0);
       tma_load_3d(qs + kPfRows * 128, &tmQ, qfull, 64, hk * G, qo + t0);
@@ -442,14 +465,8 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_con
             goto pf_prod_done;
           mbar_arrive_expect_tx(&full[s], kSlotBytes);
           uint8_t* dst = ring + s * kSlotBytes;
-          const CUtensorMap* m = kv ? &tmV : &tmK;
-          for (int j = 0; j < kKeys / 16; ++j) {
-            int bi = t * (kKeys / 16) + j;
-            bi = bi < a.max_blocks ? bi : a.max_blocks - 1;
-            const int blk = btab[bi];
-            tma_load_4d(dst + j * 2048, m, &full[s], 0, 0, hk, blk);
-            tma_load_4d(dst + 16384 + j * 2048, m, &full[s], 64, 0, hk, blk);
-          }
+          load_kv_tile(dst, kv ? &tmV : &tmK, kv ? &tmV8 : &tmK8, &full[s], btab, t * (kKeys / 16), a.max_blocks, hk,
+                       num_blocks);
           ++issued;
         }
       }
@@ -627,6 +644,9 @@ void prefill_attn_tc_launch(const PrefillAttnArgs& a, int num_blocks, int total_
   }
   make_kv_map(&tk, a.k_cache, num_blocks, a.Hk, a.block_size);
   make_kv_map(&tv, a.v_cache, num_blocks, a.Hk, a.block_size);
+  CUtensorMap tk8, tv8;
+  make_kv_map(&tk8, a.k_cache, num_blocks, a.Hk, a.block_size, kKeys / 16);
+  make_kv_map(&tv8, a.v_cache, num_blocks, a.Hk, a.block_size, kKeys / 16);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PfSmem::kAlloc);
@@ -634,7 +654,7 @@ void prefill_attn_tc_launch(const PrefillAttnArgs& a, int num_blocks, int total_
   }
   if (status == nullptr) status = status_word();
   dim3 grid((a.max_q + tpt - 1) / tpt, a.Hk, a.S);
-  attn_prefill_tc_kernel<<<grid, kPfThreads, PfSmem::kAlloc, s>>>(tq, tk, tv, a, tpt, status);
+  attn_prefill_tc_kernel<<<grid, kPfThreads, PfSmem::kAlloc, s>>>(tq, tk, tv, tk8, tv8, a, tpt, num_blocks, status);
 }
 
 }  // namespace hrm

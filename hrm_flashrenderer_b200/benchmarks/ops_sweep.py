@@ -103,13 +103,17 @@ def main():
             nb = B * (L // 16) + 8
             kc = torch.randn(nb, Hk, 16, D, device=dev, dtype=torch.bfloat16)
             vc = torch.randn_like(kc)
-            tab = torch.randperm(nb - 8, device=dev)[:B * (L // 16)].view(B, L // 16).to(torch.int32)
             cl = torch.full((B,), L, dtype=torch.int32, device=dev)
             q = torch.randn(B, Hq, D, device=dev, dtype=torch.bfloat16)
             out = torch.empty(B, Hq, D, device=dev, dtype=torch.float16)
-            us = time_op(lambda: ops.paged_decode_attention(q, kc, vc, tab, cl, out=out, max_ctx=L), a.iters,
-                         a.warmup, flush)
-            rec("attn_decode", f"B{B}xL{L}xHq{Hq}xHk{Hk}", us, 2 * B * L * Hk * D * 2, 4.0 * B * Hq * L * D)
+            # scattered block ids: one 4 KB TMA box per block; in-order ids: one box per 8 blocks (128 keys)
+            for layout, ids in (("scattered", torch.randperm(nb - 8, device=dev)),
+                                ("contiguous", torch.arange(nb - 8, device=dev))):
+                tab = ids[:B * (L // 16)].view(B, L // 16).to(torch.int32)
+                us = time_op(lambda: ops.paged_decode_attention(q, kc, vc, tab, cl, out=out, max_ctx=L), a.iters,
+                             a.warmup, flush)
+                rec("attn_decode", f"B{B}xL{L}xHq{Hq}xHk{Hk}/{layout}", us, 2 * B * L * Hk * D * 2,
+                    4.0 * B * Hq * L * D)
             del kc, vc
         for T in (512, 4096):
             nb = T // 16 + 8

@@ -8,6 +8,7 @@ run (4 KB at bf16/D=128), the unit the attention kernels fetch.
 """
 from __future__ import annotations
 
+import heapq
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence
 
@@ -19,18 +20,34 @@ class OutOfBlocks(RuntimeError):
 
 
 class BlockManager:
-    """Free-list allocator of KV blocks.  Deterministic: the lowest free block id is always handed out first."""
+    """Free-list allocator of KV blocks, deterministic and tile-aware.
 
-    def __init__(self, num_blocks: int, block_size: int = 16):
+    The attention kernels read keys in tiles of ``tile_blocks`` consecutive table entries (128 keys = 8 blocks of 16)
+    and fetch a tile with ONE TMA box when its block ids are consecutive, else one box per block.  So:
+      * a block that starts a tile (table position % tile_blocks == 0) is the first id of the lowest fully free
+        aligned group of ``tile_blocks`` ids, when one exists;
+      * any other block is the id right after the sequence's previous block, when that id is free;
+      * otherwise the lowest free id.
+    Nothing is reserved: another sequence may take an id of a started group, which only costs that tile its fast
+    fetch.  The reference grows contiguous per-sequence pages by reallocation instead (``engine/llama_tp.py:21-108``).
+    """
+
+    def __init__(self, num_blocks: int, block_size: int = 16, tile_blocks: int = 8):
         self.num_blocks = int(num_blocks)
         self.block_size = int(block_size)
-        self._free: List[int] = list(range(self.num_blocks - 1, -1, -1))   # pop() yields the lowest id
+        self.tile_blocks = max(1, int(tile_blocks))
+        self._is_free = bytearray(b"\x01") * self.num_blocks
+        self._nfree = self.num_blocks
+        self._heap: List[int] = list(range(self.num_blocks))                 # lowest-free heap (lazy deletion)
+        ng = self.num_blocks // self.tile_blocks                              # only whole groups are candidates
+        self._gfree = [self.tile_blocks] * ng
+        self._gheap: List[int] = list(range(ng))                              # fully free groups (lazy deletion)
         self.tables: Dict[int, List[int]] = {}
         self.lengths: Dict[int, int] = {}
 
     @property
     def free_blocks(self) -> int:
-        return len(self._free)
+        return self._nfree
 
     def blocks_needed(self, seq_id: int, new_len: int) -> int:
         have = len(self.tables.get(seq_id, ()))
@@ -38,27 +55,57 @@ class BlockManager:
         return max(0, need - have)
 
     def can_grow(self, seq_id: int, new_len: int) -> bool:
-        return self.blocks_needed(seq_id, new_len) <= len(self._free)
+        return self.blocks_needed(seq_id, new_len) <= self._nfree
+
+    def _take(self, b: int) -> int:
+        self._is_free[b] = 0
+        self._nfree -= 1
+        g = b // self.tile_blocks
+        if g < len(self._gfree):
+            self._gfree[g] -= 1
+        return b
+
+    def _pick(self, tab: List[int]) -> int:
+        tb = self.tile_blocks
+        if tab and len(tab) % tb:
+            nxt = tab[-1] + 1
+            if nxt < self.num_blocks and self._is_free[nxt]:
+                return self._take(nxt)
+        else:
+            while self._gheap and self._gfree[self._gheap[0]] != tb:
+                heapq.heappop(self._gheap)
+            if self._gheap:
+                return self._take(heapq.heappop(self._gheap) * tb)
+        while not self._is_free[self._heap[0]]:
+            heapq.heappop(self._heap)
+        return self._take(heapq.heappop(self._heap))
 
     def grow(self, seq_id: int, new_len: int) -> List[int]:
         """Ensure ``seq_id`` can hold ``new_len`` tokens; returns its block table."""
         n = self.blocks_needed(seq_id, new_len)
-        if n > len(self._free):
-            raise OutOfBlocks(f"need {n} blocks for seq {seq_id}, {len(self._free)} free")
+        if n > self._nfree:
+            raise OutOfBlocks(f"need {n} blocks for seq {seq_id}, {self._nfree} free")
         tab = self.tables.setdefault(seq_id, [])
         for _ in range(n):
-            tab.append(self._free.pop())
+            tab.append(self._pick(tab))
         self.lengths[seq_id] = max(self.lengths.get(seq_id, 0), int(new_len))
         return tab
 
     def free(self, seq_id: int) -> None:
-        for b in reversed(self.tables.pop(seq_id, [])):
-            self._free.append(b)
-        self._free.sort(reverse=True)
+        tb = self.tile_blocks
+        for b in self.tables.pop(seq_id, []):
+            self._is_free[b] = 1
+            self._nfree += 1
+            heapq.heappush(self._heap, b)
+            g = b // tb
+            if g < len(self._gfree):
+                self._gfree[g] += 1
+                if self._gfree[g] == tb:
+                    heapq.heappush(self._gheap, g)
         self.lengths.pop(seq_id, None)
 
     def reset(self) -> None:
-        self.__init__(self.num_blocks, self.block_size)
+        self.__init__(self.num_blocks, self.block_size, self.tile_blocks)
 
     def table_tensor(self, seq_ids: Sequence[int], width: Optional[int] = None, device="cpu") -> torch.Tensor:
         """``[len(seq_ids), width]`` int32 block tables padded with 0 (padding is never read: lengths bound it)."""

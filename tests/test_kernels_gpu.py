@@ -171,10 +171,10 @@ def test_w8a16_qkv_rope_append(D, M):
         assert (vcc[sl // bs, :, sl % bs] - vr[m]).abs().max().item() < 2e-2
 
 
-def _paged(B, lens, Hk, D, bs=16, seed=0):
+def _paged(B, lens, Hk, D, bs=16, seed=0, contiguous=False):
     g = torch.Generator().manual_seed(seed)
     nb = sum((L + bs - 1) // bs for L in lens) + 4
-    perm = torch.randperm(nb, generator=g)
+    perm = torch.arange(nb) if contiguous else torch.randperm(nb, generator=g)
     kc = torch.randn(nb, Hk, bs, D, generator=g).to(torch.bfloat16)
     vc = torch.randn(nb, Hk, bs, D, generator=g).to(torch.bfloat16)
     maxb = max((L + bs - 1) // bs for L in lens)
@@ -203,6 +203,43 @@ def test_paged_decode_attention(D, Hq, Hk, lens, splits, tc):
         per = (tiles + splits - 1) // splits
         kw = dict(splits=(tiles + per - 1) // per, keys_per_split=per * 128)
     out = ops.paged_decode_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), tab.to(DEV), cl.to(DEV), allow_tc=tc, **kw)
+    ops.check_status()
+    assert (out.float().cpu() - ref.float()).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("lens", [[4096], [33, 2000, 129, 128], [1, 17, 300]])
+@pytest.mark.parametrize("splits", [0, 3])
+def test_paged_decode_attention_contiguous_blocks(lens, splits):
+    """Pool blocks handed out in order: whole 128-key tiles come in as 8-block TMA boxes (plus one-block boxes at
+    sequence tails), same results as the reference."""
+    B = len(lens)
+    kc, vc, tab = _paged(B, lens, 8, 128, contiguous=True)
+    q = torch.randn(B, 64, 128).to(torch.bfloat16)
+    cl = torch.tensor(lens, dtype=torch.int32)
+    ref = ops.paged_decode_attention(q, kc, vc, tab, cl)
+    kw = {}
+    if splits:
+        tiles = (tab.shape[1] * 16 + 127) // 128
+        per = (tiles + splits - 1) // splits
+        kw = dict(splits=(tiles + per - 1) // per, keys_per_split=per * 128)
+    out = ops.paged_decode_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), tab.to(DEV), cl.to(DEV), **kw)
+    ops.check_status()
+    assert (out.float().cpu() - ref.float()).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("chunks", [[(0, 300)], [(200, 1029), (0, 17)], [(0, 2048)]])
+def test_paged_prefill_attention_contiguous_blocks(chunks):
+    lens = [a + b for a, b in chunks]
+    kc, vc, tab = _paged(len(chunks), lens, 8, 128, seed=4, contiguous=True)
+    Tq = sum(b for _, b in chunks)
+    q = torch.randn(Tq, 64, 128).to(torch.bfloat16)
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor([b for _, b in chunks]), 0)), dtype=torch.int32)
+    qs = torch.tensor([a for a, _ in chunks], dtype=torch.int32)
+    cl = torch.tensor(lens, dtype=torch.int32)
+    mq = max(b for _, b in chunks)
+    ref = ops.paged_prefill_attention(q, kc, vc, tab, cu, qs, cl, mq)
+    out = ops.paged_prefill_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), tab.to(DEV), cu.to(DEV), qs.to(DEV),
+                                      cl.to(DEV), mq)
     ops.check_status()
     assert (out.float().cpu() - ref.float()).abs().max().item() < 2e-2
 
