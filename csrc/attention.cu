@@ -13,6 +13,7 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <algorithm>
 #include <stdexcept>
 
 namespace hrm {
@@ -160,6 +161,8 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeAttnArgs a
 
 template <int D>
 __global__ void decode_combine_kernel(const DecodeAttnArgs a) {
+  pdl_wait();      // partials come from the attention grid launched just before
+  pdl_trigger();
   const int bh = blockIdx.x;
   const int d = threadIdx.x;
   const float* p = a.ws + (size_t)bh * a.splits * (D + 2);
@@ -179,8 +182,8 @@ __global__ void decode_combine_kernel(const DecodeAttnArgs a) {
 }
 
 void decode_combine_launch(const DecodeAttnArgs& a, cudaStream_t s) {
-  if (a.D == 128) decode_combine_kernel<128><<<a.B * a.Hq, 128, 0, s>>>(a);
-  else decode_combine_kernel<64><<<a.B * a.Hq, 64, 0, s>>>(a);
+  if (a.D == 128) launch_maybe_pdl(decode_combine_kernel<128>, dim3(a.B * a.Hq), dim3(128), 0, s, a);
+  else launch_maybe_pdl(decode_combine_kernel<64>, dim3(a.B * a.Hq), dim3(64), 0, s, a);
 }
 
 size_t decode_attn_ws_floats(int B, int Hq, int D, int splits) { return (size_t)B * Hq * splits * (D + 2); }
@@ -308,42 +311,88 @@ void prefill_attn_launch(const PrefillAttnArgs& a, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------------------------------------ argmax
-__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V, int ld,
-                                                      int vocab_start, unsigned long long* keys,
-                                                      int64_t* tokens) {
-  const int row = blockIdx.x;
+// Greedy pick over a row of logits, split over gridDim.x CTAs per row so a decode batch of a few rows still
+// streams the [M, V] logits with the whole GPU (one 1024-thread CTA per row took ~60 us for 16 x 128256).  Each CTA
+// reduces its slice to one packed key (order-preserving float bits, then ~index: larger value wins, ties go to the
+// lower id); slices meet in atomicMax on the row's accumulator, which is order independent, so the result is
+// deterministic.  The CTA that takes the last ticket publishes the key / token and re-arms accumulator and ticket
+// (both start at zero).
+__global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ logits, int V, int ld, int chunk,
+                                                     int vocab_start, unsigned long long* acc,
+                                                     unsigned long long* ticket, unsigned long long* keys,
+                                                     int64_t* tokens) {
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.y;
   const float* lr = logits + (size_t)row * ld;
+  const int i0 = blockIdx.x * chunk, i1 = min(V, i0 + chunk);
   unsigned long long best = 0ull;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const unsigned long long k = argmax_key(lr[i], (uint32_t)(vocab_start + i));
-    best = k > best ? k : best;
+  const bool vec = ((reinterpret_cast<uintptr_t>(lr + i0) & 15) == 0) && (chunk % 4 == 0);
+  if (vec) {
+    const int n4 = (i1 - i0) >> 2;
+    const float4* l4 = reinterpret_cast<const float4*>(lr + i0);
+    for (int j = threadIdx.x; j < n4; j += blockDim.x) {
+      const float4 v = l4[j];
+      const uint32_t id = (uint32_t)(vocab_start + i0 + 4 * j);
+      unsigned long long k = argmax_key(v.x, id);
+      unsigned long long t = argmax_key(v.y, id + 1);
+      k = t > k ? t : k;
+      t = argmax_key(v.z, id + 2);
+      k = t > k ? t : k;
+      t = argmax_key(v.w, id + 3);
+      k = t > k ? t : k;
+      best = k > best ? k : best;
+    }
+    for (int i = i0 + 4 * n4 + threadIdx.x; i < i1; i += blockDim.x) {
+      const unsigned long long k = argmax_key(lr[i], (uint32_t)(vocab_start + i));
+      best = k > best ? k : best;
+    }
+  } else {
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+      const unsigned long long k = argmax_key(lr[i], (uint32_t)(vocab_start + i));
+      best = k > best ? k : best;
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
     best = other > best ? other : best;
   }
-  __shared__ unsigned long long red[32];
+  __shared__ unsigned long long red[8];
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
   __syncthreads();
-  if (threadIdx.x < 32) {
-    best = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-      best = other > best ? other : best;
-    }
-    if (threadIdx.x == 0) {
-      if (keys) keys[row] = best ^ (1ull << 63);   // signed-int64 order == unsigned key order
-      if (tokens) tokens[row] = (int64_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
-    }
+  if (threadIdx.x != 0) return;
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+  if (gridDim.x > 1) {
+    atomicMax(&acc[row], best);
+    __threadfence();
+    if (atomicAdd(&ticket[row], 1ull) != (unsigned long long)(gridDim.x - 1)) return;
+    __threadfence();
+    best = atomicExch(&acc[row], 0ull);
+    ticket[row] = 0ull;
   }
+  if (keys) keys[row] = best ^ (1ull << 63);   // signed-int64 order == unsigned key order
+  if (tokens) tokens[row] = (int64_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+}
+
+int argmax_chunks(int M, int V, int sms) {
+  if (M > kArgmaxMaxRows) return 1;
+  int c = (2 * sms + M - 1) / M;
+  c = std::min(c, std::max(1, V / 2048));
+  return std::max(1, c);
 }
 
 void argmax_launch(const float* logits, int M, int V, int ld, int vocab_start, unsigned long long* keys,
-                   int64_t* tokens, cudaStream_t s) {
+                   int64_t* tokens, unsigned long long* scratch, int sms, cudaStream_t s) {
   if (M == 0) return;
-  argmax_kernel<<<M, 1024, 0, s>>>(logits, V, ld, vocab_start, keys, tokens);
+  const int c = scratch != nullptr ? argmax_chunks(M, V, sms) : 1;
+  int chunk = (V + c - 1) / c;
+  chunk = (chunk + 3) & ~3;
+  const int grid_x = (V + chunk - 1) / chunk;
+  unsigned long long* acc = scratch;
+  unsigned long long* ticket = scratch != nullptr ? scratch + kArgmaxMaxRows : nullptr;
+  launch_maybe_pdl(argmax_kernel, dim3(grid_x, M), dim3(256), 0, s, logits, V, ld, chunk, vocab_start, acc, ticket,
+                   keys, tokens);
 }
 
 }  // namespace hrm

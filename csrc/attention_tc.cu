@@ -33,13 +33,18 @@ constexpr int kSlots = 3;
 constexpr int kThreads = 6 * 32;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
+// Lazy rescale: the running max used for P and O only moves when a tile's max exceeds it by more than this (log2
+// units), so P <= 2^8 and O / the row sums stay exact relative to the same reference max.
+constexpr float kRescaleLog2 = 8.f;
+// In-kernel split merge stages (max, sum) of up to this many (head, split) pairs in the 8 KB of P buffers.
+constexpr int kMergeMax = 960;
 
 struct Smem {
   static constexpr int kRing = 0;                                  // kSlots x 32 KB
   static constexpr int kQ = kRing + kSlots * kSlotBytes;           // 2 regions x 16 rows x 128 B = 4 KB
-  static constexpr int kP = kQ + 2 * kN * 128;                     // 4 KB
-  static constexpr int kRed = kP + 2 * kN * 128;                   // [4 warps][16] floats
-  static constexpr int kBar = kRed + 4 * kN * 4 + 64 * 4;
+  static constexpr int kP = kQ + 2 * kN * 128;                     // 2 buffers x 4 KB
+  static constexpr int kRed = kP + 2 * 2 * kN * 128;               // [3][4 warps][16] floats: 2 max buffers + sums
+  static constexpr int kBar = kRed + 3 * 4 * kN * 4;
   static constexpr int kBytes = kBar + 16 * 8 + 16;
   static constexpr int kAlloc = kBytes + 1024;
 };
@@ -81,13 +86,13 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
   uint8_t* ring = base + Smem::kRing;
   uint8_t* qs = base + Smem::kQ;
   uint8_t* ps = base + Smem::kP;
-  float* red = reinterpret_cast<float*>(base + Smem::kRed);     // [4][16] tile maxima, reused for final sums
+  float* red = reinterpret_cast<float*>(base + Smem::kRed);     // [2][4][16] tile maxima, then [4][16] sums
   uint64_t* full = reinterpret_cast<uint64_t*>(base + Smem::kBar);
   uint64_t* empty = full + kSlots;
-  uint64_t* sfull = empty + kSlots;     // [2]
-  uint64_t* pfull = sfull + 2;
-  uint64_t* pvdone = pfull + 1;
-  uint64_t* qready = pvdone + 1;
+  uint64_t* sfull = empty + kSlots;     // [2] S buffer (t & 1) written
+  uint64_t* pfull = sfull + 2;          // [2] P buffer (t & 1) written
+  uint64_t* pvdone = pfull + 2;         // [2] O MMA of tile t (which read P buffer t & 1) complete
+  uint64_t* qready = pvdone + 2;
   uint64_t* mdone = qready + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -95,10 +100,6 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int G = a.Hq / a.Hk;
-  const int ctx = a.context_lens[b];
-  const int k0 = split * a.keys_per_split;
-  const int k1 = min(ctx, k0 + a.keys_per_split);
-  const int nt = k1 > k0 ? (k1 - k0 + kKeys - 1) / kKeys : 0;
   const float scale2 = a.scale * kLog2e;
 
   if (threadIdx.x == 0) {
@@ -106,10 +107,11 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(&sfull[0], 1);
-    mbar_init(&sfull[1], 1);
-    mbar_init(pfull, 128);
-    mbar_init(pvdone, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sfull[i], 1);
+      mbar_init(&pfull[i], 128);
+      mbar_init(&pvdone[i], 1);
+    }
     mbar_init(qready, 128);
     mbar_init(mdone, 1);
     *abort_flag = 0;
@@ -124,9 +126,21 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tO = tmem + 32;
+  // With kv_prefetch the caller vouches that the previous grid writes no block table, no context length and no KV
+  // entry except the last key of each sequence: the producer then streams the older tiles before pdl_wait().
+  const bool early = warp == 0 && lane == 0 && a.kv_prefetch;
+  if (!early) {
+    pdl_wait();
+    pdl_trigger();
+  }
+  const int ctx = a.context_lens[b];
+  const int k0 = split * a.keys_per_split;
+  const int k1 = min(ctx, k0 + a.keys_per_split);
+  const int nt = k1 > k0 ? (k1 - k0 + kKeys - 1) / kKeys : 0;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
+    bool waited = !early;
     if (lane == 0 && nt > 0) {
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
@@ -136,6 +150,11 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
       int issued = 0;
       for (int t = 0; t < nt; ++t) {
         const int key0 = k0 + t * kKeys;
+        if (!waited && key0 + kKeys >= ctx) {   // this tile holds the newest key: written by the previous grid
+          pdl_wait();
+          pdl_trigger();
+          waited = true;
+        }
         for (int kv = 0; kv < 2; ++kv) {
           const int u = 2 * t + kv, s = u % kSlots;
           const uint32_t ph = (uint32_t)(u / kSlots) & 1u;
@@ -151,6 +170,10 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
       // drain: every issued TMA must have landed before the CTA may exit
       for (int u = max(0, issued - kSlots); u < issued; ++u)
         mbar_wait(&full[u % kSlots], (uint32_t)(u / kSlots) & 1u, status, kErrTimeoutFull);
+    }
+    if (!waited) {
+      pdl_wait();
+      pdl_trigger();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -178,19 +201,20 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
       ok = ok && issue_s(0);
       for (int t = 0; ok && t < nt; ++t) {
         if (t + 1 < nt && !issue_s(t + 1)) break;
-        if (!mbar_wait_ab(pfull, (uint32_t)t & 1u, status, kErrTimeoutDequant, abort_flag)) break;
+        if (!mbar_wait_ab(&pfull[t & 1], (uint32_t)(t >> 1) & 1u, status, kErrTimeoutDequant, abort_flag)) break;
         const int u = 2 * t + 1, s = u % kSlots;
         if (!mbar_wait_ab(&full[s], (uint32_t)(u / kSlots) & 1u, status, kErrTimeoutFull, abort_flag)) break;
         tc_fence_after();
         const uint32_t va = smem_u32(ring + s * kSlotBytes);
+        const uint32_t pb = pa + (uint32_t)(t & 1) * (2 * kN * 128);
 #pragma unroll
         for (int kk = 0; kk < kKeys / 16; ++kk) {
           const uint32_t poff = (kk >> 2) * (kN * 128) + (kk & 3) * 32;
-          umma_f16_ss(tO, sdesc_sw128_mn(va + kk * 2048, 16384), sdesc_sw128(pa + poff), idO,
+          umma_f16_ss(tO, sdesc_sw128_mn(va + kk * 2048, 16384), sdesc_sw128(pb + poff), idO,
                       (t > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&empty[s]);
-        umma_commit(pvdone);
+        umma_commit(&pvdone[t & 1]);
       }
       // drain: all issued MMAs complete before TMEM is read for the last time / freed
       umma_commit(mdone);
@@ -226,44 +250,51 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
       tmem_ld16(tmem + (uint32_t)(it & 1) * 16u + ((uint32_t)(quad * 32) << 16), s);
       const int key = k0 + it * kKeys + row;
       const bool valid = key < k1;
-      float tmax[kN];
+      float* rbuf = red + (it & 1) * (4 * kN);
 #pragma unroll
       for (int h = 0; h < kN; ++h) {
-        s[h] = valid ? s[h] * scale2 : -INFINITY;
-        tmax[h] = warp_max(s[h]);
-      }
-      if (lane == 0) {
-#pragma unroll
-        for (int h = 0; h < kN; ++h) red[w4 * kN + h] = tmax[h];
+        if (h < G) {                      // padded heads (h >= G) are never output: skip their softmax
+          s[h] = valid ? s[h] * scale2 : -INFINITY;
+          const float tm = warp_max(s[h]);
+          if (lane == 0) rbuf[w4 * kN + h] = tm;
+        }
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
       float corr[kN];
       bool any_corr = false;
 #pragma unroll
       for (int h = 0; h < kN; ++h) {
-        const float tm = fmaxf(fmaxf(red[h], red[kN + h]), fmaxf(red[2 * kN + h], red[3 * kN + h]));
-        const float mn = fmaxf(mrun[h], tm);
-        corr[h] = (mn == -INFINITY || mrun[h] == mn) ? 1.f : exp2f(mrun[h] - mn);
-        any_corr |= corr[h] != 1.f;
-        const float p = (mn == -INFINITY) ? 0.f : exp2f(s[h] - mn);
-        s[h] = p;
-        lsum[h] = lsum[h] * corr[h] + p;
-        mrun[h] = mn;
+        corr[h] = 1.f;
+        if (h < G) {
+          const float tm = fmaxf(fmaxf(rbuf[h], rbuf[kN + h]), fmaxf(rbuf[2 * kN + h], rbuf[3 * kN + h]));
+          if (tm > mrun[h] + kRescaleLog2) {        // also taken on the first tile with a finite key (mrun = -inf)
+            corr[h] = mrun[h] == -INFINITY ? 0.f : exp2f(mrun[h] - tm);
+            any_corr = true;
+            mrun[h] = tm;
+          }
+          const float p = (mrun[h] == -INFINITY) ? 0.f : exp2f(s[h] - mrun[h]);
+          s[h] = p;
+          lsum[h] = lsum[h] * corr[h] + p;
+        }
       }
-      // previous P.V must be done before P is overwritten and O rescaled
-      if (it > 0) mbar_wait_ab(pvdone, (uint32_t)(it - 1) & 1u, status, kErrTimeoutAccum, abort_flag);
-      tc_fence_after();
+      // P buffer (it & 1) was last read by the O MMA of tile it - 2
+      if (it > 1) mbar_wait_ab(&pvdone[it & 1], (uint32_t)((it - 2) >> 1) & 1u, status, kErrTimeoutAccum, abort_flag);
       // P^T operand: row h, key k=row -> region k/64, chunk ((k%64)/8) ^ (h%8), byte (k%8)*2
       {
         const int reg = row >> 6, kk = row & 63;
-        uint8_t* pb = ps + reg * (kN * 128) + ((kk & 7) << 1);
+        uint8_t* pb = ps + (it & 1) * (2 * kN * 128) + reg * (kN * 128) + ((kk & 7) << 1);
 #pragma unroll
         for (int h = 0; h < kN; ++h) {
-          __nv_bfloat16 v = __float2bfloat16_rn(s[h]);
-          *reinterpret_cast<__nv_bfloat16*>(pb + h * 128 + ((((kk >> 3) ^ (h & 7))) << 4)) = v;
+          if (h < G) {
+            __nv_bfloat16 v = __float2bfloat16_rn(s[h]);
+            *reinterpret_cast<__nv_bfloat16*>(pb + h * 128 + ((((kk >> 3) ^ (h & 7))) << 4)) = v;
+          }
         }
       }
-      if (it > 0 && any_corr) {   // any_corr is uniform: every thread saw the same maxima
+      // any_corr is uniform (every thread saw the same maxima).  O holds tiles < it: rescale after O(it - 1) lands.
+      if (it > 0 && any_corr) {
+        mbar_wait_ab(&pvdone[(it - 1) & 1], (uint32_t)((it - 1) >> 1) & 1u, status, kErrTimeoutAccum, abort_flag);
+        tc_fence_after();
         float o[kN];
         tmem_ld16(tO + ((uint32_t)(quad * 32) << 16), o);
         uint32_t ob[kN];
@@ -273,19 +304,20 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(pfull);
-      asm volatile("bar.sync 1, 128;" ::: "memory");   // red[] reused next tile
+      mbar_arrive(&pfull[it & 1]);
     }
 
     // ---------------------------------------------------------------- epilogue
     // global row sums: reduce per-thread partial sums over the 128 threads
 #pragma unroll
     for (int h = 0; h < kN; ++h) lsum[h] = warp_sum(lsum[h]);
+    float* sums = red + 2 * (4 * kN);
     if (lane == 0) {
 #pragma unroll
-      for (int h = 0; h < kN; ++h) red[w4 * kN + h] = lsum[h];
+      for (int h = 0; h < kN; ++h) sums[w4 * kN + h] = lsum[h];
     }
-    if (nt > 0) mbar_wait_ab(pvdone, (uint32_t)(nt - 1) & 1u, status, kErrTimeoutAccum, abort_flag);
+    if (nt > 0)
+      mbar_wait_ab(&pvdone[(nt - 1) & 1], (uint32_t)((nt - 1) >> 1) & 1u, status, kErrTimeoutAccum, abort_flag);
     tc_fence_after();
     asm volatile("bar.sync 1, 128;" ::: "memory");
     float o[kN];
@@ -294,7 +326,7 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
 #pragma unroll
     for (int h = 0; h < kN; ++h) {
       if (h >= G) break;
-      const float L = red[h] + red[kN + h] + red[2 * kN + h] + red[3 * kN + h];
+      const float L = sums[h] + sums[kN + h] + sums[2 * kN + h] + sums[3 * kN + h];
       const float A = nt > 0 ? o[h] : 0.f;
       const int hq = hk * G + h;
       if (a.splits == 1) {
@@ -305,6 +337,57 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
         if (d == 0) {
           p[0] = nt > 0 ? mrun[h] * kLn2 : -INFINITY;
           p[1] = L;
+        }
+      }
+    }
+    if (a.splits > 1 && a.tickets != nullptr) {
+      // split merge in-kernel: the last CTA of this (sequence, kv head) to publish its partials combines all splits
+      // in split order (deterministic whichever CTA is last), same math as decode_combine_kernel
+      volatile int* is_last = reinterpret_cast<volatile int*>(red);   // tile maxima are no longer needed
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (t == 0) {
+        int* tk = a.tickets + (size_t)b * a.Hk + hk;
+        const int prev = atomicAdd(tk, 1);
+        *is_last = prev == a.splits - 1;
+        if (prev == a.splits - 1) *tk = 0;   // re-arm: every split of this launch has counted
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (*is_last) {
+        // all loads of a round are independent: stage (m, L) of every (head, split) in the P buffers (free now:
+        // the last O MMA has completed), per-head factors next, then each thread (= output dim) sums its column
+        __threadfence();
+        const int n = G * a.splits;                   // <= kMergeMax (checked on the host)
+        float* mst = reinterpret_cast<float*>(ps);    // [n] split maxima -> weights exp(m_s - M)
+        float* lst = mst + kMergeMax;                 // [n] split row sums
+        float* linv = lst + kMergeMax;                // [G] 1 / merged row sum (0 when empty)
+        for (int i = t; i < n; i += 128) {
+          const int h = i / a.splits, sp = i - h * a.splits;
+          const float* p = a.ws + (((size_t)b * a.Hq + hk * G + h) * a.splits + sp) * (kD + 2);
+          mst[i] = __ldcg(p);
+          lst[i] = __ldcg(p + 1);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (t < G) {
+          float M = -INFINITY;
+          for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, mst[t * a.splits + sp]);
+          float L = 0.f;
+          for (int sp = 0; sp < a.splits; ++sp) {
+            const float ms = mst[t * a.splits + sp];
+            const float f = (M == -INFINITY || ms == -INFINITY) ? 0.f : __expf(ms - M);
+            mst[t * a.splits + sp] = f;
+            L += lst[t * a.splits + sp] * f;
+          }
+          linv[t] = L > 0.f ? 1.f / L : 0.f;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        for (int h = 0; h < G; ++h) {
+          const int hq = hk * G + h;
+          const float* p = a.ws + ((size_t)b * a.Hq + hq) * a.splits * (kD + 2) + 2 + d;
+          float A = 0.f;
+#pragma unroll 4
+          for (int sp = 0; sp < a.splits; ++sp) A += __ldcg(p + sp * (kD + 2)) * mst[h * a.splits + sp];
+          a.out[((size_t)b * a.Hq + hq) * kD + d] = __float2half_rn(A * linv[h]);
         }
       }
     }
@@ -336,6 +419,8 @@ static void make_kv_map(CUtensorMap* m, const void* cache, int num_blocks, int H
   if (r != CUDA_SUCCESS) throw std::runtime_error("KV tensor map encode failed: " + std::to_string((int)r));
 }
 
+int decode_attn_tc_merge_max() { return kMergeMax; }
+
 bool decode_attn_tc_supported(const DecodeAttnArgs& a) {
   return a.D == kD && a.block_size == 16 && a.Hq / a.Hk <= kN && a.keys_per_split % kKeys == 0;
 }
@@ -354,8 +439,9 @@ void decode_attn_tc_launch(const DecodeAttnArgs& a, int num_blocks, int* status,
   }
   dim3 grid(a.splits, a.Hk, a.B);
   if (status == nullptr) status = status_word();
-  attn_decode_tc_kernel<<<grid, kThreads, Smem::kAlloc, s>>>(tk, tv, tk8, tv8, a, num_blocks, status);
-  if (a.splits > 1) decode_combine_launch(a, s);
+  launch_maybe_pdl(attn_decode_tc_kernel, grid, dim3(kThreads), (size_t)Smem::kAlloc, s, tk, tv, tk8, tv8, a,
+                   num_blocks, status);
+  if (a.splits > 1 && a.tickets == nullptr) decode_combine_launch(a, s);
 }
 
 

@@ -277,9 +277,10 @@ void embed_q8(at::Tensor ids, at::Tensor q, at::Tensor scale, int64_t vocab_star
                        (int)ids.numel(), H, (int)vocab_start, (int)q.size(0), cur_stream());
 }
 
-void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_tables,
-                      at::Tensor context_lens, at::Tensor out, at::Tensor ws, int64_t splits, int64_t keys_per_split,
-                      double scale, c10::optional<at::Tensor> status, bool allow_tc) {
+int64_t decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_tables,
+                         at::Tensor context_lens, at::Tensor out, at::Tensor ws, int64_t splits,
+                         int64_t keys_per_split, double scale, c10::optional<at::Tensor> status, bool allow_tc,
+                         bool kv_prefetch, c10::optional<at::Tensor> tickets) {
   c10::cuda::CUDAGuard g(q.device());
   CHECK_DTYPE(q, at::kBFloat16); CHECK_DTYPE(k_cache, at::kBFloat16); CHECK_DTYPE(v_cache, at::kBFloat16);
   CHECK_DTYPE(block_tables, at::kInt); CHECK_DTYPE(context_lens, at::kInt); CHECK_DTYPE(out, at::kHalf);
@@ -291,6 +292,7 @@ void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::
   a.max_blocks = (int)block_tables.size(1);
   a.splits = (int)splits; a.keys_per_split = (int)keys_per_split;
   a.scale = (float)scale;
+  a.kv_prefetch = kv_prefetch ? 1 : 0;
   TORCH_CHECK(a.Hq % a.Hk == 0, "Hq must be a multiple of Hk");
   TORCH_CHECK(out.numel() == q.numel(), "out shape mismatch");
   if (a.splits > 1) {
@@ -304,14 +306,21 @@ void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::
   a.block_tables = block_tables.data_ptr<int>();
   a.context_lens = context_lens.data_ptr<int>();
   a.out = reinterpret_cast<__half*>(out.data_ptr());
-  if (a.B == 0) return;
+  if (a.B == 0) return 0;
   int* st = nullptr;
   if (status.has_value() && status->defined()) { CHECK_DTYPE((*status), at::kInt); st = status->data_ptr<int>(); }
   if (allow_tc && hrm::decode_attn_tc_supported(a)) {
+    if (a.splits > 1 && tickets.has_value() && tickets->defined() &&
+        (a.Hq / a.Hk) * a.splits <= hrm::decode_attn_tc_merge_max()) {
+      CHECK_DTYPE((*tickets), at::kInt);
+      TORCH_CHECK(tickets->numel() >= (int64_t)a.B * a.Hk, "attention tickets: need B * Hk int32");
+      a.tickets = tickets->data_ptr<int>();
+    }
     hrm::decode_attn_tc_launch(a, (int)k_cache.size(0), st, cur_stream());
-  } else {
-    hrm::decode_attn_launch(a, cur_stream());
+    return (a.splits > 1 && a.tickets == nullptr) ? 2 : 1;
   }
+  hrm::decode_attn_launch(a, cur_stream());
+  return a.splits > 1 ? 2 : 1;
 }
 
 void prefill_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_tables,
@@ -342,7 +351,8 @@ void prefill_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at:
     hrm::prefill_attn_launch(a, cur_stream());
 }
 
-void argmax_rows(at::Tensor logits, int64_t vocab_start, c10::optional<at::Tensor> keys, at::Tensor tokens) {
+void argmax_rows(at::Tensor logits, int64_t vocab_start, c10::optional<at::Tensor> keys, at::Tensor tokens,
+                 c10::optional<at::Tensor> scratch) {
   c10::cuda::CUDAGuard g(logits.device());
   CHECK_DTYPE(logits, at::kFloat); CHECK_DTYPE(tokens, at::kLong);
   TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be [M, V] row-major");
@@ -351,8 +361,14 @@ void argmax_rows(at::Tensor logits, int64_t vocab_start, c10::optional<at::Tenso
     CHECK_DTYPE((*keys), at::kLong);
     kp = reinterpret_cast<unsigned long long*>(keys->data_ptr<int64_t>());
   }
+  unsigned long long* sp = nullptr;
+  if (scratch.has_value() && scratch->defined()) {
+    CHECK_DTYPE((*scratch), at::kLong);
+    TORCH_CHECK(scratch->numel() >= 2 * hrm::kArgmaxMaxRows, "argmax scratch: int64[2 * 4096]");
+    sp = reinterpret_cast<unsigned long long*>(scratch->data_ptr<int64_t>());
+  }
   hrm::argmax_launch(logits.data_ptr<float>(), (int)logits.size(0), (int)logits.size(1), (int)logits.stride(0),
-                     (int)vocab_start, kp, tokens.data_ptr<int64_t>(), cur_stream());
+                     (int)vocab_start, kp, tokens.data_ptr<int64_t>(), sp, hrm::gemm_sm_count(), cur_stream());
 }
 
 void decode_prepare_bs(at::Tensor positions, at::Tensor tables, int64_t block_size, c10::optional<at::Tensor> active,
@@ -401,14 +417,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("norm_prep", &norm_prep);
   m.def("decode_attention", &decode_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("block_tables"), py::arg("context_lens"), py::arg("out"), py::arg("ws"), py::arg("splits"),
-        py::arg("keys_per_split"), py::arg("scale"), py::arg("status") = py::none(), py::arg("allow_tc") = true);
+        py::arg("keys_per_split"), py::arg("scale"), py::arg("status") = py::none(), py::arg("allow_tc") = true,
+        py::arg("kv_prefetch") = false, py::arg("tickets") = py::none());
   m.def("decode_attn_ws_floats", [](int64_t B, int64_t Hq, int64_t D, int64_t s) {
     return (int64_t)hrm::decode_attn_ws_floats((int)B, (int)Hq, (int)D, (int)s);
   });
   m.def("prefill_attention", &prefill_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("block_tables"), py::arg("cu_q"), py::arg("q_start"), py::arg("context_lens"), py::arg("out"),
         py::arg("max_q"), py::arg("scale"), py::arg("allow_tc") = true);
-  m.def("argmax_rows", &argmax_rows);
+  m.def("argmax_rows", &argmax_rows, py::arg("logits"), py::arg("vocab_start"), py::arg("keys"), py::arg("tokens"),
+        py::arg("scratch") = py::none());
   m.def("decode_prepare", &decode_prepare_bs);
   m.def("decode_advance", &decode_advance);
   m.def("sm_count", []() { return hrm::gemm_sm_count(); });
@@ -443,6 +461,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                           reinterpret_cast<const uint32_t*>(q.data_ptr<int>()), (int)q.numel(),
                           scores.data_ptr<float>(), rec_ids.size(0), hrm::gemm_sm_count(), cur_stream());
   });
+  m.def("set_pdl", &hrm::set_pdl_enabled, "programmatic dependent launch of the decode-path kernels on / off");
+  m.def("pdl_enabled", &hrm::pdl_enabled);
   m.def("set_gemm_trace", [](c10::optional<at::Tensor> t) {
     if (t.has_value() && t->defined()) {
       TORCH_CHECK(t->scalar_type() == at::kLong && t->numel() >= 12 * hrm::kGemmTraceLen, "trace: int64[12*1024]");

@@ -13,6 +13,10 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <stdexcept>
+#include <string>
+#include <utility>
+
 #define HRM_DEVINL __device__ __forceinline__
 
 namespace hrm {
@@ -42,6 +46,18 @@ HRM_DEVINL uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvt
 HRM_DEVINL void record_error(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// A grid launched with the programmatic-serialization attribute may start while the previous kernel in its stream
+// is still running.  Its threads must pass pdl_wait() (griddepcontrol.wait: the previous grid has completed and its
+// memory is visible) before touching anything that grid, or an earlier one, may write.  pdl_trigger()
+// (griddepcontrol.launch_dependents) lets the NEXT grid be scheduled early.  Rules of this library: a kernel
+// triggers only after its own pdl_wait(), so when a dependent starts, every grid before its direct predecessor has
+// completed; before pdl_wait() a kernel only sets up shared memory / TMEM and reads data that no kernel of the
+// inference step writes (int8 weights), or data the caller vouches for (older KV entries).  Both are no-ops for a
+// grid launched without the attribute.
+HRM_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+HRM_DEVINL void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---------------------------------------------------------------- mbarrier
 HRM_DEVINL void mbar_init(uint64_t* bar, uint32_t count) {
@@ -325,6 +341,30 @@ HRM_DEVINL uint32_t float_order(float f) {
 }
 HRM_DEVINL unsigned long long argmax_key(float v, uint32_t idx) {
   return ((unsigned long long)float_order(v) << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
+}
+
+// ---------------------------------------------------------------- host: launches
+// Programmatic dependent launch of the decode-path kernels (on unless HRM_PDL=0 in the environment, or turned off
+// with set_pdl_enabled; defined with the GEMM host code).
+bool pdl_enabled();
+void set_pdl_enabled(bool on);
+
+// Launches `kern` (throws std::runtime_error when the launch is rejected, so a kernel never silently goes missing).
+template <typename... KArgs, typename... Args>
+inline void launch_maybe_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                             Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("kernel launch failed: ") + cudaGetErrorString(e));
 }
 
 }  // namespace hrm

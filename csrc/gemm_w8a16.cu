@@ -32,6 +32,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <stdexcept>
@@ -115,6 +116,10 @@ struct GemmSmem {
 // start/end of segment i, 7 kernel start/end).  Off (a.trace == nullptr) in normal launches.
 HRM_DEVINL void trace_mark(const GemmArgs& a, int point, int64_t i) {
   if (a.trace != nullptr && blockIdx.x == 0 && i < kGemmTraceLen) a.trace[point * kGemmTraceLen + i] = clock64();
+}
+// Per-CTA %globaltimer stamps (rows 8..11: CTA start, first weight unit landed, mainloop done, CTA end).
+HRM_DEVINL void trace_cta(const GemmArgs& a, int row) {
+  if (a.trace != nullptr && blockIdx.x < kGemmTraceLen) a.trace[row * kGemmTraceLen + blockIdx.x] = (long long)global_ns();
 }
 
 // 16 accumulator columns summed over the partial accumulators whose bit is set in `valid` (all are loaded, so the
@@ -406,7 +411,10 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
   const int64_t G = gridDim.x;
   const int64_t U = (int64_t)a.tiles * a.k_tiles;
   const int64_t u0 = unit_start(blockIdx.x, U, G), u1 = unit_start(blockIdx.x + 1, U, G);
-  if (threadIdx.x == 0) trace_mark(a, 7, 0);
+  if (threadIdx.x == 0) {
+    trace_mark(a, 7, 0);
+    trace_cta(a, 8);
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < RW; ++s) {
@@ -440,24 +448,53 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
   const uint32_t tmem = *tmem_slot;
   const int ku = a.ku;                       // k-tiles per unit (<= KU)
   const int kt_total = a.k_tiles * ku;       // 64-wide k-tiles per output tile
+  // Only the producer thread runs ahead of the previous grid (int8 weights are never written by a kernel of the
+  // inference step); every other thread starts on dependent data (activations, residual, workspace, tickets).
+  const bool producer = warp == 0 && lane == 0;
+  if (!producer) {
+    pdl_wait();
+    pdl_trigger();
+  }
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       if (a.w_tiles == nullptr) tma_prefetch_desc(&tmW);
       tma_prefetch_desc(&tmX);
-      int64_t nw = 0, nx = 0;   // units issued into each ring
+      // the first RW units' weight tiles go out before waiting for the previous grid (ring slots start free)
+      const int64_t pre = (u1 - u0) < RW ? (u1 - u0) : RW;
+      {
+        const int tile0 = (int)(u0 / a.k_tiles);
+        int kt = (int)(u0 % a.k_tiles), n_tile = tile0 % a.n_tiles;
+        for (int64_t i = 0; i < pre; ++i) {
+          uint8_t* dst = wraw + i * S::kWSlot;
+          mbar_arrive_expect_tx(&wfull[i], (uint32_t)(ku * kWrawBytes));
+          if (a.w_tiles != nullptr) {
+            bulk_load(dst, a.w_tiles + ((size_t)n_tile * kt_total + (size_t)kt * ku) * kWrawBytes,
+                      (uint32_t)(ku * kWrawBytes), &wfull[i]);
+          } else {
+            for (int j = 0; j < ku; ++j)
+              tma_load_2d(dst + j * kWrawBytes, &tmW, &wfull[i], (kt * ku + j) * kBK, n_tile * kBM);
+          }
+          if (++kt == a.k_tiles) {
+            kt = 0;
+            if (++n_tile == a.n_tiles) n_tile = 0;
+          }
+        }
+      }
+      pdl_wait();
+      pdl_trigger();
+      int64_t nw = pre, nx = 0;   // units issued into each ring
       // (n-tile, m-tile, unit-within-tile) of the current unit, advanced incrementally (no divisions in the loop)
       const int tile0 = (int)(u0 / a.k_tiles);
       int kt = (int)(u0 % a.k_tiles);
       int n_tile = tile0 % a.n_tiles, m_tile = tile0 / a.n_tiles;
       int sw = 0, sx = 0;
       uint32_t pw = 1u, px = 1u;   // producer-side parities of the empty barriers (first pass: free)
-      const bool w_ring = true;
       for (int64_t u = u0; u < u1; ++u) {
         const int64_t i = u - u0;
         trace_mark(a, 0, i);
-        if (w_ring) {
+        if (i >= pre) {
           if (!mbar_wait_ab(&wempty[sw], pw, a.status, kErrTimeoutEmpty, abort_flag)) break;
           mbar_arrive_expect_tx(&wfull[sw], (uint32_t)(ku * kWrawBytes));
           uint8_t* dst = wraw + sw * S::kWSlot;
@@ -554,6 +591,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       }
       umma_commit(mdone);
       mbar_wait(mdone, 0, a.status, kErrTimeoutAccum);
+      if (mw == 0) trace_cta(a, 10);
     }
   } else if (warp < kFirstEpiWarp) {
     // ------------------------------------------------------------------ dequant
@@ -586,7 +624,10 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
         uint32_t pw = 0u, pf = 1u, px = 0u;   // wfull parity, fempty parity (first pass free), xfull parity
         for (int64_t i = g; i < n_units; i += NG) {
           if (!mbar_wait_ab(&wfull[sw], pw, a.status, kErrTimeoutFull, abort_flag)) break;
-          if (tracer) trace_mark(a, 1, i);
+          if (tracer) {
+            trace_mark(a, 1, i);
+            if (i == 0) trace_cta(a, 9);
+          }
           if (!mbar_wait_ab(&fempty[f], pf, a.status, kErrTimeoutEmpty, abort_flag)) break;
           if constexpr (kFoldX) {
             if (!mbar_wait_ab(&xfull[sx], px, a.status, kErrTimeoutFull, abort_flag)) break;
@@ -737,7 +778,10 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) trace_mark(a, 7, 1);
+  if (threadIdx.x == 0) {
+    trace_mark(a, 7, 1);
+    trace_cta(a, 11);
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, S::kTmemCols);
@@ -810,6 +854,18 @@ int gemm_pick_bn(int M) {
   return 256;
 }
 
+namespace {
+int g_pdl = -1;   // -1: not read from the environment yet
+}
+bool pdl_enabled() {
+  if (g_pdl < 0) {
+    const char* e = std::getenv("HRM_PDL");
+    g_pdl = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return g_pdl != 0;
+}
+void set_pdl_enabled(bool on) { g_pdl = on ? 1 : 0; }
+
 int gemm_sm_count() {
   static int sms = 0;
   if (!sms) {
@@ -863,7 +919,7 @@ static void launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, const GemmAr
     cudaFuncSetAttribute(w8a16_gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
     attr_set = true;
   }
-  w8a16_gemm_kernel<BN, EPI><<<p.ctas, kThreads, S::kAlloc, stream>>>(tw, tx, a);
+  launch_maybe_pdl(w8a16_gemm_kernel<BN, EPI>, dim3(p.ctas), dim3(kThreads), (size_t)S::kAlloc, stream, tw, tx, a);
 }
 
 template <int EPI>

@@ -7,6 +7,12 @@
 
 namespace hrm {
 
+// Programmatic dependent launch of the decode-path kernels (GEMM, tensor-core decode attention, split combine):
+// on unless HRM_PDL=0 is set in the environment; set_pdl_enabled switches it at run time.
+bool pdl_enabled();
+void set_pdl_enabled(bool on);
+
+
 void rmsnorm_launch(float* x, const float* delta, const float* w, __half* out, int M, int H, float eps,
                     cudaStream_t s);
 void norm_prep_launch(float* x, const float* delta, const float* gamma, __half* xg, float* ssq, int M, int H,
@@ -32,11 +38,18 @@ struct DecodeAttnArgs {
   float* ws;                   // split partials: [B, Hq, splits, D + 2]
   int B, Hq, Hk, D, block_size, max_blocks, splits, keys_per_split;
   float scale;
+  // 1: the kernel launched right before this one writes no block table / context length and no KV entry except the
+  // last key of each sequence (one decode step), so the tensor-core kernel may stream older KV tiles before it ends
+  int kv_prefetch;
+  // optional [B * Hk] int32 tickets, zero at rest: the tensor-core kernel then merges the splits itself (the CTA
+  // that finishes last among the splits of a (sequence, kv head) combines them and re-arms its ticket)
+  int* tickets;
 };
 void decode_attn_launch(const DecodeAttnArgs& a, cudaStream_t s);
 void decode_combine_launch(const DecodeAttnArgs& a, cudaStream_t s);
 // tcgen05 variant (head_dim 128, block size 16, group <= 16, keys_per_split a multiple of 128)
 bool decode_attn_tc_supported(const DecodeAttnArgs& a);
+int decode_attn_tc_merge_max();   // largest (heads per kv head) x splits the in-kernel split merge handles
 void decode_attn_tc_launch(const DecodeAttnArgs& a, int num_blocks, int* status, cudaStream_t s);
 size_t decode_attn_ws_floats(int B, int Hq, int D, int splits);
 
@@ -59,8 +72,11 @@ bool prefill_attn_tc_supported(const PrefillAttnArgs& a);
 void prefill_attn_tc_launch(const PrefillAttnArgs& a, int num_blocks, int total_q, int* status, cudaStream_t s);
 
 // Row argmax of fp32 logits [M, V] -> packed (order(value) << 32 | ~global_idx) keys, and token ids.
+// Split argmax: `scratch` = 2 * kArgmaxMaxRows zero-initialised u64 (row accumulators, then tickets; the kernel
+// re-arms them), or nullptr for one CTA per row.  Rows beyond kArgmaxMaxRows also take one CTA per row.
+constexpr int kArgmaxMaxRows = 4096;
 void argmax_launch(const float* logits, int M, int V, int ld, int vocab_start, unsigned long long* keys,
-                   int64_t* tokens, cudaStream_t s);
+                   int64_t* tokens, unsigned long long* scratch, int sms, cudaStream_t s);
 
 void decode_prepare_launch(const int* positions, const int* tables, int maxb, int bs, const int* active, int* slots,
                            int* context_lens, int B, cudaStream_t s);

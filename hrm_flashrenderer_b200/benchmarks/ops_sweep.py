@@ -68,6 +68,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--json", default="")
     ap.add_argument("--ops", default="gemm,attn,norm")
+    ap.add_argument("--attn-b", default="1,16,64", help="decode-attention batch sizes (context 4096)")
     a = ap.parse_args()
     hbm, tfl, src = peaks()
     dev = torch.device("cuda")
@@ -99,7 +100,7 @@ def main():
     if "attn" in a.ops:
         c = LLAMA31_70B
         Hq, Hk, D = c.heads // a.tp, max(1, c.kv_heads // a.tp), c.head_dim
-        for B, L in ((1, 4096), (16, 4096), (64, 4096)):
+        for B, L in ((int(x), 4096) for x in a.attn_b.split(",") if x):
             nb = B * (L // 16) + 8
             kc = torch.randn(nb, Hk, 16, D, device=dev, dtype=torch.bfloat16)
             vc = torch.randn_like(kc)

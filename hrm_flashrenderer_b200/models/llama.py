@@ -234,8 +234,9 @@ class LlamaW8:
                                       b.slots, self.cos, self.sin, kc, vc, q_out=q_out, in_norm=norm)
             q3 = q_out.view(T, p.local_heads, D)
             if b.is_decode:
+                # the QKV GEMM just above appends exactly one key per sequence: older KV tiles may stream early
                 ops.paged_decode_attention(q3, kc, vc, b.block_tables, b.context_lens, self.scale,
-                                           b.attn_splits, b.attn_keys_per_split, out=attn)
+                                           b.attn_splits, b.attn_keys_per_split, out=attn, kv_prefetch=True)
             else:
                 ops.paged_prefill_attention(q3, kc, vc, b.block_tables, b.cu_q, b.q_start, b.context_lens, b.max_q,
                                             self.scale, out=attn)

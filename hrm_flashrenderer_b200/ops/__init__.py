@@ -10,6 +10,7 @@ engine sizes once before CUDA-graph capture so captured kernels always see the s
 from __future__ import annotations
 
 import math
+import os
 import threading
 from typing import Optional, Tuple
 
@@ -55,6 +56,9 @@ LAUNCH_COUNTER = _LaunchCounter()
 
 
 # ------------------------------------------------------------------------------------------------ workspace
+_ATTN_MERGE = os.environ.get("HRM_ATTN_MERGE", "0") == "1"
+
+
 class Workspace:
     """Per-device scratch: fp32 split-K partials + int32 tickets (zeroed once; kernels re-arm them)."""
 
@@ -66,6 +70,8 @@ class Workspace:
         self.ws = torch.empty(floats, dtype=torch.float32, device=device)
         self.counters = torch.zeros(counters, dtype=torch.int32, device=device)
         self.status = torch.zeros(4, dtype=torch.int32, device=device)   # bounded-wait error word of the kernels
+        self.argmax = torch.zeros(2 * 4096, dtype=torch.int64, device=device)   # split-argmax accumulators + tickets
+        self.attn_tickets = torch.zeros(1 << 16, dtype=torch.int32, device=device)   # decode split merge, per (b, hk)
         self.frozen = False
 
     def ensure(self, floats: int, counters: int = 0) -> None:
@@ -387,8 +393,14 @@ def check_status(device=None) -> None:
 def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                            context_lens: torch.Tensor, scale: Optional[float] = None, splits: int = 0,
                            keys_per_split: int = 0, out: Optional[torch.Tensor] = None,
-                           max_ctx: Optional[int] = None, allow_tc: bool = True) -> torch.Tensor:
-    """One query token per sequence.  ``q [B, Hq, D]`` bf16 -> ``[B, Hq, D]`` f16."""
+                           max_ctx: Optional[int] = None, allow_tc: bool = True,
+                           kv_prefetch: bool = False) -> torch.Tensor:
+    """One query token per sequence.  ``q [B, Hq, D]`` bf16 -> ``[B, Hq, D]`` f16.
+
+    ``kv_prefetch=True`` is a promise that the kernel launched right before this call writes no block table, no
+    context length and no KV entry except each sequence's last key (the decode step's QKV + append GEMM); the
+    tensor-core kernel then starts streaming the older KV tiles while that kernel finishes (programmatic dependent
+    launch)."""
     B, Hq, D = q.shape
     scale = scale if scale is not None else 1.0 / math.sqrt(D)
     if not q.is_cuda:
@@ -418,9 +430,13 @@ def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torc
     ws = Workspace.get(q.device)
     need = ext().decode_attn_ws_floats(B, Hq, D, splits) if splits > 1 else 0
     ws.ensure(need)
-    ext().decode_attention(q.contiguous(), k_cache, v_cache, block_tables, context_lens, out, ws.ws, splits,
-                           keys_per_split, float(scale), ws.status, bool(allow_tc))
-    LAUNCH_COUNTER.add(2 if splits > 1 else 1)
+    # in-kernel split merge (last split CTA of each (sequence, kv head) combines) instead of a combine launch;
+    # opt-in with HRM_ATTN_MERGE=1 until it is measured faster than the separate combine kernel
+    merge = _ATTN_MERGE and B * k_cache.shape[1] <= ws.attn_tickets.numel()
+    tickets = ws.attn_tickets if merge else None
+    n = ext().decode_attention(q.contiguous(), k_cache, v_cache, block_tables, context_lens, out, ws.ws, splits,
+                               keys_per_split, float(scale), ws.status, bool(allow_tc), bool(kv_prefetch), tickets)
+    LAUNCH_COUNTER.add(int(n))
     return out
 
 
@@ -469,7 +485,7 @@ def argmax_rows(logits: torch.Tensor, vocab_start: int = 0, keys: Optional[torch
         return idx.to(torch.int64) + vocab_start
     if tokens is None:
         tokens = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
-    ext().argmax_rows(logits, int(vocab_start), keys, tokens)
+    ext().argmax_rows(logits, int(vocab_start), keys, tokens, Workspace.get(logits.device).argmax)
     LAUNCH_COUNTER.add()
     return tokens
 

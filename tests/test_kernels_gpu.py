@@ -209,7 +209,8 @@ def test_paged_decode_attention(D, Hq, Hk, lens, splits, tc):
 
 @pytest.mark.parametrize("lens", [[4096], [33, 2000, 129, 128], [1, 17, 300]])
 @pytest.mark.parametrize("splits", [0, 3])
-def test_paged_decode_attention_contiguous_blocks(lens, splits):
+@pytest.mark.parametrize("kv_prefetch", [False, True])
+def test_paged_decode_attention_contiguous_blocks(lens, splits, kv_prefetch):
     """Pool blocks handed out in order: whole 128-key tiles come in as 8-block TMA boxes (plus one-block boxes at
     sequence tails), same results as the reference."""
     B = len(lens)
@@ -222,9 +223,32 @@ def test_paged_decode_attention_contiguous_blocks(lens, splits):
         tiles = (tab.shape[1] * 16 + 127) // 128
         per = (tiles + splits - 1) // splits
         kw = dict(splits=(tiles + per - 1) // per, keys_per_split=per * 128)
-    out = ops.paged_decode_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), tab.to(DEV), cl.to(DEV), **kw)
+    out = ops.paged_decode_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), tab.to(DEV), cl.to(DEV),
+                                     kv_prefetch=kv_prefetch, **kw)
     ops.check_status()
     assert (out.float().cpu() - ref.float()).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("lens", [[4096] * 3, [33, 2000, 129, 128], [1, 17, 300]])
+@pytest.mark.parametrize("splits", [0, 2, 5])
+def test_paged_decode_attention_in_kernel_merge(lens, splits, monkeypatch):
+    """Split merge done by the last split CTA of each (sequence, kv head) (tickets re-armed between calls)."""
+    monkeypatch.setattr(ops, "_ATTN_MERGE", True)
+    B = len(lens)
+    kc, vc, tab = _paged(B, lens, 8, 128, contiguous=True)
+    q = torch.randn(B, 64, 128).to(torch.bfloat16)
+    cl = torch.tensor(lens, dtype=torch.int32)
+    ref = ops.paged_decode_attention(q, kc, vc, tab, cl)
+    kw = {}
+    if splits:
+        tiles = (tab.shape[1] * 16 + 127) // 128
+        per = (tiles + splits - 1) // splits
+        kw = dict(splits=(tiles + per - 1) // per, keys_per_split=per * 128)
+    args = (q.to(DEV), kc.to(DEV), vc.to(DEV), tab.to(DEV), cl.to(DEV))
+    outs = [ops.paged_decode_attention(*args, **kw) for _ in range(3)]
+    ops.check_status()
+    assert (outs[0].float().cpu() - ref.float()).abs().max().item() < 2e-2
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
 
 
 @pytest.mark.parametrize("chunks", [[(0, 300)], [(200, 1029), (0, 17)], [(0, 2048)]])
@@ -292,6 +316,26 @@ def test_embedding_vocab_parallel():
     out = ops.embedding_q8(ids, q, s, vocab_start=100)
     ref = ops.embedding_q8(ids.cpu(), q.cpu(), s.cpu(), vocab_start=100)
     assert torch.allclose(out.cpu(), ref)
+
+
+@pytest.mark.parametrize("M,V", [(1, 128256), (16, 128256), (16, 16032), (4, 40001), (300, 4099), (5000, 999)])
+def test_argmax_split_matches_torch(M, V):
+    """Split over many CTAs per row (atomicMax of packed keys), ties across slice boundaries, repeated calls
+    (accumulators / tickets re-armed), rows beyond the split limit (one CTA per row)."""
+    from hrm_flashrenderer_b200.parallel.dist import pack_argmax
+    g = torch.Generator(device="cpu").manual_seed(M + V)
+    for rep in range(3):
+        logits = torch.randn(M, V, generator=g).to(DEV)
+        if V > 9000:
+            logits[0, V - 1] = 50.0
+            logits[0, 3] = 50.0              # tie in another slice: lowest id wins
+        keys = torch.empty(M, dtype=torch.int64, device=DEV)
+        t = ops.argmax_rows(logits, vocab_start=7, keys=keys)
+        val, idx = torch.max(logits.cpu(), -1)
+        assert torch.equal(t.cpu(), idx + 7)
+        assert torch.equal(keys.cpu(), pack_argmax(val, idx + 7))
+    if V > 9000:
+        assert t[0].item() == 10
 
 
 def test_argmax_ties_lowest_index():

@@ -80,3 +80,24 @@ def test_synthesize_on_device_shapes():
     assert ops.weight_nk(L.w_gu, L.s_gu) == (2 * cfg.intermediate, cfg.hidden)
     assert L.w_qkv.shape == ((cfg.q_dim + 2 * cfg.kv_dim) // 128, cfg.hidden // 64, 8192)
     assert m.weight_bytes() > 0
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_programmatic_dependent_launch_on_off_identical(graphs):
+    """Decode with programmatic dependent launch (early weight / KV prefetch before the previous grid ends) gives the
+    same tokens as plain stream order; contexts span several 128-key tiles so attention runs split and prefetches."""
+    cfg = SMALL
+    w = synth_weights(cfg, seed=3)
+    prompts = _prompts(4, 300, cfg.vocab, seed=5)
+    outs = []
+    try:
+        for on in (False, True, True):
+            ops.ext().set_pdl(on)
+            model = LlamaW8.from_weights(cfg, w, device="cuda", max_pos=1024)
+            eng = InferenceEngine(model, EngineConfig(max_seq_len=512, max_batch=4, use_cuda_graphs=graphs),
+                                  num_blocks=160)
+            outs.append(eng.generate(prompts, 24, stop_on_eos=False))
+            ops.check_status()
+    finally:
+        ops.ext().set_pdl(True)
+    assert outs[0] == outs[1] == outs[2]
