@@ -57,6 +57,8 @@ LAUNCH_COUNTER = _LaunchCounter()
 
 # ------------------------------------------------------------------------------------------------ workspace
 _ATTN_MERGE = os.environ.get("HRM_ATTN_MERGE", "0") == "1"
+# split argmax over many CTAs per row (HRM_ARGMAX_SPLIT=0: one CTA per row)
+_ARGMAX_SPLIT = os.environ.get("HRM_ARGMAX_SPLIT", "1") != "0"
 
 
 class Workspace:
@@ -485,7 +487,8 @@ def argmax_rows(logits: torch.Tensor, vocab_start: int = 0, keys: Optional[torch
         return idx.to(torch.int64) + vocab_start
     if tokens is None:
         tokens = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
-    ext().argmax_rows(logits, int(vocab_start), keys, tokens, Workspace.get(logits.device).argmax)
+    scratch = Workspace.get(logits.device).argmax if _ARGMAX_SPLIT else None
+    ext().argmax_rows(logits, int(vocab_start), keys, tokens, scratch)
     LAUNCH_COUNTER.add()
     return tokens
 
