@@ -51,6 +51,8 @@ setup(
             "hrm-flashd=hrm_flashrenderer_b200.serving.daemon:main",
             "hrm-flash-serve=hrm_flashrenderer_b200.serving.serve:main",
             "hrm-flash-router=hrm_flashrenderer_b200.serving.router:main",
+            "flash-kernel-test=hrm_flashrenderer_b200.compat.kernel_test:kernel_test_main",
+            "flash-append-test=hrm_flashrenderer_b200.compat.kernel_test:append_test_main",
         ]
     },
 )
