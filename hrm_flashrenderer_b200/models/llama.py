@@ -111,6 +111,7 @@ class LlamaW8:
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self.kv: Optional[PagedKVPool] = None
         self.symm = None   # SymmetricWorkspace: enables the fused GEMM + all-reduce kernels when TP > 1
+        self.sequence_parallel = False   # prefill: token-sharded residual between blocks (TP > 1)
 
     def enable_fused_collectives(self, group=None) -> None:
         """Allocate / exchange the NVLink symmetric buffers (collective over the TP group)."""
@@ -212,6 +213,8 @@ class LlamaW8:
         their epilogue; with TP > 1 the row-parallel partial is all-reduced first.
         """
         cfg, p = self.cfg, self.plan
+        if p.world > 1 and self.sequence_parallel and not b.is_decode:
+            return self._forward_sp(b)
         T = b.ids.shape[0]
         H = cfg.hidden
         tp = p.world > 1
@@ -273,6 +276,71 @@ class LlamaW8:
             from ..parallel.dist import unpack_argmax
             return unpack_argmax(keys)
         return ops.argmax_rows(logits, 0)
+
+    @torch.no_grad()
+    def _forward_sp(self, b: BatchMeta) -> torch.Tensor:
+        """Prefill with sequence parallelism (Megatron-SP): between blocks every rank keeps only its 1/world of the
+        token rows of the residual stream.  The vocab-parallel embedding and each row-parallel GEMM output are
+        reduce-scattered (sum over ranks, keep this rank's rows) instead of all-reduced; residual add + RMSNorm
+        inputs run on the shard; the GEMM operand ``xg`` and its ``ssq`` are all-gathered before each
+        column-parallel GEMM (QKV, gate/up) and before the lm_head.  Rows are padded to a multiple of the world
+        size; pad rows carry zeros, position 0 and slot -1 (no KV write), and attention skips them.  Same sums as
+        the all-reduce path, so the same tokens.  (The reference has no sequence parallelism.)"""
+        cfg, p = self.cfg, self.plan
+        comm, w = self.comm, p.world
+        T = b.ids.shape[0]
+        H, D = cfg.hidden, cfg.head_dim
+        dev = self.device
+        cuda = dev.type == "cuda"
+        Ts = (T + w - 1) // w
+        Tp = Ts * w
+        fdt = torch.float16 if cuda else torch.float32
+        pos = torch.zeros(Tp, dtype=b.positions.dtype, device=dev)
+        pos[:T] = b.positions
+        slots = torch.full((Tp,), -1, dtype=b.slots.dtype, device=dev)
+        slots[:T] = b.slots
+        emb = torch.zeros(Tp, H, dtype=torch.float32, device=dev)
+        emb[:T] = ops.embedding_q8(b.ids, self.embed_q, self.embed_s, p.vocab_start)
+        x = comm.reduce_scatter_rows(emb)                           # [Ts, H] fp32, this rank's rows
+        xg_s = torch.empty(Ts, H, dtype=fdt, device=dev)
+        ssq_s = torch.empty(H // 128, Ts, dtype=torch.float32, device=dev)
+        xg = torch.empty(Tp, H, dtype=fdt, device=dev)
+        ssq = torch.empty(H // 128, Tp, dtype=torch.float32, device=dev)
+        q_out = torch.empty(Tp, self.q_rows, dtype=torch.bfloat16, device=dev)
+        attn = torch.zeros(Tp, p.local_heads, D, dtype=fdt, device=dev)
+        partial = torch.empty(Tp, H, dtype=torch.float32, device=dev)
+        ps = torch.empty(Ts, H, dtype=torch.float32, device=dev)
+        norm = (ssq, H, cfg.rms_eps)
+
+        def gather():
+            comm.all_gather_rows(xg_s, xg)
+            comm.all_gather_cols(ssq_s, ssq)
+
+        ops.norm_prep(x, None, self.layers[0].ln1, xg_s, ssq_s)
+        gather()
+        for l, L in enumerate(self.layers):
+            kc, vc = self.kv.k[l], self.kv.v[l]
+            ops.w8a16_qkv_rope_append(xg, L.w_qkv, L.s_qkv, L.b_qkv, self.q_rows, self.kv_rows, D, pos, slots,
+                                      self.cos, self.sin, kc, vc, q_out=q_out, in_norm=norm)
+            q3 = q_out.view(Tp, p.local_heads, D)
+            ops.paged_prefill_attention(q3[:T], kc, vc, b.block_tables, b.cu_q, b.q_start, b.context_lens, b.max_q,
+                                        self.scale, out=attn[:T])
+            ops.w8a16_linear_out(attn.view(Tp, self.q_rows), L.w_o, L.s_o, partial)
+            ops.norm_prep(x, comm.reduce_scatter_rows(partial, ps), L.ln2, xg_s, ssq_s)
+            gather()
+            act = ops.w8a16_swiglu(xg, L.w_gu, L.s_gu, in_norm=norm)
+            g_next = self.layers[l + 1].ln1 if l + 1 < len(self.layers) else self.final_norm
+            ops.w8a16_linear_out(act, L.w_d, L.s_d, partial)
+            ops.norm_prep(x, comm.reduce_scatter_rows(partial, ps), g_next, xg_s, ssq_s)
+            gather()
+        xl = xg.index_select(0, b.last_rows)
+        nl = (ssq.index_select(1, b.last_rows).contiguous(), H, cfg.rms_eps)
+        logits = ops.w8a16_linear(xl, self.head_q, self.head_s, out_dtype=torch.float32, in_norm=nl)
+        keys = torch.empty(xl.shape[0], dtype=torch.int64, device=dev)
+        ops.argmax_rows(logits, p.vocab_start, keys=keys)
+        comm.all_reduce_max_(keys)
+        from ..parallel.dist import unpack_argmax
+        return unpack_argmax(keys)
 
     def _mm_f32(self, x, w, s, out):
         return ops.w8a16_linear_out(x, w, s, out)

@@ -27,6 +27,36 @@ class TPComm:
             dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
         return t
 
+    # ---------------------------------------------------------------- sequence parallel (token-sharded rows)
+    def reduce_scatter_rows(self, full: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+        """Sum ``full [world * R, ...]`` over ranks and keep rows ``[rank * R, (rank + 1) * R)``."""
+        if self.world == 1:
+            if out is None:
+                return full
+            return out.copy_(full)
+        rows = full.shape[0] // self.world
+        if out is None:
+            out = torch.empty((rows,) + tuple(full.shape[1:]), dtype=full.dtype, device=full.device)
+        dist.reduce_scatter_tensor(out, full.contiguous(), op=dist.ReduceOp.SUM, group=self.group)
+        return out
+
+    def all_gather_rows(self, shard: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """``out [world * R, ...]``: rank r's ``shard [R, ...]`` at rows ``[r * R, (r + 1) * R)``."""
+        if self.world == 1:
+            return out.copy_(shard)
+        dist.all_gather_into_tensor(out, shard.contiguous(), group=self.group)
+        return out
+
+    def all_gather_cols(self, shard: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """``out [C, world * R]``: rank r's ``shard [C, R]`` at columns ``[r * R, (r + 1) * R)``."""
+        if self.world == 1:
+            return out.copy_(shard)
+        C, R = shard.shape
+        buf = torch.empty(self.world * C, R, dtype=shard.dtype, device=shard.device)
+        dist.all_gather_into_tensor(buf, shard.contiguous(), group=self.group)
+        out.copy_(buf.view(self.world, C, R).permute(1, 0, 2).reshape(out.shape))
+        return out
+
     def barrier(self) -> None:
         if self.world > 1:
             dist.barrier(group=self.group)

@@ -50,6 +50,7 @@ class InferenceEngine:
         self.max_blocks = (self.ecfg.max_seq_len + bs - 1) // bs
         nb = num_blocks or self.ecfg.num_kv_blocks or self.ecfg.max_batch * self.max_blocks
         model.alloc_kv(int(nb), bs)
+        model.sequence_parallel = bool(self.ecfg.sequence_parallel)
         self.bm = BlockManager(int(nb), bs)
         self._graphs: Dict[int, _DecodeGraph] = {}
         self._next_seq = 0

@@ -28,7 +28,7 @@ def _prompts():
     return [torch.randint(0, 1024, (16,), generator=g).tolist() for _ in range(2)]
 
 
-def _run(rank, world, port, q):
+def _run(rank, world, port, q, sp=False, prompts=None):
     from hrm_flashrenderer_b200.parallel.dist import init_dist, destroy
     from hrm_flashrenderer_b200.parallel.comm import TPComm
     from hrm_flashrenderer_b200.models.llama import LlamaW8
@@ -38,18 +38,19 @@ def _run(rank, world, port, q):
     try:
         w = synth_weights(TINY, seed=0)
         model = LlamaW8.from_weights(TINY, w, rank=rank, world=world, device="cpu", comm=TPComm(), max_pos=256)
-        eng = InferenceEngine(model, EngineConfig(max_seq_len=64, max_batch=2, use_cuda_graphs=False), num_blocks=16)
-        out = eng.generate(_prompts(), 32, stop_on_eos=False)
+        eng = InferenceEngine(model, EngineConfig(max_seq_len=64, max_batch=4, use_cuda_graphs=False,
+                                                  sequence_parallel=sp), num_blocks=16)
+        out = eng.generate(prompts or _prompts(), 32, stop_on_eos=False)
         q.put((rank, out))
     finally:
         destroy()
 
 
-def _spawn(world):
+def _spawn(world, sp=False, prompts=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_run, args=(r, world, port, q)) for r in range(world)]
+    ps = [ctx.Process(target=_run, args=(r, world, port, q, sp, prompts)) for r in range(world)]
     for p in ps:
         p.start()
     res = {}
@@ -75,3 +76,18 @@ def test_tp1_matches_oracle():
     w = synth_weights(TINY, seed=0)
     ref = OracleLlama(TINY, w, max_pos=256).generate(_prompts(), 32)
     assert _spawn(1)[0] == ref
+
+
+def test_tp2_sequence_parallel_prefill_matches_tp1():
+    """Prefill with a token-sharded residual (reduce-scatter / all-gather) gives the TP=1 tokens; 2 prompts x 16
+    tokens = 32 rows split 16 / 16 per rank."""
+    tp1 = _spawn(1)[0]
+    sp = _spawn(2, sp=True)
+    assert sp[0] == sp[1] == tp1
+
+
+def test_tp2_sequence_parallel_odd_rows():
+    """23 prompt rows over 2 ranks: one pad row (zeros, slot -1) on the last rank."""
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (7, 11, 5)]
+    assert _spawn(2, sp=True, prompts=prompts)[0] == _spawn(1, prompts=prompts)[0]
