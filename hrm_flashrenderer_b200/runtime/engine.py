@@ -14,7 +14,7 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass, field
-from typing import Dict, List, Optional, Sequence, Tuple
+from typing import Callable, Dict, List, Optional, Sequence, Tuple
 
 import torch
 
@@ -238,13 +238,18 @@ class InferenceEngine:
     # ------------------------------------------------------------------ public API
     @torch.no_grad()
     def generate(self, prompts: Sequence[Sequence[int]], max_new_tokens: int, stop_on_eos: bool = True,
-                 eos_ids: Optional[Sequence[int]] = None) -> List[List[int]]:
-        """Greedy generation for a batch of token-id prompts (prompt ids H2D, tokens D2H every step)."""
+                 eos_ids: Optional[Sequence[int]] = None,
+                 on_token: Optional[Callable[[int, int], None]] = None) -> List[List[int]]:
+        """Greedy generation for a batch of token-id prompts (prompt ids H2D, tokens D2H every step).
+        ``on_token(i, token)`` is called for every token kept for prompt ``i``, as soon as it is known."""
         eos = set(self.cfg.eos_token_ids if eos_ids is None else eos_ids)
         sids = [self.new_seq() for _ in prompts]
         try:
             first = self.prefill(list(zip(sids, prompts)))
             outs = [[t] for t in first]
+            if on_token is not None and max_new_tokens >= 1:
+                for i, t in enumerate(first):
+                    on_token(i, t)
             alive = [not (stop_on_eos and t in eos) for t in first]
             if max_new_tokens <= 1 or not any(alive):
                 return [o[:max_new_tokens] for o in outs]
@@ -265,6 +270,8 @@ class InferenceEngine:
                         continue
                     t = int(pinned[i])
                     outs[i].append(t)
+                    if on_token is not None:
+                        on_token(i, t)
                     if stop_on_eos and t in eos:
                         alive[i] = False
                         changed = True
