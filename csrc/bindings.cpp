@@ -88,13 +88,8 @@ void set_in_norm(hrm::GemmArgs& a, const c10::optional<at::Tensor>& in_ssq, doub
   }
 }
 
-void w8a16_gemm(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<at::Tensor> bias, at::Tensor out,
-                at::Tensor ws, at::Tensor counters, int64_t force_ctas, c10::optional<at::Tensor> in_ssq,
-                double inv_h, double eps) {
-  c10::cuda::CUDAGuard g(x.device());
-  auto a = base_args(x, w, scale, bias, ws, counters);
-  set_in_norm(a, in_ssq, inv_h, eps);
-  if (a.M == 0) return;
+// Plain output [M, >= N] f16 or f32: returns the epilogue.
+int fill_out(hrm::GemmArgs& a, const at::Tensor& out) {
   CHECK_CUDA(out);
   TORCH_CHECK(out.dim() == 2 && out.size(0) == a.M && out.size(1) >= a.N && out.stride(1) == 1, "bad out shape");
   int epi;
@@ -103,17 +98,26 @@ void w8a16_gemm(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<at::
   else TORCH_CHECK(false, "out must be f16 or f32");
   a.out = out.data_ptr();
   a.ldo = (int)out.stride(0);
+  return epi;
+}
+
+void w8a16_gemm(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<at::Tensor> bias, at::Tensor out,
+                at::Tensor ws, at::Tensor counters, int64_t force_ctas, c10::optional<at::Tensor> in_ssq,
+                double inv_h, double eps) {
+  c10::cuda::CUDAGuard g(x.device());
+  auto a = base_args(x, w, scale, bias, ws, counters);
+  set_in_norm(a, in_ssq, inv_h, eps);
+  if (a.M == 0) return;
+  const int epi = fill_out(a, out);
   auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_ctas);
   check_ws(p, ws, counters);
   hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), epi, a, p, cur_stream());
 }
 
 // resid += x @ (w * scale)^T  (fp32 residual stream)
-void w8a16_gemm_residual(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor resid, at::Tensor ws,
-                         at::Tensor counters, int64_t force_ctas, c10::optional<at::Tensor> gamma_next,
-                         c10::optional<at::Tensor> xg_out, c10::optional<at::Tensor> ssq_out) {
-  c10::cuda::CUDAGuard g(x.device());
-  auto a = base_args(x, w, scale, c10::nullopt, ws, counters);
+// Residual epilogue fields (resid += acc; optional next-norm outputs).
+void fill_resid(hrm::GemmArgs& a, const at::Tensor& resid, const c10::optional<at::Tensor>& gamma_next,
+                const c10::optional<at::Tensor>& xg_out, const c10::optional<at::Tensor>& ssq_out) {
   if (xg_out.has_value() && xg_out->defined()) {
     TORCH_CHECK(gamma_next.has_value() && gamma_next->defined(), "xg_out needs gamma_next");
     CHECK_DTYPE((*xg_out), at::kHalf); CHECK_DTYPE((*gamma_next), at::kFloat);
@@ -124,15 +128,23 @@ void w8a16_gemm_residual(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tenso
   }
   if (ssq_out.has_value() && ssq_out->defined()) {
     CHECK_DTYPE((*ssq_out), at::kFloat);
-    TORCH_CHECK(ssq_out->numel() >= (int64_t)((a.N + 127) / 128) * x.size(0), "ssq_out too small");
+    TORCH_CHECK(ssq_out->numel() >= (int64_t)((a.N + 127) / 128) * a.M, "ssq_out too small");
     a.ssq_out = ssq_out->data_ptr<float>();
   }
-  if (a.M == 0) return;
   CHECK_CUDA(resid); CHECK_DTYPE(resid, at::kFloat);
   TORCH_CHECK(resid.dim() == 2 && resid.size(0) == a.M && resid.size(1) == a.N && resid.stride(1) == 1,
               "bad resid shape");
   a.resid = resid.data_ptr<float>();
   a.ldr = (int)resid.stride(0);
+}
+
+void w8a16_gemm_residual(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor resid, at::Tensor ws,
+                         at::Tensor counters, int64_t force_ctas, c10::optional<at::Tensor> gamma_next,
+                         c10::optional<at::Tensor> xg_out, c10::optional<at::Tensor> ssq_out) {
+  c10::cuda::CUDAGuard g(x.device());
+  auto a = base_args(x, w, scale, c10::nullopt, ws, counters);
+  if (a.M == 0) return;
+  fill_resid(a, resid, gamma_next, xg_out, ssq_out);
   auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_ctas);
   check_ws(p, ws, counters);
   hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_RESID, a, p, cur_stream());
@@ -176,6 +188,13 @@ void w8a16_gemm_residual_ar(at::Tensor x, at::Tensor w, at::Tensor scale, at::Te
                          cur_stream());
 }
 
+void fill_swiglu(hrm::GemmArgs& a, const at::Tensor& out) {
+  CHECK_CUDA(out); CHECK_DTYPE(out, at::kHalf);
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == a.M && out.size(1) == a.N / 2 && out.stride(1) == 1, "bad out");
+  a.out = out.data_ptr();
+  a.ldo = (int)out.stride(0);
+}
+
 // out [M, N/2] f16 = silu(gate) * up, where w rows are interleaved per 128-row tile: 64 gate rows then the 64
 // matching up rows.
 void w8a16_gemm_swiglu(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor out, at::Tensor ws,
@@ -185,16 +204,17 @@ void w8a16_gemm_swiglu(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor 
   auto a = base_args(x, w, scale, c10::nullopt, ws, counters);
   set_in_norm(a, in_ssq, inv_h, eps);
   if (a.M == 0) return;
-  CHECK_CUDA(out); CHECK_DTYPE(out, at::kHalf);
-  TORCH_CHECK(out.dim() == 2 && out.size(0) == a.M && out.size(1) == a.N / 2 && out.stride(1) == 1, "bad out");
-  a.out = out.data_ptr();
-  a.ldo = (int)out.stride(0);
+  fill_swiglu(a, out);
   auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_ctas);
   check_ws(p, ws, counters);
   hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_SWIGLU, a, p, cur_stream());
 }
 
 // Fused QKV projection + bias + RoPE + paged-KV append.  w rows: [q (q_rows) | k (kv_rows) | v (kv_rows)].
+void fill_qkv(hrm::GemmArgs& a, int64_t q_rows, int64_t kv_rows, int64_t head_dim, const at::Tensor& positions,
+              const at::Tensor& slots, const at::Tensor& cos_t, const at::Tensor& sin_t, const at::Tensor& q_out,
+              const at::Tensor& k_cache, const at::Tensor& v_cache);
+
 void w8a16_gemm_qkv(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<at::Tensor> bias, int64_t q_rows,
                     int64_t kv_rows, int64_t head_dim, at::Tensor positions, at::Tensor slots, at::Tensor cos_t,
                     at::Tensor sin_t, at::Tensor q_out, at::Tensor k_cache, at::Tensor v_cache, at::Tensor ws,
@@ -204,6 +224,15 @@ void w8a16_gemm_qkv(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<
   auto a = base_args(x, w, scale, bias, ws, counters);
   set_in_norm(a, in_ssq, inv_h, eps);
   if (a.M == 0) return;
+  fill_qkv(a, q_rows, kv_rows, head_dim, positions, slots, cos_t, sin_t, q_out, k_cache, v_cache);
+  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_ctas);
+  check_ws(p, ws, counters);
+  hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_QKV, a, p, cur_stream());
+}
+
+void fill_qkv(hrm::GemmArgs& a, int64_t q_rows, int64_t kv_rows, int64_t head_dim, const at::Tensor& positions,
+              const at::Tensor& slots, const at::Tensor& cos_t, const at::Tensor& sin_t, const at::Tensor& q_out,
+              const at::Tensor& k_cache, const at::Tensor& v_cache) {
   TORCH_CHECK(a.N == q_rows + 2 * kv_rows, "w rows must be q_rows + 2*kv_rows");
   CHECK_DTYPE(positions, at::kInt); CHECK_DTYPE(slots, at::kInt);
   CHECK_DTYPE(cos_t, at::kFloat); CHECK_DTYPE(sin_t, at::kFloat);
@@ -227,9 +256,72 @@ void w8a16_gemm_qkv(at::Tensor x, at::Tensor w, at::Tensor scale, c10::optional<
   a.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
   a.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr());
   a.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
-  auto p = hrm::gemm_plan(a.M, a.N, a.K, (int)force_ctas);
-  check_ws(p, ws, counters);
-  hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_QKV, a, p, cur_stream());
+}
+
+// Multi-phase decode chain in one cooperative launch.  `phases` is a list of tuples, phase p + 1 reading phase p's
+// outputs:
+//   ("f16",    x, w, scale, out, in_ssq | None, inv_h, eps)
+//   ("resid",  x, w, scale, resid, gamma_next | None, xg_out | None, ssq_out | None)
+//   ("swiglu", x, w, scale, out, in_ssq | None, inv_h, eps)
+//   ("qkv",    x, w, scale, bias | None, q_rows, kv_rows, head_dim, positions, slots, cos, sin, q_out, k_cache,
+//              v_cache, in_ssq | None, inv_h, eps)
+// w: pre-tiled int8 weights.  ws / counters: split-K scratch covering every phase; bar: int32 [5] zero at rest.
+static c10::optional<at::Tensor> opt_tensor(const py::handle& h) {
+  if (h.is_none()) return c10::nullopt;
+  return h.cast<at::Tensor>();
+}
+
+void w8a16_chain(py::list phases, at::Tensor ws, at::Tensor counters, at::Tensor bar) {
+  const int nph = (int)py::len(phases);
+  TORCH_CHECK(nph >= 1 && nph <= hrm::kMaxChainPhases, "chain: 1..4 phases");
+  CHECK_CUDA(bar); CHECK_DTYPE(bar, at::kInt);
+  TORCH_CHECK(bar.numel() >= hrm::kMaxChainPhases + 1, "chain: bar needs 5 int32");
+  std::vector<hrm::ChainPhaseDesc> d(nph);
+  c10::optional<c10::cuda::CUDAGuard> guard;
+  const int G = hrm::gemm_sm_count();
+  for (int p = 0; p < nph; ++p) {
+    py::tuple t = phases[p].cast<py::tuple>();
+    const std::string kind = t[0].cast<std::string>();
+    at::Tensor x = t[1].cast<at::Tensor>(), w = t[2].cast<at::Tensor>(), scale = t[3].cast<at::Tensor>();
+    if (!guard) guard.emplace(x.device());
+    TORCH_CHECK(w.dim() == 3, "chain: pre-tiled weights required");
+    hrm::GemmArgs a;
+    if (kind == "f16") {
+      a = base_args(x, w, scale, c10::nullopt, ws, counters);
+      set_in_norm(a, opt_tensor(t[5]), t[6].cast<double>(), t[7].cast<double>());
+      d[p].epi = fill_out(a, t[4].cast<at::Tensor>());
+      TORCH_CHECK(d[p].epi == hrm::EPI_F16, "chain: f16 output only");
+    } else if (kind == "resid") {
+      a = base_args(x, w, scale, c10::nullopt, ws, counters);
+      fill_resid(a, t[4].cast<at::Tensor>(), opt_tensor(t[5]), opt_tensor(t[6]), opt_tensor(t[7]));
+      d[p].epi = hrm::EPI_RESID;
+    } else if (kind == "swiglu") {
+      a = base_args(x, w, scale, c10::nullopt, ws, counters);
+      set_in_norm(a, opt_tensor(t[5]), t[6].cast<double>(), t[7].cast<double>());
+      fill_swiglu(a, t[4].cast<at::Tensor>());
+      d[p].epi = hrm::EPI_SWIGLU;
+    } else if (kind == "qkv") {
+      a = base_args(x, w, scale, opt_tensor(t[4]), ws, counters);
+      set_in_norm(a, opt_tensor(t[15]), t[16].cast<double>(), t[17].cast<double>());
+      fill_qkv(a, t[5].cast<int64_t>(), t[6].cast<int64_t>(), t[7].cast<int64_t>(), t[8].cast<at::Tensor>(),
+               t[9].cast<at::Tensor>(), t[10].cast<at::Tensor>(), t[11].cast<at::Tensor>(), t[12].cast<at::Tensor>(),
+               t[13].cast<at::Tensor>(), t[14].cast<at::Tensor>());
+      d[p].epi = hrm::EPI_QKV;
+    } else {
+      TORCH_CHECK(false, "chain: unknown phase kind ", kind);
+    }
+    TORCH_CHECK(a.M > 0 && a.M <= 64, "chain: 1 <= M <= 64");
+    check_ws(hrm::gemm_chain_phase_plan(a.M, a.N, a.K, G), ws, counters);
+    d[p].x = x.data_ptr();
+    d[p].ldx = (int)x.stride(0);
+    d[p].a = a;
+  }
+  hrm::gemm_chain_launch(d.data(), nph, bar.data_ptr<int>(), cur_stream());
+}
+
+std::vector<int64_t> chain_phase_plan_py(int64_t M, int64_t N, int64_t K) {
+  auto p = hrm::gemm_chain_phase_plan((int)M, (int)N, (int)K, hrm::gemm_sm_count());
+  return {p.bn, (int64_t)p.ws_floats, p.counters};
 }
 
 void rmsnorm(at::Tensor x, c10::optional<at::Tensor> delta, at::Tensor w, double eps, at::Tensor out) {
@@ -461,6 +553,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                           reinterpret_cast<const uint32_t*>(q.data_ptr<int>()), (int)q.numel(),
                           scores.data_ptr<float>(), rec_ids.size(0), hrm::gemm_sm_count(), cur_stream());
   });
+  m.def("w8a16_chain", &w8a16_chain, "multi-phase decode GEMM chain in one cooperative launch");
+  m.def("chain_phase_plan", &chain_phase_plan_py, "(bn, ws_floats, counters) of one chain phase on all SMs");
   m.def("set_pdl", &hrm::set_pdl_enabled, "programmatic dependent launch of the decode-path kernels on / off");
   m.def("pdl_enabled", &hrm::pdl_enabled);
   m.def("set_gemm_trace", [](c10::optional<at::Tensor> t) {

@@ -30,6 +30,7 @@ enum : int {
   kErrTimeoutAccum = 4,
   kErrTimeoutPeer = 5,
   kErrBadShape = 6,
+  kErrTimeoutGrid = 7,   // grid-wide barrier of a persistent multi-phase kernel
 };
 
 // Every wait is bounded in time: 2 s of %globaltimer, far above any legitimate wait in these kernels (the longest
@@ -162,6 +163,8 @@ HRM_DEVINL void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint
                : "memory");
 }
 HRM_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Orders this thread's earlier (generic-proxy) acquires before its later async-proxy (TMA / bulk) global reads.
+HRM_DEVINL void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // ---------------------------------------------------------------- tcgen05 / TMEM
 HRM_DEVINL void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {  // whole warp

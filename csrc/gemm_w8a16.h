@@ -76,6 +76,27 @@ struct GemmPlan {
 };
 
 GemmPlan gemm_plan(int M, int N, int K, int force_ctas = 0);
+
+// ---------------------------------------------------------------------------------------------- multi-phase chain
+// Up to kMaxChainPhases decode GEMMs in one persistent cooperative launch, phase p + 1 reading phase p's outputs
+// (grid barrier in between; the next phase's weights stream before it).  Supported epilogue sequences:
+// {RESID, SWIGLU, RESID, QKV}, {RESID, SWIGLU, RESID} and {F16, F16}; pre-tiled weights; M <= 64.
+constexpr int kMaxChainPhases = 4;
+struct ChainArgs {
+  int nph;
+  GemmArgs ph[kMaxChainPhases];
+  int* bar;       // [kMaxChainPhases + 1] zero-initialised: phase arrival counters, then the kernel-end ticket
+  int* status;
+};
+struct ChainPhaseDesc {
+  const void* x;  // f16 activations [M, ldx] of this phase (may be an earlier phase's output)
+  int ldx;
+  int epi;        // GemmEpilogue
+  GemmArgs a;     // M, N, K, scale, w_tiles and the epilogue's fields; ws / counters shared by all phases
+};
+// Plan of one chain phase on exactly `ctas` CTAs (no clamp to the unit count).
+GemmPlan gemm_chain_phase_plan(int M, int N, int K, int ctas);
+void gemm_chain_launch(const ChainPhaseDesc* ph, int nph, int* bar, cudaStream_t stream);
 void gemm_w8a16_launch(const void* x, int ldx, const int8_t* w, int epi, GemmArgs a, const GemmPlan& p,
                        cudaStream_t stream);
 void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,

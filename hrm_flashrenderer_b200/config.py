@@ -195,6 +195,7 @@ class EngineConfig:
     graph_batch_buckets: Sequence[int] = field(default_factory=lambda: (1, 2, 4, 8, 16, 32, 64))
     fused_collectives: bool = True       # False -> NCCL all-reduce after the local GEMM (baseline path)
     sequence_parallel: bool = False      # prefill with a token-sharded residual stream (TP > 1)
+    chain_layers: bool = False           # decode (TP = 1): o_proj..next QKV as one multi-phase GEMM launch
     seed: int = 0
 
 

@@ -112,6 +112,7 @@ class LlamaW8:
         self.kv: Optional[PagedKVPool] = None
         self.symm = None   # SymmetricWorkspace: enables the fused GEMM + all-reduce kernels when TP > 1
         self.sequence_parallel = False   # prefill: token-sharded residual between blocks (TP > 1)
+        self.chain_layers = False        # decode, TP = 1: o_proj, gate/up, down, next QKV in one GEMM launch
 
     def enable_fused_collectives(self, group=None) -> None:
         """Allocate / exchange the NVLink symmetric buffers (collective over the TP group)."""
@@ -231,10 +232,15 @@ class LlamaW8:
         q_out = torch.empty(T, self.q_rows, dtype=torch.bfloat16, device=dev)
         attn = torch.empty(T, p.local_heads, D, dtype=torch.float16 if cuda else torch.float32, device=dev)
         partial = torch.empty(T, H, dtype=torch.float32, device=dev) if tp else None
+        chain = self.chain_layers and b.is_decode and not tp and T <= 64
+        act_buf = torch.empty(T, self.layers[0].s_gu.numel() // 2, dtype=xg.dtype, device=dev) if chain else None
+        qkv_done = False   # the previous layer's chain already ran this layer's QKV GEMM
         for l, L in enumerate(self.layers):
             kc, vc = self.kv.k[l], self.kv.v[l]
-            ops.w8a16_qkv_rope_append(xg, L.w_qkv, L.s_qkv, L.b_qkv, self.q_rows, self.kv_rows, D, b.positions,
-                                      b.slots, self.cos, self.sin, kc, vc, q_out=q_out, in_norm=norm)
+            if not qkv_done:
+                ops.w8a16_qkv_rope_append(xg, L.w_qkv, L.s_qkv, L.b_qkv, self.q_rows, self.kv_rows, D, b.positions,
+                                          b.slots, self.cos, self.sin, kc, vc, q_out=q_out, in_norm=norm)
+            qkv_done = False
             q3 = q_out.view(T, p.local_heads, D)
             if b.is_decode:
                 # the QKV GEMM just above appends exactly one key per sequence: older KV tiles may stream early
@@ -244,6 +250,21 @@ class LlamaW8:
                 ops.paged_prefill_attention(q3, kc, vc, b.block_tables, b.cu_q, b.q_start, b.context_lens, b.max_q,
                                             self.scale, out=attn)
             a2 = attn.view(T, self.q_rows)
+            if chain:
+                # o_proj + residual -> gate/up + SwiGLU -> down + residual (-> next layer's QKV): one launch
+                g_next = self.layers[l + 1].ln1 if l + 1 < len(self.layers) else self.final_norm
+                inv_h = 1.0 / H
+                phases = [("resid", a2, L.w_o, L.s_o, x, L.ln2, xg, ssq),
+                          ("swiglu", xg, L.w_gu, L.s_gu, act_buf, ssq, inv_h, cfg.rms_eps),
+                          ("resid", act_buf, L.w_d, L.s_d, x, g_next, xg, ssq)]
+                if l + 1 < len(self.layers):
+                    Ln = self.layers[l + 1]
+                    phases.append(("qkv", xg, Ln.w_qkv, Ln.s_qkv, Ln.b_qkv, self.q_rows, self.kv_rows, D,
+                                   b.positions, b.slots, self.cos, self.sin, q_out, self.kv.k[l + 1],
+                                   self.kv.v[l + 1], ssq, inv_h, cfg.rms_eps))
+                    qkv_done = True
+                ops.w8a16_chain(phases)
+                continue
             fused = tp and self.symm is not None and T <= 64
             if fused:
                 ops.w8a16_residual_ar_(a2, L.w_o, L.s_o, x, self.symm, L.ln2, xg, ssq)

@@ -12,7 +12,7 @@ from __future__ import annotations
 import math
 import os
 import threading
-from typing import Optional, Tuple
+from typing import Sequence, Optional, Tuple
 
 import torch
 
@@ -74,6 +74,7 @@ class Workspace:
         self.status = torch.zeros(4, dtype=torch.int32, device=device)   # bounded-wait error word of the kernels
         self.argmax = torch.zeros(2 * 4096, dtype=torch.int64, device=device)   # split-argmax accumulators + tickets
         self.attn_tickets = torch.zeros(1 << 16, dtype=torch.int32, device=device)   # decode split merge, per (b, hk)
+        self.chain_bar = torch.zeros(8, dtype=torch.int32, device=device)   # multi-phase GEMM grid barriers + ticket
         self.frozen = False
 
     def ensure(self, floats: int, counters: int = 0) -> None:
@@ -269,6 +270,57 @@ def w8a16_swiglu(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, force_
     return out.reshape(*x.shape[:-1], F)
 
 
+def w8a16_chain(phases: Sequence[tuple]) -> None:
+    """Run decode GEMMs back to back in ONE persistent cooperative launch, phase p + 1 reading phase p's outputs.
+
+    Phases (pre-tiled weights on the GPU; M <= 64), as tuples:
+      ``("f16", x, w, scale, out, in_ssq | None, inv_h, eps)``
+      ``("resid", x, w, scale, resid, gamma_next | None, xg_out | None, ssq_out | None)``
+      ``("swiglu", x, w_gu, s_gu, out, in_ssq | None, inv_h, eps)``
+      ``("qkv", x, w, scale, bias | None, q_rows, kv_rows, head_dim, positions, slots, cos, sin, q_out, k_cache,
+      v_cache, in_ssq | None, inv_h, eps)``
+    Supported sequences: resid, swiglu, resid[, qkv] (the decode layer transition) and f16, f16.  Between phases the
+    kernel waits on a grid barrier; the next phase's weights stream before it.  On CPU tensors the phases run one
+    after the other with the single-GEMM reference math."""
+    x0 = phases[0][1]
+    if not x0.is_cuda:
+        for ph in phases:
+            _chain_phase_reference(ph)
+        return
+    w = Workspace.get(x0.device)
+    need_f = need_c = 0
+    for ph in phases:
+        M, K = ph[1].shape
+        _, wsf, cnt = ext().chain_phase_plan(int(M), int(ph[3].numel()), int(K))
+        need_f, need_c = max(need_f, wsf), max(need_c, cnt)
+    w.ensure(need_f, need_c)
+    ext().w8a16_chain(list(phases), w.ws, w.counters, w.chain_bar)
+    LAUNCH_COUNTER.add()
+
+
+def _chain_phase_reference(ph: tuple) -> None:
+    kind = ph[0]
+
+    def norm(ssq, inv_h, eps):
+        return None if ssq is None else (ssq, int(round(1.0 / inv_h)), eps)
+
+    if kind == "f16":
+        _, x, wt, sc, out, ssq, inv_h, eps = ph
+        w8a16_linear_out(x, wt, sc, out, in_norm=norm(ssq, inv_h, eps))
+    elif kind == "resid":
+        _, x, wt, sc, resid, gamma_next, xg_out, ssq_out = ph
+        w8a16_residual_(x, wt, sc, resid, gamma_next=gamma_next, xg_out=xg_out, ssq_out=ssq_out)
+    elif kind == "swiglu":
+        _, x, wt, sc, out, ssq, inv_h, eps = ph
+        out.copy_(w8a16_swiglu(x, wt, sc, in_norm=norm(ssq, inv_h, eps)))
+    elif kind == "qkv":
+        (_, x, wt, sc, bias, q_rows, kv_rows, hd, pos, slots, cos_t, sin_t, q_out, kc, vc, ssq, inv_h, eps) = ph
+        w8a16_qkv_rope_append(x, wt, sc, bias, q_rows, kv_rows, hd, pos, slots, cos_t, sin_t, kc, vc, q_out=q_out,
+                              in_norm=norm(ssq, inv_h, eps))
+    else:
+        raise ValueError(f"unknown chain phase {kind!r}")
+
+
 def w8a16_qkv_rope_append(x: torch.Tensor, w_qkv: torch.Tensor, s_qkv: torch.Tensor, bias: Optional[torch.Tensor],
                           q_rows: int, kv_rows: int, head_dim: int, positions: torch.Tensor, slots: torch.Tensor,
                           cos_t: torch.Tensor, sin_t: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
@@ -389,6 +441,7 @@ def check_status(device=None) -> None:
     if v:
         w.status.zero_()
         w.counters.zero_()   # stream-K tickets may be left mid-count by an aborted launch
+        w.chain_bar.zero_()
         raise RuntimeError(f"a kernel reported a bounded-wait timeout (code {v})")
 
 

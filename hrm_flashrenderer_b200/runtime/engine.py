@@ -51,6 +51,7 @@ class InferenceEngine:
         nb = num_blocks or self.ecfg.num_kv_blocks or self.ecfg.max_batch * self.max_blocks
         model.alloc_kv(int(nb), bs)
         model.sequence_parallel = bool(self.ecfg.sequence_parallel)
+        model.chain_layers = bool(self.ecfg.chain_layers)
         self.bm = BlockManager(int(nb), bs)
         self._graphs: Dict[int, _DecodeGraph] = {}
         self._next_seq = 0
