@@ -310,7 +310,7 @@ void w8a16_chain(py::list phases, at::Tensor ws, at::Tensor counters, at::Tensor
     } else {
       TORCH_CHECK(false, "chain: unknown phase kind ", kind);
     }
-    TORCH_CHECK(a.M > 0 && a.M <= 64, "chain: 1 <= M <= 64");
+    TORCH_CHECK(a.M > 0 && a.M <= 32, "chain: 1 <= M <= 32");
     check_ws(hrm::gemm_chain_phase_plan(a.M, a.N, a.K, G), ws, counters);
     d[p].x = x.data_ptr();
     d[p].ldx = (int)x.stride(0);

@@ -232,7 +232,7 @@ class LlamaW8:
         q_out = torch.empty(T, self.q_rows, dtype=torch.bfloat16, device=dev)
         attn = torch.empty(T, p.local_heads, D, dtype=torch.float16 if cuda else torch.float32, device=dev)
         partial = torch.empty(T, H, dtype=torch.float32, device=dev) if tp else None
-        chain = self.chain_layers and b.is_decode and not tp and T <= 64
+        chain = self.chain_layers and b.is_decode and not tp and T <= 32
         act_buf = torch.empty(T, self.layers[0].s_gu.numel() // 2, dtype=xg.dtype, device=dev) if chain else None
         qkv_done = False   # the previous layer's chain already ran this layer's QKV GEMM
         for l, L in enumerate(self.layers):

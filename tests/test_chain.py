@@ -1,8 +1,9 @@
 """Multi-phase decode GEMM chain (o_proj -> gate/up -> down -> next QKV in one launch).
 
 CPU: the model's chained decode path (ops run phase by phase) gives the same tokens as the per-GEMM path.
-GPU: the cooperative multi-phase kernel against the single-GEMM kernels.  The GPU tests run when HRM_TEST_CHAIN=1
-(the kernel is new; they are switched on together with its first measurement)."""
+GPU: the cooperative multi-phase kernel against the single-GEMM kernels.  The GPU tests run when HRM_TEST_CHAIN=1:
+the f16 pair matched the single launches bitwise at M = 1 and 16 on a B200; the decode-layer sequence has not run
+on a GPU yet, and M 33..64 (BN = 64) is rejected after a timeout on its first run."""
 import os
 from dataclasses import replace
 
@@ -37,7 +38,7 @@ def test_cpu_chained_decode_matches_per_gemm_path():
 
 @pytest.mark.gpu
 @pytest.mark.skipif(not RUN_GPU, reason="set HRM_TEST_CHAIN=1 to run the multi-phase kernel")
-@pytest.mark.parametrize("M", [1, 16, 40])
+@pytest.mark.parametrize("M", [1, 16, 32])
 def test_gpu_chain_f16_pair_matches_two_launches(M):
     dev = "cuda"
     g = torch.Generator(device="cpu").manual_seed(M)
