@@ -21,8 +21,11 @@ REF = os.path.join(HERE, "_ref")
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--src", default=os.environ.get("HRM_REFERENCE_SRC", "/root/reference"))
+    ap.add_argument("--src", default=os.environ.get("HRM_REFERENCE_SRC", ""),
+                    help="reference source tree (or set HRM_REFERENCE_SRC)")
     args = ap.parse_args()
+    if not args.src:
+        ap.error("give the reference source tree with --src or HRM_REFERENCE_SRC")
     os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0"
     from torch.utils.cpp_extension import load
     tmp = tempfile.mkdtemp(prefix="refext_")
