@@ -31,6 +31,9 @@ enum : int {
   kErrTimeoutPeer = 5,
   kErrBadShape = 6,
   kErrTimeoutGrid = 7,   // grid-wide barrier of a persistent multi-phase kernel
+  // multi-phase GEMM chain: which ring wait gave up first (the status word keeps the first error)
+  kErrChainWEmpty = 8, kErrChainXEmpty = 9, kErrChainFEmpty = 10, kErrChainWFull = 11, kErrChainXFull = 12,
+  kErrChainFFull = 13, kErrChainAEmpty = 14, kErrChainAFull = 15,
 };
 
 // Every wait is bounded in time: 2 s of %globaltimer, far above any legitimate wait in these kernels (the longest

@@ -850,7 +850,7 @@ HRM_DEVINL void chain_epi_phase(const GemmArgs& a, int64_t u0, int64_t u1, int64
     const int acc = seg & 1;
     const uint32_t acc_addr = tmem + (uint32_t)(acc * S::kAccCols) + ((uint32_t)(quad * 32) << 16);
     const uint32_t valid = (S::NACC == 1 || ue - u >= 2) ? ((1u << S::NACC) - 1u) : (1u << ((u - u0) % S::NACC));
-    mbar_wait_ab(&afull[acc], (uint32_t)(seg >> 1) & 1u, a.status, kErrTimeoutAccum, abort_flag);
+    mbar_wait_ab(&afull[acc], (uint32_t)(seg >> 1) & 1u, a.status, kErrChainAFull, abort_flag);
     tc_fence_after();
     if (whole) {
       if (a.in_ssq != nullptr) compute_row_scale<BN>(a, m_tile, inv, et);
@@ -1003,7 +1003,7 @@ w8a16_chain_kernel(const __grid_constant__ CUtensorMap tx0, const __grid_constan
         auto issue_w = [&](int64_t i) -> bool {
           const int64_t u = u0 + i;
           const int tile = (int)(u / a.k_tiles), kt = (int)(u % a.k_tiles), n_tile = tile % a.n_tiles;
-          if (!mbar_wait_ab(&wempty[sw], pw, c.status, kErrTimeoutEmpty, abort_flag)) return false;
+          if (!mbar_wait_ab(&wempty[sw], pw, c.status, kErrChainWEmpty, abort_flag)) return false;
           mbar_arrive_expect_tx(&wfull[sw], (uint32_t)(ku * kWrawBytes));
           bulk_load(wraw + sw * S::kWSlot, a.w_tiles + ((size_t)n_tile * kt_total + (size_t)kt * ku) * kWrawBytes,
                     (uint32_t)(ku * kWrawBytes), &wfull[sw]);
@@ -1022,7 +1022,7 @@ w8a16_chain_kernel(const __grid_constant__ CUtensorMap tx0, const __grid_constan
           if (i >= pre && !(ok = issue_w(i))) break;
           const int64_t u = u0 + i;
           const int tile = (int)(u / a.k_tiles), kt = (int)(u % a.k_tiles), m_tile = tile / a.n_tiles;
-          if (!(ok = mbar_wait_ab(&xempty[sx], px, c.status, kErrTimeoutEmpty, abort_flag))) break;
+          if (!(ok = mbar_wait_ab(&xempty[sx], px, c.status, kErrChainXEmpty, abort_flag))) break;
           mbar_arrive_expect_tx(&xfull[sx], (uint32_t)(ku * S::kXSub));
           tma_load_3d(xs + sx * S::kXSlot, tmx(p), &xfull[sx], 0, m_tile * BN, kt * ku);
           ++nx;
@@ -1055,7 +1055,7 @@ w8a16_chain_kernel(const __grid_constant__ CUtensorMap tx0, const __grid_constan
           const int64_t ue = tile_end < u1 ? tile_end : u1;
           const int acc = seg & 1;
           const uint32_t acc_addr = tmem + (uint32_t)(acc * S::kAccCols + mw * BN);
-          ok = mbar_wait_ab(&aempty[acc], ((uint32_t)(seg >> 1) & 1u) ^ 1u, c.status, kErrTimeoutAccum, abort_flag);
+          ok = mbar_wait_ab(&aempty[acc], ((uint32_t)(seg >> 1) & 1u) ^ 1u, c.status, kErrChainAEmpty, abort_flag);
           tc_fence_after();
           bool first = true;
           for (int64_t k = u; ok && k < ue; ++k) {
@@ -1064,8 +1064,8 @@ w8a16_chain_kernel(const __grid_constant__ CUtensorMap tx0, const __grid_constan
               if (++f == F) { f = 0; phf ^= 1u; }
               continue;
             }
-            if constexpr (!kFoldX) ok = mbar_wait_ab(&xfull[sx], phx, c.status, kErrTimeoutFull, abort_flag);
-            ok = ok && mbar_wait_ab(&ffull[f], phf, c.status, kErrTimeoutDequant, abort_flag);
+            if constexpr (!kFoldX) ok = mbar_wait_ab(&xfull[sx], phx, c.status, kErrChainXFull, abort_flag);
+            ok = ok && mbar_wait_ab(&ffull[f], phf, c.status, kErrChainFFull, abort_flag);
             if (!ok) break;
             tc_fence_after();
             const uint64_t bdesc = xdesc0 + (uint64_t)((sx * S::kXSlot) >> 4);
@@ -1111,10 +1111,10 @@ w8a16_chain_kernel(const __grid_constant__ CUtensorMap tx0, const __grid_constan
       const int64_t n = unit_start(blockIdx.x + 1, U, G) - unit_start(blockIdx.x, U, G);
       const int ku = a.ku;
       for (int64_t i = 0; i < n; ++i) {
-        if (!(ok = mbar_wait_ab(&wfull[sw], pw, c.status, kErrTimeoutFull, abort_flag))) break;
-        if (!(ok = mbar_wait_ab(&fempty[f], pf, c.status, kErrTimeoutEmpty, abort_flag))) break;
+        if (!(ok = mbar_wait_ab(&wfull[sw], pw, c.status, kErrChainWFull, abort_flag))) break;
+        if (!(ok = mbar_wait_ab(&fempty[f], pf, c.status, kErrChainFEmpty, abort_flag))) break;
         if constexpr (kFoldX) {
-          if (!(ok = mbar_wait_ab(&xfull[sx], px, c.status, kErrTimeoutFull, abort_flag))) break;
+          if (!(ok = mbar_wait_ab(&xfull[sx], px, c.status, kErrChainXFull, abort_flag))) break;
         }
         tc_fence_after();
         for (int j = half; j < ku; j += 2) {

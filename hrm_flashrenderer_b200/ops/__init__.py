@@ -434,6 +434,13 @@ def decode_splits(max_ctx: int, batch_heads: int, block_size: int = 16, sms: int
     return splits, per * KEYS_PER_TILE
 
 
+# Status-word codes written by the kernels' bounded waits (csrc/common.cuh).
+STATUS_NAMES = {1: "full", 2: "empty", 3: "dequant", 4: "accumulator", 5: "peer flag", 6: "bad shape",
+                7: "grid barrier", 8: "chain weight-empty", 9: "chain activation-empty", 10: "chain A-stage-empty",
+                11: "chain weight-full", 12: "chain activation-full", 13: "chain A-stage-full",
+                14: "chain accumulator-empty", 15: "chain accumulator-full"}
+
+
 def check_status(device=None) -> None:
     """Raise if any kernel on ``device`` hit a bounded-wait timeout (reads the status word; synchronizes)."""
     w = Workspace.get(device if device is not None else torch.device("cuda"))
@@ -442,7 +449,7 @@ def check_status(device=None) -> None:
         w.status.zero_()
         w.counters.zero_()   # stream-K tickets may be left mid-count by an aborted launch
         w.chain_bar.zero_()
-        raise RuntimeError(f"a kernel reported a bounded-wait timeout (code {v})")
+        raise RuntimeError(f"a kernel reported a bounded-wait timeout (code {v}: {STATUS_NAMES.get(v, '?')})")
 
 
 def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
