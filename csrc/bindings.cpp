@@ -150,6 +150,11 @@ void w8a16_gemm_residual(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tenso
   hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_RESID, a, p, cur_stream());
 }
 
+void fill_resid_ar(hrm::GemmArgs& a, const at::Tensor& resid, const at::Tensor& gamma_next, const at::Tensor& xg_out,
+                   const at::Tensor& ssq_out, const at::Tensor& peers, int64_t rank, int64_t world,
+                   int64_t off_partials, int64_t off_final, int64_t off_flags, int64_t tile_floats, int64_t max_tiles,
+                   int64_t epoch_ptr, const at::Tensor& launch_ticket);
+
 // Tensor-parallel residual GEMM fused with the all-reduce over peer memory (decode, M <= 64):
 //   resid = resid + sum_ranks(x_r @ W_r^T);  xg = resid * gamma_next;  ssq = per-tile sums of squares.
 void w8a16_gemm_residual_ar(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tensor resid, at::Tensor ws,
@@ -160,6 +165,18 @@ void w8a16_gemm_residual_ar(at::Tensor x, at::Tensor w, at::Tensor scale, at::Te
   c10::cuda::CUDAGuard g(x.device());
   auto a = base_args(x, w, scale, c10::nullopt, ws, counters);
   if (a.M == 0) return;
+  fill_resid_ar(a, resid, gamma_next, xg_out, ssq_out, peers, rank, world, off_partials, off_final, off_flags,
+                tile_floats, max_tiles, epoch_ptr, launch_ticket);
+  auto p = hrm::gemm_plan(a.M, a.N, a.K, 0);
+  check_ws(p, ws, counters);
+  hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_RESID_AR, a, p,
+                         cur_stream());
+}
+
+void fill_resid_ar(hrm::GemmArgs& a, const at::Tensor& resid, const at::Tensor& gamma_next, const at::Tensor& xg_out,
+                   const at::Tensor& ssq_out, const at::Tensor& peers, int64_t rank, int64_t world,
+                   int64_t off_partials, int64_t off_final, int64_t off_flags, int64_t tile_floats, int64_t max_tiles,
+                   int64_t epoch_ptr, const at::Tensor& launch_ticket) {
   CHECK_DTYPE(resid, at::kFloat); CHECK_DTYPE(gamma_next, at::kFloat); CHECK_DTYPE(xg_out, at::kHalf);
   CHECK_DTYPE(ssq_out, at::kFloat); CHECK_DTYPE(peers, at::kLong); CHECK_DTYPE(launch_ticket, at::kInt);
   TORCH_CHECK(resid.size(0) == a.M && resid.size(1) == a.N && resid.stride(1) == 1, "bad resid");
@@ -182,10 +199,6 @@ void w8a16_gemm_residual_ar(at::Tensor x, at::Tensor w, at::Tensor scale, at::Te
   a.ar_max_tiles = (int)max_tiles;
   a.epoch = reinterpret_cast<int*>((uintptr_t)epoch_ptr);
   a.launch_ticket = launch_ticket.data_ptr<int>();
-  auto p = hrm::gemm_plan(a.M, a.N, a.K, 0);
-  check_ws(p, ws, counters);
-  hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_RESID_AR, a, p,
-                         cur_stream());
 }
 
 void fill_swiglu(hrm::GemmArgs& a, const at::Tensor& out) {
@@ -295,6 +308,15 @@ void w8a16_chain(py::list phases, at::Tensor ws, at::Tensor counters, at::Tensor
       a = base_args(x, w, scale, c10::nullopt, ws, counters);
       fill_resid(a, t[4].cast<at::Tensor>(), opt_tensor(t[5]), opt_tensor(t[6]), opt_tensor(t[7]));
       d[p].epi = hrm::EPI_RESID;
+    } else if (kind == "resid_ar") {
+      // ("resid_ar", x, w, scale, resid, gamma_next, xg_out, ssq_out, peers, rank, world, off_partials, off_final,
+      //  off_flags, tile_floats, max_tiles, epoch_ptr, launch_ticket)
+      a = base_args(x, w, scale, c10::nullopt, ws, counters);
+      fill_resid_ar(a, t[4].cast<at::Tensor>(), t[5].cast<at::Tensor>(), t[6].cast<at::Tensor>(),
+                    t[7].cast<at::Tensor>(), t[8].cast<at::Tensor>(), t[9].cast<int64_t>(), t[10].cast<int64_t>(),
+                    t[11].cast<int64_t>(), t[12].cast<int64_t>(), t[13].cast<int64_t>(), t[14].cast<int64_t>(),
+                    t[15].cast<int64_t>(), t[16].cast<int64_t>(), t[17].cast<at::Tensor>());
+      d[p].epi = hrm::EPI_RESID_AR;
     } else if (kind == "swiglu") {
       a = base_args(x, w, scale, c10::nullopt, ws, counters);
       set_in_norm(a, opt_tensor(t[5]), t[6].cast<double>(), t[7].cast<double>());

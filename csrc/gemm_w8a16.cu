@@ -348,7 +348,7 @@ HRM_DEVINL void epilogue_store(const GemmArgs& a, int n_tile, int m_tile, int ro
   } else if constexpr (EPI == EPI_RESID_AR) {
     // this rank's partial tile -> its symmetric buffer ([token][128 rows], one slot per n tile)
     // push this rank's partial (16 tokens of this thread's row) into every rank's receive slot for this rank
-    const int ep = *reinterpret_cast<const volatile int*>(a.epoch) + 1;
+    const int ep = *reinterpret_cast<const volatile int*>(a.epoch) + 1 + a.ep_offset;
     const int stride = a.ar_tile_floats / kBM;
     float4 q[kChunk / 4];
 #pragma unroll
@@ -701,7 +701,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
     const int et = threadIdx.x - kFirstEpiWarp * 32;   // 0..127
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
-    const int ep = (EPI == EPI_RESID_AR) ? *reinterpret_cast<volatile int*>(a.epoch) + 1 : 0;
+    const int ep = (EPI == EPI_RESID_AR) ? *reinterpret_cast<volatile int*>(a.epoch) + 1 + a.ep_offset : 0;
     int seg = 0;
     for (int64_t u = u0; u < u1; ++seg) {
       const int tile = (int)(u / a.k_tiles);
@@ -838,8 +838,10 @@ HRM_DEVINL void chain_epi_phase(const GemmArgs& a, int64_t u0, int64_t u1, int64
                                 uint32_t tmem, uint64_t* afull, uint64_t* aempty, float* stage, float* inv,
                                 float* ssq_red, int* last_flag, volatile int* abort_flag, int et, int quad, int row) {
   using S = GemmSmem<BN>;
-  static_assert(EPI == EPI_RESID || EPI == EPI_SWIGLU || EPI == EPI_QKV || EPI == EPI_F16 || EPI == EPI_F32,
-                "chain phases: local epilogues only");
+  static_assert(EPI == EPI_RESID || EPI == EPI_SWIGLU || EPI == EPI_QKV || EPI == EPI_F16 || EPI == EPI_F32 ||
+                EPI == EPI_RESID_AR, "chain phase epilogue");
+  // the all-reduce epoch of this phase: read before any of its pushes (the kernel advances it only at its end)
+  const int ep = (EPI == EPI_RESID_AR) ? *reinterpret_cast<volatile int*>(a.epoch) + 1 + a.ep_offset : 0;
   for (int64_t u = u0; u < u1; ++seg) {
     const int tile = (int)(u / a.k_tiles);
     const int ka = (int)(u % a.k_tiles);
@@ -906,6 +908,8 @@ HRM_DEVINL void chain_epi_phase(const GemmArgs& a, int64_t u0, int64_t u1, int64
     }
     u = ue;
   }
+  // tensor-parallel phase: one flag hop, then every CTA reduces its share of the tiles from local memory
+  if constexpr (EPI == EPI_RESID_AR) ar_oneshot<BN>(a, row, et, ep, ssq_red);
 }
 
 template <int BN, int EPI>
@@ -1185,6 +1189,14 @@ w8a16_chain_kernel(const __grid_constant__ CUtensorMap tx0, const __grid_constan
     if (atomicAdd(&c.bar[kMaxChainPhases], 1) == (int)G - 1) {
       for (int p = 0; p < kMaxChainPhases; ++p) c.bar[p] = 0;
       c.bar[kMaxChainPhases] = 0;
+      // tensor-parallel chains: one epoch per all-reduce phase of this launch
+      constexpr int n_ar = (E0 == EPI_RESID_AR) + (E1 == EPI_RESID_AR) + (E2 == EPI_RESID_AR) + (E3 == EPI_RESID_AR);
+      if constexpr (n_ar > 0) {
+        int* epoch = nullptr;
+        for (int p = 0; p < nph; ++p)
+          if (c.ph[p].epoch != nullptr) epoch = c.ph[p].epoch;
+        if (epoch != nullptr) *reinterpret_cast<volatile int*>(epoch) = *reinterpret_cast<volatile int*>(epoch) + n_ar;
+      }
       __threadfence();
     }
   }
@@ -1479,6 +1491,13 @@ void gemm_chain_launch(const ChainPhaseDesc* ph, int nph, int* bar, cudaStream_t
                                   es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("x tensor map encode failed: " + std::to_string((int)r));
+    if (epi == EPI_RESID_AR) {
+      if (a.N / kBM > a.ar_max_tiles || a.N % kBM != 0) throw std::runtime_error("w8a16 chain: bad all-reduce tiles");
+      if ((int64_t)a.M * kBM > a.ar_tile_floats) throw std::runtime_error("w8a16 chain: symmetric slot too small");
+      int k = 0;
+      for (int q = 0; q < p; ++q) k += ph[q].epi == EPI_RESID_AR;
+      a.ep_offset = k;   // the k-th all-reduce of this launch
+    }
     if (a.status == nullptr) a.status = c.status;
     a.trace = nullptr;
     a.k_tiles = pl.k_tiles;
@@ -1498,6 +1517,10 @@ void gemm_chain_launch(const ChainPhaseDesc* ph, int nph, int* bar, cudaStream_t
     launch_chain<EPI_RESID, EPI_SWIGLU, EPI_RESID, EPI_QKV>(bn, tx, c, G, stream);
   else if (is(EPI_RESID, EPI_SWIGLU, EPI_RESID, -1))
     launch_chain<EPI_RESID, EPI_SWIGLU, EPI_RESID, -1>(bn, tx, c, G, stream);
+  else if (is(EPI_RESID_AR, EPI_SWIGLU, EPI_RESID_AR, EPI_QKV))
+    launch_chain<EPI_RESID_AR, EPI_SWIGLU, EPI_RESID_AR, EPI_QKV>(bn, tx, c, G, stream);
+  else if (is(EPI_RESID_AR, EPI_SWIGLU, EPI_RESID_AR, -1))
+    launch_chain<EPI_RESID_AR, EPI_SWIGLU, EPI_RESID_AR, -1>(bn, tx, c, G, stream);
   else if (is(EPI_F16, EPI_F16, -1, -1))
     launch_chain<EPI_F16, EPI_F16, -1, -1>(bn, tx, c, G, stream);
   else

@@ -49,6 +49,7 @@ struct GemmArgs {
   int ar_max_tiles;
   int* epoch;                                     // this rank's launch epoch counter (in its symmetric buffer)
   int* launch_ticket;                             // [2] CTA tickets: phase-1 barrier, kernel end (zero between launches)
+  int ep_offset;                                  // this all-reduce's epoch = *epoch + 1 + ep_offset (0 unless chained)
   float* ws;                                // stream-K partials: plan.ws_floats floats
   int* counters;                            // stream-K tickets: plan.counters ints, zero before first use
   // EPI_QKV
@@ -80,7 +81,8 @@ GemmPlan gemm_plan(int M, int N, int K, int force_ctas = 0);
 // ---------------------------------------------------------------------------------------------- multi-phase chain
 // Up to kMaxChainPhases decode GEMMs in one persistent cooperative launch, phase p + 1 reading phase p's outputs
 // (grid barrier in between; the next phase's weights stream before it).  Supported epilogue sequences:
-// {RESID, SWIGLU, RESID, QKV}, {RESID, SWIGLU, RESID} and {F16, F16}; pre-tiled weights; M <= 64.
+// {RESID, SWIGLU, RESID, QKV}, {RESID, SWIGLU, RESID}, the tensor-parallel {RESID_AR, SWIGLU, RESID_AR, QKV} /
+// {RESID_AR, SWIGLU, RESID_AR} and {F16, F16}; pre-tiled weights; M <= 32.
 constexpr int kMaxChainPhases = 4;
 struct ChainArgs {
   int nph;

@@ -112,7 +112,7 @@ class LlamaW8:
         self.kv: Optional[PagedKVPool] = None
         self.symm = None   # SymmetricWorkspace: enables the fused GEMM + all-reduce kernels when TP > 1
         self.sequence_parallel = False   # prefill: token-sharded residual between blocks (TP > 1)
-        self.chain_layers = False        # decode, TP = 1: o_proj, gate/up, down, next QKV in one GEMM launch
+        self.chain_layers = False        # decode: o_proj, gate/up, down, next QKV in one multi-phase GEMM launch
 
     def enable_fused_collectives(self, group=None) -> None:
         """Allocate / exchange the NVLink symmetric buffers (collective over the TP group)."""
@@ -232,7 +232,8 @@ class LlamaW8:
         q_out = torch.empty(T, self.q_rows, dtype=torch.bfloat16, device=dev)
         attn = torch.empty(T, p.local_heads, D, dtype=torch.float16 if cuda else torch.float32, device=dev)
         partial = torch.empty(T, H, dtype=torch.float32, device=dev) if tp else None
-        chain = self.chain_layers and b.is_decode and not tp and T <= 32
+        # multi-phase chain: TP = 1, or TP with the fused peer-memory all-reduce (symmetric workspace present)
+        chain = self.chain_layers and b.is_decode and T <= 32 and (not tp or self.symm is not None)
         act_buf = torch.empty(T, self.layers[0].s_gu.numel() // 2, dtype=xg.dtype, device=dev) if chain else None
         qkv_done = False   # the previous layer's chain already ran this layer's QKV GEMM
         for l, L in enumerate(self.layers):
@@ -254,9 +255,14 @@ class LlamaW8:
                 # o_proj + residual -> gate/up + SwiGLU -> down + residual (-> next layer's QKV): one launch
                 g_next = self.layers[l + 1].ln1 if l + 1 < len(self.layers) else self.final_norm
                 inv_h = 1.0 / H
-                phases = [("resid", a2, L.w_o, L.s_o, x, L.ln2, xg, ssq),
-                          ("swiglu", xg, L.w_gu, L.s_gu, act_buf, ssq, inv_h, cfg.rms_eps),
-                          ("resid", act_buf, L.w_d, L.s_d, x, g_next, xg, ssq)]
+                if tp:
+                    phases = [("resid_ar", a2, L.w_o, L.s_o, x, self.symm, L.ln2, xg, ssq),
+                              ("swiglu", xg, L.w_gu, L.s_gu, act_buf, ssq, inv_h, cfg.rms_eps),
+                              ("resid_ar", act_buf, L.w_d, L.s_d, x, self.symm, g_next, xg, ssq)]
+                else:
+                    phases = [("resid", a2, L.w_o, L.s_o, x, L.ln2, xg, ssq),
+                              ("swiglu", xg, L.w_gu, L.s_gu, act_buf, ssq, inv_h, cfg.rms_eps),
+                              ("resid", act_buf, L.w_d, L.s_d, x, g_next, xg, ssq)]
                 if l + 1 < len(self.layers):
                     Ln = self.layers[l + 1]
                     phases.append(("qkv", xg, Ln.w_qkv, Ln.s_qkv, Ln.b_qkv, self.q_rows, self.kv_rows, D,

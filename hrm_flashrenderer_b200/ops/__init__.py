@@ -276,10 +276,13 @@ def w8a16_chain(phases: Sequence[tuple]) -> None:
     Phases (pre-tiled weights on the GPU; M <= 64), as tuples:
       ``("f16", x, w, scale, out, in_ssq | None, inv_h, eps)``
       ``("resid", x, w, scale, resid, gamma_next | None, xg_out | None, ssq_out | None)``
+      ``("resid_ar", x, w, scale, resid, symm, gamma_next, xg_out, ssq_out)`` (tensor parallel: the partial tiles
+      are all-reduced over NVLink peer memory inside the phase, as :func:`w8a16_residual_ar_`)
       ``("swiglu", x, w_gu, s_gu, out, in_ssq | None, inv_h, eps)``
       ``("qkv", x, w, scale, bias | None, q_rows, kv_rows, head_dim, positions, slots, cos, sin, q_out, k_cache,
       v_cache, in_ssq | None, inv_h, eps)``
-    Supported sequences: resid, swiglu, resid[, qkv] (the decode layer transition) and f16, f16.  Between phases the
+    Supported sequences: resid, swiglu, resid[, qkv] (the decode layer transition), the same with resid_ar (tensor
+    parallel) and f16, f16.  Between phases the
     kernel waits on a grid barrier; the next phase's weights stream before it.  On CPU tensors the phases run one
     after the other with the single-GEMM reference math."""
     x0 = phases[0][1]
@@ -289,12 +292,19 @@ def w8a16_chain(phases: Sequence[tuple]) -> None:
         return
     w = Workspace.get(x0.device)
     need_f = need_c = 0
+    native = []
     for ph in phases:
         M, K = ph[1].shape
         _, wsf, cnt = ext().chain_phase_plan(int(M), int(ph[3].numel()), int(K))
         need_f, need_c = max(need_f, wsf), max(need_c, cnt)
+        if ph[0] == "resid_ar":
+            _, x, wt, sc, resid, symm, gamma_next, xg_out, ssq_out = ph
+            ph = ("resid_ar", x, wt, sc, resid, gamma_next, xg_out, ssq_out, symm.peers, symm.rank, symm.world,
+                  symm.off_partials, symm.off_final, symm.off_flags, symm.max_bn * 128, symm.max_tiles,
+                  symm.epoch_ptr, symm.ticket)
+        native.append(ph)
     w.ensure(need_f, need_c)
-    ext().w8a16_chain(list(phases), w.ws, w.counters, w.chain_bar)
+    ext().w8a16_chain(native, w.ws, w.counters, w.chain_bar)
     LAUNCH_COUNTER.add()
 
 
@@ -317,6 +327,8 @@ def _chain_phase_reference(ph: tuple) -> None:
         (_, x, wt, sc, bias, q_rows, kv_rows, hd, pos, slots, cos_t, sin_t, q_out, kc, vc, ssq, inv_h, eps) = ph
         w8a16_qkv_rope_append(x, wt, sc, bias, q_rows, kv_rows, hd, pos, slots, cos_t, sin_t, kc, vc, q_out=q_out,
                               in_norm=norm(ssq, inv_h, eps))
+    elif kind == "resid_ar":
+        raise RuntimeError("resid_ar chain phases need CUDA tensors (peer-memory all-reduce)")
     else:
         raise ValueError(f"unknown chain phase {kind!r}")
 

@@ -64,12 +64,14 @@ def check_engine(rank, world, dev):
     w = synth_weights(cfg, seed=1)
     prompts = [torch.randint(0, cfg.vocab, (40,), generator=torch.Generator().manual_seed(i)).tolist() for i in range(3)]
     outs = {}
-    for fused in (False, True):
+    # HRM_TEST_CHAIN=1 adds the multi-phase decode chain with in-kernel all-reduce phases
+    modes = (False, True, "chain") if os.environ.get("HRM_TEST_CHAIN", "0") == "1" else (False, True)
+    for fused in modes:
         model = LlamaW8.from_weights(cfg, w, rank=rank, world=world, device=dev, comm=TPComm(), max_pos=512)
         if fused:
             model.enable_fused_collectives()
-        eng = InferenceEngine(model, EngineConfig(tp=world, max_seq_len=256, max_batch=4, use_cuda_graphs=True),
-                              num_blocks=64)
+        eng = InferenceEngine(model, EngineConfig(tp=world, max_seq_len=256, max_batch=4, use_cuda_graphs=True,
+                                                  chain_layers=fused == "chain"), num_blocks=64)
         outs[fused] = eng.generate(prompts, 12, stop_on_eos=False)
         del eng
         if model.symm is not None:
@@ -79,22 +81,26 @@ def check_engine(rank, world, dev):
         m1 = LlamaW8.from_weights(cfg, w, device=dev, max_pos=512)
         e1 = InferenceEngine(m1, EngineConfig(max_seq_len=256, max_batch=4, use_cuda_graphs=False), num_blocks=64)
         single = e1.generate(prompts, 12, stop_on_eos=False)
-    return outs[False], outs[True], single
+    return outs[False], outs[True], single, outs.get("chain")
 
 
 def main():
     rank, local, world = init_dist_env("nccl")
     dev = torch.device("cuda", local)
     worst = check_fused_ar(rank, world, dev)
-    nccl_out, fused_out, single = check_engine(rank, world, dev)
+    nccl_out, fused_out, single, chain_out = check_engine(rank, world, dev)
     ok = True
     if rank == 0:
         first_div = lambda a, b: next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), len(a))
         agree_fused = fused_out == nccl_out
         agree_single = min(first_div(a, b) for a, b in zip(nccl_out, single))
         ok = agree_single >= 8
-        print(json.dumps({"ok": ok, "world": world, "fused_ar_max_err": worst, "fused_equals_nccl": agree_fused,
-                          "tp_vs_tp1_first_divergence": agree_single}), flush=True)
+        rec = {"ok": ok, "world": world, "fused_ar_max_err": worst, "fused_equals_nccl": agree_fused,
+               "tp_vs_tp1_first_divergence": agree_single}
+        if chain_out is not None:
+            rec["chain_equals_fused"] = chain_out == fused_out
+            ok = rec["ok"] = ok and rec["chain_equals_fused"]
+        print(json.dumps(rec), flush=True)
     dist.barrier()
     dist.destroy_process_group()
     sys.exit(0 if ok else 1)
