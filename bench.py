@@ -304,6 +304,12 @@ def run_reference(a):
         if world > 1:
             dist.destroy_process_group()
         return
+    except Exception as e:   # the reference's own code failed: report it instead of a traceback-only exit
+        _emit(rank, {"impl": "reference",
+                     "unavailable": f"reference run failed: {type(e).__name__}: {e}".replace("\n", " ")[:300]})
+        if world > 1:
+            dist.destroy_process_group()
+        return
     value = a.batch * a.steps / (ms / 1e3)
     rec = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
