@@ -32,12 +32,16 @@ class MirroredEngine:
 
     _MIRRORED = ("prefill", "load_decode_batch", "decode_step", "release", "new_seq", "capture", "reset")
 
-    def __init__(self, engine, group):
+    def __init__(self, engine, group, watchdog=None):
         self._engine = engine
         self._group = group
         self._lock = threading.Lock()
+        self._watchdog = watchdog
 
     def _bcast(self, name: str, payload) -> None:
+        # a lost follower is found on the host before the next broadcast / collective is issued
+        if self._watchdog is not None and name != "__shutdown__":
+            self._watchdog.check()
         dist.broadcast_object_list([(name, payload)], src=0, group=self._group)
 
     def __getattr__(self, item):
@@ -59,13 +63,15 @@ class MirroredEngine:
             self._bcast("__shutdown__", ((), {}))
 
 
-def follower_loop(engine, group) -> None:
+def follower_loop(engine, group, on_shutdown: Optional[Callable[[], None]] = None) -> None:
     """Replay rank 0's engine calls until shutdown."""
     while True:
         box = [None]
         dist.broadcast_object_list(box, src=0, group=group)
         name, (args, kwargs) = box[0]
         if name == "__shutdown__":
+            if on_shutdown is not None:
+                on_shutdown()
             return
         if name == "decode_step":
             engine.decode_step(engine._decode_state(args[0]))
@@ -85,6 +91,7 @@ class LaneArgs:
     master_port: int = 29555
     kv_fraction: float = 0.85
     num_kv_blocks: int = 0
+    heartbeat_timeout_s: float = 30.0   # a TP peer silent this long is treated as lost
 
 
 def build_engine(a: LaneArgs, rank: int, world: int, comm):
@@ -130,18 +137,32 @@ def run_worker(rank: int, a: LaneArgs, on_rank0: Callable[[Any], None]) -> None:
     comm = TPComm()
     comm.control = control
     engine = build_engine(a, rank, a.world, comm)
+    watchdog = None
+    closing = threading.Event()   # set once rank 0 has announced the shutdown: its exit is then expected
+    if a.world > 1:
+        from ..parallel.watchdog import HeartbeatWatchdog
+
+        def lost(e):   # followers block inside the broadcast: a silent peer ends the process
+            if closing.is_set():
+                return
+            print(f"[daemon rank {rank}] {e}; exiting", flush=True)
+            os._exit(3)
+        watchdog = HeartbeatWatchdog(dist.distributed_c10d._get_default_store(), rank, a.world,
+                                     timeout_s=a.heartbeat_timeout_s, on_failure=None if rank == 0 else lost).start()
     try:
         if a.world == 1:
             on_rank0(engine)
         elif rank == 0:
-            mirror = MirroredEngine(engine, control)
+            mirror = MirroredEngine(engine, control, watchdog)
             try:
                 on_rank0(mirror)
             finally:
                 mirror.shutdown()
         else:
-            follower_loop(engine, control)
+            follower_loop(engine, control, on_shutdown=closing.set)
     finally:
+        if watchdog is not None:
+            watchdog.stop(clean=True)
         if a.device == "cuda":
             torch.cuda.synchronize()
         del engine
