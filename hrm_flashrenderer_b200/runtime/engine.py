@@ -19,6 +19,7 @@ from typing import Callable, Dict, List, Optional, Sequence, Tuple
 import torch
 
 from .. import ops
+from ..utils.nvtx import nvtx_range
 from ..config import EngineConfig
 from ..models.llama import BatchMeta, LlamaW8
 from .kv_cache import BlockManager
@@ -118,7 +119,8 @@ class InferenceEngine:
                 if take < len(toks):
                     nxt.append((sid, toks[take:], start + take))
             meta = self._prefill_meta(chunks)
-            out = self.model.forward(meta).tolist()
+            with nvtx_range(f"prefill chunk {used} tokens"):
+                out = self.model.forward(meta).tolist()
             done_ids = {s for s, _, _ in nxt}
             for (sid, _, _), t in zip(chunks, out):
                 if sid not in done_ids:
@@ -219,10 +221,13 @@ class InferenceEngine:
         """One decode step for the staged batch; returns the device tensor of sampled tokens (bucket-sized)."""
         if self.ecfg.use_cuda_graphs and self.device.type == "cuda":
             if g.graph is None:
-                self.capture(g.bucket)
-            g.graph.replay()
+                with nvtx_range(f"capture decode b{g.bucket}"):
+                    self.capture(g.bucket)
+            with nvtx_range("decode step (graph)"):
+                g.graph.replay()
         else:
-            self._decode_body(g)
+            with nvtx_range("decode step"):
+                self._decode_body(g)
         return g.tokens
 
     def step_host(self, g: _DecodeGraph, host_ids: torch.Tensor, host_out: torch.Tensor) -> torch.Tensor:
