@@ -99,6 +99,16 @@ class ModelConfig:
         d["eos_token_ids"] = list(self.eos_token_ids)
         return d
 
+    @classmethod
+    def from_dict(cls, d: dict) -> "ModelConfig":
+        """Inverse of :meth:`to_dict`."""
+        d = dict(d)
+        rs = d.get("rope_scaling")
+        if isinstance(rs, dict):
+            d["rope_scaling"] = RopeScaling(**rs)
+        d["eos_token_ids"] = tuple(d.get("eos_token_ids", (2,)))
+        return cls(**d)
+
     # ---- HF config.json ------------------------------------------------------------------------
     @classmethod
     def from_hf_config(cls, cfg: dict, name: str = "hf") -> "ModelConfig":

@@ -95,11 +95,12 @@ class LlamaW8:
     """Int8-weight decoder shard for TP rank ``plan.rank`` of ``plan.world`` on one CUDA device."""
 
     def __init__(self, cfg: ModelConfig, plan: ShardPlan, layers: List[LayerWeights], embed: QTensor,
-                 lm_head: QTensor, final_norm: torch.Tensor, device, comm=None, max_pos: int = 8192):
+                 lm_head: QTensor, final_norm: torch.Tensor, device, comm=None, max_pos: int = 8192,
+                 head_pretiled: bool = False):
         self.cfg, self.plan, self.layers, self.device = cfg, plan, layers, torch.device(device)
         self.embed_q, self.embed_s = embed.q.contiguous(), embed.scale.contiguous()
         self.head_q, self.head_s = lm_head.q.contiguous(), lm_head.scale.contiguous()
-        if self.head_q.is_cuda:
+        if self.head_q.is_cuda and not head_pretiled:
             self.head_q = ops.tile_w8(self.head_q)
         self.final_norm = final_norm
         self.comm = comm
@@ -122,6 +123,23 @@ class LlamaW8:
                                            max_tiles=max(64, self.cfg.hidden // 128), max_bn=64, group=group)
 
     # ------------------------------------------------------------------ construction
+    @classmethod
+    def from_dsi8(cls, path: str, rank: int = 0, world: int = 1, device="cuda", comm=None, max_pos: int = 8192,
+                  cache_dir: Optional[str] = None) -> "LlamaW8":
+        """Load a DSI8 export for TP rank ``rank`` of ``world``.  With ``cache_dir`` the packed shard (fused QKV,
+        interleaved gate/up, GPU tile layout) is kept in a per-rank cache file keyed by the export's fingerprint,
+        the TP layout and the packing version, so later starts skip reading, sharding and re-tiling the export."""
+        from .packed_cache import load_packed, save_packed, cache_path
+        from ..formats.dsi8 import read_dsi8
+        cp = cache_path(cache_dir, path, rank, world, device) if cache_dir else None
+        if cp is not None and cp.is_file():
+            return load_packed(cls, cp, device, comm, max_pos)
+        cfg, w = read_dsi8(path)
+        model = cls.from_weights(cfg, w, rank=rank, world=world, device=device, comm=comm, max_pos=max_pos)
+        if cp is not None:
+            save_packed(model, cp)
+        return model
+
     @classmethod
     def from_weights(cls, cfg: ModelConfig, weights: Dict[str, Tensorish], rank: int = 0, world: int = 1,
                      device="cuda", comm=None, max_pos: int = 8192) -> "LlamaW8":

@@ -92,6 +92,7 @@ class LaneArgs:
     kv_fraction: float = 0.85
     num_kv_blocks: int = 0
     heartbeat_timeout_s: float = 30.0   # a TP peer silent this long is treated as lost
+    packed_cache_dir: str = ""           # per-rank packed-shard cache for DSI8 exports (default: HRM_PACKED_CACHE)
 
 
 def build_engine(a: LaneArgs, rank: int, world: int, comm):
@@ -105,10 +106,9 @@ def build_engine(a: LaneArgs, rank: int, world: int, comm):
         model = LlamaW8.synthesize(cfg, rank=rank, world=world, device=dev, seed=a.seed, comm=comm,
                                    max_pos=a.max_seq_len + 16)
     else:
-        from ..formats.dsi8 import read_dsi8
-        cfg, w = read_dsi8(a.model)
-        model = LlamaW8.from_weights(cfg, w, rank=rank, world=world, device=dev, comm=comm,
-                                     max_pos=a.max_seq_len + 16)
+        model = LlamaW8.from_dsi8(a.model, rank=rank, world=world, device=dev, comm=comm, max_pos=a.max_seq_len + 16,
+                                  cache_dir=a.packed_cache_dir or os.environ.get("HRM_PACKED_CACHE") or None)
+        cfg = model.cfg
     if a.num_kv_blocks:
         nb = a.num_kv_blocks
     elif dev.type == "cuda":
