@@ -170,9 +170,31 @@ def plan_lanes(layout: GPULayout, derived: Derived, env: Optional[Dict[str, str]
 RUN_DIR = REPO_ROOT / ".run" / "services"
 
 
-def lane_command(lane: str, tp: int, port: int, hrm_model: str, llm_model: str, extra: List[str]) -> List[str]:
-    return [sys.executable, "-m", "hrm_flashrenderer_b200.serving.cli", "serve", "--hrm_model", hrm_model,
-            "--llm_model", llm_model, "--world", str(tp), "--port", str(port)] + list(extra)
+# Per-lane context / prefill-chunk limits with the reference's environment overrides (names and fall-backs as
+# scripts/start_native_topology.sh:52-61,278-285: MAX_SEQ_<LANE>, then MAX_SEQ_SOLO / MAX_SEQ_NVLINK; PREFILL_*
+# alike).  The defaults are sized for B200 lanes (180 GB each), not the reference's 11-22 GB cards.
+LANE_LIMITS = {"solo_22gb": (8192, 4096, "SOLO"), "nvlink_pair": (8192, 4096, "NVLINK"),
+               "solo_3080": (8192, 4096, "SOLO")}
+
+
+def lane_limits(lane: str, env: Optional[Dict[str, str]] = None) -> Tuple[int, int]:
+    env = os.environ if env is None else env
+    seq, pre, group = LANE_LIMITS.get(lane, (4096, 768, "SOLO"))
+    up = lane.upper()
+    seq = int(env.get(f"MAX_SEQ_{up}") or env.get(f"MAX_SEQ_{group}") or seq)
+    pre = int(env.get(f"PREFILL_{up}") or env.get(f"PREFILL_{group}") or pre)
+    return seq, pre
+
+
+def lane_command(lane: str, tp: int, port: int, hrm_model: str, llm_model: str, extra: List[str],
+                 env: Optional[Dict[str, str]] = None) -> List[str]:
+    """The lane's ``serve`` command; ``HRM_FLASH_BIN`` replaces the interpreter + module prefix."""
+    env = os.environ if env is None else env
+    seq, pre = lane_limits(lane, env)
+    prefix = shlex.split(env["HRM_FLASH_BIN"]) if env.get("HRM_FLASH_BIN") else \
+        [sys.executable, "-m", "hrm_flashrenderer_b200.serving.cli"]
+    return prefix + ["serve", "--hrm_model", hrm_model, "--llm_model", llm_model, "--world", str(tp), "--port",
+                     str(port), "--max_seq_len", str(seq), "--prefill_chunk_size", str(pre)] + list(extra)
 
 
 def start_lane(lane: str, gpus: List[int], port: int, cmd: List[str], run_dir: Path = RUN_DIR) -> int:

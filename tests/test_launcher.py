@@ -77,3 +77,16 @@ def test_cli_detect(monkeypatch, tmp_path, capsys):
     assert "LANE_SOLO_22GB_GPUS=0,1,2,3" in out and "LANE_SOLO_3080_LINK=NVLINK" in out
     assert topo.main(["start", "--smi", FAKE, "--hrm_model", "m", "--llm_model", "synthetic:tiny", "--dry_run"]) == 0
     assert "CUDA_VISIBLE_DEVICES=4,5" in capsys.readouterr().out
+
+
+def test_lane_limits_and_command_env():
+    from hrm_flashrenderer_b200.launcher.topology import lane_limits, lane_command
+    assert lane_limits("nvlink_pair", {}) == (8192, 4096)
+    env = {"MAX_SEQ_SOLO": "3000", "PREFILL_SOLO_3080": "256", "MAX_SEQ_NVLINK_PAIR": "5000"}
+    assert lane_limits("solo_3080", env) == (3000, 256)
+    assert lane_limits("solo_22gb", env) == (3000, 4096)
+    assert lane_limits("nvlink_pair", env) == (5000, 4096)
+    cmd = lane_command("solo_3080", 1, 8083, "idx", "m.bin", ["--x"], env=dict(env, HRM_FLASH_BIN="/opt/bin/hrm-flash -v"))
+    assert cmd[:3] == ["/opt/bin/hrm-flash", "-v", "serve"]
+    assert cmd[cmd.index("--max_seq_len") + 1] == "3000" and cmd[cmd.index("--prefill_chunk_size") + 1] == "256"
+    assert cmd[-1] == "--x"
