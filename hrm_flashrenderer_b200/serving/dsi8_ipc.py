@@ -15,7 +15,8 @@ speaks the same protocol, so that driver can run unchanged against the B200 engi
   no EOS stop, as in the reference;
 * ``DSI8_TOKENS_FILE`` (default ``/tmp/deepseek_tokens.txt``) and ``DSI8_DONE_FILE`` (default
   ``/tmp/deepseek_done.flag``) are removed before generation; every new id is appended to the tokens file as
-  ``"<id>\\n"`` as soon as it is known, and the done file gets ``"done\\n"`` at the end.
+  ``"<id>\\n"`` as soon as it is known, and the done file gets ``"done\\n"`` at the end;
+* with ``TELEM_ENABLE=1`` the reference's UDP telemetry packets are sent (:mod:`.telemetry`).
 """
 from __future__ import annotations
 
@@ -77,9 +78,13 @@ def _read_ids(path: Path) -> List[int]:
 
 
 def poll_once(engine, paths: IpcPaths, max_ctx: int, bos_id: int, tgen: int,
-              log: Callable[[str], None] = print) -> bool:
-    """Serve one request if a prompt file is present; returns whether one was served."""
+              log: Callable[[str], None] = print, telemetry=None) -> bool:
+    """Serve one request if a prompt file is present; returns whether one was served.  With ``telemetry`` (a
+    :class:`~hrm_flashrenderer_b200.serving.telemetry.Telemetry`) an idle poll sends an ``AWAITING_PROMPT`` packet
+    and every generated token one packet with its step and the prompt, as the reference engine does."""
     if not paths.prompt.is_file():
+        if telemetry is not None:
+            telemetry.send(0, 0.0, None, "AWAITING_PROMPT")
         return False
     lines = paths.prompt.read_text(errors="replace").splitlines()
     paths.prompt.unlink(missing_ok=True)
@@ -93,20 +98,25 @@ def poll_once(engine, paths: IpcPaths, max_ctx: int, bos_id: int, tgen: int,
     paths.tokens.unlink(missing_ok=True)
     paths.done.unlink(missing_ok=True)
     if n_new > 0:
+        prompt_line = lines[0] if lines else ""
+        step = [len(ids)]
         with open(paths.tokens, "a") as f:
             def on_token(_i, t):
                 f.write(f"{int(t)}\n")
                 f.flush()
+                if telemetry is not None:
+                    telemetry.send(step[0], 0.0, None, prompt_line)
+                step[0] += 1
             engine.generate([ids], n_new, stop_on_eos=False, on_token=on_token)
     paths.done.write_text("done\n")
     return True
 
 
 def serve_forever(engine, paths: IpcPaths, max_ctx: int, bos_id: int, poll_s: float = 0.2,
-                  max_requests: Optional[int] = None, log: Callable[[str], None] = print) -> int:
+                  max_requests: Optional[int] = None, log: Callable[[str], None] = print, telemetry=None) -> int:
     served = 0
     while max_requests is None or served < max_requests:
-        if poll_once(engine, paths, max_ctx, bos_id, tgen_from_env(), log):
+        if poll_once(engine, paths, max_ctx, bos_id, tgen_from_env(), log, telemetry):
             served += 1
         else:
             time.sleep(poll_s)
@@ -120,9 +130,9 @@ def build_engine(a):
     from ..runtime.engine import InferenceEngine
     dev = torch.device(a.device)
     if a.dsi8:
-        from ..formats.dsi8 import read_dsi8
-        cfg, w = read_dsi8(a.dsi8)
-        model = LlamaW8.from_weights(cfg, w, device=dev, max_pos=a.max_seq_len + 16)
+        model = LlamaW8.from_dsi8(a.dsi8, device=dev, max_pos=a.max_seq_len + 16,
+                                  cache_dir=os.environ.get("HRM_PACKED_CACHE") or None)
+        cfg = model.cfg
     else:
         from ..models.weights import synth_weights
         cfg = get_preset(a.preset)
@@ -143,8 +153,10 @@ def main(argv=None) -> int:
     eng, cfg = build_engine(a)
     print(READY, flush=True)
     bos = int(getattr(cfg, "bos_token_id", 1) or 1)
+    from .telemetry import Telemetry
+    tel = Telemetry(model_id=cfg.name)   # TELEM_ENABLE=1 / TELEM_PORT / TELEM_TARGET
     serve_forever(eng, IpcPaths.from_env(), a.max_seq_len, bos, max_requests=a.max_requests or None,
-                  log=lambda s: print(s, flush=True))
+                  log=lambda s: print(s, flush=True), telemetry=tel if tel.enabled else None)
     return 0
 
 
