@@ -60,8 +60,8 @@ def gemm_shapes(tp: int):
     }
 
 
-def main():
-    ap = argparse.ArgumentParser()
+def main(argv=None):
+    ap = argparse.ArgumentParser(prog="hrm-flash-ops-sweep")
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--m", default="1,16,64,512,4096")
     ap.add_argument("--iters", type=int, default=10)
@@ -69,7 +69,7 @@ def main():
     ap.add_argument("--json", default="")
     ap.add_argument("--ops", default="gemm,attn,norm")
     ap.add_argument("--attn-b", default="1,16,64", help="decode-attention batch sizes (context 4096)")
-    a = ap.parse_args()
+    a = ap.parse_args(argv)
     hbm, tfl, src = peaks()
     dev = torch.device("cuda")
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
