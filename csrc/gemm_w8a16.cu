@@ -821,6 +821,7 @@ HRM_DEVINL bool grid_bar_wait(const int* p, int want, int* status, volatile int*
   const uint64_t t0 = global_ns();
   for (uint32_t i = 0;; ++i) {
     if (ld_acquire_gpu(p) >= want) return true;
+    __nanosleep(128);   // one poller per CTA role, backed off: the counter's L2 slice stays free for the arrivals
     if ((i & 63u) == 0) {
       if (*abort_flag) return false;
       if (global_ns() - t0 > kWaitLimitNs) {
@@ -951,6 +952,7 @@ w8a16_chain_kernel(const __grid_constant__ CUtensorMap tx0, const __grid_constan
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc);
   int* last_flag = misc + 1;
   volatile int* abort_flag = misc + 2;
+  volatile int* bar_ok = misc + 3;   // epilogue: the grid barrier its poller saw
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -1152,8 +1154,16 @@ w8a16_chain_kernel(const __grid_constant__ CUtensorMap tx0, const __grid_constan
     int seg = 0;
     for (int p = 0; p < nph; ++p) {
       const GemmArgs& a = c.ph[p];
-      // the residual and the folded-norm sums this phase reads were written by other CTAs in earlier phases
-      if (p > 0 && !grid_bar_wait(&c.bar[p - 1], (int)G, c.status, abort_flag)) break;
+      // the residual and the folded-norm sums this phase reads were written by other CTAs in earlier phases: one
+      // thread polls the grid barrier (acquire), the CTA barrier passes the result on, every thread fences
+      if (p > 0) {
+        if (et == 0) *bar_ok = grid_bar_wait(&c.bar[p - 1], (int)G, c.status, abort_flag) ? 1 : 0;
+        asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+        const bool passed = *bar_ok != 0;
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");   // bar_ok is rewritten next phase
+        if (!passed) break;
+      }
       const int64_t U = (int64_t)a.tiles * a.k_tiles;
       const int64_t u0 = unit_start(blockIdx.x, U, G), u1 = unit_start(blockIdx.x + 1, U, G);
       if (p == 0)
