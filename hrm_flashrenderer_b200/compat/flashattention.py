@@ -83,7 +83,7 @@ def _pool_from_pages(pages: torch.Tensor) -> Tuple[torch.Tensor, int]:
     """[B, Hk, P, PS, D] -> ([B * P * PS/16, Hk, 16, D] bf16, blocks per sequence)."""
     B, Hk, P, PS, D = pages.shape
     nbs = P * PS // 16
-    pool = pages.view(B, Hk, P, PS // 16, 16, D).permute(0, 2, 3, 1, 4, 5).reshape(B * nbs, Hk, 16, D)
+    pool = pages.reshape(B, Hk, P, PS // 16, 16, D).permute(0, 2, 3, 1, 4, 5).reshape(B * nbs, Hk, 16, D)
     return pool.to(torch.bfloat16).contiguous(), nbs
 
 
