@@ -1,0 +1,355 @@
+// Shared device code of the W8A16 tcgen05 GEMM kernels (single launch in gemm_w8a16.cu, multi-phase chain in
+// gemm_chain.cu): constants, per-width pipeline shapes, the epilogue variants, the peer-memory all-reduce epilogue and
+// the host helpers both launchers use.  The design is described at the top of gemm_w8a16.cu.
+#pragma once
+#include "common.cuh"
+#include "gemm_w8a16.h"
+
+#include <cstdint>
+
+namespace hrm {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kDqWarps = 8;
+constexpr int kEpiWarps = 4;
+constexpr int kFirstDqWarp = 2;
+constexpr int kFirstEpiWarp = kFirstDqWarp + kDqWarps;
+constexpr int kMma2Warp = kFirstEpiWarp + kEpiWarps;         // second MMA issuer (warp 14)
+constexpr int kThreads = (kMma2Warp + 1) * 32;               // 480
+constexpr int kDqThreads = kDqWarps * 32;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kWrawBytes = kBM * kBK;          // int8 tile, 8 KB
+constexpr int kW16Bytes = kBM * kBK * 2;       // f16 tile, 16 KB
+constexpr int kChunk = 16;                     // epilogue columns per TMEM load
+
+// Pipeline shape per token-tile width BN.
+//  TS (BN <= 128, decode): dequantised A tiles go to tensor memory and the MMA reads A from TMEM; one dequant group
+//    of 8 warps converts each unit (thread = weight row = TMEM lane; the two warps of a lane quarter take alternate
+//    k-tiles of the unit).  Shared memory then carries 2 bytes per weight byte (bulk-copy
+//    write + one conflict-free read) instead of 6.
+//  SS (BN = 256, prefill): A tiles in shared memory (F stages of 16 KB, 128-byte swizzle); 4 dequant groups of
+//    2 warps.  Here the MMA time per tile hides the extra shared-memory traffic.
+// KU: 64-wide k-tiles per pipeline unit.  At decode widths every per-unit step (barrier waits, commits, TMA issue)
+// costs hundreds of cycles, so units of KU k-tiles (KU x 8 KB of weights, KU x 4 MMAs) amortise them; the launcher
+// picks ku = KU, or 2 / 1 when K/64 is not a multiple of KU.
+// RW: raw weight ring (units), released by its dequant group once the unit is in registers.  RX: activation ring
+// (units), released by the MMA.  F: A stages (units).  RW and F are multiples of the group count, so every slot of
+// those rings is always consumed by the same group, in order: no waiter can ever mistake a phase two generations
+// old for the one it waits for.
+// NACC: MMA-issuing warps.  A single thread issuing one unit's small-N MMAs and then its commits and barrier waits
+// leaves the tensor core idle during the bookkeeping; with two issuers (warps 1 and 14) taking alternate units, one
+// issues while the other does its bookkeeping.  Each issuer accumulates into its own partial accumulator; the
+// epilogue sums the partials that the segment wrote.
+template <int BN> struct GemmCfg;
+template <> struct GemmCfg<16>  { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 4, RX = 8, F = 3, NACC = 2; };
+template <> struct GemmCfg<32>  { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 4, RX = 4, F = 3, NACC = 2; };
+template <> struct GemmCfg<64>  { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 4, RX = 2, F = 2, NACC = 2; };
+template <> struct GemmCfg<128> { static constexpr bool TS = true;  static constexpr int KU = 4, RW = 2, RX = 2, F = 2, NACC = 1; };
+template <> struct GemmCfg<256> { static constexpr bool TS = false; static constexpr int KU = 1, RW = 4, RX = 3, F = 4, NACC = 1; };
+
+template <int BN>
+struct GemmSmem {
+  static constexpr bool TS = GemmCfg<BN>::TS;
+  static constexpr int KU = GemmCfg<BN>::KU;
+  static constexpr int RW = GemmCfg<BN>::RW, RX = GemmCfg<BN>::RX, F = GemmCfg<BN>::F;
+  static constexpr int NACC = GemmCfg<BN>::NACC;
+  static constexpr int kAccCols = NACC * BN;                            // one accumulator buffer (NACC partials)
+  static constexpr int NG = TS ? 1 : 4;                                // dequant groups
+  static constexpr int kGroupThreads = kDqThreads / NG;
+  static constexpr int kXSub = BN * kBK * 2;                           // one k-tile of activations
+  static constexpr int kXSlot = KU * kXSub;
+  static constexpr int kWSlot = KU * kWrawBytes;
+  static constexpr int kW16Off = 0;                                    // SS only: F x 16 KB
+  static constexpr int kXOff = kW16Off + (TS ? 0 : F * kW16Bytes);
+  static constexpr int kWrawOff = kXOff + RX * kXSlot;
+  static constexpr int kStageOff = kWrawOff + RW * kWSlot;             // [16 cols][128 rows] fp32 = 8 KB
+  static constexpr int kInvOff = kStageOff + kChunk * kBM * 4;         // [BN] per-token input row scale
+  static constexpr int kSsqOff = kInvOff + BN * 4;                     // [4 warps][16] partial sums of squares
+  static constexpr int kBarOff = kSsqOff + kEpiWarps * kChunk * 4;
+  static constexpr int kNumBars = 2 * RW + 2 * RX + 2 * F + 5;
+  static constexpr int kBytes = kBarOff + kNumBars * 8 + 32;
+  static constexpr int kAlloc = kBytes + 1024;
+  static constexpr int kAcol = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;  // first TMEM column of the A stages (TS)
+  static constexpr int kAStageCols = KU * 32;
+  static constexpr int kTmemCols = 512;
+  static_assert(kAlloc <= 227 * 1024, "shared memory budget exceeded");
+  static_assert(RW % NG == 0 && F % NG == 0, "ring depths must be multiples of the dequant group count");
+  static_assert(!TS || kAcol + F * kAStageCols <= kTmemCols, "TMEM budget exceeded");
+  static_assert(TS || (2 * kAccCols <= kTmemCols && KU == 1), "SS path: TMEM budget / unit size");
+  static_assert(NACC == 1 || NACC == 2, "one or two MMA issuers");
+};
+
+// Pipeline trace for performance analysis: clock64 of CTA 0 at each stage of unit i (points listed at the call
+// sites: 0 load issued, 1 raw tile landed, 2 A stage free, 3 dequant done, 4 MMA operands ready, 5/6 epilogue
+// start/end of segment i, 7 kernel start/end).  Off (a.trace == nullptr) in normal launches.
+HRM_DEVINL void trace_mark(const GemmArgs& a, int point, int64_t i) {
+  if (a.trace != nullptr && blockIdx.x == 0 && i < kGemmTraceLen) a.trace[point * kGemmTraceLen + i] = clock64();
+}
+// Per-CTA %globaltimer stamps (rows 8..11: CTA start, first weight unit landed, mainloop done, CTA end).
+HRM_DEVINL void trace_cta(const GemmArgs& a, int row) {
+  if (a.trace != nullptr && blockIdx.x < kGemmTraceLen) a.trace[row * kGemmTraceLen + blockIdx.x] = (long long)global_ns();
+}
+
+// 16 accumulator columns summed over the partial accumulators whose bit is set in `valid` (all are loaded, so the
+// warp-collective loads stay uniform; one wait).
+template <int BN, int NACC>
+HRM_DEVINL void tmem_ld_acc(uint32_t taddr, float (&v)[16], uint32_t valid) {
+  if constexpr (NACC == 1) {
+    tmem_ld16(taddr, v);
+  } else {
+    uint32_t r[NACC][16];
+#pragma unroll
+    for (int j = 0; j < NACC; ++j)
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+          : "=r"(r[j][0]), "=r"(r[j][1]), "=r"(r[j][2]), "=r"(r[j][3]), "=r"(r[j][4]), "=r"(r[j][5]),
+            "=r"(r[j][6]), "=r"(r[j][7]), "=r"(r[j][8]), "=r"(r[j][9]), "=r"(r[j][10]), "=r"(r[j][11]),
+            "=r"(r[j][12]), "=r"(r[j][13]), "=r"(r[j][14]), "=r"(r[j][15])
+          : "r"(taddr + (uint32_t)(j * BN)));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < NACC; ++j)
+        if (valid & (1u << j)) acc += __uint_as_float(r[j][i]);
+      v[i] = acc;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ stream-K partition helpers (device + host)
+HRM_DEVINL int64_t unit_start(int64_t c, int64_t U, int64_t G) { return (c * U) / G; }
+HRM_DEVINL int owner_of(int64_t x, int64_t U, int64_t G) { return (int)(((x + 1) * G - 1) / U); }
+
+// Per-token input row scale (RMSNorm folded into the consumer GEMM): inv[j] for the tile's BN tokens.
+template <int BN>
+HRM_DEVINL void compute_row_scale(const GemmArgs& a, int m_tile, float* inv, int et) {
+  asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");   // previous tile's readers are done with inv
+  for (int j = et; j < BN; j += kEpiThreads) {
+    const int m = m_tile * BN + j;
+    float s = 0.f;
+    if (m < a.M)
+      for (int t = 0; t < a.in_ssq_tiles; ++t) s += a.in_ssq[(size_t)t * a.M + m];
+    inv[j] = rsqrtf(s * a.in_inv_h + a.in_eps);
+  }
+  asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+}
+
+// ------------------------------------------------------------------ peer-memory (NVLink) flags for EPI_RESID_AR
+HRM_DEVINL void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+HRM_DEVINL int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait for a peer flag to reach `want` (epochs only grow).  Records kErrTimeoutPeer on timeout.
+HRM_DEVINL bool wait_peer_flag(const int* p, int want, int* status) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (ld_acquire_sys(p) - want >= 0) return true;
+    if ((i & 63u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+      record_error(status, kErrTimeoutPeer);
+      return false;
+    }
+  }
+}
+
+// x_new of 16 tokens for this thread's row -> residual, xg = x * gamma_next, per-tile sums of squares.
+template <int BN>
+HRM_DEVINL void store_residual_outputs(const GemmArgs& a, int n_tile, int m_tile, int row, int c0,
+                                       const float (&xn)[kChunk], int et, float* ssq_red) {
+  const int n = n_tile * kBM + row;
+  const float gn = (a.gamma_next != nullptr && n < a.N) ? a.gamma_next[n] : 0.f;
+  float sq[kChunk];
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) {
+    const int m = m_tile * BN + c0 + j;
+    const bool ok = m < a.M && n < a.N;
+    if (ok) {
+      a.resid[(size_t)m * a.ldr + n] = xn[j];
+      if (a.xg_out != nullptr) a.xg_out[(size_t)m * a.ldxg + n] = __float2half_rn(xn[j] * gn);
+    }
+    sq[j] = ok ? xn[j] * xn[j] : 0.f;
+  }
+  if (a.ssq_out != nullptr) {
+    const int w = et >> 5, lane = et & 31;
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      const float s = warp_sum(sq[j]);
+      if (lane == 0) ssq_red[w * kChunk + j] = s;
+    }
+    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+    if (et < kChunk) {
+      const int m = m_tile * BN + c0 + et;
+      const float s = ssq_red[et] + ssq_red[kChunk + et] + ssq_red[2 * kChunk + et] + ssq_red[3 * kChunk + et];
+      if (m < a.M) a.ssq_out[(size_t)n_tile * a.M + m] = s;
+    }
+    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+  }
+}
+
+// Tensor-parallel residual epilogue: one-shot all-reduce by peer-memory PUSH over NVLink (decode, one m tile).
+// Receive area of every rank: [launch parity][source rank][tile][128 rows][max_bn tokens] fp32 (double-buffered by
+// launch parity: a slow peer may still be reading the previous launch's data).
+// Phase 1 (per finished tile, in the overlapped epilogue): the tile's partial is stored into the source-rank slot of
+// EVERY rank's receive area (posted NVLink writes: no round trip on the critical path).
+// Phase 2 (once per CTA, after the mainloop): the CTAs of this rank meet at a grid-wide ticket; the last one fences
+// and writes this rank's epoch into every rank's flag array.  Each CTA waits on its LOCAL flags, then reduces its
+// share of the tiles from local memory: x = resid + sum over source ranks in rank order, so every rank computes
+// bit-identical x / xg / ssq.  One flag hop per launch; every load is local.
+HRM_DEVINL float* ar_slot(const GemmArgs& a, int dst, int src, int par, int tile) {
+  float* base = reinterpret_cast<float*>(reinterpret_cast<char*>(a.peers[dst]) + a.off_partials);
+  return base + (((size_t)par * a.tp_world + src) * a.ar_max_tiles + tile) * a.ar_tile_floats;
+}
+
+template <int BN>
+HRM_DEVINL void ar_oneshot(const GemmArgs& a, int row, int et, int ep, float* ssq_red) {
+  int* my_flags = reinterpret_cast<int*>(reinterpret_cast<char*>(a.peers[a.tp_rank]) + a.off_flags);
+  __threadfence_system();   // this thread's pushed partials are visible system-wide before the ticket
+  asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+  if (et == 0) {
+    if (atomicAdd(&a.launch_ticket[0], 1) == (int)gridDim.x - 1) {
+      a.launch_ticket[0] = 0;   // re-arm for the next launch (every CTA has arrived)
+      __threadfence_system();
+      for (int r = 0; r < a.tp_world; ++r)
+        st_release_sys(reinterpret_cast<int*>(reinterpret_cast<char*>(a.peers[r]) + a.off_flags) + a.tp_rank, ep);
+    }
+  }
+  if (et < a.tp_world) wait_peer_flag(my_flags + et, ep, a.status);
+  asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+  const int par = ep & 1;
+  const int stride = a.ar_tile_floats / kBM;   // tokens per row slot (max_bn)
+  for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+    const int n = t * kBM + row;
+    for (int c0 = 0; c0 < BN && c0 < a.M; c0 += kChunk) {
+      float sum[kChunk];
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) sum[j] = 0.f;
+      for (int src = 0; src < a.tp_world; ++src) {
+        const float4* p = reinterpret_cast<const float4*>(ar_slot(a, a.tp_rank, src, par, t) + (size_t)row * stride + c0);
+#pragma unroll
+        for (int q = 0; q < kChunk / 4; ++q) {
+          const float4 v = __ldcg(p + q);
+          sum[4 * q] += v.x; sum[4 * q + 1] += v.y; sum[4 * q + 2] += v.z; sum[4 * q + 3] += v.w;
+        }
+      }
+      float xn[kChunk];
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        const int m = c0 + j;
+        xn[j] = (m < a.M && n < a.N) ? a.resid[(size_t)m * a.ldr + n] + sum[j] : 0.f;
+      }
+      store_residual_outputs<BN>(a, t, 0, row, c0, xn, et, ssq_red);
+    }
+  }
+}
+
+template <int BN, int EPI>
+HRM_DEVINL void epilogue_store(const GemmArgs& a, int n_tile, int m_tile, int row, int c0, const float (&v0)[kChunk],
+                               float* stage, int et, const float* inv, float* ssq_red) {
+  const int n = n_tile * kBM + row;
+  const float sc = (n < a.N) ? a.scale[n] : 0.f;
+  const float bi = (a.bias != nullptr && n < a.N) ? a.bias[n] : 0.f;
+  float v[kChunk];
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) v[j] = a.in_ssq != nullptr ? v0[j] * inv[c0 + j] : v0[j];
+  if constexpr (EPI == EPI_SWIGLU || EPI == EPI_QKV) {
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) stage[j * kBM + row] = v[j] * sc + bi;
+    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+    if constexpr (EPI == EPI_SWIGLU) {
+      // rows [0,64) are gate rows, [64,128) the matching up rows; output column n_tile*64 + i
+      for (int idx = et; idx < kChunk * 64; idx += kEpiThreads) {
+        const int j = idx >> 6, i = idx & 63;
+        const int m = m_tile * BN + c0 + j;
+        const int oc = n_tile * 64 + i;
+        if (m < a.M && oc * 2 < a.N) {
+          const float g = stage[j * kBM + i];
+          const float u = stage[j * kBM + 64 + i];
+          reinterpret_cast<__half*>(a.out)[(size_t)m * a.ldo + oc] = __float2half_rn(silu(g) * u);
+        }
+      }
+    } else {
+      const int D = a.head_dim, halfD = D >> 1;
+      for (int idx = et; idx < kChunk * kBM; idx += kEpiThreads) {
+        const int j = idx >> 7, rr = idx & (kBM - 1);
+        const int m = m_tile * BN + c0 + j;
+        const int gn = n_tile * kBM + rr;
+        if (m >= a.M || gn >= a.N) continue;
+        const int d = gn % D;
+        const float* srow = stage + j * kBM;
+        float y;
+        if (gn < a.q_rows + a.kv_rows) {
+          const int pos = a.positions[m];
+          const int dd = d < halfD ? d : d - halfD;
+          const float c = a.cos_t[(size_t)pos * halfD + dd];
+          const float s = a.sin_t[(size_t)pos * halfD + dd];
+          y = d < halfD ? srow[rr] * c - srow[rr + halfD] * s : srow[rr - halfD] * s + srow[rr] * c;
+        } else {
+          y = srow[rr];
+        }
+        if (gn < a.q_rows) {
+          a.q_out[(size_t)m * a.q_rows + gn] = __float2bfloat16_rn(y);
+        } else {
+          const int slot = a.slots[m];
+          if (slot < 0) continue;
+          const bool is_k = gn < a.q_rows + a.kv_rows;
+          const int kvh = (gn - a.q_rows - (is_k ? 0 : a.kv_rows)) / D;
+          const int blk = slot / a.block_size, off = slot - blk * a.block_size;
+          __nv_bfloat16* cache = is_k ? a.k_cache : a.v_cache;
+          cache[(((size_t)blk * a.kv_heads + kvh) * a.block_size + off) * D + d] = __float2bfloat16_rn(y);
+        }
+      }
+    }
+    asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+  } else if constexpr (EPI == EPI_RESID) {
+    float xn[kChunk];
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      const int m = m_tile * BN + c0 + j;
+      xn[j] = (m < a.M && n < a.N) ? a.resid[(size_t)m * a.ldr + n] + (v[j] * sc + bi) : 0.f;
+    }
+    store_residual_outputs<BN>(a, n_tile, m_tile, row, c0, xn, et, ssq_red);
+  } else if constexpr (EPI == EPI_RESID_AR) {
+    // this rank's partial tile -> its symmetric buffer ([token][128 rows], one slot per n tile)
+    // push this rank's partial (16 tokens of this thread's row) into every rank's receive slot for this rank
+    const int ep = *reinterpret_cast<const volatile int*>(a.epoch) + 1 + a.ep_offset;
+    const int stride = a.ar_tile_floats / kBM;
+    float4 q[kChunk / 4];
+#pragma unroll
+    for (int i = 0; i < kChunk / 4; ++i) q[i] = make_float4(v[4 * i] * sc, v[4 * i + 1] * sc, v[4 * i + 2] * sc, v[4 * i + 3] * sc);
+    for (int dst = 0; dst < a.tp_world; ++dst) {
+      float4* p = reinterpret_cast<float4*>(ar_slot(a, dst, a.tp_rank, ep & 1, n_tile) + (size_t)row * stride + c0);
+#pragma unroll
+      for (int i = 0; i < kChunk / 4; ++i) p[i] = q[i];
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      const int m = m_tile * BN + c0 + j;
+      if (m < a.M && n < a.N) {
+        const float y = v[j] * sc + bi;
+        if constexpr (EPI == EPI_F16) {
+          reinterpret_cast<__half*>(a.out)[(size_t)m * a.ldo + n] = __float2half_rn(y);
+        } else {
+          reinterpret_cast<float*>(a.out)[(size_t)m * a.ldo + n] = y;
+        }
+      }
+    }
+  }
+}
+
+
+// ------------------------------------------------------------------ host helpers shared by the launchers
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn tmap_encode_fn();
+int gemm_pick_bn(int M);
+inline int owner_host(int64_t x, int64_t U, int64_t G) { return (int)(((x + 1) * G - 1) / U); }
+
+}  // namespace hrm
