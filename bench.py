@@ -42,7 +42,9 @@ def _args():
     ap.add_argument("--baseline-comm", action="store_true",
                     help="NCCL all-reduce after the row-parallel GEMMs instead of the fused in-kernel all-reduce")
     ap.add_argument("--chain", action="store_true",
-                    help="TP=1 decode: o_proj, gate/up, down and the next QKV as one multi-phase GEMM launch")
+                    help="decode: o_proj, gate/up, down and the next QKV as one multi-phase GEMM launch")
+    ap.add_argument("--prefill-overlap", type=int, default=1,
+                    help="TP prefill: pipeline each row-parallel GEMM with its all-reduce over N row chunks")
     return ap.parse_args()
 
 
@@ -137,7 +139,8 @@ def run_ours(a):
     _log(rank, f"synthesized {cfg.name} shard in {t_synth:.1f}s ({model.weight_bytes() / 1e9:.1f} GB int8)")
     total_len = a.ctx + a.steps + a.warmup + 2 * 16 + (a.steps + 8 if not a.no_e2e else 0)
     ecfg = EngineConfig(tp=world, max_seq_len=total_len + 16, max_batch=a.batch, prefill_chunk=4096,
-                        graph_batch_buckets=(a.batch,), chain_layers=bool(a.chain))
+                        graph_batch_buckets=(a.batch,), chain_layers=bool(a.chain),
+                        prefill_overlap_chunks=int(a.prefill_overlap))
     eng = InferenceEngine(model, ecfg, num_blocks=a.batch * ((total_len + 15) // 16 + 1))
     prompts = _prompts(a.batch, a.ctx, cfg.vocab)
     sids = [eng.new_seq() for _ in prompts]

@@ -205,7 +205,8 @@ class EngineConfig:
     graph_batch_buckets: Sequence[int] = field(default_factory=lambda: (1, 2, 4, 8, 16, 32, 64))
     fused_collectives: bool = True       # False -> NCCL all-reduce after the local GEMM (baseline path)
     sequence_parallel: bool = False      # prefill with a token-sharded residual stream (TP > 1)
-    chain_layers: bool = False           # decode (TP = 1): o_proj..next QKV as one multi-phase GEMM launch
+    chain_layers: bool = False           # decode: o_proj..next QKV as one multi-phase GEMM launch
+    prefill_overlap_chunks: int = 1      # TP prefill (NCCL path): row-parallel GEMM / all-reduce pipelined in chunks
     seed: int = 0
 
 

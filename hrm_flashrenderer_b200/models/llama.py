@@ -114,6 +114,8 @@ class LlamaW8:
         self.symm = None   # SymmetricWorkspace: enables the fused GEMM + all-reduce kernels when TP > 1
         self.sequence_parallel = False   # prefill: token-sharded residual between blocks (TP > 1)
         self.chain_layers = False        # decode: o_proj, gate/up, down, next QKV in one multi-phase GEMM launch
+        self.prefill_overlap_chunks = 1  # TP prefill: row-parallel GEMM + all-reduce pipelined over this many chunks
+        self.prefill_comm_sms = 8        # SMs the pipelined GEMM leaves free for the collective's kernels
 
     def enable_fused_collectives(self, group=None) -> None:
         """Allocate / exchange the NVLink symmetric buffers (collective over the TP group)."""
@@ -293,8 +295,7 @@ class LlamaW8:
             if fused:
                 ops.w8a16_residual_ar_(a2, L.w_o, L.s_o, x, self.symm, L.ln2, xg, ssq)
             elif tp:
-                ops.w8a16_linear_out(a2, L.w_o, L.s_o, partial)
-                self.comm.all_reduce_(partial)
+                self._row_parallel(a2, L.w_o, L.s_o, partial)
                 ops.norm_prep(x, partial, L.ln2, xg, ssq)
             else:
                 ops.w8a16_residual_(a2, L.w_o, L.s_o, x, gamma_next=L.ln2, xg_out=xg, ssq_out=ssq)
@@ -303,8 +304,7 @@ class LlamaW8:
             if fused:
                 ops.w8a16_residual_ar_(act, L.w_d, L.s_d, x, self.symm, g_next, xg, ssq)
             elif tp:
-                ops.w8a16_linear_out(act, L.w_d, L.s_d, partial)
-                self.comm.all_reduce_(partial)
+                self._row_parallel(act, L.w_d, L.s_d, partial)
                 ops.norm_prep(x, partial, g_next, xg, ssq)
             else:
                 ops.w8a16_residual_(act, L.w_d, L.s_d, x, gamma_next=g_next, xg_out=xg, ssq_out=ssq)
@@ -321,6 +321,30 @@ class LlamaW8:
             from ..parallel.dist import unpack_argmax
             return unpack_argmax(keys)
         return ops.argmax_rows(logits, 0)
+
+    def _row_parallel(self, a: torch.Tensor, w: torch.Tensor, s: torch.Tensor, partial: torch.Tensor) -> None:
+        """``partial = all_reduce(a @ W^T)`` for a row-parallel projection (NCCL path).  With
+        ``prefill_overlap_chunks = n > 1`` and enough rows, the rows are cut into n chunks: chunk i's all-reduce runs
+        on the collective's stream while chunk i + 1's GEMM runs, on all SMs but ``prefill_comm_sms`` so the
+        collective's kernels are resident alongside it.  Row chunks do not change any row's result."""
+        n = int(self.prefill_overlap_chunks)
+        T = a.shape[0]
+        if n <= 1 or T < 64 * n:
+            ops.w8a16_linear_out(a, w, s, partial)
+            self.comm.all_reduce_(partial)
+            return
+        ctas = 0
+        if a.is_cuda:
+            ctas = max(1, ops.ext().sm_count() - int(self.prefill_comm_sms))
+        step = (T + n - 1) // n
+        works = []
+        for r0 in range(0, T, step):
+            r1 = min(T, r0 + step)
+            ops.w8a16_linear_out(a[r0:r1], w, s, partial[r0:r1], force_ctas=ctas)
+            works.append(self.comm.all_reduce_async_(partial[r0:r1]))
+        for wk in works:
+            if wk is not None:
+                wk.wait()
 
     @torch.no_grad()
     def _forward_sp(self, b: BatchMeta) -> torch.Tensor:

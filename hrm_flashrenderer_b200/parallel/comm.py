@@ -22,6 +22,13 @@ class TPComm:
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
         return t
 
+    def all_reduce_async_(self, t: torch.Tensor):
+        """Start an in-place SUM all-reduce; returns the work handle (``wait()`` makes the current stream wait for
+        it without blocking the host), or None when there is nothing to reduce."""
+        if self.world > 1:
+            return dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+        return None
+
     def all_reduce_max_(self, t: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)

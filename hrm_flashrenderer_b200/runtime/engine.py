@@ -53,6 +53,7 @@ class InferenceEngine:
         model.alloc_kv(int(nb), bs)
         model.sequence_parallel = bool(self.ecfg.sequence_parallel)
         model.chain_layers = bool(self.ecfg.chain_layers)
+        model.prefill_overlap_chunks = int(self.ecfg.prefill_overlap_chunks)
         self.bm = BlockManager(int(nb), bs)
         self._graphs: Dict[int, _DecodeGraph] = {}
         self._next_seq = 0

@@ -28,7 +28,7 @@ def _prompts():
     return [torch.randint(0, 1024, (16,), generator=g).tolist() for _ in range(2)]
 
 
-def _run(rank, world, port, q, sp=False, prompts=None):
+def _run(rank, world, port, q, sp=False, prompts=None, overlap=1):
     from hrm_flashrenderer_b200.parallel.dist import init_dist, destroy
     from hrm_flashrenderer_b200.parallel.comm import TPComm
     from hrm_flashrenderer_b200.models.llama import LlamaW8
@@ -38,19 +38,20 @@ def _run(rank, world, port, q, sp=False, prompts=None):
     try:
         w = synth_weights(TINY, seed=0)
         model = LlamaW8.from_weights(TINY, w, rank=rank, world=world, device="cpu", comm=TPComm(), max_pos=256)
-        eng = InferenceEngine(model, EngineConfig(max_seq_len=64, max_batch=4, use_cuda_graphs=False,
-                                                  sequence_parallel=sp), num_blocks=16)
+        eng = InferenceEngine(model, EngineConfig(max_seq_len=160, max_batch=4, use_cuda_graphs=False,
+                                                  sequence_parallel=sp, prefill_overlap_chunks=overlap),
+                              num_blocks=48)
         out = eng.generate(prompts or _prompts(), 32, stop_on_eos=False)
         q.put((rank, out))
     finally:
         destroy()
 
 
-def _spawn(world, sp=False, prompts=None):
+def _spawn(world, sp=False, prompts=None, overlap=1):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_run, args=(r, world, port, q, sp, prompts)) for r in range(world)]
+    ps = [ctx.Process(target=_run, args=(r, world, port, q, sp, prompts, overlap)) for r in range(world)]
     for p in ps:
         p.start()
     res = {}
@@ -91,3 +92,10 @@ def test_tp2_sequence_parallel_odd_rows():
     g = torch.Generator().manual_seed(5)
     prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (7, 11, 5)]
     assert _spawn(2, sp=True, prompts=prompts)[0] == _spawn(1, prompts=prompts)[0]
+
+
+def test_tp2_prefill_overlap_chunks_match_tp1():
+    """Row-parallel GEMM + asynchronous all-reduce pipelined over 2 row chunks (2 x 80 = 160 prompt rows)."""
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, 1024, (80,), generator=g).tolist() for _ in range(2)]
+    assert _spawn(2, prompts=prompts, overlap=2)[0] == _spawn(1, prompts=prompts)[0]
