@@ -193,9 +193,10 @@ class InferenceEngine:
             ws.frozen = False
         g.ids.copy_(saved[0]); g.positions.copy_(saved[1]); g.active.copy_(saved[2])
 
-    def load_decode_batch(self, seq_ids: Sequence[int], last_tokens: Sequence[int], reserve: int,
+    def load_decode_batch(self, seq_ids: Sequence[int], last_tokens: Sequence[int], reserve,
                           positions: Optional[Sequence[int]] = None) -> _DecodeGraph:
-        """Stage a decode batch: block tables grown for ``reserve`` more tokens, current tokens and positions.
+        """Stage a decode batch: block tables grown for ``reserve`` more tokens (one count for every sequence, or a
+        per-sequence list), current tokens and positions.
 
         ``positions[i]`` is the absolute position of ``last_tokens[i]`` (default: the prefilled length)."""
         n = len(seq_ids)
@@ -205,9 +206,10 @@ class InferenceEngine:
         pos = torch.zeros(bucket, dtype=torch.int32)
         ids = torch.zeros(bucket, dtype=torch.int64)
         act = torch.zeros(bucket, dtype=torch.int32)
+        res = [int(reserve)] * n if isinstance(reserve, int) else [int(x) for x in reserve]
         for i, (sid, t) in enumerate(zip(seq_ids, last_tokens)):
             L = int(positions[i]) if positions is not None else self.bm.lengths.get(sid, 0)
-            tab = self.bm.grow(sid, min(L + reserve, self.max_blocks * self.block_size))
+            tab = self.bm.grow(sid, min(L + res[i], self.max_blocks * self.block_size))
             tabs[i, :len(tab)] = torch.tensor(tab, dtype=torch.int32)
             pos[i] = L
             ids[i] = int(t)

@@ -146,9 +146,11 @@ class Scheduler:
         eng = self.engine
         while self._waiting and len(self._running) + len(batch) < self.max_batch and used < self.prefill_chunk:
             r = self._waiting[0]
-            need = eng.bm.blocks_needed(-1, len(r.prompt_ids) + r.max_new_tokens)
-            if need > eng.bm.free_blocks - sum(eng.bm.blocks_needed(-1, len(b.prompt_ids) + b.max_new_tokens)
-                                               for b in batch):
+            # a sequence ends up holding prompt + max_new_tokens + 1 positions (see _decode's reservation); the
+            # running ones were grown to that at their first staging, so free blocks are the whole budget
+            need = eng.bm.blocks_needed(-1, len(r.prompt_ids) + r.max_new_tokens + 1)
+            if need > eng.bm.free_blocks - sum(eng.bm.blocks_needed(-1, len(b.prompt_ids) + b.max_new_tokens + 1)
+                                               for b in batch) - self._pending_growth():
                 break
             self._waiting.popleft()
             r.seq_id = eng.new_seq()
@@ -169,11 +171,18 @@ class Scheduler:
                 self._running.append(r)
         return True
 
+    def _pending_growth(self) -> int:
+        """Blocks the running sequences will still take when the batch is next staged (admitted but not yet grown
+        to their full reservation)."""
+        bm = self.engine.bm
+        return sum(bm.blocks_needed(r.seq_id, r._pos + r.max_new_tokens - len(r.tokens) + 1) for r in self._running)
+
     def _decode(self, staged: bool, g) -> tuple:
         eng = self.engine
         if not staged:
+            # each sequence reserves only what it can still generate (admission counted exactly that)
             g = eng.load_decode_batch([r.seq_id for r in self._running], [r.tokens[-1] for r in self._running],
-                                      reserve=max(r.max_new_tokens - len(r.tokens) for r in self._running) + 1,
+                                      reserve=[r.max_new_tokens - len(r.tokens) + 1 for r in self._running],
                                       positions=[r._pos for r in self._running])
         tok = eng.decode_step(g)
         host = tok[:len(self._running)].tolist()

@@ -39,3 +39,24 @@ def test_scheduler_rejects_oversize():
     import pytest
     with pytest.raises(ValueError):
         sched.submit(list(range(250)), 100)
+
+
+def test_scheduler_tight_kv_pool_never_runs_out():
+    """A pool that holds only a few requests at a time: admission waits for blocks instead of over-committing, so
+    every request completes (decode staging reserves each sequence's own remaining length)."""
+    w = synth_weights(TINY, seed=4)
+    m = LlamaW8.from_weights(TINY, w, device="cpu", max_pos=512)
+    eng = InferenceEngine(m, EngineConfig(max_seq_len=256, max_batch=4, prefill_chunk=64, use_cuda_graphs=False,
+                                          graph_batch_buckets=(1, 2, 4)), num_blocks=14)
+    g = torch.Generator().manual_seed(11)
+    reqs = [(torch.randint(0, 1024, (int(torch.randint(5, 40, (1,), generator=g)),), generator=g).tolist(),
+             int(torch.randint(2, 40, (1,), generator=g))) for _ in range(12)]
+    sched = Scheduler(eng).start()
+    try:
+        handles = [sched.submit(p, n, stop_on_eos=False) for p, n in reqs]
+        got = [h.future.result(timeout=300) for h in handles]
+    finally:
+        sched.stop()
+    assert [len(t) for t in got] == [n for _, n in reqs]
+    assert sched.metrics()["completed"] == 12
+    assert eng.bm.free_blocks == 14
