@@ -94,6 +94,9 @@ class Scheduler:
         if len(prompt_ids) + max_new_tokens > limit:
             raise ValueError(f"prompt ({len(prompt_ids)}) + max_new_tokens ({max_new_tokens}) exceeds the "
                              f"engine's max sequence length {limit}")
+        need = min(self.engine.max_blocks, self.engine.bm.blocks_needed(-1, len(prompt_ids) + max_new_tokens + 1))
+        if need > self.engine.bm.num_blocks:   # could never be admitted: fail now instead of waiting forever
+            raise ValueError(f"request needs {need} KV blocks, the pool has {self.engine.bm.num_blocks}")
         with self._lock:
             rid = self._next_rid
             self._next_rid += 1
@@ -148,9 +151,8 @@ class Scheduler:
             r = self._waiting[0]
             # a sequence ends up holding prompt + max_new_tokens + 1 positions (see _decode's reservation); the
             # running ones were grown to that at their first staging, so free blocks are the whole budget
-            need = eng.bm.blocks_needed(-1, len(r.prompt_ids) + r.max_new_tokens + 1)
-            if need > eng.bm.free_blocks - sum(eng.bm.blocks_needed(-1, len(b.prompt_ids) + b.max_new_tokens + 1)
-                                               for b in batch) - self._pending_growth():
+            full = lambda q: min(eng.max_blocks, eng.bm.blocks_needed(-1, len(q.prompt_ids) + q.max_new_tokens + 1))
+            if full(r) > eng.bm.free_blocks - sum(full(b) for b in batch) - self._pending_growth():
                 break
             self._waiting.popleft()
             r.seq_id = eng.new_seq()

@@ -60,3 +60,12 @@ def test_scheduler_tight_kv_pool_never_runs_out():
     assert [len(t) for t in got] == [n for _, n in reqs]
     assert sched.metrics()["completed"] == 12
     assert eng.bm.free_blocks == 14
+
+
+def test_scheduler_rejects_request_larger_than_pool():
+    import pytest
+    w = synth_weights(TINY, seed=4)
+    m = LlamaW8.from_weights(TINY, w, device="cpu", max_pos=512)
+    eng = InferenceEngine(m, EngineConfig(max_seq_len=256, max_batch=2, use_cuda_graphs=False), num_blocks=4)
+    with pytest.raises(ValueError):
+        Scheduler(eng).submit(list(range(60)), 10)     # 71 positions = 5 blocks > 4
