@@ -92,10 +92,11 @@ class EngineBackend:
                 model = LlamaW8.synthesize(cfg, rank=rank, world=world, device=dev, seed=seed, comm=comm,
                                            max_pos=max_seq_len + 16)
             else:
-                from ..formats.dsi8 import read_dsi8
-                cfg, w = read_dsi8(model_source)
-                model = LlamaW8.from_weights(cfg, w, rank=rank, world=world, device=dev, comm=comm,
-                                             max_pos=max_seq_len + 16)
+                import os
+                model = LlamaW8.from_dsi8(model_source, rank=rank, world=world, device=dev, comm=comm,
+                                          max_pos=max_seq_len + 16,
+                                          cache_dir=os.environ.get("HRM_PACKED_CACHE") or None)
+                cfg = model.cfg
             free, _ = torch.cuda.mem_get_info(dev)
             nb = PagedKVPool.blocks_for_budget(int(free * kv_fraction), cfg.layers, model.plan.local_kv_heads,
                                                cfg.head_dim)
@@ -111,6 +112,11 @@ class EngineBackend:
         return ids
 
     def generate_ids(self, ids: List[int], max_new_tokens: int, timeout_s: float = 180.0) -> List[int]:
+        # fit the context like the reference engine (prompt + output capped at its Tmax): keep the prompt's tail
+        # and at least one new token, then cap the output
+        limit = self.engine.max_blocks * self.engine.block_size
+        ids = list(ids)[-max(1, limit - 1):]
+        max_new_tokens = max(1, min(int(max_new_tokens), limit - len(ids)))
         return self.scheduler.generate(ids, max_new_tokens, timeout=timeout_s)
 
     def generate(self, prompt_text: str, max_new_tokens: int = 256, timeout_s: float = 180.0) -> str:
