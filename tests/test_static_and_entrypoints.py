@@ -29,6 +29,7 @@ def test_every_module_imports():
     "hrm_flashrenderer_b200.serving.daemon", "hrm_flashrenderer_b200.serving.dsi8_ipc",
     "hrm_flashrenderer_b200.launcher.service", "hrm_flashrenderer_b200.launcher.topology",
     "hrm_flashrenderer_b200.launcher.preflight", "hrm_flashrenderer_b200.launcher.e2e",
+    "hrm_flashrenderer_b200.launcher.diag",
     "hrm_flashrenderer_b200.benchmarks.serving", "hrm_flashrenderer_b200.benchmarks.ops_sweep",
     "hrm_flashrenderer_b200.experiments.llm", "hrm_flashrenderer_b200.experiments.bench_cli"])
 def test_entry_point_help(mod, capsys):
@@ -86,3 +87,12 @@ def test_trace_replay_on_cpu_engine():
     finally:
         sch.stop()
     assert res["requests"] == 6 and res["generated_tokens"] == 6 * 4 and res["ttft_p50_ms"] > 0
+
+
+def test_diag_runs_without_gpu(capsys):
+    from hrm_flashrenderer_b200.launcher import diag
+    import torch
+    rep = diag.run(log=lambda s: None)
+    assert rep["cuda_available"] == torch.cuda.is_available()
+    if not rep["cuda_available"]:
+        assert rep["devices"] == [] and rep["failures"] == []
