@@ -71,6 +71,23 @@ hrm::GemmArgs base_args(const at::Tensor& x, const at::Tensor& w, const at::Tens
   return a;
 }
 
+// (n_tile, m_tile, kt) of units [u0, u1) as the GEMM producer walks them, flattened; host-side check of the walk.
+std::vector<int64_t> gemm_tile_walk_py(int64_t n_tiles, int64_t m_tiles, int64_t k_tiles, int64_t u0, int64_t u1,
+                                       bool m_fastest) {
+  if (n_tiles < 1 || m_tiles < 1 || k_tiles < 1 || u0 < 0 || u1 < u0 || u1 > n_tiles * m_tiles * k_tiles)
+    throw std::invalid_argument("gemm_tile_walk: bad tile counts or unit range");
+  hrm::TileWalk wk{(int)n_tiles, (int)m_tiles, (int)k_tiles, m_fastest ? 1 : 0, 0, 0, 0};
+  std::vector<int64_t> out;
+  out.reserve((size_t)(u1 - u0) * 3);
+  wk.start(u0);
+  for (int64_t u = u0; u < u1; ++u, wk.next()) {
+    out.push_back(wk.n_tile);
+    out.push_back(wk.m_tile);
+    out.push_back(wk.kt);
+  }
+  return out;
+}
+
 std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K, int64_t force_ctas) {
   auto p = hrm::gemm_plan((int)M, (int)N, (int)K, (int)force_ctas);
   return {p.bn, p.n_tiles, p.m_tiles, p.k_tiles, p.splits, (int64_t)p.ws_floats, p.counters, p.ku};
@@ -579,6 +596,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("chain_phase_plan", &chain_phase_plan_py, "(bn, ws_floats, counters) of one chain phase on all SMs");
   m.def("set_pdl", &hrm::set_pdl_enabled, "programmatic dependent launch of the decode-path kernels on / off");
   m.def("pdl_enabled", &hrm::pdl_enabled);
+  m.def("set_gemm_m_fastest", &hrm::set_gemm_m_fastest,
+        "m-fastest output-tile numbering for GEMMs with more than one token block on / off");
+  m.def("gemm_m_fastest", &hrm::gemm_m_fastest);
+  m.def("gemm_tile_walk", &gemm_tile_walk_py, "(n_tile, m_tile, kt) per unit of [u0, u1), flattened",
+        py::arg("n_tiles"), py::arg("m_tiles"), py::arg("k_tiles"), py::arg("u0"), py::arg("u1"),
+        py::arg("m_fastest"));
   m.def("set_gemm_trace", [](c10::optional<at::Tensor> t) {
     if (t.has_value() && t->defined()) {
       TORCH_CHECK(t->scalar_type() == at::kLong && t->numel() >= 12 * hrm::kGemmTraceLen, "trace: int64[12*1024]");

@@ -129,21 +129,17 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       // the first RW units' weight tiles go out before waiting for the previous grid (ring slots start free)
       const int64_t pre = (u1 - u0) < RW ? (u1 - u0) : RW;
       {
-        const int tile0 = (int)(u0 / a.k_tiles);
-        int kt = (int)(u0 % a.k_tiles), n_tile = tile0 % a.n_tiles;
-        for (int64_t i = 0; i < pre; ++i) {
+        TileWalk wk{a.n_tiles, a.tiles / a.n_tiles, a.k_tiles, a.m_fastest, 0, 0, 0};
+        wk.start(u0);
+        for (int64_t i = 0; i < pre; ++i, wk.next()) {
           uint8_t* dst = wraw + i * S::kWSlot;
           mbar_arrive_expect_tx(&wfull[i], (uint32_t)(ku * kWrawBytes));
           if (a.w_tiles != nullptr) {
-            bulk_load(dst, a.w_tiles + ((size_t)n_tile * kt_total + (size_t)kt * ku) * kWrawBytes,
+            bulk_load(dst, a.w_tiles + ((size_t)wk.n_tile * kt_total + (size_t)wk.kt * ku) * kWrawBytes,
                       (uint32_t)(ku * kWrawBytes), &wfull[i]);
           } else {
             for (int j = 0; j < ku; ++j)
-              tma_load_2d(dst + j * kWrawBytes, &tmW, &wfull[i], (kt * ku + j) * kBK, n_tile * kBM);
-          }
-          if (++kt == a.k_tiles) {
-            kt = 0;
-            if (++n_tile == a.n_tiles) n_tile = 0;
+              tma_load_2d(dst + j * kWrawBytes, &tmW, &wfull[i], (wk.kt * ku + j) * kBK, wk.n_tile * kBM);
           }
         }
       }
@@ -151,9 +147,8 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       pdl_trigger();
       int64_t nw = pre, nx = 0;   // units issued into each ring
       // (n-tile, m-tile, unit-within-tile) of the current unit, advanced incrementally (no divisions in the loop)
-      const int tile0 = (int)(u0 / a.k_tiles);
-      int kt = (int)(u0 % a.k_tiles);
-      int n_tile = tile0 % a.n_tiles, m_tile = tile0 / a.n_tiles;
+      TileWalk wk{a.n_tiles, a.tiles / a.n_tiles, a.k_tiles, a.m_fastest, 0, 0, 0};
+      wk.start(u0);
       int sw = 0, sx = 0;
       uint32_t pw = 1u, px = 1u;   // producer-side parities of the empty barriers (first pass: free)
       for (int64_t u = u0; u < u1; ++u) {
@@ -164,24 +159,21 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
           mbar_arrive_expect_tx(&wfull[sw], (uint32_t)(ku * kWrawBytes));
           uint8_t* dst = wraw + sw * S::kWSlot;
           if (a.w_tiles != nullptr) {
-            bulk_load(dst, a.w_tiles + ((size_t)n_tile * kt_total + (size_t)kt * ku) * kWrawBytes,
+            bulk_load(dst, a.w_tiles + ((size_t)wk.n_tile * kt_total + (size_t)wk.kt * ku) * kWrawBytes,
                       (uint32_t)(ku * kWrawBytes), &wfull[sw]);
           } else {
             for (int j = 0; j < ku; ++j)
-              tma_load_2d(dst + j * kWrawBytes, &tmW, &wfull[sw], (kt * ku + j) * kBK, n_tile * kBM);
+              tma_load_2d(dst + j * kWrawBytes, &tmW, &wfull[sw], (wk.kt * ku + j) * kBK, wk.n_tile * kBM);
           }
           nw = i + 1;
         }
         if (!mbar_wait_ab(&xempty[sx], px, a.status, kErrTimeoutEmpty, abort_flag)) break;
         mbar_arrive_expect_tx(&xfull[sx], (uint32_t)(ku * S::kXSub));
-        tma_load_3d(xs + sx * S::kXSlot, &tmX, &xfull[sx], 0, m_tile * BN, kt * ku);
+        tma_load_3d(xs + sx * S::kXSlot, &tmX, &xfull[sx], 0, wk.m_tile * BN, wk.kt * ku);
         nx = i + 1;
         if (++sw == RW) { sw = 0; pw ^= 1u; }
         if (++sx == RX) { sx = 0; px ^= 1u; }
-        if (++kt == a.k_tiles) {
-          kt = 0;
-          if (++n_tile == a.n_tiles) { n_tile = 0; ++m_tile; }
-        }
+        wk.next();
       }
       // drain: every issued load must have landed before exit (earlier ones were consumed, hence landed)
       for (int64_t j = (nw > RW ? nw - RW : 0); j < nw; ++j)
@@ -374,7 +366,8 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
       const int64_t tile_end = (int64_t)(tile + 1) * a.k_tiles;
       const int64_t ue = tile_end < u1 ? tile_end : u1;
       const bool whole = ka == 0 && ue == tile_end;
-      const int n_tile = tile % a.n_tiles, m_tile = tile / a.n_tiles;
+      int n_tile, m_tile;
+      TileWalk::coords(tile, a.n_tiles, a.tiles / a.n_tiles, a.m_fastest, n_tile, m_tile);
       const int acc = seg & 1;
       const uint32_t acc_addr = tmem + (uint32_t)(acc * S::kAccCols) + ((uint32_t)(quad * 32) << 16);
       // partials written in this segment: both issuers when it has >= 2 units, else only the owner of its unit
@@ -529,6 +522,18 @@ bool pdl_enabled() {
 }
 void set_pdl_enabled(bool on) { g_pdl = on ? 1 : 0; }
 
+static int g_mfast = -1;   // -1: read HRM_GEMM_MFAST on first use
+
+bool gemm_m_fastest() {
+  if (g_mfast < 0) {
+    const char* e = getenv("HRM_GEMM_MFAST");
+    g_mfast = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  return g_mfast == 1;
+}
+
+void set_gemm_m_fastest(bool on) { g_mfast = on ? 1 : 0; }
+
 int gemm_sm_count() {
   static int sms = 0;
   if (!sms) {
@@ -629,6 +634,7 @@ void gemm_w8a16_launch(const void* x, int ldx, const int8_t* w, int epi, GemmArg
   a.k_tiles = p.k_tiles;
   a.ku = p.ku;
   a.n_tiles = p.n_tiles;
+  a.m_fastest = (p.m_tiles > 1 && epi != EPI_RESID_AR && gemm_m_fastest()) ? 1 : 0;
   a.tiles = p.tiles;
   a.max_seg = p.max_seg;
   switch (epi) {

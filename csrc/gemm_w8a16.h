@@ -17,6 +17,42 @@ enum GemmEpilogue : int {
   EPI_RESID_AR = 5,  // tensor-parallel residual GEMM: partial tiles all-reduced over peer memory, then as EPI_RESID
 };
 
+#if defined(__CUDACC__)
+#define HRM_TILE_HD __host__ __device__ __forceinline__
+#else
+#define HRM_TILE_HD inline
+#endif
+
+// Output-tile numbering of the stream-K GEMM and the walk over consecutive pipeline units
+// (unit = tile * k_tiles + kt).  n-fastest: tile = m_tile * n_tiles + n_tile, so CTAs running side by side hold
+// different weight tiles of one token block (one pass over the weights per token block; the decode default, where
+// there is one token block).  m-fastest: tile = n_tile * m_tiles + m_tile, so a CTA keeps one weight tile for every
+// token block in turn and the weights leave DRAM once (multi-token-block, i.e. prefill, GEMMs).  Shared by the
+// kernel's producer and epilogue and by the host-side test of the walk.
+struct TileWalk {
+  int n_tiles, m_tiles, k_tiles, m_fastest;
+  int n_tile, m_tile, kt;
+  HRM_TILE_HD static void coords(int tile, int n_tiles, int m_tiles, int m_fastest, int& n_tile, int& m_tile) {
+    if (m_fastest) { n_tile = tile / m_tiles; m_tile = tile - n_tile * m_tiles; }
+    else { m_tile = tile / n_tiles; n_tile = tile - m_tile * n_tiles; }
+  }
+  HRM_TILE_HD void start(long long unit) {
+    const int tile = (int)(unit / k_tiles);
+    kt = (int)(unit - (long long)tile * k_tiles);
+    coords(tile, n_tiles, m_tiles, m_fastest, n_tile, m_tile);
+  }
+  HRM_TILE_HD void next() {
+    if (++kt < k_tiles) return;
+    kt = 0;
+    if (m_fastest) {
+      if (++m_tile == m_tiles) { m_tile = 0; ++n_tile; }
+    } else if (++n_tile == n_tiles) {
+      n_tile = 0;
+      ++m_tile;
+    }
+  }
+};
+
 struct GemmArgs {
   int M, N, K;
   int k_tiles, n_tiles, tiles, max_seg;     // filled by the launcher from the plan (k_tiles = units per tile)
@@ -50,6 +86,7 @@ struct GemmArgs {
   int* epoch;                                     // this rank's launch epoch counter (in its symmetric buffer)
   int* launch_ticket;                             // [2] CTA tickets: phase-1 barrier, kernel end (zero between launches)
   int ep_offset;                                  // this all-reduce's epoch = *epoch + 1 + ep_offset (0 unless chained)
+  int m_fastest;                                  // tile numbering: 0 n-fastest, 1 m-fastest (see TileWalk)
   float* ws;                                // stream-K partials: plan.ws_floats floats
   int* counters;                            // stream-K tickets: plan.counters ints, zero before first use
   // EPI_QKV
@@ -105,6 +142,9 @@ void make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int
                   uint64_t outer, uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
                   CUtensorMapSwizzle swz);
 int gemm_sm_count();
+// m-fastest tile numbering for GEMMs with more than one token block (default off; env HRM_GEMM_MFAST=1).
+bool gemm_m_fastest();
+void set_gemm_m_fastest(bool on);
 void set_status_word(int device, int* p);
 // Per-stage timestamps of CTA 0 for every following launch (nullptr switches tracing off).
 void set_gemm_trace(long long* p);

@@ -1,5 +1,6 @@
 """sm_100a kernels vs plain PyTorch fp32 references of the same op (run on a B200 with -m gpu)."""
 import math
+import os
 
 import pytest
 import torch
@@ -52,6 +53,28 @@ def test_w8a16_tiled_weights_bitwise_equal_plain(M, N, K):
     a = ops.w8a16_linear(x, q, s, out_dtype=torch.float32)
     b = ops.w8a16_linear(x, t, s, out_dtype=torch.float32)
     assert torch.equal(a, b)
+
+
+@pytest.mark.skipif(os.environ.get("HRM_TEST_MFAST") != "1", reason="m-fastest tile order: set HRM_TEST_MFAST=1")
+@pytest.mark.parametrize("M,N,K", [(300, 1000, 1024), (4096, 1536, 4096), (257, 384, 512)])
+def test_w8a16_m_fastest_tile_order(M, N, K):
+    """m-fastest tile numbering computes the same product (stream-K split points move, so not bitwise)."""
+    q, s = _qw(N, K, 13)
+    x = _x(M, K, 14)
+    t = ops.tile_w8(q)
+    C = ops.ext()
+    try:
+        C.set_gemm_m_fastest(False)
+        a = ops.w8a16_linear(x, t, s, out_dtype=torch.float32)
+        C.set_gemm_m_fastest(True)
+        b = ops.w8a16_linear(x, t, s, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+    finally:
+        C.set_gemm_m_fastest(False)
+    ops.check_status()
+    torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-3)
+    ref = _ref(x, q, s)
+    assert (b - ref).abs().max().item() <= 1e-3 * max(1.0, ref.abs().max().item())
 
 
 @pytest.mark.parametrize("splits", [1, 2, 3, 7, 37, 148])
