@@ -43,8 +43,10 @@ HRM_DEVINL bool grid_bar_wait(const int* p, int want, int* status, volatile int*
 }
 
 // One phase of the overlapped epilogue (the single-GEMM kernel's epilogue loop over this CTA's segments).
+// `origin`: the unit of this phase whose running index (see run_par in the kernel) is 0 mod NACC.
 template <int BN, int EPI>
-HRM_DEVINL void chain_epi_phase(const GemmArgs& a, int64_t u0, int64_t u1, int64_t U, int64_t G, int& seg,
+HRM_DEVINL void chain_epi_phase(const GemmArgs& a, int64_t u0, int64_t u1, int64_t origin, int64_t U, int64_t G,
+                                int& seg,
                                 uint32_t tmem, uint64_t* afull, uint64_t* aempty, float* stage, float* inv,
                                 float* ssq_red, int* last_flag, volatile int* abort_flag, int et, int quad, int row) {
   using S = GemmSmem<BN>;
@@ -61,7 +63,8 @@ HRM_DEVINL void chain_epi_phase(const GemmArgs& a, int64_t u0, int64_t u1, int64
     const int n_tile = tile % a.n_tiles, m_tile = tile / a.n_tiles;
     const int acc = seg & 1;
     const uint32_t acc_addr = tmem + (uint32_t)(acc * S::kAccCols) + ((uint32_t)(quad * 32) << 16);
-    const uint32_t valid = (S::NACC == 1 || ue - u >= 2) ? ((1u << S::NACC) - 1u) : (1u << ((u - u0) % S::NACC));
+    // a one-unit segment holds only the partial of the issuer that took the unit
+    const uint32_t valid = (S::NACC == 1 || ue - u >= 2) ? ((1u << S::NACC) - 1u) : (1u << ((u - origin) % S::NACC));
     mbar_wait_ab(&afull[acc], (uint32_t)(seg >> 1) & 1u, a.status, kErrChainAFull, abort_flag);
     tc_fence_after();
     if (whole) {
@@ -123,13 +126,14 @@ HRM_DEVINL void chain_epi_phase(const GemmArgs& a, int64_t u0, int64_t u1, int64
 }
 
 template <int BN, int EPI>
-HRM_DEVINL void chain_epi_dispatch(const GemmArgs& a, int64_t u0, int64_t u1, int64_t U, int64_t G, int& seg,
+HRM_DEVINL void chain_epi_dispatch(const GemmArgs& a, int64_t u0, int64_t u1, int64_t origin, int64_t U, int64_t G,
+                                   int& seg,
                                    uint32_t tmem, uint64_t* afull, uint64_t* aempty, float* stage, float* inv,
                                    float* ssq_red, int* last_flag, volatile int* abort_flag, int et, int quad,
                                    int row) {
   if constexpr (EPI >= 0)
-    chain_epi_phase<BN, EPI>(a, u0, u1, U, G, seg, tmem, afull, aempty, stage, inv, ssq_red, last_flag, abort_flag,
-                             et, quad, row);
+    chain_epi_phase<BN, EPI>(a, u0, u1, origin, U, G, seg, tmem, afull, aempty, stage, inv, ssq_red, last_flag,
+                             abort_flag, et, quad, row);
 }
 
 template <int BN, int E0, int E1, int E2, int E3>
@@ -162,6 +166,12 @@ w8a16_chain_kernel(const __grid_constant__ CUtensorMap tx0, const __grid_constan
   int* last_flag = misc + 1;
   volatile int* abort_flag = misc + 2;
   volatile int* bar_ok = misc + 3;   // epilogue: the grid barrier its poller saw
+  // The two MMA issuers take alternate units of the CTA's running unit sequence over all phases, so each issuer's
+  // previous unit is always NACC units back.  (Alternating per phase would let the gap reach NACC + 1, or more across
+  // phases with a single unit: an issuer could then wait on a ring slot whose previous fill - the other issuer's
+  // unit - is still pending, and its parity wait would return on the fill before that.)  run_par[p]: the running
+  // index of this CTA's first unit of phase p, mod NACC.
+  int* run_par = misc + 4;   // [kMaxChainPhases]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -188,6 +198,12 @@ w8a16_chain_kernel(const __grid_constant__ CUtensorMap tx0, const __grid_constan
     mbar_init(mdone, S::NACC);
     *last_flag = 0;
     *abort_flag = 0;
+    int64_t run = 0;
+    for (int p = 0; p < c.nph; ++p) {
+      run_par[p] = (int)(run % S::NACC);
+      const int64_t U = (int64_t)c.ph[p].tiles * c.ph[p].k_tiles;
+      run += unit_start(blockIdx.x + 1, U, (int64_t)gridDim.x) - unit_start(blockIdx.x, U, (int64_t)gridDim.x);
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -264,6 +280,7 @@ w8a16_chain_kernel(const __grid_constant__ CUtensorMap tx0, const __grid_constan
         const int64_t U = (int64_t)a.tiles * a.k_tiles;
         const int64_t u0 = unit_start(blockIdx.x, U, G), u1 = unit_start(blockIdx.x + 1, U, G);
         const int ku = a.ku;
+        const int64_t origin = u0 - run_par[p];   // issuer of unit k: (k - origin) % NACC
         for (int64_t u = u0; ok && u < u1; ++seg) {
           const int tile = (int)(u / a.k_tiles);
           const int64_t tile_end = (int64_t)(tile + 1) * a.k_tiles;
@@ -274,7 +291,7 @@ w8a16_chain_kernel(const __grid_constant__ CUtensorMap tx0, const __grid_constan
           tc_fence_after();
           bool first = true;
           for (int64_t k = u; ok && k < ue; ++k) {
-            if (((k - u0) % S::NACC) != mw) {
+            if (((k - origin) % S::NACC) != mw) {
               if (++sx == RX) { sx = 0; phx ^= 1u; }
               if (++f == F) { f = 0; phf ^= 1u; }
               continue;
@@ -375,18 +392,19 @@ w8a16_chain_kernel(const __grid_constant__ CUtensorMap tx0, const __grid_constan
       }
       const int64_t U = (int64_t)a.tiles * a.k_tiles;
       const int64_t u0 = unit_start(blockIdx.x, U, G), u1 = unit_start(blockIdx.x + 1, U, G);
+      const int64_t origin = u0 - run_par[p];
       if (p == 0)
-        chain_epi_dispatch<BN, E0>(a, u0, u1, U, G, seg, tmem, afull, aempty, stage, inv, ssq_red, last_flag,
-                                   abort_flag, et, quad, row);
+        chain_epi_dispatch<BN, E0>(a, u0, u1, origin, U, G, seg, tmem, afull, aempty, stage, inv, ssq_red,
+                                   last_flag, abort_flag, et, quad, row);
       else if (p == 1)
-        chain_epi_dispatch<BN, E1>(a, u0, u1, U, G, seg, tmem, afull, aempty, stage, inv, ssq_red, last_flag,
-                                   abort_flag, et, quad, row);
+        chain_epi_dispatch<BN, E1>(a, u0, u1, origin, U, G, seg, tmem, afull, aempty, stage, inv, ssq_red,
+                                   last_flag, abort_flag, et, quad, row);
       else if (p == 2)
-        chain_epi_dispatch<BN, E2>(a, u0, u1, U, G, seg, tmem, afull, aempty, stage, inv, ssq_red, last_flag,
-                                   abort_flag, et, quad, row);
+        chain_epi_dispatch<BN, E2>(a, u0, u1, origin, U, G, seg, tmem, afull, aempty, stage, inv, ssq_red,
+                                   last_flag, abort_flag, et, quad, row);
       else
-        chain_epi_dispatch<BN, E3>(a, u0, u1, U, G, seg, tmem, afull, aempty, stage, inv, ssq_red, last_flag,
-                                   abort_flag, et, quad, row);
+        chain_epi_dispatch<BN, E3>(a, u0, u1, origin, U, G, seg, tmem, afull, aempty, stage, inv, ssq_red,
+                                   last_flag, abort_flag, et, quad, row);
       // publish this CTA's phase-p outputs: every epilogue thread fences its own stores, then one arrival
       __threadfence();
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
@@ -477,8 +495,10 @@ static void launch_chain_bn(const CUtensorMap (&tx)[kMaxChainPhases], const Chai
 template <int E0, int E1, int E2, int E3>
 static void launch_chain(int bn, const CUtensorMap (&tx)[kMaxChainPhases], const ChainArgs& c, int G,
                          cudaStream_t s) {
-  // BN = 64 (M 33..64) runs the unfolded activation pipeline (MMA waits the activation ring itself); its first
-  // B200 run timed out on an empty-slot wait, so chains take M <= 32 until that path is fixed.
+  // BN = 64 (M 33..64) runs the unfolded activation pipeline: the MMA issuers wait on the two-deep activation ring
+  // themselves.  Its first B200 run timed out on a ring wait.  The cause was the issuer alternation restarting every
+  // phase (an issuer could wait one fill early on a two-deep ring and pass on the older fill); the alternation now
+  // runs over all phases (run_par).  Chains stay at M <= 32 until BN = 64 has run on a B200 again.
   switch (bn) {
     case 16: launch_chain_bn<16, E0, E1, E2, E3>(tx, c, G, s); break;
     case 32: launch_chain_bn<32, E0, E1, E2, E3>(tx, c, G, s); break;
