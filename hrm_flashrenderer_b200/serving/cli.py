@@ -58,7 +58,7 @@ def _generate(args) -> int:
     return 0
 
 
-def main(argv=None) -> int:
+def build_arg_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="hrm-flash", description="HRM FlashRenderer on B200: HRM retrieval + "
                                                                "tensor-parallel int8 inference")
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -91,7 +91,11 @@ def main(argv=None) -> int:
     g.add_argument("--print_prompt", action="store_true")
     g.add_argument("--use_daemon", action="store_true")
     g.add_argument("--device", default="cuda:0")
+    return ap
 
+
+def main(argv=None) -> int:
+    ap = build_arg_parser()
     argv = list(sys.argv[1:] if argv is None else argv)
     if argv and argv[0] in ("daemon", "serve", "router"):
         cmd, rest = argv[0], argv[1:]
