@@ -43,6 +43,9 @@ def _args():
                     help="NCCL all-reduce after the row-parallel GEMMs instead of the fused in-kernel all-reduce")
     ap.add_argument("--chain", action="store_true",
                     help="decode: o_proj, gate/up, down and the next QKV as one multi-phase GEMM launch")
+    ap.add_argument("--embed-vocab-parallel", action="store_true",
+                    help="TP: vocab-sharded embedding + all-reduce (the reference's layout) instead of the table on "
+                         "every rank")
     ap.add_argument("--prefill-overlap", type=int, default=1,
                     help="TP prefill: pipeline each row-parallel GEMM with its all-reduce over N row chunks")
     return ap.parse_args()
@@ -130,7 +133,8 @@ def run_ours(a):
     comm = TPComm() if world > 1 else None
     t0 = time.time()
     model = LlamaW8.synthesize(cfg, rank=rank, world=world, device=dev, seed=0, comm=comm,
-                               max_pos=a.ctx + a.steps + a.warmup + 256)
+                               max_pos=a.ctx + a.steps + a.warmup + 256,
+                               replicate_embedding=not a.embed_vocab_parallel)
     fused = world > 1 and not a.baseline_comm
     if fused:
         model.enable_fused_collectives()   # row-parallel GEMMs reduce over NVLink peer memory inside the kernel
@@ -218,7 +222,9 @@ def run_ours(a):
         "data": "synthetic random-token prompts, random-init N(0,0.02) int8 weights",
         "config": {"model": cfg.name, "global_batch": a.batch, "seq_len": a.ctx, "parallelism": f"tp{world}",
                    "decode_context": f"{a.ctx}..{a.ctx + a.warmup + a.steps}", "l2": "inputs larger than L2",
-                   "comm": ("fused GEMM+all-reduce over peer memory" if fused else "nccl") if world > 1 else "none"},
+                   "comm": ("fused GEMM+all-reduce over peer memory" if fused else "nccl") if world > 1 else "none",
+                   "embedding": ("replicated" if model.embed_replicated else "vocab-parallel") if world > 1
+                   else "full"},
         "p50_ttft_ms": round(ttft_p50, 2), "impl": "ours", "gpu_launches": launches,
         "clocks": clocks, "e2e": e2e, "synth_s": round(t_synth, 1),
     }

@@ -99,6 +99,11 @@ class LlamaW8:
                  head_pretiled: bool = False):
         self.cfg, self.plan, self.layers, self.device = cfg, plan, layers, torch.device(device)
         self.embed_q, self.embed_s = embed.q.contiguous(), embed.scale.contiguous()
+        # The embedding table is either this rank's vocab slice (vocab-parallel: lookup, then a sum over ranks) or
+        # the whole table on every rank (~1 GB int8 for a 128k x 8192 vocab): then the lookup is local and the
+        # collective disappears.  Same rows either way (the non-owners' contributions are exact zeros).
+        self.embed_replicated = plan.world > 1 and self.embed_q.shape[0] == cfg.vocab
+        self.embed_start = 0 if self.embed_q.shape[0] == cfg.vocab else plan.vocab_start
         self.head_q, self.head_s = lm_head.q.contiguous(), lm_head.scale.contiguous()
         if self.head_q.is_cuda and not head_pretiled:
             self.head_q = ops.tile_w8(self.head_q)
@@ -127,7 +132,7 @@ class LlamaW8:
     # ------------------------------------------------------------------ construction
     @classmethod
     def from_dsi8(cls, path: str, rank: int = 0, world: int = 1, device="cuda", comm=None, max_pos: int = 8192,
-                  cache_dir: Optional[str] = None) -> "LlamaW8":
+                  cache_dir: Optional[str] = None, replicate_embedding: bool = True) -> "LlamaW8":
         """Load a DSI8 export for TP rank ``rank`` of ``world``.  With ``cache_dir`` the packed shard (fused QKV,
         interleaved gate/up, GPU tile layout) is kept in a per-rank cache file keyed by the export's fingerprint,
         the TP layout and the packing version, so later starts skip reading, sharding and re-tiling the export."""
@@ -137,26 +142,32 @@ class LlamaW8:
         if cp is not None and cp.is_file():
             return load_packed(cls, cp, device, comm, max_pos)
         cfg, w = read_dsi8(path)
-        model = cls.from_weights(cfg, w, rank=rank, world=world, device=device, comm=comm, max_pos=max_pos)
+        model = cls.from_weights(cfg, w, rank=rank, world=world, device=device, comm=comm, max_pos=max_pos,
+                                 replicate_embedding=replicate_embedding)
         if cp is not None:
             save_packed(model, cp)
         return model
 
     @classmethod
     def from_weights(cls, cfg: ModelConfig, weights: Dict[str, Tensorish], rank: int = 0, world: int = 1,
-                     device="cuda", comm=None, max_pos: int = 8192) -> "LlamaW8":
+                     device="cuda", comm=None, max_pos: int = 8192, replicate_embedding: bool = True) -> "LlamaW8":
+        """``replicate_embedding`` (TP > 1): every rank keeps the whole embedding table, so the lookup needs no
+        collective; False keeps the reference's vocab-parallel embedding (``tp/vocab_parallel.py:9-57``)."""
         from .weights import shard_weights
         plan = shard_plan(cfg, rank, world)
         w = shard_weights(cfg, weights, rank, world) if world > 1 else dict(weights)
         if world == 1:
             w[LM_HEAD] = get_lm_head(cfg, weights)
+        elif replicate_embedding:
+            w[EMBED] = weights[EMBED]
         layers = [pack_layer(cfg, w, l, device) for l in range(cfg.layers)]
         return cls(cfg, plan, layers, w[EMBED].to(device), w[LM_HEAD].to(device),
                    w[FINAL_NORM].to(device, torch.float32), device, comm, max_pos)
 
     @classmethod
     def synthesize(cls, cfg: ModelConfig, rank: int = 0, world: int = 1, device="cuda", seed: int = 0,
-                   comm=None, max_pos: int = 8192, norm_jitter: float = 0.0) -> "LlamaW8":
+                   comm=None, max_pos: int = 8192, norm_jitter: float = 0.0,
+                   replicate_embedding: bool = True) -> "LlamaW8":
         """Random-init int8 weights generated directly on the device, layer by layer (70B never exists in fp32).
 
         Matrix ``i`` (DSI8 record order) draws from a generator seeded ``seed*1000003 + i`` exactly like
@@ -202,7 +213,9 @@ class LlamaW8:
         emb = mat(EMBED)
         head = emb if cfg.tie_embeddings else mat(LM_HEAD)
         v0, v1 = plan.vocab_start, plan.vocab_start + plan.vocab_per_rank
-        emb, head = emb.rows(v0, v1).contiguous(), head.rows(v0, v1).contiguous()
+        head = head.rows(v0, v1).contiguous()
+        if not replicate_embedding:
+            emb = emb.rows(v0, v1).contiguous()
         return cls(cfg, plan, layers, emb, head, vec[FINAL_NORM].to(dev), dev, comm, max_pos)
 
     def weight_bytes(self) -> int:
@@ -241,8 +254,8 @@ class LlamaW8:
         tp = p.world > 1
         dev = self.device
         cuda = dev.type == "cuda"
-        x = ops.embedding_q8(b.ids, self.embed_q, self.embed_s, p.vocab_start)
-        if tp:
+        x = ops.embedding_q8(b.ids, self.embed_q, self.embed_s, self.embed_start)
+        if tp and not self.embed_replicated:
             self.comm.all_reduce_(x)
         xg = torch.empty(T, H, dtype=torch.float16 if cuda else torch.float32, device=dev)
         ssq = torch.empty(H // 128, T, dtype=torch.float32, device=dev)
@@ -368,9 +381,15 @@ class LlamaW8:
         pos[:T] = b.positions
         slots = torch.full((Tp,), -1, dtype=b.slots.dtype, device=dev)
         slots[:T] = b.slots
-        emb = torch.zeros(Tp, H, dtype=torch.float32, device=dev)
-        emb[:T] = ops.embedding_q8(b.ids, self.embed_q, self.embed_s, p.vocab_start)
-        x = comm.reduce_scatter_rows(emb)                           # [Ts, H] fp32, this rank's rows
+        if self.embed_replicated:   # this rank's token rows straight from the local table
+            x = torch.zeros(Ts, H, dtype=torch.float32, device=dev)
+            r0, r1 = min(T, p.rank * Ts), min(T, (p.rank + 1) * Ts)
+            if r1 > r0:
+                x[:r1 - r0] = ops.embedding_q8(b.ids[r0:r1], self.embed_q, self.embed_s, 0)
+        else:
+            emb = torch.zeros(Tp, H, dtype=torch.float32, device=dev)
+            emb[:T] = ops.embedding_q8(b.ids, self.embed_q, self.embed_s, self.embed_start)
+            x = comm.reduce_scatter_rows(emb)                       # [Ts, H] fp32, this rank's rows
         xg_s = torch.empty(Ts, H, dtype=fdt, device=dev)
         ssq_s = torch.empty(H // 128, Ts, dtype=torch.float32, device=dev)
         xg = torch.empty(Tp, H, dtype=fdt, device=dev)

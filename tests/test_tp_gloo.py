@@ -28,7 +28,7 @@ def _prompts():
     return [torch.randint(0, 1024, (16,), generator=g).tolist() for _ in range(2)]
 
 
-def _run(rank, world, port, q, sp=False, prompts=None, overlap=1):
+def _run(rank, world, port, q, sp=False, prompts=None, overlap=1, replicate=True):
     from hrm_flashrenderer_b200.parallel.dist import init_dist, destroy
     from hrm_flashrenderer_b200.parallel.comm import TPComm
     from hrm_flashrenderer_b200.models.llama import LlamaW8
@@ -37,31 +37,41 @@ def _run(rank, world, port, q, sp=False, prompts=None, overlap=1):
     init_dist(rank, world, "127.0.0.1", port, backend="gloo", timeout_s=60)
     try:
         w = synth_weights(TINY, seed=0)
-        model = LlamaW8.from_weights(TINY, w, rank=rank, world=world, device="cpu", comm=TPComm(), max_pos=256)
+        comm = TPComm()
+        model = LlamaW8.from_weights(TINY, w, rank=rank, world=world, device="cpu", comm=comm, max_pos=256,
+                                     replicate_embedding=replicate)
+        assert model.embed_replicated == (world > 1 and replicate)
+        calls = {"all_reduce_": 0}
+        inner = comm.all_reduce_
+
+        def counted(t, *a, **k):
+            calls["all_reduce_"] += 1
+            return inner(t, *a, **k)
+        comm.all_reduce_ = counted
         eng = InferenceEngine(model, EngineConfig(max_seq_len=160, max_batch=4, use_cuda_graphs=False,
                                                   sequence_parallel=sp, prefill_overlap_chunks=overlap),
                               num_blocks=48)
         out = eng.generate(prompts or _prompts(), 32, stop_on_eos=False)
-        q.put((rank, out))
+        q.put((rank, out, calls["all_reduce_"]))
     finally:
         destroy()
 
 
-def _spawn(world, sp=False, prompts=None, overlap=1):
+def _spawn(world, sp=False, prompts=None, overlap=1, replicate=True, with_calls=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_run, args=(r, world, port, q, sp, prompts, overlap)) for r in range(world)]
+    ps = [ctx.Process(target=_run, args=(r, world, port, q, sp, prompts, overlap, replicate)) for r in range(world)]
     for p in ps:
         p.start()
-    res = {}
+    res, calls = {}, {}
     for _ in range(world):
-        r, out = q.get(timeout=300)
-        res[r] = out
+        r, out, n = q.get(timeout=300)
+        res[r], calls[r] = out, n
     for p in ps:
         p.join(timeout=60)
         assert p.exitcode == 0
-    return res
+    return (res, calls) if with_calls else res
 
 
 def test_tp2_matches_tp1_token_for_token():
@@ -99,3 +109,25 @@ def test_tp2_prefill_overlap_chunks_match_tp1():
     g = torch.Generator().manual_seed(9)
     prompts = [torch.randint(0, 1024, (80,), generator=g).tolist() for _ in range(2)]
     assert _spawn(2, prompts=prompts, overlap=2)[0] == _spawn(1, prompts=prompts)[0]
+
+
+def test_tp2_embedding_layouts_match_tp1():
+    """The whole embedding table on every rank (default) and the reference's vocab-parallel table give the TP=1
+    tokens; the replicated table saves one all-reduce per forward (prefill and every decode step)."""
+    tp1 = _spawn(1)[0]
+    rep, n_rep = _spawn(2, with_calls=True)
+    vp, n_vp = _spawn(2, replicate=False, with_calls=True)
+    assert rep[0] == rep[1] == tp1
+    assert vp[0] == vp[1] == tp1
+    forwards = 1 + 31   # one prefill forward (both prompts in one batch) and 31 decode steps
+    assert n_vp[0] - n_rep[0] == forwards, (n_vp, n_rep)
+
+
+def test_tp2_sequence_parallel_vocab_parallel_embedding():
+    """Sequence-parallel prefill with the vocab-parallel table (reduce-scatter of the lookup) and with the
+    replicated table (each rank looks up its own token rows), odd row count."""
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (7, 11, 5)]
+    tp1 = _spawn(1, prompts=prompts)[0]
+    assert _spawn(2, sp=True, prompts=prompts, replicate=False)[0] == tp1
+    assert _spawn(2, sp=True, prompts=prompts)[0] == tp1
