@@ -40,7 +40,12 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self._fh.close()
-        return summarize(open(self.path).read().splitlines(), self.gpus)
+        try:
+            with open(self.path) as f:
+                lines = f.read().splitlines()
+        finally:
+            os.unlink(self.path)
+        return summarize(lines, self.gpus)
 
 
 def visible_gpu_indices(n: int) -> List[int]:
