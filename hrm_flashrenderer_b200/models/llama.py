@@ -18,7 +18,7 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass
-from typing import Dict, List, Optional
+from typing import Dict, List, Optional, Tuple
 
 import torch
 
@@ -249,6 +249,35 @@ class LlamaW8:
         cfg, p = self.cfg, self.plan
         if p.world > 1 and self.sequence_parallel and not b.is_decode:
             return self._forward_sp(b)
+        xg, ssq = self._layers(b)
+        H = cfg.hidden
+        norm = (ssq, H, cfg.rms_eps)
+        if b.is_decode:
+            xl, nl = xg, norm
+        else:
+            xl = xg.index_select(0, b.last_rows)
+            nl = (ssq.index_select(1, b.last_rows).contiguous(), H, cfg.rms_eps)
+        logits = ops.w8a16_linear(xl, self.head_q, self.head_s, out_dtype=torch.float32, in_norm=nl)
+        if p.world > 1:
+            keys = torch.empty(xl.shape[0], dtype=torch.int64, device=self.device)
+            ops.argmax_rows(logits, p.vocab_start, keys=keys)
+            self.comm.all_reduce_max_(keys)
+            from ..parallel.dist import unpack_argmax
+            return unpack_argmax(keys)
+        return ops.argmax_rows(logits, 0)
+
+    @torch.no_grad()
+    def hidden_states(self, b: BatchMeta) -> torch.Tensor:
+        """Final RMS-normalised hidden states of every row, ``[T, H]`` fp32 (the reference model's ``forward``
+        output, ``engine/llama_tp.py:304-311``); the lm_head is left to the caller."""
+        xg, ssq = self._layers(b)
+        inv = torch.rsqrt(ssq.sum(0) / self.cfg.hidden + self.cfg.rms_eps)
+        return xg.float() * inv[:, None]
+
+    def _layers(self, b: BatchMeta) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Embedding and every decoder layer of the batch.  Returns ``xg = x * final_norm`` (the lm_head's operand)
+        and ``ssq [H / 128, T]``, the per-128-column sums of ``x^2`` that give each row's RMS scale."""
+        cfg, p = self.cfg, self.plan
         T = b.ids.shape[0]
         H = cfg.hidden
         tp = p.world > 1
@@ -321,19 +350,7 @@ class LlamaW8:
                 ops.norm_prep(x, partial, g_next, xg, ssq)
             else:
                 ops.w8a16_residual_(act, L.w_d, L.s_d, x, gamma_next=g_next, xg_out=xg, ssq_out=ssq)
-        if b.is_decode:
-            xl, nl = xg, norm
-        else:
-            xl = xg.index_select(0, b.last_rows)
-            nl = (ssq.index_select(1, b.last_rows).contiguous(), H, cfg.rms_eps)
-        logits = ops.w8a16_linear(xl, self.head_q, self.head_s, out_dtype=torch.float32, in_norm=nl)
-        if tp:
-            keys = torch.empty(xl.shape[0], dtype=torch.int64, device=dev)
-            ops.argmax_rows(logits, p.vocab_start, keys=keys)
-            self.comm.all_reduce_max_(keys)
-            from ..parallel.dist import unpack_argmax
-            return unpack_argmax(keys)
-        return ops.argmax_rows(logits, 0)
+        return xg, ssq
 
     def _row_parallel(self, a: torch.Tensor, w: torch.Tensor, s: torch.Tensor, partial: torch.Tensor) -> None:
         """``partial = all_reduce(a @ W^T)`` for a row-parallel projection (NCCL path).  With
