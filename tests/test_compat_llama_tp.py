@@ -1,7 +1,6 @@
 """The reference-named torch TP API (``compat.llama_tp``) on the engine, CPU: per-sequence KV pages, the distributed
 greedy select, loading through a reference-style loader from an HF-style config, the low-level forward /
 logits_last loop against generate_tp and the oracle, and TP=2 over gloo against TP=1."""
-import os
 import socket
 
 import pytest
