@@ -98,6 +98,8 @@ class DSI8File:
         self._f = self.path.open("rb")
         self._mm = mmap.mmap(self._f.fileno(), 0, access=mmap.ACCESS_READ)
         buf = self._mm
+        if len(buf) < 60:
+            raise ValueError(f"{path}: truncated header ({len(buf)} bytes)")
         if buf[:4] != MAGIC:
             raise ValueError(f"{path}: bad magic {bytes(buf[:4])!r}")
         (self.version,) = struct.unpack_from("<I", buf, 4)
@@ -110,15 +112,23 @@ class DSI8File:
         o = 60
         self.records: Dict[str, Tuple[int, Tuple[int, ...], int]] = {}
         n = len(buf)
-        while o + 4 <= n:
+
+        def need(end: int, what: str) -> None:
+            if end > n:
+                raise ValueError(f"{path}: truncated in {what} (needs byte {end}, file has {n})")
+
+        while o < n:   # records back to back up to the end of the file; a partial record is an error
+            need(o + 4, f"record {len(self.records)} header")
             (nl,) = struct.unpack_from("<I", buf, o)
             o += 4
-            if o + nl > n:
-                break
-            name = bytes(buf[o:o + nl]).decode()
+            need(o + nl + 8, f"record {len(self.records)} header")
+            name = bytes(buf[o:o + nl]).decode(errors="replace")
             o += nl
             ttype, ndim = struct.unpack_from("<II", buf, o)
             o += 8
+            if ndim < 1 or ndim > 4:
+                raise ValueError(f"{path}: record {name!r} has {ndim} dimensions")
+            need(o + 4 * ndim, f"record {name!r} header")
             dims = struct.unpack_from("<" + "I" * ndim, buf, o)
             o += 4 * ndim
             self.records[name] = (ttype, tuple(dims), o)
@@ -132,6 +142,7 @@ class DSI8File:
                 o += rows * 4 + rows * ((cols + 1) // 2)
             else:
                 o += int(np.prod(dims)) * 4
+            need(o, f"record {name!r} payload")
         meta = {}
         if META_NAME in self.records:
             _, dims, off = self.records[META_NAME]
@@ -176,9 +187,36 @@ class DSI8File:
     def load_all(self) -> Dict[str, Tensorish]:
         return {k: self.get(k) for k in self.names()}
 
+    def check(self) -> None:
+        """Every tensor the header's architecture needs is present with its shape and type (int8 matrices, fp32
+        vectors); raises ValueError naming what is missing or wrong.  Extra records are allowed."""
+        from ..models.weights import matrix_shapes, vector_shapes
+        missing, wrong = [], []
+        for name, (rows, cols) in matrix_shapes(self.config):
+            r = self.records.get(name)
+            if r is None:
+                missing.append(name)
+            elif r[0] != TTYPE_Q8 or r[1][:2] != (rows, cols):
+                wrong.append(f"{name}: type {r[0]} dims {r[1]}, expected q8 {(rows, cols)}")
+        for name, length in vector_shapes(self.config):
+            r = self.records.get(name)
+            if r is None:
+                missing.append(name)
+            elif r[0] != TTYPE_F32 or int(np.prod(r[1])) != length:
+                wrong.append(f"{name}: type {r[0]} dims {r[1]}, expected f32 [{length}]")
+        if missing or wrong:
+            parts = []
+            if missing:
+                parts.append(f"{len(missing)} missing tensor(s): " + ", ".join(missing[:5])
+                             + (" ..." if len(missing) > 5 else ""))
+            if wrong:
+                parts.append("; ".join(wrong[:5]) + (" ..." if len(wrong) > 5 else ""))
+            raise ValueError(f"{self.path}: not a complete {self.config.name} export: " + " | ".join(parts))
+
 
 def read_dsi8(path: str | Path) -> Tuple[ModelConfig, Dict[str, Tensorish]]:
     with DSI8File(path) as f:
+        f.check()
         return f.config, f.load_all()
 
 

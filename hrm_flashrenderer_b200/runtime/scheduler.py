@@ -26,6 +26,19 @@ from typing import Callable, Deque, Dict, List, Optional, Sequence
 import torch
 
 
+# CUDA errors after which the context is unusable (every later CUDA call in the process fails as well)
+_STICKY_CUDA = ("illegal memory access", "illegal instruction", "misaligned address", "unspecified launch failure",
+                "device-side assert", "uncorrectable ecc", "launch timed out", "hardware stack error",
+                "invalid program counter", "mmu fault", "context is destroyed", "cuda-capable device")
+
+
+def is_context_fatal(e: BaseException) -> bool:
+    """True for a CUDA error that leaves the process's CUDA context unusable."""
+    msg = str(e).lower()
+    return ("cuda" in msg or "cublas" in msg or "acceleratorerror" in type(e).__name__.lower()) and \
+        any(k in msg for k in _STICKY_CUDA)
+
+
 @dataclass
 class GenRequest:
     prompt_ids: List[int]
@@ -68,6 +81,13 @@ class Scheduler:
         self.itls: Deque[float] = collections.deque(maxlen=4096)
         self.started_at = time.perf_counter()
         self.last_error: Optional[str] = None
+        # fatal: the engine cannot serve any more (a CUDA error that poisons the context, or
+        # max_consecutive_failures failed iterations in a row).  The loop then stops, every queued request fails,
+        # submit() refuses new ones and alive() is False, so the lane's health turns false: the router fails over
+        # and the process supervisor restarts the lane (a lost CUDA context cannot be rebuilt in-process).
+        self.fatal: Optional[str] = None
+        self.max_consecutive_failures = 3
+        self._fails = 0
 
     # ------------------------------------------------------------------ lifecycle
     def start(self) -> "Scheduler":
@@ -83,11 +103,13 @@ class Scheduler:
             self._thread = None
 
     def alive(self) -> bool:
-        return self._thread is not None and self._thread.is_alive()
+        return self._thread is not None and self._thread.is_alive() and self.fatal is None
 
     # ------------------------------------------------------------------ API
     def submit(self, prompt_ids: Sequence[int], max_new_tokens: int, stop_on_eos: bool = True,
                on_token: Optional[Callable[[int], None]] = None) -> GenRequest:
+        if self.fatal is not None:
+            raise RuntimeError(f"engine stopped after a fatal error: {self.fatal}")
         if not prompt_ids:
             raise ValueError("empty prompt")
         limit = self.engine.max_blocks * self.engine.block_size
@@ -102,6 +124,8 @@ class Scheduler:
             self._next_rid += 1
         r = GenRequest(list(map(int, prompt_ids)), int(max_new_tokens), stop_on_eos, on_token, rid)
         self._inbox.put(r)
+        if self.fatal is not None:   # the loop stopped between the check above and the put
+            self._fail_queued()
         return r
 
     def generate(self, prompt_ids: Sequence[int], max_new_tokens: int, timeout: Optional[float] = None,
@@ -116,7 +140,7 @@ class Scheduler:
         return {"queue_depth": len(self._waiting) + self._inbox.qsize(), "batch_size": len(self._running),
                 "completed": self.completed, "generated_tokens": self.generated_tokens,
                 "tok_per_s": self.generated_tokens / el, "ttft_p50_ms": pct(tt, 0.5), "ttft_p99_ms": pct(tt, 0.99),
-                "itl_p50_ms": pct(it, 0.5), "last_error": self.last_error}
+                "itl_p50_ms": pct(it, 0.5), "last_error": self.last_error, "fatal": self.fatal}
 
     # ------------------------------------------------------------------ loop
     def _finish(self, r: GenRequest) -> None:
@@ -160,7 +184,19 @@ class Scheduler:
             used += len(r.prompt_ids)
         if not batch:
             return False
-        firsts = eng.prefill([(r.seq_id, r.prompt_ids) for r in batch])
+        try:
+            firsts = eng.prefill([(r.seq_id, r.prompt_ids) for r in batch])
+        except BaseException as e:   # these requests left the queue: fail them and return their blocks here
+            for r in batch:
+                try:
+                    r.future.set_exception(e)
+                except Exception:
+                    pass
+                try:
+                    eng.release(r.seq_id)
+                except Exception:
+                    pass
+            raise
         now = time.perf_counter()
         for r, t in zip(batch, firsts):
             r.first_token_at = now
@@ -216,8 +252,11 @@ class Scheduler:
                     staged, g = self._decode(staged, g)
                 elif not admitted:
                     time.sleep(self.idle_sleep_s)
-            except BaseException as e:   # fail the in-flight requests, keep serving new ones
+                if admitted or self._running:
+                    self._fails = 0
+            except BaseException as e:   # fail the in-flight requests, keep serving new ones unless fatal
                 self.last_error = repr(e)
+                self._fails += 1
                 for r in self._running + list(self._waiting):
                     if not r.future.done():
                         r.future.set_exception(e)
@@ -227,3 +266,20 @@ class Scheduler:
                         pass
                 self._running, staged = [], False
                 self._waiting.clear()
+                if is_context_fatal(e) or self._fails >= self.max_consecutive_failures:
+                    self.fatal = repr(e)
+                    break
+        if self.fatal is not None:   # nothing queued waits for a loop that is gone
+            self._fail_queued()
+
+    def _fail_queued(self) -> None:
+        err = RuntimeError(f"engine stopped after a fatal error: {self.fatal}")
+        while True:
+            try:
+                r = self._inbox.get_nowait()
+            except queue.Empty:
+                return
+            try:
+                r.future.set_exception(err)
+            except Exception:   # already resolved
+                pass

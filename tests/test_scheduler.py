@@ -69,3 +69,60 @@ def test_scheduler_rejects_request_larger_than_pool():
     eng = InferenceEngine(m, EngineConfig(max_seq_len=256, max_batch=2, use_cuda_graphs=False), num_blocks=4)
     with pytest.raises(ValueError):
         Scheduler(eng).submit(list(range(60)), 10)     # 71 positions = 5 blocks > 4
+
+
+def _fail_prefill(eng, exc, times=None):
+    """Make the engine's prefill raise ``exc`` (``times`` calls, then work again)."""
+    real = eng.prefill
+    left = [times]
+
+    def bad(*a, **k):
+        if left[0] is None or left[0] > 0:
+            if left[0] is not None:
+                left[0] -= 1
+            raise exc
+        return real(*a, **k)
+    eng.prefill = bad
+
+
+def test_sticky_cuda_error_makes_the_scheduler_fatal():
+    """A context-poisoning CUDA error: in-flight and queued requests fail, new ones are refused at once and the
+    scheduler reports itself dead (lane health false -> failover and a supervisor restart)."""
+    import pytest
+    from hrm_flashrenderer_b200.runtime.scheduler import is_context_fatal
+    eng = _engine()
+    err = RuntimeError("CUDA error: an illegal memory access was encountered")
+    assert is_context_fatal(err) and not is_context_fatal(RuntimeError("shape mismatch"))
+    _fail_prefill(eng, err)
+    sched = Scheduler(eng).start()
+    try:
+        r = sched.submit(list(range(5, 15)), 4)
+        with pytest.raises(RuntimeError, match="illegal memory access"):
+            r.future.result(timeout=60)
+        sched._thread.join(timeout=30)
+        assert not sched.alive() and "illegal memory access" in sched.metrics()["fatal"]
+        assert eng.bm.free_blocks == eng.bm.num_blocks          # the failed request's blocks went back
+        with pytest.raises(RuntimeError, match="fatal error"):
+            sched.submit([5, 6, 7], 2)
+    finally:
+        sched.stop()
+
+
+def test_transient_errors_keep_serving_until_the_limit():
+    import pytest
+    eng = _engine()
+    _fail_prefill(eng, ValueError("transient"), times=1)
+    sched = Scheduler(eng).start()
+    try:
+        with pytest.raises(ValueError):
+            sched.submit([5, 6, 7, 8], 3).future.result(timeout=60)
+        assert len(sched.submit([5, 6, 7, 8], 3).future.result(timeout=60)) == 3   # served after one failure
+        assert sched.alive() and sched.metrics()["fatal"] is None
+        _fail_prefill(eng, ValueError("broken"))
+        for _ in range(sched.max_consecutive_failures):
+            with pytest.raises((ValueError, RuntimeError)):
+                sched.submit([5, 6, 7, 8], 3).future.result(timeout=60)
+        sched._thread.join(timeout=30)
+        assert not sched.alive() and "broken" in sched.metrics()["fatal"]
+    finally:
+        sched.stop()
