@@ -17,6 +17,8 @@ package's int8 engine.
 * ``greedy_select_token_distributed(local_logits)``: global greedy ids from vocab-sharded logits with ONE
   all-reduce of packed (value, id) keys; ties go to the lowest global id (the reference needs two all-reduces and
   one broadcast per row, ties to the lowest rank, which is the same id).
+* ``WeightLoader`` (from :mod:`~hrm_flashrenderer_b200.formats.safetensors`): the reference loader interface over
+  sharded safetensors checkpoints; ``TPLlamaForCausalLM.from_pretrained(model_dir, ...)`` uses it.
 * ``PagedKVCache``: the reference's per-sequence page layout ``[B, Hk, P, PS, D]`` with ``seqlen [B]``, grown to a
   power of two of pages, for code that drives ``compat.flash_attn_paged`` directly.  The engine itself does not
   use it.
@@ -28,11 +30,12 @@ from typing import Any, Dict, Iterator, List, Optional, Sequence, Union
 import torch
 
 from ..config import EngineConfig, ModelConfig
+from ..formats.safetensors import WeightLoader
 from ..models.weights import EMBED, LM_HEAD, QTensor, matrix_shapes, quantize_rows, vector_shapes
 from ..parallel.dist import greedy_select_distributed, is_dist, rank_world
 from .flashattention import paged_kv_append
 
-__all__ = ["PagedKVCache", "TPLlamaForCausalLM", "generate_tp", "greedy_select_token_distributed"]
+__all__ = ["PagedKVCache", "TPLlamaForCausalLM", "WeightLoader", "generate_tp", "greedy_select_token_distributed"]
 
 
 # ------------------------------------------------------------------------------------------------ KV pages
@@ -138,7 +141,7 @@ class _LoaderWeights:
         t = self.loader.get(name)
         if name in self._mats:
             return quantize_rows(t.to(torch.float32))
-        return t.to(torch.float32)
+        return t.to(torch.float32, copy=True)   # never a view into the loader's storage
 
     def __getitem__(self, name: str):
         if name in self._keep:
@@ -215,6 +218,19 @@ class TPLlamaForCausalLM:
         self.model = LlamaW8.from_weights(self.cfg, weights, rank=self.rank, world=self.world, device=self.device,
                                           comm=comm, max_pos=self.max_seq_len + 16)
         self._make_engine()
+        return self
+
+    @classmethod
+    def from_pretrained(cls, model_dir, max_seq_len: int, device: Union[str, torch.device] = "cuda",
+                        max_batch: int = 16, num_blocks: Optional[int] = None) -> "TPLlamaForCausalLM":
+        """A local HF checkpoint directory: ``config.json`` plus safetensors shards read through
+        :class:`~hrm_flashrenderer_b200.formats.safetensors.WeightLoader` (zero-copy views, quantised at load)."""
+        import json
+        from pathlib import Path
+        cfg = json.loads((Path(model_dir) / "config.json").read_text())
+        self = cls(cfg, max_seq_len, device, max_batch=max_batch, num_blocks=num_blocks)
+        with WeightLoader(model_dir) as loader:
+            self.load_from_loader(loader)
         return self
 
     @classmethod
