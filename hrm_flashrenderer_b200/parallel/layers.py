@@ -17,8 +17,14 @@ import torch
 import torch.nn as nn
 
 from .. import ops
-from ..models.weights import QTensor
+from ..models.weights import QTensor, quantize_rows
 from .dist import all_reduce_sum, rank_world
+
+
+def _as_q(w) -> QTensor:
+    """The reference's layers load fp16 tensors; these take a QTensor or a float matrix (quantised per row here,
+    over the full row, so a column shard keeps the full-model scales)."""
+    return w if isinstance(w, QTensor) else quantize_rows(w.to(torch.float32))
 
 
 class _QLinearBase(nn.Module):
@@ -52,7 +58,7 @@ class ColumnParallelLinear(_QLinearBase):
 
     def load_from_full(self, w: QTensor, bias: Optional[torch.Tensor] = None) -> None:
         r0, r1 = self.rank * self.local_out, (self.rank + 1) * self.local_out
-        self.load(w.rows(r0, r1), None if bias is None else bias[r0:r1])
+        self.load(_as_q(w).rows(r0, r1), None if bias is None else bias[r0:r1])
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return self._mm(x)
@@ -69,7 +75,7 @@ class RowParallelLinear(_QLinearBase):
 
     def load_from_full(self, w: QTensor, bias: Optional[torch.Tensor] = None) -> None:
         c0, c1 = self.rank * self.local_in, (self.rank + 1) * self.local_in
-        self.load(w.cols(c0, c1), bias)
+        self.load(_as_q(w).cols(c0, c1), bias)
 
     def forward(self, x_shard: torch.Tensor) -> torch.Tensor:
         y = ops.w8a16_linear(x_shard, self.qweight, self.scale, out_dtype=torch.float32)
@@ -86,7 +92,7 @@ class ReplicatedLinear(_QLinearBase):
         super().__init__(out_features, in_features, bias, device)
 
     def load_from_full(self, w: QTensor, bias: Optional[torch.Tensor] = None) -> None:
-        self.load(w, bias)
+        self.load(_as_q(w), bias)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return self._mm(x)
@@ -107,7 +113,7 @@ class VocabParallelEmbedding(nn.Module):
         self.register_buffer("scale", torch.ones(self.vocab_per_rank, dtype=torch.float32, device=device))
 
     def load_from_full(self, w: QTensor) -> None:
-        qt = w.rows(self.vocab_start, self.vocab_start + self.vocab_per_rank)
+        qt = _as_q(w).rows(self.vocab_start, self.vocab_start + self.vocab_per_rank)
         self.qweight.copy_(qt.q.to(self.qweight.device))
         self.scale.copy_(qt.scale.to(self.scale.device))
 
@@ -127,7 +133,7 @@ class VocabParallelLMHead(_QLinearBase):
         super().__init__(self.vocab_per_rank, hidden, False, device)
 
     def load_from_full(self, w: QTensor) -> None:
-        self.load(w.rows(self.vocab_start, self.vocab_start + self.vocab_per_rank))
+        self.load(_as_q(w).rows(self.vocab_start, self.vocab_start + self.vocab_per_rank))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return ops.w8a16_linear(x, self.qweight, self.scale, out_dtype=torch.float32)
