@@ -69,6 +69,8 @@ def main(argv=None):
     ap.add_argument("--json", default="")
     ap.add_argument("--ops", default="gemm,attn,norm")
     ap.add_argument("--attn-b", default="1,16,64", help="decode-attention batch sizes (context 4096)")
+    ap.add_argument("--gemm-order", default="n",
+                    help="output-tile numbering(s) to time: n (n-fastest, default), m (m-fastest), or n,m")
     a = ap.parse_args(argv)
     hbm, tfl, src = peaks()
     dev = torch.device("cuda")
@@ -94,8 +96,15 @@ def main(argv=None):
             for M in Ms:
                 x = torch.randn(M, K, device=dev, dtype=torch.float16)
                 out = torch.empty(M, N, device=dev, dtype=torch.float16)
-                us = time_op(lambda: ops.w8a16_linear_out(x, wt, qt.scale, out), a.iters, a.warmup, flush)
-                rec(f"w8a16_gemm/{name}", f"M{M}xN{N}xK{K}", us, N * K + 2 * M * K + 2 * M * N, 2.0 * M * N * K)
+                for order in a.gemm_order.split(","):
+                    ops.ext().set_gemm_m_fastest(order == "m")
+                    try:
+                        us = time_op(lambda: ops.w8a16_linear_out(x, wt, qt.scale, out), a.iters, a.warmup, flush)
+                    finally:
+                        ops.ext().set_gemm_m_fastest(False)
+                    tag = "" if order == "n" else "/m-fastest"
+                    rec(f"w8a16_gemm/{name}{tag}", f"M{M}xN{N}xK{K}", us, N * K + 2 * M * K + 2 * M * N,
+                        2.0 * M * N * K)
             del qt, wt
     if "attn" in a.ops:
         c = LLAMA31_70B
