@@ -18,6 +18,8 @@ mistaken for a current one and no reset pass is needed between launches.
 """
 from __future__ import annotations
 
+import warnings
+
 import torch
 import torch.distributed as dist
 
@@ -74,8 +76,8 @@ class SymmetricWorkspace:
             if r != self.rank:
                 try:
                     C.symm_close(p)
-                except Exception:
-                    pass
+                except Exception as e:   # keep tearing down: the barrier below must still be reached
+                    warnings.warn(f"symmetric workspace: unmapping rank {r}'s buffer failed: {e!r}")
         if self.world > 1:
             dist.barrier(group=self.group)   # peers unmapped before the owner frees
         C.symm_free(self.local_ptr)

@@ -157,8 +157,8 @@ class Scheduler:
         if r.on_token is not None:
             try:
                 r.on_token(tok)
-            except Exception:
-                pass
+            except Exception as e:   # a broken stream consumer must not stop generation for the batch
+                self.last_error = f"on_token callback of request {r.rid}: {e!r}"
         return len(r.tokens) >= r.max_new_tokens or (r.stop_on_eos and tok in self.eos)
 
     def _admit(self) -> bool:
