@@ -66,7 +66,9 @@ def write_dsi8(path: str | Path, cfg: ModelConfig, weights: Dict[str, Tensorish]
             if name not in weights:
                 continue
             t = weights[name]
-            assert isinstance(t, QTensor) and t.shape == (rows, cols), name
+            if not isinstance(t, QTensor) or t.shape != (rows, cols):
+                raise ValueError(f"{name}: expected an int8 QTensor {(rows, cols)}, got "
+                                 f"{type(t).__name__} {tuple(getattr(t, 'shape', ()))}")
             _write_record(f, name, TTYPE_Q8, (rows, cols), [
                 t.scale.detach().cpu().to(torch.float32).contiguous().numpy().tobytes(),
                 t.q.detach().cpu().contiguous().numpy().tobytes()])
@@ -74,7 +76,8 @@ def write_dsi8(path: str | Path, cfg: ModelConfig, weights: Dict[str, Tensorish]
             if name not in weights:
                 continue
             v = weights[name].detach().cpu().to(torch.float32).contiguous()
-            assert v.numel() == n, name
+            if v.numel() != n:
+                raise ValueError(f"{name}: expected {n} values, got {v.numel()}")
             _write_record(f, name, TTYPE_F32, (n,), [v.numpy().tobytes()])
         meta = {
             "name": cfg.name,
@@ -223,53 +226,52 @@ def read_dsi8(path: str | Path) -> Tuple[ModelConfig, Dict[str, Tensorish]]:
 # ------------------------------------------------------------------------------------------------
 # safetensors -> DSI8 exporter (reference: ``export_dsi_v4``, ``hrm_flash/deepseek_export.py:110-222``)
 # ------------------------------------------------------------------------------------------------
-_ST_DTYPES = {"F32": np.float32, "F16": np.float16, "BF16": np.uint16, "I8": np.int8}
+class _ShardedExportWeights:
+    """What :func:`write_dsi8` reads, streamed from the checkpoint's safetensors shards: each tensor is read from its
+    shard's mapping and quantised only when the writer reaches its record, so one tensor is in memory at a time."""
 
+    def __init__(self, files: Dict[str, "SafetensorsFile"], cfg: ModelConfig):
+        self.files = files
+        self.want_2d = dict(matrix_shapes(cfg))
+        self.want_1d = dict(vector_shapes(cfg))
 
-def _iter_safetensors(path: Path):
-    with path.open("rb") as f:
-        (hs,) = struct.unpack("<Q", f.read(8))
-        hdr = json.loads(f.read(hs))
-    base = 8 + hs
-    mm = np.memmap(path, dtype=np.uint8, mode="r")
-    for k, m in hdr.items():
-        if k == "__metadata__":
-            continue
-        s, e = m["data_offsets"]
-        dt = m["dtype"]
-        raw = mm[base + s: base + e]
-        if dt == "BF16":
-            arr = (raw.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
-        elif dt in _ST_DTYPES:
-            arr = raw.view(_ST_DTYPES[dt]).astype(np.float32)
-        else:
-            raise ValueError(f"{path}:{k}: unsupported safetensors dtype {dt}")
-        yield k, arr.reshape(m["shape"])
+    def __contains__(self, name: str) -> bool:
+        return name in self.files and (name in self.want_2d or name in self.want_1d)
+
+    def __getitem__(self, name: str) -> Tensorish:
+        t = self.files[name].tensor(name).to(torch.float32)
+        if name in self.want_2d:
+            return quantize_rows(t)
+        return t.reshape(-1).clone()
 
 
 def export_dsi8(model_dir: str | Path, out_path: str | Path, quant: str = "q8") -> Path:
-    """Export a local HF checkpoint directory (config.json + *.safetensors) to DSI8 (q8 only).
+    """Export a local HF checkpoint directory (config.json + *.safetensors) to DSI8 (q8 only), streaming one tensor
+    at a time.  Matrices get one symmetric int8 scale per output row (``max|w| / 127``), vectors stay fp32.
 
     q4 is rejected: the reference engine parses tensor type 2 as F32 and the production scripts lock it out
     (``deepseek_export.py:53-79,196-198``; ``deepseek_native_engine.sh:342-355``).
     """
+    from .safetensors import SafetensorsFile
     if str(quant).lower() != "q8":
         raise ValueError(f"unsupported quant={quant!r}: only q8 is supported")
     model_dir = Path(model_dir)
     cfg = ModelConfig.from_hf_dir(model_dir)
-    want_2d = dict(matrix_shapes(cfg))
-    want_1d = dict(vector_shapes(cfg))
-    weights: Dict[str, Tensorish] = {}
-    for fn in sorted(model_dir.glob("*.safetensors")):
-        for k, arr in _iter_safetensors(fn):
-            if k in want_2d:
-                weights[k] = quantize_rows(torch.from_numpy(np.ascontiguousarray(arr, dtype=np.float32)))
-            elif k in want_1d:
-                weights[k] = torch.from_numpy(np.ascontiguousarray(arr, dtype=np.float32)).reshape(-1)
-    if not weights:
-        raise RuntimeError(f"no safetensors tensors found under {model_dir}")
-    if cfg.qkv_bias and not any(k.endswith("q_proj.bias") for k in weights):
-        cfg = replace(cfg, qkv_bias=False)
-    if LM_HEAD not in weights and EMBED in weights:
-        cfg = replace(cfg, tie_embeddings=True)
-    return write_dsi8(out_path, cfg, weights)
+    files: Dict[str, SafetensorsFile] = {}
+    opened = []
+    try:
+        for fn in sorted(model_dir.glob("*.safetensors")):
+            f = SafetensorsFile(fn)
+            opened.append(f)
+            for key in f.keys():
+                files[key] = f
+        if not files:
+            raise RuntimeError(f"no safetensors tensors found under {model_dir}")
+        if cfg.qkv_bias and not any(key.endswith("q_proj.bias") for key in files):
+            cfg = replace(cfg, qkv_bias=False)
+        if LM_HEAD not in files and EMBED in files:
+            cfg = replace(cfg, tie_embeddings=True)
+        return write_dsi8(out_path, cfg, _ShardedExportWeights(files, cfg))
+    finally:
+        for f in opened:
+            f.close()
