@@ -94,12 +94,14 @@ def write_dsi8(path: str | Path, cfg: ModelConfig, weights: Dict[str, Tensorish]
 
 
 class DSI8File:
-    """Memory-mapped DSI8 reader.  Tensors are zero-copy numpy views into the mapping."""
+    """Memory-mapped DSI8 reader.  ``get`` returns zero-copy views into a private copy-on-write mapping (the file is
+    never written): a 70B export is not copied into host memory, and the tensor-parallel ranks of one host share the
+    page cache and touch only the pages their shard reads.  A view keeps the mapping alive after ``close()``."""
 
     def __init__(self, path: str | Path):
         self.path = Path(path)
         self._f = self.path.open("rb")
-        self._mm = mmap.mmap(self._f.fileno(), 0, access=mmap.ACCESS_READ)
+        self._mm = mmap.mmap(self._f.fileno(), 0, access=mmap.ACCESS_COPY)
         buf = self._mm
         if len(buf) < 60:
             raise ValueError(f"{path}: truncated header ({len(buf)} bytes)")
@@ -162,7 +164,10 @@ class DSI8File:
         )
 
     def close(self) -> None:
-        self._mm.close()
+        try:
+            self._mm.close()
+        except BufferError:   # views are alive: they hold the mapping, which goes with the last of them
+            pass
         self._f.close()
 
     def __enter__(self):
@@ -174,17 +179,19 @@ class DSI8File:
     def names(self):
         return [k for k in self.records if k != META_NAME]
 
-    def get(self, name: str) -> Tensorish:
+    def get(self, name: str, copy: bool = False) -> Tensorish:
+        """Tensor ``name``: a view into the mapping, or an independent copy with ``copy=True``."""
         ttype, dims, off = self.records[name]
+        cp = (lambda a: a.copy()) if copy else (lambda a: a)
         if ttype == TTYPE_Q8:
             rows = dims[0]
             cols = dims[1] if len(dims) > 1 else 1
             scale = np.frombuffer(self._mm, dtype=np.float32, count=rows, offset=off)
             q = np.frombuffer(self._mm, dtype=np.int8, count=rows * cols, offset=off + rows * 4).reshape(rows, cols)
-            return QTensor(torch.from_numpy(q.copy()), torch.from_numpy(scale.copy()))
+            return QTensor(torch.from_numpy(cp(q)), torch.from_numpy(cp(scale)))
         if ttype == TTYPE_F32:
             cnt = int(np.prod(dims))
-            return torch.from_numpy(np.frombuffer(self._mm, dtype=np.float32, count=cnt, offset=off).copy())
+            return torch.from_numpy(cp(np.frombuffer(self._mm, dtype=np.float32, count=cnt, offset=off)))
         raise ValueError(f"{name}: unsupported tensor type {ttype} (only q8 is supported; q4 is rejected)")
 
     def load_all(self) -> Dict[str, Tensorish]:

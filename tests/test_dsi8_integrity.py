@@ -3,6 +3,8 @@ header, a payload), a missing tensor, a wrong shape or a wrong tensor type.  Fai
 "corrupt a weight file"); nothing reaches a device."""
 import struct
 
+import torch
+
 import pytest
 
 from hrm_flashrenderer_b200.config import TINY
@@ -85,3 +87,16 @@ def test_engine_load_fails_cleanly(good, tmp_path):
     p.write_bytes(good.read_bytes()[:-1000])
     with pytest.raises(ValueError, match="truncated"):
         LlamaW8.from_dsi8(str(p), device="cpu", max_pos=64)
+
+
+def test_views_share_the_mapping_and_outlive_close(good):
+    f = DSI8File(good)
+    name = "model.layers.0.mlp.gate_proj.weight"
+    v = f.get(name)
+    c = f.get(name, copy=True)
+    assert not v.q.numpy().flags.owndata and c.q.numpy().flags.owndata
+    assert torch.equal(v.q, c.q) and torch.equal(v.scale, c.scale)
+    f.close()                                  # views keep the mapping alive
+    assert torch.equal(v.q, c.q)
+    c.q[0, 0] += 1                             # a copy is independent of the file's contents
+    assert not torch.equal(v.q, c.q)
