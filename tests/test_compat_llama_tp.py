@@ -1,6 +1,7 @@
 """The reference-named torch TP API (``compat.llama_tp``) on the engine, CPU: per-sequence KV pages, the distributed
 greedy select, loading through a reference-style loader from an HF-style config, the low-level forward /
 logits_last loop against generate_tp and the oracle, and TP=2 over gloo against TP=1."""
+import os
 import socket
 
 import pytest
@@ -209,18 +210,29 @@ def test_tp2_over_gloo_matches_tp1():
 
 
 @pytest.mark.gpu
+@pytest.mark.skipif(os.environ.get("HRM_TEST_COMPAT_GPU") != "1", reason="set HRM_TEST_COMPAT_GPU=1")
 def test_gpu_generate_tp_and_low_level_first_token():
-    """On the B200: generate_tp against the oracle, and the first token through forward / logits_last / greedy
-    select against generate_tp's first token."""
+    """On the B200 (head_dim 128, the GPU kernels' shape): generate_tp against the oracle (f16 operands: a late
+    divergence is allowed, as in the engine's own GPU oracle test), and the low-level forward / logits_last logits
+    rank generate_tp's first token at the top."""
+    from hrm_flashrenderer_b200.config import ModelConfig, RopeScaling
     from hrm_flashrenderer_b200.models.oracle import OracleLlama
-    fw, qw = _float_weights()
-    m = lt.TPLlamaForCausalLM(HF_TINY, max_seq_len=64, device="cuda").load_weights(fw)
-    ids = _prompts().cuda()
-    out = lt.generate_tp(m, ids, 8, eos_token_id=None)
-    assert out.is_cuda and out.shape == (2, 20)
-    ref = OracleLlama(TINY, qw, max_pos=128).generate(ids.cpu().tolist(), 8)
-    assert out[:, 12:].cpu().tolist() == ref
+    cfg = ModelConfig(name="gpu-small", hidden=1024, layers=2, heads=8, kv_heads=2, head_dim=128,
+                      intermediate=2816, vocab=4096, rms_eps=1e-5, rope_theta=500000.0,
+                      rope_scaling=RopeScaling(8.0, 1.0, 4.0, 8192), max_position_embeddings=8192)
+    w = synth_weights(cfg, seed=0, norm_jitter=0.1)
+    m = lt.TPLlamaForCausalLM(cfg, max_seq_len=128, device="cuda", max_batch=4, num_blocks=64).load_weights(w)
+    ids = torch.randint(0, cfg.vocab, (2, 40), generator=torch.Generator().manual_seed(1)).cuda()
+    out = lt.generate_tp(m, ids, 12, eos_token_id=None)
+    assert out.is_cuda and out.shape == (2, 52)
+    ref = OracleLlama(cfg, w, max_pos=512).generate(ids.cpu().tolist(), 12)
+    for a, b in zip(out[:, 40:].cpu().tolist(), ref):
+        n = next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), len(a))
+        assert n >= 8, (a, b)
     m.reset_all_caches()
-    h = m.forward(ids, torch.arange(12, device="cuda"))
-    first = lt.greedy_select_token_distributed(m.logits_last(h[:, -1]))
-    assert first.cpu().tolist() == [r[0] for r in ref]
+    h = m.forward(ids, torch.arange(40, device="cuda"))
+    logits = m.logits_last(h[:, -1]).float().cpu()
+    first = out[:, 40].cpu()
+    for b in range(2):
+        top = logits[b].max()
+        assert logits[b, first[b]] >= top - 1e-2 * logits[b].abs().max(), (b, int(first[b]), int(logits[b].argmax()))
