@@ -1,4 +1,5 @@
-"""HTTP service of one lane: ``POST /v1/generate``, ``GET /v1/health``, ``GET /v1/metrics``.
+"""HTTP service of one lane: ``POST /v1/generate``, ``GET /v1/health``, ``GET /v1/metrics`` (JSON) and ``GET /metrics``
+(Prometheus text format).
 
 Request/response contract of the reference service (``hrm_flash/serve.py:207-301``):
 
@@ -87,6 +88,48 @@ def build_prompt(state: ServiceState, prompt: str, mode: str) -> Tuple[str, List
     return build_prompt_for_mode(q, srcs, resolved), srcs, resolved, True
 
 
+# engine metric -> (Prometheus name, type, help); values that are None are left out
+_PROM_ENGINE = (
+    ("queue_depth", "hrm_engine_queue_depth", "gauge", "requests waiting for admission"),
+    ("batch_size", "hrm_engine_batch_size", "gauge", "sequences in the running decode batch"),
+    ("completed", "hrm_engine_requests_completed_total", "counter", "finished generation requests"),
+    ("generated_tokens", "hrm_engine_generated_tokens_total", "counter", "tokens generated"),
+    ("tok_per_s", "hrm_engine_tokens_per_second", "gauge", "generated tokens per second since start"),
+    ("ttft_p50_ms", "hrm_engine_ttft_p50_ms", "gauge", "median time to first token (ms)"),
+    ("ttft_p99_ms", "hrm_engine_ttft_p99_ms", "gauge", "99th percentile time to first token (ms)"),
+    ("itl_p50_ms", "hrm_engine_itl_p50_ms", "gauge", "median inter-token latency (ms)"),
+)
+
+
+def prometheus_text(state: "ServiceState", eng: dict, running: bool) -> str:
+    """Prometheus text exposition (format 0.0.4) of the lane's audit counters and its engine's metrics."""
+    out = []
+
+    def metric(name, typ, help_, samples):
+        out.append(f"# HELP {name} {help_}")
+        out.append(f"# TYPE {name} {typ}")
+        for labels, v in samples:
+            lab = "{" + ",".join(f'{k}="{val}"' for k, val in labels.items()) + "}" if labels else ""
+            out.append(f"{name}{lab} {float(v):.6g}")
+
+    metric("hrm_lane_up", "gauge", "1 while the generation backend runs", [({}, 1 if running else 0)])
+    metric("hrm_lane_requests_total", "counter", "generate requests received", [({}, state.requests_total)])
+    metric("hrm_lane_requests_by_mode_total", "counter", "generate requests by resolved mode",
+           [({"mode": m}, n) for m, n in sorted(state.mode_counts.items())])
+    metric("hrm_lane_hrm_queries_total", "counter", "HRM retrieval queries by mode",
+           [({"mode": m}, n) for m, n in sorted(state.hrm_query_calls_by_mode.items())])
+    metric("hrm_lane_prompt_build_failures_total", "counter", "prompts that could not be built",
+           [({}, state.prompt_build_failures)])
+    for key, name, typ, help_ in _PROM_ENGINE:
+        v = eng.get(key)
+        if isinstance(v, (int, float)) and not isinstance(v, bool):
+            metric(name, typ, help_, [({}, v)])
+    if "fatal" in eng:
+        metric("hrm_engine_fatal", "gauge", "1 after a fatal engine error (the lane needs a restart)",
+               [({}, 0 if eng.get("fatal") is None else 1)])
+    return "\n".join(out) + "\n"
+
+
 def create_app(state: ServiceState):
     from fastapi import FastAPI, HTTPException, Request
     from fastapi.responses import JSONResponse
@@ -128,6 +171,20 @@ def create_app(state: ServiceState):
     @app.get("/v1/metrics")
     async def metrics():
         return state.backend.metrics() if state.backend is not None else {}
+
+    @app.get("/metrics")
+    async def prometheus():
+        """The same counters and engine metrics in the Prometheus text exposition format."""
+        from fastapi.responses import PlainTextResponse
+        try:
+            eng = state.backend.metrics() if state.backend is not None else {}
+        except Exception:
+            eng = {}
+        try:
+            running = bool(state.backend is not None and state.backend.is_running())
+        except Exception:
+            running = False
+        return PlainTextResponse(prometheus_text(state, eng, running), media_type="text/plain; version=0.0.4")
 
     @app.post("/v1/generate")
     async def generate(request: Request):

@@ -1,0 +1,45 @@
+"""Lane service ``GET /metrics``: valid Prometheus text (checked with prometheus_client's parser), audit counters and
+the engine metrics, None values left out, the fatal flag."""
+import os
+import sys
+import urllib.request
+
+from prometheus_client.parser import text_string_to_metric_families
+
+from hrm_flashrenderer_b200.serving.backend import EchoBackend
+from hrm_flashrenderer_b200.serving.serve import ServiceState, create_app, prometheus_text
+
+sys.path.insert(0, os.path.dirname(__file__))
+from _http import LiveServer, post  # noqa: E402
+
+
+def _families(text):
+    return {f.name: f for f in text_string_to_metric_families(text)}
+
+
+def test_prometheus_text_from_engine_metrics():
+    st = ServiceState(backend=EchoBackend())
+    st.requests_total = 7
+    st.mode_counts["mixed"] = 5
+    eng = {"queue_depth": 2, "batch_size": 16, "completed": 40, "generated_tokens": 9000, "tok_per_s": 812.5,
+           "ttft_p50_ms": 123.4, "ttft_p99_ms": None, "itl_p50_ms": 19.7, "last_error": None, "fatal": "boom"}
+    fam = _families(prometheus_text(st, eng, running=False))
+    val = lambda n, **lab: next(s.value for s in fam[n].samples if all(s.labels.get(k) == v for k, v in lab.items()))
+    assert val("hrm_lane_up") == 0 and val("hrm_engine_fatal") == 1
+    assert val("hrm_lane_requests") == 7 and val("hrm_lane_requests_by_mode", mode="mixed") == 5
+    assert val("hrm_engine_batch_size") == 16 and val("hrm_engine_tokens_per_second") == 812.5
+    assert val("hrm_engine_generated_tokens") == 9000 and val("hrm_engine_itl_p50_ms") == 19.7
+    assert "hrm_engine_ttft_p99_ms" not in fam
+
+
+def test_metrics_endpoint_over_http():
+    st = ServiceState(backend=EchoBackend())
+    with LiveServer(create_app(st)) as srv:
+        post(srv.url + "/v1/generate", {"prompt": "hello", "mode": "deepseek_only", "max_new_tokens": 4})
+        with urllib.request.urlopen(srv.url + "/metrics", timeout=10) as r:
+            assert r.status == 200 and r.headers["Content-Type"].startswith("text/plain")
+            fam = _families(r.read().decode())
+    up = fam["hrm_lane_up"].samples[0].value
+    req = fam["hrm_lane_requests"].samples[0].value
+    by_mode = {s.labels["mode"]: s.value for s in fam["hrm_lane_requests_by_mode"].samples}
+    assert up == 1 and req == 1 and by_mode["deepseek_only"] == 1
