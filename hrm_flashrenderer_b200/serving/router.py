@@ -71,6 +71,12 @@ class RouterState:
         self.model_id = DEFAULT_MODEL_ID
         self.post = http_json_post    # injectable transport (tests)
         self.get = http_json_get
+        # routing counters (GET /metrics)
+        self.requests_total = 0
+        self.routed: Dict[str, int] = {}        # answered requests per lane
+        self.lane_errors: Dict[str, int] = {}   # failed attempts per lane
+        self.failovers_total = 0                # answered by a lane other than the primary
+        self.all_failed_total = 0               # 503: every candidate lane failed
 
 
 def http_json_get(url: str, timeout_s: float) -> Tuple[Dict[str, Any], int]:
@@ -221,6 +227,7 @@ def create_app(st: RouterState):
             mode = normalize_mode(req.mode if req.mode is not None else st.default_mode)
         except ValueError as e:
             raise HTTPException(status_code=400, detail=str(e))
+        st.requests_total += 1
         if st.sem is None:
             st.sem = asyncio.Semaphore(st.max_concurrent)
         async with st.sem:
@@ -242,6 +249,9 @@ def create_app(st: RouterState):
                     if not bool(body.get("ok", True)):
                         raise RuntimeError(str(body.get("detail") or body.get("error") or "backend returned ok=false"))
                     out = dict(body)
+                    st.routed[lane] = st.routed.get(lane, 0) + 1
+                    if lane != primary:
+                        st.failovers_total += 1
                     out["route"] = {"primary": primary, "selected": lane, "attempted": attempted,
                                     "estimator": estimator, "prompt_tokens": ptoks,
                                     "requested_max_new_tokens": req_new, "backend_max_new_tokens": lane_new,
@@ -249,6 +259,8 @@ def create_app(st: RouterState):
                     return out
                 except Exception as e:
                     errors.append(f"{lane}: {e}")
+                    st.lane_errors[lane] = st.lane_errors.get(lane, 0) + 1
+            st.all_failed_total += 1
             raise HTTPException(status_code=503, detail={"error": "all backends failed", "primary": primary,
                                                          "attempted": attempted, "backend_errors": errors})
 
@@ -297,6 +309,25 @@ def create_app(st: RouterState):
             return {"ok": bool(payload.get("ok", False)), "latency_ms": ms, "url": be.base_url}
         except Exception as e:
             return {"ok": False, "error": str(e), "url": be.base_url}
+
+    @app.get("/metrics")
+    async def prometheus():
+        """Routing counters in the Prometheus text format."""
+        from fastapi.responses import PlainTextResponse
+        from .prom import exposition
+        lanes = [n for n in LANES if n in st.backends]
+        text = exposition([
+            ("hrm_router_requests_total", "counter", "generate requests accepted", [({}, st.requests_total)]),
+            ("hrm_router_routed_total", "counter", "requests answered, by lane",
+             [({"lane": n}, st.routed.get(n, 0)) for n in lanes]),
+            ("hrm_router_lane_errors_total", "counter", "failed attempts, by lane",
+             [({"lane": n}, st.lane_errors.get(n, 0)) for n in lanes]),
+            ("hrm_router_failovers_total", "counter", "requests answered by a lane other than the primary",
+             [({}, st.failovers_total)]),
+            ("hrm_router_all_failed_total", "counter", "requests for which every candidate lane failed (503)",
+             [({}, st.all_failed_total)]),
+        ])
+        return PlainTextResponse(text, media_type="text/plain; version=0.0.4")
 
     @app.get("/v1/health")
     async def health():

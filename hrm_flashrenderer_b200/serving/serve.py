@@ -102,32 +102,26 @@ _PROM_ENGINE = (
 
 
 def prometheus_text(state: "ServiceState", eng: dict, running: bool) -> str:
-    """Prometheus text exposition (format 0.0.4) of the lane's audit counters and its engine's metrics."""
-    out = []
-
-    def metric(name, typ, help_, samples):
-        out.append(f"# HELP {name} {help_}")
-        out.append(f"# TYPE {name} {typ}")
-        for labels, v in samples:
-            lab = "{" + ",".join(f'{k}="{val}"' for k, val in labels.items()) + "}" if labels else ""
-            out.append(f"{name}{lab} {float(v):.6g}")
-
-    metric("hrm_lane_up", "gauge", "1 while the generation backend runs", [({}, 1 if running else 0)])
-    metric("hrm_lane_requests_total", "counter", "generate requests received", [({}, state.requests_total)])
-    metric("hrm_lane_requests_by_mode_total", "counter", "generate requests by resolved mode",
-           [({"mode": m}, n) for m, n in sorted(state.mode_counts.items())])
-    metric("hrm_lane_hrm_queries_total", "counter", "HRM retrieval queries by mode",
-           [({"mode": m}, n) for m, n in sorted(state.hrm_query_calls_by_mode.items())])
-    metric("hrm_lane_prompt_build_failures_total", "counter", "prompts that could not be built",
-           [({}, state.prompt_build_failures)])
+    """Prometheus text exposition of the lane's audit counters and its engine's metrics."""
+    from .prom import exposition
+    fam = [
+        ("hrm_lane_up", "gauge", "1 while the generation backend runs", [({}, 1 if running else 0)]),
+        ("hrm_lane_requests_total", "counter", "generate requests received", [({}, state.requests_total)]),
+        ("hrm_lane_requests_by_mode_total", "counter", "generate requests by resolved mode",
+         [({"mode": m}, n) for m, n in sorted(state.mode_counts.items())]),
+        ("hrm_lane_hrm_queries_total", "counter", "HRM retrieval queries by mode",
+         [({"mode": m}, n) for m, n in sorted(state.hrm_query_calls_by_mode.items())]),
+        ("hrm_lane_prompt_build_failures_total", "counter", "prompts that could not be built",
+         [({}, state.prompt_build_failures)]),
+    ]
     for key, name, typ, help_ in _PROM_ENGINE:
         v = eng.get(key)
         if isinstance(v, (int, float)) and not isinstance(v, bool):
-            metric(name, typ, help_, [({}, v)])
+            fam.append((name, typ, help_, [({}, v)]))
     if "fatal" in eng:
-        metric("hrm_engine_fatal", "gauge", "1 after a fatal engine error (the lane needs a restart)",
-               [({}, 0 if eng.get("fatal") is None else 1)])
-    return "\n".join(out) + "\n"
+        fam.append(("hrm_engine_fatal", "gauge", "1 after a fatal engine error (the lane needs a restart)",
+                    [({}, 0 if eng.get("fatal") is None else 1)]))
+    return exposition(fam)
 
 
 def create_app(state: ServiceState):

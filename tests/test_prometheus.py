@@ -43,3 +43,27 @@ def test_metrics_endpoint_over_http():
     req = fam["hrm_lane_requests"].samples[0].value
     by_mode = {s.labels["mode"]: s.value for s in fam["hrm_lane_requests_by_mode"].samples}
     assert up == 1 and req == 1 and by_mode["deepseek_only"] == 1
+
+
+def test_router_metrics_count_failover_and_503():
+    from hrm_flashrenderer_b200.serving import router as rt
+
+    def fake_post(url, payload, timeout):
+        if url.startswith("http://c"):
+            raise RuntimeError("lane down")
+        return {"ok": True, "text": "t", "mode": payload["mode"]}, 3
+
+    st = rt.RouterState()
+    st.backends = {"solo_22gb": rt.Backend("solo_22gb", "http://a:1"),
+                   "nvlink_pair": rt.Backend("nvlink_pair", "http://b:2"),
+                   "solo_3080": rt.Backend("solo_3080", "http://c:3")}
+    st.post = fake_post
+    with LiveServer(rt.create_app(st)) as srv:
+        post(srv.url + "/v1/generate", {"prompt": "short", "max_new_tokens": 50})                  # fails over
+        post(srv.url + "/v1/generate", {"prompt": "short", "max_new_tokens": 50, "allow_failover": False})  # 503
+        with urllib.request.urlopen(srv.url + "/metrics", timeout=10) as r:
+            fam = _families(r.read().decode())
+    one = lambda n: fam[n].samples[0].value
+    by_lane = lambda n: {s.labels["lane"]: s.value for s in fam[n].samples}
+    assert one("hrm_router_requests") == 2 and one("hrm_router_failovers") == 1 and one("hrm_router_all_failed") == 1
+    assert by_lane("hrm_router_routed")["nvlink_pair"] == 1 and by_lane("hrm_router_lane_errors")["solo_3080"] == 2
