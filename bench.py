@@ -249,7 +249,20 @@ def run_reference(a):
         dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
     from types import SimpleNamespace
+    # The reference's compiled attention extension is never loaded: its D=128 kernel stores WMMA accumulators into
+    # a per-thread local array (csrc/flash_attn_sm75.cu:310-311, :390-391).  wmma.store is defined only for global
+    # or shared addresses, and the sm_100 build raised "unspecified launch failure" on the driver's B200s at every
+    # N.  A None entry in sys.modules makes `from . import _ext` raise ImportError, so flashattention_custom.ops
+    # takes its own PyTorch fallbacks (ops.py:19-72): the reference as `pip install` builds it on a host without
+    # the extension.
+    sys.modules["flashattention_custom._ext"] = None
     import flashattention_custom.ops as fops
+    if getattr(fops, "_HAS_EXT", False):
+        _emit(rank, {"impl": "reference", "unavailable": "refusing to run the reference's sm75 attention extension "
+                     "(faulted on B200: unspecified launch failure)"})
+        if world > 1:
+            dist.destroy_process_group()
+        return
     from engine.llama_tp import TPLlamaForCausalLM, greedy_select_token_distributed
     from hrm_flashrenderer_b200.utils.clocks import ClockSampler, visible_gpu_indices
     from hrm_flashrenderer_b200.config import get_preset
@@ -326,7 +339,8 @@ def run_reference(a):
         "vs_baseline": None, "dtype": "fp16 (reference TP path has fp16 weights)",
         "data": "synthetic random-token prompts, random-init weights (reference __init__ N(0,0.02))",
         "config": {"model": c.name, "global_batch": a.batch, "seq_len": a.ctx, "parallelism": f"tp{world}",
-                   "l2": "inputs larger than L2", "attention_ext": bool(getattr(fops, "_HAS_EXT", False))},
+                   "l2": "inputs larger than L2", "attention_ext": bool(getattr(fops, "_HAS_EXT", False)),
+                   "attention": "reference PyTorch fallback (ops.py); its CUDA extension is not run on B200"},
         "p50_ttft_ms": round(ttft, 2), "impl": "reference", "clocks": clocks,
         "e2e": {"value": a.batch * a.steps / wall, "unit": "tok/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 8 * a.batch, "api": "reference decode loop (host syncs inside)"},

@@ -33,29 +33,46 @@ FALLBACK_SNIPPETS = 6
 FALLBACK_QUOTE_CHARS = 240
 
 
+class RetrievalError(RuntimeError):
+    """The ``hrm`` retrieval step did not produce a usable result."""
+
+
 def hrm_query(hrm_bin: str, model_dir: str, prompt: str, top_k: int = 5, top_m: int = 400, k: int = 8,
               lam_num: int = 7, lam_den: int = 10, timeout_s: Optional[float] = 30.0) -> Dict[str, Any]:
-    cmd = [hrm_bin, "query", "--model", model_dir, "--format", "json", "--top-k", str(top_k), "--top-m", str(top_m),
-           "--k", str(k), "--lam-num", str(lam_num), "--lam-den", str(lam_den), "--prompt", prompt]
-    p = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout_s)
-    if p.returncode != 0:
-        raise RuntimeError(f"HRM query failed (code={p.returncode}): {p.stderr.strip()}")
+    """One ``hrm query`` in JSON mode.  The prompt goes through standard input (no argv length limit, no shell
+    quoting); the options are the ranking knobs of the reference renderer (``renderer/hrm_render.py:39-64``)."""
+    opts = {"--model": model_dir, "--format": "json", "--top-k": top_k, "--top-m": top_m, "--k": k,
+            "--lam-num": lam_num, "--lam-den": lam_den}
+    argv = [hrm_bin, "query", "--prompt-stdin"]
+    for flag, val in opts.items():
+        argv += [flag, str(val)]
+    done = subprocess.run(argv, input=prompt.encode("utf-8"), stdout=subprocess.PIPE, stderr=subprocess.PIPE,
+                          timeout=timeout_s)
+    out = done.stdout.decode("utf-8", "replace")
+    if done.returncode != 0:
+        err = done.stderr.decode("utf-8", "replace").strip()
+        raise RetrievalError(f"hrm query exited with status {done.returncode}" + (f": {err}" if err else ""))
     try:
-        return json.loads(p.stdout)
+        res = json.loads(out)
     except json.JSONDecodeError as e:
-        raise RuntimeError(f"HRM returned non-JSON: {p.stdout[:1000]}") from e
+        raise RetrievalError(f"hrm query printed {len(out)} bytes that are not JSON ({out[:200]!r}...)") from e
+    if not isinstance(res, dict):
+        raise RetrievalError(f"hrm query printed a JSON {type(res).__name__}, expected an object")
+    return res
+
+
+def _clip(text: str, limit: int) -> str:
+    """At most ``limit`` characters of ``text``; a clipped snippet loses its trailing blanks and ends in an
+    ellipsis, so the model can tell it was cut (quotes stay exact substrings of the clipped text)."""
+    return text if len(text) <= limit else text[:limit].rstrip() + "\u2026"
 
 
 def sources_block(chosen: List[Dict[str, Any]]) -> Tuple[str, Dict[str, str]]:
-    lines, src = ["[SOURCES]"], {}
-    for c in chosen:
-        sid, txt = str(c["sid"]), str(c.get("txt", ""))
-        if len(txt) > MAX_SNIPPET_CHARS:
-            txt = txt[:MAX_SNIPPET_CHARS].rstrip() + "…"
-        src[sid] = txt
-        lines.append(f"{sid}: {txt}")
-    lines.append("[/SOURCES]")
-    return "\n".join(lines), src
+    """The ``[SOURCES]`` block shown to the renderer and the snippet text of every id, as shown (clipped to
+    ``MAX_SNIPPET_CHARS``).  Quote validation runs against exactly the text the model saw."""
+    shown = {str(c["sid"]): _clip(str(c.get("txt", "")), MAX_SNIPPET_CHARS) for c in chosen}
+    body = [f"{sid}: {txt}" for sid, txt in shown.items()]
+    return "\n".join(["[SOURCES]", *body, "[/SOURCES]"]), shown
 
 
 def first_json_object(text: str) -> Dict[str, Any]:
@@ -90,39 +107,55 @@ def first_json_object(text: str) -> Dict[str, Any]:
     raise ValueError("no json object found")
 
 
-def validate(obj: Any, sources: Dict[str, str]) -> Tuple[bool, str]:
+def grounding_problems(obj: Any, sources: Dict[str, str]) -> List[str]:
+    """Every way in which a rendered object breaks the grounding contract, in reading order (empty list: valid).
+
+    The contract: a JSON object whose ``answer`` is a string, whose ``citations`` list names only shown snippet
+    ids, and whose ``quotes`` are ``{id, quote}`` objects with a non-blank quote that occurs verbatim in the cited
+    snippet."""
     if not isinstance(obj, dict):
-        return False, "not a dict"
+        return [f"rendered value is a {type(obj).__name__}, not an object"]
+    found: List[str] = []
     if not isinstance(obj.get("answer"), str):
-        return False, "missing answer"
+        found.append("answer: missing or not a string")
     cits = obj.get("citations", [])
-    if not isinstance(cits, list):
-        return False, "citations not list"
-    for sid in cits:
-        if sid not in sources:
-            return False, f"unknown citation {sid}"
+    if isinstance(cits, list):
+        found += [f"citation {c!r}: no such source" for c in cits if c not in sources]
+    else:
+        found.append("citations: not a list")
     quotes = obj.get("quotes", [])
     if not isinstance(quotes, list):
-        return False, "quotes not list"
-    for q in quotes:
+        return found + ["quotes: not a list"]
+    for n, q in enumerate(quotes):
         if not isinstance(q, dict):
-            return False, "quote item not dict"
-        sid, qt = q.get("id"), q.get("quote")
+            found.append(f"quotes[{n}]: not an object")
+            continue
+        sid, text = q.get("id"), q.get("quote")
         if sid not in sources:
-            return False, f"quote id unknown {sid}"
-        if not isinstance(qt, str) or not qt.strip():
-            return False, f"empty quote for {sid}"
-        if qt not in sources[sid]:
-            return False, f"quote not substring for {sid}"
-    return True, "ok"
+            found.append(f"quotes[{n}]: source {sid!r} was not shown")
+        elif not isinstance(text, str) or not text.strip():
+            found.append(f"quotes[{n}]: blank quote for {sid}")
+        elif text not in sources[sid]:
+            found.append(f"quotes[{n}]: text is not verbatim in {sid}")
+    return found
+
+
+def validate(obj: Any, sources: Dict[str, str]) -> Tuple[bool, str]:
+    """``(True, "ok")`` for a grounded object, else ``(False, problems joined by '; ')``."""
+    found = grounding_problems(obj, sources)
+    return (not found, "; ".join(found) if found else "ok")
 
 
 def extractive_answer(chosen: List[Dict[str, Any]]) -> Dict[str, Any]:
-    take = chosen[:FALLBACK_SNIPPETS]
-    return {"answer": "\n".join(f"[{c['sid']}] {c.get('txt_c', c.get('txt', ''))}" for c in take),
-            "citations": [c["sid"] for c in take],
-            "quotes": [{"id": c["sid"], "quote": str(c.get("txt", ""))[:FALLBACK_QUOTE_CHARS]} for c in take],
-            "mode": "fallback_extractive"}
+    """The answer used when rendering fails: the first ``FALLBACK_SNIPPETS`` retrieved snippets, each cited and
+    quoted by its first ``FALLBACK_QUOTE_CHARS`` characters (``txt_c``, the compact text, preferred in the answer)."""
+    lines, cited, quoted = [], [], []
+    for c in chosen[:FALLBACK_SNIPPETS]:
+        sid, full = c["sid"], str(c.get("txt", ""))
+        lines.append(f"[{sid}] {c.get('txt_c', full)}")
+        cited.append(sid)
+        quoted.append({"id": sid, "quote": full[:FALLBACK_QUOTE_CHARS]})
+    return {"answer": "\n".join(lines), "citations": cited, "quotes": quoted, "mode": "fallback_extractive"}
 
 
 def chat_prompt(system: str, user: str) -> str:

@@ -15,6 +15,7 @@ Semantics of the reference router (``hrm_flash/router.py:154-575``), retargeted 
 """
 import argparse
 import asyncio
+import contextlib
 import json
 import os
 import sys
@@ -79,37 +80,50 @@ class RouterState:
         self.all_failed_total = 0               # 503: every candidate lane failed
 
 
-def http_json_get(url: str, timeout_s: float) -> Tuple[Dict[str, Any], int]:
-    t0 = time.perf_counter()
-    with urllib.request.urlopen(urllib.request.Request(url, method="GET"), timeout=timeout_s) as r:
-        raw = r.read()
-    ms = int((time.perf_counter() - t0) * 1000)
-    obj = json.loads(raw.decode("utf-8"))
+class LaneCallError(RuntimeError):
+    """A lane request that produced no usable JSON object; ``status`` is the lane's HTTP status when it answered
+    with an error status, else None (no answer: refused, timed out, unreadable)."""
+
+    def __init__(self, url: str, reason: str, status: Optional[int] = None):
+        super().__init__(f"{url}: {reason}")
+        self.url, self.status = url, status
+
+
+def _lane_call(method: str, url: str, payload: Optional[Dict[str, Any]], timeout_s: float
+               ) -> Tuple[Dict[str, Any], int]:
+    """One JSON request to a lane.  Returns the decoded object and the round trip in whole milliseconds; every
+    failure (error status with the lane's own explanation, transport error, non-object body) is a LaneCallError,
+    which the router counts against the lane and answers by trying the next one."""
+    body = None if payload is None else json.dumps(payload).encode("utf-8")
+    headers = {} if body is None else {"Content-Type": "application/json"}
+    started = time.perf_counter()
+    try:
+        with urllib.request.urlopen(urllib.request.Request(url, data=body, method=method, headers=headers),
+                                    timeout=timeout_s) as resp:
+            raw = resp.read()
+    except urllib.error.HTTPError as e:
+        why = ""
+        with contextlib.suppress(Exception):
+            why = e.read().decode("utf-8", errors="replace").strip()
+        raise LaneCallError(url, f"status {e.code}" + (f" ({why})" if why else ""), status=e.code) from e
+    except (OSError, ValueError) as e:   # refused, reset, timeout (socket.timeout is an OSError), bad URL
+        raise LaneCallError(url, f"no answer: {type(e).__name__}: {e}") from e
+    elapsed_ms = int((time.perf_counter() - started) * 1000)
+    try:
+        obj = json.loads(raw.decode("utf-8"))
+    except (UnicodeDecodeError, json.JSONDecodeError) as e:
+        raise LaneCallError(url, f"answer is not JSON ({len(raw)} bytes)") from e
     if not isinstance(obj, dict):
-        raise RuntimeError(f"invalid JSON shape from {url}")
-    return obj, ms
+        raise LaneCallError(url, f"answer is a JSON {type(obj).__name__}, expected an object")
+    return obj, elapsed_ms
+
+
+def http_json_get(url: str, timeout_s: float) -> Tuple[Dict[str, Any], int]:
+    return _lane_call("GET", url, None, timeout_s)
 
 
 def http_json_post(url: str, payload: Dict[str, Any], timeout_s: float) -> Tuple[Dict[str, Any], int]:
-    req = urllib.request.Request(url, data=json.dumps(payload).encode("utf-8"), method="POST",
-                                 headers={"Content-Type": "application/json"})
-    t0 = time.perf_counter()
-    try:
-        with urllib.request.urlopen(req, timeout=timeout_s) as r:
-            raw = r.read()
-    except urllib.error.HTTPError as e:
-        try:
-            detail = e.read().decode("utf-8", errors="replace")
-        except Exception:
-            detail = str(e)
-        raise RuntimeError(f"HTTP {e.code} from backend {url}: {detail}") from e
-    except Exception as e:
-        raise RuntimeError(f"request to backend failed ({url}): {e}") from e
-    ms = int((time.perf_counter() - t0) * 1000)
-    obj = json.loads(raw.decode("utf-8"))
-    if not isinstance(obj, dict):
-        raise RuntimeError(f"invalid JSON shape from backend {url}")
-    return obj, ms
+    return _lane_call("POST", url, payload, timeout_s)
 
 
 def normalize_backend_name(v: Optional[str]) -> Optional[str]:

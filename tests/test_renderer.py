@@ -39,11 +39,37 @@ def test_validation_rules():
     ok = {"answer": "two soldiers", "citations": ["0001:0000"],
           "quotes": [{"id": "0001:0000", "quote": "guarded at night"}]}
     assert R.validate(ok, src) == (True, "ok")
-    assert R.validate({**ok, "citations": ["9999:0000"]}, src)[1].startswith("unknown citation")
-    assert R.validate({**ok, "quotes": [{"id": "0001:0000", "quote": "guarded by day"}]}, src)[1].startswith(
-        "quote not substring")
-    assert R.validate({**ok, "quotes": [{"id": "0001:0000", "quote": "  "}]}, src)[1].startswith("empty quote")
-    assert R.validate({"citations": []}, src)[1] == "missing answer"
+    assert R.validate({**ok, "citations": ["9999:0000"]}, src)[1] == "citation '9999:0000': no such source"
+    assert R.validate({**ok, "quotes": [{"id": "0001:0000", "quote": "guarded by day"}]}, src)[1] == \
+        "quotes[0]: text is not verbatim in 0001:0000"
+    assert R.validate({**ok, "quotes": [{"id": "0001:0000", "quote": "  "}]}, src)[1] == \
+        "quotes[0]: blank quote for 0001:0000"
+    assert R.validate({"citations": []}, src) == (False, "answer: missing or not a string")
+    assert R.validate([1], src) == (False, "rendered value is a list, not an object")
+    # every problem is reported, in reading order
+    bad = {"answer": 3, "citations": ["nope"], "quotes": ["x", {"id": "gone", "quote": "q"}]}
+    assert R.grounding_problems(bad, src) == [
+        "answer: missing or not a string", "citation 'nope': no such source", "quotes[0]: not an object",
+        "quotes[1]: source 'gone' was not shown"]
+
+
+def test_hrm_query_errors(tmp_path):
+    fake = tmp_path / "hrm"
+    fake.write_text("#!/bin/sh\ncat > /dev/null\necho \"$HRM_FAKE_OUT\"\nexit $HRM_FAKE_RC\n")
+    fake.chmod(0o755)
+    env = os.environ
+    try:
+        os.environ["HRM_FAKE_OUT"], os.environ["HRM_FAKE_RC"] = '{"cids": [3], "chosen": []}', "0"
+        assert R.hrm_query(str(fake), "m", "q")["cids"] == [3]
+        os.environ["HRM_FAKE_OUT"] = "not json"
+        with pytest.raises(R.RetrievalError, match="not JSON"):
+            R.hrm_query(str(fake), "m", "q")
+        os.environ["HRM_FAKE_OUT"], os.environ["HRM_FAKE_RC"] = "", "3"
+        with pytest.raises(R.RetrievalError, match="exited with status 3"):
+            R.hrm_query(str(fake), "m", "q")
+    finally:
+        env.pop("HRM_FAKE_OUT", None)
+        env.pop("HRM_FAKE_RC", None)
 
 
 def test_render_answer_paths():

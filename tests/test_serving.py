@@ -184,3 +184,51 @@ def test_router_failover_and_503():
         assert calls[-1][1]["mode"] == "deepseek_only" and calls[-1][1]["prompt"] == "hi"
         code, body = post(srv.url + "/v1/completions", {"prompt": "x", "stream": True})
         assert code == 200 and body.rstrip().endswith("data: [DONE]") and '"text_completion"' in body
+
+
+def test_lane_call_errors_and_success():
+    """The router's lane transport: JSON object answers pass, error statuses keep the lane's explanation, and a
+    non-object body or an unreachable lane is a LaneCallError."""
+    import http.server
+    import threading
+    from hrm_flashrenderer_b200.serving import router as RT
+
+    class H(http.server.BaseHTTPRequestHandler):
+        def log_message(self, *a):
+            pass
+
+        def _send(self, code, body):
+            self.send_response(code)
+            self.send_header("Content-Length", str(len(body)))
+            self.end_headers()
+            self.wfile.write(body)
+
+        def do_GET(self):
+            self._send(200, b"[1, 2]" if self.path == "/list" else b'{"ok": true}')
+
+        def do_POST(self):
+            n = int(self.headers.get("Content-Length", "0"))
+            got = json.loads(self.rfile.read(n))
+            if self.path == "/fail":
+                self._send(503, b"lane busy")
+            else:
+                self._send(200, json.dumps({"echo": got}).encode())
+
+    srv = http.server.ThreadingHTTPServer(("127.0.0.1", 0), H)
+    th = threading.Thread(target=srv.serve_forever, daemon=True)
+    th.start()
+    base = f"http://127.0.0.1:{srv.server_address[1]}"
+    try:
+        obj, ms = RT.http_json_post(base + "/gen", {"a": 1}, 5.0)
+        assert obj == {"echo": {"a": 1}} and ms >= 0
+        assert RT.http_json_get(base + "/h", 5.0)[0] == {"ok": True}
+        with pytest.raises(RT.LaneCallError) as ei:
+            RT.http_json_post(base + "/fail", {}, 5.0)
+        assert ei.value.status == 503 and "lane busy" in str(ei.value)
+        with pytest.raises(RT.LaneCallError, match="expected an object"):
+            RT.http_json_get(base + "/list", 5.0)
+    finally:
+        srv.shutdown()
+    with pytest.raises(RT.LaneCallError, match="no answer") as ei:
+        RT.http_json_get(base + "/h", 1.0)
+    assert ei.value.status is None
