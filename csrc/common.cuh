@@ -13,6 +13,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -347,6 +348,33 @@ HRM_DEVINL uint32_t float_order(float f) {
 }
 HRM_DEVINL unsigned long long argmax_key(float v, uint32_t idx) {
   return ((unsigned long long)float_order(v) << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
+}
+
+// ---------------------------------------------------------------- host: per-device set-up
+// cudaFuncSetAttribute acts on the CURRENT device only, so a process that drives several GPUs must raise a kernel's
+// dynamic shared-memory limit once on each of them.  One flag per device and per kernel (the template below is
+// instantiated once per kernel symbol); the flags are atomics because launches may come from several host threads.
+// A racing second call of cudaFuncSetAttribute is harmless (same value), so no lock is needed.
+constexpr int kMaxDevices = 64;
+
+inline int current_device_or_throw() {
+  int d = 0;
+  const cudaError_t e = cudaGetDevice(&d);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cudaGetDevice failed: ") + cudaGetErrorString(e));
+  if (d < 0 || d >= kMaxDevices) throw std::runtime_error("device ordinal beyond the supported 64 devices");
+  return d;
+}
+
+template <typename... KArgs>
+inline void ensure_smem_limit(void (*kern)(KArgs...), int bytes) {
+  static std::atomic<bool> done[kMaxDevices];   // zero-initialised (static storage)
+  const int d = current_device_or_throw();
+  if (done[d].load(std::memory_order_acquire)) return;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("cudaFuncSetAttribute(max dynamic shared memory) failed: ") +
+                             cudaGetErrorString(e));
+  done[d].store(true, std::memory_order_release);
 }
 
 // ---------------------------------------------------------------- host: launches

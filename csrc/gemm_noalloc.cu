@@ -75,7 +75,12 @@ extern "C" int hrm_w8a16_gemm_f16_noalloc(const void* x, int ldx, const int8_t* 
   DeviceScratch* s = nullptr;
   if (const int rc = setup_device(dev, &s)) return rc;
 
-  const hrm::GemmPlan p = hrm::gemm_plan(M, N, K, 0);
+  hrm::GemmPlan p{};
+  try {
+    p = hrm::gemm_plan(M, N, K, 0);
+  } catch (const std::exception& e) {
+    return fail(HRM_NOALLOC_ERR_SETUP, e.what());
+  }
   if (p.ws_floats > HRM_NOALLOC_MAX_WS_FLOATS || p.counters > HRM_NOALLOC_MAX_TILES) {
     std::snprintf(g_err, sizeof(g_err),
                   "shape M=%d N=%d K=%d needs %zu scratch floats and %d tickets; the static limits are %u and %d",

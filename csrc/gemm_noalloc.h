@@ -18,6 +18,9 @@
 //    device keeps the static scratch. Make that first call before any stream capture begins.
 //  * Scratch limit: the stream-K plan of (M, N, K) may need at most HRM_NOALLOC_MAX_WS_FLOATS floats of partial sums
 //    and HRM_NOALLOC_MAX_TILES output tiles; larger plans are rejected with HRM_NOALLOC_ERR_TOO_BIG and a message.
+//    On a 148-SM B200 every decode GEMM of a 70B-class model fits for M <= 16 tokens (the widest, the 128256-row
+//    lm_head at K = 8192, needs 4,104,192 floats).  From M = 17 the token tile doubles (32 columns) and that
+//    lm_head needs about 8.2M floats, so it is rejected; the hidden-size projections still fit up to M = 64.
 //  * What must start at zero: the per-tile tickets. They live in static storage, which is zero when the module
 //    loads, and every launch returns each ticket it used to zero. The partial-sum scratch needs no initial value
 //    (every partial is written before it is read). A launch that gave up on a bounded wait can leave tickets

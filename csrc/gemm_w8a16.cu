@@ -535,14 +535,21 @@ bool gemm_m_fastest() {
 void set_gemm_m_fastest(bool on) { g_mfast = on ? 1 : 0; }
 
 int gemm_sm_count() {
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
+  // Per device: a process may drive GPUs with different SM counts.  Without a usable device (host-side planning on
+  // a machine with no GPU) the plan is made for a 148-SM B200.
+  static std::atomic<int> sms[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();   // clear the sticky-free error this query left behind
+    return 148;
   }
-  return sms;
+  int n = sms[dev].load(std::memory_order_relaxed);
+  if (n <= 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      throw std::runtime_error("cudaDeviceGetAttribute(multiprocessor count) failed");
+    sms[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
 }
 
 
@@ -581,11 +588,7 @@ template <int BN, int EPI>
 static void launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, const GemmPlan& p,
                       cudaStream_t stream) {
   using S = GemmSmem<BN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(w8a16_gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
-    attr_set = true;
-  }
+  ensure_smem_limit(w8a16_gemm_kernel<BN, EPI>, S::kAlloc);
   launch_maybe_pdl(w8a16_gemm_kernel<BN, EPI>, dim3(p.ctas), dim3(kThreads), (size_t)S::kAlloc, stream, tw, tx, a);
 }
 

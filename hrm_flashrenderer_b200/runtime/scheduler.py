@@ -2,8 +2,11 @@
 
 One background thread owns the engine (and its CUDA graphs).  Each iteration it
 
-1. admits waiting requests while the decode batch has room and the KV pool has blocks (chunked prefill of up to
-   ``prefill_chunk`` prompt tokens per forward, several requests per chunk), which yields their first token;
+1. admits waiting requests while the decode batch has room and the KV pool has blocks, and runs ONE prefill forward
+   over the admitted prompts: up to ``prefill_chunk`` prompt tokens when nothing is decoding, up to
+   ``interleave_chunk`` while other requests decode (a long prompt is prefilled over several iterations, so it
+   delays each decode step by one bounded chunk instead of stalling the batch for its whole prefill).  A request
+   whose prompt is complete yields its first token and joins the decode batch;
 2. runs one graph-replayed decode step for every running request (the batch is re-staged on the device only when
    its membership changed; otherwise the sampled tokens are fed back on the device);
 3. streams tokens to the requests, retires finished ones (EOS or ``max_new_tokens``) and frees their blocks.
@@ -61,14 +64,19 @@ class GenRequest:
 
 class Scheduler:
     def __init__(self, engine, max_batch: Optional[int] = None, prefill_chunk: Optional[int] = None,
-                 idle_sleep_s: float = 0.0005):
+                 idle_sleep_s: float = 0.0005, interleave_chunk: Optional[int] = 512):
+        """``interleave_chunk``: prompt tokens prefilled per iteration while requests are decoding (None or 0:
+        admitted prompts are prefilled to completion before the next decode step)."""
         self.engine = engine
         self.max_batch = int(max_batch or engine.ecfg.max_batch)
         self.prefill_chunk = int(prefill_chunk or engine.ecfg.prefill_chunk)
+        self.interleave_chunk = int(interleave_chunk or 0)
         self.idle_sleep_s = idle_sleep_s
         self._inbox: "queue.Queue[GenRequest]" = queue.Queue()
         self._waiting: Deque[GenRequest] = collections.deque()
+        self._prefilling: List[GenRequest] = []   # admitted, prompt partly in the KV cache (r._done tokens)
         self._running: List[GenRequest] = []
+        self.prefill_calls: List[int] = []        # prompt tokens of each prefill forward (bounded record)
         self._stop = threading.Event()
         self._thread: Optional[threading.Thread] = None
         self._next_rid = 0
@@ -138,6 +146,7 @@ class Scheduler:
         it = sorted(self.itls)
         pct = lambda a, q: (a[min(len(a) - 1, int(q * len(a)))] * 1e3) if a else None
         return {"queue_depth": len(self._waiting) + self._inbox.qsize(), "batch_size": len(self._running),
+                "prefilling": len(self._prefilling),
                 "completed": self.completed, "generated_tokens": self.generated_tokens,
                 "tok_per_s": self.generated_tokens / el, "ttft_p50_ms": pct(tt, 0.5), "ttft_p99_ms": pct(tt, 0.99),
                 "itl_p50_ms": pct(it, 0.5), "last_error": self.last_error, "fatal": self.fatal}
@@ -161,44 +170,54 @@ class Scheduler:
                 self.last_error = f"on_token callback of request {r.rid}: {e!r}"
         return len(r.tokens) >= r.max_new_tokens or (r.stop_on_eos and tok in self.eos)
 
+    def _full_need(self, r: GenRequest) -> int:
+        """Blocks ``r`` still has to take to hold prompt + max_new_tokens + 1 positions (see _decode's staging)."""
+        eng = self.engine
+        total = min(eng.max_blocks * eng.block_size, len(r.prompt_ids) + r.max_new_tokens + 1)
+        return eng.bm.blocks_needed(r.seq_id, total)
+
     def _admit(self) -> bool:
+        """Admission plus one prefill forward; True when a prefill ran."""
         while True:
             try:
                 self._waiting.append(self._inbox.get_nowait())
             except queue.Empty:
                 break
-        if not self._waiting or len(self._running) >= self.max_batch:
-            return False
-        batch, used = [], 0
         eng = self.engine
-        while self._waiting and len(self._running) + len(batch) < self.max_batch and used < self.prefill_chunk:
+        # every admitted request's whole reservation is counted, so staging never runs out of blocks
+        committed = self._pending_growth() + sum(self._full_need(r) for r in self._prefilling)
+        while self._waiting and len(self._running) + len(self._prefilling) < self.max_batch:
             r = self._waiting[0]
-            # a sequence ends up holding prompt + max_new_tokens + 1 positions (see _decode's reservation); the
-            # running ones were grown to that at their first staging, so free blocks are the whole budget
-            full = lambda q: min(eng.max_blocks, eng.bm.blocks_needed(-1, len(q.prompt_ids) + q.max_new_tokens + 1))
-            if full(r) > eng.bm.free_blocks - sum(full(b) for b in batch) - self._pending_growth():
+            if self._full_need(r) > eng.bm.free_blocks - committed:
                 break
             self._waiting.popleft()
             r.seq_id = eng.new_seq()
-            batch.append(r)
-            used += len(r.prompt_ids)
-        if not batch:
+            r._done = 0
+            committed += self._full_need(r)
+            self._prefilling.append(r)
+        if not self._prefilling:
             return False
-        try:
-            firsts = eng.prefill([(r.seq_id, r.prompt_ids) for r in batch])
-        except BaseException as e:   # these requests left the queue: fail them and return their blocks here
-            for r in batch:
-                try:
-                    r.future.set_exception(e)
-                except Exception:
-                    pass
-                try:
-                    eng.release(r.seq_id)
-                except Exception:
-                    pass
-            raise
+        budget = self.prefill_chunk
+        if self._running and self.interleave_chunk > 0:
+            budget = min(budget, self.interleave_chunk)
+        chunks, used = [], 0
+        for r in self._prefilling:
+            if used >= budget:
+                break
+            take = min(len(r.prompt_ids) - r._done, budget - used)
+            chunks.append((r, take))
+            used += take
+        # a failure here propagates to the loop, which fails every request that holds engine state
+        firsts = eng.prefill([(r.seq_id, r.prompt_ids[r._done:r._done + n]) for r, n in chunks])
+        if len(self.prefill_calls) < 4096:
+            self.prefill_calls.append(used)
         now = time.perf_counter()
-        for r, t in zip(batch, firsts):
+        done = []
+        for (r, n), t in zip(chunks, firsts):
+            r._done += n
+            if r._done < len(r.prompt_ids):
+                continue   # the token after a partial prompt is not a generated token
+            done.append(r)
             r.first_token_at = now
             self.ttfts.append(now - r.arrival)
             r._last_tok_at = now
@@ -207,6 +226,9 @@ class Scheduler:
                 self._finish(r)
             else:
                 self._running.append(r)
+        if done:
+            gone = {id(r) for r in done}
+            self._prefilling = [r for r in self._prefilling if id(r) not in gone]
         return True
 
     def _pending_growth(self) -> int:
@@ -254,19 +276,24 @@ class Scheduler:
                     time.sleep(self.idle_sleep_s)
                 if admitted or self._running:
                     self._fails = 0
-            except BaseException as e:   # fail the in-flight requests, keep serving new ones unless fatal
+            except BaseException as e:
+                # fail the requests that hold engine state (decoding or partly prefilled); queued requests never
+                # reached the engine and stay queued, unless the engine cannot serve any more
                 self.last_error = repr(e)
                 self._fails += 1
-                for r in self._running + list(self._waiting):
+                fatal = is_context_fatal(e) or self._fails >= self.max_consecutive_failures
+                victims = self._running + self._prefilling + (list(self._waiting) if fatal else [])
+                for r in victims:
                     if not r.future.done():
                         r.future.set_exception(e)
-                    try:
-                        self.engine.release(r.seq_id)
-                    except Exception:
-                        pass
-                self._running, staged = [], False
-                self._waiting.clear()
-                if is_context_fatal(e) or self._fails >= self.max_consecutive_failures:
+                    if r.seq_id >= 0:
+                        try:
+                            self.engine.release(r.seq_id)
+                        except Exception:
+                            pass
+                self._running, self._prefilling, staged = [], [], False
+                if fatal:
+                    self._waiting.clear()
                     self.fatal = repr(e)
                     break
         if self.fatal is not None:   # nothing queued waits for a loop that is gone

@@ -126,3 +126,89 @@ def test_transient_errors_keep_serving_until_the_limit():
         assert not sched.alive() and "broken" in sched.metrics()["fatal"]
     finally:
         sched.stop()
+
+
+class _Recorder:
+    """Wraps an engine and records the order of prefill forwards (prompt tokens) and decode steps."""
+
+    def __init__(self, eng):
+        self.eng, self.log = eng, []
+
+    def __getattr__(self, k):
+        return getattr(self.eng, k)
+
+    def prefill(self, seqs):
+        self.log.append(("prefill", sum(len(t) for _, t in seqs)))
+        return self.eng.prefill(seqs)
+
+    def decode_step(self, g):
+        self.log.append(("decode", 0))
+        return self.eng.decode_step(g)
+
+
+def test_long_prompt_prefill_interleaves_with_decode():
+    """A long prompt that arrives while another request decodes is prefilled in interleave-sized chunks with decode
+    steps in between, and both requests still produce exactly their isolated greedy tokens."""
+    import time
+    g = torch.Generator().manual_seed(3)
+    short = torch.randint(0, 1024, (8,), generator=g).tolist()
+    long_ = torch.randint(0, 1024, (100,), generator=g).tolist()
+    ref_eng = _engine()
+    ref = [ref_eng.generate([p], n, stop_on_eos=False)[0] for p, n in ((short, 40), (long_, 5))]
+    rec = _Recorder(_engine())
+    sched = Scheduler(rec, interleave_chunk=16).start()
+    try:
+        h1 = sched.submit(short, 40, stop_on_eos=False)
+        t0 = time.time()
+        while not h1.tokens and time.time() - t0 < 60:   # the short request is decoding
+            time.sleep(0.001)
+        h2 = sched.submit(long_, 5, stop_on_eos=False)
+        got = [h1.future.result(timeout=120), h2.future.result(timeout=120)]
+    finally:
+        sched.stop()
+    assert got == ref
+    pre = [i for i, (k, _) in enumerate(rec.log) if k == "prefill"]
+    long_chunks = [rec.log[i][1] for i in pre[1:]]
+    assert sum(long_chunks) == 100 and max(long_chunks) <= 16, rec.log
+    # a decode step between consecutive chunks of the long prompt
+    assert all(any(k == "decode" for k, _ in rec.log[a + 1:b]) for a, b in zip(pre[1:], pre[2:])), rec.log
+
+
+class _FlakyEngine:
+    """Engine wrapper whose decode step raises once (a transient, non-fatal error)."""
+
+    def __init__(self, eng):
+        self.eng, self.failed = eng, False
+
+    def __getattr__(self, k):
+        return getattr(self.eng, k)
+
+    def decode_step(self, g):
+        if not self.failed:
+            self.failed = True
+            raise RuntimeError("transient decode failure")
+        return self.eng.decode_step(g)
+
+
+def test_transient_decode_error_fails_only_running_requests():
+    """A non-fatal error fails (and frees) only the requests that were in the engine; requests still queued are
+    served afterwards."""
+    import pytest
+    g = torch.Generator().manual_seed(5)
+    reqs = [torch.randint(0, 1024, (12,), generator=g).tolist() for _ in range(6)]
+    eng = _FlakyEngine(_engine())
+    sched = Scheduler(eng, max_batch=2)
+    handles = [sched.submit(p, 6, stop_on_eos=False) for p in reqs]   # queued before the loop starts
+    sched.start()
+    try:
+        outcomes = []
+        for h in handles:
+            try:
+                outcomes.append(len(h.future.result(timeout=120)))
+            except RuntimeError as e:
+                assert "transient decode failure" in str(e)
+                outcomes.append("failed")
+    finally:
+        sched.stop()
+    assert outcomes.count("failed") == 2 and outcomes[2:] == [6, 6, 6, 6]
+    assert sched.fatal is None and eng.bm.free_blocks == eng.bm.num_blocks

@@ -75,8 +75,19 @@ def test_noalloc_matches_torch_entry_point_twice(M, N, K):
     torch.testing.assert_close(out.float(), want, rtol=2e-2, atol=2e-2)
 
 
+MAX_WS_FLOATS, MAX_TILES = 4 * 1024 * 1024, 4096   # HRM_NOALLOC_MAX_WS_FLOATS / HRM_NOALLOC_MAX_TILES
+
+
+def _fits(M, N, K):
+    """Whether this GPU's stream-K plan of (M, N, K) fits the static scratch (the plan depends on the SM count)."""
+    p = ops.gemm_plan(M, N, K)
+    return p["ws_floats"] <= MAX_WS_FLOATS and p["counters"] <= MAX_TILES
+
+
 @pytest.mark.gpu
 def test_noalloc_rejects_plans_beyond_the_static_scratch():
+    """The expected answer comes from this GPU's own plan, so the test holds on any SM count.  Real buffers of the
+    full shape back the call, so an accepted plan would still run within bounds."""
     lib = _lib()
     dev = torch.device("cuda", 0)
     M, N, K = 256, 16384, 4096
@@ -84,5 +95,48 @@ def test_noalloc_rejects_plans_beyond_the_static_scratch():
     w = torch.zeros(N, K, dtype=torch.int8, device=dev)
     s = torch.ones(N, device=dev)
     out = torch.empty(M, N, dtype=torch.float16, device=dev)
-    assert _call(lib, x, w, s, out) == ERR_TOO_BIG
-    assert b"static limits" in lib.hrm_w8a16_noalloc_last_error()
+    rc = _call(lib, x, w, s, out)
+    torch.cuda.synchronize()
+    if _fits(M, N, K):
+        assert rc == 0, lib.hrm_w8a16_noalloc_last_error()
+    else:
+        assert rc == ERR_TOO_BIG
+        assert b"static limits" in lib.hrm_w8a16_noalloc_last_error()
+
+
+@pytest.mark.gpu
+def test_noalloc_accepts_the_70b_lm_head_at_16_tokens():
+    """The header's promise: every decode GEMM of a 70B-class model fits at up to 16 tokens, the widest being the
+    128256-row lm_head (K = 8192)."""
+    lib = _lib()
+    dev = torch.device("cuda", 0)
+    M, N, K = 16, 128256, 8192
+    assert _fits(M, N, K)
+    torch.manual_seed(3)
+    x = torch.randn(M, K, device=dev).half()
+    w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
+    s = torch.rand(N, device=dev) * 1e-3 + 1e-4
+    out = torch.empty(M, N, dtype=torch.float16, device=dev)
+    assert _call(lib, x, w, s, out) == 0, lib.hrm_w8a16_noalloc_last_error()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out.float(), ops.w8a16_linear(x, w, s).float(), rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_noalloc_on_a_second_device_after_the_first():
+    """Per-device set-up: the scratch address and the kernel's shared-memory limit are set on each device the first
+    time a call runs with it current, so a call on device 1 after device 0 works."""
+    lib = _lib()
+    for d in (0, 1):
+        with torch.cuda.device(d):
+            dev = torch.device("cuda", d)
+            torch.manual_seed(d)
+            x = torch.randn(16, 4096, device=dev).half()
+            w = torch.randint(-127, 128, (8192, 4096), dtype=torch.int8, device=dev)
+            s = torch.rand(8192, device=dev) * 1e-3 + 1e-4
+            out = torch.empty(16, 8192, dtype=torch.float16, device=dev)
+            assert _call(lib, x, w, s, out) == 0, lib.hrm_w8a16_noalloc_last_error()
+            torch.cuda.synchronize(dev)
+            want = x.float() @ (w.float() * s[:, None]).t()
+            torch.testing.assert_close(out.float(), want, rtol=2e-2, atol=2e-2)
