@@ -317,10 +317,44 @@ void prefill_attn_launch(const PrefillAttnArgs& a, cudaStream_t s) {
 // lower id); slices meet in atomicMax on the row's accumulator, which is order independent, so the result is
 // deterministic.  The CTA that takes the last ticket publishes the key / token and re-arms accumulator and ticket
 // (both start at zero).
+// Tensor-parallel exchange of one row's key (XCHG), run by the row's final CTA, thread 0: see ArgmaxXchg.
+HRM_DEVINL unsigned long long argmax_exchange_row(const ArgmaxXchg& x, int row, int M, unsigned long long mine) {
+  // this launch's epoch: every row's final thread reads it before taking a row ticket, and the counter only moves
+  // once all M rows have taken theirs
+  const int ep = *reinterpret_cast<volatile int*>(x.epoch) + 1;
+  const size_t slot = ((size_t)(ep & 1) * x.world + x.rank) * x.max_rows + row;
+  for (int d = 0; d < x.world; ++d) {
+    char* base = reinterpret_cast<char*>(x.peers[d]);
+    reinterpret_cast<unsigned long long*>(base + x.off_keys)[slot] = mine;
+  }
+  fence_acq_rel_sys();   // release pattern: the key stores above are visible before any of the flags below
+  for (int d = 0; d < x.world; ++d) {
+    char* base = reinterpret_cast<char*>(x.peers[d]);
+    st_relaxed_sys(reinterpret_cast<int*>(base + x.off_flags) + (size_t)x.rank * x.max_rows + row, ep);
+  }
+  char* own = reinterpret_cast<char*>(x.peers[x.rank]);
+  const int* flags = reinterpret_cast<const int*>(own + x.off_flags);
+  const unsigned long long* slots = reinterpret_cast<const unsigned long long*>(own + x.off_keys);
+  unsigned long long best = 0ull;
+  for (int r = 0; r < x.world; ++r) {   // max is order independent; rank order only fixes the reads
+    if (!wait_flag_acquire(flags + (size_t)r * x.max_rows + row, ep, x.status)) continue;
+    const unsigned long long k = __ldcg(slots + ((size_t)(ep & 1) * x.world + r) * x.max_rows + row);
+    best = k > best ? k : best;
+  }
+  __threadfence();
+  if (atomicAdd(x.row_ticket, 1) == M - 1) {   // last row of the launch: re-arm and advance the epoch
+    *x.row_ticket = 0;
+    *reinterpret_cast<volatile int*>(x.epoch) = ep;
+    __threadfence();
+  }
+  return best;
+}
+
+template <bool XCHG>
 __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ logits, int V, int ld, int chunk,
                                                      int vocab_start, unsigned long long* acc,
                                                      unsigned long long* ticket, unsigned long long* keys,
-                                                     int64_t* tokens) {
+                                                     int64_t* tokens, const ArgmaxXchg x) {
   pdl_wait();
   pdl_trigger();
   const int row = blockIdx.y;
@@ -371,6 +405,7 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ l
     best = atomicExch(&acc[row], 0ull);
     ticket[row] = 0ull;
   }
+  if constexpr (XCHG) best = argmax_exchange_row(x, row, (int)gridDim.y, best);
   if (keys) keys[row] = best ^ (1ull << 63);   // signed-int64 order == unsigned key order
   if (tokens) tokens[row] = (int64_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
 }
@@ -391,8 +426,25 @@ void argmax_launch(const float* logits, int M, int V, int ld, int vocab_start, u
   const int grid_x = (V + chunk - 1) / chunk;
   unsigned long long* acc = scratch;
   unsigned long long* ticket = scratch != nullptr ? scratch + kArgmaxMaxRows : nullptr;
-  launch_maybe_pdl(argmax_kernel, dim3(grid_x, M), dim3(256), 0, s, logits, V, ld, chunk, vocab_start, acc, ticket,
-                   keys, tokens);
+  launch_maybe_pdl(argmax_kernel<false>, dim3(grid_x, M), dim3(256), 0, s, logits, V, ld, chunk, vocab_start, acc,
+                   ticket, keys, tokens, ArgmaxXchg{});
+}
+
+void argmax_xchg_launch(const float* logits, int M, int V, int ld, int vocab_start, unsigned long long* keys,
+                        int64_t* tokens, unsigned long long* scratch, int sms, const ArgmaxXchg& x, cudaStream_t s) {
+  if (M == 0) return;
+  if (M > x.max_rows) throw std::runtime_error("argmax exchange: more rows than the symmetric key slots hold");
+  if (x.peers == nullptr || x.epoch == nullptr || x.row_ticket == nullptr || x.world < 1 || x.rank < 0 ||
+      x.rank >= x.world)
+    throw std::runtime_error("argmax exchange: bad peer table / counters");
+  const int c = scratch != nullptr ? argmax_chunks(M, V, sms) : 1;
+  int chunk = (V + c - 1) / c;
+  chunk = (chunk + 3) & ~3;
+  const int grid_x = (V + chunk - 1) / chunk;
+  unsigned long long* acc = scratch;
+  unsigned long long* ticket = scratch != nullptr ? scratch + kArgmaxMaxRows : nullptr;
+  launch_maybe_pdl(argmax_kernel<true>, dim3(grid_x, M), dim3(256), 0, s, logits, V, ld, chunk, vocab_start, acc,
+                   ticket, keys, tokens, x);
 }
 
 }  // namespace hrm

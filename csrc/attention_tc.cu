@@ -432,7 +432,7 @@ void decode_attn_tc_launch(const DecodeAttnArgs& a, int num_blocks, int* status,
   make_kv_map(&tv, a.v_cache, num_blocks, a.Hk, a.block_size);
   make_kv_map(&tk8, a.k_cache, num_blocks, a.Hk, a.block_size, kKeys / 16);
   make_kv_map(&tv8, a.v_cache, num_blocks, a.Hk, a.block_size, kKeys / 16);
-  ensure_smem_limit(attn_decode_tc_kernel, Smem::kAlloc);
+  ensure_smem_limit<attn_decode_tc_kernel>(Smem::kAlloc);
   dim3 grid(a.splits, a.Hk, a.B);
   if (status == nullptr) status = status_word();
   launch_maybe_pdl(attn_decode_tc_kernel, grid, dim3(kThreads), (size_t)Smem::kAlloc, s, tk, tv, tk8, tv8, a,
@@ -729,7 +729,7 @@ void prefill_attn_tc_launch(const PrefillAttnArgs& a, int num_blocks, int total_
   CUtensorMap tk8, tv8;
   make_kv_map(&tk8, a.k_cache, num_blocks, a.Hk, a.block_size, kKeys / 16);
   make_kv_map(&tv8, a.v_cache, num_blocks, a.Hk, a.block_size, kKeys / 16);
-  ensure_smem_limit(attn_prefill_tc_kernel, PfSmem::kAlloc);
+  ensure_smem_limit<attn_prefill_tc_kernel>(PfSmem::kAlloc);
   if (status == nullptr) status = status_word();
   dim3 grid((a.max_q + tpt - 1) / tpt, a.Hk, a.S);
   attn_prefill_tc_kernel<<<grid, kPfThreads, PfSmem::kAlloc, s>>>(tq, tk, tv, tk8, tv8, a, tpt, num_blocks, status);

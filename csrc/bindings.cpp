@@ -170,7 +170,7 @@ void w8a16_gemm_residual(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tenso
 void fill_resid_ar(hrm::GemmArgs& a, const at::Tensor& resid, const at::Tensor& gamma_next, const at::Tensor& xg_out,
                    const at::Tensor& ssq_out, const at::Tensor& peers, int64_t rank, int64_t world,
                    int64_t off_partials, int64_t off_final, int64_t off_flags, int64_t tile_floats, int64_t max_tiles,
-                   int64_t epoch_ptr, const at::Tensor& launch_ticket);
+                   int64_t epoch_ptr, const at::Tensor& launch_ticket, int64_t off_tile_flags);
 
 // Tensor-parallel residual GEMM fused with the all-reduce over peer memory (decode, M <= 64):
 //   resid = resid + sum_ranks(x_r @ W_r^T);  xg = resid * gamma_next;  ssq = per-tile sums of squares.
@@ -178,12 +178,12 @@ void w8a16_gemm_residual_ar(at::Tensor x, at::Tensor w, at::Tensor scale, at::Te
                             at::Tensor counters, at::Tensor gamma_next, at::Tensor xg_out, at::Tensor ssq_out,
                             at::Tensor peers, int64_t rank, int64_t world, int64_t off_partials, int64_t off_final,
                             int64_t off_flags, int64_t tile_floats, int64_t max_tiles, int64_t epoch_ptr,
-                            at::Tensor launch_ticket) {
+                            at::Tensor launch_ticket, int64_t off_tile_flags) {
   c10::cuda::CUDAGuard g(x.device());
   auto a = base_args(x, w, scale, c10::nullopt, ws, counters);
   if (a.M == 0) return;
   fill_resid_ar(a, resid, gamma_next, xg_out, ssq_out, peers, rank, world, off_partials, off_final, off_flags,
-                tile_floats, max_tiles, epoch_ptr, launch_ticket);
+                tile_floats, max_tiles, epoch_ptr, launch_ticket, off_tile_flags);
   auto p = hrm::gemm_plan(a.M, a.N, a.K, 0);
   check_ws(p, ws, counters);
   hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_RESID_AR, a, p,
@@ -193,7 +193,7 @@ void w8a16_gemm_residual_ar(at::Tensor x, at::Tensor w, at::Tensor scale, at::Te
 void fill_resid_ar(hrm::GemmArgs& a, const at::Tensor& resid, const at::Tensor& gamma_next, const at::Tensor& xg_out,
                    const at::Tensor& ssq_out, const at::Tensor& peers, int64_t rank, int64_t world,
                    int64_t off_partials, int64_t off_final, int64_t off_flags, int64_t tile_floats, int64_t max_tiles,
-                   int64_t epoch_ptr, const at::Tensor& launch_ticket) {
+                   int64_t epoch_ptr, const at::Tensor& launch_ticket, int64_t off_tile_flags) {
   CHECK_DTYPE(resid, at::kFloat); CHECK_DTYPE(gamma_next, at::kFloat); CHECK_DTYPE(xg_out, at::kHalf);
   CHECK_DTYPE(ssq_out, at::kFloat); CHECK_DTYPE(peers, at::kLong); CHECK_DTYPE(launch_ticket, at::kInt);
   TORCH_CHECK(resid.size(0) == a.M && resid.size(1) == a.N && resid.stride(1) == 1, "bad resid");
@@ -212,6 +212,7 @@ void fill_resid_ar(hrm::GemmArgs& a, const at::Tensor& resid, const at::Tensor& 
   a.off_partials = off_partials;
   a.off_final = off_final;
   a.off_flags = off_flags;
+  a.off_tile_flags = off_tile_flags;
   a.ar_tile_floats = (int)tile_floats;
   a.ar_max_tiles = (int)max_tiles;
   a.epoch = reinterpret_cast<int*>((uintptr_t)epoch_ptr);
@@ -332,7 +333,7 @@ void w8a16_chain(py::list phases, at::Tensor ws, at::Tensor counters, at::Tensor
       fill_resid_ar(a, t[4].cast<at::Tensor>(), t[5].cast<at::Tensor>(), t[6].cast<at::Tensor>(),
                     t[7].cast<at::Tensor>(), t[8].cast<at::Tensor>(), t[9].cast<int64_t>(), t[10].cast<int64_t>(),
                     t[11].cast<int64_t>(), t[12].cast<int64_t>(), t[13].cast<int64_t>(), t[14].cast<int64_t>(),
-                    t[15].cast<int64_t>(), t[16].cast<int64_t>(), t[17].cast<at::Tensor>());
+                    t[15].cast<int64_t>(), t[16].cast<int64_t>(), t[17].cast<at::Tensor>(), 0);
       d[p].epi = hrm::EPI_RESID_AR;
     } else if (kind == "swiglu") {
       a = base_args(x, w, scale, c10::nullopt, ws, counters);
@@ -502,6 +503,34 @@ void argmax_rows(at::Tensor logits, int64_t vocab_start, c10::optional<at::Tenso
                      (int)vocab_start, kp, tokens.data_ptr<int64_t>(), sp, hrm::gemm_sm_count(), cur_stream());
 }
 
+void argmax_rows_xchg(at::Tensor logits, int64_t vocab_start, at::Tensor tokens, c10::optional<at::Tensor> scratch,
+                      at::Tensor peers, int64_t rank, int64_t world, int64_t max_rows, int64_t off_keys,
+                      int64_t off_flags, int64_t epoch_ptr, int64_t row_ticket_ptr) {
+  c10::cuda::CUDAGuard g(logits.device());
+  CHECK_DTYPE(logits, at::kFloat); CHECK_DTYPE(tokens, at::kLong); CHECK_DTYPE(peers, at::kLong);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be [M, V] row-major");
+  TORCH_CHECK(peers.numel() == world && rank >= 0 && rank < world, "bad peer table");
+  unsigned long long* sp = nullptr;
+  if (scratch.has_value() && scratch->defined()) {
+    CHECK_DTYPE((*scratch), at::kLong);
+    TORCH_CHECK(scratch->numel() >= 2 * hrm::kArgmaxMaxRows, "argmax scratch: int64[2 * 4096]");
+    sp = reinterpret_cast<unsigned long long*>(scratch->data_ptr<int64_t>());
+  }
+  hrm::ArgmaxXchg x{};
+  x.peers = reinterpret_cast<const long long*>(peers.data_ptr<int64_t>());
+  x.rank = (int)rank;
+  x.world = (int)world;
+  x.max_rows = (int)max_rows;
+  x.off_keys = off_keys;
+  x.off_flags = off_flags;
+  x.epoch = reinterpret_cast<int*>((uintptr_t)epoch_ptr);
+  x.row_ticket = reinterpret_cast<int*>((uintptr_t)row_ticket_ptr);
+  x.status = hrm::status_word();
+  hrm::argmax_xchg_launch(logits.data_ptr<float>(), (int)logits.size(0), (int)logits.size(1), (int)logits.stride(0),
+                          (int)vocab_start, nullptr, tokens.data_ptr<int64_t>(), sp, hrm::gemm_sm_count(), x,
+                          cur_stream());
+}
+
 void decode_prepare_bs(at::Tensor positions, at::Tensor tables, int64_t block_size, c10::optional<at::Tensor> active,
                        at::Tensor slots, at::Tensor context_lens) {
   c10::cuda::CUDAGuard g(positions.device());
@@ -561,6 +590,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_prepare", &decode_prepare_bs);
   m.def("decode_advance", &decode_advance);
   m.def("sm_count", []() { return hrm::gemm_sm_count(); });
+  m.def("argmax_rows_xchg", &argmax_rows_xchg);
   m.def("grad_clip_factor", [](at::Tensor g, double clip, at::Tensor partial, at::Tensor scalars) {
     c10::cuda::CUDAGuard gd(g.device());
     TORCH_CHECK(g.is_cuda() && g.scalar_type() == at::kFloat && g.is_contiguous(), "g: contiguous f32 CUDA");
@@ -604,7 +634,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("m_fastest"));
   m.def("set_gemm_trace", [](c10::optional<at::Tensor> t) {
     if (t.has_value() && t->defined()) {
-      TORCH_CHECK(t->scalar_type() == at::kLong && t->numel() >= 12 * hrm::kGemmTraceLen, "trace: int64[12*1024]");
+      TORCH_CHECK(t->scalar_type() == at::kLong && t->numel() >= 16 * hrm::kGemmTraceLen, "trace: int64[16*1024]");
       hrm::set_gemm_trace(reinterpret_cast<long long*>(t->data_ptr<int64_t>()));
     } else {
       hrm::set_gemm_trace(nullptr);

@@ -350,11 +350,61 @@ HRM_DEVINL unsigned long long argmax_key(float v, uint32_t idx) {
   return ((unsigned long long)float_order(v) << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
 }
 
+// ---------------------------------------------------------------- peer-memory (NVLink) flags
+// Used by the fused all-reduce GEMM epilogue and the distributed argmax exchange.
+// Relaxed system-scope flag accesses and the fence that turns them into release / acquire patterns: a writer
+// fences once after its data stores (and after the named barrier that orders its CTA's other stores before the
+// fence) and then stores the flag relaxed; a reader polls relaxed and fences once after it sees the flag.
+HRM_DEVINL void st_relaxed_sys(int* p, int v) {
+  asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+HRM_DEVINL int ld_relaxed_sys(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+HRM_DEVINL void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+// Bounded relaxed poll for a flag to reach `want` (epochs only grow), then one acquire fence.  Records
+// kErrTimeoutPeer on timeout and returns false.
+HRM_DEVINL bool wait_flag_acquire(const int* p, int want, int* status) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (ld_relaxed_sys(p) - want >= 0) {
+      fence_acq_rel_sys();
+      return true;
+    }
+    if ((i & 63u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+      record_error(status, kErrTimeoutPeer);
+      return false;
+    }
+  }
+}
+HRM_DEVINL void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+HRM_DEVINL int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait for a peer flag to reach `want` (epochs only grow).  Records kErrTimeoutPeer on timeout.
+HRM_DEVINL bool wait_peer_flag(const int* p, int want, int* status) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (ld_acquire_sys(p) - want >= 0) return true;
+    if ((i & 63u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+      record_error(status, kErrTimeoutPeer);
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- host: per-device set-up
 // cudaFuncSetAttribute acts on the CURRENT device only, so a process that drives several GPUs must raise a kernel's
-// dynamic shared-memory limit once on each of them.  One flag per device and per kernel (the template below is
-// instantiated once per kernel symbol); the flags are atomics because launches may come from several host threads.
-// A racing second call of cudaFuncSetAttribute is harmless (same value), so no lock is needed.
+// dynamic shared-memory limit once on each of them.  One flag per device and per kernel: the kernel symbol is the
+// template argument, so every kernel (every template instantiation of one) has its own flags.  The flags are
+// atomics because launches may come from several host threads; a racing second cudaFuncSetAttribute is harmless
+// (same value), so no lock is needed.
 constexpr int kMaxDevices = 64;
 
 inline int current_device_or_throw() {
@@ -365,12 +415,12 @@ inline int current_device_or_throw() {
   return d;
 }
 
-template <typename... KArgs>
-inline void ensure_smem_limit(void (*kern)(KArgs...), int bytes) {
-  static std::atomic<bool> done[kMaxDevices];   // zero-initialised (static storage)
+template <auto Kernel>
+inline void ensure_smem_limit(int bytes) {
+  static std::atomic<bool> done[kMaxDevices];   // zero-initialised (static storage), one set per kernel symbol
   const int d = current_device_or_throw();
   if (done[d].load(std::memory_order_acquire)) return;
-  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  const cudaError_t e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess)
     throw std::runtime_error(std::string("cudaFuncSetAttribute(max dynamic shared memory) failed: ") +
                              cudaGetErrorString(e));

@@ -471,7 +471,7 @@ GemmPlan gemm_chain_phase_plan(int M, int N, int K, int ctas) {
 template <int BN, int E0, int E1, int E2, int E3>
 static void launch_chain_bn(const CUtensorMap (&tx)[kMaxChainPhases], const ChainArgs& c, int G, cudaStream_t s) {
   using S = GemmSmem<BN>;
-  ensure_smem_limit(w8a16_chain_kernel<BN, E0, E1, E2, E3>, S::kAlloc);
+  ensure_smem_limit<w8a16_chain_kernel<BN, E0, E1, E2, E3>>(S::kAlloc);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
   cfg.blockDim = dim3(kThreads);

@@ -386,18 +386,22 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
           }
           epilogue_store<BN, EPI>(a, n_tile, m_tile, row, c0, v, stage, et, inv, ssq_red);
         }
+        if constexpr (EPI == EPI_RESID_AR) ar_tile_finish<BN>(a, n_tile, row, et, ep, ssq_red);
       } else {
         // partial segment: write fp32 partial, take a ticket; the last segment of the tile reduces in k order
         const int first = owner_of((int64_t)tile * a.k_tiles, U, G);
         const int nseg = owner_of(tile_end - 1, U, G) - first + 1;
         const int segidx = (int)blockIdx.x - first;
+        // partial of this segment, row-major per thread ([row][BN]): a thread's chunk is 64 contiguous bytes
         float* ws_tile = a.ws + (size_t)tile * a.max_seg * (BN * kBM);
         float* mine = ws_tile + (size_t)segidx * (BN * kBM);
         for (int c0 = 0; c0 < BN; c0 += kChunk) {
           float v[kChunk];
           tmem_ld_acc<BN, S::NACC>(acc_addr + (uint32_t)c0, v, valid);
+          float4* dst = reinterpret_cast<float4*>(mine + (size_t)row * BN + c0);
 #pragma unroll
-          for (int j = 0; j < kChunk; ++j) __stcg(&mine[(c0 + j) * kBM + row], v[j]);
+          for (int q = 0; q < kChunk / 4; ++q)
+            __stcg(dst + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
         }
         tc_fence_before();
         mbar_arrive(&aempty[acc]);
@@ -417,21 +421,15 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
           if (a.in_ssq != nullptr) compute_row_scale<BN>(a, m_tile, inv, et);
           for (int c0 = 0; c0 < BN; c0 += kChunk) {
             float v[kChunk];
-#pragma unroll
-            for (int j = 0; j < kChunk; ++j) v[j] = __ldcg(&ws_tile[(c0 + j) * kBM + row]);
-            for (int sg = 1; sg < nseg; ++sg) {
-              const float* p = ws_tile + (size_t)sg * (BN * kBM);
-#pragma unroll
-              for (int j = 0; j < kChunk; ++j) v[j] += __ldcg(&p[(c0 + j) * kBM + row]);
-            }
+            sum_segments<BN>(ws_tile, nseg, row, c0, v);
             epilogue_store<BN, EPI>(a, n_tile, m_tile, row, c0, v, stage, et, inv, ssq_red);
           }
+          if constexpr (EPI == EPI_RESID_AR) ar_tile_finish<BN>(a, n_tile, row, et, ep, ssq_red);
         }
       }
       if (et == 0) trace_mark(a, 6, seg);
       u = ue;
     }
-    if constexpr (EPI == EPI_RESID_AR) ar_oneshot<BN>(a, row, et, ep, ssq_red);
   }
 
   tc_fence_before();
@@ -588,7 +586,7 @@ template <int BN, int EPI>
 static void launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, const GemmPlan& p,
                       cudaStream_t stream) {
   using S = GemmSmem<BN>;
-  ensure_smem_limit(w8a16_gemm_kernel<BN, EPI>, S::kAlloc);
+  ensure_smem_limit<w8a16_gemm_kernel<BN, EPI>>(S::kAlloc);
   launch_maybe_pdl(w8a16_gemm_kernel<BN, EPI>, dim3(p.ctas), dim3(kThreads), (size_t)S::kAlloc, stream, tw, tx, a);
 }
 

@@ -81,6 +81,7 @@ struct GemmArgs {
   const long long* peers;
   int tp_rank, tp_world;
   long long off_partials, off_final, off_flags;   // byte offsets inside every rank's buffer
+  long long off_tile_flags;                       // int32 [world][ar_max_tiles]: epoch of each (source rank, tile)
   int ar_tile_floats;                             // floats per tile slot (max_bn * 128)
   int ar_max_tiles;
   int* epoch;                                     // this rank's launch epoch counter (in its symmetric buffer)
@@ -99,7 +100,7 @@ struct GemmArgs {
   __nv_bfloat16* k_cache;                   // [num_blocks, kv_heads, block_size, head_dim]
   __nv_bfloat16* v_cache;
   int* status;                              // bounded-wait error word (may be nullptr)
-  long long* trace;                         // optional per-stage clock64 stamps of CTA 0 ([12][kGemmTraceLen])
+  long long* trace;                         // optional stamps: [16][kGemmTraceLen] (see trace_mark / trace_cta)
 };
 
 constexpr int kGemmTraceLen = 1024;

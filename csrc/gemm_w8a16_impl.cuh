@@ -86,7 +86,8 @@ struct GemmSmem {
 HRM_DEVINL void trace_mark(const GemmArgs& a, int point, int64_t i) {
   if (a.trace != nullptr && blockIdx.x == 0 && i < kGemmTraceLen) a.trace[point * kGemmTraceLen + i] = clock64();
 }
-// Per-CTA %globaltimer stamps (rows 8..11: CTA start, first weight unit landed, mainloop done, CTA end).
+// Per-CTA %globaltimer stamps (rows 8..11: CTA start, first weight unit landed, mainloop done, CTA end; fused
+// all-reduce rows 12..15: tile pushed, peers' flags seen / (chain) fence + grid ticket done, reduction written).
 HRM_DEVINL void trace_cta(const GemmArgs& a, int row) {
   if (a.trace != nullptr && blockIdx.x < kGemmTraceLen) a.trace[row * kGemmTraceLen + blockIdx.x] = (long long)global_ns();
 }
@@ -119,6 +120,44 @@ HRM_DEVINL void tmem_ld_acc(uint32_t taddr, float (&v)[16], uint32_t valid) {
   }
 }
 
+// Sum of a tile's k-segment partials for one thread's row and 16 columns [c0, c0 + 16), in k order (segment 0
+// first), so the result does not depend on which CTA finished last.  Partials are [segment][row][BN] fp32 in L2;
+// the loads of four segments are issued before their adds, so a tile cut into many segments (narrow projections
+// at high tensor-parallel degree) costs a few L2 round trips instead of one per segment.
+template <int BN>
+HRM_DEVINL void sum_segments(const float* ws_tile, int nseg, int row, int c0, float (&v)[16]) {
+  const size_t seg4 = (size_t)BN * 128 / 4;   // float4s per segment partial
+  const float4* p0 = reinterpret_cast<const float4*>(ws_tile + (size_t)row * BN + c0);
+  float4 acc[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) acc[q] = __ldcg(p0 + q);
+  int sg = 1;
+  for (; sg + 4 <= nseg; sg += 4) {
+    float4 t[4][4];
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) t[s][q] = __ldcg(p0 + (size_t)(sg + s) * seg4 + q);
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[q].x += t[s][q].x; acc[q].y += t[s][q].y; acc[q].z += t[s][q].z; acc[q].w += t[s][q].w;
+      }
+  }
+  for (; sg < nseg; ++sg) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 t = __ldcg(p0 + (size_t)sg * seg4 + q);
+      acc[q].x += t.x; acc[q].y += t.y; acc[q].z += t.z; acc[q].w += t.w;
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    v[4 * q] = acc[q].x; v[4 * q + 1] = acc[q].y; v[4 * q + 2] = acc[q].z; v[4 * q + 3] = acc[q].w;
+  }
+}
+
 // ------------------------------------------------------------------ stream-K partition helpers (device + host)
 HRM_DEVINL int64_t unit_start(int64_t c, int64_t U, int64_t G) { return (c * U) / G; }
 HRM_DEVINL int owner_of(int64_t x, int64_t U, int64_t G) { return (int)(((x + 1) * G - 1) / U); }
@@ -135,27 +174,6 @@ HRM_DEVINL void compute_row_scale(const GemmArgs& a, int m_tile, float* inv, int
     inv[j] = rsqrtf(s * a.in_inv_h + a.in_eps);
   }
   asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
-}
-
-// ------------------------------------------------------------------ peer-memory (NVLink) flags for EPI_RESID_AR
-HRM_DEVINL void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-HRM_DEVINL int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-// Bounded wait for a peer flag to reach `want` (epochs only grow).  Records kErrTimeoutPeer on timeout.
-HRM_DEVINL bool wait_peer_flag(const int* p, int want, int* status) {
-  const uint64_t t0 = global_ns();
-  for (uint32_t i = 0;; ++i) {
-    if (ld_acquire_sys(p) - want >= 0) return true;
-    if ((i & 63u) == 0 && global_ns() - t0 > kWaitLimitNs) {
-      record_error(status, kErrTimeoutPeer);
-      return false;
-    }
-  }
 }
 
 // x_new of 16 tokens for this thread's row -> residual, xg = x * gamma_next, per-tile sums of squares.
@@ -206,6 +224,71 @@ HRM_DEVINL float* ar_slot(const GemmArgs& a, int dst, int src, int par, int tile
   return base + (((size_t)par * a.tp_world + src) * a.ar_max_tiles + tile) * a.ar_tile_floats;
 }
 
+// Reduction of tile t from the receive area (every rank's partial has arrived): x = resid + sum over source ranks
+// in rank order, then residual / xg / ssq outputs.  Every rank computes bit-identical results.
+template <int BN>
+HRM_DEVINL void ar_reduce_tile(const GemmArgs& a, int t, int par, int row, int et, float* ssq_red) {
+  const int stride = a.ar_tile_floats / kBM;   // tokens per row slot (max_bn)
+  const int n = t * kBM + row;
+  for (int c0 = 0; c0 < BN && c0 < a.M; c0 += kChunk) {
+    float sum[kChunk];
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) sum[j] = 0.f;
+    for (int src = 0; src < a.tp_world; ++src) {
+      const float4* p = reinterpret_cast<const float4*>(ar_slot(a, a.tp_rank, src, par, t) + (size_t)row * stride + c0);
+      float4 v[kChunk / 4];
+#pragma unroll
+      for (int q = 0; q < kChunk / 4; ++q) v[q] = __ldcg(p + q);
+#pragma unroll
+      for (int q = 0; q < kChunk / 4; ++q) {
+        sum[4 * q] += v[q].x; sum[4 * q + 1] += v[q].y; sum[4 * q + 2] += v[q].z; sum[4 * q + 3] += v[q].w;
+      }
+    }
+    float xn[kChunk];
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      const int m = c0 + j;
+      xn[j] = (m < a.M && n < a.N) ? a.resid[(size_t)m * a.ldr + n] + sum[j] : 0.f;
+    }
+    store_residual_outputs<BN>(a, t, 0, row, c0, xn, et, ssq_red);
+  }
+}
+
+// Per-tile all-reduce of the single-launch fused row-parallel GEMM.  The CTA that completed output tile t (its
+// last k-segment) has just stored the tile's fp32 partial into slot [epoch parity][this rank][t] of EVERY rank's
+// receive area (epilogue_store, EPI_RESID_AR).  Then:
+//  1. the epilogue threads meet at their named barrier (every push issued); one thread fences once at system scope
+//     (cumulative over the CTA's pushes, ordered before it by the barrier) and stores the epoch, relaxed, into flag
+//     [this rank][t] of every rank: a release pattern;
+//  2. thread r < world polls this rank's flag [r][t] (relaxed, bounded) and fences once it reached the epoch;
+//  3. after the barrier the tile is reduced from local memory (ar_reduce_tile).
+// There is no grid-wide ticket and no whole-launch flag: tile t waits only for tile t of the other ranks, which the
+// same CTA index completes at about the same time on every rank (identical plans).  Key slots are double-buffered by
+// epoch parity: a rank cannot push launch e + 2 before every rank finished launch e, because finishing launch e + 1
+// needs every rank's launch-(e + 1) pushes, which come after that rank's launch e (stream order).
+template <int BN>
+HRM_DEVINL void ar_tile_finish(const GemmArgs& a, int t, int row, int et, int ep, float* ssq_red) {
+  asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+  if (et == 0) {
+    trace_cta(a, 12);
+    fence_acq_rel_sys();
+    for (int d = 0; d < a.tp_world; ++d) {
+      int* f = reinterpret_cast<int*>(reinterpret_cast<char*>(a.peers[d]) + a.off_tile_flags);
+      st_relaxed_sys(f + (size_t)a.tp_rank * a.ar_max_tiles + t, ep);
+    }
+  }
+  if (et < a.tp_world) {
+    const int* f = reinterpret_cast<const int*>(reinterpret_cast<char*>(a.peers[a.tp_rank]) + a.off_tile_flags);
+    wait_flag_acquire(f + (size_t)et * a.ar_max_tiles + t, ep, a.status);
+  }
+  asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
+  if (et == 0) trace_cta(a, 14);   // every rank's partial of this tile has arrived
+  ar_reduce_tile<BN>(a, t, ep & 1, row, et, ssq_red);
+  if (et == 0) trace_cta(a, 15);
+}
+
+// Whole-launch variant (multi-phase chain): all CTAs meet at a grid ticket, the last one publishes one flag per
+// rank, every CTA then reduces a share of the tiles.
 template <int BN>
 HRM_DEVINL void ar_oneshot(const GemmArgs& a, int row, int et, int ep, float* ssq_red) {
   int* my_flags = reinterpret_cast<int*>(reinterpret_cast<char*>(a.peers[a.tp_rank]) + a.off_flags);

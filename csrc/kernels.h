@@ -78,6 +78,27 @@ constexpr int kArgmaxMaxRows = 4096;
 void argmax_launch(const float* logits, int M, int V, int ld, int vocab_start, unsigned long long* keys,
                    int64_t* tokens, unsigned long long* scratch, int sms, cudaStream_t s);
 
+// Tensor-parallel greedy pick without a collective library call: every rank holds the logits of its vocab slice.
+// The CTA that finishes a row's local argmax stores the row's packed key into slot [epoch parity][rank][row] of
+// EVERY rank's symmetric buffer (NVLink stores), fences once and stores the epoch into flag [rank][row] of every
+// rank; it waits (bounded) until all ranks' flags of that row reached the epoch in its own buffer and takes the
+// maximum of the keys.  The packed key orders by value, then by the lower global token id, so every rank picks the
+// same token as one argmax over the whole vocabulary (the reference's distributed greedy rule,
+// engine/llama_tp.py:317-335, without its three collectives and per-row broadcasts).  Key slots are
+// double-buffered by epoch parity: a rank cannot start exchange e + 2 before every rank has finished reading
+// exchange e, because exchange e + 1 needs every rank's flags.
+struct ArgmaxXchg {
+  const long long* peers;   // device table: base address of every rank's symmetric buffer (local one included)
+  int rank, world, max_rows;
+  long long off_keys;       // byte offset of int64 [2][world][max_rows] key slots in every buffer
+  long long off_flags;      // byte offset of int32 [world][max_rows] epoch flags in every buffer
+  int* epoch;               // this rank's exchange counter (local memory); the launch's last row advances it
+  int* row_ticket;          // rows finished in the current launch (local memory; zero between launches)
+  int* status;              // bounded-wait error word
+};
+void argmax_xchg_launch(const float* logits, int M, int V, int ld, int vocab_start, unsigned long long* keys,
+                        int64_t* tokens, unsigned long long* scratch, int sms, const ArgmaxXchg& x, cudaStream_t s);
+
 void decode_prepare_launch(const int* positions, const int* tables, int maxb, int bs, const int* active, int* slots,
                            int* context_lens, int B, cudaStream_t s);
 void decode_advance_launch(const int64_t* tokens, int64_t* ids, int* positions, const int* active, int B,

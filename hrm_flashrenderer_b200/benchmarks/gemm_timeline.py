@@ -27,7 +27,7 @@ def timeline(N: int, K: int, M: int, pdl: bool, dev) -> dict:
     x = torch.randn(M, K, device=dev).half()
     out = torch.empty(M, N, dtype=torch.float16, device=dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
-    tr = torch.zeros(12 * 1024, dtype=torch.int64, device=dev)
+    tr = torch.zeros(16 * 1024, dtype=torch.int64, device=dev)
     C.set_pdl(pdl)
     try:
         for _ in range(3):
@@ -41,7 +41,7 @@ def timeline(N: int, K: int, M: int, pdl: bool, dev) -> dict:
         torch.cuda.synchronize()
     finally:
         C.set_pdl(True)
-    t = tr.view(12, 1024)[8:12].cpu()
+    t = tr.view(16, 1024)[8:12].cpu()
     n = int((t[0] > 0).sum())
     t = t[:, :n].double()
     rel = (t - t[0].min()) / 1e3

@@ -258,6 +258,10 @@ class LlamaW8:
             xl = xg.index_select(0, b.last_rows)
             nl = (ssq.index_select(1, b.last_rows).contiguous(), H, cfg.rms_eps)
         logits = ops.w8a16_linear(xl, self.head_q, self.head_s, out_dtype=torch.float32, in_norm=nl)
+        xchg_rows = min(self.symm.argmax_rows, ops.ARGMAX_XCHG_MAX_ROWS) if self.symm is not None else 0
+        if p.world > 1 and logits.shape[0] <= xchg_rows:
+            # global greedy pick through peer memory inside the argmax kernel (no NCCL call)
+            return ops.argmax_exchange_(logits, p.vocab_start, self.symm)
         if p.world > 1:
             keys = torch.empty(xl.shape[0], dtype=torch.int64, device=self.device)
             ops.argmax_rows(logits, p.vocab_start, keys=keys)
@@ -441,6 +445,9 @@ class LlamaW8:
         xl = xg.index_select(0, b.last_rows)
         nl = (ssq.index_select(1, b.last_rows).contiguous(), H, cfg.rms_eps)
         logits = ops.w8a16_linear(xl, self.head_q, self.head_s, out_dtype=torch.float32, in_norm=nl)
+        xchg_rows = min(self.symm.argmax_rows, ops.ARGMAX_XCHG_MAX_ROWS) if self.symm is not None else 0
+        if logits.shape[0] <= xchg_rows:
+            return ops.argmax_exchange_(logits, p.vocab_start, self.symm)
         keys = torch.empty(xl.shape[0], dtype=torch.int64, device=dev)
         ops.argmax_rows(logits, p.vocab_start, keys=keys)
         comm.all_reduce_max_(keys)

@@ -229,7 +229,7 @@ def w8a16_residual_ar_(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tens
     w = _ws_for(x2.shape[0], *weight_nk(qweight, scale), x.device)
     ext().w8a16_gemm_residual_ar(x2, qweight, scale, resid, w.ws, w.counters, gamma_next, xg_out, ssq_out, symm.peers,
                                  symm.rank, symm.world, symm.off_partials, symm.off_final, symm.off_flags,
-                                 symm.max_bn * 128, symm.max_tiles, symm.epoch_ptr, symm.ticket)
+                                 symm.max_bn * 128, symm.max_tiles, symm.epoch_ptr, symm.ticket, symm.off_tile_flags)
     LAUNCH_COUNTER.add()
     return resid
 
@@ -561,6 +561,30 @@ def argmax_rows(logits: torch.Tensor, vocab_start: int = 0, keys: Optional[torch
         tokens = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
     scratch = Workspace.get(logits.device).argmax if _ARGMAX_SPLIT else None
     ext().argmax_rows(logits, int(vocab_start), keys, tokens, scratch)
+    LAUNCH_COUNTER.add()
+    return tokens
+
+
+ARGMAX_XCHG_MAX_ROWS = 256
+
+
+def argmax_exchange_(logits: torch.Tensor, vocab_start: int, symm, tokens: Optional[torch.Tensor] = None
+                     ) -> torch.Tensor:
+    """Tensor-parallel greedy token per row: this rank's logits cover vocab ids ``[vocab_start, vocab_start + V)``;
+    every rank returns the global argmax (ties -> lowest id) after one exchange of packed keys over NVLink peer
+    memory inside the argmax kernel (no collective library call).
+
+    Each row's final CTA waits for the other ranks' key of its row, so every CTA of the launch must be resident at
+    once: rows are limited to ``ARGMAX_XCHG_MAX_ROWS`` (about two CTAs per SM); larger batches take the collective
+    path."""
+    if logits.shape[0] > ARGMAX_XCHG_MAX_ROWS:
+        raise ValueError(f"argmax exchange: {logits.shape[0]} rows > {ARGMAX_XCHG_MAX_ROWS}")
+    if tokens is None:
+        tokens = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
+    scratch = Workspace.get(logits.device).argmax if _ARGMAX_SPLIT else None
+    ext().argmax_rows_xchg(logits, int(vocab_start), tokens, scratch, symm.peers, symm.rank, symm.world,
+                           symm.argmax_rows, symm.off_ax_keys, symm.off_ax_flags, symm.argmax_epoch_ptr,
+                           symm.argmax_ticket_ptr)
     LAUNCH_COUNTER.add()
     return tokens
 

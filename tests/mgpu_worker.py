@@ -4,6 +4,9 @@
    same partials: equal within fp32 summation-order tolerance, bitwise identical on every rank, over repeated
    launches (epoch flags).
 2. The engine at TP = world (fused collectives and plain NCCL) against TP = 1: same greedy tokens.
+3. The distributed argmax exchange over peer memory against one argmax of the full logits (ties included).
+4. Llama-3.1-70B widths (2 layers): the fused all-reduce GEMM at the o_proj / down shapes against NCCL (max abs
+   error), and the engine at TP = world against TP = 1, token for token over 32 greedy tokens.
 """
 import json
 import os
@@ -84,19 +87,102 @@ def check_engine(rank, world, dev):
     return outs[False], outs[True], single, outs.get("chain")
 
 
+def check_argmax_exchange(rank, world, dev):
+    """The in-kernel distributed argmax (packed keys over peer memory) against an argmax of the full logits: same
+    token on every rank, ties across ranks to the lowest global id, over repeated launches (epochs)."""
+    symm = SymmetricWorkspace(rank, world, dev, max_tiles=64, max_bn=64)
+    V = 1000
+    for rep in range(5):
+        for M in (1, 16, 256):
+            g = torch.Generator().manual_seed(1000 * rep + M)
+            full = torch.randn(M, V * world, generator=g)
+            if rep % 2 == 1:   # exact ties: the same maximum in every rank's slice
+                full[:, ::V] = 50.0
+            local = full[:, rank * V:(rank + 1) * V].contiguous().to(dev)
+            tok = ops.argmax_exchange_(local, rank * V, symm)
+            torch.cuda.synchronize()
+            ops.check_status(dev)
+            want = torch.argmax(full, dim=1)   # first (lowest) index of the maximum
+            assert torch.equal(tok.cpu(), want), (rep, M)
+    symm.close()
+
+
+def check_fused_ar_70b(rank, world, dev):
+    """The 70B row-parallel shapes (o_proj K 8192, down K 28672, N 8192), K sharded: fused kernel vs GEMM + NCCL
+    all-reduce of the same partials, max abs error over the decode batch sizes."""
+    symm = SymmetricWorkspace(rank, world, dev, max_tiles=64, max_bn=64)
+    gamma = torch.ones(8192, device=dev)
+    worst = 0.0
+    for K in (8192, 28672):
+        Kl = K // world
+        g = torch.Generator(device="cpu").manual_seed(200 + rank)
+        w = torch.randint(-127, 128, (8192, Kl), generator=g, dtype=torch.int8).to(dev)
+        s = (torch.rand(8192, generator=g) * 1e-4 + 1e-5).to(dev)
+        wt = ops.tile_w8(w)
+        for M in (1, 16, 64):
+            x = torch.randn(M, Kl, generator=g).half().to(dev)
+            resid = torch.randn(M, 8192, generator=torch.Generator().manual_seed(M)).to(dev)
+            part = torch.empty(M, 8192, dtype=torch.float32, device=dev)
+            ops.w8a16_linear_out(x, wt, s, part)
+            dist.all_reduce(part)
+            ref = resid + part
+            got = resid.clone()
+            xg = torch.empty(M, 8192, dtype=torch.float16, device=dev)
+            ssq = torch.empty(64, M, dtype=torch.float32, device=dev)
+            ops.w8a16_residual_ar_(x, wt, s, got, symm, gamma, xg, ssq)
+            torch.cuda.synchronize()
+            ops.check_status(dev)
+            worst = max(worst, float((got - ref).abs().max()))
+    symm.close()
+    return worst
+
+
+def check_engine_70b(rank, world, dev, new_tokens=32):
+    """Llama-3.1-70B widths (2 layers), TP = world with the fused kernels, against TP = 1 on rank 0: the greedy
+    tokens of 4 prompts over ``new_tokens`` decode steps (distributed argmax semantics of the reference,
+    engine/llama_tp.py:317-335: the global argmax with the lowest token id on ties)."""
+    from hrm_flashrenderer_b200.config import LLAMA31_70B
+    cfg = LLAMA31_70B.with_layers(2)
+    prompts = [torch.randint(0, cfg.vocab, (64,), generator=torch.Generator().manual_seed(50 + i)).tolist()
+               for i in range(4)]
+    model = LlamaW8.synthesize(cfg, rank=rank, world=world, device=dev, seed=0, comm=TPComm(), max_pos=512)
+    model.enable_fused_collectives()
+    eng = InferenceEngine(model, EngineConfig(tp=world, max_seq_len=256, max_batch=4, use_cuda_graphs=True),
+                          num_blocks=128)
+    got = eng.generate(prompts, new_tokens, stop_on_eos=False)
+    eng.release_graphs()
+    model.symm.close()
+    del eng, model
+    torch.cuda.empty_cache()
+    single = None
+    if rank == 0:
+        m1 = LlamaW8.synthesize(cfg, device=dev, seed=0, max_pos=512)
+        e1 = InferenceEngine(m1, EngineConfig(max_seq_len=256, max_batch=4, use_cuda_graphs=True), num_blocks=128)
+        single = e1.generate(prompts, new_tokens, stop_on_eos=False)
+        e1.release_graphs()
+        del e1, m1
+        torch.cuda.empty_cache()
+    return got, single
+
+
 def main():
     rank, local, world = init_dist_env("nccl")
     dev = torch.device("cuda", local)
     worst = check_fused_ar(rank, world, dev)
+    check_argmax_exchange(rank, world, dev)
+    worst70 = check_fused_ar_70b(rank, world, dev)
     nccl_out, fused_out, single, chain_out = check_engine(rank, world, dev)
+    got70, single70 = check_engine_70b(rank, world, dev)
     ok = True
     if rank == 0:
         first_div = lambda a, b: next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), len(a))
         agree_fused = fused_out == nccl_out
         agree_single = min(first_div(a, b) for a, b in zip(nccl_out, single))
-        ok = agree_single >= 8
-        rec = {"ok": ok, "world": world, "fused_ar_max_err": worst, "fused_equals_nccl": agree_fused,
-               "tp_vs_tp1_first_divergence": agree_single}
+        div70 = [first_div(a, b) for a, b in zip(got70, single70)]
+        ok = agree_single >= 8 and got70 == single70
+        rec = {"ok": ok, "world": world, "fused_ar_max_err": worst, "fused_ar_70b_max_abs_err": worst70,
+               "fused_equals_nccl": agree_fused, "tp_vs_tp1_first_divergence": agree_single,
+               "tp_vs_tp1_70b_first_divergence": div70, "tp_vs_tp1_70b_equal": got70 == single70}
         if chain_out is not None:
             rec["chain_equals_fused"] = chain_out == fused_out
             ok = rec["ok"] = ok and rec["chain_equals_fused"]
