@@ -231,24 +231,43 @@ HRM_DEVINL void ar_reduce_tile(const GemmArgs& a, int t, int par, int row, int e
   const int stride = a.ar_tile_floats / kBM;   // tokens per row slot (max_bn)
   const int n = t * kBM + row;
   for (int c0 = 0; c0 < BN && c0 < a.M; c0 += kChunk) {
+    float xr[kChunk];   // residual rows, loaded before the partials so both latencies overlap
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      const int m = c0 + j;
+      xr[j] = (m < a.M && n < a.N) ? a.resid[(size_t)m * a.ldr + n] : 0.f;
+    }
     float sum[kChunk];
 #pragma unroll
     for (int j = 0; j < kChunk; ++j) sum[j] = 0.f;
-    for (int src = 0; src < a.tp_world; ++src) {
-      const float4* p = reinterpret_cast<const float4*>(ar_slot(a, a.tp_rank, src, par, t) + (size_t)row * stride + c0);
-      float4 v[kChunk / 4];
+    // source ranks two at a time: their loads are in flight together, the adds stay in rank order
+    for (int s0 = 0; s0 < a.tp_world; s0 += 2) {
+      float4 v[2][kChunk / 4];
 #pragma unroll
-      for (int q = 0; q < kChunk / 4; ++q) v[q] = __ldcg(p + q);
+      for (int s = 0; s < 2; ++s) {
+        if (s0 + s < a.tp_world) {
+          const float4* p =
+              reinterpret_cast<const float4*>(ar_slot(a, a.tp_rank, s0 + s, par, t) + (size_t)row * stride + c0);
 #pragma unroll
-      for (int q = 0; q < kChunk / 4; ++q) {
-        sum[4 * q] += v[q].x; sum[4 * q + 1] += v[q].y; sum[4 * q + 2] += v[q].z; sum[4 * q + 3] += v[q].w;
+          for (int q = 0; q < kChunk / 4; ++q) v[s][q] = __ldcg(p + q);
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        if (s0 + s < a.tp_world) {
+#pragma unroll
+          for (int q = 0; q < kChunk / 4; ++q) {
+            sum[4 * q] += v[s][q].x; sum[4 * q + 1] += v[s][q].y;
+            sum[4 * q + 2] += v[s][q].z; sum[4 * q + 3] += v[s][q].w;
+          }
+        }
       }
     }
     float xn[kChunk];
 #pragma unroll
     for (int j = 0; j < kChunk; ++j) {
       const int m = c0 + j;
-      xn[j] = (m < a.M && n < a.N) ? a.resid[(size_t)m * a.ldr + n] + sum[j] : 0.f;
+      xn[j] = (m < a.M && n < a.N) ? xr[j] + sum[j] : 0.f;
     }
     store_residual_outputs<BN>(a, t, 0, row, c0, xn, et, ssq_red);
   }

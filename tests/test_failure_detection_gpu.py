@@ -1,7 +1,8 @@
 """Failure detection on the GPU without a fault: a bounded wait runs out and the kernel reports it.
 
 The fused tensor-parallel GEMM is given a two-rank peer table whose second "rank" is just another buffer on this GPU
-that no kernel ever signals.  Its wait for that rank's epoch flag must give up after the 2 s limit, record the error
+that no kernel ever signals.  Its wait for that rank's per-tile epoch flags must give up after the 2 s limit (every
+tile-owning CTA waits in parallel), record the error
 code in the status word (read on the host by ``ops.check_status``), and leave the context usable: a normal GEMM
 launched afterwards still gives correct results.
 """
@@ -28,7 +29,8 @@ class _SilentPeerWorkspace:
         self.off_partials = 0
         self.off_final = al(2 * 2 * max_tiles * tile_bytes)
         self.off_flags = al(self.off_final + max_tiles * tile_bytes)
-        self.off_scalars = al(self.off_flags + 2 * max_tiles * 4)
+        self.off_tile_flags = al(self.off_flags + 2 * max_tiles * 4)
+        self.off_scalars = al(self.off_tile_flags + 2 * max_tiles * 4)
         size = al(self.off_scalars + 4096)
         with torch.cuda.device(dev):
             self.ptrs = [C.symm_alloc(size)[0], C.symm_alloc(size)[0]]
