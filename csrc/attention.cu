@@ -330,14 +330,14 @@ HRM_DEVINL unsigned long long argmax_exchange_row(const ArgmaxXchg& x, int row, 
   fence_acq_rel_sys();   // release pattern: the key stores above are visible before any of the flags below
   for (int d = 0; d < x.world; ++d) {
     char* base = reinterpret_cast<char*>(x.peers[d]);
-    st_relaxed_sys(reinterpret_cast<int*>(base + x.off_flags) + (size_t)x.rank * x.max_rows + row, ep);
+    st_relaxed_sys(reinterpret_cast<int*>(base + x.off_flags) + ((size_t)x.rank * x.max_rows + row) * 32, ep);
   }
   char* own = reinterpret_cast<char*>(x.peers[x.rank]);
   const int* flags = reinterpret_cast<const int*>(own + x.off_flags);
   const unsigned long long* slots = reinterpret_cast<const unsigned long long*>(own + x.off_keys);
   unsigned long long best = 0ull;
   for (int r = 0; r < x.world; ++r) {   // max is order independent; rank order only fixes the reads
-    if (!wait_flag_acquire(flags + (size_t)r * x.max_rows + row, ep, x.status)) continue;
+    if (!wait_flag_acquire(flags + ((size_t)r * x.max_rows + row) * 32, ep, x.status)) continue;
     const unsigned long long k = __ldcg(slots + ((size_t)(ep & 1) * x.world + r) * x.max_rows + row);
     best = k > best ? k : best;
   }

@@ -373,6 +373,7 @@ HRM_DEVINL bool wait_flag_acquire(const int* p, int want, int* status) {
       fence_acq_rel_sys();
       return true;
     }
+    __nanosleep(32);   // back off: the flag's line stays free for the peer's store
     if ((i & 63u) == 0 && global_ns() - t0 > kWaitLimitNs) {
       record_error(status, kErrTimeoutPeer);
       return false;

@@ -211,24 +211,33 @@ HRM_DEVINL void store_residual_outputs(const GemmArgs& a, int n_tile, int m_tile
 }
 
 // Tensor-parallel residual epilogue: one-shot all-reduce by peer-memory PUSH over NVLink (decode, one m tile).
-// Receive area of every rank: [launch parity][source rank][tile][128 rows][max_bn tokens] fp32 (double-buffered by
-// launch parity: a slow peer may still be reading the previous launch's data).
+// Receive area of every rank: [launch parity][source rank][tile][max_bn / 4 token groups][128 rows] float4
+// (double-buffered by launch parity: a slow peer may still be reading the previous launch's data).
 // Phase 1 (per finished tile, in the overlapped epilogue): the tile's partial is stored into the source-rank slot of
 // EVERY rank's receive area (posted NVLink writes: no round trip on the critical path).
 // Phase 2 (once per CTA, after the mainloop): the CTAs of this rank meet at a grid-wide ticket; the last one fences
 // and writes this rank's epoch into every rank's flag array.  Each CTA waits on its LOCAL flags, then reduces its
 // share of the tiles from local memory: x = resid + sum over source ranks in rank order, so every rank computes
 // bit-identical x / xg / ssq.  One flag hop per launch; every load is local.
-HRM_DEVINL float* ar_slot(const GemmArgs& a, int dst, int src, int par, int tile) {
+// A tile slot is laid out column-group-major: float4 element (row r, tokens 4g..4g+3) at index g * 128 + r, so the
+// 32 rows of a warp store / load 512 contiguous bytes per instruction (one NVLink write burst, not 32 short ones).
+HRM_DEVINL float4* ar_slot(const GemmArgs& a, int dst, int src, int par, int tile) {
   float* base = reinterpret_cast<float*>(reinterpret_cast<char*>(a.peers[dst]) + a.off_partials);
-  return base + (((size_t)par * a.tp_world + src) * a.ar_max_tiles + tile) * a.ar_tile_floats;
+  return reinterpret_cast<float4*>(base + (((size_t)par * a.tp_world + src) * a.ar_max_tiles + tile) *
+                                              a.ar_tile_floats);
+}
+// Flags of the per-tile protocol: one 128-byte line per (source rank, tile), so pollers of different tiles and the
+// peers' flag stores never share a line.
+constexpr int kFlagStrideInts = 32;
+HRM_DEVINL int* ar_tile_flag(const GemmArgs& a, int dst, int src, int tile) {
+  int* f = reinterpret_cast<int*>(reinterpret_cast<char*>(a.peers[dst]) + a.off_tile_flags);
+  return f + ((size_t)src * a.ar_max_tiles + tile) * kFlagStrideInts;
 }
 
 // Reduction of tile t from the receive area (every rank's partial has arrived): x = resid + sum over source ranks
 // in rank order, then residual / xg / ssq outputs.  Every rank computes bit-identical results.
 template <int BN>
 HRM_DEVINL void ar_reduce_tile(const GemmArgs& a, int t, int par, int row, int et, float* ssq_red) {
-  const int stride = a.ar_tile_floats / kBM;   // tokens per row slot (max_bn)
   const int n = t * kBM + row;
   for (int c0 = 0; c0 < BN && c0 < a.M; c0 += kChunk) {
     float xr[kChunk];   // residual rows, loaded before the partials so both latencies overlap
@@ -246,10 +255,9 @@ HRM_DEVINL void ar_reduce_tile(const GemmArgs& a, int t, int par, int row, int e
 #pragma unroll
       for (int s = 0; s < 2; ++s) {
         if (s0 + s < a.tp_world) {
-          const float4* p =
-              reinterpret_cast<const float4*>(ar_slot(a, a.tp_rank, s0 + s, par, t) + (size_t)row * stride + c0);
+          const float4* p = ar_slot(a, a.tp_rank, s0 + s, par, t) + (c0 / 4) * kBM + row;
 #pragma unroll
-          for (int q = 0; q < kChunk / 4; ++q) v[s][q] = __ldcg(p + q);
+          for (int q = 0; q < kChunk / 4; ++q) v[s][q] = __ldcg(p + q * kBM);
         }
       }
 #pragma unroll
@@ -291,15 +299,9 @@ HRM_DEVINL void ar_tile_finish(const GemmArgs& a, int t, int row, int et, int ep
   if (et == 0) {
     trace_cta(a, 12);
     fence_acq_rel_sys();
-    for (int d = 0; d < a.tp_world; ++d) {
-      int* f = reinterpret_cast<int*>(reinterpret_cast<char*>(a.peers[d]) + a.off_tile_flags);
-      st_relaxed_sys(f + (size_t)a.tp_rank * a.ar_max_tiles + t, ep);
-    }
+    for (int d = 0; d < a.tp_world; ++d) st_relaxed_sys(ar_tile_flag(a, d, a.tp_rank, t), ep);
   }
-  if (et < a.tp_world) {
-    const int* f = reinterpret_cast<const int*>(reinterpret_cast<char*>(a.peers[a.tp_rank]) + a.off_tile_flags);
-    wait_flag_acquire(f + (size_t)et * a.ar_max_tiles + t, ep, a.status);
-  }
+  if (et < a.tp_world) wait_flag_acquire(ar_tile_flag(a, a.tp_rank, et, t), ep, a.status);
   asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
   if (et == 0) trace_cta(a, 14);   // every rank's partial of this tile has arrived
   ar_reduce_tile<BN>(a, t, ep & 1, row, et, ssq_red);
@@ -324,7 +326,6 @@ HRM_DEVINL void ar_oneshot(const GemmArgs& a, int row, int et, int ep, float* ss
   if (et < a.tp_world) wait_peer_flag(my_flags + et, ep, a.status);
   asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
   const int par = ep & 1;
-  const int stride = a.ar_tile_floats / kBM;   // tokens per row slot (max_bn)
   for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
     const int n = t * kBM + row;
     for (int c0 = 0; c0 < BN && c0 < a.M; c0 += kChunk) {
@@ -332,10 +333,10 @@ HRM_DEVINL void ar_oneshot(const GemmArgs& a, int row, int et, int ep, float* ss
 #pragma unroll
       for (int j = 0; j < kChunk; ++j) sum[j] = 0.f;
       for (int src = 0; src < a.tp_world; ++src) {
-        const float4* p = reinterpret_cast<const float4*>(ar_slot(a, a.tp_rank, src, par, t) + (size_t)row * stride + c0);
+        const float4* p = ar_slot(a, a.tp_rank, src, par, t) + (c0 / 4) * kBM + row;
 #pragma unroll
         for (int q = 0; q < kChunk / 4; ++q) {
-          const float4 v = __ldcg(p + q);
+          const float4 v = __ldcg(p + q * kBM);
           sum[4 * q] += v.x; sum[4 * q + 1] += v.y; sum[4 * q + 2] += v.z; sum[4 * q + 3] += v.w;
         }
       }
@@ -420,14 +421,13 @@ HRM_DEVINL void epilogue_store(const GemmArgs& a, int n_tile, int m_tile, int ro
     // this rank's partial tile -> its symmetric buffer ([token][128 rows], one slot per n tile)
     // push this rank's partial (16 tokens of this thread's row) into every rank's receive slot for this rank
     const int ep = *reinterpret_cast<const volatile int*>(a.epoch) + 1 + a.ep_offset;
-    const int stride = a.ar_tile_floats / kBM;
     float4 q[kChunk / 4];
 #pragma unroll
     for (int i = 0; i < kChunk / 4; ++i) q[i] = make_float4(v[4 * i] * sc, v[4 * i + 1] * sc, v[4 * i + 2] * sc, v[4 * i + 3] * sc);
     for (int dst = 0; dst < a.tp_world; ++dst) {
-      float4* p = reinterpret_cast<float4*>(ar_slot(a, dst, a.tp_rank, ep & 1, n_tile) + (size_t)row * stride + c0);
+      float4* p = ar_slot(a, dst, a.tp_rank, ep & 1, n_tile) + (c0 / 4) * kBM + row;
 #pragma unroll
-      for (int i = 0; i < kChunk / 4; ++i) p[i] = q[i];
+      for (int i = 0; i < kChunk / 4; ++i) p[i * kBM] = q[i];
     }
   } else {
 #pragma unroll

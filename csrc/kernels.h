@@ -91,7 +91,7 @@ struct ArgmaxXchg {
   const long long* peers;   // device table: base address of every rank's symmetric buffer (local one included)
   int rank, world, max_rows;
   long long off_keys;       // byte offset of int64 [2][world][max_rows] key slots in every buffer
-  long long off_flags;      // byte offset of int32 [world][max_rows] epoch flags in every buffer
+  long long off_flags;      // byte offset of the epoch flags [world][max_rows], one 128-byte line each
   int* epoch;               // this rank's exchange counter (local memory); the launch's last row advances it
   int* row_ticket;          // rows finished in the current launch (local memory; zero between launches)
   int* status;              // bounded-wait error word

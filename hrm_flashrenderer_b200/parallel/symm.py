@@ -11,10 +11,11 @@ Layout of the buffer (all offsets 256-byte aligned):
   reading the previous launch's data when this rank starts the next one);
 * ``final``     fp32 [max_tiles][max_bn][128]  -- spare reduction space;
 * ``flags``     int32 [world]: the epoch up to which each source rank's partials are complete (multi-phase chain);
-* ``tile flags`` int32 [world][max_tiles]: the epoch up to which source rank r's partial of tile t has arrived
+* ``tile flags`` int32 [world][max_tiles], one 128-byte line each: the epoch up to which source rank r's partial of
+  tile t has arrived
   (single-launch fused GEMM: each tile waits only for the same tile of the other ranks);
 * ``scalars``: the per-launch epoch counter and two CTA tickets, the argmax exchange's epoch and row ticket;
-* ``argmax keys`` int64 [2][world][argmax_rows] and ``argmax flags`` int32 [world][argmax_rows] (in the extra
+* ``argmax keys`` int64 [2][world][argmax_rows] and ``argmax flags`` int32 [world][argmax_rows] (one line each; extra
   area): the distributed greedy pick, where every rank pushes each row's packed (value, token) key to every rank.
 
 Flags carry an epoch number that every fused launch increments once, so a flag written by a previous launch is never
@@ -30,6 +31,7 @@ import torch.distributed as dist
 from .. import ops
 
 ALIGN = 256
+FLAG_LINE = 128   # every epoch flag owns one cache line (kernels: kFlagStrideInts ints)
 
 
 def _al(x: int) -> int:
@@ -46,14 +48,15 @@ class SymmetricWorkspace:
         self.off_final = _al(self.off_partials + 2 * world * max_tiles * tile_bytes)
         self.off_flags = _al(self.off_final + max_tiles * tile_bytes)
         self.off_tile_flags = _al(self.off_flags + 2 * max_tiles * 4)
-        self.off_scalars = _al(self.off_tile_flags + world * max_tiles * 4)
+        self.off_scalars = _al(self.off_tile_flags + world * max_tiles * FLAG_LINE)
         self.off_extra = _al(self.off_scalars + 4096)
         self.bytes = _al(self.off_extra + extra_bytes)
         # distributed argmax exchange inside the extra area
-        self.argmax_rows = int(min(4096, (extra_bytes - 2 * ALIGN) // (world * 20)))
+        per_row = world * (16 + FLAG_LINE)   # two key slots and one flag line per source rank
+        self.argmax_rows = int(min(ops.ARGMAX_XCHG_MAX_ROWS, (extra_bytes - 2 * ALIGN) // per_row))
         self.off_ax_keys = self.off_extra
         self.off_ax_flags = _al(self.off_ax_keys + 2 * world * self.argmax_rows * 8)
-        assert self.off_ax_flags + world * self.argmax_rows * 4 <= self.bytes
+        assert self.off_ax_flags + world * self.argmax_rows * FLAG_LINE <= self.bytes
         C = ops.ext()
         with torch.cuda.device(self.device):
             self.local_ptr, handle = C.symm_alloc(self.bytes)

@@ -30,7 +30,7 @@ class _SilentPeerWorkspace:
         self.off_final = al(2 * 2 * max_tiles * tile_bytes)
         self.off_flags = al(self.off_final + max_tiles * tile_bytes)
         self.off_tile_flags = al(self.off_flags + 2 * max_tiles * 4)
-        self.off_scalars = al(self.off_tile_flags + 2 * max_tiles * 4)
+        self.off_scalars = al(self.off_tile_flags + 2 * max_tiles * 128)
         size = al(self.off_scalars + 4096)
         with torch.cuda.device(dev):
             self.ptrs = [C.symm_alloc(size)[0], C.symm_alloc(size)[0]]

@@ -25,6 +25,8 @@ def test_tp_fused_allreduce_and_engine(n):
     lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
     rec = json.loads(lines[-1]) if lines else None
     print("mgpu record:", rec)   # visible with -s / in the failure report
+    if r.returncode != 0:
+        print("mgpu stderr tail:\n" + r.stderr[-6000:])
     assert r.returncode == 0 and rec is not None, (rec, r.stderr[-3000:])
     assert rec["world"] == n and rec["ok"] and rec["fused_ar_max_err"] < 1e-2, rec
     assert rec["tp_vs_tp1_70b_equal"], rec
