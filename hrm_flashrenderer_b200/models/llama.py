@@ -121,6 +121,12 @@ class LlamaW8:
         self.chain_layers = False        # decode: o_proj, gate/up, down, next QKV in one multi-phase GEMM launch
         self.prefill_overlap_chunks = 1  # TP prefill: row-parallel GEMM + all-reduce pipelined over this many chunks
         self.prefill_comm_sms = 8        # SMs the pipelined GEMM leaves free for the collective's kernels
+        # Per-step statistics for telemetry (off unless set before the first decode graph is captured): the greedy
+        # token's negative log-probability and the final hidden row of every sampled row, in fixed buffers that
+        # graph replays rewrite in place.
+        self.collect_stats = False
+        self.stat_nll: Optional[torch.Tensor] = None
+        self.stat_hidden: Optional[torch.Tensor] = None
 
     def enable_fused_collectives(self, group=None) -> None:
         """Allocate / exchange the NVLink symmetric buffers (collective over the TP group)."""
@@ -258,6 +264,8 @@ class LlamaW8:
             xl = xg.index_select(0, b.last_rows)
             nl = (ssq.index_select(1, b.last_rows).contiguous(), H, cfg.rms_eps)
         logits = ops.w8a16_linear(xl, self.head_q, self.head_s, out_dtype=torch.float32, in_norm=nl)
+        if self.collect_stats:
+            self._record_stats(logits, xl, nl)
         xchg_rows = min(self.symm.argmax_rows, ops.ARGMAX_XCHG_MAX_ROWS) if self.symm is not None else 0
         if p.world > 1 and logits.shape[0] <= xchg_rows:
             # global greedy pick through peer memory inside the argmax kernel (no NCCL call)
@@ -269,6 +277,26 @@ class LlamaW8:
             from ..parallel.dist import unpack_argmax
             return unpack_argmax(keys)
         return ops.argmax_rows(logits, 0)
+
+    def _record_stats(self, logits: torch.Tensor, xl: torch.Tensor, nl) -> None:
+        """``stat_nll[i] = logsumexp(logits_i) - max(logits_i)``: the cross-entropy of the greedy token (the
+        reference engine's per-step loss, ``scripts/deepseek_native_engine.sh:633-663,1112-1116``), reduced over the
+        vocabulary shards under tensor parallelism; ``stat_hidden[i]`` = the final RMS-normalised hidden row."""
+        rows = logits.shape[0]
+        if self.stat_nll is None or self.stat_nll.numel() < rows:
+            self.stat_nll = torch.zeros(max(rows, 64), dtype=torch.float32, device=logits.device)
+            self.stat_hidden = torch.zeros(max(rows, 64), self.cfg.hidden, dtype=torch.float32,
+                                           device=logits.device)
+        top = logits.max(dim=-1).values
+        if self.plan.world > 1:
+            self.comm.all_reduce_max_(top)
+        sumexp = torch.exp(logits - top[:, None]).sum(-1)
+        if self.plan.world > 1:
+            self.comm.all_reduce_(sumexp)
+        self.stat_nll[:rows].copy_(torch.log(sumexp))
+        ssq, H, eps = nl
+        inv = torch.rsqrt(ssq.sum(0) / H + eps)
+        self.stat_hidden[:rows].copy_(xl.float() * inv[:, None])
 
     @torch.no_grad()
     def hidden_states(self, b: BatchMeta) -> torch.Tensor:
@@ -445,6 +473,8 @@ class LlamaW8:
         xl = xg.index_select(0, b.last_rows)
         nl = (ssq.index_select(1, b.last_rows).contiguous(), H, cfg.rms_eps)
         logits = ops.w8a16_linear(xl, self.head_q, self.head_s, out_dtype=torch.float32, in_norm=nl)
+        if self.collect_stats:
+            self._record_stats(logits, xl, nl)
         xchg_rows = min(self.symm.argmax_rows, ops.ARGMAX_XCHG_MAX_ROWS) if self.symm is not None else 0
         if logits.shape[0] <= xchg_rows:
             return ops.argmax_exchange_(logits, p.vocab_start, self.symm)

@@ -81,11 +81,13 @@ def poll_once(engine, paths: IpcPaths, max_ctx: int, bos_id: int, tgen: int,
               log: Callable[[str], None] = print, telemetry=None) -> bool:
     """Serve one request if a prompt file is present; returns whether one was served.  With ``telemetry`` (a
     :class:`~hrm_flashrenderer_b200.serving.telemetry.Telemetry`) an idle poll sends an ``AWAITING_PROMPT`` packet
-    and every generated token one packet with its step and the prompt, as the reference engine does."""
+    and every generated token one packet with its step, the greedy token's cross-entropy, a projection of the final
+    hidden row and ``TokenID: <id>``, as the reference engine does (the model must have ``collect_stats`` on)."""
     if not paths.prompt.is_file():
         if telemetry is not None:
             telemetry.send(0, 0.0, None, "AWAITING_PROMPT")
         return False
+    model = getattr(engine, "model", None)
     lines = paths.prompt.read_text(errors="replace").splitlines()
     paths.prompt.unlink(missing_ok=True)
     log(f"> Received Prompt: {lines[0] if lines else ''}")
@@ -98,14 +100,20 @@ def poll_once(engine, paths: IpcPaths, max_ctx: int, bos_id: int, tgen: int,
     paths.tokens.unlink(missing_ok=True)
     paths.done.unlink(missing_ok=True)
     if n_new > 0:
-        prompt_line = lines[0] if lines else ""
         step = [len(ids)]
         with open(paths.tokens, "a") as f:
             def on_token(_i, t):
                 f.write(f"{int(t)}\n")
                 f.flush()
                 if telemetry is not None:
-                    telemetry.send(step[0], 0.0, None, prompt_line)
+                    # the step's greedy-token cross-entropy (0 for the first token, as in the reference) and the
+                    # final hidden row, recorded by the model in this step's forward
+                    loss, hid = 0.0, None
+                    if model is not None and getattr(model, "stat_nll", None) is not None:
+                        if step[0] > len(ids):
+                            loss = float(model.stat_nll[0])
+                        hid = model.stat_hidden[0]
+                    telemetry.send(step[0], loss, hid, f"TokenID: {int(t)}")
                 step[0] += 1
             engine.generate([ids], n_new, stop_on_eos=False, on_token=on_token)
     paths.done.write_text("done\n")
@@ -154,7 +162,8 @@ def main(argv=None) -> int:
     print(READY, flush=True)
     bos = int(getattr(cfg, "bos_token_id", 1) or 1)
     from .telemetry import Telemetry
-    tel = Telemetry(model_id=cfg.name)   # TELEM_ENABLE=1 / TELEM_PORT / TELEM_TARGET
+    tel = Telemetry(model_id=cfg.name, hidden=cfg.hidden)   # TELEM_ENABLE=1 / TELEM_PORT / TELEM_TARGET
+    eng.model.collect_stats = tel.enabled   # before the first decode graph is captured
     serve_forever(eng, IpcPaths.from_env(), a.max_seq_len, bos, max_requests=a.max_requests or None,
                   log=lambda s: print(s, flush=True), telemetry=tel if tel.enabled else None)
     return 0
