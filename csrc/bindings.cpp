@@ -170,7 +170,8 @@ void w8a16_gemm_residual(at::Tensor x, at::Tensor w, at::Tensor scale, at::Tenso
 void fill_resid_ar(hrm::GemmArgs& a, const at::Tensor& resid, const at::Tensor& gamma_next, const at::Tensor& xg_out,
                    const at::Tensor& ssq_out, const at::Tensor& peers, int64_t rank, int64_t world,
                    int64_t off_partials, int64_t off_final, int64_t off_flags, int64_t tile_floats, int64_t max_tiles,
-                   int64_t epoch_ptr, const at::Tensor& launch_ticket, int64_t off_tile_flags);
+                   int64_t epoch_ptr, const at::Tensor& launch_ticket, int64_t off_tile_flags, int64_t off_ll,
+                   int64_t ll);
 
 // Tensor-parallel residual GEMM fused with the all-reduce over peer memory (decode, M <= 64):
 //   resid = resid + sum_ranks(x_r @ W_r^T);  xg = resid * gamma_next;  ssq = per-tile sums of squares.
@@ -178,12 +179,12 @@ void w8a16_gemm_residual_ar(at::Tensor x, at::Tensor w, at::Tensor scale, at::Te
                             at::Tensor counters, at::Tensor gamma_next, at::Tensor xg_out, at::Tensor ssq_out,
                             at::Tensor peers, int64_t rank, int64_t world, int64_t off_partials, int64_t off_final,
                             int64_t off_flags, int64_t tile_floats, int64_t max_tiles, int64_t epoch_ptr,
-                            at::Tensor launch_ticket, int64_t off_tile_flags) {
+                            at::Tensor launch_ticket, int64_t off_tile_flags, int64_t off_ll, int64_t ll) {
   c10::cuda::CUDAGuard g(x.device());
   auto a = base_args(x, w, scale, c10::nullopt, ws, counters);
   if (a.M == 0) return;
   fill_resid_ar(a, resid, gamma_next, xg_out, ssq_out, peers, rank, world, off_partials, off_final, off_flags,
-                tile_floats, max_tiles, epoch_ptr, launch_ticket, off_tile_flags);
+                tile_floats, max_tiles, epoch_ptr, launch_ticket, off_tile_flags, off_ll, ll);
   auto p = hrm::gemm_plan(a.M, a.N, a.K, 0);
   check_ws(p, ws, counters);
   hrm::gemm_w8a16_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr<int8_t>(), hrm::EPI_RESID_AR, a, p,
@@ -193,7 +194,8 @@ void w8a16_gemm_residual_ar(at::Tensor x, at::Tensor w, at::Tensor scale, at::Te
 void fill_resid_ar(hrm::GemmArgs& a, const at::Tensor& resid, const at::Tensor& gamma_next, const at::Tensor& xg_out,
                    const at::Tensor& ssq_out, const at::Tensor& peers, int64_t rank, int64_t world,
                    int64_t off_partials, int64_t off_final, int64_t off_flags, int64_t tile_floats, int64_t max_tiles,
-                   int64_t epoch_ptr, const at::Tensor& launch_ticket, int64_t off_tile_flags) {
+                   int64_t epoch_ptr, const at::Tensor& launch_ticket, int64_t off_tile_flags, int64_t off_ll,
+                   int64_t ll) {
   CHECK_DTYPE(resid, at::kFloat); CHECK_DTYPE(gamma_next, at::kFloat); CHECK_DTYPE(xg_out, at::kHalf);
   CHECK_DTYPE(ssq_out, at::kFloat); CHECK_DTYPE(peers, at::kLong); CHECK_DTYPE(launch_ticket, at::kInt);
   TORCH_CHECK(resid.size(0) == a.M && resid.size(1) == a.N && resid.stride(1) == 1, "bad resid");
@@ -213,6 +215,8 @@ void fill_resid_ar(hrm::GemmArgs& a, const at::Tensor& resid, const at::Tensor& 
   a.off_final = off_final;
   a.off_flags = off_flags;
   a.off_tile_flags = off_tile_flags;
+  a.off_ll = off_ll;
+  a.ar_ll = ll != 0 ? 1 : 0;
   a.ar_tile_floats = (int)tile_floats;
   a.ar_max_tiles = (int)max_tiles;
   a.epoch = reinterpret_cast<int*>((uintptr_t)epoch_ptr);
@@ -333,7 +337,7 @@ void w8a16_chain(py::list phases, at::Tensor ws, at::Tensor counters, at::Tensor
       fill_resid_ar(a, t[4].cast<at::Tensor>(), t[5].cast<at::Tensor>(), t[6].cast<at::Tensor>(),
                     t[7].cast<at::Tensor>(), t[8].cast<at::Tensor>(), t[9].cast<int64_t>(), t[10].cast<int64_t>(),
                     t[11].cast<int64_t>(), t[12].cast<int64_t>(), t[13].cast<int64_t>(), t[14].cast<int64_t>(),
-                    t[15].cast<int64_t>(), t[16].cast<int64_t>(), t[17].cast<at::Tensor>(), 0);
+                    t[15].cast<int64_t>(), t[16].cast<int64_t>(), t[17].cast<at::Tensor>(), 0, 0, 0);
       d[p].epi = hrm::EPI_RESID_AR;
     } else if (kind == "swiglu") {
       a = base_args(x, w, scale, c10::nullopt, ws, counters);

@@ -364,6 +364,16 @@ HRM_DEVINL int ld_relaxed_sys(const int* p) {
   return v;
 }
 HRM_DEVINL void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+// 64-bit relaxed system-scope accesses: an aligned 64-bit access is single-copy atomic, so a word that carries its
+// own epoch next to its payload is either wholly old or wholly new to a peer that reads it.
+HRM_DEVINL void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+HRM_DEVINL unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 // Bounded relaxed poll for a flag to reach `want` (epochs only grow), then one acquire fence.  Records
 // kErrTimeoutPeer on timeout and returns false.
 HRM_DEVINL bool wait_flag_acquire(const int* p, int want, int* status) {

@@ -386,7 +386,10 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
           }
           epilogue_store<BN, EPI>(a, n_tile, m_tile, row, c0, v, stage, et, inv, ssq_red);
         }
-        if constexpr (EPI == EPI_RESID_AR) ar_tile_finish<BN>(a, n_tile, row, et, ep, ssq_red);
+        if constexpr (EPI == EPI_RESID_AR) {
+          if (a.ar_ll) ar_tile_finish_ll<BN>(a, n_tile, row, et, ep, ssq_red);
+          else ar_tile_finish<BN>(a, n_tile, row, et, ep, ssq_red);
+        }
       } else {
         // partial segment: write fp32 partial, take a ticket; the last segment of the tile reduces in k order
         const int first = owner_of((int64_t)tile * a.k_tiles, U, G);
@@ -424,7 +427,10 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
             sum_segments<BN>(ws_tile, nseg, row, c0, v);
             epilogue_store<BN, EPI>(a, n_tile, m_tile, row, c0, v, stage, et, inv, ssq_red);
           }
-          if constexpr (EPI == EPI_RESID_AR) ar_tile_finish<BN>(a, n_tile, row, et, ep, ssq_red);
+          if constexpr (EPI == EPI_RESID_AR) {
+            if (a.ar_ll) ar_tile_finish_ll<BN>(a, n_tile, row, et, ep, ssq_red);
+            else ar_tile_finish<BN>(a, n_tile, row, et, ep, ssq_red);
+          }
         }
       }
       if (et == 0) trace_mark(a, 6, seg);

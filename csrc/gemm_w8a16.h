@@ -82,6 +82,8 @@ struct GemmArgs {
   int tp_rank, tp_world;
   long long off_partials, off_final, off_flags;   // byte offsets inside every rank's buffer
   long long off_tile_flags;                       // int32 [world][ar_max_tiles]: epoch of each (source rank, tile)
+  long long off_ll;                               // u64 [2][world][ar_max_tiles][ar_tile_floats]: epoch-tagged words
+  int ar_ll;                                      // 1: epoch-tagged words (no fence, no flag); 0: partials + flags
   int ar_tile_floats;                             // floats per tile slot (max_bn * 128)
   int ar_max_tiles;
   int* epoch;                                     // this rank's launch epoch counter (in its symmetric buffer)

@@ -226,6 +226,12 @@ HRM_DEVINL float4* ar_slot(const GemmArgs& a, int dst, int src, int par, int til
   return reinterpret_cast<float4*>(base + (((size_t)par * a.tp_world + src) * a.ar_max_tiles + tile) *
                                               a.ar_tile_floats);
 }
+// Epoch-tagged receive slot of the flag-free variant: word (token m, row r) at m * 128 + r holds the fp32 partial in
+// its low half and the launch epoch in its high half.
+HRM_DEVINL unsigned long long* ar_ll_slot(const GemmArgs& a, int dst, int src, int par, int tile) {
+  unsigned long long* base = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(a.peers[dst]) + a.off_ll);
+  return base + (((size_t)par * a.tp_world + src) * a.ar_max_tiles + tile) * a.ar_tile_floats;
+}
 // Flags of the per-tile protocol: one 128-byte line per (source rank, tile), so pollers of different tiles and the
 // peers' flag stores never share a line.
 constexpr int kFlagStrideInts = 32;
@@ -305,6 +311,60 @@ HRM_DEVINL void ar_tile_finish(const GemmArgs& a, int t, int row, int et, int ep
   asm volatile("bar.sync 2, %0;" ::"n"(kEpiThreads) : "memory");
   if (et == 0) trace_cta(a, 14);   // every rank's partial of this tile has arrived
   ar_reduce_tile<BN>(a, t, ep & 1, row, et, ssq_red);
+  if (et == 0) trace_cta(a, 15);
+}
+
+// Flag-free variant of ar_tile_finish (GemmArgs::ar_ll): every pushed element is one 64-bit word {epoch, fp32}
+// stored with a single relaxed system-scope store, so a word is either wholly this launch's or not yet arrived.  The
+// tile's owner polls the words themselves (a source rank's 16 words in flight at a time), so there is no fence, no
+// flag store and no flag round trip; the NVLink bytes double (8 per element).  Sums stay in rank order.
+template <int BN>
+HRM_DEVINL void ar_tile_finish_ll(const GemmArgs& a, int t, int row, int et, int ep, float* ssq_red) {
+  if (et == 0) trace_cta(a, 12);
+  const unsigned want = (unsigned)ep;
+  const int n = t * kBM + row;
+  const uint64_t t0 = global_ns();
+  bool gave_up = false;
+  for (int c0 = 0; c0 < BN && c0 < a.M; c0 += kChunk) {
+    float xr[kChunk];
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      const int m = c0 + j;
+      xr[j] = (m < a.M && n < a.N) ? a.resid[(size_t)m * a.ldr + n] : 0.f;
+    }
+    float sum[kChunk];
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) sum[j] = 0.f;
+    for (int src = 0; src < a.tp_world; ++src) {
+      const unsigned long long* p = ar_ll_slot(a, a.tp_rank, src, ep & 1, t) + (size_t)c0 * kBM + row;
+      unsigned long long w[kChunk];
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) w[j] = ld_relaxed_sys_u64(p + (size_t)j * kBM);
+#pragma unroll 1
+      for (int j = 0; j < kChunk; ++j) {
+        unsigned long long x = w[j];
+        for (uint32_t i = 0; (unsigned)(x >> 32) != want && !gave_up; ++i) {   // not arrived yet: poll the word
+          __nanosleep(32);
+          x = ld_relaxed_sys_u64(p + (size_t)j * kBM);
+          if ((i & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) {
+            record_error(a.status, kErrTimeoutPeer);
+            gave_up = true;
+          }
+        }
+        w[j] = x;
+      }
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) sum[j] += __uint_as_float((unsigned)w[j]);
+    }
+    if (et == 0) trace_cta(a, 14);
+    float xn[kChunk];
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      const int m = c0 + j;
+      xn[j] = (m < a.M && n < a.N) ? xr[j] + sum[j] : 0.f;
+    }
+    store_residual_outputs<BN>(a, t, 0, row, c0, xn, et, ssq_red);
+  }
   if (et == 0) trace_cta(a, 15);
 }
 
@@ -421,6 +481,15 @@ HRM_DEVINL void epilogue_store(const GemmArgs& a, int n_tile, int m_tile, int ro
     // this rank's partial tile -> its symmetric buffer ([token][128 rows], one slot per n tile)
     // push this rank's partial (16 tokens of this thread's row) into every rank's receive slot for this rank
     const int ep = *reinterpret_cast<const volatile int*>(a.epoch) + 1 + a.ep_offset;
+    if (a.ar_ll) {   // epoch-tagged words: token-major per slot, a warp stores 32 consecutive words per token
+      const unsigned long long tag = (unsigned long long)(unsigned)ep << 32;
+      for (int dst = 0; dst < a.tp_world; ++dst) {
+        unsigned long long* w = ar_ll_slot(a, dst, a.tp_rank, ep & 1, n_tile) + (size_t)c0 * kBM + row;
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) st_relaxed_sys_u64(w + (size_t)j * kBM, tag | __float_as_uint(v[j] * sc));
+      }
+      return;
+    }
     float4 q[kChunk / 4];
 #pragma unroll
     for (int i = 0; i < kChunk / 4; ++i) q[i] = make_float4(v[4 * i] * sc, v[4 * i + 1] * sc, v[4 * i + 2] * sc, v[4 * i + 3] * sc);

@@ -57,6 +57,8 @@ LAUNCH_COUNTER = _LaunchCounter()
 
 # ------------------------------------------------------------------------------------------------ workspace
 _ATTN_MERGE = os.environ.get("HRM_ATTN_MERGE", "0") == "1"
+# fused all-reduce protocol: epoch-tagged 64-bit words (default) or fp32 partials + per-tile flags (HRM_AR_LL=0)
+_AR_LL = os.environ.get("HRM_AR_LL", "1") != "0"
 # split argmax over many CTAs per row (HRM_ARGMAX_SPLIT=0: one CTA per row)
 _ARGMAX_SPLIT = os.environ.get("HRM_ARGMAX_SPLIT", "1") != "0"
 
@@ -229,7 +231,8 @@ def w8a16_residual_ar_(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tens
     w = _ws_for(x2.shape[0], *weight_nk(qweight, scale), x.device)
     ext().w8a16_gemm_residual_ar(x2, qweight, scale, resid, w.ws, w.counters, gamma_next, xg_out, ssq_out, symm.peers,
                                  symm.rank, symm.world, symm.off_partials, symm.off_final, symm.off_flags,
-                                 symm.max_bn * 128, symm.max_tiles, symm.epoch_ptr, symm.ticket, symm.off_tile_flags)
+                                 symm.max_bn * 128, symm.max_tiles, symm.epoch_ptr, symm.ticket, symm.off_tile_flags,
+                                 symm.off_ll, 1 if (_AR_LL and symm.off_ll) else 0)
     LAUNCH_COUNTER.add()
     return resid
 

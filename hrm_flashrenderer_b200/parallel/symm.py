@@ -15,6 +15,8 @@ Layout of the buffer (all offsets 256-byte aligned):
   tile t has arrived
   (single-launch fused GEMM: each tile waits only for the same tile of the other ranks);
 * ``scalars``: the per-launch epoch counter and two CTA tickets, the argmax exchange's epoch and row ticket;
+* ``epoch-tagged words`` u64 [2][world][max_tiles][max_bn][128] (after the extra area): the flag-free variant of
+  the fused all-reduce, where every pushed element carries its launch epoch in the same 64-bit word;
 * ``argmax keys`` int64 [2][world][argmax_rows] and ``argmax flags`` int32 [world][argmax_rows] (one line each; extra
   area): the distributed greedy pick, where every rank pushes each row's packed (value, token) key to every rank.
 
@@ -50,13 +52,16 @@ class SymmetricWorkspace:
         self.off_tile_flags = _al(self.off_flags + 2 * max_tiles * 4)
         self.off_scalars = _al(self.off_tile_flags + world * max_tiles * FLAG_LINE)
         self.off_extra = _al(self.off_scalars + 4096)
-        self.bytes = _al(self.off_extra + extra_bytes)
+        # epoch-tagged receive words of the flag-free fused all-reduce: u64 [2][world][max_tiles][max_bn * 128]
+        self.off_ll = _al(self.off_extra + extra_bytes)
+        ll_bytes = 2 * world * max_tiles * max_bn * 128 * 8
+        self.bytes = _al(self.off_ll + ll_bytes)
         # distributed argmax exchange inside the extra area
         per_row = world * (16 + FLAG_LINE)   # two key slots and one flag line per source rank
         self.argmax_rows = int(min(ops.ARGMAX_XCHG_MAX_ROWS, (extra_bytes - 2 * ALIGN) // per_row))
         self.off_ax_keys = self.off_extra
         self.off_ax_flags = _al(self.off_ax_keys + 2 * world * self.argmax_rows * 8)
-        assert self.off_ax_flags + world * self.argmax_rows * FLAG_LINE <= self.bytes
+        assert self.off_ax_flags + world * self.argmax_rows * FLAG_LINE <= self.off_ll
         C = ops.ext()
         with torch.cuda.device(self.device):
             self.local_ptr, handle = C.symm_alloc(self.bytes)

@@ -32,6 +32,8 @@ class _SilentPeerWorkspace:
         self.off_tile_flags = al(self.off_flags + 2 * max_tiles * 4)
         self.off_scalars = al(self.off_tile_flags + 2 * max_tiles * 128)
         size = al(self.off_scalars + 4096)
+        self.off_ll = size                     # epoch-tagged words of the flag-free variant
+        size = al(size + 2 * 2 * max_tiles * max_bn * 128 * 8)
         with torch.cuda.device(dev):
             self.ptrs = [C.symm_alloc(size)[0], C.symm_alloc(size)[0]]
         self.peers = torch.tensor(self.ptrs, dtype=torch.int64, device=dev)
