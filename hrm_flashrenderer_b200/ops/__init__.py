@@ -57,8 +57,9 @@ LAUNCH_COUNTER = _LaunchCounter()
 
 # ------------------------------------------------------------------------------------------------ workspace
 _ATTN_MERGE = os.environ.get("HRM_ATTN_MERGE", "0") == "1"
-# fused all-reduce protocol: epoch-tagged 64-bit words (default) or fp32 partials + per-tile flags (HRM_AR_LL=0)
-_AR_LL = os.environ.get("HRM_AR_LL", "1") != "0"
+# fused all-reduce protocol: fp32 partials + per-tile flags (default), or epoch-tagged 64-bit words with no fence
+# and no flag (HRM_AR_LL=1; measured slower at TP = 8: twice the NVLink bytes)
+_AR_LL = os.environ.get("HRM_AR_LL", "0") == "1"
 # split argmax over many CTAs per row (HRM_ARGMAX_SPLIT=0: one CTA per row)
 _ARGMAX_SPLIT = os.environ.get("HRM_ARGMAX_SPLIT", "1") != "0"
 
