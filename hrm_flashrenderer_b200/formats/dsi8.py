@@ -180,18 +180,26 @@ class DSI8File:
         return [k for k in self.records if k != META_NAME]
 
     def get(self, name: str, copy: bool = False) -> Tensorish:
-        """Tensor ``name``: a view into the mapping, or an independent copy with ``copy=True``."""
+        """Tensor ``name``: a view into the mapping, or an independent copy with ``copy=True``.
+
+        Record payloads follow names of any length, so an fp32 array (a row-scale vector or an F32 tensor) can start
+        at an offset that is not a multiple of 4; such an array is always returned as an aligned copy (vectorised
+        CPU kernels and pinned-memory copies assume element alignment).  The int8 matrices need no alignment and
+        stay views."""
         ttype, dims, off = self.records[name]
         cp = (lambda a: a.copy()) if copy else (lambda a: a)
+
+        def f32(count: int, at: int) -> np.ndarray:
+            a = np.frombuffer(self._mm, dtype=np.float32, count=count, offset=at)
+            return a.copy() if (copy or at % 4 != 0) else a
         if ttype == TTYPE_Q8:
             rows = dims[0]
             cols = dims[1] if len(dims) > 1 else 1
-            scale = np.frombuffer(self._mm, dtype=np.float32, count=rows, offset=off)
+            scale = f32(rows, off)
             q = np.frombuffer(self._mm, dtype=np.int8, count=rows * cols, offset=off + rows * 4).reshape(rows, cols)
-            return QTensor(torch.from_numpy(cp(q)), torch.from_numpy(cp(scale)))
+            return QTensor(torch.from_numpy(cp(q)), torch.from_numpy(scale))
         if ttype == TTYPE_F32:
-            cnt = int(np.prod(dims))
-            return torch.from_numpy(cp(np.frombuffer(self._mm, dtype=np.float32, count=cnt, offset=off)))
+            return torch.from_numpy(f32(int(np.prod(dims)), off))
         raise ValueError(f"{name}: unsupported tensor type {ttype} (only q8 is supported; q4 is rejected)")
 
     def load_all(self) -> Dict[str, Tensorish]:

@@ -100,3 +100,21 @@ def test_views_share_the_mapping_and_outlive_close(good):
     assert torch.equal(v.q, c.q)
     c.q[0, 0] += 1                             # a copy is independent of the file's contents
     assert not torch.equal(v.q, c.q)
+
+
+def test_misaligned_fp32_records_come_back_aligned(good):
+    """Payloads follow names of any length, so fp32 data (row scales, norm vectors) can start at an offset that is
+    not a multiple of 4 -- the architecture's own names already produce such offsets.  Those arrays come back as
+    aligned copies with the right values; int8 matrices stay views."""
+    ref = synth_weights(CFG, seed=0)
+    with DSI8File(good) as f:
+        offs = {k: f.records[k][2] for k in f.names()}
+        assert any(o % 4 for o in offs.values()), "no misaligned payload in this file"
+        for k in f.names():
+            t = f.get(k)
+            for arr in ((t.scale,) if isinstance(t, QTensor) else (t,)):
+                assert arr.data_ptr() % 4 == 0, k
+            if isinstance(t, QTensor):
+                assert torch.equal(t.q, ref[k].q) and torch.equal(t.scale, ref[k].scale), k
+            else:
+                assert torch.equal(t, ref[k].float()), k
