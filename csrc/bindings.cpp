@@ -593,6 +593,22 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scratch") = py::none());
   m.def("decode_prepare", &decode_prepare_bs);
   m.def("decode_advance", &decode_advance);
+  // per CTA and segment of the even stream-K split: (cta, tile, nseg, segidx), for the host-side test
+  m.def("stream_k_segments", [](int64_t tiles, int64_t k_tiles, int64_t G) {
+    std::vector<int64_t> out;
+    const long long U = tiles * k_tiles;
+    for (long long c = 0; c < G; ++c) {
+      const long long u0 = c * U / G, u1 = (c + 1) * U / G;
+      for (long long u = u0; u < u1;) {
+        const long long tile = u / k_tiles, f = tile * k_tiles, end = std::min(f + k_tiles, u1);
+        int nseg = 0, segidx = 0;
+        hrm::tile_segments(f, (int)k_tiles, u, U, G, nseg, segidx);
+        out.insert(out.end(), {c, tile, nseg, segidx});
+        u = end;
+      }
+    }
+    return out;
+  });
   m.def("sm_count", []() { return hrm::gemm_sm_count(); });
   m.def("argmax_rows_xchg", &argmax_rows_xchg);
   m.def("grad_clip_factor", [](at::Tensor g, double clip, at::Tensor partial, at::Tensor scalars) {

@@ -79,9 +79,8 @@ HRM_DEVINL void chain_epi_phase(const GemmArgs& a, int64_t u0, int64_t u1, int64
         epilogue_store<BN, EPI>(a, n_tile, m_tile, row, c0, v, stage, et, inv, ssq_red);
       }
     } else {
-      const int first = owner_of((int64_t)tile * a.k_tiles, U, G);
-      const int nseg = owner_of(tile_end - 1, U, G) - first + 1;
-      const int segidx = (int)blockIdx.x - first;
+      int nseg, segidx;   // every phase runs on all CTAs, so a phase may have fewer units than CTAs
+      tile_segments((int64_t)tile * a.k_tiles, a.k_tiles, u, U, G, nseg, segidx);
       float* ws_tile = a.ws + (size_t)tile * a.max_seg * (BN * kBM);
       float* mine = ws_tile + (size_t)segidx * (BN * kBM);
       for (int c0 = 0; c0 < BN; c0 += kChunk) {
@@ -457,7 +456,8 @@ GemmPlan gemm_chain_phase_plan(int M, int N, int K, int ctas) {
   bool any_split = false;
   for (int t = 0; t < p.tiles; ++t) {
     const int64_t f = (int64_t)t * p.k_tiles, l = f + p.k_tiles - 1;
-    const int n = owner_host(l, U, G) - owner_host(f, U, G) + 1;
+    // with fewer units than CTAs every unit is its own segment (see tile_segments)
+    const int n = U >= G ? owner_host(l, U, G) - owner_host(f, U, G) + 1 : p.k_tiles;
     max_seg = std::max(max_seg, n);
     any_split |= n > 1;
   }

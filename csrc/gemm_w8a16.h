@@ -53,6 +53,25 @@ struct TileWalk {
   }
 };
 
+// k-segments of the stream-K tile whose units are [f, f + k_tiles) when U units are split evenly over G CTAs (CTA c
+// holds [c*U/G, (c+1)*U/G)): the number of CTAs holding part of the tile, and the index of the segment that starts
+// at unit u.  With at least as many units as CTAs every CTA holds a unit, so a tile's owners are consecutive CTAs.
+// With fewer units than CTAs (a multi-phase chain runs every phase on all SMs) each CTA holds at most one unit and
+// the owners are spread out with empty CTAs between them: a tile then has one segment per unit.  Shared by the
+// kernels and the host-side test of the partition.
+HRM_TILE_HD void tile_segments(long long f, int k_tiles, long long u, long long U, long long G, int& nseg,
+                               int& segidx) {
+  auto owner = [U, G](long long x) { return (int)(((x + 1) * G - 1) / U); };
+  if (U >= G) {
+    const int first = owner(f);
+    nseg = owner(f + k_tiles - 1) - first + 1;
+    segidx = owner(u) - first;
+  } else {
+    nseg = k_tiles;
+    segidx = (int)(u - f);
+  }
+}
+
 struct GemmArgs {
   int M, N, K;
   int k_tiles, n_tiles, tiles, max_seg;     // filled by the launcher from the plan (k_tiles = units per tile)

@@ -65,3 +65,23 @@ def test_toggle_round_trip():
         assert not C.gemm_m_fastest()
     finally:
         C.set_gemm_m_fastest(was)
+
+
+@pytest.mark.parametrize("tiles,k_tiles,ctas", [(8, 4, 148), (10, 32, 148), (64, 4, 148), (3, 1, 148),
+                                                (1, 200, 148), (40, 5, 148), (16, 16, 148), (5, 7, 16)])
+def test_stream_k_segments_cover_every_tile_once(tiles, k_tiles, ctas):
+    """The segment count / index of every tile (``tile_segments`` in ``csrc/gemm_w8a16.h``, used by the multi-phase
+    chain, which runs every phase on all SMs even when a phase has fewer units than CTAs): the CTAs holding part of a
+    tile number their segments 0..nseg-1 exactly once, so the last ticket is always taken and re-armed."""
+    f = ops.ext().stream_k_segments(tiles, k_tiles, ctas)
+    segs = [tuple(f[i:i + 4]) for i in range(0, len(f), 4)]
+    by_tile = {}
+    for c, t, nseg, idx in segs:
+        by_tile.setdefault(t, []).append((nseg, idx, c))
+    assert sorted(by_tile) == list(range(tiles))
+    for t, lst in by_tile.items():
+        nsegs = {n for n, _, _ in lst}
+        assert len(nsegs) == 1, (t, lst)
+        n = nsegs.pop()
+        assert sorted(i for _, i, _ in lst) == list(range(n)), (t, lst)
+        assert [i for _, i, _ in sorted(lst, key=lambda x: x[2])] == list(range(n))   # k order follows CTA order
