@@ -395,16 +395,17 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant
         const int first = owner_of((int64_t)tile * a.k_tiles, U, G);
         const int nseg = owner_of(tile_end - 1, U, G) - first + 1;
         const int segidx = (int)blockIdx.x - first;
-        // partial of this segment, row-major per thread ([row][BN]): a thread's chunk is 64 contiguous bytes
+        // partial of this segment, column-group-major: float4 (row r, tokens 4g..4g+3) at g * 128 + r, so every warp
+        // store / load of a token group is 512 contiguous bytes
         float* ws_tile = a.ws + (size_t)tile * a.max_seg * (BN * kBM);
         float* mine = ws_tile + (size_t)segidx * (BN * kBM);
         for (int c0 = 0; c0 < BN; c0 += kChunk) {
           float v[kChunk];
           tmem_ld_acc<BN, S::NACC>(acc_addr + (uint32_t)c0, v, valid);
-          float4* dst = reinterpret_cast<float4*>(mine + (size_t)row * BN + c0);
+          float4* dst = reinterpret_cast<float4*>(mine) + (c0 / 4) * kBM + row;
 #pragma unroll
           for (int q = 0; q < kChunk / 4; ++q)
-            __stcg(dst + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+            __stcg(dst + q * kBM, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
         }
         tc_fence_before();
         mbar_arrive(&aempty[acc]);

@@ -121,23 +121,24 @@ HRM_DEVINL void tmem_ld_acc(uint32_t taddr, float (&v)[16], uint32_t valid) {
 }
 
 // Sum of a tile's k-segment partials for one thread's row and 16 columns [c0, c0 + 16), in k order (segment 0
-// first), so the result does not depend on which CTA finished last.  Partials are [segment][row][BN] fp32 in L2;
+// first), so the result does not depend on which CTA finished last.  Partials are [segment][BN / 4][128 rows] float4
+// in L2 (column-group-major: a warp reads 512 contiguous bytes per token group);
 // the loads of four segments are issued before their adds, so a tile cut into many segments (narrow projections
 // at high tensor-parallel degree) costs a few L2 round trips instead of one per segment.
 template <int BN>
 HRM_DEVINL void sum_segments(const float* ws_tile, int nseg, int row, int c0, float (&v)[16]) {
   const size_t seg4 = (size_t)BN * 128 / 4;   // float4s per segment partial
-  const float4* p0 = reinterpret_cast<const float4*>(ws_tile + (size_t)row * BN + c0);
+  const float4* p0 = reinterpret_cast<const float4*>(ws_tile) + (c0 / 4) * 128 + row;
   float4 acc[4];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) acc[q] = __ldcg(p0 + q);
+  for (int q = 0; q < 4; ++q) acc[q] = __ldcg(p0 + q * 128);
   int sg = 1;
   for (; sg + 4 <= nseg; sg += 4) {
     float4 t[4][4];
 #pragma unroll
     for (int s = 0; s < 4; ++s)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) t[s][q] = __ldcg(p0 + (size_t)(sg + s) * seg4 + q);
+      for (int q = 0; q < 4; ++q) t[s][q] = __ldcg(p0 + (size_t)(sg + s) * seg4 + q * 128);
 #pragma unroll
     for (int s = 0; s < 4; ++s)
 #pragma unroll
@@ -148,7 +149,7 @@ HRM_DEVINL void sum_segments(const float* ws_tile, int nseg, int row, int c0, fl
   for (; sg < nseg; ++sg) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const float4 t = __ldcg(p0 + (size_t)sg * seg4 + q);
+      const float4 t = __ldcg(p0 + (size_t)sg * seg4 + q * 128);
       acc[q].x += t.x; acc[q].y += t.y; acc[q].z += t.z; acc[q].w += t.w;
     }
   }
