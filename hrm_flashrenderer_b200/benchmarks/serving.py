@@ -5,7 +5,7 @@
    latency, output tokens (tokenizer or chars/4) and tok/s; summary per (scenario, mode, route_hint): mean / p50 /
    p95 / min / max latency, mean tok/s, majority selected lane, score = tok/s / p95.  Writes raw.csv, summary.csv,
    summary.txt.
-2. ``trace``: a Poisson arrival trace (N requests at R req/s, seed 0) of mixed-mode prompts =
+2. ``trace`` -- the continuous-batching serving workload: a Poisson arrival trace (N requests at R req/s, seed 0) of mixed-mode prompts =
    random-token system prefix (256) + retrieved-context block (3 chunks x 256 random tokens) + user part (uniform
    64..1024), outputs uniform 64..512 tokens, greedy; run in-process against the continuous-batching scheduler
    (token ids, no tokenizer), reporting p50 / p99 TTFT and aggregate generated tok/s.

@@ -1,4 +1,4 @@
-"""Tensor-parallel collective-GEMM op sweep: one process per GPU under torchrun.
+"""Tensor-parallel collective-GEMM op sweep (Llama-70B projection shapes): one process per GPU under torchrun.
 
     torchrun --nproc-per-node N -m hrm_flashrenderer_b200.benchmarks.tp_sweep [--m 1,8,64,512,4096]
 

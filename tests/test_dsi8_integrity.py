@@ -1,6 +1,6 @@
 """Corrupt DSI8 files fail at open with a message that says what is wrong: truncation anywhere (header, a record
-header, a payload), a missing tensor, a wrong shape or a wrong tensor type.  Failure made on the host (SURVEY-style
-"corrupt a weight file"); nothing reaches a device."""
+header, a payload), a missing tensor, a wrong shape or a wrong tensor type.  The failure is made on the host (a
+corrupted weight file); nothing reaches a device."""
 import struct
 
 import torch
