@@ -4,8 +4,8 @@ plus p50 TTFT, on synthetic random-token prompts with random-init weights.
     python bench.py --gpus N --steps K --warmup W          # this framework (one process per GPU via torchrun)
     python bench.py --impl reference --gpus N ...          # the reference's torch.distributed NCCL TP build
 
-Config (the headline benchmark workload): 80 layers, hidden 8192, 64 q / 8 kv heads (head_dim 128), FFN 28672, vocab 128256,
-llama3 RoPE; batch 16 sequences, each prefilled with 4096 random tokens, then decode.  A "step" is one decode step
+Config (the headline benchmark workload): 80 layers, hidden 8192, 64 q / 8 kv heads (head_dim 128), FFN 28672,
+vocab 128256, llama3 RoPE; batch 16 sequences, each prefilled with 4096 random tokens, then decode.  A "step" is one decode step
 of the whole batch (16 new tokens).  W untimed warm-up steps, then exactly K steps timed with CUDA events between
 barriers + synchronizes; the per-rank times are reduced with MAX.  Weights (70 GB int8 at TP=1) are far larger than
 L2 (126 MB), so every step streams them from HBM ("inputs larger than L2").
