@@ -235,6 +235,13 @@ def run_ours(a):
 
 
 # ====================================================================================================== reference
+def _block_reference_extension() -> None:
+    """Make ``from . import _ext`` inside the reference's ``flashattention_custom`` raise ImportError (a ``None``
+    entry in ``sys.modules``), whether or not a build of the extension is present, so its ops take their own
+    PyTorch fallbacks."""
+    sys.modules["flashattention_custom._ext"] = None
+
+
 def run_reference(a):
     ref_root = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref_root, "engine")):
@@ -255,7 +262,7 @@ def run_reference(a):
     # N.  A None entry in sys.modules makes `from . import _ext` raise ImportError, so flashattention_custom.ops
     # takes its own PyTorch fallbacks (ops.py:19-72): the reference as `pip install` builds it on a host without
     # the extension.
-    sys.modules["flashattention_custom._ext"] = None
+    _block_reference_extension()
     import flashattention_custom.ops as fops
     if getattr(fops, "_HAS_EXT", False):
         _emit(rank, {"impl": "reference", "unavailable": "refusing to run the reference's sm75 attention extension "
