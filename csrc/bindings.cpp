@@ -535,6 +535,22 @@ void argmax_rows_xchg(at::Tensor logits, int64_t vocab_start, at::Tensor tokens,
                           cur_stream());
 }
 
+// C [M, N] fp32 = A [M, K] . B [N, K]^T on the tensor cores (A, B bf16 or f16, same type, unit inner stride).
+void gemm_nt(at::Tensor A, at::Tensor B, at::Tensor C) {
+  c10::cuda::CUDAGuard g(A.device());
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm_nt: CUDA tensors");
+  TORCH_CHECK(A.scalar_type() == B.scalar_type() &&
+              (A.scalar_type() == at::kBFloat16 || A.scalar_type() == at::kHalf), "gemm_nt: A, B both bf16 or f16");
+  CHECK_DTYPE(C, at::kFloat);
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm_nt: 2-D operands");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm_nt: unit inner stride");
+  TORCH_CHECK(A.size(1) == B.size(1), "gemm_nt: K mismatch");
+  TORCH_CHECK(C.size(0) == A.size(0) && C.size(1) == B.size(0), "gemm_nt: C must be [M, N]");
+  hrm::gemm_nt_launch(A.data_ptr(), (int)A.stride(0), B.data_ptr(), (int)B.stride(0), C.data_ptr<float>(),
+                      (int)C.stride(0), (int)A.size(0), (int)B.size(0), (int)A.size(1),
+                      A.scalar_type() == at::kBFloat16, nullptr, cur_stream());
+}
+
 void decode_prepare_bs(at::Tensor positions, at::Tensor tables, int64_t block_size, c10::optional<at::Tensor> active,
                        at::Tensor slots, at::Tensor context_lens) {
   c10::cuda::CUDAGuard g(positions.device());
@@ -611,6 +627,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
   m.def("sm_count", []() { return hrm::gemm_sm_count(); });
   m.def("argmax_rows_xchg", &argmax_rows_xchg);
+  m.def("gemm_nt", &gemm_nt);
   m.def("grad_clip_factor", [](at::Tensor g, double clip, at::Tensor partial, at::Tensor scalars) {
     c10::cuda::CUDAGuard gd(g.device());
     TORCH_CHECK(g.is_cuda() && g.scalar_type() == at::kFloat && g.is_contiguous(), "g: contiguous f32 CUDA");

@@ -99,6 +99,11 @@ struct ArgmaxXchg {
 void argmax_xchg_launch(const float* logits, int M, int V, int ld, int vocab_start, unsigned long long* keys,
                         int64_t* tokens, unsigned long long* scratch, int sms, const ArgmaxXchg& x, cudaStream_t s);
 
+// Dense NT GEMM for the experiments plane: C [M, N] fp32 = A [M, K] . B [N, K]^T, A and B row-major bf16 (or f16),
+// leading dimensions in elements (multiples of 8), N and ldc multiples of 4 (gemm_nt.cu).
+void gemm_nt_launch(const void* A, int lda, const void* B, int ldb, float* C, int ldc, int M, int N, int K,
+                    bool bf16, int* status, cudaStream_t stream);
+
 void decode_prepare_launch(const int* positions, const int* tables, int maxb, int bs, const int* active, int* slots,
                            int* context_lens, int B, cudaStream_t s);
 void decode_advance_launch(const int64_t* tokens, int64_t* ids, int* positions, const int* active, int B,

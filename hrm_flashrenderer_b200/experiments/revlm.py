@@ -18,6 +18,7 @@ run in bf16 on the GPU (fp32 accumulate, fp32 residual halves and master weights
 from __future__ import annotations
 
 import math
+import os
 import struct
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Tuple
@@ -119,8 +120,52 @@ def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
     return Fn.gelu(x, approximate="tanh")
 
 
+# Dense products on CUDA run on this library's tensor-core NT GEMM (HRM_REVLM_TC=0: PyTorch's bf16 matmul instead).
+TC_GEMM = os.environ.get("HRM_REVLM_TC", "1") != "0"
+
+
+class _TcMatmul(torch.autograd.Function):
+    """``y = x @ W`` (``x [..., K]`` fp32, ``W [K, N]`` fp32, possibly a column slice) with bf16 operands and fp32
+    accumulation on the tensor-core NT GEMM (``ops.gemm_nt``, C = A . B^T with both operands K-major).  Backward goes
+    through the same kernel after transposing into that form, as the reference trainer does around its WMMA GEMM
+    (llm_engine.cu:500-524): ``dx = dy . W^T`` is ``gemm_nt(dy, W)`` and ``dW = x^T . dy`` is
+    ``gemm_nt(x^T, dy^T)``."""
+
+    @staticmethod
+    def forward(ctx, x, w):
+        from .. import ops
+        K, N = w.shape
+        xb = x.reshape(-1, K).to(torch.bfloat16).contiguous()
+        y = ops.gemm_nt(xb, w.t().to(torch.bfloat16).contiguous())
+        ctx.save_for_backward(xb, w)
+        ctx.xshape = x.shape
+        return y.view(*x.shape[:-1], N)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from .. import ops
+        xb, w = ctx.saved_tensors
+        K, N = w.shape
+        dyb = dy.reshape(-1, N).to(torch.bfloat16).contiguous()
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = ops.gemm_nt(dyb, w.to(torch.bfloat16).contiguous()).view(ctx.xshape)
+        if ctx.needs_input_grad[1]:
+            dw = ops.gemm_nt(xb.t().contiguous(), dyb.t().contiguous())
+        return dx, dw
+
+
+def _tc_ok(x: torch.Tensor, w: torch.Tensor) -> bool:
+    """Shapes the NT GEMM takes in both directions: every leading dimension a multiple of 8 elements."""
+    K, N = w.shape
+    M = x.numel() // max(1, K)
+    return TC_GEMM and x.is_cuda and K % 8 == 0 and N % 8 == 0 and M % 8 == 0 and M > 0
+
+
 def _mm(x: torch.Tensor, w: torch.Tensor, lowp: bool) -> torch.Tensor:
     if lowp:
+        if _tc_ok(x, w):
+            return _TcMatmul.apply(x, w)
         return (x.to(torch.bfloat16) @ w.to(torch.bfloat16)).float()
     return x.float() @ w
 

@@ -569,6 +569,19 @@ def argmax_rows(logits: torch.Tensor, vocab_start: int = 0, keys: Optional[torch
     return tokens
 
 
+def gemm_nt(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``a [M, K] @ b [N, K]^T`` -> fp32 ``[M, N]`` (bf16 or f16 operands, fp32 accumulate) on the tensor cores; the
+    experiments plane's dense product (the reference trainer's WMMA GEMM, llm_engine.cu:471-524).  CPU tensors
+    use fp32 math of the same rounded operands."""
+    if out is None:
+        out = torch.empty(a.shape[0], b.shape[0], dtype=torch.float32, device=a.device)
+    if not a.is_cuda:
+        return torch.matmul(a.float(), b.float().t(), out=out)
+    ext().gemm_nt(a, b, out)
+    LAUNCH_COUNTER.add()
+    return out
+
+
 ARGMAX_XCHG_MAX_ROWS = 256
 
 

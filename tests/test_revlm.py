@@ -69,3 +69,23 @@ def test_ckpt_v11_roundtrip(tmp_path):
     cfg, t2, f2 = load_ckpt(str(p), TINY)
     assert cfg == TINY and torch.equal(f2, flat)
     assert all(np.array_equal(x, y) for x, y in zip(tables, t2))
+
+
+def test_tc_matmul_wiring_on_cpu():
+    """The tensor-core product's autograd wiring (forward and both backward products expressed as C = A . B^T) on
+    the op's CPU reference path, against PyTorch autograd on the same bf16-rounded operands."""
+    import torch
+    from hrm_flashrenderer_b200.experiments.revlm import _TcMatmul
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(3, 16, 32, generator=g).requires_grad_(True)
+    w = torch.randn(64, 48, generator=g)[:32].requires_grad_(False)
+    w = w.clone().requires_grad_(True)
+    dy = torch.randn(3, 16, 48, generator=g)
+    y = _TcMatmul.apply(x, w)
+    y.backward(dy)
+    xr = x.detach().bfloat16().float().requires_grad_(True)
+    wr = w.detach().bfloat16().float().requires_grad_(True)
+    (xr @ wr).backward(dy.bfloat16().float())
+    torch.testing.assert_close(y, (xr @ wr).detach(), rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(x.grad, xr.grad, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(w.grad, wr.grad, rtol=1e-5, atol=1e-5)
