@@ -26,6 +26,7 @@ mistaken for a current one and no reset pass is needed between launches.
 from __future__ import annotations
 
 import warnings
+from typing import Dict
 
 import torch
 import torch.distributed as dist
@@ -40,28 +41,48 @@ def _al(x: int) -> int:
     return (x + ALIGN - 1) // ALIGN * ALIGN
 
 
+def symm_layout(world: int, max_tiles: int, max_bn: int, extra_bytes: int = 1 << 20) -> Dict[str, int]:
+    """Byte offsets of every region of one rank's symmetric buffer (all 256-byte aligned, in this order) and the
+    total size.  ``regions`` maps each region to its (offset, length); the regions never overlap."""
+    tile_bytes = max_bn * 128 * 4
+    L: Dict[str, int] = {}
+    L["off_partials"] = 0
+    L["off_final"] = _al(2 * world * max_tiles * tile_bytes)
+    L["off_flags"] = _al(L["off_final"] + max_tiles * tile_bytes)
+    L["off_tile_flags"] = _al(L["off_flags"] + 2 * max_tiles * 4)
+    L["off_scalars"] = _al(L["off_tile_flags"] + world * max_tiles * FLAG_LINE)
+    L["off_extra"] = _al(L["off_scalars"] + 4096)
+    # epoch-tagged receive words of the flag-free fused all-reduce: u64 [2][world][max_tiles][max_bn * 128]
+    L["off_ll"] = _al(L["off_extra"] + extra_bytes)
+    ll_bytes = 2 * world * max_tiles * max_bn * 128 * 8
+    L["bytes"] = _al(L["off_ll"] + ll_bytes)
+    # distributed argmax exchange inside the extra area: two key slots and one flag line per source rank and row
+    per_row = world * (16 + FLAG_LINE)
+    L["argmax_rows"] = int(min(ops.ARGMAX_XCHG_MAX_ROWS, (extra_bytes - 2 * ALIGN) // per_row))
+    L["off_ax_keys"] = L["off_extra"]
+    L["off_ax_flags"] = _al(L["off_ax_keys"] + 2 * world * L["argmax_rows"] * 8)
+    L["regions"] = {
+        "partials": (L["off_partials"], 2 * world * max_tiles * tile_bytes),
+        "final": (L["off_final"], max_tiles * tile_bytes),
+        "flags": (L["off_flags"], 2 * max_tiles * 4),
+        "tile_flags": (L["off_tile_flags"], world * max_tiles * FLAG_LINE),
+        "scalars": (L["off_scalars"], 4096),
+        "argmax_keys": (L["off_ax_keys"], 2 * world * L["argmax_rows"] * 8),
+        "argmax_flags": (L["off_ax_flags"], world * L["argmax_rows"] * FLAG_LINE),
+        "ll_words": (L["off_ll"], ll_bytes),
+    }
+    return L
+
+
 class SymmetricWorkspace:
     def __init__(self, rank: int, world: int, device: torch.device, max_tiles: int = 1024, max_bn: int = 64,
                  group=None, extra_bytes: int = 1 << 20):
         self.rank, self.world, self.device = rank, world, torch.device(device)
         self.max_tiles, self.max_bn = max_tiles, max_bn
-        tile_bytes = max_bn * 128 * 4
-        self.off_partials = 0
-        self.off_final = _al(self.off_partials + 2 * world * max_tiles * tile_bytes)
-        self.off_flags = _al(self.off_final + max_tiles * tile_bytes)
-        self.off_tile_flags = _al(self.off_flags + 2 * max_tiles * 4)
-        self.off_scalars = _al(self.off_tile_flags + world * max_tiles * FLAG_LINE)
-        self.off_extra = _al(self.off_scalars + 4096)
-        # epoch-tagged receive words of the flag-free fused all-reduce: u64 [2][world][max_tiles][max_bn * 128]
-        self.off_ll = _al(self.off_extra + extra_bytes)
-        ll_bytes = 2 * world * max_tiles * max_bn * 128 * 8
-        self.bytes = _al(self.off_ll + ll_bytes)
-        # distributed argmax exchange inside the extra area
-        per_row = world * (16 + FLAG_LINE)   # two key slots and one flag line per source rank
-        self.argmax_rows = int(min(ops.ARGMAX_XCHG_MAX_ROWS, (extra_bytes - 2 * ALIGN) // per_row))
-        self.off_ax_keys = self.off_extra
-        self.off_ax_flags = _al(self.off_ax_keys + 2 * world * self.argmax_rows * 8)
-        assert self.off_ax_flags + world * self.argmax_rows * FLAG_LINE <= self.off_ll
+        L = symm_layout(world, max_tiles, max_bn, extra_bytes)
+        for k in ("off_partials", "off_final", "off_flags", "off_tile_flags", "off_scalars", "off_extra", "off_ll",
+                  "bytes", "argmax_rows", "off_ax_keys", "off_ax_flags"):
+            setattr(self, k, L[k])
         C = ops.ext()
         with torch.cuda.device(self.device):
             self.local_ptr, handle = C.symm_alloc(self.bytes)
