@@ -93,6 +93,7 @@ class LaneArgs:
     num_kv_blocks: int = 0
     heartbeat_timeout_s: float = 30.0   # a TP peer silent this long is treated as lost
     packed_cache_dir: str = ""           # per-rank packed-shard cache for DSI8 exports (default: HRM_PACKED_CACHE)
+    fused_collectives: bool = True       # TP > 1 on CUDA: in-kernel NVLink all-reduce / argmax (False: NCCL calls)
 
 
 def build_engine(a: LaneArgs, rank: int, world: int, comm):
@@ -109,6 +110,10 @@ def build_engine(a: LaneArgs, rank: int, world: int, comm):
         model = LlamaW8.from_dsi8(a.model, rank=rank, world=world, device=dev, comm=comm, max_pos=a.max_seq_len + 16,
                                   cache_dir=a.packed_cache_dir or os.environ.get("HRM_PACKED_CACHE") or None)
         cfg = model.cfg
+    if a.fused_collectives:
+        # the row-parallel GEMMs reduce over peer memory inside the kernel and the greedy pick exchanges its argmax
+        # keys inside the argmax kernel; collective over the TP group, and a no-op at TP = 1 or on the CPU
+        model.enable_fused_collectives()
     if a.num_kv_blocks:
         nb = a.num_kv_blocks
     elif dev.type == "cuda":
@@ -313,9 +318,12 @@ def main(argv=None):
     ap.add_argument("--ready_file", default=None, help="write host:port here once listening")
     ap.add_argument("--master_port", type=int, default=29555)
     ap.add_argument("--num_kv_blocks", type=int, default=0)
+    ap.add_argument("--nccl_collectives", action="store_true",
+                    help="TP all-reduce and argmax through NCCL calls instead of the fused peer-memory kernels")
     args = ap.parse_args(argv)
     lane = LaneArgs(args.model, args.world, args.max_seq_len, args.prefill_chunk_size, args.max_batch, args.device,
-                    master_port=args.master_port, num_kv_blocks=args.num_kv_blocks)
+                    master_port=args.master_port, num_kv_blocks=args.num_kv_blocks,
+                    fused_collectives=not args.nccl_collectives)
     spawn_lane(lane, _RpcEntry(args.host, args.port, args.authkey.encode(), args.tokenizer_model, args.ready_file))
 
 

@@ -262,6 +262,8 @@ def build_arg_parser() -> argparse.ArgumentParser:
     ap.add_argument("--max_prompt_tokens", type=int, default=int(os.environ.get("DSI8_MAX_PROMPT_TOKENS", "2048")))
     ap.add_argument("--native_request_timeout_s", type=float, default=180.0)
     ap.add_argument("--device", default="cuda:0")
+    ap.add_argument("--nccl_collectives", action="store_true",
+                    help="TP lane: all-reduce and argmax through NCCL calls instead of the fused peer-memory kernels")
     return ap
 
 
@@ -292,7 +294,8 @@ def main(argv=None):
         from .daemon import LaneArgs, spawn_lane
         src, tok = resolve_model(args.llm_model, REPO_ROOT / "llm_models")
         lane = LaneArgs(src, args.world, args.max_seq_len, args.prefill_chunk_size, args.max_batch, "cuda",
-                        master_port=int(os.environ.get("HRM_LANE_MASTER_PORT", str(29600 + args.port % 1000))))
+                        master_port=int(os.environ.get("HRM_LANE_MASTER_PORT", str(29600 + args.port % 1000))),
+                        fused_collectives=not args.nccl_collectives)
         spawn_lane(lane, _HttpEntry(args, str(hrm_model), args.tokenizer_model or tok))
         return
     if args.backend == "echo":

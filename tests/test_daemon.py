@@ -49,3 +49,18 @@ def test_daemon_world2_rpc(tmp_path):
     finally:
         if p.poll() is None:
             p.kill()
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_build_engine_enables_fused_collectives(monkeypatch, fused):
+    """The lane builds its shard with the in-kernel NVLink collectives unless told to use NCCL calls (the call is
+    a no-op at TP = 1 and on the CPU, so here it is only counted)."""
+    from hrm_flashrenderer_b200.models.llama import LlamaW8
+    from hrm_flashrenderer_b200.serving.daemon import LaneArgs, build_engine
+    calls = []
+    monkeypatch.setattr(LlamaW8, "enable_fused_collectives", lambda self, group=None: calls.append(group))
+    a = LaneArgs("synthetic:tiny", 1, max_seq_len=256, max_batch=2, device="cpu", num_kv_blocks=64,
+                 fused_collectives=fused)
+    eng = build_engine(a, 0, 1, None)
+    assert calls == ([None] if fused else [])
+    assert len(eng.generate([[1, 2, 3]], 2, stop_on_eos=False)[0]) == 2
