@@ -551,6 +551,38 @@ void gemm_nt(at::Tensor A, at::Tensor B, at::Tensor C) {
                       A.scalar_type() == at::kBFloat16, nullptr, cur_stream());
 }
 
+// Trainer causal attention: every operand contiguous fp32 [B, T, H, D] (D 16 or 32) on one device, lse [B, H, T].
+static void check_flash_train(std::initializer_list<const at::Tensor*> ts, const at::Tensor& ref,
+                              const at::Tensor& lse) {
+  TORCH_CHECK(ref.dim() == 4 && (ref.size(3) == 16 || ref.size(3) == 32), "flash_train: [B, T, H, D] with D 16 or 32");
+  for (const at::Tensor* t : ts) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->sizes() == ref.sizes() &&
+                    t->device() == ref.device(), "flash_train: contiguous f32 CUDA tensors of one shape and device");
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(t->data_ptr()) & 15) == 0, "flash_train: 16-byte aligned operands");
+  }
+  TORCH_CHECK(lse.is_cuda() && lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.device() == ref.device() &&
+                  lse.dim() == 3 && lse.size(0) == ref.size(0) && lse.size(1) == ref.size(2) && lse.size(2) == ref.size(1),
+              "flash_train: lse contiguous f32 [B, H, T] on the same device");
+}
+
+void flash_train_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse) {
+  c10::cuda::CUDAGuard g(q.device());
+  check_flash_train({&q, &k, &v, &o}, q, lse);
+  hrm::flash_train_fwd_launch(q.data_ptr<float>(), k.data_ptr<float>(), v.data_ptr<float>(), o.data_ptr<float>(),
+                              lse.data_ptr<float>(), (int)q.size(0), (int)q.size(1), (int)q.size(2), (int)q.size(3),
+                              cur_stream());
+}
+
+void flash_train_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, at::Tensor dout,
+                     at::Tensor dq, at::Tensor dk, at::Tensor dv) {
+  c10::cuda::CUDAGuard g(q.device());
+  check_flash_train({&q, &k, &v, &o, &dout, &dq, &dk, &dv}, q, lse);
+  hrm::flash_train_bwd_launch(q.data_ptr<float>(), k.data_ptr<float>(), v.data_ptr<float>(), o.data_ptr<float>(),
+                              lse.data_ptr<float>(), dout.data_ptr<float>(), dq.data_ptr<float>(), dk.data_ptr<float>(),
+                              dv.data_ptr<float>(), (int)q.size(0), (int)q.size(1), (int)q.size(2), (int)q.size(3),
+                              cur_stream());
+}
+
 void decode_prepare_bs(at::Tensor positions, at::Tensor tables, int64_t block_size, c10::optional<at::Tensor> active,
                        at::Tensor slots, at::Tensor context_lens) {
   c10::cuda::CUDAGuard g(positions.device());
@@ -628,6 +660,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sm_count", []() { return hrm::gemm_sm_count(); });
   m.def("argmax_rows_xchg", &argmax_rows_xchg);
   m.def("gemm_nt", &gemm_nt);
+  m.def("flash_train_fwd", &flash_train_fwd, "trainer causal attention forward (o, lse)");
+  m.def("flash_train_bwd", &flash_train_bwd, "trainer causal attention backward (dq, dk, dv)");
   m.def("grad_clip_factor", [](at::Tensor g, double clip, at::Tensor partial, at::Tensor scalars) {
     c10::cuda::CUDAGuard gd(g.device());
     TORCH_CHECK(g.is_cuda() && g.scalar_type() == at::kFloat && g.is_contiguous(), "g: contiguous f32 CUDA");

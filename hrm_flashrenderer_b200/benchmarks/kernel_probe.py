@@ -1,7 +1,7 @@
 """Run ONE hand-written kernel at one Llama-3.1-70B shape a few times (one GPU): the small, self-ending case that a
 profiler capture wraps.
 
-    python -m hrm_flashrenderer_b200.benchmarks.kernel_probe --op NAME [--reps 3]
+    python -m hrm_flashrenderer_b200.benchmarks.kernel_probe --op NAME [--reps 3] [--time]
 
 Each op builds its inputs once, runs ``--reps`` launches of the kernel, synchronizes and checks the bounded-wait
 status word; the printed line gives the op, its shape and the algorithmic bytes / FLOPs of one launch, so a
@@ -15,6 +15,9 @@ profiler's per-launch DRAM bytes and duration can be set against them.  Ops (ker
 * ``norm_prep``     RMSNorm inputs of 16 tokens (norm_prep_kernel)
 * ``embed``         int8 embedding lookup of 16 tokens (embed_q8_kernel)
 * ``argmax``        split greedy pick over 16 x 128256 logits (argmax_kernel)
+* ``flash_train_fwd`` / ``flash_train_bwd``  the trainer's causal attention at 128 sequences x 512 tokens, 8 heads of
+  16 (flash_train_fwd_kernel; flash_train_dq_kernel + flash_train_dkv_kernel).  FLOPs are the executed multiply-adds
+  x 2: 4 D per visible (query, key) pair forward, 14 D backward (S and dP are computed in both passes).
 """
 from __future__ import annotations
 
@@ -107,24 +110,54 @@ def _argmax(dev):
     return run, f"M16xV{LLAMA31_70B.vocab}", logits.numel() * 4, 0.0
 
 
+def _flash_train(dev, backward: bool):
+    B, T, H, D = 128, 512, 8, 16
+    g = torch.Generator(device=dev).manual_seed(0)
+    q, k, v, do = (torch.randn(B, T, H, D, generator=g, device=dev) for _ in range(4))
+    o, lse = ops.flash_train_fwd(q, k, v)
+    pairs = B * H * T * (T + 1) // 2
+    row = B * T * H * D * 4
+    if backward:
+        run = lambda: ops.flash_train_bwd(q, k, v, o, lse, do)
+        return run, f"B{B}xT{T}xH{H}xD{D}", 8 * row + B * H * T * 4, 14.0 * D * pairs
+    run = lambda: ops.flash_train_fwd(q, k, v)
+    return run, f"B{B}xT{T}xH{H}xD{D}", 4 * row + B * H * T * 4, 4.0 * D * pairs
+
+
 OPS = {"gemm_prefill": _gemm_prefill, "gemm_decode_tp8": _gemm_decode_tp8, "attn_prefill": _attn_prefill,
-       "attn_decode_tp8": _attn_decode_tp8, "norm_prep": _norm_prep, "embed": _embed, "argmax": _argmax}
+       "attn_decode_tp8": _attn_decode_tp8, "norm_prep": _norm_prep, "embed": _embed, "argmax": _argmax,
+       "flash_train_fwd": lambda dev: _flash_train(dev, False), "flash_train_bwd": lambda dev: _flash_train(dev, True)}
 
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="hrm-flash-kernel-probe")
     ap.add_argument("--op", required=True, choices=sorted(OPS))
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--time", action="store_true",
+                    help="after 3 warm-up calls, time --reps calls with CUDA events and print us per call")
     a = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
     run, shape, nbytes, flops = OPS[a.op](dev)
     torch.cuda.synchronize()
-    for _ in range(a.reps):
-        run()
-    torch.cuda.synchronize()
+    rec = {"op": a.op, "shape": shape, "bytes_per_launch": nbytes, "flops_per_launch": flops, "reps": a.reps}
+    if a.time:
+        for _ in range(3):
+            run()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t0.record()
+        for _ in range(a.reps):
+            run()
+        t1.record()
+        torch.cuda.synchronize()
+        us = t0.elapsed_time(t1) * 1e3 / a.reps
+        rec.update(us_per_call=round(us, 2), gbs=round(nbytes / us / 1e3, 1), tflops=round(flops / us / 1e6, 2))
+    else:
+        for _ in range(a.reps):
+            run()
+        torch.cuda.synchronize()
     ops.check_status(dev)
-    print(json.dumps({"op": a.op, "shape": shape, "bytes_per_launch": nbytes, "flops_per_launch": flops,
-                      "reps": a.reps}), flush=True)
+    print(json.dumps(rec), flush=True)
     return 0
 
 

@@ -12,8 +12,9 @@ Design: every weight is a view of ONE flat fp32 parameter laid out exactly as ch
 (``weights_floats`` / ``pack_W``, :344-385), so checkpoints are a single copy, data-parallel gradient exchange is one
 all-reduce of one buffer, and the optimizer is one fused kernel over it (``csrc/train_ops.cu``).  The backward of the
 layer stack is reversible: activations are not stored; each layer's inputs are rebuilt from its outputs
-(x2 = y2 - G(y1), x1 = y1 - F(x2)) while walking the layers backwards, as the reference does.  Matmuls and attention
-run in bf16 on the GPU (fp32 accumulate, fp32 residual halves and master weights).
+(x2 = y2 - G(y1), x1 = y1 - F(x2)) while walking the layers backwards, as the reference does.  On the GPU the
+matmuls run on the tensor-core NT GEMM with bf16 operands and fp32 accumulation, and causal attention on the fp32
+flash kernels (``csrc/flash_train.cu``); residual halves and master weights are fp32.
 """
 from __future__ import annotations
 
@@ -170,6 +171,40 @@ def _mm(x: torch.Tensor, w: torch.Tensor, lowp: bool) -> torch.Tensor:
     return x.float() @ w
 
 
+# Causal attention on CUDA runs on this library's trainer flash kernels for head dims 16 and 32 (HRM_REVLM_FLASH=0:
+# PyTorch's scaled_dot_product_attention instead).
+FLASH_ATTN = os.environ.get("HRM_REVLM_FLASH", "1") != "0"
+
+
+class _FlashAttn(torch.autograd.Function):
+    """Causal attention of ``[B, T, H, Dh]`` fp32 rows on ``ops.flash_train_fwd`` / ``ops.flash_train_bwd``: the
+    forward keeps only the output and the per-row log-sum-exp, and the backward recomputes the probabilities tile by
+    tile, as the reference trainer's flash kernels do (llm_engine.cu:856-1146)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v):
+        from .. import ops
+        q, k, v = (t.float().contiguous() for t in (q, k, v))
+        o, lse = ops.flash_train_fwd(q, k, v)
+        ctx.save_for_backward(q, k, v, o, lse)
+        return o
+
+    @staticmethod
+    def backward(ctx, dout):
+        from .. import ops
+        return ops.flash_train_bwd(*ctx.saved_tensors, dout.float().contiguous())
+
+
+def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, lowp: bool) -> torch.Tensor:
+    """``q, k, v [B, T, H, Dh]`` -> fp32 ``[B, T, H, Dh]``."""
+    if FLASH_ATTN and q.is_cuda and q.shape[-1] in (16, 32):
+        return _FlashAttn.apply(q, k, v)
+    dt = torch.bfloat16 if lowp else torch.float32
+    o = Fn.scaled_dot_product_attention(q.transpose(1, 2).to(dt), k.transpose(1, 2).to(dt),
+                                        v.transpose(1, 2).to(dt), is_causal=True)
+    return o.transpose(1, 2).float()
+
+
 def f_block(cfg: RevConfig, x2, gf, Wq, Wk, Wv, Wo, cos, sin, lowp):
     B, T, _ = x2.shape
     n = rms(x2, gf, cfg.eps)
@@ -177,10 +212,7 @@ def f_block(cfg: RevConfig, x2, gf, Wq, Wk, Wv, Wo, cos, sin, lowp):
     k = _mm(n, Wk, lowp).view(B, T, cfg.heads, cfg.dh)
     v = _mm(n, Wv, lowp).view(B, T, cfg.heads, cfg.dh)
     q, k = apply_rope(q, cos[:T], sin[:T]), apply_rope(k, cos[:T], sin[:T])
-    dt = torch.bfloat16 if lowp else torch.float32
-    o = Fn.scaled_dot_product_attention(q.transpose(1, 2).to(dt), k.transpose(1, 2).to(dt),
-                                        v.transpose(1, 2).to(dt), is_causal=True)
-    o = o.transpose(1, 2).reshape(B, T, cfg.dhf).float()
+    o = causal_attention(q, k, v, lowp).reshape(B, T, cfg.dhf)
     return _mm(o, Wo, lowp)
 
 

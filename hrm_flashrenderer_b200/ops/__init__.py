@@ -582,6 +582,46 @@ def gemm_nt(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None
     return out
 
 
+def _causal_attention_math(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """fp32 causal attention of ``[B, T, H, D]`` rows: (output, base-2 log-sum-exp ``[B, H, T]``)."""
+    B, T, H, D = q.shape
+    s = torch.einsum("bihd,bjhd->bhij", q.float(), k.float()) * (math.log2(math.e) / math.sqrt(D))
+    s = s.masked_fill(torch.ones(T, T, dtype=torch.bool, device=q.device).triu(1), -float("inf"))
+    m = s.amax(-1, keepdim=True)
+    p = torch.exp2(s - m)
+    l = p.sum(-1, keepdim=True)
+    o = torch.einsum("bhij,bjhd->bihd", p / l, v.float())
+    return o.contiguous(), (m + torch.log2(l))[..., 0].contiguous()
+
+
+def flash_train_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Causal attention for the trainer: ``q, k, v`` contiguous fp32 ``[B, T, H, D]`` (D 16 or 32) -> ``(o, lse)``
+    with ``o`` like ``q`` and ``lse`` the base-2 log-sum-exp of each row's scaled scores, ``[B, H, T]`` (the
+    reference trainer's ``flash_fwd_hf``, llm_engine.cu:856-948).  CPU tensors use the same math in PyTorch."""
+    if not q.is_cuda:
+        return _causal_attention_math(q, k, v)
+    B, T, H, _ = q.shape
+    o = torch.empty_like(q)
+    lse = torch.empty(B, H, T, dtype=torch.float32, device=q.device)
+    ext().flash_train_fwd(q, k, v, o, lse)
+    LAUNCH_COUNTER.add()
+    return o, lse
+
+
+def flash_train_bwd(q, k, v, o, lse, dout) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Gradients of :func:`flash_train_fwd` (``dq, dk, dv``), from the saved output and log-sum-exp: a dQ pass and a
+    dK/dV pass, deterministic (llm_engine.cu:950-1146).  CPU tensors go through autograd of the same math."""
+    if not q.is_cuda:
+        with torch.enable_grad():
+            qq, kk, vv = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+            oo, _ = _causal_attention_math(qq, kk, vv)
+            return torch.autograd.grad(oo, (qq, kk, vv), dout.float())
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ext().flash_train_bwd(q, k, v, o, lse, dout.contiguous(), dq, dk, dv)
+    LAUNCH_COUNTER.add(2)
+    return dq, dk, dv
+
+
 ARGMAX_XCHG_MAX_ROWS = 256
 
 
