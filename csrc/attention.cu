@@ -350,16 +350,36 @@ HRM_DEVINL unsigned long long argmax_exchange_row(const ArgmaxXchg& x, int row, 
   return best;
 }
 
-template <bool XCHG>
+// Key of one logit: the plain argmax key, or (SAMPLE) the key of v / T + Gumbel noise for logits at or above the
+// row's top-k threshold (0, i.e. never the maximum, below it); a row with inv_temp == 0 stays greedy.
+template <bool SAMPLE>
+HRM_DEVINL unsigned long long pick_key(float v, uint32_t id, float it, float th, unsigned long long rk) {
+  if constexpr (!SAMPLE) {
+    return argmax_key(v, id);
+  } else {
+    if (it == 0.f) return argmax_key(v, id);
+    if (!(v >= th)) return 0ull;
+    return argmax_key(fmaf(v, it, gumbel_noise(rk, id)), id);
+  }
+}
+
+template <bool XCHG, bool SAMPLE>
 __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ logits, int V, int ld, int chunk,
                                                      int vocab_start, unsigned long long* acc,
                                                      unsigned long long* ticket, unsigned long long* keys,
-                                                     int64_t* tokens, const ArgmaxXchg x) {
+                                                     int64_t* tokens, const ArgmaxXchg x, const SampleArgs sp) {
   pdl_wait();
   pdl_trigger();
   const int row = blockIdx.y;
   const float* lr = logits + (size_t)row * ld;
   const int i0 = blockIdx.x * chunk, i1 = min(V, i0 + chunk);
+  float it = 0.f, th = -INFINITY;
+  unsigned long long rk = 0ull;
+  if constexpr (SAMPLE) {
+    it = sp.inv_temp[row];
+    th = sp.thresh != nullptr ? sp.thresh[row] : -INFINITY;
+    rk = sample_row_key(sp.seed[row], sp.pos[row]);
+  }
   unsigned long long best = 0ull;
   const bool vec = ((reinterpret_cast<uintptr_t>(lr + i0) & 15) == 0) && (chunk % 4 == 0);
   if (vec) {
@@ -368,22 +388,22 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ l
     for (int j = threadIdx.x; j < n4; j += blockDim.x) {
       const float4 v = l4[j];
       const uint32_t id = (uint32_t)(vocab_start + i0 + 4 * j);
-      unsigned long long k = argmax_key(v.x, id);
-      unsigned long long t = argmax_key(v.y, id + 1);
+      unsigned long long k = pick_key<SAMPLE>(v.x, id, it, th, rk);
+      unsigned long long t = pick_key<SAMPLE>(v.y, id + 1, it, th, rk);
       k = t > k ? t : k;
-      t = argmax_key(v.z, id + 2);
+      t = pick_key<SAMPLE>(v.z, id + 2, it, th, rk);
       k = t > k ? t : k;
-      t = argmax_key(v.w, id + 3);
+      t = pick_key<SAMPLE>(v.w, id + 3, it, th, rk);
       k = t > k ? t : k;
       best = k > best ? k : best;
     }
     for (int i = i0 + 4 * n4 + threadIdx.x; i < i1; i += blockDim.x) {
-      const unsigned long long k = argmax_key(lr[i], (uint32_t)(vocab_start + i));
+      const unsigned long long k = pick_key<SAMPLE>(lr[i], (uint32_t)(vocab_start + i), it, th, rk);
       best = k > best ? k : best;
     }
   } else {
     for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-      const unsigned long long k = argmax_key(lr[i], (uint32_t)(vocab_start + i));
+      const unsigned long long k = pick_key<SAMPLE>(lr[i], (uint32_t)(vocab_start + i), it, th, rk);
       best = k > best ? k : best;
     }
   }
@@ -426,8 +446,8 @@ void argmax_launch(const float* logits, int M, int V, int ld, int vocab_start, u
   const int grid_x = (V + chunk - 1) / chunk;
   unsigned long long* acc = scratch;
   unsigned long long* ticket = scratch != nullptr ? scratch + kArgmaxMaxRows : nullptr;
-  launch_maybe_pdl(argmax_kernel<false>, dim3(grid_x, M), dim3(256), 0, s, logits, V, ld, chunk, vocab_start, acc,
-                   ticket, keys, tokens, ArgmaxXchg{});
+  launch_maybe_pdl(argmax_kernel<false, false>, dim3(grid_x, M), dim3(256), 0, s, logits, V, ld, chunk, vocab_start,
+                   acc, ticket, keys, tokens, ArgmaxXchg{}, SampleArgs{});
 }
 
 void argmax_xchg_launch(const float* logits, int M, int V, int ld, int vocab_start, unsigned long long* keys,
@@ -443,8 +463,34 @@ void argmax_xchg_launch(const float* logits, int M, int V, int ld, int vocab_sta
   const int grid_x = (V + chunk - 1) / chunk;
   unsigned long long* acc = scratch;
   unsigned long long* ticket = scratch != nullptr ? scratch + kArgmaxMaxRows : nullptr;
-  launch_maybe_pdl(argmax_kernel<true>, dim3(grid_x, M), dim3(256), 0, s, logits, V, ld, chunk, vocab_start, acc,
-                   ticket, keys, tokens, x);
+  launch_maybe_pdl(argmax_kernel<true, false>, dim3(grid_x, M), dim3(256), 0, s, logits, V, ld, chunk, vocab_start,
+                   acc, ticket, keys, tokens, x, SampleArgs{});
+}
+
+void argmax_sample_launch(const float* logits, int M, int V, int ld, int vocab_start, unsigned long long* keys,
+                          int64_t* tokens, unsigned long long* scratch, int sms, const SampleArgs& sp,
+                          const ArgmaxXchg* x, cudaStream_t s) {
+  if (M == 0) return;
+  if (sp.inv_temp == nullptr || sp.seed == nullptr || sp.pos == nullptr)
+    throw std::runtime_error("sampled argmax: inv_temp, seed and pos are required");
+  if (x != nullptr) {
+    if (M > x->max_rows) throw std::runtime_error("argmax exchange: more rows than the symmetric key slots hold");
+    if (x->peers == nullptr || x->epoch == nullptr || x->row_ticket == nullptr || x->world < 1 || x->rank < 0 ||
+        x->rank >= x->world)
+      throw std::runtime_error("argmax exchange: bad peer table / counters");
+  }
+  const int c = scratch != nullptr ? argmax_chunks(M, V, sms) : 1;
+  int chunk = (V + c - 1) / c;
+  chunk = (chunk + 3) & ~3;
+  const int grid_x = (V + chunk - 1) / chunk;
+  unsigned long long* acc = scratch;
+  unsigned long long* ticket = scratch != nullptr ? scratch + kArgmaxMaxRows : nullptr;
+  if (x != nullptr)
+    launch_maybe_pdl(argmax_kernel<true, true>, dim3(grid_x, M), dim3(256), 0, s, logits, V, ld, chunk, vocab_start,
+                     acc, ticket, keys, tokens, *x, sp);
+  else
+    launch_maybe_pdl(argmax_kernel<false, true>, dim3(grid_x, M), dim3(256), 0, s, logits, V, ld, chunk,
+                     vocab_start, acc, ticket, keys, tokens, ArgmaxXchg{}, sp);
 }
 
 }  // namespace hrm

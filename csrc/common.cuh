@@ -349,6 +349,29 @@ HRM_DEVINL uint32_t float_order(float f) {
 HRM_DEVINL unsigned long long argmax_key(float v, uint32_t idx) {
   return ((unsigned long long)float_order(v) << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
 }
+HRM_DEVINL float order_to_float(uint32_t o) {
+  return __uint_as_float((o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o);
+}
+
+// Sampling noise.  A counter-based generator: the SplitMix64 output mix (Steele, Lea and Flood, "Fast splittable
+// pseudorandom number generators", OOPSLA 2014) applied to a per-(seed, position) key plus the golden-ratio step
+// times the global token id, so every rank of a tensor-parallel group draws the same noise for a token id whatever
+// its vocabulary shard, and a request's draw depends only on its seed and position (not on the batch it is in).
+constexpr unsigned long long kGoldenGamma = 0x9E3779B97F4A7C15ull;
+HRM_DEVINL unsigned long long mix64(unsigned long long z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+HRM_DEVINL unsigned long long sample_row_key(unsigned long long seed, int pos) {
+  return mix64(seed + kGoldenGamma * (unsigned long long)((long long)pos + 1));
+}
+// Standard Gumbel variate -log(-log(u)) for token `id` under row key `rk`; u in (0, 1) from the top 23 bits.
+HRM_DEVINL float gumbel_noise(unsigned long long rk, uint32_t id) {
+  const unsigned long long h = mix64(rk + kGoldenGamma * ((unsigned long long)id + 1ull));
+  const float u = ((float)(h >> 41) + 0.5f) * (1.0f / 8388608.0f);
+  return -logf(-logf(u));
+}
 
 // ---------------------------------------------------------------- peer-memory (NVLink) flags
 // Used by the fused all-reduce GEMM epilogue and the distributed argmax exchange.

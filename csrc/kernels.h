@@ -106,6 +106,22 @@ struct ArgmaxXchg {
 void argmax_xchg_launch(const float* logits, int M, int V, int ld, int vocab_start, unsigned long long* keys,
                         int64_t* tokens, unsigned long long* scratch, int sms, const ArgmaxXchg& x, cudaStream_t s);
 
+// Sampled pick (temperature / top-k, Gumbel-max) on the argmax path; per-row arrays on the device.
+struct SampleArgs {
+  const float* inv_temp;              // [M] 1 / temperature; 0 keeps the row greedy
+  const float* thresh;                // [M] keep logits >= thresh (-inf: every token); nullptr: every token
+  const unsigned long long* seed;     // [M] per-request seed
+  const int* pos;                     // [M] position of the row's input token (the noise counter)
+};
+void argmax_sample_launch(const float* logits, int M, int V, int ld, int vocab_start, unsigned long long* keys,
+                          int64_t* tokens, unsigned long long* scratch, int sms, const SampleArgs& sp,
+                          const ArgmaxXchg* x, cudaStream_t s);
+// Top-k thresholds: out[r] = k[r]-th largest of x[r, 0:n] (-inf when k[r] <= 0 or >= n); candidates: the values
+// above thresh[r] then thresh[r] up to k[r] slots, then -inf, in [rows, kmax] (k[r] <= kmax) (sampling.cu).
+void kth_largest_launch(const float* x, int rows, int n, int ld, const int* k, float* out, cudaStream_t s);
+void topk_candidates_launch(const float* x, int rows, int n, int ld, const float* thresh, const int* k, int kmax,
+                            float* cand, cudaStream_t s);
+
 // Dense NT GEMM for the experiments plane: C [M, N] fp32 = A [M, K] . B [N, K]^T, A and B row-major bf16 (or f16),
 // leading dimensions in elements (multiples of 8), N and ldc multiples of 4 (gemm_nt.cu).
 void gemm_nt_launch(const void* A, int lda, const void* B, int ldb, float* C, int ldc, int M, int N, int K,
