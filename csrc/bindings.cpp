@@ -535,6 +535,84 @@ void argmax_rows_xchg(at::Tensor logits, int64_t vocab_start, at::Tensor tokens,
                           cur_stream());
 }
 
+// Sampled pick on the argmax path (temperature / top-k, Gumbel-max); with ``peers`` defined the rows' keys are
+// exchanged over peer memory as in argmax_rows_xchg.
+void argmax_rows_sample(at::Tensor logits, int64_t vocab_start, c10::optional<at::Tensor> keys, at::Tensor tokens,
+                        c10::optional<at::Tensor> scratch, at::Tensor inv_temp, c10::optional<at::Tensor> thresh,
+                        at::Tensor seed, at::Tensor pos, c10::optional<at::Tensor> peers, int64_t rank, int64_t world,
+                        int64_t max_rows, int64_t off_keys, int64_t off_flags, int64_t epoch_ptr,
+                        int64_t row_ticket_ptr) {
+  c10::cuda::CUDAGuard g(logits.device());
+  CHECK_DTYPE(logits, at::kFloat); CHECK_DTYPE(tokens, at::kLong);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be [M, V] row-major");
+  const int64_t M = logits.size(0);
+  CHECK_DTYPE(inv_temp, at::kFloat); CHECK_DTYPE(seed, at::kLong); CHECK_DTYPE(pos, at::kInt);
+  for (const at::Tensor* t : {&inv_temp, &seed, &pos, &tokens})
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->numel() >= M, "per-row sampling arrays: >= M entries");
+  hrm::SampleArgs sa{};
+  sa.inv_temp = inv_temp.data_ptr<float>();
+  sa.seed = reinterpret_cast<const unsigned long long*>(seed.data_ptr<int64_t>());
+  sa.pos = pos.data_ptr<int>();
+  if (thresh.has_value() && thresh->defined()) {
+    CHECK_DTYPE((*thresh), at::kFloat);
+    TORCH_CHECK(thresh->is_contiguous() && thresh->numel() >= M, "thresh: f32 [M]");
+    sa.thresh = thresh->data_ptr<float>();
+  }
+  unsigned long long* kp = nullptr;
+  if (keys.has_value() && keys->defined()) {
+    CHECK_DTYPE((*keys), at::kLong);
+    kp = reinterpret_cast<unsigned long long*>(keys->data_ptr<int64_t>());
+  }
+  unsigned long long* sp = nullptr;
+  if (scratch.has_value() && scratch->defined()) {
+    CHECK_DTYPE((*scratch), at::kLong);
+    TORCH_CHECK(scratch->numel() >= 2 * hrm::kArgmaxMaxRows, "argmax scratch: int64[2 * 4096]");
+    sp = reinterpret_cast<unsigned long long*>(scratch->data_ptr<int64_t>());
+  }
+  hrm::ArgmaxXchg x{};
+  const bool xchg = peers.has_value() && peers->defined();
+  if (xchg) {
+    CHECK_DTYPE((*peers), at::kLong);
+    TORCH_CHECK(peers->numel() == world && rank >= 0 && rank < world, "bad peer table");
+    x.peers = reinterpret_cast<const long long*>(peers->data_ptr<int64_t>());
+    x.rank = (int)rank;
+    x.world = (int)world;
+    x.max_rows = (int)max_rows;
+    x.off_keys = off_keys;
+    x.off_flags = off_flags;
+    x.epoch = reinterpret_cast<int*>((uintptr_t)epoch_ptr);
+    x.row_ticket = reinterpret_cast<int*>((uintptr_t)row_ticket_ptr);
+    x.status = hrm::status_word();
+  }
+  hrm::argmax_sample_launch(logits.data_ptr<float>(), (int)M, (int)logits.size(1), (int)logits.stride(0),
+                            (int)vocab_start, kp, tokens.data_ptr<int64_t>(), sp, hrm::gemm_sm_count(), sa,
+                            xchg ? &x : nullptr, cur_stream());
+}
+
+// Top-k selection helpers of the sampled pick: k-th largest per row, and each row's top-k candidate values.
+void kth_largest_rows(at::Tensor x, at::Tensor k, at::Tensor out) {
+  c10::cuda::CUDAGuard g(x.device());
+  CHECK_DTYPE(x, at::kFloat); CHECK_DTYPE(k, at::kInt); CHECK_DTYPE(out, at::kFloat);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be [R, n] row-major");
+  TORCH_CHECK(k.is_contiguous() && out.is_contiguous() && k.numel() >= x.size(0) && out.numel() >= x.size(0),
+              "k int32 [R], out f32 [R]");
+  hrm::kth_largest_launch(x.data_ptr<float>(), (int)x.size(0), (int)x.size(1), (int)x.stride(0), k.data_ptr<int>(),
+                          out.data_ptr<float>(), cur_stream());
+}
+
+void topk_candidates_rows(at::Tensor x, at::Tensor thresh, at::Tensor k, at::Tensor cand) {
+  c10::cuda::CUDAGuard g(x.device());
+  CHECK_DTYPE(x, at::kFloat); CHECK_DTYPE(thresh, at::kFloat);
+  CHECK_DTYPE(k, at::kInt); CHECK_DTYPE(cand, at::kFloat);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be [R, n] row-major");
+  TORCH_CHECK(cand.dim() == 2 && cand.is_contiguous() && cand.size(0) == x.size(0), "cand: f32 [R, kmax] contiguous");
+  TORCH_CHECK(thresh.is_contiguous() && k.is_contiguous() && thresh.numel() >= x.size(0) && k.numel() >= x.size(0),
+              "thresh f32 [R], k int32 [R]");
+  hrm::topk_candidates_launch(x.data_ptr<float>(), (int)x.size(0), (int)x.size(1), (int)x.stride(0),
+                              thresh.data_ptr<float>(), k.data_ptr<int>(), (int)cand.size(1), cand.data_ptr<float>(),
+                              cur_stream());
+}
+
 // C [M, N] fp32 = A [M, K] . B [N, K]^T on the tensor cores (A, B bf16 or f16, same type, unit inner stride).
 void gemm_nt(at::Tensor A, at::Tensor B, at::Tensor C) {
   c10::cuda::CUDAGuard g(A.device());
@@ -659,6 +737,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
   m.def("sm_count", []() { return hrm::gemm_sm_count(); });
   m.def("argmax_rows_xchg", &argmax_rows_xchg);
+  m.def("argmax_rows_sample", &argmax_rows_sample, "temperature / top-k sampled pick on the argmax path");
+  m.def("kth_largest_rows", &kth_largest_rows, "k-th largest value of every row (radix select)");
+  m.def("topk_candidates_rows", &topk_candidates_rows, "each row's top-k candidate values");
   m.def("gemm_nt", &gemm_nt);
   m.def("flash_train_fwd", &flash_train_fwd, "trainer causal attention forward (o, lse)");
   m.def("flash_train_bwd", &flash_train_bwd, "trainer causal attention backward (dq, dk, dv)");

@@ -18,7 +18,7 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass
-from typing import Dict, List, Optional, Tuple
+from typing import TYPE_CHECKING, Dict, List, Optional, Tuple
 
 import torch
 
@@ -28,6 +28,9 @@ from ..models.oracle import rope_tables
 from ..models.weights import (QTensor, Tensorish, ShardPlan, layer_names, shard_plan, synth_matrix, matrix_shapes,
                               vector_shapes, quantize_rows, EMBED, FINAL_NORM, LM_HEAD, get_lm_head)
 from ..runtime.kv_cache import PagedKVPool
+
+if TYPE_CHECKING:
+    from ..runtime.sampling import SampleMeta
 
 
 @dataclass
@@ -66,6 +69,7 @@ class BatchMeta:
     max_q: int = 1
     attn_splits: int = 0
     attn_keys_per_split: int = 0
+    sample: Optional["SampleMeta"] = None   # per-row temperature / top-k / seed / position; None = greedy
 
 
 def pack_layer(cfg: ModelConfig, w: Dict[str, Tensorish], l: int, device) -> LayerWeights:
@@ -266,17 +270,50 @@ class LlamaW8:
         logits = ops.w8a16_linear(xl, self.head_q, self.head_s, out_dtype=torch.float32, in_norm=nl)
         if self.collect_stats:
             self._record_stats(logits, xl, nl)
+        return self._pick(logits, b)
+
+    def _pick(self, logits: torch.Tensor, b: BatchMeta) -> torch.Tensor:
+        """Next token per logits row, global ids: greedy, or sampled when the batch carries sampling rows."""
+        p = self.plan
+        if b.sample is not None:
+            return self._sample(logits, b.sample)
         xchg_rows = min(self.symm.argmax_rows, ops.ARGMAX_XCHG_MAX_ROWS) if self.symm is not None else 0
         if p.world > 1 and logits.shape[0] <= xchg_rows:
             # global greedy pick through peer memory inside the argmax kernel (no NCCL call)
             return ops.argmax_exchange_(logits, p.vocab_start, self.symm)
         if p.world > 1:
-            keys = torch.empty(xl.shape[0], dtype=torch.int64, device=self.device)
+            keys = torch.empty(logits.shape[0], dtype=torch.int64, device=self.device)
             ops.argmax_rows(logits, p.vocab_start, keys=keys)
             self.comm.all_reduce_max_(keys)
             from ..parallel.dist import unpack_argmax
             return unpack_argmax(keys)
         return ops.argmax_rows(logits, 0)
+
+    def _sample(self, logits: torch.Tensor, sm) -> torch.Tensor:
+        """Temperature / top-k pick.  Top-k threshold: the row's k-th largest logit; under tensor parallelism each
+        rank contributes its local top-k values (``topk_candidates``), one all-gather joins them and the same radix
+        select runs over the joined rows, so every rank applies the same global threshold.  The draw itself is the
+        argmax kernel's Gumbel-max pick, exchanged like the greedy one."""
+        p = self.plan
+        R = logits.shape[0]
+        k = sm.top_k[:R]
+        thr = ops.kth_largest(logits, k)
+        if p.world > 1:
+            cand = ops.topk_candidates(logits, thr, k, sm.kmax)
+            joined = torch.empty(R, p.world * sm.kmax, dtype=torch.float32, device=logits.device)
+            self.comm.all_gather_cols(cand, joined)
+            thr = ops.kth_largest(joined, k)
+        xchg_rows = min(self.symm.argmax_rows, ops.ARGMAX_XCHG_MAX_ROWS) if self.symm is not None else 0
+        args = (sm.inv_temp[:R], sm.seed[:R], sm.pos[:R], thr)
+        if p.world > 1 and R <= xchg_rows:
+            return ops.sample_rows(logits, p.vocab_start, *args, symm=self.symm)
+        if p.world > 1:
+            keys = torch.empty(R, dtype=torch.int64, device=self.device)
+            ops.sample_rows(logits, p.vocab_start, *args, keys=keys)
+            self.comm.all_reduce_max_(keys)
+            from ..parallel.dist import unpack_argmax
+            return unpack_argmax(keys)
+        return ops.sample_rows(logits, 0, *args)
 
     def _record_stats(self, logits: torch.Tensor, xl: torch.Tensor, nl) -> None:
         """``stat_nll[i] = logsumexp(logits_i) - max(logits_i)``: the cross-entropy of the greedy token (the
@@ -475,14 +512,7 @@ class LlamaW8:
         logits = ops.w8a16_linear(xl, self.head_q, self.head_s, out_dtype=torch.float32, in_norm=nl)
         if self.collect_stats:
             self._record_stats(logits, xl, nl)
-        xchg_rows = min(self.symm.argmax_rows, ops.ARGMAX_XCHG_MAX_ROWS) if self.symm is not None else 0
-        if logits.shape[0] <= xchg_rows:
-            return ops.argmax_exchange_(logits, p.vocab_start, self.symm)
-        keys = torch.empty(xl.shape[0], dtype=torch.int64, device=dev)
-        ops.argmax_rows(logits, p.vocab_start, keys=keys)
-        comm.all_reduce_max_(keys)
-        from ..parallel.dist import unpack_argmax
-        return unpack_argmax(keys)
+        return self._pick(logits, b)
 
     def _mm_f32(self, x, w, s, out):
         return ops.w8a16_linear_out(x, w, s, out)

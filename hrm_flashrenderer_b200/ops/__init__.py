@@ -646,6 +646,121 @@ def argmax_exchange_(logits: torch.Tensor, vocab_start: int, symm, tokens: Optio
     return tokens
 
 
+# ------------------------------------------------------------------------------------------------ sampling
+# Temperature / top-k sampling on the argmax path (Gumbel-max): a row's token is the argmax over the kept logits of
+# v / T + Gumbel(seed, position, global token id); "kept" = v >= the row's global k-th largest logit.  The noise is a
+# counter-based hash of (seed, position, id), so a request's draw does not depend on its batch or on the vocabulary
+# sharding, and tensor-parallel ranks agree without exchanging noise.
+SAMPLE_MAX_TOP_K = 1024
+_GAMMA = 0x9E3779B97F4A7C15
+_MIX1, _MIX2 = 0xBF58476D1CE4E5B9, 0x94D049BB133111EB
+
+
+def _mix64(z):
+    import numpy as np
+    with np.errstate(over="ignore"):
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(_MIX1)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(_MIX2)
+        return z ^ (z >> np.uint64(31))
+
+
+def gumbel_noise_host(seed: int, pos: int, ids) -> torch.Tensor:
+    """The kernels' sampling noise for global token ids ``ids`` of one row (fp32), computed on the host: the SplitMix64
+    output mix (Steele, Lea, Flood, OOPSLA 2014) of ``mix64(seed + gamma * (pos + 1)) + gamma * (id + 1)``, top 23
+    bits -> u in (0, 1), ``-log(-log(u))``."""
+    import numpy as np
+    with np.errstate(over="ignore"):
+        s = np.array([seed], dtype=np.int64).view(np.uint64)
+        p = np.array([pos + 1], dtype=np.int64).view(np.uint64)
+        rk = _mix64(s + np.uint64(_GAMMA) * p)
+        i = np.asarray(ids, dtype=np.int64).view(np.uint64) + np.uint64(1)
+        h = _mix64(rk + np.uint64(_GAMMA) * i)
+    u = ((h >> np.uint64(41)).astype(np.float32) + np.float32(0.5)) * np.float32(1.0 / 8388608.0)
+    return torch.from_numpy(-np.log(-np.log(u)))
+
+
+def kth_largest(x: torch.Tensor, k: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``out[r]`` = the ``k[r]``-th largest value of row ``r`` of ``x [R, n]`` (fp32); ``-inf`` when ``k[r] <= 0`` or
+    ``k[r] >= n`` (no restriction).  Radix select, one CTA per row."""
+    R, n = x.shape
+    if out is None:
+        out = torch.empty(R, dtype=torch.float32, device=x.device)
+    if not x.is_cuda:
+        for r in range(R):
+            kr = int(k[r])
+            out[r] = -float("inf") if kr <= 0 or kr >= n else torch.topk(x[r].float(), kr).values[-1]
+        return out
+    ext().kth_largest_rows(x, k, out)
+    LAUNCH_COUNTER.add()
+    return out
+
+
+def topk_candidates(x: torch.Tensor, thresh: torch.Tensor, k: torch.Tensor, kmax: int) -> torch.Tensor:
+    """Each row's top-``k`` values as ``[R, kmax]``: the values above ``thresh[r]``, then ``thresh[r]`` up to ``k[r]``
+    slots, then ``-inf`` (in no particular order; ``k[r] <= kmax``).  Rows with ``k[r] <= 0`` are all ``-inf``."""
+    R, n = x.shape
+    cand = torch.empty(R, kmax, dtype=torch.float32, device=x.device)
+    if not x.is_cuda:
+        cand.fill_(-float("inf"))
+        for r in range(R):
+            kr = min(int(k[r]), kmax)
+            if kr <= 0:
+                continue
+            t = float(thresh[r])
+            above = x[r][x[r].float() > t].float()[:kmax]
+            cand[r, :above.numel()] = above
+            if t != -float("inf") and above.numel() < kr:
+                cand[r, above.numel():kr] = t
+        return cand
+    ext().topk_candidates_rows(x, thresh, k, cand)
+    LAUNCH_COUNTER.add()
+    return cand
+
+
+def sample_rows(logits: torch.Tensor, vocab_start: int, inv_temp: torch.Tensor, seed: torch.Tensor,
+                pos: torch.Tensor, thresh: Optional[torch.Tensor] = None, keys: Optional[torch.Tensor] = None,
+                symm=None, tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Sampled token per row of this rank's logits ``[R, V]`` (global ids from ``vocab_start``): rows with
+    ``inv_temp == 0`` stay greedy, the others take the argmax of ``v * inv_temp + Gumbel(seed, pos, id)`` over the
+    logits ``>= thresh`` (all when ``thresh`` is None).  ``keys`` receives the packed (value, lowest id) keys for a
+    collective max; with ``symm`` the keys are exchanged over peer memory inside the kernel and the returned tokens
+    are already global.  ``inv_temp`` f32, ``seed`` int64, ``pos`` int32, all ``[>= R]``."""
+    R, V = logits.shape
+    if not logits.is_cuda:
+        from ..parallel.dist import pack_argmax
+        lf = logits.float()
+        vals = torch.empty(R, dtype=torch.float32)
+        idx = torch.empty(R, dtype=torch.int64)
+        ids = torch.arange(V, dtype=torch.int64) + int(vocab_start)
+        for r in range(R):
+            it = float(inv_temp[r])
+            if it == 0.0:
+                v, i = torch.max(lf[r], dim=0)
+            else:
+                z = lf[r] * it + gumbel_noise_host(int(seed[r]), int(pos[r]), ids.numpy())
+                if thresh is not None:
+                    z = torch.where(lf[r] >= float(thresh[r]), z, torch.full_like(z, -float("inf")))
+                v, i = torch.max(z, dim=0)
+            vals[r], idx[r] = v, i
+        if keys is not None:
+            keys.copy_(pack_argmax(vals, idx + int(vocab_start)))
+        return idx + int(vocab_start)
+    if tokens is None:
+        tokens = torch.empty(R, dtype=torch.int64, device=logits.device)
+    scratch = Workspace.get(logits.device).argmax if _ARGMAX_SPLIT else None
+    if symm is not None:
+        if R > min(symm.argmax_rows, ARGMAX_XCHG_MAX_ROWS):
+            raise ValueError(f"sampled exchange: {R} rows > {min(symm.argmax_rows, ARGMAX_XCHG_MAX_ROWS)}")
+        ext().argmax_rows_sample(logits, int(vocab_start), keys, tokens, scratch, inv_temp, thresh, seed, pos,
+                                 symm.peers, symm.rank, symm.world, symm.argmax_rows, symm.off_ax_keys,
+                                 symm.off_ax_flags, symm.argmax_epoch_ptr, symm.argmax_ticket_ptr)
+    else:
+        ext().argmax_rows_sample(logits, int(vocab_start), keys, tokens, scratch, inv_temp, thresh, seed, pos,
+                                 None, 0, 1, 0, 0, 0, 0, 0)
+    LAUNCH_COUNTER.add()
+    return tokens
+
+
 # ------------------------------------------------------------------------------------------------ decode bookkeeping
 def decode_prepare(positions: torch.Tensor, tables: torch.Tensor, block_size: int, active: Optional[torch.Tensor],
                    slots: torch.Tensor, context_lens: torch.Tensor) -> None:

@@ -23,6 +23,7 @@ from ..utils.nvtx import nvtx_range
 from ..config import EngineConfig
 from ..models.llama import BatchMeta, LlamaW8
 from .kv_cache import BlockManager
+from .sampling import SampleMeta, SamplingParams, any_sampled
 
 
 @dataclass
@@ -38,6 +39,11 @@ class _DecodeGraph:
     tokens: torch.Tensor
     graph: Optional[torch.cuda.CUDAGraph] = None
     meta: Optional[BatchMeta] = None
+    # sampled variant of the step (same buffers plus per-row sampling arrays); ``sampled`` selects it
+    sample: Optional[SampleMeta] = None
+    meta_sample: Optional[BatchMeta] = None
+    graph_sample: Optional[torch.cuda.CUDAGraph] = None
+    sampled: bool = False
 
 
 class InferenceEngine:
@@ -72,7 +78,8 @@ class InferenceEngine:
         self.bm.reset()
 
     # ------------------------------------------------------------------ prefill
-    def _prefill_meta(self, chunks: List[Tuple[int, List[int], int]]) -> BatchMeta:
+    def _prefill_meta(self, chunks: List[Tuple[int, List[int], int]],
+                      sampling: Optional[Sequence[Optional[SamplingParams]]] = None) -> BatchMeta:
         """chunks: (seq_id, token ids of this chunk, absolute start position)."""
         dev = self.device
         bs = self.block_size
@@ -100,12 +107,20 @@ class InferenceEngine:
             context_lens=torch.tensor(ctx, dtype=torch.int32), last_rows=torch.tensor(last, dtype=torch.int64),
             cu_q=torch.tensor(cu, dtype=torch.int32), q_start=torch.tensor(qst, dtype=torch.int32))
         dv = {k: v.pin_memory().to(dev, non_blocking=True) if dev.type == "cuda" else v for k, v in host.items()}
-        return BatchMeta(is_decode=False, max_q=max(len(c[1]) for c in chunks), **dv)
+        meta = BatchMeta(is_decode=False, max_q=max(len(c[1]) for c in chunks), **dv)
+        if any_sampled(sampling):
+            # one row per chunk (its last token); the noise counter is that token's absolute position
+            meta.sample = SampleMeta.alloc(len(chunks), dev)
+            meta.sample.fill(sampling, positions=[start + len(toks) - 1 for _, toks, start in chunks])
+        return meta
 
     @torch.no_grad()
-    def prefill(self, seqs: Sequence[Tuple[int, Sequence[int]]]) -> List[int]:
-        """Chunked prefill of whole prompts; returns the first generated token of each sequence."""
+    def prefill(self, seqs: Sequence[Tuple[int, Sequence[int]]],
+                sampling: Optional[Sequence[Optional[SamplingParams]]] = None) -> List[int]:
+        """Chunked prefill of whole prompts; returns the first generated token of each sequence (greedy, or drawn
+        with ``sampling[i]`` for sequence ``i``)."""
         budget = int(self.ecfg.prefill_chunk)
+        by_sid = {sid: (sampling[i] if sampling is not None else None) for i, (sid, _) in enumerate(seqs)}
         pending = [(sid, list(toks), self.bm.lengths.get(sid, 0)) for sid, toks in seqs]
         first: Dict[int, int] = {}
         while pending:
@@ -119,7 +134,7 @@ class InferenceEngine:
                 used += take
                 if take < len(toks):
                     nxt.append((sid, toks[take:], start + take))
-            meta = self._prefill_meta(chunks)
+            meta = self._prefill_meta(chunks, [by_sid[c[0]] for c in chunks] if sampling is not None else None)
             with nvtx_range(f"prefill chunk {used} tokens"):
                 out = self.model.forward(meta).tolist()
             done_ids = {s for s, _, _ in nxt}
@@ -154,9 +169,20 @@ class InferenceEngine:
         self._graphs[bucket] = g
         return g
 
-    def _decode_body(self, g: _DecodeGraph) -> None:
+    def _sample_state(self, g: _DecodeGraph) -> None:
+        """The sampled variant's arrays; its noise counter is the step's device-side positions."""
+        if g.sample is None:
+            g.sample = SampleMeta.alloc(g.bucket, self.device)
+            g.sample.pos = g.positions
+            m = g.meta
+            g.meta_sample = BatchMeta(ids=m.ids, positions=m.positions, slots=m.slots, block_tables=m.block_tables,
+                                      context_lens=m.context_lens, last_rows=m.last_rows, is_decode=True,
+                                      attn_splits=m.attn_splits, attn_keys_per_split=m.attn_keys_per_split,
+                                      sample=g.sample)
+
+    def _decode_body(self, g: _DecodeGraph, sampled: bool = False) -> None:
         ops.decode_prepare(g.positions, g.tables, self.block_size, g.active, g.slots, g.context_lens)
-        tok = self.model.forward(g.meta)
+        tok = self.model.forward(g.meta_sample if sampled else g.meta)
         g.tokens.copy_(tok)
         ops.decode_advance(g.tokens, g.ids, g.positions, g.active)
 
@@ -167,19 +193,23 @@ class InferenceEngine:
             torch.cuda.synchronize(self.device)
         for g in self._graphs.values():
             g.graph = None
+            g.graph_sample = None
         self._graphs.clear()
 
-    def capture(self, bucket: int) -> None:
-        """Warm up (sizes the workspace) and capture the decode step of ``bucket`` sequences."""
+    def capture(self, bucket: int, sampled: bool = False) -> None:
+        """Warm up (sizes the workspace) and capture the decode step of ``bucket`` sequences (greedy, or the
+        sampled variant)."""
         g = self._decode_state(bucket)
-        if g.graph is not None or not self.ecfg.use_cuda_graphs:
+        if sampled:
+            self._sample_state(g)
+        if (g.graph_sample if sampled else g.graph) is not None or not self.ecfg.use_cuda_graphs:
             return
         saved = (g.ids.clone(), g.positions.clone(), g.active.clone())
         g.active.zero_()
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
-            self._decode_body(g)
+            self._decode_body(g, sampled)
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
         ws = ops.Workspace.get(self.device)
@@ -187,18 +217,23 @@ class InferenceEngine:
         try:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                self._decode_body(g)
-            g.graph = graph
+                self._decode_body(g, sampled)
+            if sampled:
+                g.graph_sample = graph
+            else:
+                g.graph = graph
         finally:
             ws.frozen = False
         g.ids.copy_(saved[0]); g.positions.copy_(saved[1]); g.active.copy_(saved[2])
 
     def load_decode_batch(self, seq_ids: Sequence[int], last_tokens: Sequence[int], reserve,
-                          positions: Optional[Sequence[int]] = None) -> _DecodeGraph:
+                          positions: Optional[Sequence[int]] = None,
+                          sampling: Optional[Sequence[Optional[SamplingParams]]] = None) -> _DecodeGraph:
         """Stage a decode batch: block tables grown for ``reserve`` more tokens (one count for every sequence, or a
         per-sequence list), current tokens and positions.
 
-        ``positions[i]`` is the absolute position of ``last_tokens[i]`` (default: the prefilled length)."""
+        ``positions[i]`` is the absolute position of ``last_tokens[i]`` (default: the prefilled length);
+        ``sampling[i]`` the sampling parameters of sequence ``i`` (None or absent: greedy)."""
         n = len(seq_ids)
         bucket = self._bucket(n)
         g = self._decode_state(bucket)
@@ -218,19 +253,25 @@ class InferenceEngine:
         g.positions.copy_(pos)
         g.ids.copy_(ids)
         g.active.copy_(act)
+        g.sampled = any_sampled(sampling)
+        if g.sampled:
+            self._sample_state(g)
+            g.sample.fill(sampling)
         return g
 
     def decode_step(self, g: _DecodeGraph) -> torch.Tensor:
         """One decode step for the staged batch; returns the device tensor of sampled tokens (bucket-sized)."""
         if self.ecfg.use_cuda_graphs and self.device.type == "cuda":
-            if g.graph is None:
+            graph = g.graph_sample if g.sampled else g.graph
+            if graph is None:
                 with nvtx_range(f"capture decode b{g.bucket}"):
-                    self.capture(g.bucket)
+                    self.capture(g.bucket, g.sampled)
+                graph = g.graph_sample if g.sampled else g.graph
             with nvtx_range("decode step (graph)"):
-                g.graph.replay()
+                graph.replay()
         else:
             with nvtx_range("decode step"):
-                self._decode_body(g)
+                self._decode_body(g, g.sampled)
         return g.tokens
 
     def step_host(self, g: _DecodeGraph, host_ids: torch.Tensor, host_out: torch.Tensor) -> torch.Tensor:
@@ -248,13 +289,17 @@ class InferenceEngine:
     @torch.no_grad()
     def generate(self, prompts: Sequence[Sequence[int]], max_new_tokens: int, stop_on_eos: bool = True,
                  eos_ids: Optional[Sequence[int]] = None,
-                 on_token: Optional[Callable[[int, int], None]] = None) -> List[List[int]]:
-        """Greedy generation for a batch of token-id prompts (prompt ids H2D, tokens D2H every step).
-        ``on_token(i, token)`` is called for every token kept for prompt ``i``, as soon as it is known."""
+                 on_token: Optional[Callable[[int, int], None]] = None,
+                 sampling=None) -> List[List[int]]:
+        """Generation for a batch of token-id prompts (prompt ids H2D, tokens D2H every step): greedy, or drawn with
+        ``sampling`` (one :class:`SamplingParams` for every prompt, or one per prompt).  ``on_token(i, token)`` is
+        called for every token kept for prompt ``i``, as soon as it is known."""
+        if isinstance(sampling, SamplingParams):
+            sampling = [sampling] * len(prompts)
         eos = set(self.cfg.eos_token_ids if eos_ids is None else eos_ids)
         sids = [self.new_seq() for _ in prompts]
         try:
-            first = self.prefill(list(zip(sids, prompts)))
+            first = self.prefill(list(zip(sids, prompts)), sampling)
             outs = [[t] for t in first]
             if on_token is not None and max_new_tokens >= 1:
                 for i, t in enumerate(first):
@@ -262,7 +307,7 @@ class InferenceEngine:
             alive = [not (stop_on_eos and t in eos) for t in first]
             if max_new_tokens <= 1 or not any(alive):
                 return [o[:max_new_tokens] for o in outs]
-            g = self.load_decode_batch(sids, first, reserve=max_new_tokens)
+            g = self.load_decode_batch(sids, first, reserve=max_new_tokens, sampling=sampling)
             act_host = torch.zeros(g.bucket, dtype=torch.int32)
             act_host[:len(sids)] = torch.tensor([1 if a else 0 for a in alive], dtype=torch.int32)
             g.active.copy_(act_host)

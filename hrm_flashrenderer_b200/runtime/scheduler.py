@@ -28,6 +28,8 @@ from typing import Callable, Deque, Dict, List, Optional, Sequence
 
 import torch
 
+from .sampling import SamplingParams
+
 
 # CUDA errors after which the context is unusable (every later CUDA call in the process fails as well)
 _STICKY_CUDA = ("illegal memory access", "illegal instruction", "misaligned address", "unspecified launch failure",
@@ -56,6 +58,7 @@ class GenRequest:
     future: Future = field(default_factory=Future)
     seq_id: int = -1
     error: Optional[BaseException] = None
+    sampling: Optional[SamplingParams] = None   # None: greedy
 
     @property
     def ttft_s(self) -> Optional[float]:
@@ -115,7 +118,8 @@ class Scheduler:
 
     # ------------------------------------------------------------------ API
     def submit(self, prompt_ids: Sequence[int], max_new_tokens: int, stop_on_eos: bool = True,
-               on_token: Optional[Callable[[int], None]] = None) -> GenRequest:
+               on_token: Optional[Callable[[int], None]] = None,
+               sampling: Optional[SamplingParams] = None) -> GenRequest:
         if self.fatal is not None:
             raise RuntimeError(f"engine stopped after a fatal error: {self.fatal}")
         if not prompt_ids:
@@ -130,15 +134,16 @@ class Scheduler:
         with self._lock:
             rid = self._next_rid
             self._next_rid += 1
-        r = GenRequest(list(map(int, prompt_ids)), int(max_new_tokens), stop_on_eos, on_token, rid)
+        r = GenRequest(list(map(int, prompt_ids)), int(max_new_tokens), stop_on_eos, on_token, rid,
+                       sampling=sampling if sampling is not None and not sampling.greedy else None)
         self._inbox.put(r)
         if self.fatal is not None:   # the loop stopped between the check above and the put
             self._fail_queued()
         return r
 
     def generate(self, prompt_ids: Sequence[int], max_new_tokens: int, timeout: Optional[float] = None,
-                 stop_on_eos: bool = True) -> List[int]:
-        return self.submit(prompt_ids, max_new_tokens, stop_on_eos).future.result(timeout)
+                 stop_on_eos: bool = True, sampling: Optional[SamplingParams] = None) -> List[int]:
+        return self.submit(prompt_ids, max_new_tokens, stop_on_eos, sampling=sampling).future.result(timeout)
 
     def metrics(self) -> Dict:
         el = max(1e-9, time.perf_counter() - self.started_at)
@@ -208,7 +213,11 @@ class Scheduler:
             chunks.append((r, take))
             used += take
         # a failure here propagates to the loop, which fails every request that holds engine state
-        firsts = eng.prefill([(r.seq_id, r.prompt_ids[r._done:r._done + n]) for r, n in chunks])
+        seqs = [(r.seq_id, r.prompt_ids[r._done:r._done + n]) for r, n in chunks]
+        if any(r.sampling is not None for r, _ in chunks):
+            firsts = eng.prefill(seqs, [r.sampling for r, _ in chunks])
+        else:
+            firsts = eng.prefill(seqs)
         if len(self.prefill_calls) < 4096:
             self.prefill_calls.append(used)
         now = time.perf_counter()
@@ -241,9 +250,12 @@ class Scheduler:
         eng = self.engine
         if not staged:
             # each sequence reserves only what it can still generate (admission counted exactly that)
+            extra = {}
+            if any(r.sampling is not None for r in self._running):
+                extra["sampling"] = [r.sampling for r in self._running]
             g = eng.load_decode_batch([r.seq_id for r in self._running], [r.tokens[-1] for r in self._running],
                                       reserve=[r.max_new_tokens - len(r.tokens) + 1 for r in self._running],
-                                      positions=[r._pos for r in self._running])
+                                      positions=[r._pos for r in self._running], **extra)
         tok = eng.decode_step(g)
         host = tok[:len(self._running)].tolist()
         now = time.perf_counter()

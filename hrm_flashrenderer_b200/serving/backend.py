@@ -53,8 +53,8 @@ class EchoBackend:
         self.fail = fail
         self.calls: List[Dict] = []
 
-    def generate(self, prompt_text: str, max_new_tokens: int = 64, timeout_s: float = 180.0) -> str:
-        self.calls.append({"prompt": prompt_text, "max_new_tokens": max_new_tokens})
+    def generate(self, prompt_text: str, max_new_tokens: int = 64, timeout_s: float = 180.0, sampling=None) -> str:
+        self.calls.append({"prompt": prompt_text, "max_new_tokens": max_new_tokens, "sampling": sampling})
         if self.fail:
             raise RuntimeError("echo backend configured to fail")
         h = hashlib.sha256(prompt_text.encode()).hexdigest()[:16]
@@ -111,16 +111,20 @@ class EngineBackend:
             ids = ids[-self.max_prompt_tokens:]
         return ids
 
-    def generate_ids(self, ids: List[int], max_new_tokens: int, timeout_s: float = 180.0) -> List[int]:
+    def generate_ids(self, ids: List[int], max_new_tokens: int, timeout_s: float = 180.0,
+                     sampling=None) -> List[int]:
+        """Token ids of the completion; ``sampling`` (a ``runtime.sampling.SamplingParams``) draws instead of the
+        greedy pick."""
         # fit the context like the reference engine (prompt + output capped at its Tmax): keep the prompt's tail
         # and at least one new token, then cap the output
         limit = self.engine.max_blocks * self.engine.block_size
         ids = list(ids)[-max(1, limit - 1):]
         max_new_tokens = max(1, min(int(max_new_tokens), limit - len(ids)))
-        return self.scheduler.generate(ids, max_new_tokens, timeout=timeout_s)
+        return self.scheduler.generate(ids, max_new_tokens, timeout=timeout_s, sampling=sampling)
 
-    def generate(self, prompt_text: str, max_new_tokens: int = 256, timeout_s: float = 180.0) -> str:
-        out = self.generate_ids(self.encode_prompt(prompt_text), max_new_tokens, timeout_s)
+    def generate(self, prompt_text: str, max_new_tokens: int = 256, timeout_s: float = 180.0,
+                 sampling=None) -> str:
+        out = self.generate_ids(self.encode_prompt(prompt_text), max_new_tokens, timeout_s, sampling)
         return self.tokenizer.decode(out, skip_special_tokens=True)
 
     def is_running(self) -> bool:

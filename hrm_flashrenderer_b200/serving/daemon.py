@@ -26,6 +26,8 @@ from typing import Any, Callable, Dict, Optional
 import torch
 import torch.distributed as dist
 
+from ..runtime.sampling import sampling_from_request
+
 
 class MirroredEngine:
     """Rank-0 proxy of an :class:`InferenceEngine`: every state-changing call is first broadcast to the followers."""
@@ -212,8 +214,9 @@ def rpc_serve(engine, host: str, port: int, authkey: bytes, tokenizer_source: Op
                 elif cmd == "generate":
                     try:
                         ids = msg.get("input_ids") or tok(str(msg.get("prompt", "")), add_special_tokens=True)["input_ids"]
+                        sp = sampling_from_request(msg.get("temperature"), msg.get("top_k"), msg.get("seed"))
                         out = sched.generate(ids, int(msg.get("max_new_tokens", 64)),
-                                             stop_on_eos=bool(msg.get("stop_on_eos", True)))
+                                             stop_on_eos=bool(msg.get("stop_on_eos", True)), sampling=sp)
                         conn.send({"ok": True, "tokens": out, "text": tok.decode(out, skip_special_tokens=True)})
                     except Exception as e:
                         conn.send({"ok": False, "error": repr(e)})

@@ -228,6 +228,9 @@ def create_app(st: RouterState):
         route_hint: Optional[str] = None
         prefer_backend: Optional[str] = None
         allow_failover: bool = True
+        temperature: Optional[float] = None   # forwarded to the lane only when given (absent: greedy)
+        top_k: Optional[int] = None
+        seed: Optional[int] = None
 
     def truncate(prompt: str) -> str:
         t = str(prompt or "").strip()
@@ -257,9 +260,11 @@ def create_app(st: RouterState):
                 lane_new = min(req_new, max_new_limit(st, lane))
                 attempted.append(lane)
                 try:
-                    body, ms = await asyncio.to_thread(st.post, be.base_url + "/v1/generate",
-                                                       {"prompt": prompt, "max_new_tokens": lane_new, "mode": mode,
-                                                        "show_sources": show}, st.request_timeout_s)
+                    lane_req = {"prompt": prompt, "max_new_tokens": lane_new, "mode": mode, "show_sources": show}
+                    lane_req.update({k: v for k, v in (("temperature", req.temperature), ("top_k", req.top_k),
+                                                       ("seed", req.seed)) if v is not None})
+                    body, ms = await asyncio.to_thread(st.post, be.base_url + "/v1/generate", lane_req,
+                                                       st.request_timeout_s)
                     if not bool(body.get("ok", True)):
                         raise RuntimeError(str(body.get("detail") or body.get("error") or "backend returned ok=false"))
                     out = dict(body)
@@ -375,7 +380,8 @@ def create_app(st: RouterState):
         req = GenerateReq(prompt=prompt, mode=str(body.get("mode") or "deepseek_only"),
                           max_new_tokens=body.get("max_tokens") or body.get("max_completion_tokens")
                           or body.get("max_new_tokens"),
-                          route_hint=body.get("route_hint"), prefer_backend=body.get("prefer_backend"))
+                          route_hint=body.get("route_hint"), prefer_backend=body.get("prefer_backend"),
+                          temperature=body.get("temperature"), top_k=body.get("top_k"), seed=body.get("seed"))
         if bool(body.get("stream")):
             task = asyncio.create_task(run_generate(req))
             return StreamingResponse(stream(task, model, prompt, chat), media_type="text/event-stream")

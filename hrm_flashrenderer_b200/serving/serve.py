@@ -24,6 +24,7 @@ from typing import Any, List, Optional, Tuple
 from .hrm_client import run_hrm_query
 from .prompt_builder import build_prompt_for_mode, build_sources, fit_prompt_to_token_budget, normalize_mode
 from .utils import find_hrm_binary
+from ..runtime.sampling import sampling_from_request
 
 REPO_ROOT = Path(__file__).resolve().parents[2]
 TEMPLATES = {"mixed": "mixed_silent", "retrieval": "retrieval_explicit", "deepseek_only": "deepseek_only_raw"}
@@ -136,6 +137,9 @@ def create_app(state: ServiceState):
         max_new_tokens: Optional[int] = None
         mode: Optional[str] = None
         show_sources: Optional[bool] = None
+        temperature: Optional[float] = None   # absent or 0: greedy (the default)
+        top_k: Optional[int] = None
+        seed: Optional[int] = None
 
     def sem() -> asyncio.Semaphore:
         if state.sem is None:
@@ -190,6 +194,7 @@ def create_app(state: ServiceState):
             raise HTTPException(status_code=400, detail="prompt required")
         try:
             mode = normalize_mode(req.mode)
+            sampling = sampling_from_request(req.temperature, req.top_k, req.seed)
         except ValueError as e:
             raise HTTPException(status_code=400, detail=str(e))
         async with sem():
@@ -215,7 +220,11 @@ def create_app(state: ServiceState):
                 raise HTTPException(status_code=500, detail="generation backend not initialized")
         # generation runs outside the admission semaphore's prompt-build section: the engine batches requests
         try:
-            text = await asyncio.to_thread(state.backend.generate, prompt_text, max_new, state.request_timeout_s)
+            if sampling is None:
+                text = await asyncio.to_thread(state.backend.generate, prompt_text, max_new, state.request_timeout_s)
+            else:
+                text = await asyncio.to_thread(state.backend.generate, prompt_text, max_new, state.request_timeout_s,
+                                               sampling=sampling)
         except Exception as e:
             raise HTTPException(status_code=500, detail=str(e))
         payload = {"ok": True, "text": text, "source_count": len(sources), "mode": mode, "hrm_active": hrm_active,

@@ -19,7 +19,7 @@ NVCC_FLAGS = [
 CXX_FLAGS = ["-O3", "-std=c++17"]
 
 CUDA_SOURCES = ["bindings.cpp", "gemm_w8a16.cu", "gemm_chain.cu", "norm.cu", "attention.cu", "attention_tc.cu", "comm.cu",
-                "gemm_noalloc.cu", "gemm_nt.cu", "flash_train.cu", "pho.cu",
+                "gemm_noalloc.cu", "gemm_nt.cu", "flash_train.cu", "sampling.cu", "pho.cu",
                 "train_ops.cu"]
 
 

@@ -130,6 +130,23 @@ def test_missing_tokenizer_means_no_prompt(hrm_model):
     assert text == "" and srcs == [] and active is True
 
 
+def test_sampling_fields_reach_the_backend(hrm_model):
+    """``temperature`` / ``top_k`` / ``seed`` on /v1/generate become the backend's sampling parameters; absent or
+    zero temperature keeps the greedy call unchanged; bad values are a 400."""
+    from hrm_flashrenderer_b200.runtime.sampling import SamplingParams
+    be = EchoBackend()
+    st = _state(hrm_model, be)
+    with LiveServer(create_app(st)) as srv:
+        code, _ = post(srv.url + "/v1/generate", {"prompt": "hi", "mode": "deepseek_only", "temperature": 0.7,
+                                                  "top_k": 40, "seed": 5})
+        assert code == 200 and be.calls[-1]["sampling"] == SamplingParams(0.7, 40, 5)
+        code, _ = post(srv.url + "/v1/generate", {"prompt": "hi", "mode": "deepseek_only", "temperature": 0})
+        assert code == 200 and be.calls[-1]["sampling"] is None
+        for bad in ({"temperature": -1}, {"temperature": 1, "top_k": -3}, {"temperature": 1, "top_k": 5000}):
+            code, _ = post(srv.url + "/v1/generate", dict({"prompt": "hi", "mode": "deepseek_only"}, **bad))
+            assert code == 400, bad
+
+
 # ---------------------------------------------------------------------------------------------- router
 def _router(post_fn, endpoints=None):
     st = rt.RouterState()
@@ -184,6 +201,10 @@ def test_router_failover_and_503():
         assert calls[-1][1]["mode"] == "deepseek_only" and calls[-1][1]["prompt"] == "hi"
         code, body = post(srv.url + "/v1/completions", {"prompt": "x", "stream": True})
         assert code == 200 and body.rstrip().endswith("data: [DONE]") and '"text_completion"' in body
+        assert "temperature" not in calls[-1][1]                    # greedy requests keep the lane body unchanged
+        post(srv.url + "/v1/chat/completions", {"messages": [{"role": "user", "content": "hi"}], "temperature": 0.5,
+                                                "top_k": 8, "seed": 3})
+        assert (calls[-1][1]["temperature"], calls[-1][1]["top_k"], calls[-1][1]["seed"]) == (0.5, 8, 3)
 
 
 def test_lane_call_errors_and_success():

@@ -28,7 +28,7 @@ def _prompts():
     return [torch.randint(0, 1024, (16,), generator=g).tolist() for _ in range(2)]
 
 
-def _run(rank, world, port, q, sp=False, prompts=None, overlap=1, replicate=True):
+def _run(rank, world, port, q, sp=False, prompts=None, overlap=1, replicate=True, sampling=None):
     from hrm_flashrenderer_b200.parallel.dist import init_dist, destroy
     from hrm_flashrenderer_b200.parallel.comm import TPComm
     from hrm_flashrenderer_b200.models.llama import LlamaW8
@@ -51,17 +51,18 @@ def _run(rank, world, port, q, sp=False, prompts=None, overlap=1, replicate=True
         eng = InferenceEngine(model, EngineConfig(max_seq_len=160, max_batch=4, use_cuda_graphs=False,
                                                   sequence_parallel=sp, prefill_overlap_chunks=overlap),
                               num_blocks=48)
-        out = eng.generate(prompts or _prompts(), 32, stop_on_eos=False)
+        out = eng.generate(prompts or _prompts(), 32, stop_on_eos=False, sampling=sampling)
         q.put((rank, out, calls["all_reduce_"]))
     finally:
         destroy()
 
 
-def _spawn(world, sp=False, prompts=None, overlap=1, replicate=True, with_calls=False):
+def _spawn(world, sp=False, prompts=None, overlap=1, replicate=True, with_calls=False, sampling=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_run, args=(r, world, port, q, sp, prompts, overlap, replicate)) for r in range(world)]
+    ps = [ctx.Process(target=_run, args=(r, world, port, q, sp, prompts, overlap, replicate, sampling))
+          for r in range(world)]
     for p in ps:
         p.start()
     res, calls = {}, {}
@@ -131,3 +132,16 @@ def test_tp2_sequence_parallel_vocab_parallel_embedding():
     tp1 = _spawn(1, prompts=prompts)[0]
     assert _spawn(2, sp=True, prompts=prompts, replicate=False)[0] == tp1
     assert _spawn(2, sp=True, prompts=prompts)[0] == tp1
+
+
+def test_tp2_sampled_decode_matches_tp1():
+    """Temperature / top-k sampling: the noise is keyed by (seed, position, global token id) and the top-k threshold
+    is the global one (local candidates joined by one all-gather), so TP = 2 draws the TP = 1 tokens; a greedy row in
+    the same batch keeps its greedy tokens."""
+    from hrm_flashrenderer_b200.runtime.sampling import SamplingParams
+    sampling = [SamplingParams(temperature=0.8, top_k=20, seed=11), None]
+    tp1 = _spawn(1, sampling=sampling)[0]
+    tp2 = _spawn(2, sampling=sampling)
+    assert tp2[0] == tp2[1] == tp1
+    assert tp1[1] == _spawn(1)[0][1]          # the greedy row is unchanged
+    assert tp1[0] != _spawn(1)[0][0]          # the sampled row is not the greedy continuation
