@@ -15,6 +15,8 @@ profiler's per-launch DRAM bytes and duration can be set against them.  Ops (ker
 * ``norm_prep``     RMSNorm inputs of 16 tokens (norm_prep_kernel)
 * ``embed``         int8 embedding lookup of 16 tokens (embed_q8_kernel)
 * ``argmax``        split greedy pick over 16 x 128256 logits (argmax_kernel)
+* ``topk_threshold`` k-th largest of 16 x 128256 logits, k = 50 (kth_largest_kernel)
+* ``sample``        sampled pick (temperature 0.8, top-50 threshold) over 16 x 128256 logits (argmax_kernel<0, 1>)
 * ``flash_train_fwd`` / ``flash_train_bwd``  the trainer's causal attention at 128 sequences x 512 tokens, 8 heads of
   16 (flash_train_fwd_kernel; flash_train_dq_kernel + flash_train_dkv_kernel).  FLOPs are the executed multiply-adds
   x 2: 4 D per visible (query, key) pair forward, 14 D backward (S and dP are computed in both passes).
@@ -110,6 +112,23 @@ def _argmax(dev):
     return run, f"M16xV{LLAMA31_70B.vocab}", logits.numel() * 4, 0.0
 
 
+def _topk_threshold(dev):
+    logits = torch.randn(16, LLAMA31_70B.vocab, device=dev)
+    k = torch.full((16,), 50, dtype=torch.int32, device=dev)
+    run = lambda: ops.kth_largest(logits, k)
+    return run, f"M16xV{LLAMA31_70B.vocab}", logits.numel() * 4 * 4, 0.0   # four radix passes over the row
+
+
+def _sample(dev):
+    logits = torch.randn(16, LLAMA31_70B.vocab, device=dev)
+    thr = ops.kth_largest(logits, torch.full((16,), 50, dtype=torch.int32, device=dev))
+    it = torch.full((16,), 1 / 0.8, device=dev)
+    seed = torch.arange(16, dtype=torch.int64, device=dev)
+    pos = torch.full((16,), 100, dtype=torch.int32, device=dev)
+    run = lambda: ops.sample_rows(logits, 0, it, seed, pos, thr)
+    return run, f"M16xV{LLAMA31_70B.vocab}", logits.numel() * 4, 0.0
+
+
 def _flash_train(dev, backward: bool):
     B, T, H, D = 128, 512, 8, 16
     g = torch.Generator(device=dev).manual_seed(0)
@@ -126,6 +145,7 @@ def _flash_train(dev, backward: bool):
 
 OPS = {"gemm_prefill": _gemm_prefill, "gemm_decode_tp8": _gemm_decode_tp8, "attn_prefill": _attn_prefill,
        "attn_decode_tp8": _attn_decode_tp8, "norm_prep": _norm_prep, "embed": _embed, "argmax": _argmax,
+       "topk_threshold": _topk_threshold, "sample": _sample,
        "flash_train_fwd": lambda dev: _flash_train(dev, False), "flash_train_bwd": lambda dev: _flash_train(dev, True)}
 
 
