@@ -590,14 +590,17 @@ void argmax_rows_sample(at::Tensor logits, int64_t vocab_start, c10::optional<at
 }
 
 // Top-k selection helpers of the sampled pick: k-th largest per row, and each row's top-k candidate values.
-void kth_largest_rows(at::Tensor x, at::Tensor k, at::Tensor out) {
+void kth_largest_rows(at::Tensor x, at::Tensor k, at::Tensor out, at::Tensor state) {
   c10::cuda::CUDAGuard g(x.device());
-  CHECK_DTYPE(x, at::kFloat); CHECK_DTYPE(k, at::kInt); CHECK_DTYPE(out, at::kFloat);
+  CHECK_DTYPE(x, at::kFloat); CHECK_DTYPE(k, at::kInt); CHECK_DTYPE(out, at::kFloat); CHECK_DTYPE(state, at::kInt);
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be [R, n] row-major");
   TORCH_CHECK(k.is_contiguous() && out.is_contiguous() && k.numel() >= x.size(0) && out.numel() >= x.size(0),
               "k int32 [R], out f32 [R]");
+  TORCH_CHECK(state.is_contiguous() && state.numel() >= hrm::kth_largest_state_words((int)x.size(0)),
+              "state: int32 [kth_largest_state_words(R)]");
   hrm::kth_largest_launch(x.data_ptr<float>(), (int)x.size(0), (int)x.size(1), (int)x.stride(0), k.data_ptr<int>(),
-                          out.data_ptr<float>(), cur_stream());
+                          out.data_ptr<float>(), reinterpret_cast<uint32_t*>(state.data_ptr<int>()),
+                          hrm::gemm_sm_count(), cur_stream());
 }
 
 void topk_candidates_rows(at::Tensor x, at::Tensor thresh, at::Tensor k, at::Tensor cand) {
@@ -739,6 +742,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax_rows_xchg", &argmax_rows_xchg);
   m.def("argmax_rows_sample", &argmax_rows_sample, "temperature / top-k sampled pick on the argmax path");
   m.def("kth_largest_rows", &kth_largest_rows, "k-th largest value of every row (radix select)");
+  m.def("kth_largest_state_words", [](int64_t rows) { return (int64_t)hrm::kth_largest_state_words((int)rows); });
   m.def("topk_candidates_rows", &topk_candidates_rows, "each row's top-k candidate values");
   m.def("gemm_nt", &gemm_nt);
   m.def("flash_train_fwd", &flash_train_fwd, "trainer causal attention forward (o, lse)");

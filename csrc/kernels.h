@@ -118,7 +118,10 @@ void argmax_sample_launch(const float* logits, int M, int V, int ld, int vocab_s
                           const ArgmaxXchg* x, cudaStream_t s);
 // Top-k thresholds: out[r] = k[r]-th largest of x[r, 0:n] (-inf when k[r] <= 0 or >= n); candidates: the values
 // above thresh[r] then thresh[r] up to k[r] slots, then -inf, in [rows, kmax] (k[r] <= kmax) (sampling.cu).
-void kth_largest_launch(const float* x, int rows, int n, int ld, const int* k, float* out, cudaStream_t s);
+// kth_largest needs kth_largest_state_words(rows) u32 of scratch (initialised by the launch itself).
+int kth_largest_state_words(int rows);
+void kth_largest_launch(const float* x, int rows, int n, int ld, const int* k, float* out, uint32_t* state, int sms,
+                        cudaStream_t s);
 void topk_candidates_launch(const float* x, int rows, int n, int ld, const float* thresh, const int* k, int kmax,
                             float* cand, cudaStream_t s);
 

@@ -8,12 +8,12 @@
 // local top-k values: each rank writes its candidates (values above its local threshold, padded with the threshold
 // itself up to k), the candidates are gathered, and the same selection runs over the gathered rows.
 //
-// Selection: one CTA per row, radix select over the order-preserving 32-bit image of the floats, 8 bits per pass
-// (4 passes over the row), a 256-bin shared histogram fed through warp-aggregated atomics (lanes with the same bin
-// add once), so a row whose values share their top bits does not serialise on one bin.
+// Selection: radix select over the order-preserving 32-bit image of the floats in three passes (11 / 11 / 10 bits),
+// each pass spread over many CTAs per row so a decode batch of a few rows still uses the whole GPU.
 #include "common.cuh"
 #include "kernels.h"
 
+#include <algorithm>
 #include <stdexcept>
 #include <string>
 
@@ -22,57 +22,94 @@ namespace {
 constexpr int kSelThreads = 512;
 }
 
-// out[row] = k-th largest of x[row, 0:n] (k = kvec[row]); -inf when k <= 0 or k >= n (no restriction).
-__global__ void __launch_bounds__(kSelThreads)
-kth_largest_kernel(const float* __restrict__ x, int n, int ld, const int* __restrict__ kvec, float* __restrict__ out) {
-  __shared__ unsigned int hist[256];
-  __shared__ unsigned int s_prefix, s_remaining;
-  const int row = blockIdx.x;
-  const int k = kvec[row];
-  if (k <= 0 || k >= n) {
-    if (threadIdx.x == 0) out[row] = -INFINITY;
+// Multi-CTA radix select of the k-th largest value of every row, three digits of 11 / 11 / 10 bits over the
+// order-preserving image of the floats.  Per row, a state record { prefix, mask, remaining, pad, hist[2048] } lives
+// in global scratch; each pass is a histogram launch (grid: chunks x rows, every CTA counts the elements that match
+// the row's prefix in a shared histogram and adds its non-zero bins to the row's) followed by a select launch (one
+// CTA per row: finds the bin holding the remaining-th largest, extends the prefix and clears the histogram).
+constexpr int kRadixBins = 2048;
+constexpr int kRadixState = 4 + kRadixBins;   // u32 words per row
+constexpr int kHistThreads = 256;
+
+HRM_DEVINL void radix_digit(int pass, int& shift, uint32_t& digit) {
+  shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
+  digit = pass == 2 ? 0x3FFu : 0x7FFu;
+}
+
+__global__ void __launch_bounds__(kHistThreads)
+radix_init_kernel(const int* __restrict__ kvec, int n, uint32_t* __restrict__ state) {
+  uint32_t* st = state + (size_t)blockIdx.x * kRadixState;
+  const int k = kvec[blockIdx.x];
+  for (int i = threadIdx.x; i < kRadixState; i += blockDim.x) st[i] = 0u;
+  if (threadIdx.x == 0 && k > 0 && k < n) st[2] = (uint32_t)k;   // remaining; 0 marks "no restriction"
+}
+
+__global__ void __launch_bounds__(kHistThreads)
+radix_hist_kernel(const float* __restrict__ x, int n, int ld, int chunk, uint32_t* __restrict__ state, int pass) {
+  __shared__ uint32_t sh[kRadixBins];
+  const int row = blockIdx.y;
+  uint32_t* st = state + (size_t)row * kRadixState;
+  if (st[2] == 0u) return;   // row without a top-k restriction (uniform over the CTA)
+  const uint32_t prefix = st[0], mask = st[1];
+  int shift;
+  uint32_t digit;
+  radix_digit(pass, shift, digit);
+  for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) sh[b] = 0u;
+  __syncthreads();
+  const float* xr = x + (size_t)row * ld;
+  const int i0 = blockIdx.x * chunk, i1 = min(n, i0 + chunk);
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const uint32_t o = float_order(xr[i]);
+    if ((o & mask) == prefix) atomicAdd(&sh[(o >> shift) & digit], 1u);
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b <= (int)digit; b += blockDim.x)
+    if (sh[b] != 0u) atomicAdd(&st[4 + b], sh[b]);
+}
+
+// One warp per row: lane l sums a block of the bins (highest bins first), a warp scan over the block sums finds the
+// block that crosses `remaining`, and that lane walks its block.
+__global__ void __launch_bounds__(32)
+radix_select_kernel(uint32_t* __restrict__ state, int pass, float* __restrict__ out) {
+  const int row = blockIdx.x, lane = threadIdx.x;
+  uint32_t* st = state + (size_t)row * kRadixState;
+  const uint32_t remaining = st[2];
+  if (remaining == 0u) {
+    if (pass == 2 && lane == 0) out[row] = -INFINITY;
     return;
   }
-  const float* xr = x + (size_t)row * ld;
-  const int lane = threadIdx.x & 31;
-  uint32_t prefix = 0u, mask = 0u;
-  uint32_t remaining = (uint32_t)k;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0u;
-    __syncthreads();
-    // every thread of a warp runs the same number of iterations, so the warp-wide match below is well formed
-    for (int base = 0; base < n; base += blockDim.x) {
-      const int i = base + threadIdx.x;
-      bool take = false;
-      uint32_t bin = 0u;
-      if (i < n) {
-        const uint32_t o = float_order(xr[i]);
-        take = (o & mask) == prefix;
-        bin = (o >> shift) & 255u;
-      }
-      const unsigned active = __ballot_sync(0xffffffffu, take);
-      if (take) {
-        const unsigned peers = __match_any_sync(active, bin);
-        if (lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (unsigned)__popc(peers));
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      uint32_t above = 0u, b = 255u;
-      for (;; --b) {   // the bin holding the remaining-th largest of the values under the current prefix
-        if (above + hist[b] >= remaining || b == 0u) break;
-        above += hist[b];
-      }
-      s_prefix = prefix | (b << shift);
-      s_remaining = remaining - above;
-    }
-    __syncthreads();
-    prefix = s_prefix;
-    remaining = s_remaining;
-    mask |= 255u << shift;
-    __syncthreads();   // hist is cleared by the next pass
+  int shift;
+  uint32_t digit;
+  radix_digit(pass, shift, digit);
+  const int nb = (int)digit + 1, per = nb / 32;     // 64 or 32 bins per lane
+  const int hi = nb - 1 - lane * per;               // lane's block: bins hi, hi - 1, ..., hi - per + 1
+  uint32_t sum = 0u;
+  for (int j = 0; j < per; ++j) sum += st[4 + hi - j];
+  uint32_t incl = sum;                              // inclusive scan from the top bins down
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
   }
-  if (threadIdx.x == 0) out[row] = order_to_float(prefix);
+  const uint32_t excl = incl - sum;
+  const unsigned hit = __ballot_sync(0xffffffffu, excl < remaining && incl >= remaining);
+  const int owner = hit != 0u ? __ffs(hit) - 1 : 31;
+  if (lane == owner) {
+    uint32_t above = excl;
+    int b = hi;
+    for (int j = 0; j < per - 1; ++j, --b) {
+      const uint32_t c = st[4 + b];
+      if (above + c >= remaining) break;
+      above += c;
+    }
+    const uint32_t prefix = st[0] | ((uint32_t)b << shift);
+    st[0] = prefix;
+    st[1] |= digit << shift;
+    st[2] = remaining - above;
+    if (pass == 2) out[row] = order_to_float(prefix);
+  }
+  __syncwarp();
+  for (int b = lane; b < kRadixBins; b += 32) st[4 + b] = 0u;
 }
 
 // cand[row, 0:kmax] = the values of x[row] above thresh[row], then thresh[row] up to k slots, then -inf.  With no
@@ -103,10 +140,21 @@ topk_candidates_kernel(const float* __restrict__ x, int n, int ld, const float* 
   for (int i = filled + threadIdx.x; i < kmax; i += blockDim.x) cr[i] = (i < k && t != -INFINITY) ? t : -INFINITY;
 }
 
-void kth_largest_launch(const float* x, int rows, int n, int ld, const int* k, float* out, cudaStream_t s) {
+int kth_largest_state_words(int rows) { return rows * kRadixState; }
+
+void kth_largest_launch(const float* x, int rows, int n, int ld, const int* k, float* out, uint32_t* state, int sms,
+                        cudaStream_t s) {
   if (rows <= 0) return;
   if (n <= 0 || ld < n) throw std::runtime_error("kth_largest: bad row length / stride");
-  kth_largest_kernel<<<rows, kSelThreads, 0, s>>>(x, n, ld, k, out);
+  // about two CTAs per SM over all rows, at least 2048 elements per CTA
+  int chunks = std::max(1, std::min((2 * sms + rows - 1) / rows, (n + 2047) / 2048));
+  const int chunk = (n + chunks - 1) / chunks;
+  chunks = (n + chunk - 1) / chunk;
+  radix_init_kernel<<<rows, kHistThreads, 0, s>>>(k, n, state);
+  for (int pass = 0; pass < 3; ++pass) {
+    radix_hist_kernel<<<dim3(chunks, rows), kHistThreads, 0, s>>>(x, n, ld, chunk, state, pass);
+    radix_select_kernel<<<rows, 32, 0, s>>>(state, pass, out);
+  }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("kth_largest launch failed: ") + cudaGetErrorString(e));
 }

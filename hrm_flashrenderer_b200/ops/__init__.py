@@ -165,6 +165,8 @@ def _norm_kw(in_norm):
         return {}
     ssq, H, eps = in_norm
     return dict(in_ssq=ssq, inv_h=1.0 / float(H), eps=float(eps))
+
+
 def w8a16_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, bias: Optional[torch.Tensor] = None,
                  out_dtype: Optional[torch.dtype] = None, force_ctas: int = 0, in_norm=None) -> torch.Tensor:
     """``y = x @ (qweight * scale[:, None])^T (+ bias)``; int8 weights ``[N, K]`` (or pre-tiled by :func:`tile_w8`)
@@ -681,7 +683,7 @@ def gumbel_noise_host(seed: int, pos: int, ids) -> torch.Tensor:
 
 def kth_largest(x: torch.Tensor, k: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``out[r]`` = the ``k[r]``-th largest value of row ``r`` of ``x [R, n]`` (fp32); ``-inf`` when ``k[r] <= 0`` or
-    ``k[r] >= n`` (no restriction).  Radix select, one CTA per row."""
+    ``k[r] >= n`` (no restriction).  Radix select in three passes, each spread over many CTAs per row."""
     R, n = x.shape
     if out is None:
         out = torch.empty(R, dtype=torch.float32, device=x.device)
@@ -690,8 +692,9 @@ def kth_largest(x: torch.Tensor, k: torch.Tensor, out: Optional[torch.Tensor] = 
             kr = int(k[r])
             out[r] = -float("inf") if kr <= 0 or kr >= n else torch.topk(x[r].float(), kr).values[-1]
         return out
-    ext().kth_largest_rows(x, k, out)
-    LAUNCH_COUNTER.add()
+    state = torch.empty(int(ext().kth_largest_state_words(R)), dtype=torch.int32, device=x.device)
+    ext().kth_largest_rows(x, k, out, state)
+    LAUNCH_COUNTER.add(7)
     return out
 
 

@@ -78,16 +78,18 @@ def test_sampled_frequencies_follow_softmax():
 
 
 def test_engine_sampled_decode_graph_equals_eager():
-    from hrm_flashrenderer_b200.config import TINY, EngineConfig
+    from hrm_flashrenderer_b200.config import EngineConfig, ModelConfig
     from hrm_flashrenderer_b200.models.llama import LlamaW8
     from hrm_flashrenderer_b200.runtime.engine import InferenceEngine
     from hrm_flashrenderer_b200.runtime.sampling import SamplingParams
+    cfg = ModelConfig(name="gpu-sample", hidden=1024, layers=2, heads=8, kv_heads=2, head_dim=128,
+                      intermediate=2816, vocab=4096, rms_eps=1e-5, rope_theta=500000.0)
     g = torch.Generator().manual_seed(2)
-    prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (12, 5, 30)]
+    prompts = [torch.randint(0, 4096, (n,), generator=g).tolist() for n in (12, 5, 30)]
     sampling = [SamplingParams(0.9, 20, 7), None, SamplingParams(1.5, 0, 8)]
     outs = {}
     for graphs in (True, False):
-        m = LlamaW8.synthesize(TINY, device="cuda", max_pos=512 + 16)
+        m = LlamaW8.synthesize(cfg, device="cuda", max_pos=512 + 16)
         eng = InferenceEngine(m, EngineConfig(max_seq_len=512, max_batch=8, use_cuda_graphs=graphs), num_blocks=256)
         outs[graphs] = eng.generate(prompts, 24, stop_on_eos=False, sampling=sampling)
         again = eng.generate(prompts, 24, stop_on_eos=False, sampling=sampling)
