@@ -646,22 +646,22 @@ static void check_flash_train(std::initializer_list<const at::Tensor*> ts, const
               "flash_train: lse contiguous f32 [B, H, T] on the same device");
 }
 
-void flash_train_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse) {
+void flash_train_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, int64_t rpt) {
   c10::cuda::CUDAGuard g(q.device());
   check_flash_train({&q, &k, &v, &o}, q, lse);
   hrm::flash_train_fwd_launch(q.data_ptr<float>(), k.data_ptr<float>(), v.data_ptr<float>(), o.data_ptr<float>(),
                               lse.data_ptr<float>(), (int)q.size(0), (int)q.size(1), (int)q.size(2), (int)q.size(3),
-                              cur_stream());
+                              (int)rpt, cur_stream());
 }
 
 void flash_train_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, at::Tensor dout,
-                     at::Tensor dq, at::Tensor dk, at::Tensor dv) {
+                     at::Tensor dq, at::Tensor dk, at::Tensor dv, int64_t rpt) {
   c10::cuda::CUDAGuard g(q.device());
   check_flash_train({&q, &k, &v, &o, &dout, &dq, &dk, &dv}, q, lse);
   hrm::flash_train_bwd_launch(q.data_ptr<float>(), k.data_ptr<float>(), v.data_ptr<float>(), o.data_ptr<float>(),
                               lse.data_ptr<float>(), dout.data_ptr<float>(), dq.data_ptr<float>(), dk.data_ptr<float>(),
                               dv.data_ptr<float>(), (int)q.size(0), (int)q.size(1), (int)q.size(2), (int)q.size(3),
-                              cur_stream());
+                              (int)rpt, cur_stream());
 }
 
 void decode_prepare_bs(at::Tensor positions, at::Tensor tables, int64_t block_size, c10::optional<at::Tensor> active,
@@ -745,8 +745,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kth_largest_state_words", [](int64_t rows) { return (int64_t)hrm::kth_largest_state_words((int)rows); });
   m.def("topk_candidates_rows", &topk_candidates_rows, "each row's top-k candidate values");
   m.def("gemm_nt", &gemm_nt);
-  m.def("flash_train_fwd", &flash_train_fwd, "trainer causal attention forward (o, lse)");
-  m.def("flash_train_bwd", &flash_train_bwd, "trainer causal attention backward (dq, dk, dv)");
+  m.def("flash_train_fwd", &flash_train_fwd, "trainer causal attention forward (o, lse)", py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("rpt") = 2);
+  m.def("flash_train_bwd", &flash_train_bwd, "trainer causal attention backward (dq, dk, dv)", py::arg("q"),
+        py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("dout"), py::arg("dq"), py::arg("dk"),
+        py::arg("dv"), py::arg("rpt") = 2);
   m.def("grad_clip_factor", [](at::Tensor g, double clip, at::Tensor partial, at::Tensor scalars) {
     c10::cuda::CUDAGuard gd(g.device());
     TORCH_CHECK(g.is_cuda() && g.scalar_type() == at::kFloat && g.is_contiguous(), "g: contiguous f32 CUDA");

@@ -25,11 +25,12 @@ void grad_clip_factor_launch(const float* g, long long n, float clip, float* par
 void adamw_flat_launch(float* w, float* m, float* v, const float* g, long long n, float lr, float wd, float b1,
                        float b2, float eps, int* step, const float* scalars, int sm_count, cudaStream_t s);
 // Trainer causal attention (head dim 16 or 32, fp32, [B, T, H, D] rows, lse [B, H, T] in base-2 units): forward,
-// then backward as a dQ pass and a dK/dV pass (deterministic, no atomics).
+// then backward as a dQ pass and a dK/dV pass (deterministic, no atomics).  rpt: rows per thread (2: the D = 16
+// kernels that share each shared-memory read between two rows; 1: one row per thread).
 void flash_train_fwd_launch(const float* q, const float* k, const float* v, float* o, float* lse, int B, int T, int H,
-                            int D, cudaStream_t s);
+                            int D, int rpt, cudaStream_t s);
 void flash_train_bwd_launch(const float* q, const float* k, const float* v, const float* o, const float* lse,
-                            const float* dout, float* dq, float* dk, float* dv, int B, int T, int H, int D,
+                            const float* dout, float* dq, float* dk, float* dv, int B, int T, int H, int D, int rpt,
                             cudaStream_t s);
 void embed_q8_launch(const int64_t* ids, const int8_t* q, const float* scale, float* out, int M, int H,
                      int vocab_start, int vocab_local, cudaStream_t s);

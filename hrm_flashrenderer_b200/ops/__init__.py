@@ -596,6 +596,10 @@ def _causal_attention_math(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) ->
     return o.contiguous(), (m + torch.log2(l))[..., 0].contiguous()
 
 
+# Rows per thread of the trainer's flash kernels at head dim 16 (HRM_FLASH_RPT=1: the one-row kernels).
+FLASH_RPT = 1 if os.environ.get("HRM_FLASH_RPT", "2") == "1" else 2
+
+
 def flash_train_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     """Causal attention for the trainer: ``q, k, v`` contiguous fp32 ``[B, T, H, D]`` (D 16 or 32) -> ``(o, lse)``
     with ``o`` like ``q`` and ``lse`` the base-2 log-sum-exp of each row's scaled scores, ``[B, H, T]`` (the
@@ -605,7 +609,7 @@ def flash_train_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> Tuple[
     B, T, H, _ = q.shape
     o = torch.empty_like(q)
     lse = torch.empty(B, H, T, dtype=torch.float32, device=q.device)
-    ext().flash_train_fwd(q, k, v, o, lse)
+    ext().flash_train_fwd(q, k, v, o, lse, FLASH_RPT)
     LAUNCH_COUNTER.add()
     return o, lse
 
@@ -619,7 +623,7 @@ def flash_train_bwd(q, k, v, o, lse, dout) -> Tuple[torch.Tensor, torch.Tensor, 
             oo, _ = _causal_attention_math(qq, kk, vv)
             return torch.autograd.grad(oo, (qq, kk, vv), dout.float())
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    ext().flash_train_bwd(q, k, v, o, lse, dout.contiguous(), dq, dk, dv)
+    ext().flash_train_bwd(q, k, v, o, lse, dout.contiguous(), dq, dk, dv, FLASH_RPT)
     LAUNCH_COUNTER.add(2)
     return dq, dk, dv
 

@@ -22,9 +22,11 @@ def _ref(q, k, v, dout):
     return o, lse * math.log2(math.e), dq, dk, dv
 
 
+@pytest.mark.parametrize("rpt", [1, 2])
 @pytest.mark.parametrize("B,T,H,D", [(2, 1, 3, 16), (1, 7, 2, 16), (2, 64, 8, 16), (1, 130, 4, 32), (3, 512, 8, 16),
-                                     (1, 300, 2, 32), (1, 1000, 1, 16), (2, 129, 8, 16)])
-def test_flash_train_matches_fp64_math(B, T, H, D):
+                                     (1, 300, 2, 32), (1, 1000, 1, 16), (2, 129, 8, 16), (1, 257, 2, 16)])
+def test_flash_train_matches_fp64_math(B, T, H, D, rpt, monkeypatch):
+    monkeypatch.setattr(ops, "FLASH_RPT", rpt)
     g = torch.Generator(device="cpu").manual_seed(B * 1000 + T + H + D)
     q, k, v, dout = (torch.randn(B, T, H, D, generator=g).cuda() for _ in range(4))
     o, lse = ops.flash_train_fwd(q, k, v)
@@ -37,7 +39,9 @@ def test_flash_train_matches_fp64_math(B, T, H, D):
         torch.testing.assert_close(got.double(), want, rtol=1e-3, atol=2e-4 * max(1.0, T ** 0.5))
 
 
-def test_flash_train_backward_is_deterministic():
+@pytest.mark.parametrize("rpt", [1, 2])
+def test_flash_train_backward_is_deterministic(rpt, monkeypatch):
+    monkeypatch.setattr(ops, "FLASH_RPT", rpt)
     g = torch.Generator(device="cpu").manual_seed(11)
     q, k, v, dout = (torch.randn(4, 384, 8, 16, generator=g).cuda() for _ in range(4))
     o, lse = ops.flash_train_fwd(q, k, v)
