@@ -27,6 +27,7 @@ def _ref(q, k, v, dout):
                                      (1, 300, 2, 32), (1, 1000, 1, 16), (2, 129, 8, 16), (1, 257, 2, 16)])
 def test_flash_train_matches_fp64_math(B, T, H, D, rpt, monkeypatch):
     monkeypatch.setattr(ops, "FLASH_RPT", rpt)
+    monkeypatch.setattr(ops, "FLASH_FWD_RPT", rpt)
     g = torch.Generator(device="cpu").manual_seed(B * 1000 + T + H + D)
     q, k, v, dout = (torch.randn(B, T, H, D, generator=g).cuda() for _ in range(4))
     o, lse = ops.flash_train_fwd(q, k, v)
@@ -42,6 +43,7 @@ def test_flash_train_matches_fp64_math(B, T, H, D, rpt, monkeypatch):
 @pytest.mark.parametrize("rpt", [1, 2])
 def test_flash_train_backward_is_deterministic(rpt, monkeypatch):
     monkeypatch.setattr(ops, "FLASH_RPT", rpt)
+    monkeypatch.setattr(ops, "FLASH_FWD_RPT", rpt)
     g = torch.Generator(device="cpu").manual_seed(11)
     q, k, v, dout = (torch.randn(4, 384, 8, 16, generator=g).cuda() for _ in range(4))
     o, lse = ops.flash_train_fwd(q, k, v)
