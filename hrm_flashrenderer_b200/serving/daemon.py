@@ -278,10 +278,13 @@ def client_ping(addr: DaemonAddr) -> bool:
 
 
 def client_generate(addr: DaemonAddr, prompt: str = "", max_new_tokens: int = 64, input_ids=None,
-                    stop_on_eos: bool = True) -> Dict:
+                    stop_on_eos: bool = True, temperature: Optional[float] = None, top_k: Optional[int] = None,
+                    seed: Optional[int] = None) -> Dict:
+    """Generate through the lane daemon; ``temperature`` / ``top_k`` / ``seed`` request a sampled draw (absent:
+    greedy)."""
     c = Client((addr.host, addr.port), authkey=addr.authkey)
     c.send({"cmd": "generate", "prompt": prompt, "max_new_tokens": int(max_new_tokens), "input_ids": input_ids,
-            "stop_on_eos": stop_on_eos})
+            "stop_on_eos": stop_on_eos, "temperature": temperature, "top_k": top_k, "seed": seed})
     r = c.recv()
     c.close()
     if not r.get("ok"):

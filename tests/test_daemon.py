@@ -13,13 +13,13 @@ from _http import free_port  # noqa: E402
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _reference_tokens(prompts, n):
+def _reference_tokens(prompts, n, sampling=None):
     from hrm_flashrenderer_b200.config import TINY, EngineConfig
     from hrm_flashrenderer_b200.models.llama import LlamaW8
     from hrm_flashrenderer_b200.runtime.engine import InferenceEngine
     m = LlamaW8.synthesize(TINY, device="cpu", max_pos=512 + 16)
     eng = InferenceEngine(m, EngineConfig(max_seq_len=512, max_batch=8, use_cuda_graphs=False), num_blocks=256)
-    return eng.generate(prompts, n, stop_on_eos=False)
+    return eng.generate(prompts, n, stop_on_eos=False, sampling=sampling)
 
 
 def test_daemon_world2_rpc(tmp_path):
@@ -43,6 +43,12 @@ def test_daemon_world2_rpc(tmp_path):
         prompts = [torch.randint(0, 1024, (12,), generator=g).tolist() for _ in range(2)]
         outs = [client_generate(addr, input_ids=pr, max_new_tokens=10, stop_on_eos=False)["tokens"] for pr in prompts]
         assert outs == _reference_tokens(prompts, 10)
+        # a sampled request: the TP = 2 lane draws what one unsharded engine draws with the same seed
+        from hrm_flashrenderer_b200.runtime.sampling import SamplingParams
+        got = client_generate(addr, input_ids=prompts[0], max_new_tokens=10, stop_on_eos=False, temperature=0.9,
+                              top_k=30, seed=77)["tokens"]
+        assert got == _reference_tokens(prompts[:1], 10, SamplingParams(0.9, 30, 77))[0]
+        assert got != outs[0]
         client_shutdown(addr)
         p.wait(timeout=120)
         assert p.returncode == 0
