@@ -172,6 +172,9 @@ def run_worker(rank: int, a: LaneArgs, on_rank0: Callable[[Any], None]) -> None:
             watchdog.stop(clean=True)
         if a.device == "cuda":
             torch.cuda.synchronize()
+            # captured decode graphs may hold NCCL calls (the NCCL collectives, a sampled step's all-gather): they
+            # must go before the process group, or its teardown waits on them
+            engine.release_graphs()
         del engine
         dist.destroy_process_group()
 
