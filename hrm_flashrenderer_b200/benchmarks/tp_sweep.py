@@ -13,7 +13,6 @@ fused op = max(weights / HBM, (world - 1) x M x N x 4 B / NVLink), with the meas
 """
 import argparse
 import json
-import os
 
 import torch
 import torch.distributed as dist

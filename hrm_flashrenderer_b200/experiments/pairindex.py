@@ -9,7 +9,7 @@ from __future__ import annotations
 import ctypes
 import os
 from pathlib import Path
-from typing import Iterable, List, Optional, Sequence
+from typing import Iterable, Sequence
 
 import numpy as np
 

@@ -22,7 +22,7 @@ import os
 import struct
 from dataclasses import replace
 from pathlib import Path
-from typing import Dict, Iterable, Optional, Tuple
+from typing import Dict, Iterable, Tuple
 
 import numpy as np
 import torch

@@ -10,7 +10,7 @@ from __future__ import annotations
 import json
 import sys
 import time
-from typing import Callable, Dict, List
+from typing import Callable, Dict
 
 
 def run(log: Callable[[str], None] = print) -> Dict:

@@ -17,7 +17,7 @@ import sys
 import threading
 import time
 import urllib.request
-from typing import Dict, List, Optional
+from typing import Dict, Optional
 
 BANNED_MIXED = ("quellen", "snippets", "laut den", "basierend auf", "according to the documents",
                 "retrieved information")

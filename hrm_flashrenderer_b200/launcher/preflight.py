@@ -15,8 +15,8 @@ import sys
 from pathlib import Path
 from typing import Callable, List, Tuple
 
-from .hw import HWError, derive, load_selection
-from .topology import TopologyError, detect_layout, plan_lanes
+from .hw import derive, load_selection
+from .topology import detect_layout, plan_lanes
 
 REPO_ROOT = Path(__file__).resolve().parents[2]
 

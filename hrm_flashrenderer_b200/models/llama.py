@@ -26,7 +26,7 @@ from .. import ops
 from ..config import ModelConfig
 from ..models.oracle import rope_tables
 from ..models.weights import (QTensor, Tensorish, ShardPlan, layer_names, shard_plan, synth_matrix, matrix_shapes,
-                              vector_shapes, quantize_rows, EMBED, FINAL_NORM, LM_HEAD, get_lm_head)
+                              vector_shapes, EMBED, FINAL_NORM, LM_HEAD, get_lm_head)
 from ..runtime.kv_cache import PagedKVPool
 
 if TYPE_CHECKING:
@@ -183,7 +183,7 @@ class LlamaW8:
         Matrix ``i`` (DSI8 record order) draws from a generator seeded ``seed*1000003 + i`` exactly like
         :func:`~hrm_flashrenderer_b200.models.weights.synth_weights`, so a shard equals the slice of the full model.
         """
-        from .weights import synth_weights, shard_weights
+        from .weights import shard_weights
         dev = torch.device(device)
         plan = shard_plan(cfg, rank, world)
         shapes = list(matrix_shapes(cfg))

@@ -15,7 +15,6 @@ import json
 import os
 from dataclasses import asdict, fields
 from pathlib import Path
-from typing import Optional
 
 import torch
 

@@ -10,7 +10,7 @@ keyed by them.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Dict, Iterator, Optional, Tuple, Union
+from typing import Dict, Iterator, Tuple, Union
 
 import torch
 

@@ -12,8 +12,7 @@ syncs + 2 scale read-backs per layer, no EOS stop).  Here:
 """
 from __future__ import annotations
 
-import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from typing import Callable, Dict, List, Optional, Sequence, Tuple
 
 import torch

@@ -12,8 +12,6 @@ All backends expose ``tokenizer``, ``generate(prompt_text, max_new_tokens, timeo
 from __future__ import annotations
 
 import hashlib
-import threading
-from pathlib import Path
 from typing import Dict, List, Optional
 
 

@@ -16,8 +16,6 @@ from __future__ import annotations
 import argparse
 import datetime
 import os
-import socket
-import sys
 import threading
 from dataclasses import dataclass
 from multiprocessing.connection import Client, Listener

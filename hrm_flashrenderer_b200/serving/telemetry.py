@@ -14,7 +14,7 @@ import math
 import os
 import socket
 import struct
-from typing import Optional, Sequence
+from typing import Optional
 
 PACKET = struct.Struct("<I6f3f3f64s64s")
 

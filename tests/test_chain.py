@@ -5,7 +5,6 @@ GPU: the cooperative multi-phase kernel against the single-GEMM kernels.  The GP
 the f16 pair matched the single launches bitwise at M = 1 and 16 on a B200; the decode-layer sequence has not run
 on a GPU yet, and M 33..64 (BN = 64) is rejected after a timeout on its first run."""
 import os
-from dataclasses import replace
 
 import pytest
 import torch

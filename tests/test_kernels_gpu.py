@@ -1,5 +1,4 @@
 """sm_100a kernels vs plain PyTorch fp32 references of the same op (run on a B200 with -m gpu)."""
-import math
 import os
 
 import pytest

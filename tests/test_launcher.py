@@ -1,6 +1,5 @@
 """Hardware selection + topology planning with a fake nvidia-smi (no GPU)."""
 import os
-import sys
 
 import pytest
 

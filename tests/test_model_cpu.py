@@ -3,9 +3,9 @@ import numpy as np
 import torch
 
 from hrm_flashrenderer_b200.config import TINY, LLAMA31_70B, rope_inv_freq
-from hrm_flashrenderer_b200.formats.dsi8 import write_dsi8, read_dsi8, DSI8File
+from hrm_flashrenderer_b200.formats.dsi8 import write_dsi8, read_dsi8
 from hrm_flashrenderer_b200.models.oracle import OracleLlama
-from hrm_flashrenderer_b200.models.weights import quantize_rows, synth_weights, shard_weights, QTensor
+from hrm_flashrenderer_b200.models.weights import quantize_rows, synth_weights, QTensor
 from hrm_flashrenderer_b200.models.llama import LlamaW8
 from hrm_flashrenderer_b200.runtime.engine import InferenceEngine
 from hrm_flashrenderer_b200.config import EngineConfig

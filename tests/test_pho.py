@@ -7,7 +7,6 @@ from pathlib import Path
 
 import numpy as np
 import pytest
-import torch
 
 from hrm_flashrenderer_b200.experiments import pho
 

@@ -1,6 +1,5 @@
 """Reversible LM of the experiments plane: reversible backward == plain autograd, loss/decode consistency,
 checkpoint v11 round trip (CPU, fp32)."""
-import math
 
 import numpy as np
 import torch

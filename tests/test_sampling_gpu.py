@@ -1,8 +1,6 @@
 """Sampling kernels on the GPU: the radix-select top-k threshold and candidates against torch.topk, the sampled argmax
 against the host computation of the same noise, the draw frequencies against softmax(v / T), and sampled decoding
 through the engine (graph replay equals eager steps, reproducible, greedy rows unchanged)."""
-import math
-
 import pytest
 import torch
 

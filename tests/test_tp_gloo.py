@@ -4,10 +4,8 @@ Architecture: 4 layers, hidden 256, 8 q heads / 2 kv heads (head_dim 32), SwiGLU
 theta 1e4, no bias; weights N(0, 0.02) from seed 0 quantised per row; paged KV block 16; 2 prompts x 16 ids from
 seed 1; 32 greedy tokens.
 """
-import os
 import socket
 
-import pytest
 import torch
 import torch.multiprocessing as mp
 
