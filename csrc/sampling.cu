@@ -146,6 +146,7 @@ void kth_largest_launch(const float* x, int rows, int n, int ld, const int* k, f
                         cudaStream_t s) {
   if (rows <= 0) return;
   if (n <= 0 || ld < n) throw std::runtime_error("kth_largest: bad row length / stride");
+  if (rows > 65535) throw std::runtime_error("kth_largest: more than 65535 rows");
   // about two CTAs per SM over all rows, at least 2048 elements per CTA
   int chunks = std::max(1, std::min((2 * sms + rows - 1) / rows, (n + 2047) / 2048));
   const int chunk = (n + chunks - 1) / chunks;
