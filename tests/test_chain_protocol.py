@@ -193,7 +193,7 @@ def sim(G, phases, RW, RX, F, NACC, fold, owner="run", seed=0):
                 events.pop()()
                 moved = True
             if not moved and not events:
-                # nothing delivered or stepped this round: try every role once before declaring a deadlock
+                # nothing delivered or stepped in this pass: try every role once before declaring a deadlock
                 if not any(step(i) for i in list(pending) if i in pending):
                     return "deadlock", sorted(pending)[:12]
     except Alias as e:
