@@ -212,3 +212,40 @@ def test_transient_decode_error_fails_only_running_requests():
         sched.stop()
     assert outcomes.count("failed") == 2 and outcomes[2:] == [6, 6, 6, 6]
     assert sched.fatal is None and eng.bm.free_blocks == eng.bm.num_blocks
+
+
+def test_concurrent_submitters_get_their_isolated_tokens():
+    """Eight threads submit 24 requests at once (greedy and sampled, different lengths); every request still gets
+    exactly the tokens of its isolated run: batching, admission order and the submitting thread change nothing."""
+    import threading
+    from hrm_flashrenderer_b200.runtime.sampling import SamplingParams
+    g = torch.Generator().manual_seed(11)
+    reqs = []
+    for i in range(24):
+        prompt = torch.randint(0, 1024, (int(torch.randint(3, 40, (1,), generator=g)),), generator=g).tolist()
+        sp = SamplingParams(temperature=0.7 + 0.1 * (i % 3), top_k=(0, 8, 50)[i % 3], seed=1000 + i) if i % 2 else None
+        reqs.append((prompt, 4 + i % 7, sp))
+    ref_eng = _engine()
+    want = [ref_eng.generate([p], n, stop_on_eos=False, sampling=sp)[0] for p, n, sp in reqs]
+    sched = Scheduler(_engine(), interleave_chunk=16).start()
+    got = [None] * len(reqs)
+    errors = []
+
+    def worker(ids):
+        try:
+            hs = [(i, sched.submit(reqs[i][0], reqs[i][1], stop_on_eos=False, sampling=reqs[i][2])) for i in ids]
+            for i, h in hs:
+                got[i] = h.future.result(timeout=300)
+        except BaseException as e:   # surfaced by the main thread
+            errors.append(e)
+
+    try:
+        ts = [threading.Thread(target=worker, args=(list(range(t, 24, 8)),)) for t in range(8)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join(timeout=600)
+    finally:
+        sched.stop()
+    assert not errors, errors
+    assert got == want
