@@ -95,9 +95,12 @@ class EngineBackend:
                                           max_pos=max_seq_len + 16,
                                           cache_dir=os.environ.get("HRM_PACKED_CACHE") or None)
                 cfg = model.cfg
-            free, _ = torch.cuda.mem_get_info(dev)
-            nb = PagedKVPool.blocks_for_budget(int(free * kv_fraction), cfg.layers, model.plan.local_kv_heads,
-                                               cfg.head_dim)
+            if dev.type == "cuda":
+                free, _ = torch.cuda.mem_get_info(dev)
+                nb = PagedKVPool.blocks_for_budget(int(free * kv_fraction), cfg.layers, model.plan.local_kv_heads,
+                                                   cfg.head_dim)
+            else:   # CPU (tests, oracle runs): room for max_batch full-length sequences
+                nb = max_batch * ((max_seq_len + 15) // 16 + 1)
             ecfg = EngineConfig(tp=world, max_seq_len=max_seq_len, max_batch=max_batch, prefill_chunk=prefill_chunk)
             engine = InferenceEngine(model, ecfg, num_blocks=nb)
         self.engine = engine

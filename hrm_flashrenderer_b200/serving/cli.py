@@ -40,19 +40,25 @@ def _generate(args) -> int:
     if args.print_prompt:
         print(prompt)
         return 0
+    from ..runtime.sampling import sampling_from_request
+    try:
+        sampling = sampling_from_request(args.temperature, args.sample_top_k, args.seed)
+    except ValueError as e:
+        raise SystemExit(f"ERR: {e}")
     if args.use_daemon:
         from .daemon import parse_daemon_addr, client_generate
         addr = parse_daemon_addr()
         if addr is None:
             raise SystemExit("ERR: --use_daemon needs HRM_FLASH_DAEMON=host:port")
-        print(client_generate(addr, prompt=prompt, max_new_tokens=args.max_new_tokens)["text"])
+        print(client_generate(addr, prompt=prompt, max_new_tokens=args.max_new_tokens, temperature=args.temperature,
+                              top_k=args.sample_top_k, seed=args.seed)["text"])
         return 0
     from .backend import EngineBackend
     src, tok_src = resolve_model(args.llm_model, REPO_ROOT / "llm_models")
     be = EngineBackend(src, tokenizer_source=args.tokenizer_model or tok_src, device=args.device,
                        max_seq_len=args.max_seq_len, max_batch=1, prefill_chunk=args.prefill_chunk_size)
     try:
-        print(be.generate(prompt, args.max_new_tokens, args.native_request_timeout_s))
+        print(be.generate(prompt, args.max_new_tokens, args.native_request_timeout_s, sampling=sampling))
     finally:
         be.stop()
     return 0
@@ -91,6 +97,10 @@ def build_arg_parser() -> argparse.ArgumentParser:
     g.add_argument("--print_prompt", action="store_true")
     g.add_argument("--use_daemon", action="store_true")
     g.add_argument("--device", default="cuda:0")
+    # sampling (absent: greedy).  --top_k above is the HRM retrieval's cluster count, hence --sample_top_k here.
+    g.add_argument("--temperature", type=float, default=None)
+    g.add_argument("--sample_top_k", type=int, default=None)
+    g.add_argument("--seed", type=int, default=None)
     return ap
 
 

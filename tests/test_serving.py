@@ -253,3 +253,19 @@ def test_lane_call_errors_and_success():
     with pytest.raises(RT.LaneCallError, match="no answer") as ei:
         RT.http_json_get(base + "/h", 1.0)
     assert ei.value.status is None
+
+
+def test_cli_generate_greedy_and_sampled_on_cpu(capsys):
+    """``hrm-flash generate`` end to end on the CPU engine (synthetic tiny model, deepseek_only): the greedy answer
+    repeats, a seeded sampled answer repeats, and an invalid sampling flag is refused."""
+    from hrm_flashrenderer_b200.serving import cli
+    base = ["generate", "--hrm_model", "unused", "--llm_model", "synthetic:tiny", "--prompt", "hello there",
+            "--mode", "deepseek_only", "--device", "cpu", "--max_new_tokens", "6", "--max_seq_len", "128"]
+    outs = []
+    for extra in ([], [], ["--temperature", "0.9", "--sample_top_k", "20", "--seed", "5"],
+                  ["--temperature", "0.9", "--sample_top_k", "20", "--seed", "5"]):
+        assert cli.main(base + extra) == 0
+        outs.append(capsys.readouterr().out)
+    assert outs[0] == outs[1] and outs[2] == outs[3]
+    with pytest.raises(SystemExit):
+        cli.main(base + ["--temperature", "-1"])
