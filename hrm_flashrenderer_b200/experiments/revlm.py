@@ -137,7 +137,7 @@ class _TcMatmul(torch.autograd.Function):
         from .. import ops
         K, N = w.shape
         xb = x.reshape(-1, K).to(torch.bfloat16).contiguous()
-        y = ops.gemm_nt(xb, w.t().to(torch.bfloat16).contiguous())
+        y = ops.gemm_nt(xb, _bf16_copy(w.t()))
         ctx.save_for_backward(xb, w)
         ctx.xshape = x.shape
         return y.view(*x.shape[:-1], N)
@@ -150,10 +150,18 @@ class _TcMatmul(torch.autograd.Function):
         dyb = dy.reshape(-1, N).to(torch.bfloat16).contiguous()
         dx = dw = None
         if ctx.needs_input_grad[0]:
-            dx = ops.gemm_nt(dyb, w.to(torch.bfloat16).contiguous()).view(ctx.xshape)
+            dx = ops.gemm_nt(dyb, _bf16_copy(w)).view(ctx.xshape)
         if ctx.needs_input_grad[1]:
-            dw = ops.gemm_nt(xb.t().contiguous(), dyb.t().contiguous())
+            dw = ops.gemm_nt(_bf16_copy(xb.t()), _bf16_copy(dyb.t()))
         return dx, dw
+
+
+def _bf16_copy(t: torch.Tensor) -> torch.Tensor:
+    """A contiguous bf16 copy of a (possibly transposed or sliced) 2-D view in one copy kernel (conversion and
+    layout change together, where ``.to(bf16).contiguous()`` of a transposed view takes two)."""
+    out = torch.empty(t.shape, dtype=torch.bfloat16, device=t.device)
+    out.copy_(t)
+    return out
 
 
 def _tc_ok(x: torch.Tensor, w: torch.Tensor) -> bool:
