@@ -148,6 +148,7 @@ def main(argv=None) -> int:
     t.add_argument("--max_batch", type=int, default=64)
     t.add_argument("--max_seq_len", type=int, default=2560)
     t.add_argument("--device", default="cuda:0")
+    t.add_argument("--prefix_cache", action="store_true", help="share the trace's common system-prompt blocks")
     a = ap.parse_args(argv)
     if a.cmd == "grid":
         s = run_grid(a.router_url, Path(a.out_dir), modes=a.modes.split(","), route_hints=a.route_hints.split(","),
@@ -155,7 +156,8 @@ def main(argv=None) -> int:
         print(json.dumps(s, indent=1))
         return 0
     from ..serving.backend import EngineBackend
-    be = EngineBackend(a.model, device=a.device, max_seq_len=a.max_seq_len, max_batch=a.max_batch)
+    be = EngineBackend(a.model, device=a.device, max_seq_len=a.max_seq_len, max_batch=a.max_batch,
+                       prefix_cache=a.prefix_cache)
     try:
         res = run_trace(be.scheduler, make_trace(a.requests, a.rate, be.engine.cfg.vocab))
         print(json.dumps(res))

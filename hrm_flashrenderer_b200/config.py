@@ -207,6 +207,7 @@ class EngineConfig:
     sequence_parallel: bool = False      # prefill with a token-sharded residual stream (TP > 1)
     chain_layers: bool = False           # decode: o_proj..next QKV as one multi-phase GEMM launch
     prefill_overlap_chunks: int = 1      # TP prefill (NCCL path): row-parallel GEMM / all-reduce pipelined in chunks
+    prefix_cache: bool = False           # share the KV blocks of a prompt prefix seen before (shared system prompts)
     seed: int = 0
 
 

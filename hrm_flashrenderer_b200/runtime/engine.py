@@ -59,7 +59,7 @@ class InferenceEngine:
         model.sequence_parallel = bool(self.ecfg.sequence_parallel)
         model.chain_layers = bool(self.ecfg.chain_layers)
         model.prefill_overlap_chunks = int(self.ecfg.prefill_overlap_chunks)
-        self.bm = BlockManager(int(nb), bs)
+        self.bm = BlockManager(int(nb), bs, prefix_cache=bool(self.ecfg.prefix_cache))
         self._graphs: Dict[int, _DecodeGraph] = {}
         self._next_seq = 0
         self._pinned_tokens: Dict[int, torch.Tensor] = {}
@@ -72,6 +72,15 @@ class InferenceEngine:
 
     def release(self, seq_id: int) -> None:
         self.bm.free(seq_id)
+
+    def match_prefix(self, seq_id: int, tokens: Sequence[int]) -> int:
+        """Prefix cache: give the new sequence the published KV blocks its prompt starts with; returns the number of
+        prompt tokens already in the cache (prefill continues from there).  0 when the cache is off."""
+        return self.bm.match_prefix(seq_id, tokens)
+
+    def publish_prefix(self, seq_id: int, tokens: Sequence[int]) -> int:
+        """Prefix cache: publish the full blocks holding the (already prefilled) prompt ``tokens`` of ``seq_id``."""
+        return self.bm.publish(seq_id, tokens)
 
     def reset(self) -> None:
         self.bm.reset()
@@ -298,7 +307,10 @@ class InferenceEngine:
         eos = set(self.cfg.eos_token_ids if eos_ids is None else eos_ids)
         sids = [self.new_seq() for _ in prompts]
         try:
-            first = self.prefill(list(zip(sids, prompts)), sampling)
+            cached = [self.match_prefix(s, p) for s, p in zip(sids, prompts)]
+            first = self.prefill([(s, list(p)[c:]) for s, p, c in zip(sids, prompts, cached)], sampling)
+            for s, p in zip(sids, prompts):
+                self.publish_prefix(s, p)
             outs = [[t] for t in first]
             if on_token is not None and max_new_tokens >= 1:
                 for i, t in enumerate(first):

@@ -8,7 +8,9 @@ run (4 KB at bf16/D=128), the unit the attention kernels fetch.
 """
 from __future__ import annotations
 
+import hashlib
 import heapq
+from collections import OrderedDict
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence
 
@@ -30,9 +32,16 @@ class BlockManager:
       * otherwise the lowest free id.
     Nothing is reserved: another sequence may take an id of a started group, which only costs that tile its fast
     fetch.  The reference grows contiguous per-sequence pages by reallocation instead (``engine/llama_tp.py:21-108``).
+
+    ``prefix_cache``: full prompt blocks are published under a hash chain of their tokens (each key covers the
+    whole prefix up to that block), blocks are reference-counted, and a new sequence whose prompt starts with
+    published blocks shares them instead of recomputing them (:meth:`match_prefix`).  A published block whose last
+    user leaves stays cached and is evicted least-recently-freed first when a sequence needs a block.  Shared blocks
+    are never written: a sequence only writes positions at or after its own length, which starts behind its last
+    shared block.
     """
 
-    def __init__(self, num_blocks: int, block_size: int = 16, tile_blocks: int = 8):
+    def __init__(self, num_blocks: int, block_size: int = 16, tile_blocks: int = 8, prefix_cache: bool = False):
         self.num_blocks = int(num_blocks)
         self.block_size = int(block_size)
         self.tile_blocks = max(1, int(tile_blocks))
@@ -44,10 +53,78 @@ class BlockManager:
         self._gheap: List[int] = list(range(ng))                              # fully free groups (lazy deletion)
         self.tables: Dict[int, List[int]] = {}
         self.lengths: Dict[int, int] = {}
+        self.prefix_cache = bool(prefix_cache)
+        self._ref = [0] * self.num_blocks                      # users of each block
+        self._key_of: Dict[int, bytes] = {}                     # published block -> prefix key
+        self._block_of: Dict[bytes, int] = {}                   # prefix key -> published block
+        self._idle: "OrderedDict[int, None]" = OrderedDict()    # published blocks without users (evictable)
+        self.prefix_hits = 0                                    # blocks shared instead of recomputed
 
     @property
     def free_blocks(self) -> int:
-        return self._nfree
+        """Blocks a sequence can still take: free ones plus cached blocks nobody uses."""
+        return self._nfree + len(self._idle)
+
+    def _keys(self, tokens: Sequence[int], nblocks: int) -> List[bytes]:
+        bs, out, prev = self.block_size, [], b""
+        for i in range(nblocks):
+            h = hashlib.sha256(prev)
+            h.update(",".join(str(int(t)) for t in tokens[i * bs:(i + 1) * bs]).encode())
+            prev = h.digest()
+            out.append(prev)
+        return out
+
+    def match_prefix(self, seq_id: int, tokens: Sequence[int]) -> int:
+        """Share the longest run of published blocks that starts ``tokens`` with the new sequence ``seq_id``; at least
+        one token is left to compute (its logits give the first generated token).  Returns the tokens covered."""
+        if not self.prefix_cache or self.tables.get(seq_id):
+            return 0
+        tab = self.tables.setdefault(seq_id, [])
+        for key in self._keys(tokens, (len(tokens) - 1) // self.block_size):
+            b = self._block_of.get(key)
+            if b is None:
+                break
+            if self._ref[b] == 0:
+                self._idle.pop(b, None)
+            self._ref[b] += 1
+            tab.append(b)
+        self.prefix_hits += len(tab)
+        self.lengths[seq_id] = len(tab) * self.block_size
+        return self.lengths[seq_id]
+
+    def publish(self, seq_id: int, tokens: Sequence[int]) -> int:
+        """Publish the full blocks of ``seq_id`` that hold ``tokens`` (its prompt, already in the cache); returns the
+        number of newly published blocks.  A prefix some other block already publishes is left as it is."""
+        if not self.prefix_cache:
+            return 0
+        tab = self.tables.get(seq_id, [])
+        n = min(len(tokens) // self.block_size, len(tab))
+        added = 0
+        for b, key in zip(tab[:n], self._keys(tokens, n)):
+            if key in self._block_of or b in self._key_of:
+                continue
+            self._block_of[key] = b
+            self._key_of[b] = key
+            added += 1
+        return added
+
+    def _evict(self, n: int) -> None:
+        """Return ``n`` idle cached blocks (least recently freed first) to the free pool."""
+        for _ in range(n):
+            b, _ = self._idle.popitem(last=False)
+            del self._block_of[self._key_of.pop(b)]
+            self._release_block(b)
+
+    def _release_block(self, b: int) -> None:
+        tb = self.tile_blocks
+        self._is_free[b] = 1
+        self._nfree += 1
+        heapq.heappush(self._heap, b)
+        g = b // tb
+        if g < len(self._gfree):
+            self._gfree[g] += 1
+            if self._gfree[g] == tb:
+                heapq.heappush(self._gheap, g)
 
     def blocks_needed(self, seq_id: int, new_len: int) -> int:
         have = len(self.tables.get(seq_id, ()))
@@ -55,11 +132,12 @@ class BlockManager:
         return max(0, need - have)
 
     def can_grow(self, seq_id: int, new_len: int) -> bool:
-        return self.blocks_needed(seq_id, new_len) <= self._nfree
+        return self.blocks_needed(seq_id, new_len) <= self.free_blocks
 
     def _take(self, b: int) -> int:
         self._is_free[b] = 0
         self._nfree -= 1
+        self._ref[b] = 1
         g = b // self.tile_blocks
         if g < len(self._gfree):
             self._gfree[g] -= 1
@@ -83,8 +161,10 @@ class BlockManager:
     def grow(self, seq_id: int, new_len: int) -> List[int]:
         """Ensure ``seq_id`` can hold ``new_len`` tokens; returns its block table."""
         n = self.blocks_needed(seq_id, new_len)
+        if n > self.free_blocks:
+            raise OutOfBlocks(f"need {n} blocks for seq {seq_id}, {self.free_blocks} free")
         if n > self._nfree:
-            raise OutOfBlocks(f"need {n} blocks for seq {seq_id}, {self._nfree} free")
+            self._evict(n - self._nfree)
         tab = self.tables.setdefault(seq_id, [])
         for _ in range(n):
             tab.append(self._pick(tab))
@@ -92,20 +172,18 @@ class BlockManager:
         return tab
 
     def free(self, seq_id: int) -> None:
-        tb = self.tile_blocks
         for b in self.tables.pop(seq_id, []):
-            self._is_free[b] = 1
-            self._nfree += 1
-            heapq.heappush(self._heap, b)
-            g = b // tb
-            if g < len(self._gfree):
-                self._gfree[g] += 1
-                if self._gfree[g] == tb:
-                    heapq.heappush(self._gheap, g)
+            self._ref[b] -= 1
+            if self._ref[b] > 0:
+                continue                       # still shared by another sequence
+            if b in self._key_of:
+                self._idle[b] = None           # cached: reusable until evicted
+            else:
+                self._release_block(b)
         self.lengths.pop(seq_id, None)
 
     def reset(self) -> None:
-        self.__init__(self.num_blocks, self.block_size, self.tile_blocks)
+        self.__init__(self.num_blocks, self.block_size, self.tile_blocks, self.prefix_cache)
 
     def table_tensor(self, seq_ids: Sequence[int], width: Optional[int] = None, device="cpu") -> torch.Tensor:
         """``[len(seq_ids), width]`` int32 block tables padded with 0 (padding is never read: lengths bound it)."""

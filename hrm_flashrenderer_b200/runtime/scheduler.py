@@ -74,6 +74,7 @@ class Scheduler:
         self.max_batch = int(max_batch or engine.ecfg.max_batch)
         self.prefill_chunk = int(prefill_chunk or engine.ecfg.prefill_chunk)
         self.interleave_chunk = int(interleave_chunk or 0)
+        self.prefix_cache = bool(getattr(engine.ecfg, "prefix_cache", False))
         self.idle_sleep_s = idle_sleep_s
         self._inbox: "queue.Queue[GenRequest]" = queue.Queue()
         self._waiting: Deque[GenRequest] = collections.deque()
@@ -154,7 +155,8 @@ class Scheduler:
                 "prefilling": len(self._prefilling),
                 "completed": self.completed, "generated_tokens": self.generated_tokens,
                 "tok_per_s": self.generated_tokens / el, "ttft_p50_ms": pct(tt, 0.5), "ttft_p99_ms": pct(tt, 0.99),
-                "itl_p50_ms": pct(it, 0.5), "last_error": self.last_error, "fatal": self.fatal}
+                "itl_p50_ms": pct(it, 0.5), "last_error": self.last_error, "fatal": self.fatal,
+                "prefix_cache_hit_blocks": getattr(getattr(self.engine, "bm", None), "prefix_hits", 0)}
 
     # ------------------------------------------------------------------ loop
     def _finish(self, r: GenRequest) -> None:
@@ -197,7 +199,8 @@ class Scheduler:
                 break
             self._waiting.popleft()
             r.seq_id = eng.new_seq()
-            r._done = 0
+            # prefix cache: the prompt's leading blocks may already be in the KV cache (a shared system prompt)
+            r._done = eng.match_prefix(r.seq_id, r.prompt_ids) if self.prefix_cache else 0
             committed += self._full_need(r)
             self._prefilling.append(r)
         if not self._prefilling:
@@ -227,6 +230,8 @@ class Scheduler:
             if r._done < len(r.prompt_ids):
                 continue   # the token after a partial prompt is not a generated token
             done.append(r)
+            if self.prefix_cache:
+                eng.publish_prefix(r.seq_id, r.prompt_ids)
             r.first_token_at = now
             self.ttfts.append(now - r.arrival)
             r._last_tok_at = now

@@ -74,7 +74,7 @@ class EngineBackend:
     def __init__(self, model_source: str, tokenizer_source: Optional[str] = None, device: str = "cuda:0",
                  max_seq_len: int = 8192, max_batch: int = 64, prefill_chunk: int = 4096,
                  kv_fraction: float = 0.85, max_prompt_tokens: int = 2048, local_files_only: bool = True,
-                 seed: int = 0, comm=None, rank: int = 0, world: int = 1, engine=None):
+                 seed: int = 0, comm=None, rank: int = 0, world: int = 1, engine=None, prefix_cache: bool = False):
         import torch
         from ..config import EngineConfig, get_preset
         from ..models.llama import LlamaW8
@@ -101,7 +101,8 @@ class EngineBackend:
                                                    cfg.head_dim)
             else:   # CPU (tests, oracle runs): room for max_batch full-length sequences
                 nb = max_batch * ((max_seq_len + 15) // 16 + 1)
-            ecfg = EngineConfig(tp=world, max_seq_len=max_seq_len, max_batch=max_batch, prefill_chunk=prefill_chunk)
+            ecfg = EngineConfig(tp=world, max_seq_len=max_seq_len, max_batch=max_batch, prefill_chunk=prefill_chunk,
+                                prefix_cache=prefix_cache)
             engine = InferenceEngine(model, ecfg, num_blocks=nb)
         self.engine = engine
         self.scheduler = Scheduler(engine).start()

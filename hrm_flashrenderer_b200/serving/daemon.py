@@ -30,7 +30,8 @@ from ..runtime.sampling import sampling_from_request
 class MirroredEngine:
     """Rank-0 proxy of an :class:`InferenceEngine`: every state-changing call is first broadcast to the followers."""
 
-    _MIRRORED = ("prefill", "load_decode_batch", "decode_step", "release", "new_seq", "capture", "reset")
+    _MIRRORED = ("prefill", "load_decode_batch", "decode_step", "release", "new_seq", "capture", "reset",
+                 "match_prefix", "publish_prefix")
 
     def __init__(self, engine, group, watchdog=None):
         self._engine = engine
@@ -94,6 +95,7 @@ class LaneArgs:
     heartbeat_timeout_s: float = 30.0   # a TP peer silent this long is treated as lost
     packed_cache_dir: str = ""           # per-rank packed-shard cache for DSI8 exports (default: HRM_PACKED_CACHE)
     fused_collectives: bool = True       # TP > 1 on CUDA: in-kernel NVLink all-reduce / argmax (False: NCCL calls)
+    prefix_cache: bool = False           # share the KV blocks of prompt prefixes seen before (shared system prompts)
 
 
 def build_engine(a: LaneArgs, rank: int, world: int, comm):
@@ -128,7 +130,7 @@ def build_engine(a: LaneArgs, rank: int, world: int, comm):
         dist.all_reduce(t, op=dist.ReduceOp.MIN, group=comm.control if hasattr(comm, "control") else None)
         nb = int(t.item())
     ecfg = EngineConfig(tp=world, max_seq_len=a.max_seq_len, max_batch=a.max_batch, prefill_chunk=a.prefill_chunk_size,
-                        use_cuda_graphs=dev.type == "cuda")
+                        use_cuda_graphs=dev.type == "cuda", prefix_cache=a.prefix_cache)
     return InferenceEngine(model, ecfg, num_blocks=nb)
 
 
@@ -278,6 +280,15 @@ def client_ping(addr: DaemonAddr) -> bool:
         return False
 
 
+def client_metrics(addr: DaemonAddr) -> Dict:
+    """The lane scheduler's metrics (queue, batch, throughput, latency percentiles, prefix-cache hits)."""
+    c = Client((addr.host, addr.port), authkey=addr.authkey)
+    c.send({"cmd": "ping"})
+    r = c.recv()
+    c.close()
+    return dict(r.get("metrics") or {})
+
+
 def client_generate(addr: DaemonAddr, prompt: str = "", max_new_tokens: int = 64, input_ids=None,
                     stop_on_eos: bool = True, temperature: Optional[float] = None, top_k: Optional[int] = None,
                     seed: Optional[int] = None) -> Dict:
@@ -327,10 +338,11 @@ def main(argv=None):
     ap.add_argument("--num_kv_blocks", type=int, default=0)
     ap.add_argument("--nccl_collectives", action="store_true",
                     help="TP all-reduce and argmax through NCCL calls instead of the fused peer-memory kernels")
+    ap.add_argument("--prefix_cache", action="store_true", help="share KV blocks of prompt prefixes seen before")
     args = ap.parse_args(argv)
     lane = LaneArgs(args.model, args.world, args.max_seq_len, args.prefill_chunk_size, args.max_batch, args.device,
                     master_port=args.master_port, num_kv_blocks=args.num_kv_blocks,
-                    fused_collectives=not args.nccl_collectives)
+                    fused_collectives=not args.nccl_collectives, prefix_cache=args.prefix_cache)
     spawn_lane(lane, _RpcEntry(args.host, args.port, args.authkey.encode(), args.tokenizer_model, args.ready_file))
 
 

@@ -271,6 +271,8 @@ def build_arg_parser() -> argparse.ArgumentParser:
     ap.add_argument("--max_prompt_tokens", type=int, default=int(os.environ.get("DSI8_MAX_PROMPT_TOKENS", "2048")))
     ap.add_argument("--native_request_timeout_s", type=float, default=180.0)
     ap.add_argument("--device", default="cuda:0")
+    ap.add_argument("--prefix_cache", action="store_true",
+                    help="share the KV blocks of prompt prefixes seen before (the system prompt, repeated context)")
     ap.add_argument("--nccl_collectives", action="store_true",
                     help="TP lane: all-reduce and argmax through NCCL calls instead of the fused peer-memory kernels")
     return ap
@@ -304,7 +306,7 @@ def main(argv=None):
         src, tok = resolve_model(args.llm_model, REPO_ROOT / "llm_models")
         lane = LaneArgs(src, args.world, args.max_seq_len, args.prefill_chunk_size, args.max_batch, "cuda",
                         master_port=int(os.environ.get("HRM_LANE_MASTER_PORT", str(29600 + args.port % 1000))),
-                        fused_collectives=not args.nccl_collectives)
+                        fused_collectives=not args.nccl_collectives, prefix_cache=args.prefix_cache)
         spawn_lane(lane, _HttpEntry(args, str(hrm_model), args.tokenizer_model or tok))
         return
     if args.backend == "echo":
@@ -316,7 +318,7 @@ def main(argv=None):
         backend = EngineBackend(src, tokenizer_source=args.tokenizer_model or tok, device=args.device,
                                 max_seq_len=args.max_seq_len, max_batch=args.max_batch,
                                 prefill_chunk=args.prefill_chunk_size, max_prompt_tokens=args.max_prompt_tokens,
-                                local_files_only=args.local_files_only)
+                                local_files_only=args.local_files_only, prefix_cache=args.prefix_cache)
     state = ServiceState(backend=backend, hrm_model=hrm_model,
                          hrm_bin=find_hrm_binary(repo_root=REPO_ROOT, explicit=args.hrm_bin),
                          max_seq_len=args.max_seq_len, max_new_tokens=args.max_new_tokens,

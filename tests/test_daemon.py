@@ -70,3 +70,36 @@ def test_build_engine_enables_fused_collectives(monkeypatch, fused):
     eng = build_engine(a, 0, 1, None)
     assert calls == ([None] if fused else [])
     assert len(eng.generate([[1, 2, 3]], 2, stop_on_eos=False)[0]) == 2
+
+
+def test_daemon_world2_prefix_cache(tmp_path):
+    """TP = 2 lane with the prefix cache: prefix matching and publication are mirrored to the follower, so both
+    ranks share the same blocks, and requests sharing a prefix still get the unsharded engine's tokens."""
+    from hrm_flashrenderer_b200.serving.daemon import DaemonAddr, client_generate, client_metrics, client_shutdown
+    ready = tmp_path / "ready"
+    env = dict(os.environ, OMP_NUM_THREADS="2")
+    p = subprocess.Popen([sys.executable, "-m", "hrm_flashrenderer_b200.serving.daemon", "--model", "synthetic:tiny",
+                          "--world", "2", "--device", "cpu", "--max_seq_len", "512", "--max_batch", "8",
+                          "--ready_file", str(ready), "--master_port", str(free_port()), "--num_kv_blocks", "256",
+                          "--prefix_cache"],
+                         cwd=ROOT, env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT)
+    try:
+        t0 = time.time()
+        while not ready.exists():
+            assert p.poll() is None, p.stdout.read().decode()[-3000:]
+            assert time.time() - t0 < 180, "daemon did not start"
+            time.sleep(0.2)
+        host, port = ready.read_text().strip().rsplit(":", 1)
+        addr = DaemonAddr(host, int(port), b"hrmflash")
+        g = torch.Generator().manual_seed(8)
+        system = torch.randint(0, 1024, (40,), generator=g).tolist()
+        prompts = [system + torch.randint(0, 1024, (5 + 3 * i,), generator=g).tolist() for i in range(3)]
+        outs = [client_generate(addr, input_ids=pr, max_new_tokens=8, stop_on_eos=False)["tokens"] for pr in prompts]
+        assert outs == _reference_tokens(prompts, 8)
+        assert client_metrics(addr)["prefix_cache_hit_blocks"] >= 4
+        client_shutdown(addr)
+        p.wait(timeout=120)
+        assert p.returncode == 0
+    finally:
+        if p.poll() is None:
+            p.kill()

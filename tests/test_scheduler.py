@@ -137,9 +137,9 @@ class _Recorder:
     def __getattr__(self, k):
         return getattr(self.eng, k)
 
-    def prefill(self, seqs):
+    def prefill(self, seqs, *rest):
         self.log.append(("prefill", sum(len(t) for _, t in seqs)))
-        return self.eng.prefill(seqs)
+        return self.eng.prefill(seqs, *rest)
 
     def decode_step(self, g):
         self.log.append(("decode", 0))
@@ -249,3 +249,39 @@ def test_concurrent_submitters_get_their_isolated_tokens():
         sched.stop()
     assert not errors, errors
     assert got == want
+
+
+def _engine_pc(prefix_cache, num_blocks=96):
+    w = synth_weights(TINY, seed=4)
+    m = LlamaW8.from_weights(TINY, w, device="cpu", max_pos=512)
+    return InferenceEngine(m, EngineConfig(max_seq_len=256, max_batch=4, prefill_chunk=40, use_cuda_graphs=False,
+                                           graph_batch_buckets=(1, 2, 4), prefix_cache=prefix_cache),
+                           num_blocks=num_blocks)
+
+
+def test_prefix_cache_gives_the_same_tokens_and_skips_shared_blocks():
+    """Requests that share a 48-token system prefix: with the prefix cache the later ones reuse its KV blocks (fewer
+    prompt tokens prefilled) and every request still produces its isolated tokens, greedy and sampled; a pool too
+    small to keep everything cached evicts and stays correct."""
+    from hrm_flashrenderer_b200.runtime.sampling import SamplingParams
+    g = torch.Generator().manual_seed(21)
+    system = torch.randint(0, 1024, (48,), generator=g).tolist()
+    reqs = [(system + torch.randint(0, 1024, (int(n),), generator=g).tolist(), 6,
+             SamplingParams(0.8, 20, 40 + i) if i % 3 == 2 else None)
+            for i, n in enumerate(torch.randint(1, 30, (9,), generator=g))]
+    ref = _engine_pc(False)
+    want = [ref.generate([p], n, stop_on_eos=False, sampling=sp)[0] for p, n, sp in reqs]
+    for blocks in (96, 24):
+        eng = _engine_pc(True, blocks)
+        rec = _Recorder(eng)
+        sched = Scheduler(rec, interleave_chunk=16).start()
+        try:
+            got = []
+            for p, n, sp in reqs:                  # one after another: each finds the published prefix
+                got.append(sched.generate(p, n, timeout=120, stop_on_eos=False, sampling=sp))
+            hits = sched.metrics()["prefix_cache_hit_blocks"]
+        finally:
+            sched.stop()
+        assert got == want, blocks
+        prefilled = sum(t for k, t in rec.log if k == "prefill")
+        assert hits >= 3 * (len(reqs) - 1) and prefilled == sum(len(p) for p, _, _ in reqs) - 16 * hits
