@@ -99,6 +99,9 @@ _PROM_ENGINE = (
     ("ttft_p50_ms", "hrm_engine_ttft_p50_ms", "gauge", "median time to first token (ms)"),
     ("ttft_p99_ms", "hrm_engine_ttft_p99_ms", "gauge", "99th percentile time to first token (ms)"),
     ("itl_p50_ms", "hrm_engine_itl_p50_ms", "gauge", "median inter-token latency (ms)"),
+    ("prefilling", "hrm_engine_prefilling", "gauge", "admitted requests whose prompt is still being prefilled"),
+    ("prefix_cache_hit_blocks", "hrm_engine_prefix_cache_hit_blocks_total", "counter",
+     "KV blocks shared from the prefix cache instead of recomputed"),
 )
 
 
