@@ -22,7 +22,8 @@ import collections
 import queue
 import threading
 import time
-from concurrent.futures import Future
+from concurrent.futures import CancelledError, Future
+from concurrent.futures import TimeoutError as FutureTimeout
 from dataclasses import dataclass, field
 from typing import Callable, Deque, Dict, List, Optional, Sequence
 
@@ -59,6 +60,7 @@ class GenRequest:
     seq_id: int = -1
     error: Optional[BaseException] = None
     sampling: Optional[SamplingParams] = None   # None: greedy
+    cancelled: bool = False                     # set by Scheduler.cancel; the loop drops the request
 
     @property
     def ttft_s(self) -> Optional[float]:
@@ -88,6 +90,7 @@ class Scheduler:
         self.eos = set(engine.cfg.eos_token_ids)
         # metrics
         self.completed = 0
+        self.cancelled_total = 0
         self.generated_tokens = 0
         self.ttfts: Deque[float] = collections.deque(maxlen=4096)
         self.itls: Deque[float] = collections.deque(maxlen=4096)
@@ -144,7 +147,19 @@ class Scheduler:
 
     def generate(self, prompt_ids: Sequence[int], max_new_tokens: int, timeout: Optional[float] = None,
                  stop_on_eos: bool = True, sampling: Optional[SamplingParams] = None) -> List[int]:
-        return self.submit(prompt_ids, max_new_tokens, stop_on_eos, sampling=sampling).future.result(timeout)
+        """Submit and wait; a request that outlives ``timeout`` is cancelled (its KV blocks and batch slot are
+        given back) before the timeout propagates."""
+        r = self.submit(prompt_ids, max_new_tokens, stop_on_eos, sampling=sampling)
+        try:
+            return r.future.result(timeout)
+        except FutureTimeout:
+            self.cancel(r)
+            raise
+
+    def cancel(self, r: GenRequest) -> None:
+        """Stop ``r``: the loop drops it before its next prefill chunk or decode step, releases its KV blocks and
+        fails its future with ``CancelledError``.  No effect on a finished request."""
+        r.cancelled = True
 
     def metrics(self) -> Dict:
         el = max(1e-9, time.perf_counter() - self.started_at)
@@ -156,7 +171,8 @@ class Scheduler:
                 "completed": self.completed, "generated_tokens": self.generated_tokens,
                 "tok_per_s": self.generated_tokens / el, "ttft_p50_ms": pct(tt, 0.5), "ttft_p99_ms": pct(tt, 0.99),
                 "itl_p50_ms": pct(it, 0.5), "last_error": self.last_error, "fatal": self.fatal,
-                "prefix_cache_hit_blocks": getattr(getattr(self.engine, "bm", None), "prefix_hits", 0)}
+                "prefix_cache_hit_blocks": getattr(getattr(self.engine, "bm", None), "prefix_hits", 0),
+                "cancelled": self.cancelled_total}
 
     # ------------------------------------------------------------------ loop
     def _finish(self, r: GenRequest) -> None:
@@ -195,6 +211,10 @@ class Scheduler:
         committed = self._pending_growth() + sum(self._full_need(r) for r in self._prefilling)
         while self._waiting and len(self._running) + len(self._prefilling) < self.max_batch:
             r = self._waiting[0]
+            if r.cancelled:   # cancelled while it arrived: never touches the engine
+                self._waiting.popleft()
+                self._cancel_future(r)
+                continue
             if self._full_need(r) > eng.bm.free_blocks - committed:
                 break
             self._waiting.popleft()
@@ -277,6 +297,30 @@ class Scheduler:
         self._running = still
         return (not changed), g
 
+    def _drop_cancelled(self) -> bool:
+        """Remove cancelled requests from every stage; True when the decode batch changed."""
+        changed = False
+        for name in ("_prefilling", "_running"):
+            keep = []
+            for r in getattr(self, name):
+                if r.cancelled:
+                    self.engine.release(r.seq_id)
+                    self._cancel_future(r)
+                    changed |= name == "_running"
+                else:
+                    keep.append(r)
+            setattr(self, name, keep)
+        if any(r.cancelled for r in self._waiting):
+            for r in [r for r in self._waiting if r.cancelled]:
+                self._cancel_future(r)
+            self._waiting = collections.deque(r for r in self._waiting if not r.cancelled)
+        return changed
+
+    def _cancel_future(self, r: GenRequest) -> None:
+        self.cancelled_total += 1
+        if not r.future.done():
+            r.future.set_exception(CancelledError(f"request {r.rid} cancelled"))
+
     def _loop(self) -> None:
         staged, g = False, None
         dev = self.engine.device
@@ -284,6 +328,8 @@ class Scheduler:
             torch.cuda.set_device(dev)
         while not self._stop.is_set():
             try:
+                if self._drop_cancelled():
+                    staged = False
                 admitted = self._admit()
                 if admitted:
                     staged = False

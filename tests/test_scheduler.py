@@ -1,5 +1,6 @@
 """Continuous-batching scheduler on the CPU engine: concurrent requests with different lengths join and leave the
 decode batch; each request's tokens equal an isolated greedy run."""
+import pytest
 import torch
 
 from hrm_flashrenderer_b200.config import TINY, EngineConfig
@@ -285,3 +286,42 @@ def test_prefix_cache_gives_the_same_tokens_and_skips_shared_blocks():
         assert got == want, blocks
         prefilled = sum(t for k, t in rec.log if k == "prefill")
         assert hits >= 3 * (len(reqs) - 1) and prefilled == sum(len(p) for p, _, _ in reqs) - 16 * hits
+
+
+def test_cancel_running_waiting_and_timed_out_requests():
+    """A cancelled request leaves the batch before its next step and gives its KV blocks back; a request cancelled
+    while queued never reaches the engine; ``generate`` cancels a request whose wait timed out; requests that run
+    alongside still produce their isolated tokens."""
+    import time
+    from concurrent.futures import CancelledError
+    from concurrent.futures import TimeoutError as FutureTimeout
+    g = torch.Generator().manual_seed(13)
+    keep = torch.randint(0, 1024, (10,), generator=g).tolist()
+    ref = _engine().generate([keep], 30, stop_on_eos=False)[0]
+    eng = _engine()
+    total = eng.bm.free_blocks
+    sched = Scheduler(eng, max_batch=2).start()
+    try:
+        long_ = sched.submit(torch.randint(0, 1024, (12,), generator=g).tolist(), 200, stop_on_eos=False)
+        other = sched.submit(keep, 30, stop_on_eos=False)
+        queued = sched.submit([1, 2, 3], 5, stop_on_eos=False)      # batch full: waits
+        sched.cancel(queued)
+        t0 = time.time()
+        while len(long_.tokens) < 5 and time.time() - t0 < 60:
+            time.sleep(0.001)
+        sched.cancel(long_)
+        with pytest.raises(CancelledError):
+            long_.future.result(timeout=60)
+        with pytest.raises(CancelledError):
+            queued.future.result(timeout=60)
+        assert queued.seq_id == -1 and len(long_.tokens) < 200
+        assert other.future.result(timeout=120) == ref
+        with pytest.raises(FutureTimeout):
+            sched.generate([4, 5, 6], 200, timeout=0.05, stop_on_eos=False)
+        t0 = time.time()
+        while (sched.metrics()["batch_size"] or sched.metrics()["prefilling"]) and time.time() - t0 < 60:
+            time.sleep(0.01)
+        assert sched.metrics()["cancelled"] == 3
+        assert eng.bm.free_blocks == total
+    finally:
+        sched.stop()
