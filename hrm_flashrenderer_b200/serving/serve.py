@@ -102,6 +102,7 @@ _PROM_ENGINE = (
     ("prefilling", "hrm_engine_prefilling", "gauge", "admitted requests whose prompt is still being prefilled"),
     ("prefix_cache_hit_blocks", "hrm_engine_prefix_cache_hit_blocks_total", "counter",
      "KV blocks shared from the prefix cache instead of recomputed"),
+    ("cancelled", "hrm_engine_requests_cancelled_total", "counter", "requests cancelled (caller timed out)"),
 )
 
 
