@@ -6,13 +6,15 @@
   architecture; the tokenizer is a local HF tokenizer or the byte tokenizer.
 * :class:`EchoBackend` -- deterministic stand-in used by tests and the mock lanes.
 
-All backends expose ``tokenizer``, ``generate(prompt_text, max_new_tokens, timeout_s) -> str``, ``is_running()``,
-``stop()`` and ``metrics()``.
+All backends expose ``tokenizer``, ``generate(prompt_text, max_new_tokens, timeout_s, sampling=None) -> str``,
+``generate_stream(...)`` (an iterator of text deltas), ``is_running()``, ``stop()`` and ``metrics()``.
 """
 from __future__ import annotations
 
 import hashlib
-from typing import Dict, List, Optional
+import queue
+import time
+from typing import Dict, Iterator, List, Optional
 
 
 class ByteTokenizer:
@@ -57,6 +59,13 @@ class EchoBackend:
             raise RuntimeError("echo backend configured to fail")
         h = hashlib.sha256(prompt_text.encode()).hexdigest()[:16]
         return f"answer-{h}"[: max(1, max_new_tokens * 4)]
+
+    def generate_stream(self, prompt_text: str, max_new_tokens: int = 64, timeout_s: float = 180.0,
+                        sampling=None) -> Iterator[str]:
+        """The same answer in 4-character pieces."""
+        text = self.generate(prompt_text, max_new_tokens, timeout_s, sampling)
+        for i in range(0, len(text), 4):
+            yield text[i:i + 4]
 
     def is_running(self) -> bool:
         return True
@@ -128,6 +137,48 @@ class EngineBackend:
                  sampling=None) -> str:
         out = self.generate_ids(self.encode_prompt(prompt_text), max_new_tokens, timeout_s, sampling)
         return self.tokenizer.decode(out, skip_special_tokens=True)
+
+    def generate_stream(self, prompt_text: str, max_new_tokens: int = 256, timeout_s: float = 180.0,
+                        sampling=None) -> Iterator[str]:
+        """Text deltas as tokens are generated (the scheduler's per-token callback feeds a queue).  The deltas
+        concatenate to :meth:`generate`'s text: each one is the growth of the decoded text, held back while it ends
+        in an incomplete UTF-8 sequence.  A caller that stops early, or a wait longer than ``timeout_s``, cancels
+        the request."""
+        ids = self.encode_prompt(prompt_text)
+        limit = self.engine.max_blocks * self.engine.block_size
+        ids = list(ids)[-max(1, limit - 1):]
+        n = max(1, min(int(max_new_tokens), limit - len(ids)))
+        q: "queue.Queue" = queue.Queue()
+        r = self.scheduler.submit(ids, n, on_token=q.put, sampling=sampling)
+        r.future.add_done_callback(lambda f: q.put(None))
+        toks: List[int] = []
+        sent = ""
+        deadline = time.monotonic() + float(timeout_s)
+        try:
+            while True:
+                left = deadline - time.monotonic()
+                if left <= 0:
+                    raise TimeoutError(f"generation exceeded {timeout_s} s")
+                try:
+                    t = q.get(timeout=left)
+                except queue.Empty:
+                    raise TimeoutError(f"generation exceeded {timeout_s} s")
+                if t is None:
+                    break
+                toks.append(int(t))
+                text = self.tokenizer.decode(toks, skip_special_tokens=True)
+                if text.endswith("\ufffd"):
+                    continue                      # an incomplete multi-byte character: wait for the rest
+                if len(text) > len(sent) and text.startswith(sent):
+                    yield text[len(sent):]
+                    sent = text
+            r.future.result()                     # raises the request's error, if any
+            text = self.tokenizer.decode(r.future.result(), skip_special_tokens=True)
+            if text != sent and text.startswith(sent):
+                yield text[len(sent):]
+        finally:
+            if not r.future.done():
+                self.scheduler.cancel(r)
 
     def is_running(self) -> bool:
         return self.scheduler.alive()

@@ -144,6 +144,7 @@ def create_app(state: ServiceState):
         temperature: Optional[float] = None   # absent or 0: greedy (the default)
         top_k: Optional[int] = None
         seed: Optional[int] = None
+        stream: Optional[bool] = None         # server-sent events: text deltas, then the full payload
 
     def sem() -> asyncio.Semaphore:
         if state.sem is None:
@@ -218,10 +219,24 @@ def create_app(state: ServiceState):
                                      "prompt_template": template}}
                 if show or state.expose_sources:
                     payload["sources"] = []
+                if req.stream:
+                    return _sse_response(iter(()), payload)
                 return JSONResponse(payload)
             max_new = int(req.max_new_tokens) if req.max_new_tokens is not None else state.max_new_tokens
             if state.backend is None:
                 raise HTTPException(status_code=500, detail="generation backend not initialized")
+        base = {"ok": True, "source_count": len(sources), "mode": mode, "hrm_active": hrm_active,
+                "audit": {"mode_resolved": mode, "hrm_called": bool(hrm_active),
+                          "source_injected_count": len(sources), "prompt_template": template}}
+        if (show or state.expose_sources) and mode != "deepseek_only":
+            base["sources"] = [{"sid": s.sid, "txt": s.txt} for s in sources]
+        if req.stream:
+            kw = {} if sampling is None else {"sampling": sampling}
+            try:
+                pieces = state.backend.generate_stream(prompt_text, max_new, state.request_timeout_s, **kw)
+            except AttributeError:
+                raise HTTPException(status_code=400, detail="this backend does not stream")
+            return _sse_response(pieces, base)
         # generation runs outside the admission semaphore's prompt-build section: the engine batches requests
         try:
             if sampling is None:
@@ -231,12 +246,42 @@ def create_app(state: ServiceState):
                                                sampling=sampling)
         except Exception as e:
             raise HTTPException(status_code=500, detail=str(e))
-        payload = {"ok": True, "text": text, "source_count": len(sources), "mode": mode, "hrm_active": hrm_active,
-                   "audit": {"mode_resolved": mode, "hrm_called": bool(hrm_active),
-                             "source_injected_count": len(sources), "prompt_template": template}}
-        if (show or state.expose_sources) and mode != "deepseek_only":
-            payload["sources"] = [{"sid": s.sid, "txt": s.txt} for s in sources]
+        payload = {"ok": True, "text": text}
+        payload.update((k, v) for k, v in base.items() if k != "ok")
         return JSONResponse(payload)
+
+    def _sse_response(pieces, payload):
+        """``data: {"delta": ...}`` per text piece, then the full payload (with ``text``), then ``[DONE]``; a
+        generation error ends the stream with ``{"ok": false, "error": ...}``.  A client that goes away closes the
+        piece iterator, which cancels the request."""
+        from fastapi.responses import StreamingResponse
+        import json as _json
+        it = iter(pieces)
+
+        async def events():
+            parts = []
+            try:
+                while True:
+                    piece = await asyncio.to_thread(next, it, None)
+                    if piece is None:
+                        break
+                    parts.append(piece)
+                    yield f"data: {_json.dumps({'delta': piece})}\n\n"
+                out = dict(payload)
+                out.setdefault("text", "".join(parts))
+                yield f"data: {_json.dumps(out)}\n\n"
+            except Exception as e:
+                yield f"data: {_json.dumps({'ok': False, 'error': str(e)})}\n\n"
+            finally:
+                close = getattr(it, "close", None)
+                if close is not None:
+                    try:
+                        close()
+                    except ValueError:   # a next() still running in its thread: the request ends on its own
+                        pass
+            yield "data: [DONE]\n\n"
+
+        return StreamingResponse(events(), media_type="text/event-stream")
 
     @app.on_event("shutdown")
     def _shutdown():

@@ -269,3 +269,53 @@ def test_cli_generate_greedy_and_sampled_on_cpu(capsys):
     assert outs[0] == outs[1] and outs[2] == outs[3]
     with pytest.raises(SystemExit):
         cli.main(base + ["--temperature", "-1"])
+
+
+def _sse_events(url, payload):
+    import urllib.request
+    req = urllib.request.Request(url, data=json.dumps(payload).encode(), headers={"Content-Type": "application/json"})
+    out = []
+    with urllib.request.urlopen(req, timeout=120) as r:
+        for line in r:
+            line = line.decode().strip()
+            if line.startswith("data: "):
+                out.append(line[6:])
+    return out
+
+
+def test_lane_streams_deltas_then_the_payload(hrm_model):
+    """``stream: true`` on /v1/generate: server-sent text deltas that concatenate to the text of the same request
+    without streaming, then the full payload, then [DONE]."""
+    be = EchoBackend()
+    st = _state(hrm_model, be)
+    with LiveServer(create_app(st)) as srv:
+        body = {"prompt": "who guards the silver bridge", "mode": "retrieval"}
+        code, plain = post(srv.url + "/v1/generate", body)
+        plain = json.loads(plain)
+        ev = _sse_events(srv.url + "/v1/generate", dict(body, stream=True))
+    assert ev[-1] == "[DONE]"
+    final = json.loads(ev[-2])
+    deltas = [json.loads(e)["delta"] for e in ev[:-2]]
+    assert len(deltas) > 1 and "".join(deltas) == final["text"] == plain["text"]
+    assert final == plain
+
+
+def test_engine_backend_stream_matches_generate_on_cpu():
+    from hrm_flashrenderer_b200.runtime.sampling import SamplingParams
+    from hrm_flashrenderer_b200.serving.backend import EngineBackend
+    be = EngineBackend("synthetic:tiny", device="cpu", max_seq_len=128, max_batch=2)
+    try:
+        for sp in (None, SamplingParams(0.9, 30, 4)):
+            full = be.generate("hello there", 10, sampling=sp)
+            parts = list(be.generate_stream("hello there", 10, sampling=sp))
+            assert "".join(parts) == full and len(parts) >= 2
+        it = be.generate_stream("stop early", 100)
+        next(it)
+        it.close()                                   # the consumer went away: the request is cancelled
+        import time
+        t0 = time.time()
+        while be.metrics()["cancelled"] < 1 and time.time() - t0 < 30:
+            time.sleep(0.01)
+        assert be.metrics()["cancelled"] == 1
+    finally:
+        be.stop()
