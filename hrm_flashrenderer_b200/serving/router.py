@@ -19,11 +19,12 @@ import contextlib
 import json
 import os
 import sys
+import threading
 import time
 import urllib.error
 import urllib.request
 from dataclasses import dataclass
-from typing import Any, Dict, List, Optional, Tuple
+from typing import Any, Dict, Iterator, List, Optional, Tuple
 
 from .prompt_builder import SUPPORTED_MODES, normalize_mode
 
@@ -71,6 +72,7 @@ class RouterState:
         self.keepalive_s = 5.0
         self.model_id = DEFAULT_MODEL_ID
         self.post = http_json_post    # injectable transport (tests)
+        self.post_stream = http_sse_post
         self.get = http_json_get
         # routing counters (GET /metrics)
         self.requests_total = 0
@@ -116,6 +118,39 @@ def _lane_call(method: str, url: str, payload: Optional[Dict[str, Any]], timeout
     if not isinstance(obj, dict):
         raise LaneCallError(url, f"answer is a JSON {type(obj).__name__}, expected an object")
     return obj, elapsed_ms
+
+
+def http_sse_post(url: str, payload: Dict[str, Any], timeout_s: float) -> Iterator[Dict[str, Any]]:
+    """POST to a lane's streaming endpoint and yield the JSON object of every ``data:`` event as it arrives (until
+    ``[DONE]``).  Failures before or during the stream are LaneCallErrors."""
+    body = json.dumps(payload).encode("utf-8")
+    req = urllib.request.Request(url, data=body, method="POST", headers={"Content-Type": "application/json"})
+    try:
+        resp = urllib.request.urlopen(req, timeout=timeout_s)
+    except urllib.error.HTTPError as e:
+        why = ""
+        with contextlib.suppress(Exception):
+            why = e.read().decode("utf-8", errors="replace").strip()
+        raise LaneCallError(url, f"status {e.code}" + (f" ({why})" if why else ""), status=e.code) from e
+    except (OSError, ValueError) as e:
+        raise LaneCallError(url, f"no answer: {type(e).__name__}: {e}") from e
+    with resp:
+        try:
+            for raw in resp:
+                line = raw.decode("utf-8", errors="replace").strip()
+                if not line.startswith("data:"):
+                    continue            # keepalive comments and blank separators
+                data = line[5:].strip()
+                if data == "[DONE]":
+                    return
+                try:
+                    obj = json.loads(data)
+                except json.JSONDecodeError as e:
+                    raise LaneCallError(url, f"stream event is not JSON: {data[:80]!r}") from e
+                if isinstance(obj, dict):
+                    yield obj
+        except OSError as e:
+            raise LaneCallError(url, f"stream broken: {type(e).__name__}: {e}") from e
 
 
 def http_json_get(url: str, timeout_s: float) -> Tuple[Dict[str, Any], int]:
@@ -288,37 +323,95 @@ def create_app(st: RouterState):
         c, _ = estimate_prompt_tokens(st, text)
         return {"prompt_tokens": p, "completion_tokens": c, "total_tokens": p + c}
 
-    async def stream(task: "asyncio.Task", model: str, prompt: str, chat: bool):
-        while not task.done():
-            yield ": keepalive\n\n"
-            try:
-                await asyncio.wait_for(asyncio.shield(task), timeout=st.keepalive_s)
-            except asyncio.TimeoutError:
-                pass
-            except Exception:
-                break
-        try:
-            result = await task
-        except HTTPException as e:
-            yield f"data: {json.dumps({'error': e.detail})}\n\n"
-            yield "data: [DONE]\n\n"
-            return
-        text = str(result.get("text") or "")
+    def chunk(cid: str, model: str, chat: bool, piece: Optional[str], finish: Optional[str] = None,
+              extra: Optional[Dict[str, Any]] = None, role: bool = False) -> str:
         now = int(time.time())
         if chat:
-            cid = f"chatcmpl-{int(time.time() * 1000)}"
-            first = {"id": cid, "object": "chat.completion.chunk", "created": now, "model": model,
-                     "choices": [{"index": 0, "delta": {"content": text}, "finish_reason": None}]}
-            done = {"id": cid, "object": "chat.completion.chunk", "created": now, "model": model,
-                    "choices": [{"index": 0, "delta": {}, "finish_reason": "stop"}], "usage": usage(prompt, text)}
+            delta = {"role": "assistant"} if role else ({} if piece is None else {"content": piece})
+            choice = {"index": 0, "delta": delta, "finish_reason": finish}
+            obj = {"id": cid, "object": "chat.completion.chunk", "created": now, "model": model, "choices": [choice]}
         else:
-            cid = f"cmpl-{int(time.time() * 1000)}"
-            first = {"id": cid, "object": "text_completion", "created": now, "model": model,
-                     "choices": [{"index": 0, "text": text, "finish_reason": None}]}
-            done = {"id": cid, "object": "text_completion", "created": now, "model": model,
-                    "choices": [{"index": 0, "text": "", "finish_reason": "stop"}], "usage": usage(prompt, text)}
-        yield f"data: {json.dumps(first)}\n\n"
-        yield f"data: {json.dumps(done)}\n\n"
+            choice = {"index": 0, "text": piece or "", "finish_reason": finish}
+            obj = {"id": cid, "object": "text_completion", "created": now, "model": model, "choices": [choice]}
+        if extra:
+            obj.update(extra)
+        return f"data: {json.dumps(obj)}\n\n"
+
+    async def relay(req: GenerateReq, model: str, prompt: str, chat: bool):
+        """OpenAI streaming: the selected lane streams text deltas, relayed as chunks while it generates.  A lane
+        that fails before its first delta is replaced by the next candidate (as for non-streaming requests);
+        after that, an error ends the stream with an error event.  Comment lines keep the connection alive while a
+        lane is silent."""
+        cid = f"{'chatcmpl' if chat else 'cmpl'}-{int(time.time() * 1000)}"
+        try:
+            mode = normalize_mode(req.mode if req.mode is not None else st.default_mode)
+        except ValueError as e:
+            yield f"data: {json.dumps({'error': str(e)})}\n\n"
+            yield "data: [DONE]\n\n"
+            return
+        st.requests_total += 1
+        req_new = max(1, min(4096, int(req.max_new_tokens) if req.max_new_tokens is not None else 256))
+        ptoks, _ = estimate_prompt_tokens(st, prompt)
+        primary = primary_backend(st, ptoks, req_new, req.route_hint, req.prefer_backend)
+        attempted, errors = [], []
+        loop = asyncio.get_running_loop()
+        for lane in candidate_order(st, primary, bool(req.allow_failover)):
+            be = st.backends[lane]
+            attempted.append(lane)
+            lane_req = {"prompt": prompt, "max_new_tokens": min(req_new, max_new_limit(st, lane)), "mode": mode,
+                        "show_sources": resolve_show_sources(req.show_sources, mode), "stream": True}
+            lane_req.update({k: v for k, v in (("temperature", req.temperature), ("top_k", req.top_k),
+                                               ("seed", req.seed)) if v is not None})
+            q: "asyncio.Queue" = asyncio.Queue()
+
+            def pump(url=be.base_url + "/v1/generate", payload=lane_req):
+                try:
+                    for ev in st.post_stream(url, payload, st.request_timeout_s):
+                        loop.call_soon_threadsafe(q.put_nowait, ("ev", ev))
+                    loop.call_soon_threadsafe(q.put_nowait, ("end", None))
+                except Exception as e:   # handed to the event loop
+                    loop.call_soon_threadsafe(q.put_nowait, ("err", e))
+
+            threading.Thread(target=pump, daemon=True).start()
+            started, text = False, []
+            while True:
+                try:
+                    kind, ev = await asyncio.wait_for(q.get(), timeout=st.keepalive_s)
+                except asyncio.TimeoutError:
+                    yield ": keepalive\n\n"
+                    continue
+                failed = kind == "err" or (kind == "ev" and ev.get("ok") is False) or (kind == "end" and not started)
+                if failed:
+                    why = ev if kind == "err" else (ev or {}).get("error", "stream ended without an answer")
+                    st.lane_errors[lane] = st.lane_errors.get(lane, 0) + 1
+                    if not started:
+                        errors.append(f"{lane}: {why}")
+                        break                                  # next candidate lane
+                    yield f"data: {json.dumps({'error': str(why)})}\n\n"
+                    yield "data: [DONE]\n\n"
+                    return
+                if kind == "end":
+                    ev = {"text": "".join(text)}
+                if "delta" in ev:
+                    if not started and chat:
+                        yield chunk(cid, model, chat, None, role=True)
+                    started = True
+                    text.append(str(ev["delta"]))
+                    yield chunk(cid, model, chat, str(ev["delta"]))
+                    continue
+                # the final payload: close the stream
+                full = str(ev.get("text", "".join(text)))
+                if not started and full:
+                    yield chunk(cid, model, chat, full)
+                st.routed[lane] = st.routed.get(lane, 0) + 1
+                if lane != primary:
+                    st.failovers_total += 1
+                yield chunk(cid, model, chat, None, "stop", {"usage": usage(prompt, full)})
+                yield "data: [DONE]\n\n"
+                return
+        st.all_failed_total += 1
+        detail = {"error": "all backends failed", "primary": primary, "attempted": attempted, "backend_errors": errors}
+        yield f"data: {json.dumps({'error': detail})}\n\n"
         yield "data: [DONE]\n\n"
 
     def check(lane: str) -> Dict[str, Any]:
@@ -383,8 +476,7 @@ def create_app(st: RouterState):
                           route_hint=body.get("route_hint"), prefer_backend=body.get("prefer_backend"),
                           temperature=body.get("temperature"), top_k=body.get("top_k"), seed=body.get("seed"))
         if bool(body.get("stream")):
-            task = asyncio.create_task(run_generate(req))
-            return StreamingResponse(stream(task, model, prompt, chat), media_type="text/event-stream")
+            return StreamingResponse(relay(req, model, prompt, chat), media_type="text/event-stream")
         result = await run_generate(req)
         text = str(result.get("text") or "")
         if chat:

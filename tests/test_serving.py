@@ -148,11 +148,23 @@ def test_sampling_fields_reach_the_backend(hrm_model):
 
 
 # ---------------------------------------------------------------------------------------------- router
+def _stream_from(post_fn):
+    """A lane's streaming answer built from a fake non-streaming one: two deltas, then the payload."""
+    def post_stream(url, payload, timeout):
+        body, _ = post_fn(url, dict(payload, stream=False), timeout)
+        text = str(body.get("text", ""))
+        yield {"delta": text[:1]}
+        yield {"delta": text[1:]}
+        yield body
+    return post_stream
+
+
 def _router(post_fn, endpoints=None):
     st = rt.RouterState()
     endpoints = endpoints or {"solo_22gb": "http://a", "nvlink_pair": "http://b", "solo_3080": "http://c"}
     st.backends = {n: rt.Backend(n, u) for n, u in endpoints.items()}
     st.post = post_fn
+    st.post_stream = _stream_from(post_fn) if post_fn is not None else None
     st.get = lambda url, t: ({"ok": not url.startswith("http://c")}, 1)
     st.keepalive_s = 0.05
     return st
@@ -319,3 +331,29 @@ def test_engine_backend_stream_matches_generate_on_cpu():
         assert be.metrics()["cancelled"] == 1
     finally:
         be.stop()
+
+
+def test_router_relays_lane_stream_with_failover_before_first_delta(hrm_model):
+    """OpenAI streaming through the router over real HTTP: the primary lane is down, the next lane (a live lane
+    service) streams its deltas, which arrive as chat chunks that concatenate to the lane's non-streamed text."""
+    lane_state = _state(hrm_model, EchoBackend())
+    with LiveServer(create_app(lane_state)) as lane:
+        st = rt.RouterState()
+        st.backends = {"solo_3080": rt.Backend("solo_3080", "http://127.0.0.1:9"),      # nothing listens there
+                       "nvlink_pair": rt.Backend("nvlink_pair", lane.url),
+                       "solo_22gb": rt.Backend("solo_22gb", "http://127.0.0.1:7")}
+        st.keepalive_s = 0.05
+        with LiveServer(rt.create_app(st)) as router:
+            ev = _sse_events(router.url + "/v1/chat/completions",
+                             {"messages": [{"role": "user", "content": "hello lane"}], "stream": True,
+                              "max_tokens": 50})                      # short request: the primary is solo_3080
+            code, plain = post(lane.url + "/v1/generate", {"prompt": "hello lane", "mode": "deepseek_only",
+                                                           "max_new_tokens": 50})
+    assert ev[-1] == "[DONE]"
+    chunks = [json.loads(e) for e in ev[:-1]]
+    assert chunks[0]["choices"][0]["delta"] == {"role": "assistant"}
+    content = "".join(c["choices"][0]["delta"].get("content", "") for c in chunks)
+    assert content == json.loads(plain)["text"]
+    assert sum(1 for c in chunks if c["choices"][0]["delta"].get("content")) > 1      # really streamed in pieces
+    assert chunks[-1]["choices"][0]["finish_reason"] == "stop" and chunks[-1]["usage"]["completion_tokens"] > 0
+    assert st.failovers_total == 1 and st.lane_errors["solo_3080"] == 1
