@@ -61,10 +61,12 @@ class EchoBackend:
         return f"answer-{h}"[: max(1, max_new_tokens * 4)]
 
     def generate_stream(self, prompt_text: str, max_new_tokens: int = 64, timeout_s: float = 180.0,
-                        sampling=None) -> Iterator[str]:
-        """The same answer in 4-character pieces."""
+                        sampling=None, cancel=None) -> Iterator[str]:
+        """The same answer in 4-character pieces (stops early once ``cancel`` is set)."""
         text = self.generate(prompt_text, max_new_tokens, timeout_s, sampling)
         for i in range(0, len(text), 4):
+            if cancel is not None and cancel.is_set():
+                return
             yield text[i:i + 4]
 
     def is_running(self) -> bool:
@@ -139,11 +141,12 @@ class EngineBackend:
         return self.tokenizer.decode(out, skip_special_tokens=True)
 
     def generate_stream(self, prompt_text: str, max_new_tokens: int = 256, timeout_s: float = 180.0,
-                        sampling=None) -> Iterator[str]:
+                        sampling=None, cancel=None) -> Iterator[str]:
         """Text deltas as tokens are generated (the scheduler's per-token callback feeds a queue).  The deltas
         concatenate to :meth:`generate`'s text: each one is the growth of the decoded text, held back while it ends
-        in an incomplete UTF-8 sequence.  A caller that stops early, or a wait longer than ``timeout_s``, cancels
-        the request."""
+        in an incomplete UTF-8 sequence.  A caller that stops early (closes the iterator, or sets the
+        ``threading.Event`` ``cancel``, which is checked between tokens), or a wait longer than ``timeout_s``,
+        cancels the request."""
         ids = self.encode_prompt(prompt_text)
         limit = self.engine.max_blocks * self.engine.block_size
         ids = list(ids)[-max(1, limit - 1):]
@@ -156,13 +159,15 @@ class EngineBackend:
         deadline = time.monotonic() + float(timeout_s)
         try:
             while True:
+                if cancel is not None and cancel.is_set():
+                    return
                 left = deadline - time.monotonic()
                 if left <= 0:
                     raise TimeoutError(f"generation exceeded {timeout_s} s")
                 try:
-                    t = q.get(timeout=left)
+                    t = q.get(timeout=min(left, 0.05))
                 except queue.Empty:
-                    raise TimeoutError(f"generation exceeded {timeout_s} s")
+                    continue                      # re-check the cancel flag and the deadline
                 if t is None:
                     break
                 toks.append(int(t))

@@ -341,7 +341,8 @@ def create_app(st: RouterState):
         """OpenAI streaming: the selected lane streams text deltas, relayed as chunks while it generates.  A lane
         that fails before its first delta is replaced by the next candidate (as for non-streaming requests);
         after that, an error ends the stream with an error event.  Comment lines keep the connection alive while a
-        lane is silent."""
+        lane is silent.  When the client goes away, the lane connection is closed, which cancels the request on
+        the lane."""
         cid = f"{'chatcmpl' if chat else 'cmpl'}-{int(time.time() * 1000)}"
         try:
             mode = normalize_mode(req.mode if req.mode is not None else st.default_mode)
@@ -363,52 +364,65 @@ def create_app(st: RouterState):
             lane_req.update({k: v for k, v in (("temperature", req.temperature), ("top_k", req.top_k),
                                                ("seed", req.seed)) if v is not None})
             q: "asyncio.Queue" = asyncio.Queue()
+            gone = threading.Event()   # set when this relay stops reading: the pump then drops the lane stream
 
-            def pump(url=be.base_url + "/v1/generate", payload=lane_req):
+            def pump(url=be.base_url + "/v1/generate", payload=lane_req, gone=gone, q=q):
+                events = None
                 try:
-                    for ev in st.post_stream(url, payload, st.request_timeout_s):
+                    events = st.post_stream(url, payload, st.request_timeout_s)
+                    for ev in events:
+                        if gone.is_set():
+                            return
                         loop.call_soon_threadsafe(q.put_nowait, ("ev", ev))
                     loop.call_soon_threadsafe(q.put_nowait, ("end", None))
                 except Exception as e:   # handed to the event loop
-                    loop.call_soon_threadsafe(q.put_nowait, ("err", e))
+                    if not gone.is_set():
+                        loop.call_soon_threadsafe(q.put_nowait, ("err", e))
+                finally:
+                    close = getattr(events, "close", None)
+                    if close is not None:
+                        close()          # closes the lane connection; the lane then cancels the request
 
             threading.Thread(target=pump, daemon=True).start()
             started, text = False, []
-            while True:
-                try:
-                    kind, ev = await asyncio.wait_for(q.get(), timeout=st.keepalive_s)
-                except asyncio.TimeoutError:
-                    yield ": keepalive\n\n"
-                    continue
-                failed = kind == "err" or (kind == "ev" and ev.get("ok") is False) or (kind == "end" and not started)
-                if failed:
-                    why = ev if kind == "err" else (ev or {}).get("error", "stream ended without an answer")
-                    st.lane_errors[lane] = st.lane_errors.get(lane, 0) + 1
-                    if not started:
-                        errors.append(f"{lane}: {why}")
-                        break                                  # next candidate lane
-                    yield f"data: {json.dumps({'error': str(why)})}\n\n"
+            try:
+                while True:
+                    try:
+                        kind, ev = await asyncio.wait_for(q.get(), timeout=st.keepalive_s)
+                    except asyncio.TimeoutError:
+                        yield ": keepalive\n\n"
+                        continue
+                    failed = (kind == "err" or (kind == "ev" and ev.get("ok") is False)
+                              or (kind == "end" and not started))
+                    if failed:
+                        why = ev if kind == "err" else (ev or {}).get("error", "stream ended without an answer")
+                        st.lane_errors[lane] = st.lane_errors.get(lane, 0) + 1
+                        if not started:
+                            errors.append(f"{lane}: {why}")
+                            break                              # next candidate lane
+                        yield f"data: {json.dumps({'error': str(why)})}\n\n"
+                        yield "data: [DONE]\n\n"
+                        return
+                    if kind == "end":
+                        ev = {"text": "".join(text)}
+                    if "delta" in ev:
+                        if not started and chat:
+                            yield chunk(cid, model, chat, None, role=True)
+                        started = True
+                        text.append(str(ev["delta"]))
+                        yield chunk(cid, model, chat, str(ev["delta"]))
+                        continue
+                    full = str(ev.get("text", "".join(text)))   # the final payload closes the stream
+                    if not started and full:
+                        yield chunk(cid, model, chat, full)
+                    st.routed[lane] = st.routed.get(lane, 0) + 1
+                    if lane != primary:
+                        st.failovers_total += 1
+                    yield chunk(cid, model, chat, None, "stop", {"usage": usage(prompt, full)})
                     yield "data: [DONE]\n\n"
                     return
-                if kind == "end":
-                    ev = {"text": "".join(text)}
-                if "delta" in ev:
-                    if not started and chat:
-                        yield chunk(cid, model, chat, None, role=True)
-                    started = True
-                    text.append(str(ev["delta"]))
-                    yield chunk(cid, model, chat, str(ev["delta"]))
-                    continue
-                # the final payload: close the stream
-                full = str(ev.get("text", "".join(text)))
-                if not started and full:
-                    yield chunk(cid, model, chat, full)
-                st.routed[lane] = st.routed.get(lane, 0) + 1
-                if lane != primary:
-                    st.failovers_total += 1
-                yield chunk(cid, model, chat, None, "stop", {"usage": usage(prompt, full)})
-                yield "data: [DONE]\n\n"
-                return
+            finally:
+                gone.set()
         st.all_failed_total += 1
         detail = {"error": "all backends failed", "primary": primary, "attempted": attempted, "backend_errors": errors}
         yield f"data: {json.dumps({'error': detail})}\n\n"

@@ -18,6 +18,7 @@ busy; generation goes to the continuous-batching engine, so ``--max_concurrent``
 import argparse
 import asyncio
 import os
+import time
 from pathlib import Path
 from typing import Any, List, Optional, Tuple
 
@@ -231,12 +232,14 @@ def create_app(state: ServiceState):
         if (show or state.expose_sources) and mode != "deepseek_only":
             base["sources"] = [{"sid": s.sid, "txt": s.txt} for s in sources]
         if req.stream:
-            kw = {} if sampling is None else {"sampling": sampling}
+            import threading
+            stop = threading.Event()
+            kw = {"cancel": stop} if sampling is None else {"cancel": stop, "sampling": sampling}
             try:
                 pieces = state.backend.generate_stream(prompt_text, max_new, state.request_timeout_s, **kw)
             except AttributeError:
                 raise HTTPException(status_code=400, detail="this backend does not stream")
-            return _sse_response(pieces, base)
+            return _sse_response(pieces, base, stop, request)
         # generation runs outside the admission semaphore's prompt-build section: the engine batches requests
         try:
             if sampling is None:
@@ -250,7 +253,7 @@ def create_app(state: ServiceState):
         payload.update((k, v) for k, v in base.items() if k != "ok")
         return JSONResponse(payload)
 
-    def _sse_response(pieces, payload):
+    def _sse_response(pieces, payload, stop=None, request=None):
         """``data: {"delta": ...}`` per text piece, then the full payload (with ``text``), then ``[DONE]``; a
         generation error ends the stream with ``{"ok": false, "error": ...}``.  A client that goes away closes the
         piece iterator, which cancels the request."""
@@ -267,18 +270,35 @@ def create_app(state: ServiceState):
                         break
                     parts.append(piece)
                     yield f"data: {_json.dumps({'delta': piece})}\n\n"
+                    # the server does not close this generator when the client leaves (its next write just fails),
+                    # so look for the disconnect between pieces
+                    if request is not None and await request.is_disconnected():
+                        return
                 out = dict(payload)
                 out.setdefault("text", "".join(parts))
                 yield f"data: {_json.dumps(out)}\n\n"
             except Exception as e:
                 yield f"data: {_json.dumps({'ok': False, 'error': str(e)})}\n\n"
             finally:
+                if stop is not None:
+                    stop.set()           # the piece iterator sees it between tokens and cancels the request
                 close = getattr(it, "close", None)
                 if close is not None:
                     try:
                         close()
-                    except ValueError:   # a next() still running in its thread: the request ends on its own
-                        pass
+                    except ValueError:
+                        # a next() is still running in its worker thread: close the iterator as soon as it
+                        # returns (its cleanup cancels the engine request)
+                        import threading
+
+                        def close_later():
+                            for _ in range(2000):
+                                try:
+                                    close()
+                                    return
+                                except ValueError:
+                                    time.sleep(0.01)
+                        threading.Thread(target=close_later, daemon=True).start()
             yield "data: [DONE]\n\n"
 
         return StreamingResponse(events(), media_type="text/event-stream")

@@ -357,3 +357,39 @@ def test_router_relays_lane_stream_with_failover_before_first_delta(hrm_model):
     assert sum(1 for c in chunks if c["choices"][0]["delta"].get("content")) > 1      # really streamed in pieces
     assert chunks[-1]["choices"][0]["finish_reason"] == "stop" and chunks[-1]["usage"]["completion_tokens"] > 0
     assert st.failovers_total == 1 and st.lane_errors["solo_3080"] == 1
+
+
+def test_lane_stream_client_disconnect_cancels_the_request(hrm_model):
+    """A streaming client that closes its connection after the first delta: the lane's engine request is cancelled
+    (KV blocks and the batch slot given back) instead of generating to the end."""
+    import http.client
+    import time
+    from hrm_flashrenderer_b200.serving.backend import EngineBackend
+    be = EngineBackend("synthetic:tiny", device="cpu", max_seq_len=512, max_batch=2)
+    step = be.engine.decode_step
+
+    def slow_step(g):                                  # 400 steps take seconds: time to notice the disconnect
+        time.sleep(0.01)
+        return step(g)
+    be.engine.decode_step = slow_step
+    st = _state(hrm_model, be)
+    try:
+        with LiveServer(create_app(st)) as srv:
+            conn = http.client.HTTPConnection("127.0.0.1", srv.port, timeout=60)
+            conn.request("POST", "/v1/generate", body=json.dumps({"prompt": "tell me", "mode": "deepseek_only",
+                                                                  "max_new_tokens": 400, "stream": True}),
+                         headers={"Content-Type": "application/json"})
+            resp = conn.getresponse()
+            while True:
+                line = resp.fp.readline().decode()
+                if line.startswith("data: ") and "delta" in line:
+                    break
+            conn.close()
+            t0 = time.time()
+            while be.metrics()["cancelled"] < 1 and time.time() - t0 < 60:
+                time.sleep(0.05)
+            m = be.metrics()
+            assert m["cancelled"] == 1 and m["batch_size"] == 0, m
+            assert m["generated_tokens"] < 400
+    finally:
+        be.stop()
