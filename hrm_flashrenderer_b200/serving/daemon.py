@@ -95,7 +95,7 @@ class LaneArgs:
     heartbeat_timeout_s: float = 30.0   # a TP peer silent this long is treated as lost
     packed_cache_dir: str = ""           # per-rank packed-shard cache for DSI8 exports (default: HRM_PACKED_CACHE)
     fused_collectives: bool = True       # TP > 1 on CUDA: in-kernel NVLink all-reduce / argmax (False: NCCL calls)
-    prefix_cache: bool = False           # share the KV blocks of prompt prefixes seen before (shared system prompts)
+    prefix_cache: bool = True            # share the KV blocks of prompt prefixes seen before (shared system prompts)
 
 
 def build_engine(a: LaneArgs, rank: int, world: int, comm):
@@ -338,7 +338,8 @@ def main(argv=None):
     ap.add_argument("--num_kv_blocks", type=int, default=0)
     ap.add_argument("--nccl_collectives", action="store_true",
                     help="TP all-reduce and argmax through NCCL calls instead of the fused peer-memory kernels")
-    ap.add_argument("--prefix_cache", action="store_true", help="share KV blocks of prompt prefixes seen before")
+    ap.add_argument("--no_prefix_cache", dest="prefix_cache", action="store_false",
+                    help="recompute every prompt (default: share KV blocks of prompt prefixes seen before)")
     args = ap.parse_args(argv)
     lane = LaneArgs(args.model, args.world, args.max_seq_len, args.prefill_chunk_size, args.max_batch, args.device,
                     master_port=args.master_port, num_kv_blocks=args.num_kv_blocks,

@@ -340,8 +340,9 @@ def build_arg_parser() -> argparse.ArgumentParser:
     ap.add_argument("--max_prompt_tokens", type=int, default=int(os.environ.get("DSI8_MAX_PROMPT_TOKENS", "2048")))
     ap.add_argument("--native_request_timeout_s", type=float, default=180.0)
     ap.add_argument("--device", default="cuda:0")
-    ap.add_argument("--prefix_cache", action="store_true",
-                    help="share the KV blocks of prompt prefixes seen before (the system prompt, repeated context)")
+    ap.add_argument("--no_prefix_cache", dest="prefix_cache", action="store_false",
+                    help="recompute every prompt (default: share the KV blocks of prompt prefixes seen before, such as "
+                         "the system prompt)")
     ap.add_argument("--nccl_collectives", action="store_true",
                     help="TP lane: all-reduce and argmax through NCCL calls instead of the fused peer-memory kernels")
     return ap

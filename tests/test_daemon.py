@@ -80,8 +80,7 @@ def test_daemon_world2_prefix_cache(tmp_path):
     env = dict(os.environ, OMP_NUM_THREADS="2")
     p = subprocess.Popen([sys.executable, "-m", "hrm_flashrenderer_b200.serving.daemon", "--model", "synthetic:tiny",
                           "--world", "2", "--device", "cpu", "--max_seq_len", "512", "--max_batch", "8",
-                          "--ready_file", str(ready), "--master_port", str(free_port()), "--num_kv_blocks", "256",
-                          "--prefix_cache"],
+                          "--ready_file", str(ready), "--master_port", str(free_port()), "--num_kv_blocks", "256"],
                          cwd=ROOT, env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT)
     try:
         t0 = time.time()
