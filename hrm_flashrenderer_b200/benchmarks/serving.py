@@ -126,9 +126,13 @@ def run_trace(scheduler, trace, time_scale: float = 1.0) -> Dict:
     wall = time.perf_counter() - t0
     ttft = [r.ttft_s for r in reqs]
     gen = sum(len(r.tokens) for r in reqs)
+    m = scheduler.metrics()
     return {"requests": len(reqs), "wall_s": round(wall, 3), "generated_tokens": gen,
             "tok_s": round(gen / wall, 2), "ttft_p50_ms": round(_pct(ttft, 0.5) * 1e3, 2),
-            "ttft_p99_ms": round(_pct(ttft, 0.99) * 1e3, 2)}
+            "ttft_p99_ms": round(_pct(ttft, 0.99) * 1e3, 2),
+            "prompt_tokens": sum(len(ids) for _, ids, _ in trace),
+            "prefilled_tokens": sum(scheduler.prefill_calls),
+            "prefix_cache_hit_blocks": m.get("prefix_cache_hit_blocks", 0)}
 
 
 def main(argv=None) -> int:

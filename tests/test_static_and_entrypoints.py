@@ -77,16 +77,26 @@ def test_trace_replay_on_cpu_engine():
     from hrm_flashrenderer_b200.models.weights import synth_weights
     from hrm_flashrenderer_b200.runtime.engine import InferenceEngine
     from hrm_flashrenderer_b200.runtime.scheduler import Scheduler
-    trace = [(t, ids[:40], 4) for t, ids, _ in make_trace(n=6, rate=50.0, vocab=TINY.vocab, seed=3)]
+    # the trace's shared system prompt (first 32 tokens) plus the start of each request's own context
+    trace = [(t, ids[:32] + ids[256:264], 4) for t, ids, _ in make_trace(n=6, rate=50.0, vocab=TINY.vocab, seed=3)]
     model = LlamaW8.from_weights(TINY, synth_weights(TINY, seed=0), device="cpu", max_pos=128)
-    eng = InferenceEngine(model, EngineConfig(max_seq_len=96, max_batch=4, use_cuda_graphs=False), num_blocks=64)
-    sch = Scheduler(eng)
-    sch.start()
-    try:
-        res = run_trace(sch, trace, time_scale=0.1)
-    finally:
-        sch.stop()
-    assert res["requests"] == 6 and res["generated_tokens"] == 6 * 4 and res["ttft_p50_ms"] > 0
+    results = {}
+    for pc in (False, True):
+        eng = InferenceEngine(model, EngineConfig(max_seq_len=96, max_batch=4, use_cuda_graphs=False,
+                                                  prefix_cache=pc), num_blocks=64)
+        sch = Scheduler(eng)
+        sch.start()
+        try:
+            res = run_trace(sch, trace, time_scale=0.1)
+        finally:
+            sch.stop()
+        assert res["requests"] == 6 and res["generated_tokens"] == 6 * 4 and res["ttft_p50_ms"] > 0
+        assert res["prompt_tokens"] == 6 * 40
+        results[pc] = res
+    assert results[False]["prefilled_tokens"] == 6 * 40 and results[False]["prefix_cache_hit_blocks"] == 0
+    # with the cache, requests that arrive after the first one finished its prompt skip the two shared blocks
+    hits = results[True]["prefix_cache_hit_blocks"]
+    assert hits >= 2 and results[True]["prefilled_tokens"] == 6 * 40 - 16 * hits
 
 
 def test_diag_runs_without_gpu(capsys):
