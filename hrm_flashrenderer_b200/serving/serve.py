@@ -17,7 +17,9 @@ busy; generation goes to the continuous-batching engine, so ``--max_concurrent``
 """
 import argparse
 import asyncio
+import json
 import os
+import threading
 import time
 from pathlib import Path
 from typing import Any, List, Optional, Tuple
@@ -232,7 +234,6 @@ def create_app(state: ServiceState):
         if (show or state.expose_sources) and mode != "deepseek_only":
             base["sources"] = [{"sid": s.sid, "txt": s.txt} for s in sources]
         if req.stream:
-            import threading
             stop = threading.Event()
             kw = {"cancel": stop} if sampling is None else {"cancel": stop, "sampling": sampling}
             try:
@@ -258,7 +259,6 @@ def create_app(state: ServiceState):
         generation error ends the stream with ``{"ok": false, "error": ...}``.  A client that goes away closes the
         piece iterator, which cancels the request."""
         from fastapi.responses import StreamingResponse
-        import json as _json
         it = iter(pieces)
 
         async def events():
@@ -269,16 +269,16 @@ def create_app(state: ServiceState):
                     if piece is None:
                         break
                     parts.append(piece)
-                    yield f"data: {_json.dumps({'delta': piece})}\n\n"
+                    yield f"data: {json.dumps({'delta': piece})}\n\n"
                     # the server does not close this generator when the client leaves (its next write just fails),
                     # so look for the disconnect between pieces
                     if request is not None and await request.is_disconnected():
                         return
                 out = dict(payload)
                 out.setdefault("text", "".join(parts))
-                yield f"data: {_json.dumps(out)}\n\n"
+                yield f"data: {json.dumps(out)}\n\n"
             except Exception as e:
-                yield f"data: {_json.dumps({'ok': False, 'error': str(e)})}\n\n"
+                yield f"data: {json.dumps({'ok': False, 'error': str(e)})}\n\n"
             finally:
                 if stop is not None:
                     stop.set()           # the piece iterator sees it between tokens and cancels the request
@@ -289,8 +289,6 @@ def create_app(state: ServiceState):
                     except ValueError:
                         # a next() is still running in its worker thread: close the iterator as soon as it
                         # returns (its cleanup cancels the engine request)
-                        import threading
-
                         def close_later():
                             for _ in range(2000):
                                 try:
