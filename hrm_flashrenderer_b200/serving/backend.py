@@ -14,7 +14,35 @@ from __future__ import annotations
 import hashlib
 import queue
 import time
-from typing import Dict, Iterator, List, Optional
+from typing import Dict, Iterator, List, Optional, Sequence
+
+
+def cut_at_stop(pieces: Iterator[str], stops: Sequence[str]) -> Iterator[str]:
+    """Pass text pieces through until the text contains one of ``stops``; the output ends just before the earliest
+    stop string (which is not emitted) and the piece source is closed (for a backend stream that cancels the
+    request).  Text that could still turn into a stop string is held back until it cannot."""
+    stops = [s for s in stops if s]
+    hold = max((len(s) for s in stops), default=1) - 1
+    text, sent = "", 0
+    try:
+        for piece in pieces:
+            text += piece
+            hits = [i for i in (text.find(s, max(0, sent - len(s) + 1)) for s in stops) if i >= 0]
+            if hits:
+                cut = min(hits)
+                if cut > sent:
+                    yield text[sent:cut]
+                return
+            safe = len(text) - hold
+            if safe > sent:
+                yield text[sent:safe]
+                sent = safe
+        if len(text) > sent:
+            yield text[sent:]
+    finally:
+        close = getattr(pieces, "close", None)
+        if close is not None:
+            close()
 
 
 class ByteTokenizer:
@@ -53,21 +81,27 @@ class EchoBackend:
         self.fail = fail
         self.calls: List[Dict] = []
 
-    def generate(self, prompt_text: str, max_new_tokens: int = 64, timeout_s: float = 180.0, sampling=None) -> str:
-        self.calls.append({"prompt": prompt_text, "max_new_tokens": max_new_tokens, "sampling": sampling})
+    def generate(self, prompt_text: str, max_new_tokens: int = 64, timeout_s: float = 180.0, sampling=None,
+                 stop: Optional[Sequence[str]] = None) -> str:
+        self.calls.append({"prompt": prompt_text, "max_new_tokens": max_new_tokens, "sampling": sampling,
+                           "stop": stop})
         if self.fail:
             raise RuntimeError("echo backend configured to fail")
         h = hashlib.sha256(prompt_text.encode()).hexdigest()[:16]
-        return f"answer-{h}"[: max(1, max_new_tokens * 4)]
+        text = f"answer-{h}"[: max(1, max_new_tokens * 4)]
+        return "".join(cut_at_stop(iter([text]), stop)) if stop else text
 
     def generate_stream(self, prompt_text: str, max_new_tokens: int = 64, timeout_s: float = 180.0,
-                        sampling=None, cancel=None) -> Iterator[str]:
+                        sampling=None, cancel=None, stop: Optional[Sequence[str]] = None) -> Iterator[str]:
         """The same answer in 4-character pieces (stops early once ``cancel`` is set)."""
         text = self.generate(prompt_text, max_new_tokens, timeout_s, sampling)
-        for i in range(0, len(text), 4):
-            if cancel is not None and cancel.is_set():
-                return
-            yield text[i:i + 4]
+
+        def pieces():
+            for i in range(0, len(text), 4):
+                if cancel is not None and cancel.is_set():
+                    return
+                yield text[i:i + 4]
+        return cut_at_stop(pieces(), stop) if stop else pieces()
 
     def is_running(self) -> bool:
         return True
@@ -136,12 +170,21 @@ class EngineBackend:
         return self.scheduler.generate(ids, max_new_tokens, timeout=timeout_s, sampling=sampling)
 
     def generate(self, prompt_text: str, max_new_tokens: int = 256, timeout_s: float = 180.0,
-                 sampling=None) -> str:
+                 sampling=None, stop: Optional[Sequence[str]] = None) -> str:
+        """The completion text; with ``stop`` strings it ends before the first one and generation stops there."""
+        if stop:
+            return "".join(self.generate_stream(prompt_text, max_new_tokens, timeout_s, sampling, stop=stop))
         out = self.generate_ids(self.encode_prompt(prompt_text), max_new_tokens, timeout_s, sampling)
         return self.tokenizer.decode(out, skip_special_tokens=True)
 
     def generate_stream(self, prompt_text: str, max_new_tokens: int = 256, timeout_s: float = 180.0,
-                        sampling=None, cancel=None) -> Iterator[str]:
+                        sampling=None, cancel=None, stop: Optional[Sequence[str]] = None) -> Iterator[str]:
+        """Text deltas of the completion as it is generated; with ``stop`` strings the stream ends before the first
+        one and the request is cancelled there (see :meth:`_stream` for the rest)."""
+        pieces = self._stream(prompt_text, max_new_tokens, timeout_s, sampling, cancel)
+        return cut_at_stop(pieces, stop) if stop else pieces
+
+    def _stream(self, prompt_text: str, max_new_tokens: int, timeout_s: float, sampling, cancel) -> Iterator[str]:
         """Text deltas as tokens are generated (the scheduler's per-token callback feeds a queue).  The deltas
         concatenate to :meth:`generate`'s text: each one is the growth of the decoded text, held back while it ends
         in an incomplete UTF-8 sequence.  A caller that stops early (closes the iterator, or sets the

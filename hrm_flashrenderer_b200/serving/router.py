@@ -24,7 +24,7 @@ import time
 import urllib.error
 import urllib.request
 from dataclasses import dataclass
-from typing import Any, Dict, Iterator, List, Optional, Tuple
+from typing import Any, Dict, Iterator, List, Optional, Tuple, Union
 
 from .prompt_builder import SUPPORTED_MODES, normalize_mode
 
@@ -266,6 +266,7 @@ def create_app(st: RouterState):
         temperature: Optional[float] = None   # forwarded to the lane only when given (absent: greedy)
         top_k: Optional[int] = None
         seed: Optional[int] = None
+        stop: Optional[Union[str, List[str]]] = None
 
     def truncate(prompt: str) -> str:
         t = str(prompt or "").strip()
@@ -297,7 +298,7 @@ def create_app(st: RouterState):
                 try:
                     lane_req = {"prompt": prompt, "max_new_tokens": lane_new, "mode": mode, "show_sources": show}
                     lane_req.update({k: v for k, v in (("temperature", req.temperature), ("top_k", req.top_k),
-                                                       ("seed", req.seed)) if v is not None})
+                                                       ("seed", req.seed), ("stop", req.stop)) if v is not None})
                     body, ms = await asyncio.to_thread(st.post, be.base_url + "/v1/generate", lane_req,
                                                        st.request_timeout_s)
                     if not bool(body.get("ok", True)):
@@ -362,7 +363,7 @@ def create_app(st: RouterState):
             lane_req = {"prompt": prompt, "max_new_tokens": min(req_new, max_new_limit(st, lane)), "mode": mode,
                         "show_sources": resolve_show_sources(req.show_sources, mode), "stream": True}
             lane_req.update({k: v for k, v in (("temperature", req.temperature), ("top_k", req.top_k),
-                                               ("seed", req.seed)) if v is not None})
+                                               ("seed", req.seed), ("stop", req.stop)) if v is not None})
             q: "asyncio.Queue" = asyncio.Queue()
             gone = threading.Event()   # set when this relay stops reading: the pump then drops the lane stream
 
@@ -488,7 +489,8 @@ def create_app(st: RouterState):
                           max_new_tokens=body.get("max_tokens") or body.get("max_completion_tokens")
                           or body.get("max_new_tokens"),
                           route_hint=body.get("route_hint"), prefer_backend=body.get("prefer_backend"),
-                          temperature=body.get("temperature"), top_k=body.get("top_k"), seed=body.get("seed"))
+                          temperature=body.get("temperature"), top_k=body.get("top_k"), seed=body.get("seed"),
+                          stop=body.get("stop"))
         if bool(body.get("stream")):
             return StreamingResponse(relay(req, model, prompt, chat), media_type="text/event-stream")
         result = await run_generate(req)

@@ -22,7 +22,7 @@ import os
 import threading
 import time
 from pathlib import Path
-from typing import Any, List, Optional, Tuple
+from typing import Any, List, Optional, Tuple, Union
 
 from .hrm_client import run_hrm_query
 from .prompt_builder import build_prompt_for_mode, build_sources, fit_prompt_to_token_budget, normalize_mode
@@ -148,6 +148,7 @@ def create_app(state: ServiceState):
         top_k: Optional[int] = None
         seed: Optional[int] = None
         stream: Optional[bool] = None         # server-sent events: text deltas, then the full payload
+        stop: Optional[Union[str, List[str]]] = None   # end the answer before the first of these strings
 
     def sem() -> asyncio.Semaphore:
         if state.sem is None:
@@ -233,9 +234,12 @@ def create_app(state: ServiceState):
                           "source_injected_count": len(sources), "prompt_template": template}}
         if (show or state.expose_sources) and mode != "deepseek_only":
             base["sources"] = [{"sid": s.sid, "txt": s.txt} for s in sources]
+        stops = [req.stop] if isinstance(req.stop, str) else list(req.stop or [])
         if req.stream:
             stop = threading.Event()
             kw = {"cancel": stop} if sampling is None else {"cancel": stop, "sampling": sampling}
+            if stops:
+                kw["stop"] = stops
             try:
                 pieces = state.backend.generate_stream(prompt_text, max_new, state.request_timeout_s, **kw)
             except AttributeError:
@@ -243,11 +247,13 @@ def create_app(state: ServiceState):
             return _sse_response(pieces, base, stop, request)
         # generation runs outside the admission semaphore's prompt-build section: the engine batches requests
         try:
-            if sampling is None:
-                text = await asyncio.to_thread(state.backend.generate, prompt_text, max_new, state.request_timeout_s)
-            else:
-                text = await asyncio.to_thread(state.backend.generate, prompt_text, max_new, state.request_timeout_s,
-                                               sampling=sampling)
+            kw = {}
+            if sampling is not None:
+                kw["sampling"] = sampling
+            if stops:
+                kw["stop"] = stops
+            text = await asyncio.to_thread(state.backend.generate, prompt_text, max_new, state.request_timeout_s,
+                                           **kw)
         except Exception as e:
             raise HTTPException(status_code=500, detail=str(e))
         payload = {"ok": True, "text": text}

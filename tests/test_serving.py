@@ -393,3 +393,34 @@ def test_lane_stream_client_disconnect_cancels_the_request(hrm_model):
             assert m["generated_tokens"] < 400
     finally:
         be.stop()
+
+
+def test_stop_strings_cut_the_answer(hrm_model):
+    """``stop`` on /v1/generate (and forwarded by the router): the answer ends before the first stop string, in the
+    plain and the streamed form, and the engine request stops there."""
+    from hrm_flashrenderer_b200.serving.backend import EngineBackend, cut_at_stop
+    assert "".join(cut_at_stop(iter(["hel", "lo wo", "rld"]), ["o w"])) == "hell"
+    assert "".join(cut_at_stop(iter(["xSTO", "Py"]), ["STOP", "Py"])) == "x"
+    be = EchoBackend()
+    st = _state(hrm_model, be)
+    with LiveServer(create_app(st)) as srv:
+        full = json.loads(post(srv.url + "/v1/generate", {"prompt": "hi", "mode": "deepseek_only"})[1])["text"]
+        stop = full[5:7]
+        cut = json.loads(post(srv.url + "/v1/generate", {"prompt": "hi", "mode": "deepseek_only",
+                                                         "stop": stop})[1])["text"]
+        assert cut == full[:full.find(stop)]
+        ev = _sse_events(srv.url + "/v1/generate", {"prompt": "hi", "mode": "deepseek_only", "stop": [stop],
+                                                    "stream": True})
+        assert json.loads(ev[-2])["text"] == cut
+    eng = EngineBackend("synthetic:tiny", device="cpu", max_seq_len=256, max_batch=2)
+    try:
+        full = eng.generate("hello", 40)
+        stop = full[6:8]
+        assert eng.generate("hello", 40, stop=[stop]) == full[:full.find(stop)]
+        import time
+        t0 = time.time()
+        while eng.metrics()["cancelled"] < 1 and time.time() - t0 < 30:
+            time.sleep(0.01)
+        assert eng.metrics()["cancelled"] == 1              # generation stopped at the stop string
+    finally:
+        eng.stop()
