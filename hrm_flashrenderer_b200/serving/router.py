@@ -267,6 +267,7 @@ def create_app(st: RouterState):
         top_k: Optional[int] = None
         seed: Optional[int] = None
         stop: Optional[Union[str, List[str]]] = None
+        stream: Optional[bool] = None           # server-sent events: the lane's deltas, then its payload + route
 
     def truncate(prompt: str) -> str:
         t = str(prompt or "").strip()
@@ -338,12 +339,13 @@ def create_app(st: RouterState):
             obj.update(extra)
         return f"data: {json.dumps(obj)}\n\n"
 
-    async def relay(req: GenerateReq, model: str, prompt: str, chat: bool):
+    async def relay(req: GenerateReq, model: str, prompt: str, chat: bool, native: bool = False):
         """OpenAI streaming: the selected lane streams text deltas, relayed as chunks while it generates.  A lane
         that fails before its first delta is replaced by the next candidate (as for non-streaming requests);
         after that, an error ends the stream with an error event.  Comment lines keep the connection alive while a
         lane is silent.  When the client goes away, the lane connection is closed, which cancels the request on
-        the lane."""
+        the lane.  ``native``: the lane's own events are passed on (``{"delta": ...}``, then its payload with the
+        router's ``route`` record) instead of OpenAI chunks."""
         cid = f"{'chatcmpl' if chat else 'cmpl'}-{int(time.time() * 1000)}"
         try:
             mode = normalize_mode(req.mode if req.mode is not None else st.default_mode)
@@ -401,32 +403,43 @@ def create_app(st: RouterState):
                         if not started:
                             errors.append(f"{lane}: {why}")
                             break                              # next candidate lane
-                        yield f"data: {json.dumps({'error': str(why)})}\n\n"
+                        err = {"ok": False, "error": str(why)} if native else {"error": str(why)}
+                        yield f"data: {json.dumps(err)}\n\n"
                         yield "data: [DONE]\n\n"
                         return
                     if kind == "end":
                         ev = {"text": "".join(text)}
                     if "delta" in ev:
-                        if not started and chat:
+                        if not started and chat and not native:
                             yield chunk(cid, model, chat, None, role=True)
                         started = True
                         text.append(str(ev["delta"]))
-                        yield chunk(cid, model, chat, str(ev["delta"]))
+                        if native:
+                            yield f"data: {json.dumps({'delta': str(ev['delta'])})}\n\n"
+                        else:
+                            yield chunk(cid, model, chat, str(ev["delta"]))
                         continue
                     full = str(ev.get("text", "".join(text)))   # the final payload closes the stream
-                    if not started and full:
-                        yield chunk(cid, model, chat, full)
                     st.routed[lane] = st.routed.get(lane, 0) + 1
                     if lane != primary:
                         st.failovers_total += 1
-                    yield chunk(cid, model, chat, None, "stop", {"usage": usage(prompt, full)})
+                    if native:
+                        out = dict(ev)
+                        out["route"] = {"primary": primary, "selected": lane, "attempted": attempted,
+                                        "prompt_tokens": ptoks, "requested_max_new_tokens": req_new,
+                                        "backend_max_new_tokens": lane_req["max_new_tokens"]}
+                        yield f"data: {json.dumps(out)}\n\n"
+                    else:
+                        if not started and full:
+                            yield chunk(cid, model, chat, full)
+                        yield chunk(cid, model, chat, None, "stop", {"usage": usage(prompt, full)})
                     yield "data: [DONE]\n\n"
                     return
             finally:
                 gone.set()
         st.all_failed_total += 1
         detail = {"error": "all backends failed", "primary": primary, "attempted": attempted, "backend_errors": errors}
-        yield f"data: {json.dumps({'error': detail})}\n\n"
+        yield f"data: {json.dumps({'ok': False, 'detail': detail} if native else {'error': detail})}\n\n"
         yield "data: [DONE]\n\n"
 
     def check(lane: str) -> Dict[str, Any]:
@@ -475,7 +488,13 @@ def create_app(st: RouterState):
 
     @app.post("/v1/generate")
     async def generate(request: Request):
-        return JSONResponse(await run_generate(GenerateReq(**(await request.json()))))
+        req = GenerateReq(**(await request.json()))
+        if req.stream:
+            if not req.prompt or not req.prompt.strip():
+                raise HTTPException(status_code=400, detail="prompt required")
+            return StreamingResponse(relay(req, st.model_id, truncate(req.prompt), chat=False, native=True),
+                                     media_type="text/event-stream")
+        return JSONResponse(await run_generate(req))
 
     @app.get("/v1/models")
     async def models():

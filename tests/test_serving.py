@@ -424,3 +424,24 @@ def test_stop_strings_cut_the_answer(hrm_model):
         assert eng.metrics()["cancelled"] == 1              # generation stopped at the stop string
     finally:
         eng.stop()
+
+
+def test_router_generate_stream_passes_lane_events_with_route(hrm_model):
+    """``stream: true`` on the router's /v1/generate: the lane's deltas pass through and the final event is the
+    lane's payload plus the router's route record."""
+    lane_state = _state(hrm_model, EchoBackend())
+    with LiveServer(create_app(lane_state)) as lane:
+        st = rt.RouterState()
+        st.backends = {"solo_3080": rt.Backend("solo_3080", lane.url),
+                       "nvlink_pair": rt.Backend("nvlink_pair", "http://127.0.0.1:9"),
+                       "solo_22gb": rt.Backend("solo_22gb", "http://127.0.0.1:7")}
+        st.keepalive_s = 0.05
+        with LiveServer(rt.create_app(st)) as router:
+            body = {"prompt": "who guards the silver bridge", "mode": "retrieval", "max_new_tokens": 50}
+            ev = _sse_events(router.url + "/v1/generate", dict(body, stream=True))
+            plain = json.loads(post(router.url + "/v1/generate", body)[1])
+    assert ev[-1] == "[DONE]"
+    final = json.loads(ev[-2])
+    deltas = [json.loads(e)["delta"] for e in ev[:-2]]
+    assert "".join(deltas) == final["text"] == plain["text"]
+    assert final["route"]["selected"] == "solo_3080" and final["sources"] == plain["sources"]
