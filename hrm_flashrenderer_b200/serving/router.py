@@ -18,6 +18,7 @@ import asyncio
 import contextlib
 import json
 import os
+import secrets
 import sys
 import threading
 import time
@@ -510,19 +511,35 @@ def create_app(st: RouterState):
                           route_hint=body.get("route_hint"), prefer_backend=body.get("prefer_backend"),
                           temperature=body.get("temperature"), top_k=body.get("top_k"), seed=body.get("seed"),
                           stop=body.get("stop"))
+        n = int(body.get("n") or 1)
+        if not 1 <= n <= 16:
+            raise HTTPException(status_code=400, detail="n must be in 1..16")
         if bool(body.get("stream")):
+            if n != 1:
+                raise HTTPException(status_code=400, detail="stream supports n = 1")
             return StreamingResponse(relay(req, model, prompt, chat), media_type="text/event-stream")
-        result = await run_generate(req)
-        text = str(result.get("text") or "")
+        if n == 1 or not req.temperature:
+            texts = [str((await run_generate(req)).get("text") or "")] * n   # greedy: every choice is the same
+        else:
+            # n independent draws: one request per choice, seeds seed, seed + 1, ... (random when no seed)
+            base = int(req.seed) if req.seed is not None else secrets.randbits(62)
+            reqs = [req.model_copy(update={"seed": base + i}) for i in range(n)]
+            texts = [str(r.get("text") or "") for r in await asyncio.gather(*(run_generate(r) for r in reqs))]
+        use = usage(prompt, texts[0])
+        if n > 1:
+            comp = sum(usage(prompt, t)["completion_tokens"] for t in texts)
+            use = {"prompt_tokens": use["prompt_tokens"], "completion_tokens": comp,
+                   "total_tokens": use["prompt_tokens"] + comp}
         if chat:
             return JSONResponse({"id": f"chatcmpl-{int(time.time() * 1000)}", "object": "chat.completion",
                                  "created": int(time.time()), "model": model,
-                                 "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
-                                              "finish_reason": "stop"}], "usage": usage(prompt, text)})
+                                 "choices": [{"index": i, "message": {"role": "assistant", "content": t},
+                                              "finish_reason": "stop"} for i, t in enumerate(texts)],
+                                 "usage": use})
         return JSONResponse({"id": f"cmpl-{int(time.time() * 1000)}", "object": "text_completion",
                              "created": int(time.time()), "model": model,
-                             "choices": [{"index": 0, "text": text, "finish_reason": "stop"}],
-                             "usage": usage(prompt, text)})
+                             "choices": [{"index": i, "text": t, "finish_reason": "stop"} for i, t in enumerate(texts)],
+                             "usage": use})
 
     @app.post("/v1/completions")
     async def completions(request: Request):

@@ -445,3 +445,27 @@ def test_router_generate_stream_passes_lane_events_with_route(hrm_model):
     deltas = [json.loads(e)["delta"] for e in ev[:-2]]
     assert "".join(deltas) == final["text"] == plain["text"]
     assert final["route"]["selected"] == "solo_3080" and final["sources"] == plain["sources"]
+
+
+def test_openai_n_choices():
+    """``n`` choices: one lane request per choice with seeds seed, seed + 1, ... when sampling; greedy requests are
+    answered once and repeated; streaming accepts n = 1 only."""
+    calls = []
+
+    def fake_post(url, payload, timeout):
+        calls.append(payload)
+        return {"ok": True, "text": f"t{payload.get('seed', 'g')}", "mode": payload["mode"]}, 1
+
+    st = _router(fake_post)
+    with LiveServer(rt.create_app(st)) as srv:
+        code, body = post(srv.url + "/v1/chat/completions", {"messages": [{"role": "user", "content": "hi"}],
+                                                             "n": 3, "temperature": 0.7, "seed": 10})
+        r = json.loads(body)
+        assert code == 200 and [c["message"]["content"] for c in r["choices"]] == ["t10", "t11", "t12"]
+        assert [c["index"] for c in r["choices"]] == [0, 1, 2]
+        calls.clear()
+        code, body = post(srv.url + "/v1/completions", {"prompt": "hi", "n": 2})
+        r = json.loads(body)
+        assert [c["text"] for c in r["choices"]] == ["tg", "tg"] and len(calls) == 1
+        code, _ = post(srv.url + "/v1/completions", {"prompt": "hi", "n": 2, "stream": True})
+        assert code == 400
