@@ -469,3 +469,22 @@ def test_openai_n_choices():
         assert [c["text"] for c in r["choices"]] == ["tg", "tg"] and len(calls) == 1
         code, _ = post(srv.url + "/v1/completions", {"prompt": "hi", "n": 2, "stream": True})
         assert code == 400
+
+
+def test_router_stream_error_after_first_delta_is_not_retried():
+    """Once a lane has streamed a delta, a later failure ends the stream with an error event (no second lane, so
+    the client never sees two answers)."""
+    tried = []
+
+    def post_stream(url, payload, timeout):
+        tried.append(url)
+        yield {"delta": "par"}
+        raise rt.LaneCallError(url, "stream broken")
+
+    st = _router(lambda u, p, t: ({"ok": True, "text": "x", "mode": p["mode"]}, 1))
+    st.post_stream = post_stream
+    with LiveServer(rt.create_app(st)) as srv:
+        ev = _sse_events(srv.url + "/v1/chat/completions", {"messages": [{"role": "user", "content": "hi"}],
+                                                            "stream": True, "max_tokens": 50})
+    assert ev[-1] == "[DONE]" and "error" in json.loads(ev[-2]) and len(tried) == 1
+    assert "".join(json.loads(e)["choices"][0]["delta"].get("content", "") for e in ev[:-2]) == "par"
