@@ -126,6 +126,8 @@ class Scheduler:
                sampling: Optional[SamplingParams] = None) -> GenRequest:
         if self.fatal is not None:
             raise RuntimeError(f"engine stopped after a fatal error: {self.fatal}")
+        if self._stop.is_set():
+            raise RuntimeError("scheduler stopped")
         if not prompt_ids:
             raise ValueError("empty prompt")
         limit = self.engine.max_blocks * self.engine.block_size
@@ -361,6 +363,27 @@ class Scheduler:
                     break
         if self.fatal is not None:   # nothing queued waits for a loop that is gone
             self._fail_queued()
+        else:                        # stopped: every request still in flight ends with an error
+            self._fail_outstanding(RuntimeError("scheduler stopped"))
+
+    def _fail_outstanding(self, err: BaseException) -> None:
+        for r in self._running + self._prefilling + list(self._waiting):
+            if r.seq_id >= 0 and r in self._running + self._prefilling:
+                try:
+                    self.engine.release(r.seq_id)
+                except Exception:
+                    pass
+            if not r.future.done():
+                r.future.set_exception(err)
+        self._running, self._prefilling = [], []
+        self._waiting.clear()
+        while True:
+            try:
+                r = self._inbox.get_nowait()
+            except queue.Empty:
+                return
+            if not r.future.done():
+                r.future.set_exception(err)
 
     def _fail_queued(self) -> None:
         err = RuntimeError(f"engine stopped after a fatal error: {self.fatal}")

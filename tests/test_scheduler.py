@@ -325,3 +325,27 @@ def test_cancel_running_waiting_and_timed_out_requests():
         assert eng.bm.free_blocks == total
     finally:
         sched.stop()
+
+
+def test_stop_fails_requests_in_flight_and_refuses_new_ones():
+    import time
+    eng = _engine()
+    step = eng.decode_step
+
+    def slow(g):
+        time.sleep(0.01)
+        return step(g)
+    eng.decode_step = slow
+    sched = Scheduler(eng, max_batch=1).start()
+    running = sched.submit([1, 2, 3], 200, stop_on_eos=False)
+    queued = sched.submit([4, 5, 6], 5, stop_on_eos=False)
+    t0 = time.time()
+    while not running.tokens and time.time() - t0 < 60:
+        time.sleep(0.001)
+    sched.stop()
+    for r in (running, queued):
+        with pytest.raises(RuntimeError, match="stopped"):
+            r.future.result(timeout=10)
+    with pytest.raises(RuntimeError, match="stopped"):
+        sched.submit([7], 2)
+    assert eng.bm.free_blocks == eng.bm.num_blocks
