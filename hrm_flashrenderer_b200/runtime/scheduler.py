@@ -130,6 +130,8 @@ class Scheduler:
             raise RuntimeError("scheduler stopped")
         if not prompt_ids:
             raise ValueError("empty prompt")
+        if int(max_new_tokens) < 1:
+            raise ValueError(f"max_new_tokens must be >= 1, got {max_new_tokens}")
         limit = self.engine.max_blocks * self.engine.block_size
         if len(prompt_ids) + max_new_tokens > limit:
             raise ValueError(f"prompt ({len(prompt_ids)}) + max_new_tokens ({max_new_tokens}) exceeds the "
