@@ -12,6 +12,7 @@
 """
 import argparse
 import csv
+import dataclasses
 import json
 import math
 import random
@@ -112,15 +113,18 @@ def make_trace(n: int = 512, rate: float = 4.0, vocab: int = 128256, seed: int =
     return out
 
 
-def run_trace(scheduler, trace, time_scale: float = 1.0) -> Dict:
-    """Replay ``trace`` against a started Scheduler; arrivals are honoured in wall time (scaled)."""
+def run_trace(scheduler, trace, time_scale: float = 1.0, sampling=None) -> Dict:
+    """Replay ``trace`` against a started Scheduler; arrivals are honoured in wall time (scaled).  ``sampling``
+    (``runtime.sampling.SamplingParams``) draws every request's tokens instead of the greedy pick; request ``i``
+    gets seed ``sampling.seed + i``."""
     t0 = time.perf_counter()
     reqs = []
     for arr, ids, n in trace:
         wait = arr * time_scale - (time.perf_counter() - t0)
         if wait > 0:
             time.sleep(wait)
-        reqs.append(scheduler.submit(ids, n, stop_on_eos=False))
+        sp = None if sampling is None else dataclasses.replace(sampling, seed=sampling.seed + len(reqs))
+        reqs.append(scheduler.submit(ids, n, stop_on_eos=False, sampling=sp))
     for r in reqs:
         r.future.result()
     wall = time.perf_counter() - t0
@@ -153,6 +157,8 @@ def main(argv=None) -> int:
     t.add_argument("--max_seq_len", type=int, default=2560)
     t.add_argument("--device", default="cuda:0")
     t.add_argument("--prefix_cache", action="store_true", help="share the trace's common system-prompt blocks")
+    t.add_argument("--temperature", type=float, default=0.0, help="sampled decoding (0: greedy)")
+    t.add_argument("--top_k", type=int, default=0)
     a = ap.parse_args(argv)
     if a.cmd == "grid":
         s = run_grid(a.router_url, Path(a.out_dir), modes=a.modes.split(","), route_hints=a.route_hints.split(","),
@@ -163,7 +169,9 @@ def main(argv=None) -> int:
     be = EngineBackend(a.model, device=a.device, max_seq_len=a.max_seq_len, max_batch=a.max_batch,
                        prefix_cache=a.prefix_cache)
     try:
-        res = run_trace(be.scheduler, make_trace(a.requests, a.rate, be.engine.cfg.vocab))
+        from ..runtime.sampling import SamplingParams
+        sp = SamplingParams(a.temperature, a.top_k, 0) if a.temperature > 0 else None
+        res = run_trace(be.scheduler, make_trace(a.requests, a.rate, be.engine.cfg.vocab), sampling=sp)
         print(json.dumps(res))
     finally:
         be.stop()
